@@ -1,0 +1,233 @@
+"""Generate the golden fixtures in this directory by running the REFERENCE implementation (zekun-shi/freesolo) on CPU.
+
+Usage (only where a checkout of the reference exists; the fixtures it writes are committed and travel on their own):
+
+    python tests/golden/make_golden.py --reference /path/to/freesolo [--only fsl_small,...]
+
+The script imports the reference as a library, drives its own FSAttn / FSKVCache / kv_int8 / local_attention code
+in fp32 on CPU with seeded inputs, and stores inputs (as bf16 bit patterns, so every consumer sees identical
+values) together with the reference's outputs. Nothing here is imported by the product.
+
+Fixtures:
+  fsl_<kind>.npz   one FS-L layer driven at the Q/K/V level (projections replaced by fixed tensors, W_o = identity):
+                   cell statistics, int8 codes, prefill selections (deterministic tie rule), prefill W_o input,
+                   window branch alone, and a run of decode steps that crosses cell and block boundaries.
+  fsl_config1.npz  BASELINE config 1: FSAttn(d_model=1024, 16 heads) with its own seeded projections, 4096-token
+                   prefill + 1 decode step, fp32; selections, margins and a strided sample of the outputs.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _bf16_bits(x: torch.Tensor) -> np.ndarray:
+    return x.to(torch.bfloat16).contiguous().view(torch.int16).numpy()
+
+
+def make_inputs(kind: str, B: int, H: int, N: int, D: int, seed: int):
+    """Q, K, V (B,H,N,D) with bf16-representable values, as fp32. Kinds follow the reference's own adversarial
+    inputs (tests/test_fsl_fast_select.py:41-61): randn, vocab (tied ceilings), periodic (equal cells), lowprec."""
+    g = torch.Generator().manual_seed(seed)
+    if kind == "randn":
+        x = torch.randn(B, N, 3, H, D, generator=g)
+    elif kind == "vocab":
+        voc = torch.randn(40, 3, H, D, generator=g)
+        x = voc[torch.randint(0, 40, (B, N), generator=g)]
+    elif kind == "periodic":
+        voc = torch.randn(32, 3, H, D, generator=g)
+        x = voc[(torch.arange(N) % 32).expand(B, N)]
+    elif kind == "lowprec":
+        x = torch.randint(-2, 3, (B, N, 3, H, D), generator=g).float() * 0.25
+    else:
+        raise ValueError(kind)
+    x = x.to(torch.bfloat16).float()
+    return tuple(x[:, :, i].transpose(1, 2).contiguous() for i in range(3))
+
+
+class _Fixed(torch.nn.Module):
+    """Stands in for a projection: returns rows [cursor, cursor + n) of a fixed (B, Ntot, H*D) tensor."""
+
+    def __init__(self, full):
+        super().__init__()
+        self.full = full
+        self.cursor = 0
+        self.bias = None
+        self.weight = torch.nn.Parameter(torch.zeros(1, 1), requires_grad=False)
+
+    def forward(self, x):
+        n = x.shape[1]
+        out = self.full[:, self.cursor:self.cursor + n]
+        self.cursor += n
+        return out
+
+
+def _layer(ref, H, D, seed, fused):
+    from src.fsattn import FSAttn
+    from bench_efficiency import serve_kwargs
+    kw = serve_kwargs("sparse")
+    kw.update(fs_fused_attn=1 if fused else 0, cell_prune_stable_ties=1)
+    a = FSAttn(d_model=H * D, n_heads=H, causal=True, bias=False, max_seq_len=4096, **kw).eval()
+    a.cell_prune_stable_ties = 1
+    g = torch.Generator().manual_seed(seed)
+    with torch.no_grad():
+        a.sel_scale.copy_(0.5 + torch.rand(H, generator=g) * 2)
+        a.log_sigma.copy_(torch.log(1.0 + torch.rand(H, generator=g) * 40))
+        a.long_range_scale.copy_((0.05 + torch.rand(H, generator=g)).view(H, 1, 1))
+        a.lr_norm.scale.copy_(0.5 + torch.rand(D, generator=g))
+        a.W_o.weight.copy_(torch.eye(H * D))
+    return a
+
+
+def gen_fsl(kind: str, B=1, H=2, D=64, N=1000, T=72, seed=7):
+    """One FS-L layer at the Q/K/V level: prefill of N tokens, then T decode steps."""
+    from kv_cache import FSKVCache
+    from src.fsattn import kv_int8
+    from src.fsattn.attention import _apply_rotary_emb
+    from src.utils.local_attention import local_attention
+    Q, K, V = make_inputs(kind, B, H, N + T, D, seed)
+    flat = [t.transpose(1, 2).reshape(B, N + T, H * D).contiguous() for t in (Q, K, V)]
+    out = {"kind": kind, "B": B, "H": H, "D": D, "N": N, "T": T,
+           "Q": _bf16_bits(Q), "K": _bf16_bits(K), "V": _bf16_bits(V)}
+    x = torch.zeros(B, N + T, H * D)
+
+    def run(fused):
+        a = _layer(None, H, D, seed + 1, fused)
+        a.W_q, a.W_k, a.W_v = _Fixed(flat[0]), _Fixed(flat[1]), _Fixed(flat[2])
+        sels = []
+        if fused:
+            from src.fsattn import fsb_tree
+
+            def grab(Qx, Kx, Vx, sel, s, Bq, bias=None, q_pos=0):
+                sels.append(sel.clone())
+                return torch.zeros_like(Qx)
+            a._cell_fused_lr = grab
+        c = FSKVCache(a)
+        ys = []
+        with torch.no_grad():
+            ys.append(a(x[:, :N], cache=c))
+            stats = (c._kbar.clone(), c._ceil.clone())
+            for t in range(T):
+                ys.append(a(x[:, N + t:N + t + 1], cache=c))
+        return a, ys, sels, stats, c
+
+    a, ys, _, stats, c = run(False)
+    out["lam"] = a.sel_scale.detach().numpy()
+    out["sigma"] = a.sigma.detach().numpy()
+    out["lrs"] = a.long_range_scale.detach().reshape(H).numpy()
+    out["norm_w"] = a.lr_norm.scale.detach().numpy()
+    out["eps"] = np.float32(a.lr_norm.eps)
+    out["y_prefill"] = ys[0].numpy()
+    out["y_decode"] = torch.cat(ys[1:], dim=1).numpy()
+    out["kbar"] = stats[0].numpy()
+    out["ceil"] = stats[1].numpy()
+    out["kbar_end"] = c._kbar.numpy()
+    out["ceil_end"] = c._ceil.numpy()
+    _, _, sels, _, _ = run(True)
+    out["sel_prefill"] = sels[0][:, :, :N].numpy().astype(np.int32)
+    kk = a.cell_topk
+    sd = np.full((T, B, H, kk), -1, np.int32)
+    for t, s_ in enumerate(sels[1:]):
+        sd[t, :, :, :s_.shape[-1]] = s_[:, :, 0].numpy()
+    out["sel_decode"] = sd
+    # window branch alone, the reference's own rope + band attention
+    with torch.no_grad():
+        cos, sin = a.rope(N)
+        sr = local_attention(_apply_rotary_emb(Q[:, :, :N], cos, sin), _apply_rotary_emb(K[:, :, :N], cos, sin),
+                             V[:, :, :N], a.window_size, scale=a.scale, causal=True, sigma=None)
+    out["window_prefill"] = sr.numpy()
+    out["rope_cos"] = a.rope.cos_cached[:N + T].numpy()
+    out["rope_sin"] = a.rope.sin_cached[:N + T].numpy()
+    # int8 codec on the bf16 tensors themselves
+    qk, sk = kv_int8.quantize_cells(K[:, :, :N].to(torch.bfloat16), a.cell_stride)
+    qv, sv = kv_int8.quantize_cells(V[:, :, :N].to(torch.bfloat16), a.cell_stride)
+    out["qk"], out["qv"] = qk.numpy(), qv.numpy()
+    out["sk"], out["sv"] = _bf16_bits(sk), _bf16_bits(sv)
+    out["deq_k"] = _bf16_bits(kv_int8.dequant_cells(qk, sk, a.cell_stride))
+    # the decode pool of the first decode block, as the reference builds it
+    with torch.no_grad():
+        blk = (N // a._cell_block) * a._cell_block
+        ncell0 = N // a.cell_stride
+
+        class _C:
+            bounded_kv = False
+
+            def completed_cells(self_):
+                return stats[0], stats[1], ncell0
+        pc = a._build_decode_pool(_C(), blk, a.cell_stride, torch.device("cpu"), need_tokens=False)
+    out["pool_cand_c"] = pc["cand_c"].numpy()
+    out["pool_ok"] = pc["ok_cell"].numpy()
+    np.savez_compressed(os.path.join(HERE, f"fsl_{kind}.npz"), **out)
+    print("wrote", f"fsl_{kind}.npz")
+
+
+def gen_config1():
+    """single random-init FS-L layer, d_model 1024, 16 heads x 64, fp32 on CPU, 4096-token
+    prefix then one decode step."""
+    from src.fsattn import FSAttn
+    from bench_efficiency import serve_kwargs
+    from kv_cache import FSKVCache
+    out = {}
+
+    def run(fused):
+        torch.manual_seed(0)
+        kw = serve_kwargs("sparse")
+        kw.update(fs_fused_attn=1 if fused else 0, cell_prune_stable_ties=1)
+        a = FSAttn(d_model=1024, n_heads=16, causal=True, bias=False, max_seq_len=4352, **kw).eval()
+        a.cell_prune_stable_ties = 1
+        x = torch.randn(1, 4097, 1024, generator=torch.Generator().manual_seed(1234))
+        sels = []
+        if fused:
+            def grab(Qx, Kx, Vx, sel, s, Bq, bias=None, q_pos=0):
+                sels.append(sel.clone())
+                return torch.zeros_like(Qx)
+            a._cell_fused_lr = grab
+        c = FSKVCache(a)
+        with torch.no_grad():
+            y0 = a(x[:, :4096], cache=c)
+            y1 = a(x[:, 4096:4097], cache=c)
+        return a, x, y0, y1, sels, c
+
+    a, x, y0, y1, _, c = run(False)
+    _, _, _, _, sels, _ = run(True)
+    out["x_checksum"] = np.float64(x.double().sum().item())
+    out["w_checksum"] = np.float64(sum(p.double().sum().item() for p in a.parameters()))
+    out["sel_prefill"] = sels[0][:, :, :4096].numpy().astype(np.int16)
+    out["sel_decode"] = sels[1][:, :, 0].numpy().astype(np.int16)
+    out["y_prefill_rows"] = np.arange(0, 4096, 16)
+    out["y_prefill"] = y0[:, ::16].numpy()
+    out["y_decode"] = y1.numpy()
+    out["ceil"] = c._ceil.numpy()
+    np.savez_compressed(os.path.join(HERE, "fsl_config1.npz"), **out)
+    print("wrote fsl_config1.npz")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only", default="")
+    args = ap.parse_args()
+    sys.path[:0] = [os.path.join(args.reference, "experiments", "scaling"), args.reference]
+    os.environ.update(FS_STRICT_CAUSAL="1", FS_PRUNE_KERNEL="1", FSB_TRAIN_GRAPH="0")
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    only = set(filter(None, args.only.split(",")))
+    jobs = {
+        "fsl_randn": lambda: gen_fsl("randn"),
+        "fsl_vocab": lambda: gen_fsl("vocab", N=1000, T=40, seed=11),
+        "fsl_periodic": lambda: gen_fsl("periodic", N=640, T=8, seed=13),
+        "fsl_lowprec": lambda: gen_fsl("lowprec", N=640, T=8, seed=17),
+        "fsl_config1": gen_config1,
+    }
+    for name, fn in jobs.items():
+        if not only or name in only:
+            fn()
+
+
+if __name__ == "__main__":
+    main()
