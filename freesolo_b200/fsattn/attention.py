@@ -1,0 +1,322 @@
+"""FSAttn: the reference's attention-layer API (src/fsattn/attention.py) on the sm_100a kernels, inference only.
+
+    out = W_o( window_branch + long_range_scale * RMSNorm(long_range_branch) )
+
+* window branch: causal sliding-window softmax attention over the last W+1 tokens, RoPE on Q/K only here;
+* long-range branch (FS-L): per query the kk best completed 32-token cells among the block's candidate pool (top-P
+  cells by ceiling + the Wc newest), scored on the un-rotated chunk-mean key, then softmax over those kk*32 tokens.
+
+Same constructor keywords, parameter / buffer names (a reference state dict loads with ``load_state_dict``), forward
+signature and cache protocol as the reference. Only the cacheable serving configuration exists here (causal, window RoPE,
+un-rotated long range, strict-causal selection, uniform window): anything else raises, there is no eager fallback, and
+``forward`` without a cache (training) is not provided.
+"""
+from __future__ import annotations
+
+import math
+import os
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .. import ops
+
+
+class RMSNorm(nn.Module):
+    """src/fsattn/attention.py:57-65 (parameter holder; the arithmetic is fused into the readout kernels)."""
+
+    def __init__(self, dim: int, eps: float = 1e-8):
+        super().__init__()
+        self.eps = eps
+        self.scale = nn.Parameter(torch.ones(dim))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        rms = torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.eps)
+        return x * rms * self.scale
+
+
+class Rotary(nn.Module):
+    """RoPE tables as the reference builds them with YaRN scale 1 (experiments/scaling/yarn_rope.py:36-121): fp32
+    frequencies blended through the YaRN ramp (which moves some by an ulp), tables built in fp32 and cast with the
+    module; grown in fp32 even after a cast to bf16."""
+
+    def __init__(self, dim: int, max_seq_len: int, base: float = 10000.0, beta_fast: float = 32.0, beta_slow: float = 1.0):
+        super().__init__()
+        self.dim, self.base, self.original_max_seq_len = dim, base, max_seq_len
+        self.beta_fast, self.beta_slow = beta_fast, beta_slow
+        self.register_buffer("inv_freq", self._inv_freq(), persistent=False)
+        self._build_cache(max_seq_len)
+
+    def _inv_freq(self) -> torch.Tensor:
+        D, base, L0 = self.dim, self.base, self.original_max_seq_len
+        a = 1.0 / (base ** (torch.arange(0, D, 2, dtype=torch.float32) / D))
+
+        def corr(rot):
+            return (D * math.log(L0 / (rot * 2 * math.pi))) / (2 * math.log(base))
+        low = max(math.floor(corr(self.beta_fast)), 0)
+        high = min(math.ceil(corr(self.beta_slow)), D - 1)
+        hi = high + 0.001 if low == high else high
+        ramp = ((torch.arange(D // 2, dtype=torch.float32) - low) / (hi - low)).clamp(0.0, 1.0)
+        m = 1.0 - ramp
+        return a * (1.0 - m) + a * m
+
+    def _build_cache(self, seq_len: int):
+        old = getattr(self, "cos_cached", None)
+        dev = self.inv_freq.device
+        start = 0
+        if self.inv_freq.dtype != torch.float32 and old is not None and seq_len > old.shape[0]:
+            start = old.shape[0]
+        inv = self._inv_freq().to(dev)
+        t = torch.arange(start, seq_len, dtype=torch.float32, device=dev)
+        freqs = torch.outer(t, inv)
+        emb = torch.cat([freqs, freqs], dim=-1)
+        cos, sin = emb.cos(), emb.sin()
+        if start > 0:
+            cos = torch.cat([old, cos.to(old.dtype)])
+            sin = torch.cat([self.sin_cached, sin.to(old.dtype)])
+        elif old is not None:
+            cos, sin = cos.to(old.dtype), sin.to(old.dtype)
+        self.register_buffer("cos_cached", cos, persistent=False)
+        self.register_buffer("sin_cached", sin, persistent=False)
+        self._bf16 = None
+
+    def forward(self, seq_len: int):
+        if seq_len > self.cos_cached.shape[0]:
+            self._build_cache(seq_len)
+        return self.cos_cached[:seq_len], self.sin_cached[:seq_len]
+
+    def tables_bf16(self, need: int):
+        """Contiguous bf16 (L, D) tables covering at least `need` positions (what the kernels read)."""
+        if need > self.cos_cached.shape[0]:
+            self._build_cache(need)
+        c = self._bf16
+        if c is None or c[0].shape[0] != self.cos_cached.shape[0] or c[0].device != self.cos_cached.device:
+            c = (self.cos_cached.to(torch.bfloat16).contiguous(), self.sin_cached.to(torch.bfloat16).contiguous())
+            self._bf16 = c
+        return c
+
+
+class FSAttn(nn.Module):
+    VARIANTS = ("cell_topk",)
+
+    def __init__(self, d_model: int, n_heads: int, window_size: int = 128, sigma_init: float = 4.0,
+                 learnable_sigma: bool = True, dropout: float = 0.0, bias: bool = True, causal: bool = False,
+                 long_range_variant: str = "cell_topk", use_rope: bool = False, rope_long_range: bool = True,
+                 max_seq_len: int = 8192, lr_scale_mode: str = "learn", cell_stride: int = 64, cell_topk: int = 1,
+                 cell_select: str = "score", **kwargs):
+        super().__init__()
+        assert d_model % n_heads == 0, "d_model must be divisible by n_heads"
+        assert long_range_variant in self.VARIANTS, f"Unknown variant '{long_range_variant}'"
+        assert cell_select in ("score",), f"bad cell_select '{cell_select}'"
+        self.d_model, self.n_heads = d_model, n_heads
+        self.head_dim = d_model // n_heads
+        self.scale = 1.0 / math.sqrt(self.head_dim)
+        self.window_size = window_size
+        self.causal = causal
+        self.long_range_variant = long_range_variant
+        self.disable_short_range = kwargs.get("disable_short_range", False)
+        self.disable_long_range = kwargs.get("disable_long_range", False)
+        self.fs_uniform_sr = bool(kwargs.get("fs_uniform_sr", False))
+        self.sel_content_only = bool(kwargs.get("sel_content_only", False))
+        self.use_rope = use_rope
+        self.rope_long_range = rope_long_range
+        self.cell_stride = cell_stride if cell_stride > 0 else window_size
+        self.cell_topk = max(1, cell_topk)
+        self._cell_block = 128
+        self.cell_select = cell_select
+        self.cell_prune_kernel = kwargs.get("cell_prune_kernel", None)
+        self.cell_prune_pool = kwargs.get("cell_prune_pool", None)
+        self.cell_prune_window = kwargs.get("cell_prune_window", None)
+        self.cell_prune_blkchunk = kwargs.get("cell_prune_blkchunk", None)
+        self.sel_strict_causal = kwargs.get("sel_strict_causal", None)
+        self.fs_fused_attn = kwargs.get("fs_fused_attn", None)
+        self.cell_fused_select = kwargs.get("cell_fused_select", None)
+        self.fsb_enabled = bool(kwargs.get("fsb_enabled", False))
+        self.decode_splits = int(kwargs.get("decode_splits", 8))
+        if dropout != 0.0:
+            raise NotImplementedError("inference only: dropout must be 0")
+        self.sel_scale = nn.Parameter(torch.ones(n_heads))
+        log_sigma = torch.full((n_heads,), math.log(sigma_init))
+        if learnable_sigma and not self.fs_uniform_sr:
+            self.log_sigma = nn.Parameter(log_sigma)
+        else:
+            self.register_buffer("log_sigma", log_sigma)
+        if lr_scale_mode == "learn":
+            self.long_range_scale = nn.Parameter(torch.full((n_heads, 1, 1), 0.1))
+        else:
+            self.register_buffer("long_range_scale", torch.ones(n_heads, 1, 1))
+        self.lr_norm = RMSNorm(self.head_dim)
+        if use_rope:
+            self.rope = Rotary(self.head_dim, max_seq_len)
+        self.W_q = nn.Linear(d_model, d_model, bias=bias)
+        self.W_k = nn.Linear(d_model, d_model, bias=bias)
+        self.W_v = nn.Linear(d_model, d_model, bias=bias)
+        self.W_o = nn.Linear(d_model, d_model, bias=bias)
+        self.dropout = nn.Dropout(dropout)
+        self._last_sel = None          # selections of the last call when FSATTN_KEEP_SEL=1 (tests, diagnostics)
+        self._last_margin = None
+
+    # ---- configuration helpers (same names as the reference) ---------------------------------------------------------
+    @property
+    def sigma(self) -> torch.Tensor:
+        return self.log_sigma.exp()
+
+    def _prune_cfg(self, attr, env, dflt):
+        """src/fsattn/attention.py:335-337: keyword over environment over default."""
+        v = getattr(self, attr, None)
+        return int(v) if v is not None else int(os.environ.get(env, str(dflt)))
+
+    def _is_dense_lr(self):
+        return not bool(self._prune_cfg("cell_prune_kernel", "FS_PRUNE_KERNEL", 0))
+
+    def _assert_cacheable(self, phase="decode"):
+        """src/fsattn/attention.py:872-891, plus the configurations this implementation does not cover."""
+        if not self.causal:
+            raise NotImplementedError("FSKVCache requires causal=True.")
+        if not self.use_rope or self.rope_long_range:
+            raise NotImplementedError("only the deployed window-RoPE + un-rotated long-range configuration "
+                                      "(use_rope=True, rope_long_range=False) is implemented")
+        if self.disable_short_range or self.disable_long_range:
+            raise NotImplementedError("FSKVCache requires both SR and LR branches enabled.")
+        if not bool(self._prune_cfg("sel_strict_causal", "FS_STRICT_CAUSAL", 0)):
+            raise NotImplementedError("FSKVCache requires sel_strict_causal=1 (block-causal path is non-cacheable).")
+        if not self.fs_uniform_sr:
+            raise NotImplementedError("only the uniform window (fs_uniform_sr=True) is implemented")
+        if self.sel_content_only:
+            raise NotImplementedError("sel_content_only is not implemented")
+        if self.cell_stride != ops.CELL:
+            raise NotImplementedError(f"cell_stride {self.cell_stride}: the kernels are specialised for {ops.CELL}")
+        if self.fsb_enabled:
+            raise NotImplementedError("FS-B layers use freesolo_b200.fsattn.fsb (not built into this layer yet)")
+        if self._is_dense_lr():
+            raise NotImplementedError("the dense FS variant (cell_prune_kernel=0) is not implemented")
+
+    def _pool_cfg(self):
+        return (self._prune_cfg("cell_prune_pool", "FS_PRUNE_POOL", 64), self._prune_cfg("cell_prune_window", "FS_PRUNE_WINDOW", 8))
+
+    def _ensure_qkv_cache(self):
+        """src/fsattn/attention.py:1396-1410: one fused (3d, d) projection weight the three Linear weights are views of."""
+        wq, wk, wv = self.W_q.weight, self.W_k.weight, self.W_v.weight
+        dm = self.d_model
+        key = (wq.data_ptr(), wq._version, wk.data_ptr(), wk._version, wv.data_ptr(), wv._version, wq.dtype)
+        c = getattr(self, "_w_qkv_cache", None)
+        if c is None or c[0] != key:
+            qkv_w = torch.cat([wq.data, wk.data, wv.data], dim=0)
+            self.W_q.weight.data = qkv_w[:dm]
+            self.W_k.weight.data = qkv_w[dm:2 * dm]
+            self.W_v.weight.data = qkv_w[2 * dm:]
+            wq, wk, wv = self.W_q.weight, self.W_k.weight, self.W_v.weight
+            key = (wq.data_ptr(), wq._version, wk.data_ptr(), wk._version, wv.data_ptr(), wv._version, wq.dtype)
+            c = (key, qkv_w)
+            self._w_qkv_cache = c
+        return c[1], dm
+
+    def head_params(self):
+        """fp32 device tensors the kernels read: (lam (H), sigma (H), lrs (H), norm_w (D)). Cached per parameter version."""
+        ps = (self.sel_scale, self.log_sigma, self.long_range_scale, self.lr_norm.scale)
+        key = tuple((p.data_ptr(), p._version, p.device) for p in ps)
+        c = getattr(self, "_head_params", None)
+        if c is None or c[0] != key:
+            vals = (self.sel_scale.detach().float().contiguous(), self.log_sigma.detach().float().exp().contiguous(),
+                    self.long_range_scale.detach().float().reshape(-1).contiguous(), self.lr_norm.scale.detach().float().contiguous())
+            c = (key, vals)
+            self._head_params = c
+        return c[1]
+
+    # ---- forward ---------------------------------------------------------------------------------------------------------
+    def forward(self, x: torch.Tensor, mask: torch.Tensor | None = None, cache=None) -> torch.Tensor:
+        if cache is None:
+            raise NotImplementedError("this build covers cached inference only: pass an FSKVCache (the training forward "
+                                      "stays with the reference implementation)")
+        return self._forward_cached(x, cache)
+
+    def _project_qkv(self, x):
+        B, N, _ = x.shape
+        H, D = self.n_heads, self.head_dim
+        if self.W_q.bias is not None:
+            raise NotImplementedError("projection biases are not supported (the LM uses bias=False)")
+        w, dm = self._ensure_qkv_cache()
+        qkv = F.linear(x, w)                                   # (B, N, 3d), one GEMM
+        q, k, v = (qkv[..., i * dm:(i + 1) * dm].view(B, N, H, D).transpose(1, 2) for i in range(3))
+        return q, k, v
+
+    @torch.no_grad()
+    def _forward_cached(self, x, cache):
+        B, N, _ = x.shape
+        self._assert_cacheable(phase="prefill" if (cache.pos == 0 and N > 1) else "decode")
+        if x.dtype != torch.bfloat16 or not x.is_cuda:
+            raise RuntimeError("FSAttn runs on bf16 CUDA activations only (there is no CPU or fp32 path)")
+        Q, K, V = self._project_qkv(x)
+        if cache.pos == 0 and N > 1:
+            y = self._prefill(Q, K, V, cache)
+        else:
+            ys = [self._decode_one(Q[:, :, t], K[:, :, t], V[:, :, t], cache) for t in range(N)]
+            y = torch.stack(ys, dim=1) if N > 1 else ys[0].unsqueeze(1)
+        return self.W_o(y)
+
+    def _prefill(self, Q, K, V, cache):
+        """src/fsattn/attention.py:1003-1078 (standard prefill): window branch, cell statistics + KV store, per-block
+        candidate pools, selection, fused readout + combine. Returns W_o's input (B,N,H*D)."""
+        B, H, N, D = Q.shape
+        s = self.cell_stride
+        P, Wc = self._pool_cfg()
+        cos, sin = self.rope.tables_bf16(N)
+        sr = ops.window_prefill(Q, K, V, cos, sin, self.window_size, self.scale)
+        kbar, ceil = cache.prefill(K, V)
+        ncell = N // s
+        M = (N + s - 1) // s
+        kk = min(self.cell_topk, M)
+        Bq = min(self._cell_block, N)
+        nb = (N + Bq - 1) // Bq
+        lam, sigma, lrs, norm_w = self.head_params()
+        if ncell == 0:
+            # nothing completed: every selection is empty; the readout still applies the combine (lr = 0)
+            sel = torch.full((B, H, nb * Bq, kk), -1, dtype=torch.int32, device=Q.device)
+            margin = None
+        else:
+            topp = ops.fsl_prefix_topp(ceil, ncell, Bq, nb, min(P, M))
+            keep = os.environ.get("FSATTN_KEEP_SEL", "0") == "1"
+            res = ops.fsl_select(Q, kbar, ceil, topp, lam, sigma, N=N, ncell=ncell, Bq=Bq, nb=nb, P=min(P, M), Wc=Wc,
+                                 kk=kk, scale=self.scale, want_margin=keep)
+            sel, margin = res if keep else (res, None)
+        if os.environ.get("FSATTN_KEEP_SEL", "0") == "1":
+            self._last_sel, self._last_margin = sel, margin
+        return ops.readout_combine(Q, K, V, sel, sr, norm_w, lrs, self.lr_norm.eps, scale=self.scale, Bq=Bq, n_kv=N,
+                                   out=sr)
+
+    def _decode_one(self, q, k, v, cache, pos_t=None, y=None):
+        """One token through the fused decode-step kernel (src/fsattn/attention.py:1116-1131 and 1493-1559).
+        q,k,v (B,H,D) views; returns W_o's input (B, H*D)."""
+        st = cache.decode_state(q)
+        if pos_t is None:
+            if cache.pos >= st.cap_rows:
+                raise RuntimeError(f"KV store holds {st.cap_rows} positions; set cache.reserve before the prefill")
+            pos_t = cache.pos_t
+            pos_t.fill_(cache.pos)
+        cos, sin = self.rope.tables_bf16(st.cap_rows)
+        lam, sigma, lrs, norm_w = self.head_params()
+        sel_out = None
+        if os.environ.get("FSATTN_KEEP_SEL", "0") == "1":
+            sel_out = torch.empty(st.B, st.H, st.kk, dtype=torch.int32, device=q.device)
+            self._last_sel = sel_out
+        y = ops.fsl_decode_step(st, q, k, v, pos_t, cos, sin, lam, sigma, lrs, norm_w, scale=self.scale,
+                                eps=self.lr_norm.eps, y=y, sel_out=sel_out, splits=self.decode_splits)
+        cache.advance_in_place()
+        return y
+
+    def graph_decode_layer(self, x, buf):
+        """One decode token inside a captured whole-step graph (src/fsattn/attention.py:1493-1559): x (B,1,d); buf holds
+        the shared device position `pos_t` and the layer's `cache`. Everything the reference does around its graph replay
+        for this layer (pool refresh, cell close) happens inside the one kernel launch."""
+        B, N, _ = x.shape
+        H, D = self.n_heads, self.head_dim
+        w, dm = self._ensure_qkv_cache()
+        qkv = F.linear(x.view(B, dm), w).view(B, 3, H, D)
+        cache = buf["cache"]
+        st = cache.decode_state(qkv)
+        cos, sin = self.rope.tables_bf16(st.cap_rows)
+        lam, sigma, lrs, norm_w = self.head_params()
+        y = ops.fsl_decode_step(st, qkv[:, 0], qkv[:, 1], qkv[:, 2], buf["pos_t"], cos, sin, lam, sigma, lrs, norm_w,
+                                scale=self.scale, eps=self.lr_norm.eps, y=buf.get("y"), splits=self.decode_splits)
+        return self.W_o(y.view(B, 1, dm))

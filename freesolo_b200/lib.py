@@ -1,0 +1,169 @@
+"""ctypes binding of libfsattn_b200.so (the C ABI declared in include/fsattn_b200.h).
+
+The library is built in-tree by ``freesolo_b200/csrc/build.sh`` (``__graft_entry__.build()``). There is no fallback:
+if the shared object is missing or a call is rejected, a RuntimeError is raised.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libfsattn_b200.so")
+
+OK, EINVAL, EUNSUPPORTED, ELAUNCH = 0, -1, -2, -3
+CELL = 32
+MAX_POOL = 128
+MAX_KK = 8
+ST_SLOT_OVERFLOW, ST_POOL_NO_SLOT, ST_BAD_INDEX, ST_WORDS = 0, 1, 2, 4
+
+i32, i64, f32, vp = C.c_int32, C.c_int64, C.c_float, C.c_void_p
+
+
+class BHND(C.Structure):
+    _fields_ = [("ptr", vp), ("sb", i64), ("sh", i64), ("sn", i64)]
+
+
+class CellIngest(C.Structure):
+    _fields_ = [("k", BHND), ("v", BHND),
+                ("B", i32), ("H", i32), ("D", i32), ("ncell", i32), ("cell0", i32),
+                ("kbar", vp), ("kbar_sb", i64), ("kbar_sh", i64),
+                ("ceil", vp), ("ceil_sb", i64), ("ceil_sh", i64),
+                ("kq", vp), ("vq", vp), ("q_sb", i64), ("q_sh", i64),
+                ("ks", vp), ("vs", vp), ("sc_sb", i64), ("sc_sh", i64)]
+
+
+class Dequant(C.Structure):
+    _fields_ = [("q", vp), ("q_sb", i64), ("q_sh", i64),
+                ("sc", vp), ("sc_sb", i64), ("sc_sh", i64),
+                ("out", vp), ("o_sb", i64), ("o_sh", i64),
+                ("B", i32), ("H", i32), ("D", i32), ("nrows", i64)]
+
+
+class FslTopp(C.Structure):
+    _fields_ = [("ceil", vp), ("ceil_sb", i64), ("ceil_sh", i64),
+                ("B", i32), ("H", i32), ("ncell", i32), ("Bq", i32), ("nb", i32), ("P", i32),
+                ("topp", vp)]
+
+
+class FslSelect(C.Structure):
+    _fields_ = [("q", BHND),
+                ("kbar", vp), ("kbar_sb", i64), ("kbar_sh", i64),
+                ("ceil", vp), ("ceil_sb", i64), ("ceil_sh", i64),
+                ("topp", vp), ("lam", vp), ("sigma", vp),
+                ("B", i32), ("H", i32), ("D", i32), ("N", i32), ("ncell", i32), ("Bq", i32), ("nb", i32),
+                ("P", i32), ("Wc", i32), ("kk", i32),
+                ("scale", f32),
+                ("sel", vp), ("margin", vp)]
+
+
+class WindowPrefill(C.Structure):
+    _fields_ = [("q", BHND), ("k", BHND), ("v", BHND),
+                ("cos", vp), ("sin", vp),
+                ("B", i32), ("H", i32), ("D", i32), ("N", i32), ("W", i32), ("pos0", i32),
+                ("scale", f32),
+                ("out", vp),
+                ("impl", i32)]
+
+
+class ReadoutCombine(C.Structure):
+    _fields_ = [("q", BHND), ("k", BHND), ("v", BHND),
+                ("sel", vp), ("sel_sb", i64), ("sel_sh", i64),
+                ("sr", vp), ("y", vp),
+                ("norm_w", vp), ("lrs", vp),
+                ("B", i32), ("H", i32), ("D", i32), ("N", i32), ("n_kv", i32), ("Bq", i32), ("kk", i32),
+                ("q_pos0", i32),
+                ("scale", f32), ("eps", f32)]
+
+
+class FslState(C.Structure):
+    _fields_ = [("store_mode", i32), ("B", i32), ("H", i32), ("D", i32), ("P", i32), ("Wc", i32), ("W", i32),
+                ("Bq", i32), ("kk", i32), ("n_slots", i32),
+                ("cap_rows", i64), ("cap_cells", i64),
+                ("kbuf", vp), ("vbuf", vp), ("buf_sb", i64), ("buf_sh", i64),
+                ("kq", vp), ("vq", vp), ("q_sb", i64), ("q_sh", i64),
+                ("ks", vp), ("vs", vp), ("sc_sb", i64), ("sc_sh", i64),
+                ("khot", vp), ("vhot", vp), ("hot_sb", i64), ("hot_sh", i64),
+                ("kbar", vp), ("kbar_sb", i64), ("kbar_sh", i64),
+                ("ceil", vp), ("ceil_sb", i64), ("ceil_sh", i64),
+                ("slot_of", vp), ("so_sb", i64), ("so_sh", i64),
+                ("cell_in", vp), ("ci_sb", i64), ("ci_sh", i64),
+                ("top_idx", vp), ("top_blk", vp),
+                ("status", vp)]
+
+
+class FslDecode(C.Structure):
+    _fields_ = [("st", FslState),
+                ("q", vp), ("k", vp), ("v", vp), ("in_sb", i64), ("in_sh", i64),
+                ("pos", vp),
+                ("cos", vp), ("sin", vp),
+                ("lam", vp), ("sigma", vp), ("lrs", vp), ("norm_w", vp),
+                ("scale", f32), ("eps", f32),
+                ("y", vp), ("sel_out", vp),
+                ("splits", i32)]
+
+
+class SlotPrefill(C.Structure):
+    _fields_ = [("st", FslState), ("k", BHND), ("v", BHND),
+                ("kbar_cells", vp), ("kc_sb", i64), ("kc_sh", i64),
+                ("N", i32)]
+
+
+# every exported symbol of include/fsattn_b200.h with its argument struct (None = no struct argument)
+ENTRY_POINTS = {
+    "fsattn_version": None,
+    "fsattn_last_error": None,
+    "fsattn_init": None,
+    "fsattn_cell_ingest": CellIngest,
+    "fsattn_dequant_cells": Dequant,
+    "fsattn_fsl_prefix_topp": FslTopp,
+    "fsattn_fsl_select": FslSelect,
+    "fsattn_window_prefill": WindowPrefill,
+    "fsattn_readout_combine": ReadoutCombine,
+    "fsattn_fsl_decode_step": FslDecode,
+    "fsattn_slot_prefill": SlotPrefill,
+}
+
+_lib = None
+_inited = set()
+
+
+def load() -> C.CDLL:
+    """The loaded library; raises if the extension has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.isfile(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with freesolo_b200/csrc/build.sh "
+                               "(__graft_entry__.build()); there is no fallback path")
+        lib = C.CDLL(LIB_PATH)
+        lib.fsattn_version.restype = C.c_int
+        lib.fsattn_last_error.restype = C.c_char_p
+        lib.fsattn_init.argtypes = [C.c_int]
+        lib.fsattn_init.restype = C.c_int
+        for name, st in ENTRY_POINTS.items():
+            fn = getattr(lib, name)         # AttributeError here = header and library disagree
+            if st is not None:
+                fn.argtypes = [C.POINTER(st), vp]
+                fn.restype = C.c_int
+        _lib = lib
+    return _lib
+
+
+def last_error() -> str:
+    return load().fsattn_last_error().decode("utf-8", "replace")
+
+
+def check(rc: int, what: str) -> None:
+    if rc != OK:
+        kind = {EINVAL: "invalid argument", EUNSUPPORTED: "unsupported configuration", ELAUNCH: "launch failure"}.get(rc, rc)
+        raise RuntimeError(f"{what}: {kind}: {last_error()}")
+
+
+def init(device_index: int) -> None:
+    if device_index not in _inited:
+        check(load().fsattn_init(int(device_index)), "fsattn_init")
+        _inited.add(device_index)
+
+
+def call(name: str, args: C.Structure, stream_ptr: int) -> None:
+    check(getattr(load(), name)(C.byref(args), vp(stream_ptr)), name)

@@ -1,0 +1,364 @@
+"""Torch-tensor front end of the C ABI: fills the argument structs of include/fsattn_b200.h from tensors and launches on
+the current CUDA stream. PyTorch owns every buffer; these functions only allocate outputs the caller did not pass.
+
+Every function raises when its tensors are not CUDA tensors: there is no CPU path.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import lib as L
+
+CELL = L.CELL
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("freesolo_b200 kernels need CUDA tensors: there is no CPU fallback")
+
+
+def _stream(t: torch.Tensor) -> int:
+    L.init(t.device.index if t.device.index is not None else torch.cuda.current_device())
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _bhnd(t: torch.Tensor, name: str) -> L.BHND:
+    if t.dim() != 4 or t.stride(-1) != 1 or t.dtype != torch.bfloat16:
+        raise ValueError(f"{name}: expected a bf16 (B,H,N,D) view with unit inner stride, got {tuple(t.shape)} {t.dtype} "
+                         f"strides {t.stride()}")
+    return L.BHND(t.data_ptr(), t.stride(0), t.stride(1), t.stride(2))
+
+
+def _null() -> L.BHND:
+    return L.BHND(None, 0, 0, 0)
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _f32(t: torch.Tensor) -> torch.Tensor:
+    return t.detach().to(torch.float32).contiguous()
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+def cell_ingest(K, V=None, *, ncell: int, cell0: int = 0, kbar=None, ceil=None, kq=None, ks=None, vq=None, vs=None):
+    """One pass over ncell completed cells of K (and V): chunk-mean keys, ceilings and/or int8 codes + scales, written
+    at cell index cell0 + c of the outputs. kbar (B,H,*,D) fp32, ceil (B,H,*) fp32, kq/vq (B,H,*,D) int8 with row stride
+    D, ks/vs (B,H,*) bf16."""
+    _need_cuda(K, V)
+    B, H, _, D = K.shape
+    a = L.CellIngest()
+    a.k = _bhnd(K, "K")
+    a.v = _bhnd(V, "V") if V is not None else _null()
+    a.B, a.H, a.D, a.ncell, a.cell0 = B, H, D, int(ncell), int(cell0)
+    if kbar is not None:
+        assert kbar.dtype == torch.float32 and kbar.stride(-1) == 1 and kbar.stride(2) == D
+        a.kbar, a.kbar_sb, a.kbar_sh = kbar.data_ptr(), kbar.stride(0), kbar.stride(1)
+    if ceil is not None:
+        assert ceil.dtype == torch.float32 and ceil.stride(-1) == 1
+        a.ceil, a.ceil_sb, a.ceil_sh = ceil.data_ptr(), ceil.stride(0), ceil.stride(1)
+    qs = [t for t in (kq, vq) if t is not None]
+    if qs:
+        q0 = qs[0]
+        for t in qs:
+            assert t.dtype == torch.int8 and t.stride(-1) == 1 and t.stride(2) == D and t.stride()[:2] == q0.stride()[:2]
+        a.kq, a.vq, a.q_sb, a.q_sh = _p(kq), _p(vq), q0.stride(0), q0.stride(1)
+        ss = [t for t in (ks, vs) if t is not None]
+        for t in ss:
+            assert t.dtype == torch.bfloat16 and t.stride(-1) == 1 and t.stride()[:2] == ss[0].stride()[:2]
+        a.ks, a.vs, a.sc_sb, a.sc_sh = _p(ks), _p(vs), ss[0].stride(0), ss[0].stride(1)
+    L.call("fsattn_cell_ingest", a, _stream(K))
+
+
+def cell_stats(K, ncell: int):
+    """(kbar (B,H,ncell,D) fp32, ceil (B,H,ncell) fp32) of the first ncell cells of K."""
+    B, H, _, D = K.shape
+    kbar = torch.empty(B, H, ncell, D, dtype=torch.float32, device=K.device)
+    ceil = torch.empty(B, H, ncell, dtype=torch.float32, device=K.device)
+    if ncell > 0:
+        cell_ingest(K, ncell=ncell, kbar=kbar, ceil=ceil)
+    return kbar, ceil
+
+
+def quantize_cells(x, s: int = CELL, q=None, sc=None):
+    """int8 codes and bf16 scales of the whole cells of x (B,H,N,D) bf16; q/sc may be preallocated slices."""
+    if s != CELL:
+        raise RuntimeError(f"cell size {s} unsupported (kernels are specialised for {CELL})")
+    B, H, N, D = x.shape
+    nc = N // s
+    if q is None:
+        q = torch.empty(B, H, nc * s, D, dtype=torch.int8, device=x.device)
+    if sc is None:
+        sc = torch.empty(B, H, nc, dtype=torch.bfloat16, device=x.device)
+    if nc > 0:
+        cell_ingest(x, ncell=nc, kq=q, ks=sc)
+    return q, sc
+
+
+def dequant_cells(q, sc, s: int = CELL, dtype=torch.bfloat16, out=None):
+    """bf16(f32(q) * f32(scale)) over the quantised rows; out (B,H,>=N,D) optional."""
+    _need_cuda(q, sc)
+    if s != CELL or dtype != torch.bfloat16:
+        raise RuntimeError("dequant_cells: only cell size 32 and bf16 output are supported")
+    B, H, N, D = q.shape
+    nrows = (N // s) * s
+    ret = out
+    if out is None:
+        out = torch.empty(B, H, nrows, D, dtype=torch.bfloat16, device=q.device)
+        ret = out
+    assert q.stride(-1) == 1 and q.stride(2) == D and out.stride(-1) == 1 and out.stride(2) == D and sc.stride(-1) == 1
+    a = L.Dequant()
+    a.q, a.q_sb, a.q_sh = q.data_ptr(), q.stride(0), q.stride(1)
+    a.sc, a.sc_sb, a.sc_sh = sc.data_ptr(), sc.stride(0), sc.stride(1)
+    a.out, a.o_sb, a.o_sh = out.data_ptr(), out.stride(0), out.stride(1)
+    a.B, a.H, a.D, a.nrows = B, H, D, nrows
+    L.call("fsattn_dequant_cells", a, _stream(q))
+    return ret
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+def fsl_prefix_topp(ceil, ncell: int, Bq: int, nb: int, P: int):
+    """(B*H, nb, P) int32: per query block the top-P visible cells in pool order, -1 fill."""
+    _need_cuda(ceil)
+    B, H = ceil.shape[:2]
+    assert ceil.dtype == torch.float32 and ceil.stride(-1) == 1
+    if ncell <= 0:
+        return torch.full((B * H, nb, P), -1, dtype=torch.int32, device=ceil.device)
+    topp = torch.empty(B * H, nb, P, dtype=torch.int32, device=ceil.device)
+    a = L.FslTopp()
+    a.ceil, a.ceil_sb, a.ceil_sh = ceil.data_ptr(), ceil.stride(0), ceil.stride(1)
+    a.B, a.H, a.ncell, a.Bq, a.nb, a.P = B, H, int(ncell), int(Bq), int(nb), int(P)
+    a.topp = topp.data_ptr()
+    L.call("fsattn_fsl_prefix_topp", a, _stream(ceil))
+    return topp
+
+
+def fsl_select(Q, kbar, ceil, topp, lam, sigma, *, N: int, ncell: int, Bq: int, nb: int, P: int, Wc: int, kk: int,
+               scale: float, want_margin: bool = False):
+    """sel (B,H,nb*Bq,kk) int32 (and the fp32 margins when asked)."""
+    _need_cuda(Q, kbar, ceil, topp)
+    B, H, _, D = Q.shape
+    if ncell <= 0:      # nothing completed: no cell can be selected
+        sel = torch.full((B, H, nb * Bq, kk), -1, dtype=torch.int32, device=Q.device)
+        margin = torch.full((B, H, nb * Bq), float("inf"), dtype=torch.float32, device=Q.device)
+        return (sel, margin) if want_margin else sel
+    sel = torch.empty(B, H, nb * Bq, kk, dtype=torch.int32, device=Q.device)
+    margin = torch.empty(B, H, nb * Bq, dtype=torch.float32, device=Q.device) if want_margin else None
+    lam, sigma = _f32(lam), _f32(sigma)
+    a = L.FslSelect()
+    a.q = _bhnd(Q, "Q")
+    assert kbar.dtype == torch.float32 and kbar.stride(-1) == 1 and kbar.stride(2) == D
+    a.kbar, a.kbar_sb, a.kbar_sh = kbar.data_ptr(), kbar.stride(0), kbar.stride(1)
+    a.ceil, a.ceil_sb, a.ceil_sh = ceil.data_ptr(), ceil.stride(0), ceil.stride(1)
+    a.topp, a.lam, a.sigma = topp.data_ptr(), lam.data_ptr(), sigma.data_ptr()
+    a.B, a.H, a.D, a.N, a.ncell, a.Bq, a.nb, a.P, a.Wc, a.kk = B, H, D, N, ncell, Bq, nb, P, Wc, kk
+    a.scale = float(scale)
+    a.sel, a.margin = sel.data_ptr(), _p(margin)
+    L.call("fsattn_fsl_select", a, _stream(Q))
+    return (sel, margin) if want_margin else sel
+
+
+def window_prefill(Q, K, V, cos, sin, W: int, scale: float, pos0: int = 0, impl: int = 0, out=None):
+    """Causal band attention with RoPE on Q and K. Returns (B,N,H*D) bf16 (W_o's input layout)."""
+    _need_cuda(Q, K, V, cos, sin)
+    B, H, N, D = Q.shape
+    if out is None:
+        out = torch.empty(B, N, H * D, dtype=torch.bfloat16, device=Q.device)
+    assert cos.dtype == torch.bfloat16 and sin.dtype == torch.bfloat16 and cos.is_contiguous() and sin.is_contiguous()
+    assert cos.shape[1] == D and cos.shape[0] >= pos0 + N, "rope table too short"
+    assert out.is_contiguous()
+    a = L.WindowPrefill()
+    a.q, a.k, a.v = _bhnd(Q, "Q"), _bhnd(K, "K"), _bhnd(V, "V")
+    a.cos, a.sin = cos.data_ptr(), sin.data_ptr()
+    a.B, a.H, a.D, a.N, a.W, a.pos0 = B, H, D, N, int(W), int(pos0)
+    a.scale = float(scale)
+    a.out = out.data_ptr()
+    a.impl = int(impl)
+    L.call("fsattn_window_prefill", a, _stream(Q))
+    return out
+
+
+def readout_combine(Q, K, V, sel, sr, norm_w, lrs, eps: float, *, scale: float, Bq: int, n_kv: int | None = None,
+                    q_pos0: int = 0, out=None):
+    """y (B,N,H*D) bf16 = bf16(sr + lrs[h] * lr_norm(bf16(readout of the selected cells))). sr (B,N,H*D) bf16 or None
+    (treated as zero); out may be sr itself (in place)."""
+    _need_cuda(Q, K, V, sel)
+    B, H, N, D = Q.shape
+    kk = sel.shape[-1]
+    if out is None:
+        out = torch.empty(B, N, H * D, dtype=torch.bfloat16, device=Q.device)
+    assert sel.dtype == torch.int32 and sel.stride(-1) == 1 and sel.stride(2) == kk and sel.shape[2] >= N
+    assert out.is_contiguous() and (sr is None or (sr.is_contiguous() and sr.dtype == torch.bfloat16))
+    norm_w, lrs = _f32(norm_w), _f32(lrs).reshape(-1)
+    a = L.ReadoutCombine()
+    a.q, a.k, a.v = _bhnd(Q, "Q"), _bhnd(K, "K"), _bhnd(V, "V")
+    a.sel, a.sel_sb, a.sel_sh = sel.data_ptr(), sel.stride(0), sel.stride(1)
+    a.sr, a.y = _p(sr), out.data_ptr()
+    a.norm_w, a.lrs = norm_w.data_ptr(), lrs.data_ptr()
+    a.B, a.H, a.D, a.N, a.n_kv, a.Bq, a.kk, a.q_pos0 = B, H, D, N, int(K.shape[2] if n_kv is None else n_kv), Bq, kk, q_pos0
+    a.scale, a.eps = float(scale), float(eps)
+    L.call("fsattn_readout_combine", a, _stream(Q))
+    return out
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+class FslDecodeState:
+    """Device buffers of one FS-L layer's decode-time KV state (see fsattn_fsl_state_t in include/fsattn_b200.h).
+
+    mode: "bf16" (full bf16 store), "int8" (full int8 store) or "bounded" (int8 slot store that keeps only readable
+    cells). cap_rows bounds the absolute token position; the bounded store holds n_slots * 32 rows whatever the length."""
+
+    MODES = {"bf16": 0, "int8": 1, "bounded": 2}
+
+    def __init__(self, B, H, D, cap_rows, device, *, mode="int8", P=64, Wc=8, W=512, Bq=128, kk=4):
+        self.B, self.H, self.D = B, H, D
+        self.mode = mode
+        self.P, self.Wc, self.W, self.Bq, self.kk = P, Wc, W, Bq, kk
+        self.cap_rows = int(cap_rows)
+        self.cap_cells = max(1, (self.cap_rows + CELL - 1) // CELL)
+        dev = torch.device(device)
+        z = dict(device=dev)
+        self.n_slots = P + max(-(-W // CELL), Wc) + -(-Bq // CELL) + 1
+        self.kbuf = self.vbuf = self.kq = self.vq = self.ks = self.vs = self.khot = self.vhot = None
+        self.slot_of = self.cell_in = None
+        if mode == "bf16":
+            self.kbuf = torch.zeros(B, H, self.cap_rows, D, dtype=torch.bfloat16, **z)
+            self.vbuf = torch.zeros(B, H, self.cap_rows, D, dtype=torch.bfloat16, **z)
+            stat_cells = self.cap_cells
+        elif mode == "int8":
+            rows = self.cap_cells * CELL
+            self.kq = torch.zeros(B, H, rows, D, dtype=torch.int8, **z)
+            self.vq = torch.zeros(B, H, rows, D, dtype=torch.int8, **z)
+            self.ks = torch.ones(B, H, self.cap_cells, dtype=torch.bfloat16, **z)
+            self.vs = torch.ones(B, H, self.cap_cells, dtype=torch.bfloat16, **z)
+            stat_cells = self.cap_cells
+        elif mode == "bounded":
+            rows = self.n_slots * CELL
+            self.kq = torch.zeros(B, H, rows, D, dtype=torch.int8, **z)
+            self.vq = torch.zeros(B, H, rows, D, dtype=torch.int8, **z)
+            self.ks = torch.ones(B, H, self.n_slots, dtype=torch.bfloat16, **z)
+            self.vs = torch.ones(B, H, self.n_slots, dtype=torch.bfloat16, **z)
+            self.slot_of = torch.full((B, H, self.cap_cells), -1, dtype=torch.int32, **z)
+            self.cell_in = torch.full((B, H, self.n_slots), -1, dtype=torch.int32, **z)
+            stat_cells = self.n_slots
+        else:
+            raise ValueError(f"unknown store mode {mode!r}")
+        if mode != "bf16":
+            self.khot = torch.zeros(B, H, CELL, D, dtype=torch.bfloat16, **z)
+            self.vhot = torch.zeros(B, H, CELL, D, dtype=torch.bfloat16, **z)
+        self.kbar = torch.zeros(B, H, stat_cells, D, dtype=torch.float32, **z)
+        self.ceil = torch.zeros(B, H, self.cap_cells, dtype=torch.float32, **z)
+        self.top_idx = torch.full((B, H, P), -1, dtype=torch.int32, **z)
+        self.top_blk = torch.zeros(B, H, dtype=torch.int32, **z)
+        self.status = torch.zeros(L.ST_WORDS, dtype=torch.int32, **z)
+
+    def nbytes(self) -> int:
+        ts = (self.kbuf, self.vbuf, self.kq, self.vq, self.ks, self.vs, self.khot, self.vhot, self.slot_of, self.cell_in,
+              self.kbar, self.ceil, self.top_idx, self.top_blk, self.status)
+        return sum(t.numel() * t.element_size() for t in ts if t is not None)
+
+    def struct(self) -> L.FslState:
+        s = L.FslState()
+        s.store_mode = self.MODES[self.mode]
+        s.B, s.H, s.D, s.P, s.Wc, s.W, s.Bq, s.kk, s.n_slots = (self.B, self.H, self.D, self.P, self.Wc, self.W, self.Bq,
+                                                              self.kk, self.n_slots)
+        s.cap_rows, s.cap_cells = self.cap_rows, self.cap_cells
+        if self.kbuf is not None:
+            s.kbuf, s.vbuf, s.buf_sb, s.buf_sh = self.kbuf.data_ptr(), self.vbuf.data_ptr(), self.kbuf.stride(0), self.kbuf.stride(1)
+        if self.kq is not None:
+            s.kq, s.vq, s.q_sb, s.q_sh = self.kq.data_ptr(), self.vq.data_ptr(), self.kq.stride(0), self.kq.stride(1)
+            s.ks, s.vs, s.sc_sb, s.sc_sh = self.ks.data_ptr(), self.vs.data_ptr(), self.ks.stride(0), self.ks.stride(1)
+            s.khot, s.vhot, s.hot_sb, s.hot_sh = self.khot.data_ptr(), self.vhot.data_ptr(), self.khot.stride(0), self.khot.stride(1)
+        s.kbar, s.kbar_sb, s.kbar_sh = self.kbar.data_ptr(), self.kbar.stride(0), self.kbar.stride(1)
+        s.ceil, s.ceil_sb, s.ceil_sh = self.ceil.data_ptr(), self.ceil.stride(0), self.ceil.stride(1)
+        if self.slot_of is not None:
+            s.slot_of, s.so_sb, s.so_sh = self.slot_of.data_ptr(), self.slot_of.stride(0), self.slot_of.stride(1)
+            s.cell_in, s.ci_sb, s.ci_sh = self.cell_in.data_ptr(), self.cell_in.stride(0), self.cell_in.stride(1)
+        s.top_idx, s.top_blk, s.status = self.top_idx.data_ptr(), self.top_blk.data_ptr(), self.status.data_ptr()
+        return s
+
+    @torch.no_grad()
+    def prefill(self, K, V, N: int, kbar=None, ceil=None):
+        """Load the store from the un-rotated K, V (B,H,N,D) of a prompt: cell statistics (recomputed unless handed
+        over), the first decode block's top-P list, the completed cells (quantised / copied / the kept slots) and the
+        open cell's rows."""
+        ncell = N // CELL
+        if ncell > self.cap_cells or N > self.cap_rows:
+            raise ValueError(f"KV store sized for {self.cap_rows} rows, prompt has {N}")
+        if kbar is None or ceil is None:
+            kbar, ceil = cell_stats(K, ncell)
+        self.status.zero_()
+        self.top_idx.fill_(-1)
+        blk = (N // self.Bq) * self.Bq
+        self.top_blk.fill_(blk)
+        if ncell > 0:
+            self.ceil[:, :, :ncell].copy_(ceil)
+            nb = blk // self.Bq + 1
+            topp = fsl_prefix_topp(ceil, ncell, self.Bq, nb, self.P)
+            self.top_idx.copy_(topp[:, nb - 1].view(self.B, self.H, self.P))
+        if self.mode == "bf16":
+            self.kbuf[:, :, :N].copy_(K[:, :, :N])
+            self.vbuf[:, :, :N].copy_(V[:, :, :N])
+            if ncell > 0:
+                self.kbar[:, :, :ncell].copy_(kbar)
+        elif self.mode == "int8":
+            if ncell > 0:
+                cell_ingest(K, V, ncell=ncell, kq=self.kq, ks=self.ks, vq=self.vq, vs=self.vs)
+                self.kbar[:, :, :ncell].copy_(kbar)
+        else:
+            slot_prefill(self, K, V, kbar if ncell > 0 else self.kbar, N)
+        r = N - ncell * CELL
+        if r > 0 and self.mode != "bf16":
+            self.khot[:, :, :r].copy_(K[:, :, ncell * CELL:N])
+            self.vhot[:, :, :r].copy_(V[:, :, ncell * CELL:N])
+
+    def faults(self):
+        """(slot overflows, readable cells without a slot, rejected indices): a host sync."""
+        f = self.status.tolist()
+        return int(f[L.ST_SLOT_OVERFLOW]), int(f[L.ST_POOL_NO_SLOT]), int(f[L.ST_BAD_INDEX])
+
+
+def slot_prefill(state: FslDecodeState, K, V, kbar_cells, N: int):
+    _need_cuda(K, V, kbar_cells)
+    a = L.SlotPrefill()
+    a.st = state.struct()
+    a.k, a.v = _bhnd(K, "K"), _bhnd(V, "V")
+    assert kbar_cells.dtype == torch.float32 and kbar_cells.stride(-1) == 1 and kbar_cells.stride(2) == state.D
+    a.kbar_cells, a.kc_sb, a.kc_sh = kbar_cells.data_ptr(), kbar_cells.stride(0), kbar_cells.stride(1)
+    a.N = int(N)
+    L.call("fsattn_slot_prefill", a, _stream(K))
+
+
+def fsl_decode_step(state: FslDecodeState, q, k, v, pos_t, cos, sin, lam, sigma, lrs, norm_w, *, scale: float, eps: float,
+                    y=None, sel_out=None, splits: int = 8):
+    """One decode token of one FS-L layer. q,k,v: (B,H,D) bf16 views with equal strides and unit inner stride (e.g. slices
+    of a fused QKV projection); pos_t: int64 device scalar; lam/sigma/lrs (H) fp32, norm_w (D) fp32 (all device tensors
+    that stay alive until the launch has run). Returns y (B, H*D) bf16."""
+    _need_cuda(q, k, v, pos_t, cos, sin, lam, sigma, lrs, norm_w)
+    B, H, D = state.B, state.H, state.D
+    for t in (q, k, v):
+        assert t.dtype == torch.bfloat16 and tuple(t.shape) == (B, H, D) and t.stride(-1) == 1 and t.stride() == q.stride()
+    for t in (lam, sigma, lrs, norm_w):
+        assert t.dtype == torch.float32 and t.is_contiguous()
+    assert pos_t.dtype == torch.int64 and cos.dtype == torch.bfloat16 and cos.is_contiguous() and cos.shape[1] == D
+    if y is None:
+        y = torch.empty(B, H * D, dtype=torch.bfloat16, device=q.device)
+    a = L.FslDecode()
+    a.st = state.struct()
+    a.q, a.k, a.v, a.in_sb, a.in_sh = q.data_ptr(), k.data_ptr(), v.data_ptr(), q.stride(0), q.stride(1)
+    a.pos = pos_t.data_ptr()
+    a.cos, a.sin = cos.data_ptr(), sin.data_ptr()
+    a.lam, a.sigma, a.lrs, a.norm_w = lam.data_ptr(), sigma.data_ptr(), lrs.data_ptr(), norm_w.data_ptr()
+    a.scale, a.eps = float(scale), float(eps)
+    a.y, a.sel_out = y.data_ptr(), _p(sel_out)
+    a.splits = int(splits)
+    L.call("fsattn_fsl_decode_step", a, _stream(q))
+    return y
+
+
+def default_scale(D: int) -> float:
+    return 1.0 / math.sqrt(D)

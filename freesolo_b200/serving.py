@@ -1,0 +1,289 @@
+"""Serving plumbing around the attention hot path: the FreeSoloLM trunk (embedding, RMSNorm, SwiGLU, tied LM head; module
+and parameter names of experiments/scaling/model.py so a reference state dict loads), the serve presets of
+experiments/scaling/bench_efficiency.py:72-87, a cached prefill driver and the whole-step CUDA-graph decoder
+(experiments/scaling/decode_graph.py:27-289).
+
+The trunk's dense layers are library GEMMs (cuBLAS through torch); the attention layer is ``fsattn.FSAttn``.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .fsattn import FSAttn, FSKVCache, make_caches
+from .fsattn import kv_bounded as _kvb
+
+MODEL_CONFIGS = {   # experiments/scaling/model.py:38-80 (vocab 32000 as the benchmark loads them)
+    "debug": dict(d_model=256, n_layers=4, n_heads=4, d_ff=688, max_seq_len=1024, vocab_size=32000),
+    "340m": dict(d_model=1024, n_layers=24, n_heads=16, d_ff=2816, max_seq_len=2048, vocab_size=32000),
+    "800m": dict(d_model=1536, n_layers=24, n_heads=16, d_ff=4224, max_seq_len=2048, vocab_size=32000),
+}
+
+
+def serve_kwargs(serve: str, fsb_union_tau_quantile: float = 0.0) -> dict:
+    """experiments/scaling/bench_efficiency.py:72-87."""
+    kw = dict(window_size=512, long_range_variant="cell_topk", cell_stride=32, cell_topk=4, cell_select="score",
+              sel_strict_causal=1, use_rope=True, fs_uniform_sr=True, rope_long_range=False)
+    if serve == "sparse":
+        kw.update(cell_prune_kernel=1, cell_prune_pool=64, cell_prune_window=8, cell_prune_blkchunk=16)
+    elif serve == "fsb":
+        kw.update(cell_prune_kernel=0, fsb_enabled=True, fsb_policy="fixed", fsb_width=16, fsb_delta=0,
+                  fsb_node_score="bound", fsb_bound_radius_coef=8.0, fsb_tree="forest", fsb_read_top=4,
+                  fsb_rerank_score="lse_pos", fsb_rerank_query="raw", fsb_union_width=16)
+        if fsb_union_tau_quantile > 0:
+            kw["fsb_union_tau_quantile"] = fsb_union_tau_quantile
+    else:
+        kw.update(cell_prune_kernel=0)
+    return kw
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, dim: int, eps: float = 1e-6):
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(dim))
+
+    def forward(self, x):
+        return F.rms_norm(x, (x.shape[-1],), self.weight, self.eps)
+
+
+class SwiGLU(nn.Module):
+    def __init__(self, d_model: int, d_ff: int):
+        super().__init__()
+        self.w_gate = nn.Linear(d_model, d_ff, bias=False)
+        self.w_up = nn.Linear(d_model, d_ff, bias=False)
+        self.w_down = nn.Linear(d_ff, d_model, bias=False)
+
+    def _ensure_gu_cache(self):
+        """One fused (2*d_ff, d) weight the gate and up weights are views of (experiments/scaling/model.py:111-125)."""
+        wg, wu = self.w_gate.weight, self.w_up.weight
+        key = (wg.data_ptr(), wg._version, wu.data_ptr(), wu._version, wg.dtype)
+        c = getattr(self, "_w_gu_cache", None)
+        if c is None or c[0] != key:
+            d_ff = wg.shape[0]
+            gu = torch.cat([wg.data, wu.data], dim=0)
+            self.w_gate.weight.data = gu[:d_ff]
+            self.w_up.weight.data = gu[d_ff:]
+            wg, wu = self.w_gate.weight, self.w_up.weight
+            c = ((wg.data_ptr(), wg._version, wu.data_ptr(), wu._version, wg.dtype), gu)
+            self._w_gu_cache = c
+        return c[1], self.w_gate.weight.shape[0]
+
+    def forward(self, x):
+        gu_w, d_ff = self._ensure_gu_cache()
+        gu = F.linear(x, gu_w)
+        return self.w_down(F.silu(gu[..., :d_ff]) * gu[..., d_ff:])
+
+
+class AttentionWithRoPE(nn.Module):
+    def __init__(self, d_model, n_heads, max_seq_len, attn_type="fsattn", causal=True, layer_idx=0, **attn_kwargs):
+        super().__init__()
+        if attn_type != "fsattn":
+            raise ValueError(f"attn_type {attn_type!r} is not part of this build")
+        self.attn_type = attn_type
+        use_rope = attn_kwargs.pop("use_rope", True)
+        self.fsattn = FSAttn(d_model, n_heads, causal=causal, bias=False, use_rope=use_rope, max_seq_len=max_seq_len,
+                             **attn_kwargs)
+
+    def forward(self, x, cache=None):
+        return self.fsattn(x, cache=cache)
+
+
+class TransformerBlock(nn.Module):
+    def __init__(self, d_model, n_heads, d_ff, max_seq_len, attn_type="fsattn", layer_idx=0, **attn_kwargs):
+        super().__init__()
+        self.ln1 = RMSNorm(d_model)
+        self.attn = AttentionWithRoPE(d_model, n_heads, max_seq_len, attn_type=attn_type, causal=True, layer_idx=layer_idx,
+                                      **attn_kwargs)
+        self.ln2 = RMSNorm(d_model)
+        self.ffn = SwiGLU(d_model, d_ff)
+
+    def forward(self, x, cache=None):
+        """RMSNorm -> attention -> residual -> RMSNorm -> SwiGLU -> residual (experiments/scaling/model.py:211-237); the
+        FFN of a long prefill runs in token chunks to bound its intermediate."""
+        x = x + self.attn(self.ln1(x), cache=cache)
+        N = x.shape[1]
+        chunk = 16384
+        if N > chunk:
+            for s0 in range(0, N, chunk):
+                xc = x[:, s0:s0 + chunk]
+                xc.add_(self.ffn(self.ln2(xc)))
+            return x
+        return x + self.ffn(self.ln2(x))
+
+
+class FreeSoloLM(nn.Module):
+    """experiments/scaling/model.py:248-359, inference part."""
+
+    def __init__(self, vocab_size=32000, d_model=1024, n_layers=24, n_heads=16, d_ff=2816, max_seq_len=2048,
+                 attn_type="fsattn", **attn_kwargs):
+        super().__init__()
+        self.d_model, self.vocab_size = d_model, vocab_size
+        self.tok_emb = nn.Embedding(vocab_size, d_model)
+        self.blocks = nn.ModuleList([TransformerBlock(d_model, n_heads, d_ff, max_seq_len, attn_type, layer_idx=i,
+                                                      **attn_kwargs) for i in range(n_layers)])
+        self.ln_final = RMSNorm(d_model)
+        self.lm_head = nn.Linear(d_model, vocab_size, bias=False)
+        self.lm_head.weight = self.tok_emb.weight
+        self._init_weights()
+
+    def _init_weights(self):
+        """N(0, 0.02) for every matrix (experiments/scaling/model.py:318-323)."""
+        for name, p in self.named_parameters():
+            if p.dim() > 1 and "tok_emb" not in name and "long_range_scale" not in name:
+                nn.init.normal_(p, mean=0.0, std=0.02)
+        nn.init.normal_(self.tok_emb.weight, mean=0.0, std=0.02)
+
+    @classmethod
+    def from_config(cls, name: str, **kwargs):
+        cfg = dict(MODEL_CONFIGS[name])
+        cfg.update(kwargs)
+        return cls(**cfg)
+
+    def count_params(self) -> int:
+        return sum(p.numel() for p in self.parameters())
+
+
+def extend_rope_cache(model, n: int):
+    for blk in model.blocks:
+        blk.attn.fsattn.rope.tables_bf16(n)
+
+
+@torch.no_grad()
+def trunk_cached(model, idx, caches, last_n: int | None = None):
+    """experiments/scaling/kv_cache.py:541-547: embedding, blocks with their caches, final norm."""
+    x = model.tok_emb(idx)
+    for i, blk in enumerate(model.blocks):
+        x = blk(x, cache=caches[i])
+    if last_n is not None and x.shape[1] > last_n:
+        x = x[:, -last_n:].contiguous()
+    return model.ln_final(x)
+
+
+def lm_head(model, hidden):
+    """Last-token logits with the tied head (experiments/scaling/longctx_infer.py:281-290 under bf16 autocast)."""
+    return F.linear(hidden, model.lm_head.weight)
+
+
+class GraphedDecoder:
+    """Whole-step CUDA-graph greedy decoder for FS-L models (experiments/scaling/decode_graph.py:27-289), any batch size.
+
+    One graph replay per token and nothing else: the token id, the position and every layer's KV bookkeeping (row append,
+    cell close, top-P refresh, slot frees) live on the device, so consecutive steps need no host work between replays.
+    kv: "bounded" (default, as the reference's FSL_KV_BOUNDED=1), "int8" or "bf16"."""
+
+    def __init__(self, model, prompt_ids, Lmax, device="cuda", dtype=torch.bfloat16, kv="bounded", eager_steps=2):
+        self.m = model
+        self.dev = torch.device(device)
+        self.dt = dtype
+        self.Lmax = int(Lmax)
+        self.blocks = list(model.blocks)
+        self.attn = [b.attn.fsattn for b in self.blocks]
+        self.prompt = prompt_ids
+        self.kv = kv
+        self.cache = None
+        self.graph = None
+        self.eager_steps = eager_steps
+        self._steps = 0
+        self.bounded_kv = False
+
+    @torch.no_grad()
+    def prefill(self):
+        m = self.m
+        seq = self.prompt.to(self.dev)
+        if seq.dim() == 1:
+            seq = seq.view(1, -1)
+        B, P0 = seq.shape
+        extend_rope_cache(m, self.Lmax + 8)
+        self.cache = make_caches(m, reserve=max(0, self.Lmax - P0))
+        kv = self.kv
+        if kv == "bounded" and not (P0 >= self.attn[0].window_size and _kvb.supported(self.attn, self.dt, self.dev)):
+            kv = "int8"      # prompts shorter than the window keep the full store (decode_graph.py:89-93)
+        for c in self.cache:
+            if kv == "bounded":
+                c.enable_bounded()
+            elif kv == "int8":
+                c.enable_int8()
+        self.bounded_kv = kv == "bounded"
+        hidden = trunk_cached(m, seq, self.cache, last_n=1)
+        logits = lm_head(m, hidden[:, -1])
+        self.tok = logits.argmax(dim=-1).view(B, 1)
+        self.pos = P0
+        self.pos_t = torch.full((), P0, dtype=torch.int64, device=self.dev)
+        self.bufs = [{"pos_t": self.pos_t, "cache": c} for c in self.cache]
+        for blk in self.blocks:
+            blk.ffn._ensure_gu_cache()
+        return self.tok
+
+    def _trunk_step(self):
+        """One token through the model: reads self.tok and pos_t, overwrites self.tok with the greedy next token and
+        advances pos_t, all on the device."""
+        m = self.m
+        x = m.tok_emb(self.tok)
+        for i, blk in enumerate(self.blocks):
+            x = x + self.attn[i].graph_decode_layer(blk.ln1(x), self.bufs[i])
+            x = x + blk.ffn(blk.ln2(x))
+        logits = lm_head(m, m.ln_final(x)[:, -1])
+        self.logits = logits
+        self.tok.copy_(logits.argmax(dim=-1, keepdim=True))
+        self.pos_t.add_(1)
+
+    @torch.no_grad()
+    def _capture(self):
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._trunk_step()
+
+    @torch.no_grad()
+    def step(self):
+        """Advance one token; returns the device tensor holding the new token ids (B,1)."""
+        if self.pos + 1 >= self.Lmax:
+            raise RuntimeError(f"decoder sized for {self.Lmax} positions")
+        if self.graph is None and self._steps >= self.eager_steps:
+            self._capture()
+        if self.graph is None:
+            self._trunk_step()
+        else:
+            self.graph.replay()
+        self._steps += 1
+        self.pos += 1
+        return self.tok
+
+    def sync_caches(self):
+        for c in self.cache:
+            c.pos = self.pos
+            c._ncell = self.pos // c.s
+
+    def kv_faults(self) -> tuple:
+        """(slot overflows, readable cells without a slot, rejected indices) over all layers; one host sync."""
+        tot = torch.stack([c.state.status for c in self.cache]).sum(0).tolist()
+        return int(tot[0]), int(tot[1]), int(tot[2])
+
+    def kv_bytes(self) -> int:
+        return sum(c.state.nbytes() for c in self.cache)
+
+
+@torch.no_grad()
+def cached_generate(model, prompt_ids, max_new_tokens, device="cuda", kv="bf16"):
+    """Greedy generation through the eager per-token path (experiments/scaling/kv_cache.py:484-526)."""
+    seq = prompt_ids.to(device)
+    if seq.dim() == 1:
+        seq = seq.view(1, -1)
+    caches = make_caches(model, reserve=max_new_tokens)
+    for c in caches:
+        if kv == "int8":
+            c.enable_int8()
+        elif kv == "bounded":
+            c.enable_bounded()
+    extend_rope_cache(model, seq.shape[1] + max_new_tokens + 8)
+    step_in = seq
+    out = []
+    for _ in range(max_new_tokens):
+        hidden = trunk_cached(model, step_in, caches, last_n=1)
+        nxt = lm_head(model, hidden[:, -1]).argmax(dim=-1)
+        out.append(nxt)
+        step_in = nxt.view(-1, 1)
+    gen = torch.stack(out, dim=1) if out else seq[:, :0]
+    return torch.cat([seq, gen], dim=1)

@@ -1,0 +1,212 @@
+/* C ABI of libfsattn_b200: hand-written sm_100a kernels for the FreeSolo sparse-attention inference hot path.
+ *
+ * The reference project (zekun-shi/freesolo) has no C ABI of its own: its native kernels are CUDA sources compiled at
+ * run time and launched from Python with raw device pointers (src/fsattn/fsl_select_cuda.py:132-142,
+ * src/fsattn/fsb_beam_cuda.py:224-237) or Triton kernels. Each entry point below names the reference function or
+ * kernel launch it replaces. The conventions mirror how the reference launches its kernels:
+ *
+ *  - every pointer is a DEVICE pointer owned by the caller; the library never allocates or frees device memory
+ *    (outputs are pre-allocated by the caller, as the reference does with torch.empty before each launch);
+ *  - every call is asynchronous on the CUDA stream passed in (a cudaStream_t cast to void*; NULL = legacy default
+ *    stream), does not synchronise, and reads positions from device scalars, so it may be captured in a CUDA graph;
+ *  - strides are in ELEMENTS of the tensor's dtype; the innermost (head-dim) stride is always 1;
+ *  - return value 0 = launched; negative = rejected on the host before any launch (fsattn_last_error() has the text).
+ *    Conditions detected on the device (slot overflow, pool cell without a slot) are counted in a caller-provided
+ *    int32 status buffer, read by the caller where the reference reads its own fault counters
+ *    (src/fsattn/kv_bounded.py:104,225-228).
+ *
+ * Tensor vocabulary: B batch, H heads, D head dim (64, 96 or 128), N tokens, s = 32 tokens per cell ("chunk"),
+ * Bq = 128 queries per block, kk cells read per query, P pool size, Wc newest-cell slots, W window.
+ */
+#ifndef FSATTN_B200_H
+#define FSATTN_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define FSATTN_API __attribute__((visibility("default")))
+#else
+#define FSATTN_API
+#endif
+
+#define FSATTN_OK 0
+#define FSATTN_EINVAL (-1)        /* bad argument (shape, alignment, null pointer) */
+#define FSATTN_EUNSUPPORTED (-2)  /* a configuration the kernels do not cover (no fallback exists) */
+#define FSATTN_ELAUNCH (-3)       /* the CUDA runtime refused the launch */
+
+#define FSATTN_CELL 32            /* tokens per cell the kernels are specialised for */
+#define FSATTN_MAX_POOL 128       /* P + Wc upper bound */
+#define FSATTN_MAX_KK 8
+
+/* status words written by device code (int32 each) */
+#define FSATTN_ST_SLOT_OVERFLOW 0 /* completed cell found no free slot (bounded store) */
+#define FSATTN_ST_POOL_NO_SLOT 1  /* readable pool cell without a slot (bounded store) */
+#define FSATTN_ST_BAD_INDEX 2     /* an index failed a bounds check and its access was skipped */
+#define FSATTN_ST_WORDS 4
+
+typedef void* fsattn_stream_t;
+
+FSATTN_API int fsattn_version(void);
+FSATTN_API const char* fsattn_last_error(void);
+/* Per-device one-time setup (dynamic shared-memory opt-in of the kernels). Call once per device before other calls. */
+FSATTN_API int fsattn_init(int device);
+
+/* ---- a (B,H,N,D) view with unit inner stride, bf16 ------------------------------------------------------------- */
+typedef struct {
+    const void* ptr;
+    int64_t sb, sh, sn; /* element strides of batch, head, token */
+} fsattn_bhnd_t;
+
+/* ---- chunk statistics + int8 codec ------------------------------------------------------------------------------
+ * Replaces: FSKVCache._cell_stats_of / fsl_select_cuda.cache_cell_stats (experiments/scaling/kv_cache.py:274-285,
+ * src/fsattn/fsl_select.cu:79-125), kv_int8.quantize_cells_fast / dequant_cells (src/fsattn/kv_int8.py:82-118).
+ * One pass over ncell completed cells of K (and V): any of the outputs may be NULL to skip it.
+ *   kbar  (B,H,*,D) fp32: chunk-mean key, mean taken in bf16 like the reference (bf16-rounded value stored as fp32)
+ *   ceil  (B,H,*)   fp32: largest token-key L2 norm of the cell
+ *   kq,vq (B,H,*,D) int8 codes; ks,vs (B,H,*) bf16 scales: scale = bf16(max|x|/127) (1.0 if 0), q = rint(x/scale)
+ * Cells [0, ncell) of the inputs are written at cell index cell0 + c of the outputs. */
+typedef struct {
+    fsattn_bhnd_t k, v; /* v.ptr may be NULL */
+    int32_t B, H, D, ncell, cell0;
+    float* kbar; int64_t kbar_sb, kbar_sh;   /* cell stride = D */
+    float* ceil; int64_t ceil_sb, ceil_sh;   /* cell stride = 1 */
+    int8_t* kq; int8_t* vq; int64_t q_sb, q_sh; /* row stride = D */
+    void* ks; void* vs; int64_t sc_sb, sc_sh;   /* bf16, cell stride = 1 */
+} fsattn_cell_ingest_t;
+FSATTN_API int fsattn_cell_ingest(const fsattn_cell_ingest_t* a, fsattn_stream_t stream);
+
+/* x = bf16(f32(q) * f32(scale[row / 32])) for rows [0, nrows) of every (b,h). Replaces kv_int8.dequant_cells
+ * (src/fsattn/kv_int8.py:63-71). */
+typedef struct {
+    const int8_t* q; int64_t q_sb, q_sh;
+    const void* sc; int64_t sc_sb, sc_sh;
+    void* out; int64_t o_sb, o_sh; /* bf16 (B,H,*,D), row stride D */
+    int32_t B, H, D; int64_t nrows;
+} fsattn_dequant_t;
+FSATTN_API int fsattn_dequant_cells(const fsattn_dequant_t* a, fsattn_stream_t stream);
+
+/* ---- FS-L prefix top-P ---------------------------------------------------------------------------------------------
+ * Replaces attention.py:766-778 (topk of the masked ceilings per block) / fsl_topp, fsl_topp_par
+ * (src/fsattn/fsl_select.cu:247-391). For every query block n in [0, nb): the min(P, vis_n) best cells among the
+ * vis_n = min(ncell, n*Bq/32) visible ones under (ceiling desc, cell index asc), in that order; unused slots -1.
+ * topp (B*H, nb, P) int32. */
+typedef struct {
+    const float* ceil; int64_t ceil_sb, ceil_sh;
+    int32_t B, H, ncell, Bq, nb, P;
+    int32_t* topp;
+} fsattn_fsl_topp_t;
+FSATTN_API int fsattn_fsl_prefix_topp(const fsattn_fsl_topp_t* a, fsattn_stream_t stream);
+
+/* ---- FS-L prefill selection -----------------------------------------------------------------------------------------
+ * Replaces attention.py:779-821 / fsl_prep + fsl_select + fsl_fused (src/fsattn/fsl_select.cu:396-769): candidate
+ * slots = top-P list of the block, then the Wc newest visible cells; score = (q.kbar)*scale + lam*ceil*erf(|p-cen|/
+ * (2 sigma)) in fp32, -1e9 for slots that are invalid, invisible or repeat an earlier slot's cell; per query the kk
+ * best by (score desc, slot asc); sel holds the cell id or -1. sel (B,H,nb*Bq,kk) int32; queries >= N are padding
+ * and are scored as zero vectors like the reference. margin (optional, same leading shape, fp32): smallest gap
+ * between consecutive entries of the best kk+1 scores. */
+typedef struct {
+    fsattn_bhnd_t q;
+    const float* kbar; int64_t kbar_sb, kbar_sh;
+    const float* ceil; int64_t ceil_sb, ceil_sh;
+    const int32_t* topp; /* (B*H, nb, P) */
+    const float* lam; const float* sigma; /* (H) */
+    int32_t B, H, D, N, ncell, Bq, nb, P, Wc, kk;
+    float scale;
+    int32_t* sel; float* margin;
+} fsattn_fsl_select_t;
+FSATTN_API int fsattn_fsl_select(const fsattn_fsl_select_t* a, fsattn_stream_t stream);
+
+/* ---- window branch, prefill -----------------------------------------------------------------------------------------
+ * Replaces FSAttn._short_range / _chunked_rope_window (src/fsattn/attention.py:225-259) and
+ * local_attention._batched_sliding_window_rope (src/utils/local_attention.py:191-235): causal band softmax attention
+ * max(0,p-W) <= j <= p with rotate-half RoPE applied to Q and K at absolute positions pos0 + i. cos/sin (L,D) bf16
+ * tables (row stride D). out (B,N,H,D) bf16 = W_o's input layout. */
+typedef struct {
+    fsattn_bhnd_t q, k, v;
+    const void* cos; const void* sin;
+    int32_t B, H, D, N, W, pos0;
+    float scale;
+    void* out; /* (B,N,H*D) bf16 contiguous */
+    int32_t impl; /* 0 = default (tensor-core kernel when the shape allows), 1 = force the CUDA-core kernel */
+} fsattn_window_prefill_t;
+FSATTN_API int fsattn_window_prefill(const fsattn_window_prefill_t* a, fsattn_stream_t stream);
+
+/* ---- fused readout + combine, prefill ---------------------------------------------------------------------------------
+ * Replaces FSAttn._cell_fused_lr / readout_triton.readout_combine (src/fsattn/attention.py:344-361,
+ * src/fsattn/readout_triton.py:34-159) and indexed_cell_attention (src/fsattn/cell_select_triton.py:97-282):
+ * per query softmax attention over the tokens (tok < query position) of its valid distinct selected cells,
+ * o rounded to bf16, lr = (o * rsqrt(mean(o^2)+eps)) * norm_w, y = bf16(sr + lrs[h] * lr).
+ * sr and y are (B,N,H*D) bf16; y may alias sr (in place, as the reference does). */
+typedef struct {
+    fsattn_bhnd_t q, k, v;
+    const int32_t* sel; int64_t sel_sb, sel_sh; /* (B,H,*,kk), row stride kk */
+    const void* sr; void* y;
+    const float* norm_w; const float* lrs;
+    int32_t B, H, D, N, n_kv, Bq, kk, q_pos0;
+    float scale, eps;
+} fsattn_readout_combine_t;
+FSATTN_API int fsattn_readout_combine(const fsattn_readout_combine_t* a, fsattn_stream_t stream);
+
+/* ---- FS-L decode state + fused decode step -----------------------------------------------------------------------------
+ * One layer's decode-time KV state. store_mode: 0 = bf16 full store, 1 = int8 full store (kv_int8), 2 = int8 bounded
+ * slot store (kv_bounded.SlotStore: rows of cell c live at slot_of[c]*32 + t%32). Layout per (b,h):
+ *   kbuf,vbuf (cap,D) bf16 [mode 0]; kq,vq (rows,D) int8 + ks,vs (cells|slots) bf16 [modes 1,2];
+ *   khot,vhot (32,D) bf16 open cell [modes 1,2]; kbar (cells|slots, D) fp32; ceil (cells) fp32;
+ *   slot_of (cells) int32, cell_in (slots) int32 [mode 2]; top_idx (P) int32 = the block's top-P cells in pool order,
+ *   top_blk (1) int32 = block start that list is valid for.
+ * Rows below (pos/32)*32 are completed cells; later rows are the open cell. */
+typedef struct {
+    int32_t store_mode, B, H, D, P, Wc, W, Bq, kk, n_slots;
+    int64_t cap_rows, cap_cells;
+    void* kbuf; void* vbuf; int64_t buf_sb, buf_sh;
+    int8_t* kq; int8_t* vq; int64_t q_sb, q_sh;
+    void* ks; void* vs; int64_t sc_sb, sc_sh;
+    void* khot; void* vhot; int64_t hot_sb, hot_sh;
+    float* kbar; int64_t kbar_sb, kbar_sh;
+    float* ceil; int64_t ceil_sb, ceil_sh;
+    int32_t* slot_of; int64_t so_sb, so_sh;
+    int32_t* cell_in; int64_t ci_sb, ci_sh;
+    int32_t* top_idx; int32_t* top_blk; /* (B,H,P), (B,H) contiguous */
+    int32_t* status;                    /* FSATTN_ST_WORDS int32 */
+} fsattn_fsl_state_t;
+
+/* One decode token of one FS-L layer in ONE launch. Replaces the chain of FSAttn.graph_decode_layer
+ * (src/fsattn/attention.py:1493-1559): _sr_kv_rope(_int8)_kernel + 2 einsums + _sr_softmax_cast_kernel (window,
+ * src/utils/trunk_triton.py:194-480,1086-1211), _lrc_comb_int8_kernel / _fsl_lr_decode_combine_kernel (score the
+ * pool, top-kk, readout, lr_norm, combine; trunk_triton.py:536-704,1688-1872), and the host-side bookkeeping between
+ * graph replays: the block's pool refresh every Bq tokens (attention.py:1313-1369, kv_bounded.py:175-221) and the
+ * cell close every 32 tokens (kv_cache.py:326-382, kv_bounded.py:155-173), both decided on the device from *pos.
+ * q,k,v: the new token's projections (B,H,D) bf16 (strides sb, sh). y (B, H*D) bf16 = W_o's input.
+ * sel_out (optional) (B,H,kk) int32: the cells read. splits = CTAs per (b,h) (1, 2, 4 or 8; a thread-block cluster). */
+typedef struct {
+    fsattn_fsl_state_t st;
+    const void* q; const void* k; const void* v; int64_t in_sb, in_sh;
+    const int64_t* pos;                  /* device scalar: index of the new token */
+    const void* cos; const void* sin;    /* (L,D) bf16 */
+    const float* lam; const float* sigma; const float* lrs; const float* norm_w;
+    float scale, eps;
+    void* y; int32_t* sel_out;
+    int32_t splits;
+} fsattn_fsl_decode_t;
+FSATTN_API int fsattn_fsl_decode_step(const fsattn_fsl_decode_t* a, fsattn_stream_t stream);
+
+/* Bounded store after a prefill of N tokens. Replaces SlotStore.prefill (src/fsattn/kv_bounded.py:115-152): keeps the
+ * top-P cells visible to the first decode block (top_idx, already filled for block (N/Bq)*Bq) and every cell from
+ * c_lo = max(0, min((blk-W)/32, m_vis-Wc)) on; slots in cell order; writes slot_of, cell_in, quantises the kept cells
+ * of k/v into their slots and copies their kbar rows (kbar_cells (B,H,ncell,D) fp32 -> st.kbar per slot). */
+typedef struct {
+    fsattn_fsl_state_t st;
+    fsattn_bhnd_t k, v;
+    const float* kbar_cells; int64_t kc_sb, kc_sh;
+    int32_t N;
+} fsattn_slot_prefill_t;
+FSATTN_API int fsattn_slot_prefill(const fsattn_slot_prefill_t* a, fsattn_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FSATTN_B200_H */

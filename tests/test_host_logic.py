@@ -1,0 +1,73 @@
+"""Host-side mirror of the reference API: construction, names, configuration errors (CPU only)."""
+import pytest
+import torch
+
+from freesolo_b200 import FSAttn, FSKVCache
+from freesolo_b200.fsattn import kv_bounded
+from freesolo_b200.fsattn.attention import Rotary
+from freesolo_b200.serving import FreeSoloLM, MODEL_CONFIGS, serve_kwargs
+from oracle import fsl
+
+
+def _attn(**over):
+    kw = serve_kwargs("sparse")
+    kw.update(over)
+    return FSAttn(d_model=256, n_heads=4, causal=True, bias=False, max_seq_len=1024, **kw)
+
+
+def test_state_dict_names_match_the_reference():
+    a = _attn()
+    keys = set(a.state_dict().keys())
+    # src/fsattn/attention.py:129-158: parameters and persistent buffers of an FS-L layer (rope tables are non-persistent)
+    assert keys == {"sel_scale", "log_sigma", "long_range_scale", "lr_norm.scale", "W_q.weight", "W_k.weight", "W_v.weight",
+                    "W_o.weight"}
+    assert tuple(a.long_range_scale.shape) == (4, 1, 1) and a.head_dim == 64 and a._cell_block == 128
+    assert torch.allclose(a.sigma, torch.full((4,), 4.0))
+
+
+def test_lm_parameter_count_and_names():
+    m = FreeSoloLM.from_config("debug", max_seq_len=512, **serve_kwargs("sparse"))
+    names = dict(m.named_parameters())
+    assert "blocks.0.attn.fsattn.W_q.weight" in names and "blocks.3.ffn.w_down.weight" in names and "ln_final.weight" in names
+    assert m.lm_head.weight is m.tok_emb.weight
+    c = MODEL_CONFIGS["340m"]
+    d, f, L_, V = c["d_model"], c["d_ff"], c["n_layers"], c["vocab_size"]
+    per_layer = 4 * d * d + 3 * d * f + 2 * d + 2 * 16 + 64   # log_sigma is a buffer when the window is uniform
+    assert L_ * per_layer + V * d + d == 341_101_824      # the reference's 341M
+
+
+def test_rotary_tables_match_oracle_and_grow_in_fp32():
+    r = Rotary(64, 4096)
+    cos, sin = fsl.rope_tables(64, 4096, orig_len=4096)
+    assert torch.equal(r.cos_cached, cos) and torch.equal(r.sin_cached, sin)
+    r = r.to(torch.bfloat16)
+    r._build_cache(6000)
+    cos2, _ = fsl.rope_tables(64, 6000, orig_len=4096)
+    assert r.cos_cached.dtype == torch.bfloat16 and torch.equal(r.cos_cached, cos2.to(torch.bfloat16))
+
+
+def test_uncacheable_configurations_raise():
+    for over in (dict(rope_long_range=True), dict(sel_strict_causal=0), dict(cell_prune_kernel=0), dict(cell_stride=64),
+                 dict(fs_uniform_sr=False), dict(fsb_enabled=True)):
+        with pytest.raises(NotImplementedError):
+            FSKVCache(_attn(**over))
+    a = _attn()
+    with pytest.raises(NotImplementedError):
+        a(torch.zeros(1, 4, 256))            # no cache: the training forward is not part of this build
+    with pytest.raises(RuntimeError):
+        a(torch.zeros(1, 4, 256), cache=FSKVCache(a))    # CPU / fp32 activations: no fallback
+
+
+def test_bounded_slot_count_and_config():
+    a = _attn()
+    assert kv_bounded.slot_count(a) == 64 + 16 + 4 + 1 == 85          # src/fsattn/kv_bounded.py:59-61
+    assert kv_bounded._cfg(a) == (64, 8, 512, 128, 32)
+    assert not kv_bounded.supported([a], torch.bfloat16, "cpu")
+
+
+def test_fused_projection_weights_are_views():
+    a = _attn()
+    w, dm = a._ensure_qkv_cache()
+    assert w.shape == (768, 256) and a.W_k.weight.data_ptr() == w[dm:].data_ptr()
+    w2, _ = a._ensure_qkv_cache()
+    assert w2 is w
