@@ -357,10 +357,13 @@ class FSLLayerOracle:
         self.pos = 0
 
     def _kv_read(self):
-        """K/V as a decode step reads them: completed cells through the int8 codec when enabled, the open cell raw."""
+        """K/V as a decode step reads them with the int8 store: cells completed BEFORE the current token through the
+        codec, the open cell (which includes the current token, even when it is the cell's last) raw. This is the
+        graph decoder's order: the step reads, then the bookkeeping closes the cell
+        (experiments/scaling/decode_graph.py:223-241, 261-289)."""
         if not self.int8:
             return self.K, self.V
-        n_q = (self.K.shape[2] // self.s) * self.s
+        n_q = ((self.K.shape[2] - 1) // self.s) * self.s
         out = []
         for x in (self.K, self.V):
             q, sc = quantize_cells(x[:, :, :n_q], self.s)

@@ -86,7 +86,7 @@ def test_cell_ingest_matches_reference_codes(dev, kind):
     kb_o, ce_o = fsl.cell_stats(K[:, :, :N], 32)
     kb = kbar.cpu()
     mism = (kb != kb_o)
-    assert mism.float().mean() < 1e-3, f"chunk-mean keys: {mism.float().mean():.2e} of the values differ from torch's bf16 mean"
+    assert not mism.any(), f"chunk-mean keys: {int(mism.sum())} values differ from torch bf16 mean"
     assert ((kb - kb_o).abs() <= kb_o.abs() * 2 ** -7 + 1e-30).all(), "chunk-mean key off by more than one bf16 ulp"
     ce = ceil.cpu()
     assert ((ce - ce_o).abs() <= ce_o * 4e-7).all(), "ceilings differ from the oracle by more than 3 ulp"
@@ -140,7 +140,9 @@ def test_prefix_topp_is_the_stable_topk(dev, kind):
     nb = (N + 127) // 128 + 1
     for P in (64, 5):
         got = ops.fsl_prefix_topp(ceil.to(dev), N // 32, 128, nb, P).cpu()
-        want = fsl.fsl_prefix_topp(ceil, 32, 128, nb, P).reshape(-1, nb, P).to(torch.int32)
+        w = fsl.fsl_prefix_topp(ceil, 32, 128, nb, P)                       # (B,H,nb,min(P,M))
+        want = torch.full((w.shape[0] * w.shape[1], nb, P), -1, dtype=torch.int32)
+        want[:, :, :w.shape[-1]] = w.reshape(-1, nb, w.shape[-1]).to(torch.int32)
         assert torch.equal(got, want), f"top-{P} lists differ"
 
 
@@ -260,14 +262,18 @@ def test_layer_prefill_then_decode(dev, kind, mode):
     N, T = int(g["N"]), int(g["T"])
     y, sel, ys, sels, st = _run_layer(dev, g, Q, K, V, mode, splits=4)
     orc = _oracle(g, int8=(mode != "bf16"))
-    y0, sel0, mg0 = orc.prefill(Q[:, :, :N].float(), K[:, :, :N].float(), V[:, :, :N].float())
+    y0, sel0, mg0 = orc.prefill(Q[:, :, :N], K[:, :, :N], V[:, :, :N])
     _sel_check(sel, sel0, mg0, f"{kind}/{mode} prefill selection")
     _close(y, y0, f"{kind}/{mode} prefill output vs oracle")
-    _close(y, torch.from_numpy(g["y_prefill"]), f"{kind}/{mode} prefill output vs reference fp32", mean_rel=8e-3)
+    # against the reference's fp32 run: it took its chunk means in fp32, so a few of its selections differ from the bf16
+    # semantics; the output bound applies to the rows where every head reads the reference's cells
+    agree = (sel.cpu() == torch.from_numpy(g["sel_prefill"])).all(-1).all(1)           # (B, N)
+    assert agree.float().mean() > 0.9
+    _close(y[agree], torch.from_numpy(g["y_prefill"])[agree], f"{kind}/{mode} prefill output vs reference fp32", mean_rel=8e-3)
     worst = 0.0
     for t in range(T):
         sl = slice(N + t, N + t + 1)
-        yo, so, mo = orc.decode(Q[:, :, sl].float(), K[:, :, sl].float(), V[:, :, sl].float())
+        yo, so, mo = orc.decode(Q[:, :, sl], K[:, :, sl], V[:, :, sl])
         _sel_check(sels[t].unsqueeze(2), so, mo, f"{kind}/{mode} decode step {t} (pos {N + t}) selection")
         ma, _ = _close(ys[t].view(-1), yo.reshape(-1), f"{kind}/{mode} decode step {t} (pos {N + t}) output", mean_rel=4e-3)
         worst = max(worst, ma)
@@ -317,7 +323,9 @@ def test_bounded_store_reads_equal_full_int8_store(dev):
     want.scatter_(2, top, True)
     held = st_b.slot_of.cpu()[:, :, :pos // 32] >= 0
     assert torch.equal(held, want), "bounded store does not hold exactly the readable cells"
-    assert torch.equal(st_b.top_idx.cpu().long(), top), "top-P list differs from the stable top-k of the ceilings"
+    ti = st_b.top_idx.cpu().long()
+    assert torch.equal(ti[:, :, :top.shape[-1]], top) and (ti[:, :, top.shape[-1]:] == -1).all(), \
+        "top-P list differs from the stable top-k of the ceilings"
     cin = st_b.cell_in.cpu()
     so = st_b.slot_of.cpu()
     for b in range(cin.shape[0]):
@@ -336,12 +344,12 @@ def test_short_prompts_then_decode(dev, N):
     for mode in ("bf16", "int8"):
         y, sel, ys, sels, st = _run_layer(dev, g2, Q[:, :, :N + T], K[:, :, :N + T], V[:, :, :N + T], mode, 2, T=T)
         orc = _oracle(g, int8=(mode != "bf16"))
-        y0, sel0, mg0 = orc.prefill(Q[:, :, :N].float(), K[:, :, :N].float(), V[:, :, :N].float())
+        y0, sel0, mg0 = orc.prefill(Q[:, :, :N], K[:, :, :N], V[:, :, :N])
         _sel_check(sel, sel0, mg0, f"N={N} prefill selection")
         _close(y, y0, f"N={N}/{mode} prefill output", mean_rel=4e-3)
         for t in range(T):
             sl = slice(N + t, N + t + 1)
-            yo, so, mo = orc.decode(Q[:, :, sl].float(), K[:, :, sl].float(), V[:, :, sl].float())
+            yo, so, mo = orc.decode(Q[:, :, sl], K[:, :, sl], V[:, :, sl])
             _sel_check(sels[t].unsqueeze(2), so, mo, f"N={N}/{mode} decode step {t} selection")
             _close(ys[t].view(-1), yo.reshape(-1), f"N={N}/{mode} decode step {t} output", mean_rel=6e-3)
         assert st.faults() == (0, 0, 0)
@@ -370,7 +378,7 @@ def test_other_head_dims_layer(dev, D):
                          kk=4, scale=sc)
     y = ops.readout_combine(Qd[:, :, :N], Kd[:, :, :N], Vd[:, :, :N], sel, sr, pd["norm_w"], pd["lrs"], 1e-8, scale=sc, Bq=128,
                             n_kv=N)
-    y0, sel0, mg0 = orc.prefill(Q[:, :, :N].float(), K[:, :, :N].float(), V[:, :, :N].float())
+    y0, sel0, mg0 = orc.prefill(Q[:, :, :N], K[:, :, :N], V[:, :, :N])
     _sel_check(sel[:, :, :N], sel0, mg0, f"D={D} prefill selection")
     _close(y, y0, f"D={D} prefill output", mean_rel=3e-3)
     pos_t = torch.zeros((), dtype=torch.int64, device=dev)
@@ -380,6 +388,6 @@ def test_other_head_dims_layer(dev, D):
         yd = ops.fsl_decode_step(st, Qd[:, :, N + t], Kd[:, :, N + t], Vd[:, :, N + t], pos_t, cos, sin, pd["lam"], pd["sigma"],
                                  pd["lrs"], pd["norm_w"], scale=sc, eps=1e-8, sel_out=so, splits=2)
         sl = slice(N + t, N + t + 1)
-        yo, s_o, mo = orc.decode(Q[:, :, sl].float(), K[:, :, sl].float(), V[:, :, sl].float())
+        yo, s_o, mo = orc.decode(Q[:, :, sl], K[:, :, sl], V[:, :, sl])
         _sel_check(so.unsqueeze(2), s_o, mo, f"D={D} decode step {t} selection")
         _close(yd.view(-1), yo.reshape(-1), f"D={D} decode step {t} output", mean_rel=6e-3)
