@@ -193,10 +193,16 @@ def run_ours(args):
     e1.record()
     torch.cuda.synchronize()
     prefill_ms = e0.elapsed_time(e1)
+    def mark(what):
+        if os.environ.get("FSATTN_BENCH_TRACE", "0") == "1":
+            torch.cuda.synchronize()
+            print(f"[bench] {what} ok", file=sys.stderr, flush=True)
+    mark("prefill")
     for _ in range(Wm):
         gd.step()
     torch.cuda.synchronize()
     assert gd.graph is not None
+    mark("warmup")
 
     def barrier():
         if world > 1:
@@ -212,6 +218,7 @@ def run_ours(args):
         e1.record()
         barrier()
     ms = e0.elapsed_time(e1)
+    mark("timed region")
     # ---- end to end: token id from pinned host memory in, sampled token back to the host, every step --------------
     tok_host = torch.zeros(B, 1, dtype=torch.int64).pin_memory()
     tok_host.copy_(gd.tok.cpu())
@@ -226,6 +233,7 @@ def run_ours(args):
         tok_host.copy_(out_host)
     barrier()
     e2e_s = time.perf_counter() - t0
+    mark("e2e region")
     t = torch.tensor([ms, e2e_s * 1e3], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -257,7 +265,7 @@ def run_ours(args):
                    "parallelism": f"batch-sharded x{world}, no collective"},
         "clocks": cs.summary(),
         "e2e": {"value": world * B * K / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 8 * B},
-        "gpu_launches": K * nL,
+        "gpu_launches": K * (5 * nL + 1),
         "roofline": {"kernel": "fsl_decode_kernel", "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind, "bytes_per_launch": kbytes,
                      "avg_launch_us": k_avg_ms * 1e3, "median_launch_us": k_med_ms * 1e3,

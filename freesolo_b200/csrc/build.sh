@@ -5,7 +5,7 @@ here="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
 out="$here/../libfsattn_b200.so"
 nvcc=${NVCC:-/usr/local/cuda/bin/nvcc}
 flags=(-gencode arch=compute_100a,code=sm_100a -O3 -lineinfo -std=c++17 -Xcompiler -fPIC -Xcompiler -fvisibility=hidden
-       --expt-relaxed-constexpr ${FSATTN_PTXAS_V:+-Xptxas -v})
+       --expt-relaxed-constexpr ${FSATTN_PTXAS_V:+-Xptxas -v} ${FSATTN_EXTRA_FLAGS:-})
 objs=()
 mkdir -p "$here/build"
 pids=()

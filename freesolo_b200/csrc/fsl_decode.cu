@@ -31,13 +31,13 @@ struct RowL {
 };
 
 // raw words of one row for this lane: [0, NW) first half, [NW, 2NW) second half
-template <int D, bool I8>
+template <int D>
 struct RawRow {
     uint2 w[2 * RowL<D>::NW];  // int8 rows use only .x
 };
 
 template <int D, bool I8>
-__device__ __forceinline__ void raw_load(RawRow<D, I8>& r, const void* row, int sub, bool valid) {
+__device__ __forceinline__ void raw_load(RawRow<D>& r, const void* row, int sub, bool valid) {
     using L = RowL<D>;
 #pragma unroll
     for (int i = 0; i < 2 * L::NW; i++) r.w[i] = make_uint2(0u, 0u);
@@ -57,7 +57,7 @@ __device__ __forceinline__ void raw_load(RawRow<D, I8>& r, const void* row, int 
 
 // the lane's values of a row as fp32; int8 rows are read as bf16(f32(code) * f32(scale)) like the reference's int8 read
 template <int D, bool I8>
-__device__ __forceinline__ void raw_floats(const RawRow<D, I8>& r, float sc, float* lo, float* hi) {
+__device__ __forceinline__ void raw_floats(const RawRow<D>& r, float sc, float* lo, float* hi) {
     using L = RowL<D>;
 #pragma unroll
     for (int i = 0; i < L::NW; i++) {
@@ -88,29 +88,45 @@ struct Part {
     }
 };
 
-// score one row (4 lanes), fold it into the group's partial
-template <int D, bool I8, bool ROPE>
-__device__ __forceinline__ void attend_row(Part<D>& P, const void* krow, const void* vrow, float ksc, float vsc, bool valid,
-                                           const bf16* cosr, const bf16* sinr, const float* qlo, const float* qhi,
-                                           float scale, int sub) {
+// A row in flight: its K and V words (and the rotary table words for window rows) are loaded first, consumed later, so a
+// warp can keep several rows' loads outstanding.
+template <int D>
+struct RowFlight {
+    RawRow<D> k, v;
+    uint2 c[RowL<D>::NW], s[RowL<D>::NW];
+    float ksc, vsc;
+    bool valid, i8;
+};
+
+template <int D, bool ROPE>
+__device__ __forceinline__ void row_issue(RowFlight<D>& f, const void* krow, const void* vrow, const bf16* ksc_p, const bf16* vsc_p,
+                                          bool valid, bool i8, const bf16* cosr, const bf16* sinr, int sub) {
     using L = RowL<D>;
-    RawRow<D, I8> rk, rv;
-    raw_load<D, I8>(rk, krow, sub, valid);
-    raw_load<D, I8>(rv, vrow, sub, valid);
+    f.valid = valid; f.i8 = i8;
+    f.ksc = 1.0f; f.vsc = 1.0f;
+    if (valid && i8) { f.ksc = __bfloat162float(*ksc_p); f.vsc = __bfloat162float(*vsc_p); }
+    if (i8) { raw_load<D, true>(f.k, krow, sub, valid); raw_load<D, true>(f.v, vrow, sub, valid); }
+    else { raw_load<D, false>(f.k, krow, sub, valid); raw_load<D, false>(f.v, vrow, sub, valid); }
+    if (ROPE) {
+#pragma unroll
+        for (int i = 0; i < L::NW; i++) {
+            f.c[i] = valid ? reinterpret_cast<const uint2*>(cosr + sub * L::DPL)[i] : make_uint2(0u, 0u);
+            f.s[i] = valid ? reinterpret_cast<const uint2*>(sinr + sub * L::DPL)[i] : make_uint2(0u, 0u);
+        }
+    }
+}
+
+// score the row (4 lanes cooperate) and fold it into the group's partial; every lane of the warp must call it
+template <int D, bool ROPE>
+__device__ __forceinline__ void row_consume(Part<D>& P, const RowFlight<D>& f, const float* qlo, const float* qhi, float scale) {
+    using L = RowL<D>;
     float klo[L::DPL], khi[L::DPL];
-    raw_floats<D, I8>(rk, ksc, klo, khi);
+    if (f.i8) raw_floats<D, true>(f.k, f.ksc, klo, khi); else raw_floats<D, false>(f.k, 1.0f, klo, khi);
     float dot = 0.0f;
     if (ROPE) {
         float c[L::DPL], s[L::DPL];
-        if (valid) {
-            const uint2* cp = reinterpret_cast<const uint2*>(cosr + sub * L::DPL);
-            const uint2* sp = reinterpret_cast<const uint2*>(sinr + sub * L::DPL);
 #pragma unroll
-            for (int i = 0; i < L::NW; i++) { unpack4_bf(cp[i], c + 4 * i); unpack4_bf(sp[i], s + 4 * i); }
-        } else {
-#pragma unroll
-            for (int j = 0; j < L::DPL; j++) { c[j] = 0.0f; s[j] = 0.0f; }
-        }
+        for (int i = 0; i < L::NW; i++) { unpack4_bf(f.c[i], c + 4 * i); unpack4_bf(f.s[i], s + 4 * i); }
 #pragma unroll
         for (int j = 0; j < L::DPL; j++) {
             const float r1 = bf_round(klo[j] * c[j] - khi[j] * s[j]);
@@ -127,10 +143,10 @@ __device__ __forceinline__ void attend_row(Part<D>& P, const void* krow, const v
     }
     dot += __shfl_xor_sync(FS_FULL, dot, 1);
     dot += __shfl_xor_sync(FS_FULL, dot, 2);
-    if (!valid) return;   // uniform within the 4-lane group; no shuffles below
+    if (!f.valid) return;   // uniform within the 4-lane group; no shuffles below
     const float sc = dot * scale;
     float vlo[L::DPL], vhi[L::DPL];
-    raw_floats<D, I8>(rv, vsc, vlo, vhi);
+    if (f.i8) raw_floats<D, true>(f.v, f.vsc, vlo, vhi); else raw_floats<D, false>(f.v, 1.0f, vlo, vhi);
     const float m_new = fmaxf(P.m, sc);
     const float alpha = (P.m == -INFINITY) ? 0.0f : __expf(P.m - m_new);
     const float p = __expf(sc - m_new);
@@ -198,9 +214,16 @@ __device__ __forceinline__ void rec_merge(const float* recs, int n, int rs, int 
     l_out = l;
 }
 
-struct RowSrc {
-    const void* k; const void* v; float ksc, vsc; bool i8;
-};
+
+#ifdef FSATTN_DEC_TIMING
+// debug build only: clock64 phase stamps of CTA (rank 0 / rank 1) of head 0, read back with fsattn_debug_dec_timing
+__device__ long long g_dec_stamps[2][16];
+#define STAMP(r, i) do { if (bh == 0 && tid == 0 && rank == (r)) g_dec_stamps[(r)][(i)] = clock64(); } while (0)
+#else
+#define STAMP(r, i) do { } while (0)
+#endif
+
+constexpr int SC_ITERS = (MAXC + 31) / 32;     // scoring rounds: 32 candidates per round over the 8 warps
 
 template <int D>
 struct Smem {
@@ -210,264 +233,427 @@ struct Smem {
     int li[FSATTN_MAX_POOL];
     int ccell[MAXC];
     int cok[MAXC];
-    int cslot[MAXC];
-    float cceil[MAXC];
+    int crow[MAXC];
     float score[MAXC];
+    float prior[MAXC];
     int selcell[FSATTN_MAX_KK];
-    int selslot[FSATTN_MAX_KK];
+    int selrow[FSATTN_MAX_KK];
     int n_list;
     float wrec[NWARP][D + 2];   // per-warp partials (window, then long-range)
-    float win_rec[D + 2];       // this CTA's window partial (read by rank 0 through distributed shared memory)
+    float win_recs[8][D + 2];   // rank 0: window partials pushed by the window CTAs through distributed shared memory
     float lr_rec[D + 2];
+    unsigned long long pool_bar;   // mbarrier of the pool's bulk copy
+    int pool_timeout;
 };
+
+// ---- mbarrier + bulk (TMA) copy helpers; every wait is bounded ----------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, unsigned long long* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+// returns false when the phase did not complete within the iteration budget
+__device__ __forceinline__ bool mbar_wait_bounded(unsigned long long* bar, uint32_t parity, int max_iters) {
+    const uint32_t addr = smem_u32(bar);
+    for (int i = 0; i < max_iters; i++) {
+        uint32_t done;
+        asm volatile("{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}"
+                     : "=r"(done) : "r"(addr), "r"(parity) : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+// Pointers of one (b,h) into the layer state.
+struct HeadPtrs {
+    const int8_t* kq; const int8_t* vq; const bf16* ks; const bf16* vs;
+    bf16* khot; bf16* vhot; bf16* kbuf; bf16* vbuf;
+    int32_t* slot_of; int32_t* cell_in;
+    float* kbar; float* ceil;
+};
+
+__device__ __forceinline__ HeadPtrs head_ptrs(const fsattn_fsl_state_t& st, int b, int h) {
+    HeadPtrs p;
+    p.kq = st.kq ? st.kq + b * st.q_sb + h * st.q_sh : nullptr;
+    p.vq = st.vq ? st.vq + b * st.q_sb + h * st.q_sh : nullptr;
+    p.ks = st.ks ? (const bf16*)st.ks + b * st.sc_sb + h * st.sc_sh : nullptr;
+    p.vs = st.vs ? (const bf16*)st.vs + b * st.sc_sb + h * st.sc_sh : nullptr;
+    p.khot = st.khot ? (bf16*)st.khot + b * st.hot_sb + h * st.hot_sh : nullptr;
+    p.vhot = st.vhot ? (bf16*)st.vhot + b * st.hot_sb + h * st.hot_sh : nullptr;
+    p.kbuf = st.kbuf ? (bf16*)st.kbuf + b * st.buf_sb + h * st.buf_sh : nullptr;
+    p.vbuf = st.vbuf ? (bf16*)st.vbuf + b * st.buf_sb + h * st.buf_sh : nullptr;
+    p.slot_of = st.slot_of ? st.slot_of + b * st.so_sb + h * st.so_sh : nullptr;
+    p.cell_in = st.cell_in ? st.cell_in + b * st.ci_sb + h * st.ci_sh : nullptr;
+    p.kbar = st.kbar + b * st.kbar_sb + h * st.kbar_sh;
+    p.ceil = st.ceil + b * st.ceil_sb + h * st.ceil_sh;
+    return p;
+}
+
+// ---- window branch: rows [max(0,pos-W), pos) from the store + the new token's row -------------------------------------
+// The stored rows depend only on the position and this layer's own state, so a warp issues the loads of its first two
+// 8-row groups BEFORE the producer kernel (the QKV projection) has finished; only the arithmetic needs q.
+template <int D>
+struct WinCtx {
+    int64_t pos, nq, lo_row, g_lo, g_hi;
+    int nw, gw, mode;
+    bool pos_ok;
+};
+
+template <int D>
+__device__ __forceinline__ void window_issue2(RowFlight<D>* f, const WinCtx<D>& w, const fsattn_fsl_decode_t& a, const HeadPtrs& hp,
+                                              int64_t g0, int lane) {
+    const int sub = lane & 3, grp = lane >> 2;
+    const fsattn_fsl_state_t& st = a.st;
+    const bf16* cosT = (const bf16*)a.cos;
+    const bf16* sinT = (const bf16*)a.sin;
+    int64_t r[2]; bool valid[2], i8[2]; int slot[2];
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+        const int64_t g = g0 + (int64_t)u * w.nw;
+        r[u] = (g << 3) + grp;
+        // the new token's row (r == pos) is handled separately: its key and value come from the producer kernel
+        valid[u] = w.pos_ok && g <= w.g_hi && r[u] >= w.lo_row && r[u] < w.pos;
+        i8[u] = valid[u] && w.mode != 0 && r[u] < w.nq;
+        slot[u] = 0;
+        if (i8[u] && w.mode == 2) slot[u] = hp.slot_of[r[u] / FSATTN_CELL];
+    }
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+        const void* kp = nullptr; const void* vp = nullptr;
+        const bf16* ksp = nullptr; const bf16* vsp = nullptr;
+        bool ok = valid[u];
+        if (valid[u]) {
+            if (w.mode == 0) { kp = hp.kbuf + r[u] * D; vp = hp.vbuf + r[u] * D; }
+            else if (!i8[u]) { kp = hp.khot + (r[u] - w.nq) * D; vp = hp.vhot + (r[u] - w.nq) * D; }
+            else {
+                int64_t cell = r[u] / FSATTN_CELL;
+                int64_t prow = r[u];
+                if (w.mode == 2) {
+                    if (slot[u] < 0) { ok = false; if (sub == 0) atomicAdd(st.status + FSATTN_ST_POOL_NO_SLOT, 1); }
+                    prow = (int64_t)slot[u] * FSATTN_CELL + (r[u] - cell * FSATTN_CELL);
+                    cell = slot[u];
+                }
+                if (ok) { kp = hp.kq + prow * D; vp = hp.vq + prow * D; ksp = hp.ks + cell; vsp = hp.vs + cell; }
+            }
+        }
+        row_issue<D, true>(f[u], kp, vp, ksp, vsp, ok, i8[u] && ok, cosT + r[u] * D, sinT + r[u] * D, sub);
+    }
+}
+
+// consumes the pre-issued groups, walks the remaining groups of this warp, adds the new token's row (warp gw == 0), and
+// leaves the CTA's merged partial in `out_rec` (m, l, acc[D])
+template <int D>
+__device__ __forceinline__ void window_finish(Smem<D>& sm, RowFlight<D>* f, const WinCtx<D>& w, const fsattn_fsl_decode_t& a,
+                                              const HeadPtrs& hp, const bf16* k_in, const bf16* v_in, float* out_rec, int warp, int lane) {
+    using L = RowL<D>;
+    const int sub = lane & 3, grp = lane >> 2;
+    const bf16* cosT = (const bf16*)a.cos;
+    const bf16* sinT = (const bf16*)a.sin;
+    float qlo[L::DPL], qhi[L::DPL];
+#pragma unroll
+    for (int j = 0; j < L::DPL; j++) { qlo[j] = sm.q_rot[sub * L::DPL + j]; qhi[j] = sm.q_rot[L::HALF + sub * L::DPL + j]; }
+    Part<D> P;
+    P.init();
+    int64_t g0 = w.g_lo + w.gw;
+    for (;;) {
+#pragma unroll
+        for (int u = 0; u < 2; u++) row_consume<D, true>(P, f[u], qlo, qhi, a.scale);
+        g0 += 2 * (int64_t)w.nw;
+        if (g0 > w.g_hi) break;                 // warp-uniform
+        window_issue2<D>(f, w, a, hp, g0, lane);
+    }
+    if (w.gw == 0) {                            // the new token itself: always inside its own window
+        RowFlight<D> c;
+        const bool mine = w.pos_ok && grp == 0;
+        row_issue<D, true>(c, k_in, v_in, nullptr, nullptr, mine, false, cosT + w.pos * D, sinT + w.pos * D, sub);
+        row_consume<D, true>(P, c, qlo, qhi, a.scale);
+    }
+    part_merge_warp<D>(P);
+    part_store<D>(P, sm.wrec[warp], lane);
+    __syncthreads();
+    if (warp == 0) {
+        float l, acc[D / 32];
+        rec_merge<D>(&sm.wrec[0][0], NWARP, D + 2, lane, l, acc);
+        float m = -INFINITY;
+        for (int i = 0; i < NWARP; i++) m = fmaxf(m, sm.wrec[i][0]);
+        if (lane == 0) { out_rec[0] = m; out_rec[1] = l; }
+#pragma unroll
+        for (int j = 0; j < D / 32; j++) out_rec[2 + lane + 32 * j] = acc[j];
+    }
+}
+
+// ---- append the new row; close the cell when this token completes it (one warp) ---------------------------------------
+template <int D>
+__device__ __forceinline__ void append_and_close(const fsattn_fsl_state_t& st, const HeadPtrs& hp, int64_t pos,
+                                                 const bf16* k_in, const bf16* v_in, int lane) {
+    const int mode = st.store_mode;
+    const int64_t nq = (pos / FSATTN_CELL) * FSATTN_CELL;
+    const int hr = (int)(pos - nq);
+    if (mode == 0) {
+        for (int d = lane; d < D; d += 32) { hp.kbuf[pos * D + d] = k_in[d]; hp.vbuf[pos * D + d] = v_in[d]; }
+    } else {
+        for (int d = lane; d < D; d += 32) { hp.khot[hr * D + d] = k_in[d]; hp.vhot[hr * D + d] = v_in[d]; }
+    }
+    if (hr != FSATTN_CELL - 1) return;
+    const int cell = (int)(pos / FSATTN_CELL);
+    const bool in_table = cell < st.cap_cells;
+    int dst = cell;          // where the quantised rows and the mean key go (cell or slot index)
+    bool store_ok = in_table;
+    if (mode == 2) {
+        int slot = -1;
+        for (int s0 = 0; s0 < st.n_slots && slot < 0; s0 += 32) {
+            const int si = s0 + lane;
+            const bool free_ = si < st.n_slots && hp.cell_in[si] < 0;
+            const unsigned bal = __ballot_sync(FS_FULL, free_);
+            if (bal) slot = s0 + __ffs(bal) - 1;
+        }
+        store_ok = in_table && slot >= 0;
+        dst = slot;
+        if (!store_ok && lane == 0) atomicAdd(st.status + FSATTN_ST_SLOT_OVERFLOW, 1);
+        if (store_ok && lane == 0) { hp.slot_of[cell] = slot; hp.cell_in[slot] = cell; }
+    }
+    const bf16* kcell = (mode == 0) ? hp.kbuf + nq * D : hp.khot;
+    const bf16* vcell = (mode == 0) ? hp.vbuf + nq * D : hp.vhot;
+    CellRegs<D> cr;
+    cell_load_rows<D>(cr, kcell, D, lane, k_in);
+    // the ceiling table is indexed by cell; the mean keys by cell (full stores) or slot (bounded store)
+    cell_stats_warp<D>(cr, lane, store_ok ? hp.kbar + (int64_t)dst * D : nullptr, in_table ? hp.ceil + cell : nullptr);
+    if (mode != 0 && store_ok) {
+        cell_quant_warp<D>(cr, lane, const_cast<int8_t*>(hp.kq) + (int64_t)dst * FSATTN_CELL * D, const_cast<bf16*>(hp.ks) + dst);
+        cell_load_rows<D>(cr, vcell, D, lane, v_in);
+        cell_quant_warp<D>(cr, lane, const_cast<int8_t*>(hp.vq) + (int64_t)dst * FSATTN_CELL * D, const_cast<bf16*>(hp.vs) + dst);
+    }
+}
+
+// ---- block change: refresh the top-P list, free unreadable slots, gather the block's candidate pool (whole CTA) -----------
+template <int D>
+__device__ __forceinline__ void refresh_pool(Smem<D>& sm, const fsattn_fsl_state_t& st, const HeadPtrs& hp, int bh, int blk_start,
+                                             int tid, float* pool_s, int4* meta_s) {
+    const int warp = tid >> 5, lane = tid & 31;
+    const int mode = st.store_mode;
+    const int M_vis = blk_start / FSATTN_CELL;
+    const int C = st.P + st.Wc;
+    int32_t* top_idx = st.top_idx + (int64_t)bh * st.P;
+    if (warp == 0) {
+        int n = 0;
+        for (int p = lane; p < st.P; p += 32) {
+            const int ci = top_idx[p];
+            sm.li[p] = ci;
+            sm.lc[p] = (ci >= 0) ? hp.ceil[ci] : 0.0f;
+            n += (ci >= 0);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(FS_FULL, n, o);
+        __syncwarp();
+        const int have_blk = st.top_blk[bh];
+        if (have_blk != blk_start) {
+            int c0 = have_blk / FSATTN_CELL; if (c0 < 0) c0 = 0;
+            for (int c = c0; c < M_vis; c++) pool_list_insert(sm.lc, sm.li, n, st.P, hp.ceil[c], c, lane);
+            for (int p = lane; p < st.P; p += 32) top_idx[p] = (p < n) ? sm.li[p] : -1;
+            if (lane == 0) st.top_blk[bh] = blk_start;
+            if (mode == 2) {
+                // free the slots of cells no later step reads: below c_lo and outside the top-P
+                int c_lo = (blk_start - st.W) / FSATTN_CELL;
+                if ((blk_start - st.W) < 0) c_lo = -1;      // floor division of a negative number
+                if (M_vis - st.Wc < c_lo) c_lo = M_vis - st.Wc;
+                if (c_lo < 0) c_lo = 0;
+                for (int s0 = 0; s0 < st.n_slots; s0 += 32) {
+                    const int si = s0 + lane;
+                    if (si < st.n_slots) {
+                        const int occ = hp.cell_in[si];
+                        if (occ >= 0 && occ < c_lo) {
+                            bool in_top = false;
+                            for (int p = 0; p < n; p++) in_top |= (sm.li[p] == occ);
+                            if (!in_top) { hp.cell_in[si] = -1; hp.slot_of[occ] = -1; }
+                        }
+                    }
+                }
+            }
+        }
+        if (lane == 0) sm.n_list = n;
+    }
+    __syncthreads();
+    // candidate slots: the top-P list, then the Wc newest visible cells
+    const int n_list = sm.n_list;
+    for (int t = tid; t < C; t += blockDim.x) {
+        const int cand = (t < st.P) ? ((t < n_list) ? sm.li[t] : -1) : (M_vis - 1) - (t - st.P);
+        const int cc = cand < 0 ? 0 : cand;
+        sm.ccell[t] = cc;
+        sm.cok[t] = (cand >= 0) && (cc < M_vis);
+    }
+    __syncthreads();
+    int32_t* meta = st.pool_meta + (int64_t)bh * C * 4;
+    for (int t = tid; t < C; t += blockDim.x) {
+        int ok = sm.cok[t];
+        const int cc = sm.ccell[t];
+        for (int j = 0; j < t && ok; j++) ok = (sm.ccell[j] != cc);     // a slot that repeats an earlier slot's cell is out
+        int row = cc;
+        if (ok && mode == 2) {
+            row = hp.slot_of[cc];
+            if (row < 0) { atomicAdd(st.status + FSATTN_ST_POOL_NO_SLOT, 1); ok = 0; row = 0; }
+        }
+        sm.crow[t] = ok ? row : -1;
+        const float ce = ok ? hp.ceil[cc] : 0.0f;
+        const int4 mv = make_int4(ok ? cc : -1, row, __float_as_int(ce), 0);
+        reinterpret_cast<int4*>(meta)[t] = mv;
+        meta_s[t] = mv;                          // this step scores from the shared-memory copy
+    }
+    __syncthreads();
+    float* pk = st.pool_kbar + (int64_t)bh * C * D;
+    constexpr int V4 = D / 4;
+    for (int i = tid; i < C * V4; i += blockDim.x) {
+        const int t = i / V4, e = i - t * V4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (sm.crow[t] >= 0) v = reinterpret_cast<const float4*>(hp.kbar + (int64_t)sm.crow[t] * D)[e];
+        reinterpret_cast<float4*>(pk + (size_t)t * D)[e] = v;
+        reinterpret_cast<float4*>(pool_s + (size_t)t * D)[e] = v;
+    }
+    if (tid == 0) st.pool_blk[bh] = blk_start;
+    __threadfence();
+    __syncthreads();
+}
 
 template <int D>
 __global__ void __launch_bounds__(NWARP * 32) fsl_decode_kernel(const fsattn_fsl_decode_t a) {
     using L = RowL<D>;
+    constexpr int F = D / 8;                  // floats per lane when 8 lanes share a mean key
     __shared__ Smem<D> sm;
+    extern __shared__ __align__(128) unsigned char dyn_smem[];     // rank 0: the block's candidate pool (mean keys, meta)
     cg::cluster_group cluster = cg::this_cluster();
-    const int S = (int)gridDim.x;              // CTAs per (b,h) = cluster size
+    const int S = (int)gridDim.x;             // CTAs per (b,h) = cluster size
     const int rank = (int)blockIdx.x;
     const int bh = blockIdx.y;
     const fsattn_fsl_state_t& st = a.st;
     const int b = bh / st.H, h = bh - b * st.H;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int sub = lane & 3, grp = lane >> 2;
+    const int sub = lane & 3, grp = lane >> 2, s8 = lane & 7;
     const int mode = st.store_mode;
+    const int C = st.P + st.Wc;
+    float* pool_s = reinterpret_cast<float*>(dyn_smem);
+    int4* meta_s = reinterpret_cast<int4*>(dyn_smem + (size_t)C * D * 4);
+    STAMP(0, 0); STAMP(1, 0);
 
-    const int64_t pos = *a.pos;
-    const int64_t nq = (pos / FSATTN_CELL) * FSATTN_CELL;      // rows below nq are completed cells
-    const int blk_start = (int)((pos / st.Bq) * st.Bq);
-    const bool pos_ok = pos >= 0 && pos < st.cap_rows;
+    // "every CTA of the cluster has started": arrive now, wait right before the first distributed-shared-memory access
+    if (S > 1) cluster.barrier_arrive();
 
     const bf16* q_in = (const bf16*)a.q + b * a.in_sb + h * a.in_sh;
     const bf16* k_in = (const bf16*)a.k + b * a.in_sb + h * a.in_sh;
     const bf16* v_in = (const bf16*)a.v + b * a.in_sb + h * a.in_sh;
     const bf16* cosT = (const bf16*)a.cos;
     const bf16* sinT = (const bf16*)a.sin;
+    const HeadPtrs hp = head_ptrs(st, b, h);
 
-    // ---- q: raw and rotated (rounded to bf16 like the reference's rotated query), into shared memory -----------------
-    for (int d = tid; d < L::HALF; d += blockDim.x) {
-        const float x1 = __bfloat162float(q_in[d]), x2 = __bfloat162float(q_in[d + L::HALF]);
-        const float c = __bfloat162float(cosT[pos * D + d]), s = __bfloat162float(sinT[pos * D + d]);
-        sm.q_raw[d] = x1; sm.q_raw[d + L::HALF] = x2;
-        sm.q_rot[d] = bf_round(x1 * c - x2 * s);
-        sm.q_rot[d + L::HALF] = bf_round(x2 * c + x1 * s);
+    // =========== before the producer kernel has finished: everything that depends only on the position and on this
+    // layer's own state (last written by this layer's kernel of the previous step, long complete) =====================
+    const int64_t pos = *a.pos;
+    const bool pos_ok = pos >= 0 && pos < st.cap_rows;
+    const int blk_start = (int)((pos / st.Bq) * st.Bq);
+    int pool_blk = 0;
+    if (rank == 0) {
+        if (tid == 0) {
+            sm.pool_timeout = 0;
+            mbar_init(&sm.pool_bar, 1);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            const uint32_t kb_bytes = (uint32_t)C * D * 4, mt_bytes = (uint32_t)C * 16;
+            mbar_expect_tx(&sm.pool_bar, kb_bytes + mt_bytes);
+            bulk_g2s(pool_s, st.pool_kbar + (int64_t)bh * C * D, kb_bytes, &sm.pool_bar);
+            bulk_g2s(meta_s, st.pool_meta + (int64_t)bh * C * 4, mt_bytes, &sm.pool_bar);
+        }
+        pool_blk = st.pool_blk[bh];
+        __syncthreads();          // the barrier is initialised before any thread polls it (rank is CTA-uniform)
+    }
+    // per-head parameters (warp 0 of rank 0 also needs the norm weights of its output dims)
+    const float lam = a.lam[h];
+    const float two_sigma = f_mul(2.0f, a.sigma[h]);
+    const float g_lrs = a.lrs[h];
+    float nw_reg[D / 32];
+#pragma unroll
+    for (int j = 0; j < D / 32; j++) nw_reg[j] = a.norm_w[lane + 32 * j];
+    float rc = 0.f, rs = 0.f;
+    if (tid < L::HALF && pos_ok) { rc = __bfloat162float(cosT[pos * D + tid]); rs = __bfloat162float(sinT[pos * D + tid]); }
+    WinCtx<D> w;
+    w.pos = pos; w.pos_ok = pos_ok; w.mode = mode;
+    w.nq = (pos / FSATTN_CELL) * FSATTN_CELL;
+    w.lo_row = (pos - st.W > 0) ? pos - st.W : 0;
+    w.g_lo = w.lo_row >> 3; w.g_hi = pos >> 3;
+    w.nw = (S == 1) ? NWARP : (S - 1) * NWARP;
+    w.gw = (S == 1) ? warp : (rank - 1) * NWARP + warp;
+    const bool do_window = (S == 1) || (rank > 0);
+    RowFlight<D> wf[2];
+    if (do_window) window_issue2<D>(wf, w, a, hp, w.g_lo + w.gw, lane);
+    if (rank == 0) {
+        // the pool's bulk copy; the wait is bounded. The position priors of the candidates need no query: compute them now.
+        if (!mbar_wait_bounded(&sm.pool_bar, 0, 1 << 22)) {
+            if (lane == 0) { atomicAdd(st.status + FSATTN_ST_BAD_INDEX, 1); sm.pool_timeout = 1; }
+        }
+        if (pool_blk == blk_start) {
+            for (int t = tid; t < C; t += blockDim.x) {
+                const int4 mt = meta_s[t];
+                sm.prior[t] = (mt.x >= 0) ? fs_prior(lam, __int_as_float(mt.z), (float)pos, mt.x, (float)FSATTN_CELL, two_sigma) : 0.0f;
+            }
+        }
+    }
+
+    // =========== the producer (QKV projection) is complete from here on =====================================================
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    STAMP(0, 1); STAMP(1, 1);
+
+    // q: raw and rotated (rounded to bf16 like the reference's rotated query), into shared memory
+    if (tid < L::HALF) {
+        const float x1 = __bfloat162float(q_in[tid]), x2 = __bfloat162float(q_in[tid + L::HALF]);
+        sm.q_raw[tid] = x1; sm.q_raw[tid + L::HALF] = x2;
+        sm.q_rot[tid] = bf_round(x1 * rc - x2 * rs);
+        sm.q_rot[tid + L::HALF] = bf_round(x2 * rc + x1 * rs);
     }
     if (tid == 0 && !pos_ok) atomicAdd(st.status + FSATTN_ST_BAD_INDEX, 1);
     __syncthreads();
-
-    const int8_t* kq = st.kq ? st.kq + b * st.q_sb + h * st.q_sh : nullptr;
-    const int8_t* vq = st.vq ? st.vq + b * st.q_sb + h * st.q_sh : nullptr;
-    const bf16* ks = st.ks ? (const bf16*)st.ks + b * st.sc_sb + h * st.sc_sh : nullptr;
-    const bf16* vs = st.vs ? (const bf16*)st.vs + b * st.sc_sb + h * st.sc_sh : nullptr;
-    bf16* khot = st.khot ? (bf16*)st.khot + b * st.hot_sb + h * st.hot_sh : nullptr;
-    bf16* vhot = st.vhot ? (bf16*)st.vhot + b * st.hot_sb + h * st.hot_sh : nullptr;
-    bf16* kbuf = st.kbuf ? (bf16*)st.kbuf + b * st.buf_sb + h * st.buf_sh : nullptr;
-    bf16* vbuf = st.vbuf ? (bf16*)st.vbuf + b * st.buf_sb + h * st.buf_sh : nullptr;
-    int32_t* slot_of = st.slot_of ? st.slot_of + b * st.so_sb + h * st.so_sh : nullptr;
-    int32_t* cell_in = st.cell_in ? st.cell_in + b * st.ci_sb + h * st.ci_sh : nullptr;
-    float* kbar = st.kbar + b * st.kbar_sb + h * st.kbar_sh;
-    float* ceil = st.ceil + b * st.ceil_sb + h * st.ceil_sh;
+    STAMP(0, 2); STAMP(1, 2);
 
     // ================= window branch =====================================================================================
-    const bool do_window = (S == 1) || (rank > 0);
     if (do_window) {
-        float qlo[L::DPL], qhi[L::DPL];
-#pragma unroll
-        for (int j = 0; j < L::DPL; j++) { qlo[j] = sm.q_rot[sub * L::DPL + j]; qhi[j] = sm.q_rot[L::HALF + sub * L::DPL + j]; }
-        Part<D> P;
-        P.init();
-        const int64_t lo_row = (pos - st.W > 0) ? pos - st.W : 0;
-        const int nw = (S == 1) ? NWARP : (S - 1) * NWARP;
-        const int gw = (S == 1) ? warp : (rank - 1) * NWARP + warp;
-        const int64_t g_lo = lo_row >> 3, g_hi = pos >> 3;
-        for (int64_t g = g_lo + gw; g <= g_hi; g += nw) {
-            const int64_t r = (g << 3) + grp;
-            const bool valid = pos_ok && r >= lo_row && r <= pos;
-            const void* kp = nullptr; const void* vp = nullptr;
-            float ksc = 1.0f, vsc = 1.0f;
-            bool i8 = false;
-            if (r == pos) { kp = k_in; vp = v_in; }
-            else if (mode == 0) { kp = kbuf + r * D; vp = vbuf + r * D; }
-            else if (r >= nq) { kp = khot + (r - nq) * D; vp = vhot + (r - nq) * D; }
-            else {
-                i8 = true;
-                int64_t cell = r / FSATTN_CELL;
-                int64_t prow = r;
-                bool have = true;
-                if (mode == 2) {
-                    const int slot = valid ? slot_of[cell] : -1;
-                    have = slot >= 0;
-                    prow = (int64_t)slot * FSATTN_CELL + (r - cell * FSATTN_CELL);
-                    cell = slot;
-                }
-                if (valid && have) {
-                    kp = kq + prow * D; vp = vq + prow * D;
-                    ksc = __bfloat162float(ks[cell]); vsc = __bfloat162float(vs[cell]);
-                }
-            }
-            const bool ok = valid && kp != nullptr;
-            if (valid && !ok && sub == 0) atomicAdd(st.status + FSATTN_ST_POOL_NO_SLOT, 1);
-            // all rows of an aligned 8-row group come from the same kind of storage, except the new token's row
-            const bool any_i8 = __any_sync(FS_FULL, i8 && ok);
-            const bf16* cr = cosT + r * D; const bf16* sr_ = sinT + r * D;
-            if (any_i8) {
-                attend_row<D, true, true>(P, kp, vp, ksc, vsc, ok && i8, cr, sr_, qlo, qhi, a.scale, sub);
-                if (__any_sync(FS_FULL, ok && !i8))
-                    attend_row<D, false, true>(P, kp, vp, 1.0f, 1.0f, ok && !i8, cr, sr_, qlo, qhi, a.scale, sub);
-            } else {
-                attend_row<D, false, true>(P, kp, vp, 1.0f, 1.0f, ok, cr, sr_, qlo, qhi, a.scale, sub);
-            }
+        float* out_rec = sm.win_recs[0];
+        if (S > 1) {
+            cluster.barrier_wait();                                   // rank 0 is running: its shared memory may be written
+            out_rec = cluster.map_shared_rank(&sm.win_recs[rank][0], 0);
         }
-        part_merge_warp<D>(P);
-        part_store<D>(P, sm.wrec[warp], lane);
-        __syncthreads();
-        if (warp == 0) {
-            float l, acc[D / 32];
-            rec_merge<D>(&sm.wrec[0][0], NWARP, D + 2, lane, l, acc);
-            float m = -INFINITY;
-            for (int i = 0; i < NWARP; i++) m = fmaxf(m, sm.wrec[i][0]);
-            if (lane == 0) { sm.win_rec[0] = m; sm.win_rec[1] = l; }
-#pragma unroll
-            for (int j = 0; j < D / 32; j++) sm.win_rec[2 + lane + 32 * j] = acc[j];
-        }
-        __syncthreads();
+        window_finish<D>(sm, wf, w, a, hp, k_in, v_in, out_rec, warp, lane);
     }
+    STAMP(1, 3);
 
     // ================= long-range branch + bookkeeping (rank 0) ==============================================================
     float lr_l = 0.0f;
     if (rank == 0) {
-        // ---- append the new row; close the cell when this token completes it (last warp) --------------------------------
-        if (warp == NWARP - 1 && pos_ok) {
-            const int hr = (int)(pos - nq);
-            if (mode == 0) {
-                for (int d = lane; d < D; d += 32) { kbuf[pos * D + d] = k_in[d]; vbuf[pos * D + d] = v_in[d]; }
-            } else {
-                for (int d = lane; d < D; d += 32) { khot[hr * D + d] = k_in[d]; vhot[hr * D + d] = v_in[d]; }
+        if (warp == NWARP - 1 && pos_ok) append_and_close<D>(st, hp, pos, k_in, v_in, lane);
+        if (pool_blk != blk_start) {               // CTA-uniform, once per Bq tokens
+            refresh_pool<D>(sm, st, hp, bh, blk_start, tid, pool_s, meta_s);
+            for (int t = tid; t < C; t += blockDim.x) {
+                const int4 mt = meta_s[t];
+                sm.prior[t] = (mt.x >= 0) ? fs_prior(lam, __int_as_float(mt.z), (float)pos, mt.x, (float)FSATTN_CELL, two_sigma) : 0.0f;
             }
-            if (hr == FSATTN_CELL - 1) {
-                const int cell = (int)(pos / FSATTN_CELL);
-                const bool in_table = cell < st.cap_cells;
-                int dst = cell;          // where the quantised rows and the mean key go (cell or slot index)
-                bool store_ok = in_table;
-                if (mode == 2) {
-                    int slot = -1;
-                    for (int s0 = 0; s0 < st.n_slots && slot < 0; s0 += 32) {
-                        const int si = s0 + lane;
-                        const bool free_ = si < st.n_slots && cell_in[si] < 0;
-                        const unsigned bal = __ballot_sync(FS_FULL, free_);
-                        if (bal) slot = s0 + __ffs(bal) - 1;
-                    }
-                    store_ok = in_table && slot >= 0;
-                    dst = slot;
-                    if (!store_ok && lane == 0) atomicAdd(st.status + FSATTN_ST_SLOT_OVERFLOW, 1);
-                    if (store_ok && lane == 0) { slot_of[cell] = slot; cell_in[slot] = cell; }
-                }
-                const bf16* kcell = (mode == 0) ? kbuf + nq * D : khot;
-                const bf16* vcell = (mode == 0) ? vbuf + nq * D : vhot;
-                CellRegs<D> cr;
-                cell_load_rows<D>(cr, kcell, D, lane, k_in);
-                float cl_tmp = 0.0f;
-                (void)cl_tmp;
-                if (mode == 2) {
-                    // the ceiling table is indexed by cell, the mean keys by slot
-                    cell_stats_warp<D>(cr, lane, store_ok ? kbar + (int64_t)dst * D : nullptr, in_table ? ceil + cell : nullptr);
-                } else {
-                    cell_stats_warp<D>(cr, lane, in_table ? kbar + (int64_t)cell * D : nullptr, in_table ? ceil + cell : nullptr);
-                }
-                if (mode != 0 && store_ok) {
-                    cell_quant_warp<D>(cr, lane, const_cast<int8_t*>(kq) + (int64_t)dst * FSATTN_CELL * D, const_cast<bf16*>(ks) + dst);
-                    cell_load_rows<D>(cr, vcell, D, lane, v_in);
-                    cell_quant_warp<D>(cr, lane, const_cast<int8_t*>(vq) + (int64_t)dst * FSATTN_CELL * D, const_cast<bf16*>(vs) + dst);
-                }
-            }
+            __syncthreads();
         }
-
-        // ---- the block's top-P list (refreshed when the block changed) ------------------------------------------------------
-        const int M_vis = blk_start / FSATTN_CELL;
-        int32_t* top_idx = st.top_idx + (int64_t)bh * st.P;
-        if (warp == 0) {
-            int n = 0;
-            for (int p = lane; p < st.P; p += 32) {
-                const int ci = top_idx[p];
-                sm.li[p] = ci;
-                sm.lc[p] = (ci >= 0) ? ceil[ci] : 0.0f;
-                n += (ci >= 0);
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(FS_FULL, n, o);
-            __syncwarp();
-            const int have_blk = st.top_blk[bh];
-            if (have_blk != blk_start) {
-                int c0 = have_blk / FSATTN_CELL; if (c0 < 0) c0 = 0;
-                for (int c = c0; c < M_vis; c++) pool_list_insert(sm.lc, sm.li, n, st.P, ceil[c], c, lane);
-                for (int p = lane; p < st.P; p += 32) top_idx[p] = (p < n) ? sm.li[p] : -1;
-                if (lane == 0) st.top_blk[bh] = blk_start;
-                if (mode == 2) {
-                    // free the slots of cells no later step reads: below c_lo and outside the top-P
-                    int c_lo = (blk_start - st.W) / FSATTN_CELL;
-                    if ((blk_start - st.W) < 0) c_lo = -1;      // floor division of a negative number
-                    if (M_vis - st.Wc < c_lo) c_lo = M_vis - st.Wc;
-                    if (c_lo < 0) c_lo = 0;
-                    for (int s0 = 0; s0 < st.n_slots; s0 += 32) {
-                        const int si = s0 + lane;
-                        if (si < st.n_slots) {
-                            const int occ = cell_in[si];
-                            if (occ >= 0 && occ < c_lo) {
-                                bool in_top = false;
-                                for (int p = 0; p < n; p++) in_top |= (sm.li[p] == occ);
-                                if (!in_top) { cell_in[si] = -1; slot_of[occ] = -1; }
-                            }
-                        }
-                    }
-                }
-            }
-            if (lane == 0) sm.n_list = n;
-        }
-        __syncthreads();
-
-        // ---- candidate slots ---------------------------------------------------------------------------------------------------
-        const int C = st.P + st.Wc;
-        const int n_list = sm.n_list;
-        for (int t = tid; t < C; t += blockDim.x) {
-            const int cand = (t < st.P) ? ((t < n_list) ? sm.li[t] : -1) : (M_vis - 1) - (t - st.P);
-            const int cc = cand < 0 ? 0 : cand;
-            sm.ccell[t] = cc;
-            sm.cok[t] = (cand >= 0) && (cc < M_vis);
-        }
-        __syncthreads();
-        for (int t = tid; t < C; t += blockDim.x) {
-            int ok = sm.cok[t];
-            const int cc = sm.ccell[t];
-            for (int j = 0; j < t && ok; j++) ok = (sm.ccell[j] != cc);
-            int slot = cc;
-            if (ok && mode == 2) {
-                slot = slot_of[cc];
-                if (slot < 0) { atomicAdd(st.status + FSATTN_ST_POOL_NO_SLOT, 1); ok = 0; slot = 0; }
-            }
-            sm.cok[t] = ok;
-            sm.cslot[t] = slot;
-            sm.cceil[t] = ok ? ceil[cc] : 0.0f;
-        }
-        __syncthreads();
-
-        // ---- scores: 8 lanes per candidate ---------------------------------------------------------------------------------------
+        STAMP(0, 3);
+        // ---- scores: 8 lanes per candidate, mean keys from shared memory ---------------------------------------------------
         {
-            constexpr int F = D / 8;             // floats per lane
-            const int s8 = lane & 7;
             float qv[F];
 #pragma unroll
             for (int j = 0; j < F; j++) qv[j] = sm.q_raw[s8 * F + j];
-            const float lam = a.lam[h];
-            const float two_sigma = f_mul(2.0f, a.sigma[h]);
-            const float qpos = (float)pos;
             for (int t0 = warp * 4; t0 < C; t0 += NWARP * 4) {
                 const int t = t0 + (lane >> 3);
-                const bool ok = t < C && sm.cok[t];
+                int4 mt = make_int4(-1, 0, 0, 0);
+                if (t < C) mt = meta_s[t];
+                const bool ok = mt.x >= 0;
                 float dot = 0.0f;
                 if (ok) {
-                    const float4* kr = reinterpret_cast<const float4*>(kbar + (int64_t)sm.cslot[t] * D + s8 * F);
+                    const float4* kr = reinterpret_cast<const float4*>(pool_s + (size_t)t * D + s8 * F);
 #pragma unroll
                     for (int j = 0; j < F / 4; j++) {
                         const float4 kv = kr[j];
@@ -480,47 +666,49 @@ __global__ void __launch_bounds__(NWARP * 32) fsl_decode_kernel(const fsattn_fsl
                 dot += __shfl_xor_sync(FS_FULL, dot, 4);
                 if (t < C && s8 == 0) {
                     float sc = FS_NEG_SCORE;
-                    if (ok) sc = f_add(f_mul(dot, a.scale), fs_prior(lam, sm.cceil[t], qpos, sm.ccell[t], (float)FSATTN_CELL, two_sigma));
+                    if (ok) sc = f_add(f_mul(dot, a.scale), sm.prior[t]);
                     sm.score[t] = sc;
+                    sm.ccell[t] = mt.x;
+                    sm.crow[t] = mt.y;
                 }
             }
         }
         __syncthreads();
+        STAMP(0, 4);
 
         // ---- top-kk by (score desc, slot asc): warp 0 ---------------------------------------------------------------------------------
         if (warp == 0) {
-            constexpr int PER = (MAXC + 31) / 32;
-            float sv[PER];
+            float sv[SC_ITERS];
 #pragma unroll
-            for (int j = 0; j < PER; j++) { const int t = lane + 32 * j; sv[j] = (t < C) ? sm.score[t] : -INFINITY; }
+            for (int j = 0; j < SC_ITERS; j++) { const int t = lane + 32 * j; sv[j] = (t < C) ? sm.score[t] : -INFINITY; }
             for (int k = 0; k < st.kk; k++) {
                 float best = -INFINITY; int bslot = 0x7fffffff;
 #pragma unroll
-                for (int j = 0; j < PER; j++) {
+                for (int j = 0; j < SC_ITERS; j++) {
                     const int t = lane + 32 * j;
                     if (sv[j] > best) { best = sv[j]; bslot = t; }     // ascending t: ties keep the lower slot
                 }
+                // order-preserving map float -> uint, then two warp reductions: the best score, the lowest slot holding it
+                const uint32_t bits = __float_as_uint(best);
+                const uint32_t key = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
+                const uint32_t kmax = __reduce_max_sync(FS_FULL, key);
+                const int wslot = (int)__reduce_min_sync(FS_FULL, (key == kmax) ? (uint32_t)bslot : 0x7fffffffu);
+                int cell = -1, row = -1;
+                if (kmax > 0x007fffffu && wslot < C) {                 // kmax of -inf maps to 0x007fffff
+                    cell = sm.ccell[wslot]; row = sm.crow[wslot];
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const float ob = __shfl_xor_sync(FS_FULL, best, o);
-                    const int os = __shfl_xor_sync(FS_FULL, bslot, o);
-                    if (ob > best || (ob == best && os < bslot)) { best = ob; bslot = os; }
-                }
-                int cell = -1, slot = -1;
-                if (best > -INFINITY && bslot < C) {
-                    if (sm.cok[bslot]) { cell = sm.ccell[bslot]; slot = sm.cslot[bslot]; }
-#pragma unroll
-                    for (int j = 0; j < PER; j++) if (lane + 32 * j == bslot) sv[j] = -INFINITY;
+                    for (int j = 0; j < SC_ITERS; j++) if (lane + 32 * j == wslot) sv[j] = -INFINITY;
                 }
                 if (lane == 0) {
-                    sm.selcell[k] = cell; sm.selslot[k] = slot;
+                    sm.selcell[k] = cell; sm.selrow[k] = (cell >= 0) ? row : -1;
                     if (a.sel_out != nullptr) a.sel_out[(int64_t)bh * st.kk + k] = cell;
                 }
             }
         }
         __syncthreads();
+        STAMP(0, 5);
 
-        // ---- readout of the selected cells: 4 groups of 8 rows per cell, spread over the warps ----------------------------------------
+        // ---- readout of the selected cells: 4 groups of 8 rows per cell, spread over the warps, all loads in flight at once -----------
         {
             float qlo[L::DPL], qhi[L::DPL];
 #pragma unroll
@@ -528,57 +716,53 @@ __global__ void __launch_bounds__(NWARP * 32) fsl_decode_kernel(const fsattn_fsl
             Part<D> P;
             P.init();
             const int ngroups = st.kk * 4;
-            for (int gi = warp; gi < ngroups; gi += NWARP) {
-                const int k = gi >> 2;
-                const int cell = sm.selcell[k];
-                if (cell < 0) continue;                       // warp-uniform
-                const int rr = ((gi & 3) << 3) + grp;
-                const int64_t tok = (int64_t)cell * FSATTN_CELL + rr;
-                const bool valid = pos_ok && tok < pos;
-                if (mode == 0) {
-                    attend_row<D, false, false>(P, kbuf + tok * D, vbuf + tok * D, 1.0f, 1.0f, valid, nullptr, nullptr, qlo, qhi, a.scale, sub);
-                } else {
-                    const int64_t base = (mode == 2) ? (int64_t)sm.selslot[k] : (int64_t)cell;
-                    const int64_t prow = base * FSATTN_CELL + rr;
-                    attend_row<D, true, false>(P, kq + prow * D, vq + prow * D, __bfloat162float(ks[base]), __bfloat162float(vs[base]),
-                                               valid, nullptr, nullptr, qlo, qhi, a.scale, sub);
+            for (int g0 = warp; g0 < ngroups; g0 += 2 * NWARP) {       // warp-uniform; kk = 4: one pass, two groups per warp
+                RowFlight<D> f[2];
+#pragma unroll
+                for (int u = 0; u < 2; u++) {
+                    const int gi = g0 + u * NWARP;
+                    const int k = (gi >> 2) & (FSATTN_MAX_KK - 1);
+                    const int cell = (gi < ngroups) ? sm.selcell[k] : -1;
+                    const int rr = ((gi & 3) << 3) + grp;
+                    const int64_t tok = (int64_t)cell * FSATTN_CELL + rr;
+                    const bool valid = pos_ok && cell >= 0 && tok < pos;
+                    const void* kp = nullptr; const void* vp = nullptr; const bf16* ksp = nullptr; const bf16* vsp = nullptr;
+                    if (valid) {
+                        if (mode == 0) { kp = hp.kbuf + tok * D; vp = hp.vbuf + tok * D; }
+                        else {
+                            const int64_t base = sm.selrow[k];
+                            kp = hp.kq + (base * FSATTN_CELL + rr) * D; vp = hp.vq + (base * FSATTN_CELL + rr) * D;
+                            ksp = hp.ks + base; vsp = hp.vs + base;
+                        }
+                    }
+                    row_issue<D, false>(f[u], kp, vp, ksp, vsp, valid, valid && mode != 0, nullptr, nullptr, sub);
                 }
+#pragma unroll
+                for (int u = 0; u < 2; u++) row_consume<D, false>(P, f[u], qlo, qhi, a.scale);
             }
+            STAMP(0, 10);
             part_merge_warp<D>(P);
             part_store<D>(P, sm.wrec[warp], lane);
         }
         __syncthreads();
+        STAMP(0, 11);
         if (warp == 0) {
             float acc[D / 32];
             rec_merge<D>(&sm.wrec[0][0], NWARP, D + 2, lane, lr_l, acc);
-            if (lane == 0) sm.lr_rec[1] = lr_l;
 #pragma unroll
             for (int j = 0; j < D / 32; j++) sm.lr_rec[2 + lane + 32 * j] = acc[j];
         }
+        if (S > 1) cluster.barrier_wait();        // completes the "everyone started" phase before the final barrier
     }
 
     // ================= exchange + combine ============================================================================================
-    if (S > 1) cluster.sync();
+    STAMP(0, 6);
+    if (S > 1) cluster.sync(); else __syncthreads();     // the window partials are in rank 0's shared memory
+    STAMP(0, 7); STAMP(1, 4);
     if (rank == 0 && warp == 0) {
-        // window: merge the partials of the window CTAs
-        float wm = -INFINITY;
         const int first = (S == 1) ? 0 : 1;
-        for (int r = first; r < S; r++) {
-            const float* rec = (S == 1) ? sm.win_rec : cluster.map_shared_rank(sm.win_rec, r);
-            wm = fmaxf(wm, rec[0]);
-        }
-        float wl = 0.0f, wacc[D / 32];
-#pragma unroll
-        for (int j = 0; j < D / 32; j++) wacc[j] = 0.0f;
-        for (int r = first; r < S; r++) {
-            const float* rec = (S == 1) ? sm.win_rec : cluster.map_shared_rank(sm.win_rec, r);
-            const float mi = rec[0];
-            if (mi == -INFINITY) continue;
-            const float f = __expf(mi - wm);
-            wl = fmaf(rec[1], f, wl);
-#pragma unroll
-            for (int j = 0; j < D / 32; j++) wacc[j] = fmaf(rec[2 + lane + 32 * j], f, wacc[j]);
-        }
+        float wl, wacc[D / 32];
+        rec_merge<D>(&sm.win_recs[first][0], (S == 1) ? 1 : S - 1, D + 2, lane, wl, wacc);
         const float winv = (wl > 0.0f) ? 1.0f / wl : 0.0f;
         const float linv = (lr_l > 0.0f) ? 1.0f / lr_l : 0.0f;
         float o[D / 32], ss = 0.0f;
@@ -589,17 +773,16 @@ __global__ void __launch_bounds__(NWARP * 32) fsl_decode_kernel(const fsattn_fsl
         }
         ss = warp_sum(ss);
         const float rn = f_div(1.0f, f_sqrt(f_add(ss * (1.0f / D), a.eps)));
-        const float g = a.lrs[h];
         bf16* yp = (bf16*)a.y + (int64_t)b * st.H * D + (int64_t)h * D;
 #pragma unroll
         for (int j = 0; j < D / 32; j++) {
             const int d = lane + 32 * j;
             const float sr = bf_round(wacc[j] * winv);
-            const float lr = f_mul(f_mul(o[j], rn), a.norm_w[d]);
-            yp[d] = __float2bfloat16_rn(f_add(sr, f_mul(g, lr)));
+            const float lr = f_mul(f_mul(o[j], rn), nw_reg[j]);
+            yp[d] = __float2bfloat16_rn(f_add(sr, f_mul(g_lrs, lr)));
         }
     }
-    if (S > 1) cluster.sync();   // remote shared memory stays valid until rank 0 has read it
+    STAMP(0, 8);
 }
 
 template <int D>
@@ -607,17 +790,31 @@ int launch_decode(const fsattn_fsl_decode_t* a, cudaStream_t stream) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a->splits, a->st.B * a->st.H, 1);
     cfg.blockDim = dim3(NWARP * 32, 1, 1);
-    cfg.dynamicSmemBytes = 0;
+    const size_t dyn = (size_t)(a->st.P + a->st.Wc) * ((size_t)D * 4 + 16);
+    static size_t opted[16] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dyn > 24 * 1024 && dev >= 0 && dev < 16 && opted[dev] < dyn) {
+        if (cudaFuncSetAttribute(fsl_decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) != cudaSuccess) {
+            fs_set_error("fsl_decode_step: cannot opt in to %zu bytes of shared memory", dyn);
+            return FSATTN_ELAUNCH;
+        }
+        opted[dev] = dyn;
+    }
+    cfg.dynamicSmemBytes = dyn;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = a->splits;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = a->pdl ? 1 : 0;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     cudaError_t e = cudaLaunchKernelEx(&cfg, fsl_decode_kernel<D>, *a);
     if (e != cudaSuccess) {
+        (void)cudaGetLastError();       // the error is reported through the return code; do not leave it pending
         fs_set_error("fsl_decode_step: launch failed: %s", cudaGetErrorString(e));
         return FSATTN_ELAUNCH;
     }
@@ -625,6 +822,12 @@ int launch_decode(const fsattn_fsl_decode_t* a, cudaStream_t stream) {
 }
 
 }  // namespace
+
+#ifdef FSATTN_DEC_TIMING
+extern "C" __attribute__((visibility("default"))) int fsattn_debug_dec_timing(long long* out32) {
+    return cudaMemcpyFromSymbol(out32, g_dec_stamps, sizeof(long long) * 32) == cudaSuccess ? 0 : -1;
+}
+#endif
 
 extern "C" int fsattn_fsl_decode_step(const fsattn_fsl_decode_t* a, fsattn_stream_t stream) {
     FS_REQUIRE(a != nullptr, "fsl_decode_step: null args");
@@ -639,7 +842,8 @@ extern "C" int fsattn_fsl_decode_step(const fsattn_fsl_decode_t* a, fsattn_strea
     FS_REQUIRE(st.Bq > 0 && st.Bq % FSATTN_CELL == 0, "fsl_decode_step: query block %d must be a multiple of the cell size", st.Bq);
     FS_REQUIRE(st.W >= 0, "fsl_decode_step: window %d", st.W);
     FS_REQUIRE(a->splits == 1 || a->splits == 2 || a->splits == 4 || a->splits == 8, "fsl_decode_step: splits %d not in {1,2,4,8}", a->splits);
-    FS_REQUIRE(st.kbar && st.ceil && st.top_idx && st.top_blk && st.status, "fsl_decode_step: null state pointer");
+    FS_REQUIRE(st.kbar && st.ceil && st.top_idx && st.top_blk && st.status && st.pool_kbar && st.pool_meta && st.pool_blk, "fsl_decode_step: null state pointer");
+    FS_REQUIRE(((uintptr_t)st.pool_kbar & 15) == 0 && ((uintptr_t)st.pool_meta & 15) == 0, "fsl_decode_step: pool buffers must be 16-byte aligned");
     if (st.store_mode == 0) {
         FS_REQUIRE(st.kbuf && st.vbuf, "fsl_decode_step: bf16 store without buffers");
         FS_REQUIRE(((uintptr_t)st.kbuf & 15) == 0 && ((uintptr_t)st.vbuf & 15) == 0 && st.buf_sb % 8 == 0 && st.buf_sh % 8 == 0,

@@ -133,7 +133,7 @@ class FSAttn(nn.Module):
         self.fs_fused_attn = kwargs.get("fs_fused_attn", None)
         self.cell_fused_select = kwargs.get("cell_fused_select", None)
         self.fsb_enabled = bool(kwargs.get("fsb_enabled", False))
-        self.decode_splits = int(kwargs.get("decode_splits", 8))
+        self.decode_splits = int(kwargs.get("decode_splits", os.environ.get("FSATTN_DECODE_SPLITS", "8")))
         if dropout != 0.0:
             raise NotImplementedError("inference only: dropout must be 0")
         self.sel_scale = nn.Parameter(torch.ones(n_heads))
@@ -320,3 +320,15 @@ class FSAttn(nn.Module):
         y = ops.fsl_decode_step(st, qkv[:, 0], qkv[:, 1], qkv[:, 2], buf["pos_t"], cos, sin, lam, sigma, lrs, norm_w,
                                 scale=self.scale, eps=self.lr_norm.eps, y=buf.get("y"), splits=self.decode_splits)
         return self.W_o(y.view(B, 1, dm))
+
+    def graph_decode_attn(self, qkv, buf, y=None, pdl=True):
+        """The attention part of one decode token given the fused projection qkv (B, 3*d) bf16: returns W_o's input
+        (B, d). Used by the decoder whose trunk projections run in this library's own GEMV kernels."""
+        B = qkv.shape[0]
+        H, D = self.n_heads, self.head_dim
+        q4 = qkv.view(B, 3, H, D)
+        st = buf["cache"].decode_state(q4)
+        cos, sin = self.rope.tables_bf16(st.cap_rows)
+        lam, sigma, lrs, norm_w = self.head_params()
+        return ops.fsl_decode_step(st, q4[:, 0], q4[:, 1], q4[:, 2], buf["pos_t"], cos, sin, lam, sigma, lrs, norm_w,
+                                   scale=self.scale, eps=self.lr_norm.eps, y=y, splits=self.decode_splits, pdl=pdl)

@@ -89,6 +89,7 @@ class FslState(C.Structure):
                 ("slot_of", vp), ("so_sb", i64), ("so_sh", i64),
                 ("cell_in", vp), ("ci_sb", i64), ("ci_sh", i64),
                 ("top_idx", vp), ("top_blk", vp),
+                ("pool_kbar", vp), ("pool_meta", vp), ("pool_blk", vp),
                 ("status", vp)]
 
 
@@ -100,7 +101,7 @@ class FslDecode(C.Structure):
                 ("lam", vp), ("sigma", vp), ("lrs", vp), ("norm_w", vp),
                 ("scale", f32), ("eps", f32),
                 ("y", vp), ("sel_out", vp),
-                ("splits", i32)]
+                ("splits", i32), ("pdl", i32)]
 
 
 class SlotPrefill(C.Structure):
@@ -108,6 +109,17 @@ class SlotPrefill(C.Structure):
                 ("kbar_cells", vp), ("kc_sb", i64), ("kc_sh", i64),
                 ("N", i32)]
 
+
+class TrunkGemv(C.Structure):
+    _fields_ = [("w", vp), ("x", vp), ("x_stride", i64),
+                ("norm_w", vp), ("eps", f32),
+                ("out", vp), ("out_stride", i64),
+                ("res", vp), ("res_stride", i64),
+                ("M", i32), ("K", i32), ("n_out", i32), ("epilogue", i32), ("m0", i32), ("pdl", i32)]
+
+
+EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU = 0, 1, 2
+EXTRA_STRUCTS = {"fsattn_trunk_gemv_t": TrunkGemv}
 
 # every exported symbol of include/fsattn_b200.h with its argument struct (None = no struct argument)
 ENTRY_POINTS = {
@@ -122,6 +134,7 @@ ENTRY_POINTS = {
     "fsattn_readout_combine": ReadoutCombine,
     "fsattn_fsl_decode_step": FslDecode,
     "fsattn_slot_prefill": SlotPrefill,
+    "fsattn_trunk_gemv": TrunkGemv,
 }
 
 _lib = None

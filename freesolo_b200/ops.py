@@ -254,11 +254,14 @@ class FslDecodeState:
         self.ceil = torch.zeros(B, H, self.cap_cells, dtype=torch.float32, **z)
         self.top_idx = torch.full((B, H, P), -1, dtype=torch.int32, **z)
         self.top_blk = torch.zeros(B, H, dtype=torch.int32, **z)
+        self.pool_kbar = torch.zeros(B, H, P + Wc, D, dtype=torch.float32, **z)
+        self.pool_meta = torch.full((B, H, P + Wc, 4), -1, dtype=torch.int32, **z)
+        self.pool_blk = torch.full((B, H), -1, dtype=torch.int32, **z)
         self.status = torch.zeros(L.ST_WORDS, dtype=torch.int32, **z)
 
     def nbytes(self) -> int:
         ts = (self.kbuf, self.vbuf, self.kq, self.vq, self.ks, self.vs, self.khot, self.vhot, self.slot_of, self.cell_in,
-              self.kbar, self.ceil, self.top_idx, self.top_blk, self.status)
+              self.kbar, self.ceil, self.top_idx, self.top_blk, self.pool_kbar, self.pool_meta, self.pool_blk, self.status)
         return sum(t.numel() * t.element_size() for t in ts if t is not None)
 
     def struct(self) -> L.FslState:
@@ -279,6 +282,7 @@ class FslDecodeState:
             s.slot_of, s.so_sb, s.so_sh = self.slot_of.data_ptr(), self.slot_of.stride(0), self.slot_of.stride(1)
             s.cell_in, s.ci_sb, s.ci_sh = self.cell_in.data_ptr(), self.cell_in.stride(0), self.cell_in.stride(1)
         s.top_idx, s.top_blk, s.status = self.top_idx.data_ptr(), self.top_blk.data_ptr(), self.status.data_ptr()
+        s.pool_kbar, s.pool_meta, s.pool_blk = self.pool_kbar.data_ptr(), self.pool_meta.data_ptr(), self.pool_blk.data_ptr()
         return s
 
     @torch.no_grad()
@@ -292,6 +296,7 @@ class FslDecodeState:
         if kbar is None or ceil is None:
             kbar, ceil = cell_stats(K, ncell)
         self.status.zero_()
+        self.pool_blk.fill_(-1)             # the first decode step gathers the block's candidate pool
         self.top_idx.fill_(-1)
         blk = (N // self.Bq) * self.Bq
         self.top_blk.fill_(blk)
@@ -334,7 +339,7 @@ def slot_prefill(state: FslDecodeState, K, V, kbar_cells, N: int):
 
 
 def fsl_decode_step(state: FslDecodeState, q, k, v, pos_t, cos, sin, lam, sigma, lrs, norm_w, *, scale: float, eps: float,
-                    y=None, sel_out=None, splits: int = 8):
+                    y=None, sel_out=None, splits: int = 8, pdl: bool = False):
     """One decode token of one FS-L layer. q,k,v: (B,H,D) bf16 views with equal strides and unit inner stride (e.g. slices
     of a fused QKV projection); pos_t: int64 device scalar; lam/sigma/lrs (H) fp32, norm_w (D) fp32 (all device tensors
     that stay alive until the launch has run). Returns y (B, H*D) bf16."""
@@ -356,8 +361,37 @@ def fsl_decode_step(state: FslDecodeState, q, k, v, pos_t, cos, sin, lam, sigma,
     a.scale, a.eps = float(scale), float(eps)
     a.y, a.sel_out = y.data_ptr(), _p(sel_out)
     a.splits = int(splits)
+    a.pdl = 1 if pdl else 0
     L.call("fsattn_fsl_decode_step", a, _stream(q))
     return y
+
+
+def trunk_gemv(x, w, *, norm_w=None, eps: float = 1e-6, res=None, swiglu: bool = False, out=None, pdl: bool = True):
+    """Decode-step trunk projection for a few rows: out = epilogue([rmsnorm](x) @ w^T).
+    x (M,K) bf16 (row stride free), w (n_out,K) bf16 contiguous, norm_w (K) bf16 or None. res (M,n_out) adds a residual
+    (out may be res itself); swiglu treats w as [gate rows; up rows] and returns silu(gate)*up (M, n_out/2)."""
+    _need_cuda(x, w, norm_w, res)
+    M, K = x.shape
+    n_out = w.shape[0]
+    assert x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and w.is_contiguous() and w.shape[1] == K and x.stride(1) == 1
+    n_cols = n_out // 2 if swiglu else n_out
+    if out is None:
+        out = torch.empty(M, n_cols, dtype=torch.bfloat16, device=x.device)
+    assert out.dtype == torch.bfloat16 and out.stride(1) == 1 and tuple(out.shape) == (M, n_cols)
+    a = L.TrunkGemv()
+    a.w, a.x, a.x_stride = w.data_ptr(), x.data_ptr(), x.stride(0)
+    if norm_w is not None:
+        assert norm_w.dtype == torch.bfloat16 and norm_w.is_contiguous() and norm_w.numel() == K
+        a.norm_w = norm_w.data_ptr()
+    a.eps = float(eps)
+    a.out, a.out_stride = out.data_ptr(), out.stride(0)
+    a.epilogue = L.EPI_SWIGLU if swiglu else (L.EPI_RESIDUAL if res is not None else L.EPI_STORE)
+    if res is not None:
+        assert not swiglu and res.dtype == torch.bfloat16 and res.stride(1) == 1 and tuple(res.shape) == (M, n_out)
+        a.res, a.res_stride = res.data_ptr(), res.stride(0)
+    a.M, a.K, a.n_out, a.m0, a.pdl = M, K, n_out, 0, 1 if pdl else 0
+    L.call("fsattn_trunk_gemv", a, _stream(x))
+    return out
 
 
 def default_scale(D: int) -> float:

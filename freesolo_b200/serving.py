@@ -214,19 +214,39 @@ class GraphedDecoder:
         self.bufs = [{"pos_t": self.pos_t, "cache": c} for c in self.cache]
         for blk in self.blocks:
             blk.ffn._ensure_gu_cache()
+        d, f = m.d_model, self.blocks[0].ffn.w_gate.weight.shape[0]
+        z = dict(dtype=torch.bfloat16, device=self.dev)
+        self.x = torch.zeros(B, d, **z)             # residual stream of the current token
+        self.qkv = torch.zeros(B, 3 * d, **z)
+        self.y = torch.zeros(B, d, **z)
+        self.act = torch.zeros(B, f, **z)
+        self.logits = torch.zeros(B, m.vocab_size, **z)
         return self.tok
 
     def _trunk_step(self):
         """One token through the model: reads self.tok and pos_t, overwrites self.tok with the greedy next token and
-        advances pos_t, all on the device."""
+        advances pos_t, all on the device. Per layer five launches of this library: RMSNorm+QKV projection, the fused
+        attention step, W_o + residual, RMSNorm + gate/up + SwiGLU, down projection + residual (each projection kernel
+        starts streaming its weights before its producer has finished: programmatic dependent launch)."""
+        from . import ops
+        import os
         m = self.m
-        x = m.tok_emb(self.tok)
+        x = self.x
+        pdl = os.environ.get("FSATTN_PDL", "1") == "1"
+        skip_attn = os.environ.get("FSATTN_DEBUG_SKIP_ATTN", "0") == "1"     # timing experiments only
+        x.copy_(m.tok_emb(self.tok).view(x.shape))
         for i, blk in enumerate(self.blocks):
-            x = x + self.attn[i].graph_decode_layer(blk.ln1(x), self.bufs[i])
-            x = x + blk.ffn(blk.ln2(x))
-        logits = lm_head(m, m.ln_final(x)[:, -1])
-        self.logits = logits
-        self.tok.copy_(logits.argmax(dim=-1, keepdim=True))
+            a = self.attn[i]
+            wqkv, _ = a._ensure_qkv_cache()
+            ops.trunk_gemv(x, wqkv, norm_w=blk.ln1.weight, eps=blk.ln1.eps, out=self.qkv, pdl=pdl)
+            if not skip_attn:
+                a.graph_decode_attn(self.qkv, self.bufs[i], y=self.y, pdl=pdl)
+            ops.trunk_gemv(self.y, a.W_o.weight, res=x, out=x, pdl=pdl)
+            wgu, _ = blk.ffn._ensure_gu_cache()
+            ops.trunk_gemv(x, wgu, norm_w=blk.ln2.weight, eps=blk.ln2.eps, swiglu=True, out=self.act, pdl=pdl)
+            ops.trunk_gemv(self.act, blk.ffn.w_down.weight, res=x, out=x, pdl=pdl)
+        ops.trunk_gemv(x, m.lm_head.weight, norm_w=m.ln_final.weight, eps=m.ln_final.eps, out=self.logits, pdl=pdl)
+        self.tok.copy_(self.logits.argmax(dim=-1, keepdim=True))
         self.pos_t.add_(1)
 
     @torch.no_grad()

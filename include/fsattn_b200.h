@@ -157,7 +157,7 @@ FSATTN_API int fsattn_readout_combine(const fsattn_readout_combine_t* a, fsattn_
  *   kbuf,vbuf (cap,D) bf16 [mode 0]; kq,vq (rows,D) int8 + ks,vs (cells|slots) bf16 [modes 1,2];
  *   khot,vhot (32,D) bf16 open cell [modes 1,2]; kbar (cells|slots, D) fp32; ceil (cells) fp32;
  *   slot_of (cells) int32, cell_in (slots) int32 [mode 2]; top_idx (P) int32 = the block's top-P cells in pool order,
- *   top_blk (1) int32 = block start that list is valid for.
+ *   top_blk (1) int32 = block start that list is valid for; pool_* = the gathered candidate pool (see below).
  * Rows below (pos/32)*32 are completed cells; later rows are the open cell. */
 typedef struct {
     int32_t store_mode, B, H, D, P, Wc, W, Bq, kk, n_slots;
@@ -171,6 +171,11 @@ typedef struct {
     int32_t* slot_of; int64_t so_sb, so_sh;
     int32_t* cell_in; int64_t ci_sb, ci_sh;
     int32_t* top_idx; int32_t* top_blk; /* (B,H,P), (B,H) contiguous */
+    /* the current block's candidate pool, gathered once per block by the decode step so that the other Bq-1 steps read
+     * it without any index indirection: pool_kbar (B,H,P+Wc,D) fp32 mean keys, pool_meta (B,H,P+Wc,4) int32 =
+     * {cell id or -1 when the slot is not selectable, row base (cell or slot index), ceiling bits, 0}, pool_blk (B,H)
+     * int32 = block start the pool is valid for (-1: rebuild at the next step). All contiguous. */
+    float* pool_kbar; int32_t* pool_meta; int32_t* pool_blk;
     int32_t* status;                    /* FSATTN_ST_WORDS int32 */
 } fsattn_fsl_state_t;
 
@@ -191,6 +196,7 @@ typedef struct {
     float scale, eps;
     void* y; int32_t* sel_out;
     int32_t splits;
+    int32_t pdl; /* 1 = launch with programmatic stream serialization (overlaps the launch with the producer's tail) */
 } fsattn_fsl_decode_t;
 FSATTN_API int fsattn_fsl_decode_step(const fsattn_fsl_decode_t* a, fsattn_stream_t stream);
 
@@ -205,6 +211,26 @@ typedef struct {
     int32_t N;
 } fsattn_slot_prefill_t;
 FSATTN_API int fsattn_slot_prefill(const fsattn_slot_prefill_t* a, fsattn_stream_t stream);
+
+/* ---- decode-step trunk projection (small batch) -------------------------------------------------------------------------
+ * The glue around the attention kernel in a decode step: out = epilogue([rmsnorm](x) @ W^T) for M rows of activations.
+ * Replaces, for B*N == 1.. rows, trunk_triton.rms_norm_cast + the fused QKV / gate-up GEMVs + silu_mul + the residual adds
+ * of experiments/scaling/model.py:111-145,211-237 and src/fsattn/attention.py:1396-1420 (cuBLAS + Triton launches there).
+ * W (n_out, K) bf16 row-major; x (M, K) bf16 rows x_stride apart; norm_w (K) bf16 or NULL (no norm);
+ * epilogue: STORE out[m,n] = acc; RESIDUAL out[m,n] = res[m,n] + acc (out may alias res);
+ * SWIGLU: W holds n_out/2 gate rows then n_out/2 up rows, out (M, n_out/2) = silu(gate) * up.
+ * m0 is used internally (first row of a pass); pass 0. */
+#define FSATTN_EPI_STORE 0
+#define FSATTN_EPI_RESIDUAL 1
+#define FSATTN_EPI_SWIGLU 2
+typedef struct {
+    const void* w; const void* x; int64_t x_stride;
+    const void* norm_w; float eps;
+    void* out; int64_t out_stride;
+    const void* res; int64_t res_stride;
+    int32_t M, K, n_out, epilogue, m0, pdl;
+} fsattn_trunk_gemv_t;
+FSATTN_API int fsattn_trunk_gemv(const fsattn_trunk_gemv_t* a, fsattn_stream_t stream);
 
 #ifdef __cplusplus
 }
