@@ -223,6 +223,7 @@ __device__ long long g_dec_stamps[2][16];
 #define STAMP(r, i) do { } while (0)
 #endif
 
+constexpr int WIN_NF = 3;                      // 8-row groups of window rows a warp keeps in flight
 constexpr int SC_ITERS = (MAXC + 31) / 32;     // scoring rounds: 32 candidates per round over the 8 warps
 
 template <int D>
@@ -313,9 +314,9 @@ __device__ __forceinline__ void window_issue2(RowFlight<D>* f, const WinCtx<D>& 
     const fsattn_fsl_state_t& st = a.st;
     const bf16* cosT = (const bf16*)a.cos;
     const bf16* sinT = (const bf16*)a.sin;
-    int64_t r[2]; bool valid[2], i8[2]; int slot[2];
+    int64_t r[WIN_NF]; bool valid[WIN_NF], i8[WIN_NF]; int slot[WIN_NF];
 #pragma unroll
-    for (int u = 0; u < 2; u++) {
+    for (int u = 0; u < WIN_NF; u++) {
         const int64_t g = g0 + (int64_t)u * w.nw;
         r[u] = (g << 3) + grp;
         // the new token's row (r == pos) is handled separately: its key and value come from the producer kernel
@@ -325,7 +326,7 @@ __device__ __forceinline__ void window_issue2(RowFlight<D>* f, const WinCtx<D>& 
         if (i8[u] && w.mode == 2) slot[u] = hp.slot_of[r[u] / FSATTN_CELL];
     }
 #pragma unroll
-    for (int u = 0; u < 2; u++) {
+    for (int u = 0; u < WIN_NF; u++) {
         const void* kp = nullptr; const void* vp = nullptr;
         const bf16* ksp = nullptr; const bf16* vsp = nullptr;
         bool ok = valid[u];
@@ -364,8 +365,8 @@ __device__ __forceinline__ void window_finish(Smem<D>& sm, RowFlight<D>* f, cons
     int64_t g0 = w.g_lo + w.gw;
     for (;;) {
 #pragma unroll
-        for (int u = 0; u < 2; u++) row_consume<D, true>(P, f[u], qlo, qhi, a.scale);
-        g0 += 2 * (int64_t)w.nw;
+        for (int u = 0; u < WIN_NF; u++) row_consume<D, true>(P, f[u], qlo, qhi, a.scale);
+        g0 += WIN_NF * (int64_t)w.nw;
         if (g0 > w.g_hi) break;                 // warp-uniform
         window_issue2<D>(f, w, a, hp, g0, lane);
     }
@@ -586,7 +587,7 @@ __global__ void __launch_bounds__(NWARP * 32) fsl_decode_kernel(const fsattn_fsl
     w.nw = (S == 1) ? NWARP : (S - 1) * NWARP;
     w.gw = (S == 1) ? warp : (rank - 1) * NWARP + warp;
     const bool do_window = (S == 1) || (rank > 0);
-    RowFlight<D> wf[2];
+    RowFlight<D> wf[WIN_NF];
     if (do_window) window_issue2<D>(wf, w, a, hp, w.g_lo + w.gw, lane);
     if (rank == 0) {
         // the pool's bulk copy; the wait is bounded. The position priors of the candidates need no query: compute them now.

@@ -133,7 +133,7 @@ class FSAttn(nn.Module):
         self.fs_fused_attn = kwargs.get("fs_fused_attn", None)
         self.cell_fused_select = kwargs.get("cell_fused_select", None)
         self.fsb_enabled = bool(kwargs.get("fsb_enabled", False))
-        self.decode_splits = int(kwargs.get("decode_splits", os.environ.get("FSATTN_DECODE_SPLITS", "8")))
+        self.decode_splits = int(kwargs.get("decode_splits", os.environ.get("FSATTN_DECODE_SPLITS", "4")))
         if dropout != 0.0:
             raise NotImplementedError("inference only: dropout must be 0")
         self.sel_scale = nn.Parameter(torch.ones(n_heads))
