@@ -1,9 +1,456 @@
-// Tensor-core (tcgen05 / TMEM / TMA) window attention for prefill. Placeholder dispatch until the kernel lands: reports
-// that no shape is covered, so every call takes the CUDA-core kernel.
+// Window branch of a prefill on the 5th-generation tensor cores: tcgen05.mma with TMEM accumulators, operands staged by
+// TMA (cp.async.bulk.tensor, 128-byte swizzle), one CTA per 128 queries of one (batch, head).
+//
+//   pass 0 (rope_qk_kernel): rotate Q and K once into a (B*H, N, D) bf16 workspace (HBM-bound: 2 reads + 2 writes of N*D)
+//   pass 1 (window_tc_kernel): for the W/128 + 1 key tiles of the band
+//        S  = Qr Kr^T        tcgen05.mma 128x128x64 (4 k-steps), accumulator in TMEM
+//        P  = exp2(S*c - m)  4 softmax warps, one query row per thread (tcgen05.ld), band mask on the edge tiles,
+//                            P written as bf16 into shared memory in the K-major swizzled operand layout
+//        PV = P V            tcgen05.mma 128x64x128 (8 k-steps) into a second TMEM accumulator; the running output lives in
+//                            registers: O = O * alpha + PV
+// Warp roles: warps 0-3 softmax/epilogue (TMEM lane quarter = warp id), warp 4 TMA producer, warp 5 MMA issuer.
+// Every mbarrier wait is bounded; on a timeout the CTA records it in *status, stops issuing work and still frees its TMEM.
+//
+// FLOPs per CTA: (W/128+1) tiles * (2*128*128*64 + 2*128*128*64); algorithmic FLOPs per query 4*D*min(i+1, W+1).
+#include <cuda.h>
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 
-bool fs_window_prefill_tc_ok(const fsattn_window_prefill_t*) { return false; }
-int fs_window_prefill_tc(const fsattn_window_prefill_t*, cudaStream_t) {
-    fs_set_error("window_prefill: tensor-core kernel not built");
-    return FSATTN_EUNSUPPORTED;
+namespace {
+
+constexpr int TC_BM = 128;          // queries per CTA
+constexpr int TC_BN = 128;          // keys per tile
+constexpr int TC_D = 64;
+constexpr int TC_THREADS = 192;
+constexpr int TC_WAIT_ITERS = 1 << 24;
+
+// shared memory map (bytes, from a 1024-byte aligned base)
+constexpr int SM_Q = 0;                         // 128 x 64 bf16
+constexpr int SM_K = SM_Q + 16384;              // 2 stages
+constexpr int SM_V = SM_K + 2 * 16384;          // 2 stages
+constexpr int SM_P = SM_V + 2 * 16384;          // 2 buffers of 128 x 128 bf16 (two K-blocks of 128 x 64)
+constexpr int SM_BAR = SM_P + 2 * 32768;        // mbarriers
+constexpr int SM_TOTAL = SM_BAR + 256;
+
+enum { BAR_Q = 0, BAR_KV_FULL = 1, BAR_KV_EMPTY = 3, BAR_S_FULL = 5, BAR_S_FREE = 7, BAR_P_FULL = 9, BAR_PV_FULL = 11,
+       BAR_PV_FREE = 13, BAR_COUNT = 15 };
+
+__device__ __forceinline__ uint32_t s_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void bar_init(uint64_t* bar, int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(s_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void bar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(s_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void bar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(s_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity) {
+    const uint32_t addr = s_u32(bar);
+    for (int i = 0; i < TC_WAIT_ITERS; i++) {
+        uint32_t done;
+        asm volatile("{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}"
+                     : "=r"(done) : "r"(addr), "r"(parity) : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+                 ::"r"(s_u32(dst)), "l"(map), "r"(s_u32(bar)), "r"(c0), "r"(c1), "r"(c2) : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3, uint64_t* bar) {
+    asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];"
+                 ::"r"(s_u32(dst)), "l"(map), "r"(s_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3) : "memory");
+}
+
+// shared-memory matrix descriptor, 128-byte swizzle, 8-row groups 1024 bytes apart (K-major and MN-major tiles of 128-byte rows)
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3ffff) >> 4);           // start address
+    d |= (uint64_t)1 << 16;                            // leading byte offset (unused with one 128-byte atom per row)
+    d |= (uint64_t)(1024 >> 4) << 32;                  // stride byte offset: next 8-row group
+    d |= (uint64_t)1 << 46;                            // descriptor version (Blackwell)
+    d |= (uint64_t)2 << 61;                            // SWIZZLE_128B
+    return d;
+}
+
+// instruction descriptor: (bf16 | fp16) x bf16 -> fp32, M = 128, N = n, A K-major (a_bf16 = 0: fp16), B K-major (b_mn = 0) or
+// MN-major (b_mn = 1)
+__device__ __forceinline__ uint32_t instr_desc(int n, int b_mn, int a_bf16) {
+    return (1u << 4) | ((uint32_t)a_bf16 << 7) | (1u << 10) | ((uint32_t)b_mn << 16) | ((uint32_t)(n >> 3) << 17) |
+           ((uint32_t)(TC_BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, int accumulate) {
+    asm volatile("{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\ntcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
+                 ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(s_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+    uint32_t r[32];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+                 "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+                   "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+                   "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                 : "r"(taddr) : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+
+// ---- pass 0: rotate Q and K into the workspace ----------------------------------------------------------------------
+__global__ void __launch_bounds__(256) rope_qk_kernel(const fsattn_window_prefill_t a, bf16* qr, bf16* kr) {
+    constexpr int HALF = TC_D / 2, CH = HALF / 8;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t total = (int64_t)a.B * a.H * a.N * CH;
+    if (i >= total) return;
+    const int e = (int)(i % CH);
+    const int64_t row = i / CH;                         // (b*H + h)*N + n
+    const int n = (int)(row % a.N);
+    const int64_t bh = row / a.N;
+    const int b = (int)(bh / a.H), h = (int)(bh - (int64_t)b * a.H);
+    const int64_t tp = (int64_t)(a.pos0 + n) * TC_D;
+    const uint4 c = reinterpret_cast<const uint4*>((const bf16*)a.cos + tp)[e];
+    const uint4 s = reinterpret_cast<const uint4*>((const bf16*)a.sin + tp)[e];
+    const float cc[8] = {bf_lo(c.x), bf_hi(c.x), bf_lo(c.y), bf_hi(c.y), bf_lo(c.z), bf_hi(c.z), bf_lo(c.w), bf_hi(c.w)};
+    const float ss[8] = {bf_lo(s.x), bf_hi(s.x), bf_lo(s.y), bf_hi(s.y), bf_lo(s.z), bf_hi(s.z), bf_lo(s.w), bf_hi(s.w)};
+#pragma unroll
+    for (int t = 0; t < 2; t++) {
+        const fsattn_bhnd_t& src = t == 0 ? a.q : a.k;
+        const bf16* p = (const bf16*)src.ptr + b * src.sb + h * src.sh + (int64_t)n * src.sn;
+        const uint4 lo = reinterpret_cast<const uint4*>(p)[e];
+        const uint4 hi = reinterpret_cast<const uint4*>(p + HALF)[e];
+        const float x1[8] = {bf_lo(lo.x), bf_hi(lo.x), bf_lo(lo.y), bf_hi(lo.y), bf_lo(lo.z), bf_hi(lo.z), bf_lo(lo.w), bf_hi(lo.w)};
+        const float x2[8] = {bf_lo(hi.x), bf_hi(hi.x), bf_lo(hi.y), bf_hi(hi.y), bf_lo(hi.z), bf_hi(hi.z), bf_lo(hi.w), bf_hi(hi.w)};
+        uint4 o1, o2;
+        o1.x = pack_bf2(x1[0] * cc[0] - x2[0] * ss[0], x1[1] * cc[1] - x2[1] * ss[1]);
+        o1.y = pack_bf2(x1[2] * cc[2] - x2[2] * ss[2], x1[3] * cc[3] - x2[3] * ss[3]);
+        o1.z = pack_bf2(x1[4] * cc[4] - x2[4] * ss[4], x1[5] * cc[5] - x2[5] * ss[5]);
+        o1.w = pack_bf2(x1[6] * cc[6] - x2[6] * ss[6], x1[7] * cc[7] - x2[7] * ss[7]);
+        o2.x = pack_bf2(x2[0] * cc[0] + x1[0] * ss[0], x2[1] * cc[1] + x1[1] * ss[1]);
+        o2.y = pack_bf2(x2[2] * cc[2] + x1[2] * ss[2], x2[3] * cc[3] + x1[3] * ss[3]);
+        o2.z = pack_bf2(x2[4] * cc[4] + x1[4] * ss[4], x2[5] * cc[5] + x1[5] * ss[5]);
+        o2.w = pack_bf2(x2[6] * cc[6] + x1[6] * ss[6], x2[7] * cc[7] + x1[7] * ss[7]);
+        bf16* dst = (t == 0 ? qr : kr) + row * TC_D;
+        reinterpret_cast<uint4*>(dst)[e] = o1;
+        reinterpret_cast<uint4*>(dst + HALF)[e] = o2;
+    }
+}
+
+struct TcParams {
+    int N, W, H;
+    float c2;              // scale * log2(e)
+    bf16* out;             // (B, N, H*D)
+    int32_t* status;       // optional: timeouts are counted in status[0]
+};
+
+// ---- pass 1 -------------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(TC_THREADS, 1)
+window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                 const __grid_constant__ CUtensorMap tm_v, const TcParams p) {
+    extern __shared__ unsigned char tc_smem_raw[];
+    __shared__ uint32_t tmem_base_s;
+    __shared__ int abort_s;
+    unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(base + SM_BAR);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int q0 = blockIdx.x * TC_BM;
+    const int bh = blockIdx.y;
+    const int b = bh / p.H, h = bh - b * p.H;
+    const int ntile_total = p.W / TC_BN + 1;
+    int t_first = (p.W - q0) / TC_BN;                 // tiles that lie entirely before the sequence start are skipped
+    if (t_first < 0) t_first = 0;
+    const int nt = ntile_total - t_first;
+
+    if (tid == 0) {
+        bar_init(&bars[BAR_Q], 1);
+        for (int s = 0; s < 2; s++) {
+            bar_init(&bars[BAR_KV_FULL + s], 1);
+            bar_init(&bars[BAR_KV_EMPTY + s], 1);
+            bar_init(&bars[BAR_S_FULL + s], 1);
+            bar_init(&bars[BAR_S_FREE + s], 128);
+            bar_init(&bars[BAR_P_FULL + s], 128);
+            bar_init(&bars[BAR_PV_FULL + s], 1);
+            bar_init(&bars[BAR_PV_FREE + s], 128);
+        }
+        abort_s = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 4) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s_u32(&tmem_base_s)), "r"(512) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_s;
+    volatile int* abortp = &abort_s;
+
+    if (warp == 4) {
+        // ================= TMA producer ====================================================================================
+        if (lane == 0) {
+            bar_expect_tx(&bars[BAR_Q], 16384);
+            tma_load_3d(base + SM_Q, &tm_q, 0, q0, bh, &bars[BAR_Q]);
+            for (int i = 0; i < nt && !*abortp; i++) {
+                const int s = i & 1;
+                const int kt0 = q0 - p.W + (t_first + i) * TC_BN;
+                if (i >= 2 && !bar_wait(&bars[BAR_KV_EMPTY + s], ((i >> 1) - 1) & 1)) { *abortp = 1; break; }
+                bar_expect_tx(&bars[BAR_KV_FULL + s], 32768);
+                tma_load_3d(base + SM_K + s * 16384, &tm_k, 0, kt0, bh, &bars[BAR_KV_FULL + s]);
+                tma_load_4d(base + SM_V + s * 16384, &tm_v, 0, kt0, h, b, &bars[BAR_KV_FULL + s]);
+            }
+        }
+    } else if (warp == 5) {
+        // ================= MMA issuer ======================================================================================
+        if (lane == 0) {
+            const uint32_t idesc_s = instr_desc(TC_BN, 0, 1);
+            const uint32_t idesc_pv = instr_desc(TC_D, 1, 1);      // A and B of one MMA must share their 16-bit format: P is bf16 like V
+            bool ok = bar_wait(&bars[BAR_Q], 0);
+            for (int i = 0; i <= nt && ok && !*abortp; i++) {
+                if (i < nt) {
+                    const int s = i & 1;
+                    ok = bar_wait(&bars[BAR_KV_FULL + s], (i >> 1) & 1);
+                    if (ok && i >= 2) ok = bar_wait(&bars[BAR_S_FREE + s], ((i >> 1) - 1) & 1);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t aq = s_u32(base + SM_Q), bk = s_u32(base + SM_K + s * 16384);
+#pragma unroll
+                    for (int k = 0; k < TC_D / 16; k++)
+                        umma(tmem + s * TC_BN, smem_desc(aq + k * 32), smem_desc(bk + k * 32), idesc_s, k > 0);
+                    umma_commit(&bars[BAR_S_FULL + s]);
+                }
+                if (i >= 1) {
+                    const int j = i - 1, bb = j & 1;
+                    ok = bar_wait(&bars[BAR_P_FULL + bb], (j >> 1) & 1);
+                    if (ok && j >= 2) ok = bar_wait(&bars[BAR_PV_FREE + bb], ((j >> 1) - 1) & 1);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t ap = s_u32(base + SM_P + bb * 32768), bv = s_u32(base + SM_V + bb * 16384);
+#pragma unroll
+                    for (int k = 0; k < TC_BN / 16; k++)
+                        umma(tmem + 256 + bb * TC_D, smem_desc(ap + (k >> 2) * 16384 + (k & 3) * 32), smem_desc(bv + k * 2048), idesc_pv, k > 0);
+                    umma_commit(&bars[BAR_PV_FULL + bb]);
+                    umma_commit(&bars[BAR_KV_EMPTY + bb]);
+                }
+            }
+            if (!ok) *abortp = 1;
+        }
+    } else {
+        // ================= softmax + epilogue: one query row per thread ===================================================
+        const int r = warp * 32 + lane;
+        const int qi = q0 + r;
+        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+        float m = -INFINITY, l = 0.0f, a_pend = 0.0f;
+        float O[TC_D];
+#pragma unroll
+        for (int d = 0; d < TC_D; d++) O[d] = 0.0f;
+        bool ok = true;
+        for (int i = 0; i < nt; i++) {
+            const int bb = i & 1;
+            const int t = t_first + i;
+            ok = ok && bar_wait(&bars[BAR_S_FULL + bb], (i >> 1) & 1) && !*abortp;
+            if (!__all_sync(FS_FULL, ok)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t s_addr = lane_base + bb * TC_BN;
+            const bool lower_edge = (t == 0), upper_edge = (t == ntile_total - 1);
+            // pass 1: masked row maximum
+            float mx = -INFINITY;
+#pragma unroll 1
+            for (int c0 = 0; c0 < TC_BN; c0 += 32) {
+                float v[32];
+                tmem_ld32(s_addr + c0, v);
+#pragma unroll
+                for (int c = 0; c < 32; c++) {
+                    const int col = c0 + c;
+                    const bool valid = !(lower_edge && col < r) && !(upper_edge && col > r);
+                    mx = fmaxf(mx, valid ? v[c] : -INFINITY);
+                }
+            }
+            const float m_new = fmaxf(m, mx);
+            const float alpha = (m == -INFINITY) ? 0.0f : exp2f((m - m_new) * p.c2);
+            const float mc = (m_new == -INFINITY) ? 0.0f : m_new * p.c2;
+            // pass 2: probabilities, row sum, bf16 P into the swizzled K-major operand layout
+            float rowsum = 0.0f;
+            unsigned char* prow = base + SM_P + bb * 32768 + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll 1
+            for (int c0 = 0; c0 < TC_BN; c0 += 32) {
+                float v[32];
+                tmem_ld32(s_addr + c0, v);
+                uint32_t pk[16];
+#pragma unroll
+                for (int c = 0; c < 32; c += 2) {
+                    const int col = c0 + c;
+                    const bool v0 = !(lower_edge && col < r) && !(upper_edge && col > r);
+                    const bool v1 = !(lower_edge && col + 1 < r) && !(upper_edge && col + 1 > r);
+                    const float p0 = v0 ? exp2f(v[c] * p.c2 - mc) : 0.0f;
+                    const float p1 = v1 ? exp2f(v[c + 1] * p.c2 - mc) : 0.0f;
+                    pk[c >> 1] = pack_bf2(p0, p1);
+                    // the row sum uses the rounded values the tensor core will multiply
+                    rowsum += bf_lo(pk[c >> 1]) + bf_hi(pk[c >> 1]);
+                }
+#pragma unroll
+                for (int q4 = 0; q4 < 4; q4++) {
+                    const int cc = (c0 >> 3) + q4;                 // 16-byte chunk index within the 128-key row
+                    unsigned char* dst = prow + (cc >> 3) * 16384 + (((cc & 7) ^ (r & 7)) << 4);
+                    *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+                }
+            }
+            tc_fence_before();
+            bar_arrive(&bars[BAR_S_FREE + bb]);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            bar_arrive(&bars[BAR_P_FULL + bb]);
+            l = l * alpha + rowsum;
+            m = m_new;
+            // fold the previous tile's P V into the running output
+            if (i >= 1) {
+                const int j = i - 1, jb = j & 1;
+                ok = bar_wait(&bars[BAR_PV_FULL + jb], (j >> 1) & 1) && !*abortp;
+                if (!__all_sync(FS_FULL, ok)) { ok = false; break; }
+                tc_fence_after();
+#pragma unroll
+                for (int c0 = 0; c0 < TC_D; c0 += 32) {
+                    float v[32];
+                    tmem_ld32(lane_base + 256 + jb * TC_D + c0, v);
+#pragma unroll
+                    for (int c = 0; c < 32; c++) O[c0 + c] = fmaf(O[c0 + c], a_pend, v[c]);
+                }
+                tc_fence_before();
+                bar_arrive(&bars[BAR_PV_FREE + jb]);
+            }
+            a_pend = alpha;
+        }
+        if (ok && nt > 0) {
+            const int j = nt - 1, jb = j & 1;
+            ok = bar_wait(&bars[BAR_PV_FULL + jb], (j >> 1) & 1) && !*abortp;
+            if (__all_sync(FS_FULL, ok)) {
+                tc_fence_after();
+#pragma unroll
+                for (int c0 = 0; c0 < TC_D; c0 += 32) {
+                    float v[32];
+                    tmem_ld32(lane_base + 256 + jb * TC_D + c0, v);
+#pragma unroll
+                    for (int c = 0; c < 32; c++) O[c0 + c] = fmaf(O[c0 + c], a_pend, v[c]);
+                }
+                tc_fence_before();
+            } else {
+                ok = false;
+            }
+        }
+        if (!ok) *abortp = 1;
+        if (ok && qi < p.N) {
+            const float inv = (l > 0.0f) ? 1.0f / l : 0.0f;
+            bf16* op = p.out + ((int64_t)b * p.N + qi) * ((int64_t)p.H * TC_D) + (int64_t)h * TC_D;
+#pragma unroll
+            for (int e = 0; e < TC_D / 8; e++) {
+                uint4 w;
+                w.x = pack_bf2(O[8 * e + 0] * inv, O[8 * e + 1] * inv);
+                w.y = pack_bf2(O[8 * e + 2] * inv, O[8 * e + 3] * inv);
+                w.z = pack_bf2(O[8 * e + 4] * inv, O[8 * e + 5] * inv);
+                w.w = pack_bf2(O[8 * e + 6] * inv, O[8 * e + 7] * inv);
+                reinterpret_cast<uint4*>(op)[e] = w;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0 && abort_s && p.status != nullptr) atomicAdd(p.status, 1);
+    if (warp == 4) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
+    }
+}
+
+}  // namespace
+
+// ---- host side -------------------------------------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
+                                  const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (fn == nullptr) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+static bool make_map(CUtensorMap* m, void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_bytes, const cuuint32_t* box) {
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    EncodeTiledFn fn = encode_fn();
+    if (fn == nullptr) return false;
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, base, dims, strides_bytes, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+size_t fs_window_prefill_tc_workspace(const fsattn_window_prefill_t* a) {
+    return (size_t)2 * a->B * a->H * a->N * TC_D * sizeof(bf16);
+}
+
+bool fs_window_prefill_tc_ok(const fsattn_window_prefill_t* a) {
+    return a->D == TC_D && a->W >= TC_BN && a->W % TC_BN == 0 && a->workspace != nullptr &&
+           a->workspace_bytes >= (int64_t)fs_window_prefill_tc_workspace(a) && ((uintptr_t)a->workspace & 1023) == 0 &&
+           (a->v.sn * 2) % 16 == 0 && (a->v.sh * 2) % 16 == 0 && (a->v.sb * 2) % 16 == 0 && encode_fn() != nullptr;
+}
+
+int fs_window_prefill_tc(const fsattn_window_prefill_t* a, cudaStream_t st) {
+    bf16* qr = (bf16*)a->workspace;
+    bf16* kr = qr + (size_t)a->B * a->H * a->N * TC_D;
+    {
+        const int64_t total = (int64_t)a->B * a->H * a->N * (TC_D / 16);
+        const int64_t blocks = (total + 255) / 256;
+        FS_REQUIRE(blocks < (1ll << 31), "window_prefill: too many rows");
+        rope_qk_kernel<<<(unsigned)blocks, 256, 0, st>>>(*a, qr, kr);
+        const int rc = fs_check_launch("rope_qk");
+        if (rc != FSATTN_OK) return rc;
+    }
+    CUtensorMap tq, tk, tv;
+    const cuuint64_t BH = (cuuint64_t)a->B * a->H;
+    {
+        const cuuint64_t dims[3] = {TC_D, (cuuint64_t)a->N, BH};
+        const cuuint64_t strides[2] = {TC_D * 2, (cuuint64_t)a->N * TC_D * 2};
+        const cuuint32_t box[3] = {TC_D, TC_BM, 1};
+        FS_REQUIRE(make_map(&tq, qr, 3, dims, strides, box) && make_map(&tk, kr, 3, dims, strides, box),
+                   "window_prefill: cuTensorMapEncodeTiled failed for the rotated Q/K workspace");
+    }
+    {
+        const cuuint64_t dims[4] = {TC_D, (cuuint64_t)a->N, (cuuint64_t)a->H, (cuuint64_t)a->B};
+        const cuuint64_t strides[3] = {(cuuint64_t)a->v.sn * 2, (cuuint64_t)a->v.sh * 2, (cuuint64_t)(a->B > 1 ? a->v.sb : a->v.sn * a->N) * 2};
+        const cuuint32_t box[4] = {TC_D, TC_BN, 1, 1};
+        FS_REQUIRE(make_map(&tv, const_cast<void*>(a->v.ptr), 4, dims, strides, box), "window_prefill: cuTensorMapEncodeTiled failed for V");
+    }
+    static bool opted[16] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int smem = SM_TOTAL + 1024;
+    if (dev >= 0 && dev < 16 && !opted[dev]) {
+        if (cudaFuncSetAttribute(window_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+            (void)cudaGetLastError();
+            fs_set_error("window_prefill: cannot opt in to %d bytes of shared memory", smem);
+            return FSATTN_ELAUNCH;
+        }
+        opted[dev] = true;
+    }
+    TcParams p;
+    p.N = a->N; p.W = a->W; p.H = a->H;
+    p.c2 = a->scale * 1.4426950408889634f;
+    p.out = (bf16*)a->out;
+    p.status = a->status;
+    dim3 grid((a->N + TC_BM - 1) / TC_BM, a->B * a->H);
+    window_tc_kernel<<<grid, TC_THREADS, smem, st>>>(tq, tk, tv, p);
+    return fs_check_launch("window_prefill_tc");
 }

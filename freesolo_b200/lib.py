@@ -63,7 +63,9 @@ class WindowPrefill(C.Structure):
                 ("B", i32), ("H", i32), ("D", i32), ("N", i32), ("W", i32), ("pos0", i32),
                 ("scale", f32),
                 ("out", vp),
-                ("impl", i32)]
+                ("impl", i32),
+                ("workspace", vp), ("workspace_bytes", i64),
+                ("status", vp)]
 
 
 class ReadoutCombine(C.Structure):

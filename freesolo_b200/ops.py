@@ -162,7 +162,7 @@ def fsl_select(Q, kbar, ceil, topp, lam, sigma, *, N: int, ncell: int, Bq: int, 
     return (sel, margin) if want_margin else sel
 
 
-def window_prefill(Q, K, V, cos, sin, W: int, scale: float, pos0: int = 0, impl: int = 0, out=None):
+def window_prefill(Q, K, V, cos, sin, W: int, scale: float, pos0: int = 0, impl: int = 0, out=None, status=None):
     """Causal band attention with RoPE on Q and K. Returns (B,N,H*D) bf16 (W_o's input layout)."""
     _need_cuda(Q, K, V, cos, sin)
     B, H, N, D = Q.shape
@@ -178,7 +178,18 @@ def window_prefill(Q, K, V, cos, sin, W: int, scale: float, pos0: int = 0, impl:
     a.scale = float(scale)
     a.out = out.data_ptr()
     a.impl = int(impl)
+    ws = None
+    if impl == 0 and D == 64 and W >= 128 and W % 128 == 0:
+        # scratch of the tensor-core kernel (rotated Q and K); torch's allocator returns 512-byte aligned blocks, so
+        # over-allocate and align to 1024
+        nbytes = 2 * B * H * N * D * 2
+        ws = torch.empty(nbytes + 1024, dtype=torch.uint8, device=Q.device)
+        off = (-ws.data_ptr()) % 1024
+        a.workspace, a.workspace_bytes = ws.data_ptr() + off, nbytes
+    a.status = _p(status)
     L.call("fsattn_window_prefill", a, _stream(Q))
+    if ws is not None:
+        ws.record_stream(torch.cuda.current_stream(Q.device))
     return out
 
 

@@ -132,6 +132,10 @@ typedef struct {
     float scale;
     void* out; /* (B,N,H*D) bf16 contiguous */
     int32_t impl; /* 0 = default (tensor-core kernel when the shape allows), 1 = force the CUDA-core kernel */
+    /* scratch for the tensor-core kernel: the rotated Q and K, 2*B*H*N*D*2 bytes, 1024-byte aligned (caller-owned; the
+     * kernel is used when head_dim = 64, W is a multiple of 128 and this is large enough, else the CUDA-core kernel runs) */
+    void* workspace; int64_t workspace_bytes;
+    int32_t* status; /* optional int32: incremented when a bounded wait inside the tensor-core kernel ran out */
 } fsattn_window_prefill_t;
 FSATTN_API int fsattn_window_prefill(const fsattn_window_prefill_t* a, fsattn_stream_t stream);
 

@@ -303,12 +303,14 @@ def apply_rope(x, cos, sin):
 
 
 def window_attention(Q, K, V, cos, sin, W: int, scale: float, q_pos0: int = 0, k_pos0: int = 0,
-                     act_dtype=None):
+                     act_dtype=None, p_dtype=None):
     """Causal sliding-window softmax attention with RoPE on Q and K only; src/utils/local_attention.py:317-353
     (generic loop, uniform window) and src/fsattn/attention.py:225-231. Query at absolute position p attends keys
     max(0, p - W) <= j <= p. The rotated Q and K are rounded to act_dtype (the dtype they are stored in before the
     score product) when it is given. Q (B,H,Nq,D) at positions q_pos0.., K/V (B,H,Nk,D) at positions k_pos0...
-    Returns fp32 (B,H,Nq,D)."""
+    p_dtype: when given, the softmax weights are rounded to it before they multiply V, as the reference's low-precision
+    path does (`w = torch.softmax(scores, dim=-1).to(Vw.dtype)`, src/fsattn/attention.py:1155; SDPA's bf16 kernels do the
+    same with their probabilities). Returns fp32 (B,H,Nq,D)."""
     B, H, Nq, D = Q.shape
     Nk = K.shape[2]
     cf, sf = cos.float(), sin.float()
@@ -330,7 +332,10 @@ def window_attention(Q, K, V, cos, sin, W: int, scale: float, q_pos0: int = 0, k
         kj = torch.arange(j0, j1)[None, :]
         band = (qi - kj >= 0) & (qi - kj <= W)
         sc = sc.masked_fill(~band, float("-inf"))
-        out[:, :, c0:c1] = torch.einsum("bhqk,bhkd->bhqd", torch.softmax(sc, -1), Vf[:, :, j0 - k_pos0:j1 - k_pos0])
+        wts = torch.softmax(sc, -1)
+        if p_dtype is not None:
+            wts = wts.to(p_dtype).float()
+        out[:, :, c0:c1] = torch.einsum("bhqk,bhkd->bhqd", wts, Vf[:, :, j0 - k_pos0:j1 - k_pos0])
     return out
 
 

@@ -177,13 +177,18 @@ def test_window_prefill(dev, kind, impl):
     g, Q, K, V = _g(kind)
     N = int(g["N"])
     cos, sin = fsl.rope_tables(64, 4096, torch.bfloat16, orig_len=4096)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
     out = ops.window_prefill(Q[:, :, :N].to(dev), K[:, :, :N].to(dev), V[:, :, :N].to(dev), cos.to(dev), sin.to(dev), 512,
-                             0.125, impl=impl)
+                             0.125, impl=impl, status=status)
+    assert int(status.item()) == 0, "a bounded wait inside the tensor-core kernel ran out"
     B, H = Q.shape[:2]
     got = out.view(B, N, H, 64).transpose(1, 2)
     want = fsl.window_attention(Q[:, :, :N].float(), K[:, :, :N].float(), V[:, :, :N].float(), cos, sin, 512, 0.125,
                                 act_dtype=torch.bfloat16)
-    _close(got, want.to(torch.bfloat16), f"{kind} window (impl {impl}) vs oracle")
+    # The tensor-core kernel multiplies bf16 probabilities with V (as the reference's bf16 paths do: SDPA, and
+    # `softmax(...).to(V.dtype)` in its decode step). Rounding the probabilities to bf16 alone moves the output by
+    # mean-rel 1.4e-3 from exact probabilities (CPU emulation), so that path's bar against the exact oracle is 2e-3.
+    _close(got, want.to(torch.bfloat16), f"{kind} window (impl {impl}) vs oracle", mean_rel=2e-3 if impl == 0 else MEAN_REL)
     _close(got, torch.from_numpy(g["window_prefill"]), f"{kind} window (impl {impl}) vs reference fp32", mean_rel=6e-3)
 
 
@@ -194,10 +199,16 @@ def test_window_prefill_shapes(dev, N, W, pos0):
     g = torch.Generator().manual_seed(N)
     Q, K, V = (torch.randn(B, H, N, D, generator=g).to(torch.bfloat16) for _ in range(3))
     cos, sin = fsl.rope_tables(D, 2048, torch.bfloat16)
-    want = fsl.window_attention(Q.float(), K.float(), V.float(), cos, sin, W, 0.125, q_pos0=pos0, k_pos0=pos0, act_dtype=torch.bfloat16)
     for impl in (0, 1):
-        out = ops.window_prefill(Q.to(dev), K.to(dev), V.to(dev), cos.to(dev), sin.to(dev), W, 0.125, pos0=pos0, impl=impl)
-        _close(out.view(B, N, H, D).transpose(1, 2), want.to(torch.bfloat16), f"window N={N} W={W} pos0={pos0} impl={impl}")
+        want = fsl.window_attention(Q.float(), K.float(), V.float(), cos, sin, W, 0.125, q_pos0=pos0, k_pos0=pos0,
+                                    act_dtype=torch.bfloat16)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        out = ops.window_prefill(Q.to(dev), K.to(dev), V.to(dev), cos.to(dev), sin.to(dev), W, 0.125, pos0=pos0, impl=impl,
+                                 status=status)
+        assert int(status.item()) == 0, "a bounded wait inside the tensor-core kernel ran out"
+        tc = impl == 0 and W >= 128 and W % 128 == 0          # shapes the tensor-core kernel takes (bf16 probabilities)
+        _close(out.view(B, N, H, D).transpose(1, 2), want.to(torch.bfloat16), f"window N={N} W={W} pos0={pos0} impl={impl}",
+               mean_rel=2e-3 if tc else MEAN_REL)
 
 
 @pytest.mark.parametrize("kind", KINDS)
