@@ -185,6 +185,10 @@ def run_ours(args):
     B = args.batch
     ids = torch.randint(0, model.vocab_size, (B, ctx), generator=torch.Generator().manual_seed(4321 + ctx + rank))
     total = Wm + 2 * K + 32
+    # one short untimed prefill first: library handles, kernel attributes and allocator pools are initialised there
+    warm = GraphedDecoder(model, ids[:, :min(ctx, 2048)], Lmax=min(ctx, 2048) + 64, device=dev, kv=args.kv)
+    warm.prefill()
+    del warm
     gd = GraphedDecoder(model, ids, Lmax=ctx + total, device=dev, kv=args.kv)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -272,7 +276,7 @@ def run_ours(args):
                      "how": "launched alone with an L2 flush before every launch, CUDA events on the launching stream"},
         "step_roofline": {"step_bytes": step_bytes, "achieved_gbs": step_bytes / (ms / K * 1e-3) / 1e9,
                           "frac": step_bytes / (ms / K * 1e-3) / 1e9 / peak, "peak_kind": peak_kind},
-        "prefill": {"ktok_s": B * ctx / prefill_ms, "ms": prefill_ms, "note": "single cold run incl. KV store fill, untimed for the headline"},
+        "prefill": {"ktok_s": B * ctx / prefill_ms, "ms": prefill_ms, "note": "one run after a 2048-token warm-up prefill, incl. KV store fill and last-token logits; untimed for the headline"},
         "kv_bytes_per_layer": gd.kv_bytes() // nL, "kv_faults": list(faults),
         "peak_mem_gib": torch.cuda.max_memory_allocated() / 2 ** 30,
     }
