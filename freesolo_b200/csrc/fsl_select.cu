@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(128) fsl_select_kernel(const fsattn_fsl_select
     const int blk_start = blk * a.Bq;
     const float* kbar = a.kbar + b * a.kbar_sb + h * a.kbar_sh;
     const float* ceil = a.ceil + b * a.ceil_sb + h * a.ceil_sh;
-    const int32_t* topp = a.topp + ((int64_t)bh * a.nb + blk) * a.P;
+    const int32_t* topp = a.topp + ((int64_t)bh * (a.topp_nb > 0 ? a.topp_nb : a.nb) + blk) * a.P;
 
     // candidate slots
     for (int t = tid; t < C; t += blockDim.x) {
@@ -188,7 +188,7 @@ static int launch_select(const fsattn_fsl_select_t* a, cudaStream_t st) {
 extern "C" int fsattn_fsl_select(const fsattn_fsl_select_t* a, fsattn_stream_t stream) {
     FS_REQUIRE(a != nullptr && a->q.ptr && a->kbar && a->ceil && a->topp && a->lam && a->sigma && a->sel,
                "fsl_select: null pointer");
-    FS_REQUIRE(a->B > 0 && a->H > 0 && a->N > 0 && a->nb > 0 && a->ncell >= 0, "fsl_select: bad sizes");
+    FS_REQUIRE(a->B > 0 && a->H > 0 && a->N > 0 && a->nb > 0 && a->ncell >= 0 && (a->topp_nb == 0 || a->topp_nb >= a->nb), "fsl_select: bad sizes");
     FS_REQUIRE(a->Bq >= 1 && a->Bq <= 128, "fsl_select: query block %d not in [1,128]", a->Bq);
     FS_REQUIRE(a->P >= 1 && a->Wc >= 0 && a->P + a->Wc <= FSATTN_MAX_POOL + 8, "fsl_select: pool %d + %d too large", a->P, a->Wc);
     FS_REQUIRE(a->kk >= 1 && a->kk <= FSATTN_MAX_KK, "fsl_select: kk %d not in [1,%d]", a->kk, FSATTN_MAX_KK);

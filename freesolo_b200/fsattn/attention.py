@@ -275,7 +275,12 @@ class FSAttn(nn.Module):
             sel = torch.full((B, H, nb * Bq, kk), -1, dtype=torch.int32, device=Q.device)
             margin = None
         else:
-            topp = ops.fsl_prefix_topp(ceil, ncell, Bq, nb, min(P, M))
+            st = cache.state
+            topp = getattr(st, "prefill_topp", None) if st is not None else None
+            if topp is None or topp.shape[2] != min(P, M) or topp.shape[1] < nb or Bq != self._cell_block:
+                topp = ops.fsl_prefix_topp(ceil, ncell, Bq, nb, min(P, M))
+            if st is not None:
+                st.prefill_topp = None
             keep = os.environ.get("FSATTN_KEEP_SEL", "0") == "1"
             res = ops.fsl_select(Q, kbar, ceil, topp, lam, sigma, N=N, ncell=ncell, Bq=Bq, nb=nb, P=min(P, M), Wc=Wc,
                                  kk=kk, scale=self.scale, want_margin=keep)

@@ -54,7 +54,8 @@ class FslSelect(C.Structure):
                 ("B", i32), ("H", i32), ("D", i32), ("N", i32), ("ncell", i32), ("Bq", i32), ("nb", i32),
                 ("P", i32), ("Wc", i32), ("kk", i32),
                 ("scale", f32),
-                ("sel", vp), ("margin", vp)]
+                ("sel", vp), ("margin", vp),
+                ("topp_nb", i32)]
 
 
 class WindowPrefill(C.Structure):

@@ -158,6 +158,8 @@ def fsl_select(Q, kbar, ceil, topp, lam, sigma, *, N: int, ncell: int, Bq: int, 
     a.B, a.H, a.D, a.N, a.ncell, a.Bq, a.nb, a.P, a.Wc, a.kk = B, H, D, N, ncell, Bq, nb, P, Wc, kk
     a.scale = float(scale)
     a.sel, a.margin = sel.data_ptr(), _p(margin)
+    assert topp.is_contiguous() and topp.shape[0] == B * H and topp.shape[1] >= nb and topp.shape[2] == P
+    a.topp_nb = topp.shape[1]
     L.call("fsattn_fsl_select", a, _stream(Q))
     return (sel, margin) if want_margin else sel
 
@@ -269,6 +271,7 @@ class FslDecodeState:
         self.pool_meta = torch.full((B, H, P + Wc, 4), -1, dtype=torch.int32, **z)
         self.pool_blk = torch.full((B, H), -1, dtype=torch.int32, **z)
         self.status = torch.zeros(L.ST_WORDS, dtype=torch.int32, **z)
+        self.prefill_topp = None
 
     def nbytes(self) -> int:
         ts = (self.kbuf, self.vbuf, self.kq, self.vq, self.ks, self.vs, self.khot, self.vhot, self.slot_of, self.cell_in,
@@ -316,6 +319,7 @@ class FslDecodeState:
             nb = blk // self.Bq + 1
             topp = fsl_prefix_topp(ceil, ncell, self.Bq, nb, self.P)
             self.top_idx.copy_(topp[:, nb - 1].view(self.B, self.H, self.P))
+            self.prefill_topp = topp        # per-block lists of the prompt: the layer's own selection reuses them
         if self.mode == "bf16":
             self.kbuf[:, :, :N].copy_(K[:, :, :N])
             self.vbuf[:, :, :N].copy_(V[:, :, :N])

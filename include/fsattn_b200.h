@@ -117,6 +117,7 @@ typedef struct {
     int32_t B, H, D, N, ncell, Bq, nb, P, Wc, kk;
     float scale;
     int32_t* sel; float* margin;
+    int32_t topp_nb; /* blocks per head in the topp buffer when it holds more than nb (0: nb) */
 } fsattn_fsl_select_t;
 FSATTN_API int fsattn_fsl_select(const fsattn_fsl_select_t* a, fsattn_stream_t stream);
 
