@@ -454,3 +454,61 @@ int fs_window_prefill_tc(const fsattn_window_prefill_t* a, cudaStream_t st) {
     window_tc_kernel<<<grid, TC_THREADS, smem, st>>>(tq, tk, tv, p);
     return fs_check_launch("window_prefill_tc");
 }
+
+// ---- allocation-free variant ------------------------------------------------------------------------------------------------
+// Some hosts of this library may not create device memory at the moment they need a prefill: a serving process whose
+// memory plan was fixed at start-up and hands out no further blocks, a plugin that runs inside another framework's step and
+// is not allowed to call that framework's (or CUDA's) allocator from there, a caller on a latency path where cudaMalloc's
+// implicit device synchronisation is unacceptable. For them the tensor-core window kernel is offered with its scratch (the
+// rotated Q and K) in a fixed array that is part of the library image: every GPU that loads the library holds these
+// FSATTN_WINDOW_STATIC_BYTES until the process exits, whether or not the entry point is ever called.
+//
+// The array's name below is only a host-side handle. The device address is looked up once per device (with that device
+// current) by cudaGetSymbolAddress at the first call on that device, so that first call should happen before any stream capture.
+// Every call uses the same array and leaves its last contents there; nothing in it has to start at zero (pass 0 rewrites
+// every row pass 1 reads), but two calls that overlap on the GPU (different streams, or a graph replayed concurrently) would
+// race on it.
+static __device__ __align__(256) unsigned char g_window_static_scratch[FSATTN_WINDOW_STATIC_BYTES];
+
+extern "C" int fsattn_window_prefill_static(const fsattn_window_prefill_t* a, fsattn_stream_t stream) {
+    FS_REQUIRE(a != nullptr && a->q.ptr && a->k.ptr && a->v.ptr && a->cos && a->sin && a->out, "window_prefill_static: null pointer");
+    FS_REQUIRE(a->B > 0 && a->H > 0 && a->N > 0 && a->pos0 >= 0, "window_prefill_static: bad sizes");
+    FS_UNSUPPORTED(a->D != TC_D || a->W < TC_BN || a->W % TC_BN != 0,
+                   "window_prefill_static: only head_dim 64 and windows that are multiples of 128 (got D=%d, W=%d)", a->D, a->W);
+    const fsattn_bhnd_t* t[3] = {&a->q, &a->k, &a->v};
+    for (int i = 0; i < 3; i++)
+        FS_REQUIRE(((uintptr_t)t[i]->ptr & 15) == 0 && t[i]->sn % 8 == 0 && t[i]->sh % 8 == 0 && t[i]->sb % 8 == 0,
+                   "window_prefill_static: Q, K and V rows must be 16-byte aligned");
+    FS_REQUIRE(((uintptr_t)a->cos & 15) == 0 && ((uintptr_t)a->sin & 15) == 0 && ((uintptr_t)a->out & 15) == 0,
+               "window_prefill_static: tables and output must be 16-byte aligned");
+    const size_t need = fs_window_prefill_tc_workspace(a);
+    if (need > (size_t)FSATTN_WINDOW_STATIC_BYTES) {
+        fs_set_error("window_prefill_static: B*H*N = %lld rows need %zu bytes of scratch, the built-in array holds %d (B*H*N <= %d); "
+                     "use fsattn_window_prefill with a caller-owned workspace", (long long)a->B * a->H * a->N, need,
+                     FSATTN_WINDOW_STATIC_BYTES, FSATTN_WINDOW_STATIC_BYTES / (2 * TC_D * 2));
+        return FSATTN_EINVAL;
+    }
+    FS_REQUIRE(encode_fn() != nullptr, "window_prefill_static: the driver does not export cuTensorMapEncodeTiled");
+    // one-time set-up per device: the array's device address on the current device
+    static void* dev_ptr[64] = {nullptr};
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        (void)cudaGetLastError();
+        fs_set_error("window_prefill_static: no current CUDA device");
+        return FSATTN_ELAUNCH;
+    }
+    if (dev_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_window_static_scratch);
+        if (e != cudaSuccess || p == nullptr) {
+            (void)cudaGetLastError();
+            fs_set_error("window_prefill_static: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+            return FSATTN_ELAUNCH;
+        }
+        dev_ptr[dev] = p;
+    }
+    fsattn_window_prefill_t b = *a;
+    b.workspace = dev_ptr[dev];
+    b.workspace_bytes = FSATTN_WINDOW_STATIC_BYTES;
+    return fs_window_prefill_tc(&b, (cudaStream_t)stream);
+}

@@ -15,6 +15,7 @@ OK, EINVAL, EUNSUPPORTED, ELAUNCH = 0, -1, -2, -3
 CELL = 32
 MAX_POOL = 128
 MAX_KK = 8
+WINDOW_STATIC_BYTES = 32 * 1024 * 1024
 ST_SLOT_OVERFLOW, ST_POOL_NO_SLOT, ST_BAD_INDEX, ST_WORDS = 0, 1, 2, 4
 
 i32, i64, f32, vp = C.c_int32, C.c_int64, C.c_float, C.c_void_p
@@ -134,6 +135,7 @@ ENTRY_POINTS = {
     "fsattn_fsl_prefix_topp": FslTopp,
     "fsattn_fsl_select": FslSelect,
     "fsattn_window_prefill": WindowPrefill,
+    "fsattn_window_prefill_static": WindowPrefill,
     "fsattn_readout_combine": ReadoutCombine,
     "fsattn_fsl_decode_step": FslDecode,
     "fsattn_slot_prefill": SlotPrefill,

@@ -195,6 +195,30 @@ def window_prefill(Q, K, V, cos, sin, W: int, scale: float, pos0: int = 0, impl:
     return out
 
 
+def window_prefill_static(Q, K, V, cos, sin, W: int, scale: float, pos0: int = 0, out=None, status=None):
+    """window_prefill through the allocation-free entry point: the kernel's scratch is a fixed array inside the library, so
+    nothing is allocated for it here. For callers that may not create device memory at call time. Only head_dim 64, W a
+    multiple of 128 and B*H*N <= 131072; larger or other shapes raise. `out` must be passed by such callers (when it is
+    None this convenience wrapper allocates the output, which is not scratch). Calls that overlap on the GPU race on the
+    shared array; the first call on a device must come before any stream capture."""
+    _need_cuda(Q, K, V, cos, sin)
+    B, H, N, D = Q.shape
+    if out is None:
+        out = torch.empty(B, N, H * D, dtype=torch.bfloat16, device=Q.device)
+    assert cos.dtype == torch.bfloat16 and sin.dtype == torch.bfloat16 and cos.is_contiguous() and sin.is_contiguous()
+    assert cos.shape[1] == D and cos.shape[0] >= pos0 + N, "rope table too short"
+    assert out.is_contiguous()
+    a = L.WindowPrefill()
+    a.q, a.k, a.v = _bhnd(Q, "Q"), _bhnd(K, "K"), _bhnd(V, "V")
+    a.cos, a.sin = cos.data_ptr(), sin.data_ptr()
+    a.B, a.H, a.D, a.N, a.W, a.pos0 = B, H, D, N, int(W), int(pos0)
+    a.scale = float(scale)
+    a.out = out.data_ptr()
+    a.status = _p(status)
+    L.call("fsattn_window_prefill_static", a, _stream(Q))
+    return out
+
+
 def readout_combine(Q, K, V, sel, sr, norm_w, lrs, eps: float, *, scale: float, Bq: int, n_kv: int | None = None,
                     q_pos0: int = 0, out=None):
     """y (B,N,H*D) bf16 = bf16(sr + lrs[h] * lr_norm(bf16(readout of the selected cells))). sr (B,N,H*D) bf16 or None

@@ -140,6 +140,18 @@ typedef struct {
 } fsattn_window_prefill_t;
 FSATTN_API int fsattn_window_prefill(const fsattn_window_prefill_t* a, fsattn_stream_t stream);
 
+/* The same tensor-core window attention for callers that cannot obtain device memory at call time (a process with a frozen
+ * memory plan, a plugin that must not touch its host framework's allocator, a latency path that cannot afford cudaMalloc's
+ * device synchronisation). It has no counterpart in the reference, which allocates through PyTorch wherever it likes.
+ * The scratch for the rotated Q and K is a fixed array inside the library (FSATTN_WINDOW_STATIC_BYTES on every GPU that loads
+ * it, until the process exits); a->workspace and a->workspace_bytes are ignored and nothing is allocated or freed.
+ * Limits: head_dim 64, W a multiple of 128, and 2*B*H*N*64*2 bytes <= FSATTN_WINDOW_STATIC_BYTES, i.e. B*H*N <= 131072 rows;
+ * anything else is rejected with FSATTN_EINVAL / FSATTN_EUNSUPPORTED and a message. The first call on a device looks up the
+ * array's device address: make that call before capturing a stream. All calls share the array, so calls that overlap on
+ * the GPU race on it; consecutive calls on one stream are safe and need no clearing in between. */
+#define FSATTN_WINDOW_STATIC_BYTES (32 * 1024 * 1024)
+FSATTN_API int fsattn_window_prefill_static(const fsattn_window_prefill_t* a, fsattn_stream_t stream);
+
 /* ---- fused readout + combine, prefill ---------------------------------------------------------------------------------
  * Replaces FSAttn._cell_fused_lr / readout_triton.readout_combine (src/fsattn/attention.py:344-361,
  * src/fsattn/readout_triton.py:34-159) and indexed_cell_attention (src/fsattn/cell_select_triton.py:97-282):
