@@ -12,6 +12,8 @@ Fixtures:
   fsl_<kind>.npz   one FS-L layer driven at the Q/K/V level (projections replaced by fixed tensors, W_o = identity):
                    cell statistics, int8 codes, prefill selections (deterministic tie rule), prefill W_o input,
                    window branch alone, and a run of decode steps that crosses cell and block boundaries.
+  fsb_<kind>.npz   one FS-B layer (serve configuration, two forests) driven the same way: the reference's forest
+                   tables, spines and beam cells of the prefill stage, prefill and decode selections, outputs.
   fsl_config1.npz  BASELINE config 1: FSAttn(d_model=1024, 16 heads) with its own seeded projections, 4096-token
                    prefill + 1 decode step, fp32; selections, margins and a strided sample of the outputs.
 """
@@ -208,6 +210,124 @@ def gen_config1():
     print("wrote fsl_config1.npz")
 
 
+def gen_fsb(kind: str, B=1, H=2, D=64, N=2000, T=140, seed=23, q_main=0.3, q_union=0.7):
+    """One FS-B layer (the serve configuration: fixed policy, width 16, bound score with radius coefficient 8, token
+    LSE re-rank to 4, second beam over a second forest) at the Q/K/V level: prefill of N tokens, then T decode steps
+    that cross a 128-token block boundary. The two admission thresholds are per-head quantiles of the ceilings.
+    Stores the reference's forest tables (main forest), the spines and beam cells of every (row, block), the
+    selections and the layer outputs."""
+    from kv_cache import FSKVCache
+    from bench_efficiency import serve_kwargs
+    from src.fsattn import FSAttn, fsb_tree
+    Q, K, V = make_inputs(kind, B, H, N + T, D, seed)
+    flat = [t.transpose(1, 2).reshape(B, N + T, H * D).contiguous() for t in (Q, K, V)]
+    out = {"kind": kind, "B": B, "H": H, "D": D, "N": N, "T": T,
+           "Q": _bf16_bits(Q), "K": _bf16_bits(K), "V": _bf16_bits(V)}
+    x = torch.zeros(B, N + T, H * D)
+    s = 32
+    ncell = N // s
+    ceil0 = K[:, :, :ncell * s].reshape(B, H, ncell, s, D).norm(dim=-1).amax(-1)
+    tau = torch.quantile(ceil0[0], q_main, dim=-1)
+    tau_u = torch.quantile(ceil0[0], q_union, dim=-1)
+    rec = {"beam": [], "spines": [], "forest": []}
+
+    def run(fused, record):
+        kw = serve_kwargs("fsb", 0.5)
+        kw.update(fs_fused_attn=1 if fused else 0)
+        a = FSAttn(d_model=H * D, n_heads=H, causal=True, bias=False, max_seq_len=4096, **kw).eval()
+        g = torch.Generator().manual_seed(seed + 1)
+        with torch.no_grad():
+            a.sel_scale.copy_(0.5 + torch.rand(H, generator=g) * 2)
+            a.log_sigma.copy_(torch.log(1.0 + torch.rand(H, generator=g) * 40))
+            a.long_range_scale.copy_((0.05 + torch.rand(H, generator=g)).view(H, 1, 1))
+            a.lr_norm.scale.copy_(0.5 + torch.rand(D, generator=g))
+            a.W_o.weight.copy_(torch.eye(H * D))
+            a.fsb_tau.copy_(tau)
+            a.fsb_tau_union.copy_(tau_u)
+        a.W_q, a.W_k, a.W_v = _Fixed(flat[0]), _Fixed(flat[1]), _Fixed(flat[2])
+        sels = []
+        if fused:
+            def grab(Qx, Kx, Vx, sel, s_, Bq, bias=None, q_pos=0):
+                sels.append(sel.clone())
+                return torch.zeros_like(Qx)
+            a._cell_fused_lr = grab
+        c = FSKVCache(a)
+        ys, dsel = [], []
+        orig = (fsb_tree._forest_beam, fsb_tree.build_spines, fsb_tree.build_forest)
+        if record:
+            def beam(*args, **kws):
+                r = orig[0](*args, **kws)
+                rec["beam"].append((r[0].clone(), r[1].clone()))
+                return r
+
+            def spines(F, m_b, t_idx, out=None):
+                r = orig[1](F, m_b, t_idx, out=out)
+                rec["spines"].append({k_: v_.clone() for k_, v_ in r.items()})
+                return r
+
+            def forest(*args, **kws):
+                r = orig[2](*args, **kws)
+                rec["forest"].append(r)
+                return r
+            fsb_tree._forest_beam, fsb_tree.build_spines, fsb_tree.build_forest = beam, spines, forest
+        try:
+            with torch.no_grad():
+                ys.append(a(x[:, :N], cache=c))
+        finally:
+            fsb_tree._forest_beam, fsb_tree.build_spines, fsb_tree.build_forest = orig
+        with torch.no_grad():
+            for t in range(T):
+                ys.append(a(x[:, N + t:N + t + 1], cache=c))
+                fc = getattr(c, "_fsb_forest", None)
+                ls = getattr(fc, "_last_sel", None) if fc is not None else None
+                dsel.append(None if ls is None else ls.clone().reshape(B, H, -1))
+        return a, ys, sels, dsel, c
+
+    a, ys, _, dsel, c = run(False, record=True)
+    out["lam"] = a.sel_scale.detach().numpy()
+    out["sigma"] = a.sigma.detach().numpy()
+    out["lrs"] = a.long_range_scale.detach().reshape(H).numpy()
+    out["norm_w"] = a.lr_norm.scale.detach().numpy()
+    out["eps"] = np.float32(a.lr_norm.eps)
+    out["tau"] = tau.numpy()
+    out["tau_u"] = tau_u.numpy()
+    out["y_prefill"] = ys[0].numpy()
+    out["y_decode"] = torch.cat(ys[1:], dim=1).numpy()
+    sd = np.full((T, B, H, 4), -1, np.int32)
+    for t, s_ in enumerate(dsel):
+        if s_ is not None:
+            sd[t] = s_.numpy()
+    out["sel_decode"] = sd
+    _, _, sels, _, _ = run(True, record=False)
+    out["sel_prefill"] = sels[0][:, :, :N].numpy().astype(np.int32)
+    # the recorded stage: forests [main, second], spines [main, second], beams [main, second]
+    assert len(rec["forest"]) == 2 and len(rec["spines"]) == 2 and len(rec["beam"]) == 2, \
+        [len(v) for v in rec.values()]
+    for tag, F in zip(("f", "fu"), rec["forest"]):
+        out[tag + "_node"] = F["node"].numpy()
+        out[tag + "_leaf"] = F["leaf"].numpy().astype(np.int32)
+        out[tag + "_adm"] = F["adm"].numpy().astype(np.int32)
+        out[tag + "_mtot"] = F["m_tot"].numpy().astype(np.int32)
+        ks = sorted(F["bases"])
+        out[tag + "_ks"] = np.array(ks, np.int32)
+        out[tag + "_bases"] = np.array([F["bases"][k] for k in ks], np.int32)
+        out[tag + "_leafbases"] = np.array([F["leafbases"][k] for k in ks], np.int32)
+        out[tag + "_Kmax"] = np.int32(F["Kmax"])
+    for tag, SP in zip(("sp", "spu"), rec["spines"]):
+        out[tag + "_node"] = SP["node"].numpy()
+        out[tag + "_root"] = SP["root"].numpy().astype(np.int32)
+        out[tag + "_height"] = SP["height"].numpy().astype(np.int32)
+        out[tag + "_mb"] = SP["m_b"].numpy().astype(np.int32)
+        out[tag + "_tidx"] = SP["t_idx"].numpy().astype(np.int32)
+    for tag, (cells, nv) in zip(("beam", "beamu"), rec["beam"]):
+        out[tag + "_cells"] = cells.numpy().astype(np.int32)
+        out[tag + "_nvis"] = nv.numpy().astype(np.int32)
+    out["kbar"] = c._kbar.numpy() if hasattr(c, "_kbar") else np.zeros(0)
+    out["ceil"] = c._ceil.numpy() if hasattr(c, "_ceil") else np.zeros(0)
+    np.savez_compressed(os.path.join(HERE, f"fsb_{kind}.npz"), **out)
+    print("wrote", f"fsb_{kind}.npz", {k_: v_.shape for k_, v_ in out.items() if hasattr(v_, "shape") and v_.ndim})
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -223,6 +343,8 @@ def main():
         "fsl_periodic": lambda: gen_fsl("periodic", N=640, T=8, seed=13),
         "fsl_lowprec": lambda: gen_fsl("lowprec", N=640, T=8, seed=17),
         "fsl_config1": gen_config1,
+        "fsb_randn": lambda: gen_fsb("randn"),
+        "fsb_vocab": lambda: gen_fsb("vocab", N=1500, T=40, seed=29),
     }
     for name, fn in jobs.items():
         if not only or name in only:
