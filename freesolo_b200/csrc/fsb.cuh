@@ -1,0 +1,73 @@
+// FS-B shared device helpers: forest arena indexing and the fixed-order ("halving") reductions every FS-B kernel uses.
+#pragma once
+#include "common.cuh"
+
+#define FSB_SMALL_K 5          // chunks of up to 2^5 cells are built in shared memory by the small-chunk kernel
+#define FSB_MAX_MCAP 8192      // largest supported cell capacity per row (262 144 tokens)
+#define FSB_AUX 4              // floats per node in node_aux
+#define FSB_ROOT_PAD 4         // floats after the D mean words of a root32 row (radius + 3 pad)
+
+__host__ __device__ __forceinline__ int fsb_log2(int x) {
+    int l = 0;
+    while ((1 << l) < x) ++l;
+    return l;
+}
+// first node id of the chunks of height k inside a row's arena
+__host__ __device__ __forceinline__ int64_t fsb_nbase(int k, int m_cap) {
+    return (int64_t)k * m_cap - m_cap + (m_cap >> k);
+}
+__host__ __device__ __forceinline__ int64_t fsb_root_node(int k, int j, int m_cap) {
+    return fsb_nbase(k, m_cap) + (int64_t)(j >> 1) * ((2 << k) - 1);
+}
+__host__ __device__ __forceinline__ int fsb_chunk_id(int k, int j, int m_cap) { return m_cap - (m_cap >> k) + (j >> 1); }
+__host__ __device__ __forceinline__ int64_t fsb_nodes_per_row(int m_cap) { return (int64_t)(fsb_log2(m_cap) + 1) * m_cap; }
+
+// ---- halving-order sum over the head dimension, one warp per vector ------------------------------------------------
+// Lane L holds the values of dims L, L+32, L+64, L+96 (zero beyond D). The order is that of repeated halving over the
+// dimension padded to a power of two: x[i] + x[i + n/2], n = DP, DP/2, ..., 2. Every lane returns the same bits.
+template <int D>
+struct FsbDim {
+    static constexpr int DP = (D <= 64) ? 64 : 128;
+    static constexpr int NPL = DP / 32;
+};
+
+template <int D>
+__device__ __forceinline__ float fsb_warp_det_sum(const float (&v)[FsbDim<D>::NPL]) {
+    float a;
+    if constexpr (FsbDim<D>::NPL == 2) {
+        a = f_add(v[0], v[1]);
+    } else {
+        a = f_add(f_add(v[0], v[2]), f_add(v[1], v[3]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = f_add(a, __shfl_xor_sync(FS_FULL, a, o));
+    return a;
+}
+
+template <int D>
+__device__ __forceinline__ void fsb_load_row(const float* row, int lane, float (&v)[FsbDim<D>::NPL]) {
+#pragma unroll
+    for (int i = 0; i < FsbDim<D>::NPL; ++i) {
+        const int d = lane + 32 * i;
+        v[i] = (d < D) ? row[d] : 0.0f;
+    }
+}
+template <int D>
+__device__ __forceinline__ void fsb_store_row(float* row, int lane, const float (&v)[FsbDim<D>::NPL]) {
+#pragma unroll
+    for (int i = 0; i < FsbDim<D>::NPL; ++i) {
+        const int d = lane + 32 * i;
+        if (d < D) row[d] = v[i];
+    }
+}
+
+// ---- halving-order sum of D values held by ONE thread (beam / re-rank dot products) -------------------------------------
+template <int D>
+__device__ __forceinline__ float fsb_thread_det_sum(float (&p)[FsbDim<D>::DP]) {
+#pragma unroll
+    for (int h = FsbDim<D>::DP / 2; h > 0; h >>= 1) {
+#pragma unroll
+        for (int i = 0; i < h; ++i) p[i] = f_add(p[i], p[i + h]);
+    }
+    return p[0];
+}

@@ -1,0 +1,373 @@
+// FS-B forest: admission of cells and construction of the chunk trees (one chunk per newly admitted position).
+//
+// A chunk tree over n = 2^k cells is built level by level by one CTA. All nodes of a level hold m = n >> l cells in
+// consecutive slots of an order array, so every pass below is a flat parallel loop over slots, slot pairs or
+// (slot, dim) elements. Reductions keep the halving association order of the reference's det_sum and use explicit
+// IEEE intrinsics, so the trees match a CPU build bit for bit:
+//   mean     : Y[q] = x[i] + x[i + m/2] then in-place halving steps            (sum over a node's cells)
+//   |x-mu|^2 : one warp per cell, lanes hold dims L, L+32, ...                    (sum over the head dimension)
+//   split    : farthest member -> two power iterations -> projection -> stable rank sort; lower half goes left.
+// Chunks of up to 32 cells live entirely in shared memory; larger ones use an L2-resident scratch area.
+#include "fsb.cuh"
+
+namespace {
+
+struct BuildArgs {
+    fsattn_fsb_forest_t f[4];
+    int nf;
+    int k_cap;
+    int mode;              // 0: every position of the arena in big-first order; 1: positions m_prev + blockIdx.x
+    int x0;                // mode 0: first item index of this launch
+    float* scratch;        // big chunks: per forest, per row
+    int64_t scratch_per_forest, scratch_per_row;
+};
+
+__device__ __forceinline__ int64_t scratch_cells_before(int k, int jj, int k_cap, int m_cap) {
+    // cells of scratch in front of chunk (k, jj) inside one row's area; heights below 6 never use it
+    return (int64_t)(k - (FSB_SMALL_K + 1)) * (m_cap >> 1) + ((k < k_cap) ? ((int64_t)jj << k) : 0);
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// admission: cells [cb, ce) with ceil >= tau[h] are appended to adm in ascending order
+// ------------------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) fsb_admit_kernel(BuildArgs a, int cb, int ce) {
+    const fsattn_fsb_forest_t& F = a.f[blockIdx.y];
+    const int t = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __shared__ int wsum[8];
+    __shared__ int base;
+    const float tau = F.tau[t % F.H];
+    const float* ceil = F.ceil + (int64_t)t * F.ceil_st;
+    int* adm = F.adm + (int64_t)t * F.m_cap;
+    if (tid == 0) {
+        base = F.m_tot[t];
+        F.m_prev[t] = base;
+    }
+    __syncthreads();
+    for (int c0 = cb; c0 < ce; c0 += 256) {
+        const int c = c0 + tid;
+        const bool ok = c < ce && ceil[c] >= tau;
+        const unsigned bal = __ballot_sync(FS_FULL, ok);
+        if (lane == 0) wsum[warp] = __popc(bal);
+        __syncthreads();
+        int off = base;
+        for (int w = 0; w < warp; ++w) off += wsum[w];
+        off += __popc(bal & ((1u << lane) - 1));
+        if (ok && off < F.m_cap) adm[off] = c;
+        __syncthreads();
+        if (tid == 0) {
+            int tot = 0;
+            for (int w = 0; w < 8; ++w) tot += wsum[w];
+            base = min(base + tot, F.m_cap);
+        }
+        __syncthreads();
+    }
+    if (tid == 0) F.m_tot[t] = base;
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// chunk build
+// ------------------------------------------------------------------------------------------------------------------
+template <int D, int THREADS, bool SMALL>
+__global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
+    constexpr int NPL = FsbDim<D>::NPL;
+    constexpr int NW = THREADS / 32;
+    constexpr int SN = SMALL ? 32 : 1;                    // shared-memory capacity in cells (small kernel)
+    const fsattn_fsb_forest_t& F = a.f[blockIdx.z];
+    const int t = blockIdx.y;
+    const int m_cap = F.m_cap, k_cap = a.k_cap;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+    // ---- which admitted position does this CTA complete a chunk for? ----
+    int p;
+    if (a.mode == 0) {
+        const int x = a.x0 + blockIdx.x;
+        if (x == 0) {
+            p = m_cap - 1;
+        } else {
+            const int fl = 31 - __clz(x);
+            const int k_ = k_cap - 1 - fl;
+            p = ((2 * (x - (1 << fl)) + 1) << k_) - 1;
+        }
+    } else {
+        p = F.m_prev[t] + blockIdx.x;
+    }
+    if (p < F.m_prev[t] || p >= F.m_tot[t]) return;
+    const int k = __ffs(p + 1) - 1;
+    if (SMALL ? (k > FSB_SMALL_K) : (k <= FSB_SMALL_K)) return;
+    const int n = 1 << k;
+    const int j = ((p + 1) >> k) - 1, jj = j >> 1;
+    const int pos0 = p + 1 - n;
+
+    const int* adm = F.adm + (int64_t)t * m_cap + pos0;
+    const float* kbar = F.kbar + (int64_t)t * F.kbar_st;
+    const float* ceil = F.ceil + (int64_t)t * F.ceil_st;
+    const int64_t node0 = (int64_t)t * fsb_nodes_per_row(m_cap) + fsb_nbase(k, m_cap) + (int64_t)jj * (2 * n - 1);
+    bf16* node_mu = (bf16*)F.node_mu + node0 * D;
+    float4* node_aux = (float4*)F.node_aux + node0;
+    float* root32 = F.root32 + ((int64_t)t * m_cap + fsb_chunk_id(k, j, m_cap)) * (D + FSB_ROOT_PAD);
+
+    // ---- working arrays ----
+    __shared__ float sm_f[SMALL ? (SN * D * 2 + SN) : 1];
+    __shared__ int sm_i[SMALL ? (SN * 2 + SN / 2) : 1];
+    __shared__ float sm_proj[SMALL ? 1 : FSB_MAX_MCAP];
+    float *XC, *Y, *VV, *S1;
+    int *ordA, *ordB, *FAR;
+    if constexpr (SMALL) {
+        XC = sm_f; Y = XC + SN * D; VV = Y + (SN / 2) * D; S1 = VV + (SN / 2) * D;
+        ordA = sm_i; ordB = ordA + SN; FAR = ordB + SN;
+    } else {
+        float* base = a.scratch + blockIdx.z * a.scratch_per_forest + t * a.scratch_per_row +
+                      scratch_cells_before(k, jj, k_cap, m_cap) * (2 * D + 4);
+        XC = base; Y = XC + (int64_t)n * D; VV = Y + (int64_t)(n / 2) * D; S1 = VV + (int64_t)(n / 2) * D;
+        ordA = (int*)(S1 + n); ordB = ordA + n; FAR = ordB + n;
+    }
+    for (int i = tid; i < n; i += THREADS) ordA[i] = i;
+    __syncthreads();
+
+    for (int l = 0; l <= k; ++l) {
+        const int lm = k - l, m = 1 << lm, h = m >> 1, nodes = 1 << l;
+        // ---- P1: mean = halving sum of the members / m ----
+        if (m >= 2) {
+            for (int e = tid; e < (n / 2) * D; e += THREADS) {
+                const int d = e % D, q = e / D;
+                const int g = q >> (lm - 1), i = q & (h - 1);
+                const float x0 = kbar[(int64_t)adm[ordA[(g << lm) + i]] * D + d];
+                const float x1 = kbar[(int64_t)adm[ordA[(g << lm) + i + h]] * D + d];
+                Y[(int64_t)q * D + d] = f_add(x0, x1);
+            }
+            for (int h2 = h >> 1; h2 >= 1; h2 >>= 1) {
+                __syncthreads();
+                const int lh2 = 31 - __clz(h2);
+                for (int e = tid; e < nodes * h2 * D; e += THREADS) {
+                    const int d = e % D, q = e / D;
+                    const int g = q >> lh2, i = q & (h2 - 1);
+                    const int64_t r = ((int64_t)g * h + i) * D + d;
+                    Y[r] = f_add(Y[r], Y[r + (int64_t)h2 * D]);
+                }
+            }
+            __syncthreads();
+        }
+        // ---- P2: centre the members, squared distance ----
+        for (int c = warp; c < n; c += NW) {
+            const int g = c >> lm;
+            float x[NPL], mu[NPL], xc[NPL], sq[NPL];
+            fsb_load_row<D>(kbar + (int64_t)adm[ordA[c]] * D, lane, x);
+            if (m >= 2) {
+                fsb_load_row<D>(Y + (int64_t)g * h * D, lane, mu);
+#pragma unroll
+                for (int i = 0; i < NPL; ++i) mu[i] = f_div(mu[i], (float)m);
+            } else {
+#pragma unroll
+                for (int i = 0; i < NPL; ++i) mu[i] = x[i];
+            }
+#pragma unroll
+            for (int i = 0; i < NPL; ++i) {
+                xc[i] = f_add(x[i], -mu[i]);
+                sq[i] = f_mul(xc[i], xc[i]);
+            }
+            fsb_store_row<D>(XC + (int64_t)c * D, lane, xc);
+            const float d2 = fsb_warp_det_sum<D>(sq);
+            if (lane == 0) S1[c] = d2;
+        }
+        __syncthreads();
+        // ---- P3: node statistics, node tables, farthest member ----
+        for (int g = warp; g < nodes; g += NW) {
+            float best = -1.0f, am = -INFINITY;
+            int bi = 0x7fffffff, pm = 0x7fffffff;
+            for (int c = (g << lm) + lane; c < ((g + 1) << lm); c += 32) {
+                const float v = S1[c];
+                if (v > best) { best = v; bi = c; }
+                const int id = adm[ordA[c]];
+                am = fmaxf(am, ceil[id]);
+                pm = min(pm, id);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(FS_FULL, best, o);
+                const int oi = __shfl_xor_sync(FS_FULL, bi, o);
+                if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+                am = fmaxf(am, __shfl_xor_sync(FS_FULL, am, o));
+                pm = min(pm, __shfl_xor_sync(FS_FULL, pm, o));
+            }
+            if (lane == 0) FAR[g] = bi;
+            float mu[NPL], er[NPL];
+            if (m >= 2) {
+                fsb_load_row<D>(Y + (int64_t)g * h * D, lane, mu);
+#pragma unroll
+                for (int i = 0; i < NPL; ++i) mu[i] = f_div(mu[i], (float)m);
+            } else {
+                fsb_load_row<D>(kbar + (int64_t)adm[ordA[g]] * D, lane, mu);
+            }
+            const int nidx = nodes - 1 + g;
+#pragma unroll
+            for (int i = 0; i < NPL; ++i) {
+                const int d = lane + 32 * i;
+                const bf16 b = __float2bfloat16_rn(mu[i]);
+                if (d < D) node_mu[(int64_t)nidx * D + d] = b;
+                const float e = (d < D) ? f_add(mu[i], -__bfloat162float(b)) : 0.0f;
+                er[i] = f_mul(e, e);
+            }
+            const float eps = f_sqrt(fsb_warp_det_sum<D>(er));
+            const float rad = f_sqrt(best);
+            if (lane == 0) {
+                const int meta = (l == k) ? adm[ordA[g]] : ~((nidx << 4) | lm);
+                node_aux[nidx] = make_float4(f_add(rad, eps), fmaxf(am, 0.0f), __int_as_float(pm), __int_as_float(meta));
+            }
+            if (l == 0) {
+                fsb_store_row<D>(root32, lane, mu);
+                if (lane == 0) root32[D] = rad;
+            }
+        }
+        if (l == k) break;
+        __syncthreads();
+        // ---- P4: start direction = farthest member, normalised ----
+        for (int e = tid; e < nodes * D; e += THREADS) {
+            const int g = e / D, d = e % D;
+            const int fc = FAR[g];
+            VV[e] = f_div(XC[(int64_t)fc * D + d], fmaxf(f_sqrt(S1[fc]), 1e-6f));
+        }
+        __syncthreads();
+        // ---- P5: two power iterations v <- normalise(sum_c xc_c (xc_c . v)) ; P6: projections ----
+        for (int it = 0; it < 3; ++it) {
+            for (int c = warp; c < n; c += NW) {
+                float xc[NPL], v[NPL], pr[NPL];
+                fsb_load_row<D>(XC + (int64_t)c * D, lane, xc);
+                fsb_load_row<D>(VV + (int64_t)(c >> lm) * D, lane, v);
+#pragma unroll
+                for (int i = 0; i < NPL; ++i) pr[i] = f_mul(xc[i], v[i]);
+                const float pv = fsb_warp_det_sum<D>(pr);
+                if (lane == 0) S1[c] = pv;
+            }
+            __syncthreads();
+            if (it == 2) break;
+            for (int e = tid; e < (n / 2) * D; e += THREADS) {
+                const int d = e % D, q = e / D;
+                const int g = q >> (lm - 1), i = q & (h - 1);
+                const int c0 = (g << lm) + i, c1 = c0 + h;
+                Y[(int64_t)q * D + d] = f_add(f_mul(XC[(int64_t)c0 * D + d], S1[c0]), f_mul(XC[(int64_t)c1 * D + d], S1[c1]));
+            }
+            for (int h2 = h >> 1; h2 >= 1; h2 >>= 1) {
+                __syncthreads();
+                const int lh2 = 31 - __clz(h2);
+                for (int e = tid; e < nodes * h2 * D; e += THREADS) {
+                    const int d = e % D, q = e / D;
+                    const int g = q >> lh2, i = q & (h2 - 1);
+                    const int64_t r = ((int64_t)g * h + i) * D + d;
+                    Y[r] = f_add(Y[r], Y[r + (int64_t)h2 * D]);
+                }
+            }
+            __syncthreads();
+            for (int g = warp; g < nodes; g += NW) {
+                float vn[NPL], sq[NPL];
+                fsb_load_row<D>(Y + (int64_t)g * h * D, lane, vn);
+#pragma unroll
+                for (int i = 0; i < NPL; ++i) sq[i] = f_mul(vn[i], vn[i]);
+                const float nrm = fmaxf(f_sqrt(fsb_warp_det_sum<D>(sq)), 1e-6f);
+#pragma unroll
+                for (int i = 0; i < NPL; ++i) vn[i] = f_div(vn[i], nrm);
+                fsb_store_row<D>(VV + (int64_t)g * D, lane, vn);
+            }
+            __syncthreads();
+        }
+        // ---- P7: stable ascending rank of the projections inside each node; the lower half becomes the left child ----
+        const float* PJ = S1;
+        if constexpr (!SMALL) {
+            for (int i = tid; i < n; i += THREADS) sm_proj[i] = S1[i];
+            __syncthreads();
+            PJ = sm_proj;
+        }
+        for (int c = tid; c < n; c += THREADS) {
+            const int b0 = (c >> lm) << lm;
+            const float pc = PJ[c];
+            int r = 0;
+            for (int o = 0; o < m; ++o) {
+                const float po = PJ[b0 + o];
+                r += (po < pc || (po == pc && b0 + o < c)) ? 1 : 0;
+            }
+            ordB[b0 + r] = ordA[c];
+        }
+        __syncthreads();
+        int* tmp = ordA; ordA = ordB; ordB = tmp;
+    }
+}
+
+template <int D>
+int launch_build(const BuildArgs& a0, int T, int new_cells, cudaStream_t st) {
+    BuildArgs a = a0;
+    const int m_cap = a.f[0].m_cap;
+    if (a.mode == 0) {
+        const int big_items = (a.k_cap > FSB_SMALL_K) ? (m_cap >> (FSB_SMALL_K + 1)) : 0;
+        if (big_items > 0) {
+            a.x0 = 0;
+            fsb_build_kernel<D, 512, false><<<dim3(big_items, T, a.nf), 512, 0, st>>>(a);
+        }
+        a.x0 = big_items;
+        if (m_cap - big_items > 0)
+            fsb_build_kernel<D, 128, true><<<dim3(m_cap - big_items, T, a.nf), 128, 0, st>>>(a);
+    } else {
+        if (a.k_cap > FSB_SMALL_K) fsb_build_kernel<D, 512, false><<<dim3(new_cells, T, a.nf), 512, 0, st>>>(a);
+        fsb_build_kernel<D, 128, true><<<dim3(new_cells, T, a.nf), 128, 0, st>>>(a);
+    }
+    return fs_check_launch("fsb_build_kernel");
+}
+
+}  // namespace
+
+int64_t fs_fsb_scratch_cells(int m_cap) {
+    const int k_cap = fsb_log2(m_cap);
+    if (k_cap <= FSB_SMALL_K) return 0;
+    return (int64_t)(k_cap - (FSB_SMALL_K + 1)) * (m_cap >> 1) + m_cap;
+}
+
+extern "C" int64_t fsattn_fsb_scratch_floats(int32_t m_cap, int32_t D, int32_t T) {
+    if (m_cap <= 0 || D <= 0 || T <= 0) return 0;
+    return fs_fsb_scratch_cells(m_cap) * (2 * (int64_t)D + 4) * T;
+}
+
+int fs_fsb_check_forest(const fsattn_fsb_forest_t& f, const char* what) {
+    FS_REQUIRE(f.T > 0 && f.H > 0 && f.T % f.H == 0, "%s: T = %d must be a positive multiple of H = %d", what, f.T, f.H);
+    FS_UNSUPPORTED(f.D != 64 && f.D != 96 && f.D != 128, "%s: head dim %d (64, 96 or 128)", what, f.D);
+    FS_REQUIRE(f.m_cap >= 1 && (f.m_cap & (f.m_cap - 1)) == 0, "%s: m_cap = %d must be a power of two", what, f.m_cap);
+    FS_UNSUPPORTED(f.m_cap > FSB_MAX_MCAP, "%s: m_cap = %d cells (at most %d)", what, f.m_cap, FSB_MAX_MCAP);
+    FS_REQUIRE(f.kbar && f.ceil && f.tau && f.adm && f.m_tot && f.m_prev && f.node_mu && f.node_aux && f.root32,
+               "%s: null forest buffer", what);
+    return FSATTN_OK;
+}
+
+extern "C" int fsattn_fsb_ingest(const fsattn_fsb_forest_t* forests, int32_t n_forests, int32_t cell_begin,
+                                 int32_t cell_end, float* scratch, int64_t scratch_floats, fsattn_stream_t stream) {
+    FS_REQUIRE(forests && n_forests >= 1 && n_forests <= 4, "fsb_ingest: 1 to 4 forests per call (got %d)", n_forests);
+    BuildArgs a{};
+    a.nf = n_forests;
+    for (int i = 0; i < n_forests; ++i) {
+        int rc = fs_fsb_check_forest(forests[i], "fsb_ingest");
+        if (rc != FSATTN_OK) return rc;
+        FS_REQUIRE(forests[i].T == forests[0].T && forests[i].D == forests[0].D && forests[i].m_cap == forests[0].m_cap,
+                   "fsb_ingest: the forests of one call share T, D and m_cap");
+        a.f[i] = forests[i];
+    }
+    const fsattn_fsb_forest_t& f0 = forests[0];
+    FS_REQUIRE(cell_begin >= 0 && cell_end >= cell_begin && cell_end <= f0.m_cap,
+               "fsb_ingest: cells [%d, %d) outside the capacity %d", cell_begin, cell_end, f0.m_cap);
+    if (cell_end == cell_begin) return FSATTN_OK;
+    a.k_cap = fsb_log2(f0.m_cap);
+    const int64_t per_row = fs_fsb_scratch_cells(f0.m_cap) * (2 * (int64_t)f0.D + 4);
+    a.scratch = scratch;
+    a.scratch_per_row = per_row;
+    a.scratch_per_forest = per_row * f0.T;
+    FS_REQUIRE(per_row == 0 || (scratch && scratch_floats >= a.scratch_per_forest * n_forests),
+               "fsb_ingest: scratch of %lld floats needed (got %lld)", (long long)(a.scratch_per_forest * n_forests),
+               (long long)scratch_floats);
+    cudaStream_t st = (cudaStream_t)stream;
+    fsb_admit_kernel<<<dim3(f0.T, n_forests), 256, 0, st>>>(a, cell_begin, cell_end);
+    int rc = fs_check_launch("fsb_admit_kernel");
+    if (rc != FSATTN_OK) return rc;
+    const int new_cells = cell_end - cell_begin;
+    a.mode = (new_cells > 64) ? 0 : 1;
+    switch (f0.D) {
+        case 64: return launch_build<64>(a, f0.T, new_cells, st);
+        case 96: return launch_build<96>(a, f0.T, new_cells, st);
+        default: return launch_build<128>(a, f0.T, new_cells, st);
+    }
+}

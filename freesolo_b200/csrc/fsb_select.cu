@@ -1,0 +1,401 @@
+// FS-B selection: spines, the two beams, union of candidates, token-level re-rank, top-K.
+//
+// One warp per query. A beam keeps its frontier (<= 16 node refs) in lanes 0..15; each level the 32 lanes score the
+// 32 possible children (lane c = child c&1 of frontier slot c>>1), rank them with shuffles and rebuild the frontier:
+// carried nodes first in slot order, then children by (score desc, position asc). Node tables are read straight from
+// the L2-resident arena (one 2D-byte mean row + one 16-byte aux word per child); the spine nodes of the block live in
+// shared memory. The re-rank reads the candidate cells' raw token keys, one token per lane.
+#include "fsb.cuh"
+
+namespace {
+
+constexpr int SPW = FSATTN_FSB_SPINE_MAX;      // spine slots per forest
+constexpr int WMAX = 16;                       // frontier slots
+
+template <int D>
+struct SpineSm {
+    float node[SPW][D + 8];     // [mu | rad amax pmin cnt chl chr pad pad]
+    int root, height, m_b, pad;
+};
+
+// ---- spine of the first m_b admitted cells of row t (one warp) ------------------------------------------------------
+template <int D>
+__device__ void build_spine(const fsattn_fsb_forest_t& F, int t, int m_b, SpineSm<D>& S, int lane) {
+    constexpr int NPL = FsbDim<D>::NPL;
+    const int m_cap = F.m_cap;
+    const float4* aux = (const float4*)F.node_aux + (int64_t)t * fsb_nodes_per_row(m_cap);
+    const float* root32 = F.root32 + (int64_t)t * m_cap * (D + FSB_ROOT_PAD);
+    float rmu[NPL];
+    float r_rad = 0.f, r_am = 0.f, r_cnt = 0.f;
+    int r_pm = 0x7fffffff, r_ref = -1, npres = 0;
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) rmu[i] = 0.f;
+    for (int k = 0; (m_b >> k) != 0; ++k) {
+        if (!((m_b >> k) & 1)) continue;
+        ++npres;
+        const int j = (m_b >> (k + 1)) << 1;
+        const int cref = (int)fsb_root_node(k, j, m_cap);
+        const float* cr = root32 + (int64_t)fsb_chunk_id(k, j, m_cap) * (D + FSB_ROOT_PAD);
+        float cmu[NPL];
+        fsb_load_row<D>(cr, lane, cmu);
+        const float c_rad = cr[D];
+        const float4 ca = aux[cref];
+        const float c_am = ca.y, c_cnt = (float)(1 << k);
+        const int c_pm = __float_as_int(ca.z);
+        if (r_ref == -1) {
+#pragma unroll
+            for (int i = 0; i < NPL; ++i) rmu[i] = cmu[i];
+            r_rad = c_rad; r_am = c_am; r_cnt = c_cnt; r_pm = c_pm; r_ref = cref;
+            continue;
+        }
+        const float tot = f_add(c_cnt, r_cnt);
+        float nmu[NPL], dc[NPL], dr[NPL];
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) {
+            nmu[i] = f_div(f_add(f_mul(c_cnt, cmu[i]), f_mul(r_cnt, rmu[i])), tot);
+            const float a = f_add(cmu[i], -nmu[i]), b = f_add(rmu[i], -nmu[i]);
+            dc[i] = f_mul(a, a);
+            dr[i] = f_mul(b, b);
+        }
+        const float nc = f_sqrt(fsb_warp_det_sum<D>(dc)), nr = f_sqrt(fsb_warp_det_sum<D>(dr));
+        const float n_rad = fmaxf(f_add(c_rad, nc), f_add(r_rad, nr));
+        const float n_am = fmaxf(c_am, r_am);
+        const int n_pm = min(c_pm, r_pm);
+        fsb_store_row<D>(S.node[k], lane, nmu);
+        if (lane == 0) {
+            float* x = S.node[k] + D;
+            x[0] = n_rad; x[1] = n_am; x[2] = __int_as_float(n_pm); x[3] = tot;
+            x[4] = __int_as_float(cref); x[5] = __int_as_float(r_ref);
+        }
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) rmu[i] = nmu[i];
+        r_rad = n_rad; r_am = n_am; r_cnt = tot; r_pm = n_pm; r_ref = -(k + 2);
+    }
+    if (lane == 0) {
+        S.root = (m_b > 0) ? r_ref : -1;
+        S.height = (m_b > 1) ? (31 - __clz(m_b)) + (npres >= 2 ? 1 : 0) : 0;
+        S.m_b = m_b;
+    }
+}
+
+__device__ __forceinline__ int count_below(const int* adm, int m_tot, int E) {
+    int lo = 0, hi = m_tot;                       // first index with adm[i] >= E
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (adm[mid] < E) lo = mid + 1; else hi = mid;
+    }
+    return lo;
+}
+
+// ---- one beam (one warp). Returns the frontier's cell in lanes 0..15 (-1 none); adds the scored children to nvis ----
+template <int D>
+__device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, const float* qs, float qn, float qpos,
+                    float lam, float sig, float scale, int width, int lane, int* fr, int& nvis) {
+    constexpr int DP = FsbDim<D>::DP;
+    const int m_cap = F.m_cap;
+    const int64_t nrow = (int64_t)t * fsb_nodes_per_row(m_cap);
+    const bf16* node_mu = (const bf16*)F.node_mu + nrow * D;
+    const float4* aux = (const float4*)F.node_aux + nrow;
+    const int root = S.root;
+    int ref = -1, meta = 0;
+    if (root == -1) return -1;
+    const int d0 = S.height;                                  // delta = 0: stop depth = height, budget 1
+    const int W = min(width, (d0 >= 5) ? 32 : (1 << d0));
+    if (lane == 0) {
+        ref = root;
+        meta = (root >= 0) ? __float_as_int(aux[root].w) : 0;
+    }
+    for (int it = 0; it < 40; ++it) {
+        const bool active = lane < WMAX && ref != -1;
+        const bool expand = active && (ref < -1 || meta < 0);
+        const unsigned emask = __ballot_sync(FS_FULL, expand);
+        if (emask == 0) break;
+        const unsigned cmask = __ballot_sync(FS_FULL, active && !expand);
+        // ---- children ----
+        const int ps = lane >> 1, side = lane & 1;
+        const int pref = __shfl_sync(FS_FULL, ref, ps), pmeta = __shfl_sync(FS_FULL, meta, ps);
+        const bool valid = (emask >> ps) & 1;
+        int cref = -1, cmeta = 0;
+        float score = FS_NEG_SCORE;
+        if (valid) {
+            float rad, am;
+            int pm;
+            float p[DP];
+            if (pref >= 0) {
+                cref = pref + ((~pmeta) >> 4) + 1 + side;
+            } else {
+                const float* x = S.node[-pref - 2] + D;
+                cref = __float_as_int(x[4 + side]);
+            }
+            if (cref >= 0) {
+                const uint4* mr = (const uint4*)(node_mu + (int64_t)cref * D);
+#pragma unroll
+                for (int v = 0; v < D / 8; ++v) {
+                    const uint4 w = mr[v];
+                    const float4 qa = *(const float4*)(qs + v * 8), qb = *(const float4*)(qs + v * 8 + 4);
+                    p[v * 8 + 0] = f_mul(qa.x, bf_lo(w.x)); p[v * 8 + 1] = f_mul(qa.y, bf_hi(w.x));
+                    p[v * 8 + 2] = f_mul(qa.z, bf_lo(w.y)); p[v * 8 + 3] = f_mul(qa.w, bf_hi(w.y));
+                    p[v * 8 + 4] = f_mul(qb.x, bf_lo(w.z)); p[v * 8 + 5] = f_mul(qb.y, bf_hi(w.z));
+                    p[v * 8 + 6] = f_mul(qb.z, bf_lo(w.w)); p[v * 8 + 7] = f_mul(qb.w, bf_hi(w.w));
+                }
+                const float4 ax = aux[cref];
+                rad = ax.x; am = ax.y; pm = __float_as_int(ax.z); cmeta = __float_as_int(ax.w);
+            } else {
+                const float* x = S.node[-cref - 2];
+#pragma unroll
+                for (int d = 0; d < D; ++d) p[d] = f_mul(qs[d], x[d]);
+                rad = x[D]; am = x[D + 1]; pm = __float_as_int(x[D + 2]);
+            }
+#pragma unroll
+            for (int d = D; d < DP; ++d) p[d] = 0.f;
+            float content = f_mul(fsb_thread_det_sum<D>(p), scale);
+            content = f_add(content, f_mul(f_mul(qn, rad), scale));
+            const float ppos = f_mul(f_add((float)pm, 0.5f), 32.0f);
+            const float e = erff(f_div(fabsf(f_add(qpos, -ppos)), f_mul(2.0f, sig)));
+            score = f_add(content, f_mul(f_mul(lam, am), e));
+        }
+        nvis += __popc(__ballot_sync(FS_FULL, valid));
+        // ---- rank the children: (score desc, position asc) ----
+        int rank = 0;
+#pragma unroll 8
+        for (int o = 0; o < 32; ++o) {
+            const float so = __shfl_sync(FS_FULL, score, o);
+            rank += (so > score || (so == score && o < lane)) ? 1 : 0;
+        }
+        const int ncar = __popc(cmask & 0xffffu);
+        int* fm = fr + WMAX;                   // fr: WMAX refs then WMAX metas
+        if (lane < WMAX) fr[lane] = -1;
+        __syncwarp();
+        if (active && !expand) {
+            const int pos = __popc(cmask & ((1u << lane) - 1));
+            fr[pos] = ref; fm[pos] = meta;
+        }
+        if (valid && score > 0.5f * FS_NEG_SCORE && ncar + rank < W) {
+            fr[ncar + rank] = cref; fm[ncar + rank] = cmeta;
+        }
+        __syncwarp();
+        if (lane < WMAX) { ref = fr[lane]; meta = fm[lane]; }
+        __syncwarp();
+    }
+    return (lane < WMAX && ref >= 0 && meta >= 0) ? meta : -1;
+}
+
+struct SelArgs {
+    fsattn_fsb_select_t a;
+    int H, ncell_k;
+};
+
+template <int D, int NWARP>
+__global__ void __launch_bounds__(NWARP * 32) fsb_select_kernel(SelArgs A) {
+    constexpr int DP = FsbDim<D>::DP;
+    const fsattn_fsb_select_t& a = A.a;
+    const int blk = blockIdx.x, t = blockIdx.y;
+    const int b = t / A.H, hd = t % A.H;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __shared__ SpineSm<D> sp[2];
+    __shared__ __align__(16) float qsm[NWARP][DP];
+    __shared__ int frs[NWARP][WMAX * 2];
+
+    // ---- spines of this block (warp 0: main, warp 1: second) ----
+    if (warp < 2) {
+        const fsattn_fsb_forest_t& F = warp == 0 ? a.main : a.second;
+        if (a.use_spines) {
+            const float* src = a.spine[warp] + (int64_t)t * SPW * (D + 8);
+            float* dst = &sp[warp].node[0][0];
+            for (int i = lane; i < SPW * (D + 8); i += 32) dst[i] = src[i];
+            if (lane == 0) {
+                const int* h = a.hdr[warp] + t * 4;
+                sp[warp].root = h[0]; sp[warp].height = h[1]; sp[warp].m_b = h[2];
+            }
+        } else {
+            const int E = (a.q_pos0 + blk * a.Bq) / 32;
+            const int m_b = count_below(F.adm + (int64_t)t * F.m_cap, F.m_tot[t], E);
+            build_spine<D>(F, t, m_b, sp[warp], lane);
+        }
+    }
+    __syncthreads();
+
+    const float lam = a.lam[hd], sig = a.sigma[hd];
+    const int Wc = a.width + a.width2;
+    const int nq = a.use_spines ? 1 : min(a.Bq, a.N - blk * a.Bq);
+    const int64_t pos_dec = a.use_spines ? *a.pos : 0;
+    for (int qi = warp; qi < a.Bq; qi += NWARP) {
+        const int64_t row = ((int64_t)t * gridDim.x + blk) * a.Bq + qi;         // (B,H,Npad) flattened
+        if (qi >= nq) {
+            if (lane < a.read_top) a.sel[row * a.read_top + lane] = -1;
+            if (a.cand && lane < Wc) a.cand[row * Wc + lane] = -1;
+            if (a.nvis && lane == 0) a.nvis[row] = 0;
+            continue;
+        }
+        const int qidx = blk * a.Bq + qi;
+        const float qpos = a.use_spines ? (float)pos_dec : (float)(a.q_pos0 + qidx);
+        const bf16* qp = (const bf16*)a.q.ptr + b * a.q.sb + hd * a.q.sh + (int64_t)qidx * a.q.sn;
+        float* qs = qsm[warp];
+        __syncwarp();
+        for (int d = lane; d < DP; d += 32) qs[d] = (d < D) ? __bfloat162float(qp[d]) : 0.f;
+        __syncwarp();
+        float qq[FsbDim<D>::NPL];
+#pragma unroll
+        for (int i = 0; i < FsbDim<D>::NPL; ++i) { const float v = qs[lane + 32 * i]; qq[i] = f_mul(v, v); }
+        const float qn = f_mul(f_sqrt(fsb_warp_det_sum<D>(qq)), a.radius_coef);
+
+        int nv = 0;
+        int* fr = frs[warp];
+        const int c_main = beam<D>(a.main, t, sp[0], qs, qn, qpos, lam, sig, a.scale, a.width, lane, fr, nv);
+        int c_sec = -1;
+        if (a.width2 > 0) c_sec = beam<D>(a.second, t, sp[1], qs, qn, qpos, lam, sig, a.scale, a.width2, lane, fr, nv);
+        // ---- union: lanes 0..15 main, 16..31 second beam minus repeats of a main cell ----
+        const int c_sec_sh = __shfl_sync(FS_FULL, c_sec, lane & (WMAX - 1));     // every lane takes part
+        int cand = (lane < WMAX) ? c_main : c_sec_sh;
+        {
+            bool dup = false;
+            for (int o = 0; o < WMAX; ++o) {
+                const int mc = __shfl_sync(FS_FULL, cand, o);
+                dup |= (lane >= WMAX && mc == cand);
+            }
+            if (dup) cand = -1;
+        }
+        if (lane >= WMAX && lane - WMAX >= a.width2) cand = -1;
+        if (lane < WMAX && lane >= a.width) cand = -1;
+        if (a.cand) {
+            if (lane < a.width) a.cand[row * Wc + lane] = cand;
+            if (lane >= WMAX && lane - WMAX < a.width2) a.cand[row * Wc + a.width + lane - WMAX] = cand;
+        }
+        if (a.nvis && lane == 0) a.nvis[row] = nv;
+        // ---- re-rank: u = LSE_t((q.k_t) scale) + lam ceil erf(|p - (c+.5) 32| / (2 sig)) ----
+        float u = -INFINITY;
+        const float* ceil = a.main.ceil + (int64_t)t * a.main.ceil_st;
+        for (int i = 0; i < 32; ++i) {
+            const int cell = __shfl_sync(FS_FULL, cand, i);
+            if (cell < 0) continue;
+            float p[DP];
+            const int64_t tok = (int64_t)cell * 32 + lane;
+            if (a.k.ptr) {
+                const uint4* kr = (const uint4*)((const bf16*)a.k.ptr + b * a.k.sb + hd * a.k.sh + tok * a.k.sn);
+#pragma unroll
+                for (int v = 0; v < D / 8; ++v) {
+                    const uint4 w = kr[v];
+                    const float4 qa = *(const float4*)(qs + v * 8), qb = *(const float4*)(qs + v * 8 + 4);
+                    p[v * 8 + 0] = f_mul(bf_lo(w.x), qa.x); p[v * 8 + 1] = f_mul(bf_hi(w.x), qa.y);
+                    p[v * 8 + 2] = f_mul(bf_lo(w.y), qa.z); p[v * 8 + 3] = f_mul(bf_hi(w.y), qa.w);
+                    p[v * 8 + 4] = f_mul(bf_lo(w.z), qb.x); p[v * 8 + 5] = f_mul(bf_hi(w.z), qb.y);
+                    p[v * 8 + 6] = f_mul(bf_lo(w.w), qb.z); p[v * 8 + 7] = f_mul(bf_hi(w.w), qb.w);
+                }
+            } else {
+                const uint32_t* kr = (const uint32_t*)(a.kq + b * a.kq_sb + hd * a.kq_sh + tok * D);
+                const float sc = __bfloat162float(((const bf16*)a.ks)[b * a.ks_sb + hd * a.ks_sh + cell]);
+#pragma unroll
+                for (int v = 0; v < D / 4; ++v) {
+                    float o[4];
+                    unpack4_i8(kr[v], o);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) p[v * 4 + e] = f_mul(bf_round(f_mul(o[e], sc)), qs[v * 4 + e]);
+                }
+            }
+#pragma unroll
+            for (int d = D; d < DP; ++d) p[d] = 0.f;
+            const float sc = f_mul(fsb_thread_det_sum<D>(p), a.scale);
+            const float m = warp_max(sc);
+            float e = expf(f_add(sc, -m));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) e = f_add(e, __shfl_xor_sync(FS_FULL, e, o));
+            const float lse = f_add(m, logf(e));
+            const float cpos = f_mul(f_add((float)cell, 0.5f), 32.0f);
+            const float er = erff(f_div(fabsf(f_add(qpos, -cpos)), f_mul(2.0f, sig)));
+            const float ui = f_add(lse, f_mul(f_mul(lam, ceil[cell]), er));
+            if (lane == i) u = ui;
+        }
+        int rank = 0;
+#pragma unroll 8
+        for (int o = 0; o < 32; ++o) {
+            const float uo = __shfl_sync(FS_FULL, u, o);
+            rank += (uo > u || (uo == u && o < lane)) ? 1 : 0;
+        }
+        if (rank < a.read_top) a.sel[row * a.read_top + rank] = (u == -INFINITY) ? -1 : cand;
+    }
+}
+
+template <int D>
+__global__ void fsb_spine_kernel(fsattn_fsb_forest_t F, int n_visible, float* spine, int* hdr) {
+    const int t = blockIdx.x, lane = threadIdx.x;
+    __shared__ SpineSm<D> S;
+    for (int i = lane; i < SPW * (D + 8); i += 32) (&S.node[0][0])[i] = 0.f;
+    __syncwarp();
+    const int m_b = count_below(F.adm + (int64_t)t * F.m_cap, F.m_tot[t], n_visible);
+    build_spine<D>(F, t, m_b, S, lane);
+    __syncwarp();
+    float* dst = spine + (int64_t)t * SPW * (D + 8);
+    for (int i = lane; i < SPW * (D + 8); i += 32) dst[i] = (&S.node[0][0])[i];
+    if (lane == 0) {
+        hdr[t * 4 + 0] = S.root; hdr[t * 4 + 1] = S.height; hdr[t * 4 + 2] = S.m_b; hdr[t * 4 + 3] = 0;
+    }
+}
+
+}  // namespace
+
+int fs_fsb_check_forest(const fsattn_fsb_forest_t& f, const char* what);
+
+extern "C" int fsattn_fsb_spines(const fsattn_fsb_forest_t* forests, int32_t n_forests, int32_t n_visible,
+                                 float* const* spine, int32_t* const* hdr, fsattn_stream_t stream) {
+    FS_REQUIRE(forests && spine && hdr && n_forests >= 1, "fsb_spines: null argument");
+    for (int i = 0; i < n_forests; ++i) {
+        const fsattn_fsb_forest_t& F = forests[i];
+        int rc = fs_fsb_check_forest(F, "fsb_spines");
+        if (rc != FSATTN_OK) return rc;
+        FS_REQUIRE(spine[i] && hdr[i] && n_visible >= 0, "fsb_spines: null output");
+        cudaStream_t st = (cudaStream_t)stream;
+        switch (F.D) {
+            case 64: fsb_spine_kernel<64><<<F.T, 32, 0, st>>>(F, n_visible, spine[i], hdr[i]); break;
+            case 96: fsb_spine_kernel<96><<<F.T, 32, 0, st>>>(F, n_visible, spine[i], hdr[i]); break;
+            default: fsb_spine_kernel<128><<<F.T, 32, 0, st>>>(F, n_visible, spine[i], hdr[i]); break;
+        }
+        rc = fs_check_launch("fsb_spine_kernel");
+        if (rc != FSATTN_OK) return rc;
+    }
+    return FSATTN_OK;
+}
+
+extern "C" int fsattn_fsb_select(const fsattn_fsb_select_t* a, fsattn_stream_t stream) {
+    FS_REQUIRE(a, "fsb_select: null argument");
+    int rc = fs_fsb_check_forest(a->main, "fsb_select(main)");
+    if (rc != FSATTN_OK) return rc;
+    rc = fs_fsb_check_forest(a->second, "fsb_select(second)");
+    if (rc != FSATTN_OK) return rc;
+    FS_REQUIRE(a->main.T == a->second.T && a->main.D == a->second.D, "fsb_select: the two forests share T and D");
+    FS_REQUIRE(a->B > 0 && a->main.T % a->B == 0, "fsb_select: B = %d does not divide T = %d", a->B, a->main.T);
+    FS_REQUIRE(a->q.ptr && a->sel && a->lam && a->sigma, "fsb_select: null q / sel / lam / sigma");
+    FS_REQUIRE(a->k.ptr || (a->kq && a->ks), "fsb_select: token keys missing (bf16 k, or int8 kq + scales ks)");
+    FS_UNSUPPORTED(a->width < 1 || a->width > WMAX || a->width2 < 0 || a->width2 > WMAX,
+                   "fsb_select: beam widths %d / %d (1..16 and 0..16)", a->width, a->width2);
+    FS_REQUIRE(a->read_top >= 1 && a->read_top <= 32, "fsb_select: read_top = %d", a->read_top);
+    FS_REQUIRE(a->Bq >= 1 && a->N >= 1, "fsb_select: N = %d, Bq = %d", a->N, a->Bq);
+    if (a->use_spines) {
+        FS_REQUIRE(a->spine[0] && a->hdr[0] && a->pos && (a->width2 == 0 || (a->spine[1] && a->hdr[1])),
+                   "fsb_select: decode needs the spines, their headers and pos");
+        FS_REQUIRE(a->N == 1 && a->Bq == 1, "fsb_select: decode takes one query per row (N = Bq = 1)");
+    } else {
+        FS_REQUIRE((a->q_pos0 % 32) == 0 && ((a->Bq % 32) == 0 || a->N <= a->Bq),
+                   "fsb_select: q_pos0 and Bq must be multiples of the cell (Bq may be ragged for a single block)");
+    }
+    SelArgs A;
+    A.a = *a;
+    A.H = a->main.T / a->B;
+    A.ncell_k = 0;
+    const int nb = (a->N + a->Bq - 1) / a->Bq;
+    cudaStream_t st = (cudaStream_t)stream;
+    dim3 grid(nb, a->main.T);
+    if (a->use_spines) {
+        switch (a->main.D) {
+            case 64: fsb_select_kernel<64, 2><<<grid, 64, 0, st>>>(A); break;
+            case 96: fsb_select_kernel<96, 2><<<grid, 64, 0, st>>>(A); break;
+            default: fsb_select_kernel<128, 2><<<grid, 64, 0, st>>>(A); break;
+        }
+    } else {
+        switch (a->main.D) {
+            case 64: fsb_select_kernel<64, 8><<<grid, 256, 0, st>>>(A); break;
+            case 96: fsb_select_kernel<96, 8><<<grid, 256, 0, st>>>(A); break;
+            default: fsb_select_kernel<128, 8><<<grid, 256, 0, st>>>(A); break;
+        }
+    }
+    return fs_check_launch("fsb_select_kernel");
+}

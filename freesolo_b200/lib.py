@@ -123,7 +123,26 @@ class TrunkGemv(C.Structure):
 
 
 EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU = 0, 1, 2
-EXTRA_STRUCTS = {"fsattn_trunk_gemv_t": TrunkGemv}
+class FsbForest(C.Structure):
+    _fields_ = [("T", i32), ("H", i32), ("D", i32), ("m_cap", i32),
+                ("kbar", vp), ("kbar_st", i64), ("ceil", vp), ("ceil_st", i64), ("tau", vp),
+                ("adm", vp), ("m_tot", vp), ("m_prev", vp),
+                ("node_mu", vp), ("node_aux", vp), ("root32", vp)]
+
+
+class FsbSelect(C.Structure):
+    _fields_ = [("main", FsbForest), ("second", FsbForest), ("q", BHND), ("k", BHND),
+                ("kq", vp), ("ks", vp), ("kq_sb", i64), ("kq_sh", i64), ("ks_sb", i64), ("ks_sh", i64),
+                ("lam", vp), ("sigma", vp), ("scale", f32), ("radius_coef", f32),
+                ("B", i32), ("N", i32), ("q_pos0", i32), ("Bq", i32), ("width", i32), ("width2", i32), ("read_top", i32),
+                ("use_spines", i32), ("spine", vp * 2), ("hdr", vp * 2), ("pos", vp),
+                ("sel", vp), ("cand", vp), ("nvis", vp)]
+
+
+FSB_SPINE_MAX = 20
+FSB_MAX_MCAP = 8192
+
+EXTRA_STRUCTS = {"fsattn_trunk_gemv_t": TrunkGemv, "fsattn_fsb_forest_t": FsbForest, "fsattn_fsb_select_t": FsbSelect}
 
 # every exported symbol of include/fsattn_b200.h with its argument struct (None = no struct argument)
 ENTRY_POINTS = {
@@ -140,6 +159,10 @@ ENTRY_POINTS = {
     "fsattn_fsl_decode_step": FslDecode,
     "fsattn_slot_prefill": SlotPrefill,
     "fsattn_trunk_gemv": TrunkGemv,
+    "fsattn_fsb_scratch_floats": ([i32, i32, i32], i64),
+    "fsattn_fsb_ingest": ([C.POINTER(FsbForest), i32, i32, i32, vp, i64, vp], C.c_int),
+    "fsattn_fsb_spines": ([C.POINTER(FsbForest), i32, i32, C.POINTER(vp), C.POINTER(vp), vp], C.c_int),
+    "fsattn_fsb_select": FsbSelect,
 }
 
 _lib = None
@@ -160,7 +183,9 @@ def load() -> C.CDLL:
         lib.fsattn_init.restype = C.c_int
         for name, st in ENTRY_POINTS.items():
             fn = getattr(lib, name)         # AttributeError here = header and library disagree
-            if st is not None:
+            if isinstance(st, tuple):       # (argtypes, restype): entry points that do not take one struct
+                fn.argtypes, fn.restype = st
+            elif st is not None:
                 fn.argtypes = [C.POINTER(st), vp]
                 fn.restype = C.c_int
         _lib = lib

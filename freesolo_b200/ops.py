@@ -435,3 +435,138 @@ def trunk_gemv(x, w, *, norm_w=None, eps: float = 1e-6, res=None, swiglu: bool =
 
 def default_scale(D: int) -> float:
     return 1.0 / math.sqrt(D)
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# FS-B: forests, spines, beam + re-rank selection
+# ---------------------------------------------------------------------------------------------------------------------
+_FSB_SCRATCH = {}
+
+
+def _fsb_scratch(device, floats: int) -> torch.Tensor:
+    """Build scratch shared by every layer of a device (layers run one after another on one stream)."""
+    key = (device.type, device.index)
+    buf = _FSB_SCRATCH.get(key)
+    if buf is None or buf.numel() < floats:
+        buf = torch.empty(max(floats, 1), dtype=torch.float32, device=device)
+        _FSB_SCRATCH[key] = buf
+    return buf
+
+
+class FsbForests:
+    """Device buffers of one layer's FS-B forests (fsattn_fsb_forest_t in include/fsattn_b200.h): the main forest
+    (admission tau) and, when tau_u is given, the second beam's forest (tau_u). kbar (B,H,>=cells,D) fp32 and ceil
+    (B,H,>=cells) fp32 are the layer's cell statistics; the forests read them in place. cap_cells bounds the number
+    of cells ever ingested (rounded up to a power of two)."""
+
+    def __init__(self, kbar, ceil, tau, tau_u=None, *, cap_cells: int):
+        _need_cuda(kbar, ceil)
+        B, H, _, D = kbar.shape
+        assert kbar.dtype == torch.float32 and kbar.is_contiguous() and ceil.dtype == torch.float32 and ceil.is_contiguous()
+        self.B, self.H, self.D, self.T = B, H, D, B * H
+        m_cap = 1
+        while m_cap < max(1, int(cap_cells)):
+            m_cap *= 2
+        if m_cap > L.FSB_MAX_MCAP:
+            raise RuntimeError(f"FS-B: {cap_cells} cells per row exceed the supported {L.FSB_MAX_MCAP}")
+        self.m_cap = m_cap
+        self.k_cap = m_cap.bit_length() - 1
+        self.kbar, self.ceil = kbar, ceil
+        dev = kbar.device
+        self.taus = [_f32(tau).to(dev)] + ([_f32(tau_u).to(dev)] if tau_u is not None else [])
+        self.nf = len(self.taus)
+        nodes = (self.k_cap + 1) * m_cap
+        T = self.T
+        self.adm = [torch.full((T, m_cap), -1, dtype=torch.int32, device=dev) for _ in range(self.nf)]
+        self.m_tot = [torch.zeros(T, dtype=torch.int32, device=dev) for _ in range(self.nf)]
+        self.m_prev = [torch.zeros(T, dtype=torch.int32, device=dev) for _ in range(self.nf)]
+        self.node_mu = [torch.zeros(T, nodes, D, dtype=torch.bfloat16, device=dev) for _ in range(self.nf)]
+        self.node_aux = [torch.zeros(T, nodes, 4, dtype=torch.float32, device=dev) for _ in range(self.nf)]
+        self.root32 = [torch.zeros(T, m_cap, D + 4, dtype=torch.float32, device=dev) for _ in range(self.nf)]
+        self.spine = [torch.zeros(T, L.FSB_SPINE_MAX, D + 8, dtype=torch.float32, device=dev) for _ in range(self.nf)]
+        self.hdr = [torch.full((T, 4), -1, dtype=torch.int32, device=dev) for _ in range(self.nf)]
+        self.n_seen = 0
+
+    def nbytes(self) -> int:
+        ts = self.adm + self.m_tot + self.m_prev + self.node_mu + self.node_aux + self.root32 + self.spine + self.hdr
+        return sum(t.numel() * t.element_size() for t in ts)
+
+    def struct(self, i: int) -> L.FsbForest:
+        f = L.FsbForest()
+        f.T, f.H, f.D, f.m_cap = self.T, self.H, self.D, self.m_cap
+        f.kbar, f.kbar_st = self.kbar.data_ptr(), self.kbar.stride(1)
+        f.ceil, f.ceil_st = self.ceil.data_ptr(), self.ceil.stride(1)
+        f.tau = self.taus[i].data_ptr()
+        f.adm, f.m_tot, f.m_prev = self.adm[i].data_ptr(), self.m_tot[i].data_ptr(), self.m_prev[i].data_ptr()
+        f.node_mu, f.node_aux, f.root32 = self.node_mu[i].data_ptr(), self.node_aux[i].data_ptr(), self.root32[i].data_ptr()
+        return f
+
+    def ingest(self, cell_end: int) -> None:
+        """Admit the cells [n_seen, cell_end) and build the chunks they complete (both forests, one set of launches)."""
+        cell_end = int(cell_end)
+        if cell_end <= self.n_seen:
+            return
+        if cell_end > self.m_cap:
+            raise RuntimeError(f"FS-B: cell {cell_end} beyond the forest capacity {self.m_cap}")
+        lib = L.load()
+        floats = lib.fsattn_fsb_scratch_floats(self.m_cap, self.D, self.T) * self.nf
+        scratch = _fsb_scratch(self.kbar.device, floats)
+        arr = (L.FsbForest * self.nf)(*[self.struct(i) for i in range(self.nf)])
+        L.check(lib.fsattn_fsb_ingest(arr, self.nf, self.n_seen, cell_end, scratch.data_ptr(), scratch.numel(),
+                                      _stream(self.kbar)), "fsattn_fsb_ingest")
+        self.n_seen = cell_end
+
+    def build_spines(self, n_visible: int) -> None:
+        """Spines of the prefix of cells [0, n_visible) for decode queries (kept until the next call)."""
+        lib = L.load()
+        arr = (L.FsbForest * self.nf)(*[self.struct(i) for i in range(self.nf)])
+        sp = (L.vp * self.nf)(*[t.data_ptr() for t in self.spine])
+        hd = (L.vp * self.nf)(*[t.data_ptr() for t in self.hdr])
+        L.check(lib.fsattn_fsb_spines(arr, self.nf, int(n_visible), sp, hd, _stream(self.kbar)), "fsattn_fsb_spines")
+
+
+def fsb_select(forests: FsbForests, Q, K, lam, sigma, *, scale: float, N: int = None, q_pos0: int = 0, Bq: int = 128,
+               width: int = 16, width2: int = 16, read_top: int = 4, radius_coef: float = 8.0, pos=None,
+               kq=None, ks=None, debug: bool = False):
+    """FS-B selection. Prefill (pos None): Q (B,H,N,D) bf16 at positions q_pos0.., blocks of Bq -> sel (B,H,nb*Bq,K)
+    int32. Decode (pos = device int64 scalar): Q (B,H,1,D), the spines of forests.build_spines -> sel (B,H,1,K).
+    K: raw bf16 token keys (B,H,>=cells*32,D), or None with the int8 codes kq (B,H,rows,D) and scales ks (B,H,cells).
+    debug=True also returns the candidates (B,H,Npad,width+width2) and the visit counts."""
+    _need_cuda(Q, K, kq, ks)
+    B, H, Nq, D = Q.shape
+    decode = pos is not None
+    N = Nq if N is None else int(N)
+    if decode:
+        N, Bq = 1, 1
+    Bq = min(Bq, N) if not decode else 1
+    nb = (N + Bq - 1) // Bq
+    dev = Q.device
+    sel = torch.empty(B, H, nb * Bq, read_top, dtype=torch.int32, device=dev)
+    cand = torch.empty(B, H, nb * Bq, width + width2, dtype=torch.int32, device=dev) if debug else None
+    nvis = torch.empty(B, H, nb * Bq, dtype=torch.int32, device=dev) if debug else None
+    lam, sigma = _f32(lam).to(dev), _f32(sigma).to(dev)
+    a = L.FsbSelect()
+    a.main = forests.struct(0)
+    a.second = forests.struct(1 if forests.nf > 1 else 0)
+    a.q = _bhnd(Q, "Q")
+    if K is not None:
+        a.k = _bhnd(K, "K")
+    else:
+        a.k = _null()
+        assert kq.dtype == torch.int8 and kq.stride(2) == D and ks.dtype == torch.bfloat16
+        a.kq, a.ks = kq.data_ptr(), ks.data_ptr()
+        a.kq_sb, a.kq_sh, a.ks_sb, a.ks_sh = kq.stride(0), kq.stride(1), ks.stride(0), ks.stride(1)
+    a.lam, a.sigma = lam.data_ptr(), sigma.data_ptr()
+    a.scale, a.radius_coef = float(scale), float(radius_coef)
+    a.B, a.N, a.q_pos0, a.Bq = B, N, int(q_pos0), Bq
+    a.width, a.width2, a.read_top = int(width), int(width2), int(read_top)
+    if decode:
+        a.use_spines = 1
+        j = 1 if forests.nf > 1 else 0
+        a.spine[0], a.spine[1] = forests.spine[0].data_ptr(), forests.spine[j].data_ptr()
+        a.hdr[0], a.hdr[1] = forests.hdr[0].data_ptr(), forests.hdr[j].data_ptr()
+        assert pos.dtype == torch.int64 and pos.is_cuda
+        a.pos = pos.data_ptr()
+    a.sel, a.cand, a.nvis = sel.data_ptr(), _p(cand), _p(nvis)
+    L.call("fsattn_fsb_select", a, _stream(Q))
+    return (sel, cand, nvis) if debug else sel

@@ -249,6 +249,71 @@ typedef struct {
 } fsattn_trunk_gemv_t;
 FSATTN_API int fsattn_trunk_gemv(const fsattn_trunk_gemv_t* a, fsattn_stream_t stream);
 
+/* ---- FS-B: two forests over the admitted cells, beam search, candidate re-rank ------------------------------------------
+ * One fsattn_fsb_forest_t describes ONE forest (admission threshold tau) of one layer for all T = B*H rows.
+ *
+ * Layout (own; the reference's packed arena is fsb_tree.py:1008-1046 and its one-chunk-per-height decode arena
+ * fsb_tree.py:1496-1522). The forest is the binary counter over the admitted-cell sequence (fsb_tree.py:897-911):
+ * chunk (k, j) holds the admitted positions [j 2^k, (j+1) 2^k). Only chunks with EVEN j are ever the root named by a bit
+ * of a prefix length (fsb_tree.py:1092-1098), so only those are stored, each at a fixed place: admitted position p
+ * completes exactly one of them, (k = ctz(p+1), j = ((p+1) >> k) - 1). A chunk is therefore built once, when its last
+ * cell is admitted, and never rebuilt; prefill and the decode-time ingest are the same operation on different ranges.
+ *   node id of node n (level order, children 2n+1 / 2n+2) of chunk (k, j):  nbase(k) + (j/2) (2^{k+1}-1) + n,
+ *   nbase(k) = k m_cap - m_cap + (m_cap >> k);  nodes per row = (k_cap+1) m_cap;  chunk id = m_cap - (m_cap >> k) + j/2.
+ *   node_mu  (T, nodes, D) bf16: the mean the beam scores with;
+ *   node_aux (T, nodes, 4) fp32: radius (inflated by the bf16 rounding error of the mean, fsb_tree.py:1049-1066),
+ *            max ceiling (>= 0), min cell id (int bits), meta (int bits): >= 0 a leaf's cell id, < 0 ~((n << 4) | log2 cnt);
+ *   root32   (T, m_cap, D+4) fp32: each chunk root's exact mean, un-inflated radius (the spines merge these,
+ *            fsb_tree.py:1088-1124), 3 pad words.
+ * adm (T, m_cap) int32 admitted cell ids ascending, m_tot (T), m_prev (T) (m_tot before the last ingest).
+ * kbar (T rows kbar_st floats apart, D per cell) / ceil (T rows ceil_st apart): the cells' statistics (fp32). */
+typedef struct {
+    int32_t T, H, D, m_cap;
+    const float* kbar; int64_t kbar_st;
+    const float* ceil; int64_t ceil_st;
+    const float* tau;                  /* (H) admission threshold per head */
+    int32_t* adm; int32_t* m_tot; int32_t* m_prev;
+    void* node_mu; float* node_aux; float* root32;
+} fsattn_fsb_forest_t;
+
+/* Admit the cells [cell_begin, cell_end) of every row (ceil >= tau[h], fsb_tree.py:936-941, 1465-1494) into each of
+ * the n_forests (<= 4) forests and build every chunk the newly admitted positions complete. Replaces build_forest
+ * (fsb_tree.py:932-951, build_trees 616-678, GPU fsb_build.cu) and ForestCache.ingest's carry-chain rebuild
+ * (fsb_tree.py:2033-2049). Chunk trees are bit-identical to the reference's CPU trees: every sum runs in the halving
+ * order of det_reduce.det_sum and no multiply-add is contracted. scratch: fsattn_fsb_scratch_floats(m_cap, D, T) floats
+ * per forest, used only during the call. */
+FSATTN_API int64_t fsattn_fsb_scratch_floats(int32_t m_cap, int32_t D, int32_t T);
+FSATTN_API int fsattn_fsb_ingest(const fsattn_fsb_forest_t* forests, int32_t n_forests, int32_t cell_begin,
+                                 int32_t cell_end, float* scratch, int64_t scratch_floats, fsattn_stream_t stream);
+
+/* Spines (fsb_tree.py:1070-1132): per forest and row, the nodes that merge the chunk roots named by the bits of
+ * m_b = #admitted cells with id < n_visible. spine (T, FSATTN_FSB_SPINE_MAX, D+8) fp32 per forest:
+ * [mu (D) | rad, amax, pmin(int), cnt(int), child_l(int), child_r(int), pad, pad]; hdr (T, 4) int32: root ref, height,
+ * m_b, 0. Node refs: >= 0 a node id of the row's arena, -(k+2) the spine node of height k, -1 none. */
+#define FSATTN_FSB_SPINE_MAX 20
+FSATTN_API int fsattn_fsb_spines(const fsattn_fsb_forest_t* forests, int32_t n_forests, int32_t n_visible,
+                                 float* const* spine, int32_t* const* hdr, fsattn_stream_t stream);
+
+/* Selection for queries. Replaces traverse_forest in the serve configuration (fsb_tree.py:1183-1317: fixed policy,
+ * delta 0, 'bound' node score, second beam, token-LSE re-rank 'lse_pos' with the raw query, read_top): both beams
+ * (_forest_beam 1321-1400; fsb_beam.cu / fsb_fast_step.py kernels), union_candidates (711-713), rerank_top (820-869,
+ * fsb_rerank.py:83-125). main / second: the two forests (second may equal main).
+ * Prefill (n_q > 1): q (B,H,N,D) bf16, queries q_pos0 .. q_pos0+N-1 in blocks of Bq; block b sees the cells
+ * [0, (q_pos0 + b Bq) / 32); spines are built on the fly. Decode (use_spines = 1): one query per row at *pos with the
+ * spines of fsattn_fsb_spines. k: raw token keys (B,H,>=cells*32,D) bf16, or int8 codes + scales (kq/ks) when k.ptr is NULL.
+ * sel (B,H,Npad,K) int32 (-1 pad). Optional outputs for tests: cand (B,H,Npad,W_main+W_second) int32, nvis (B,H,Npad). */
+typedef struct {
+    fsattn_fsb_forest_t main, second;
+    fsattn_bhnd_t q, k;
+    const int8_t* kq; const void* ks; int64_t kq_sb, kq_sh, ks_sb, ks_sh;
+    const float* lam; const float* sigma;
+    float scale, radius_coef;
+    int32_t B, N, q_pos0, Bq, width, width2, read_top;
+    int32_t use_spines; const float* spine[2]; const int32_t* hdr[2]; const int64_t* pos;
+    int32_t* sel; int32_t* cand; int32_t* nvis;
+} fsattn_fsb_select_t;
+FSATTN_API int fsattn_fsb_select(const fsattn_fsb_select_t* a, fsattn_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -40,12 +40,21 @@ def det_sum(x: torch.Tensor, dim: int) -> torch.Tensor:
     return x[..., 0]
 
 
+def ieee_sqrt(x: torch.Tensor) -> torch.Tensor:
+    """Correctly rounded fp32 square root. torch's vectorised CPU sqrt is not (it is off by one ulp for about 5% of
+    inputs on AVX2 hosts, measured against numpy and float64), while CUDA's sqrtf and numpy's are; the restatement
+    uses the IEEE result so that it does not depend on the host CPU. The reference's CPU fixtures therefore match radii
+    to one ulp only."""
+    import numpy as np
+    return torch.from_numpy(np.asarray(np.sqrt(x.detach().contiguous().numpy()), dtype=np.float32)).reshape(x.shape)
+
+
 def det_dot(a, b):
     return det_sum(a * b, -1)
 
 
 def det_norm(a):
-    return det_sum(a * a, -1).sqrt()
+    return ieee_sqrt(det_sum(a * a, -1))
 
 
 # ---------------------------------------------------------------------------------------------------------------
@@ -80,7 +89,7 @@ def chunk_trees(X: torch.Tensor, ce: torch.Tensor, ids: torch.Tensor) -> dict:
         Xc = Xn - mu[:, :, None, :]
         d2 = det_sum(Xc * Xc, -1)
         mu_l.append(mu)
-        rad_l.append(d2.amax(-1).sqrt())
+        rad_l.append(ieee_sqrt(d2.amax(-1)))
         am_l.append(torch.gather(ce, 1, order).view(C, nodes, m).amax(-1).clamp(min=0.0))
         pm_l.append(torch.gather(ids, 1, order).view(C, nodes, m).amin(-1))
         if l == k:
@@ -119,7 +128,7 @@ def beam_tables(F: dict) -> None:
     for t in F["chunks"].values():
         mu16 = t["mu"].to(torch.bfloat16)
         t["mu16"] = mu16
-        t["rad_b"] = t["rad"] + (t["mu"] - mu16.float()).norm(dim=-1)
+        t["rad_b"] = t["rad"] + det_norm(t["mu"] - mu16.float())
 
 
 def flatten_row(F: dict, D: int) -> dict:
@@ -227,6 +236,7 @@ def beam_row(tab: dict, root: int, q: torch.Tensor, qpos: torch.Tensor, lam: flo
     qn = det_norm(q) * rc
     nvis = torch.zeros(Bq)
     slot = torch.arange(W_max)
+    margin = torch.full((Bq,), float("inf"))      # smallest score gap at a frontier cut-off (test bookkeeping)
     for _ in range(iters):
         act = ref >= 0
         rc_ = ref.clamp(min=0)
@@ -247,8 +257,14 @@ def beam_row(tab: dict, root: int, q: torch.Tensor, qpos: torch.Tensor, lam: flo
         ok = (tv > NEG / 2) & (slot[None] < W)
         ref = torch.gather(cand, 1, ti).masked_fill(~ok, -1)
         nvis = nvis + (ch >= 0).sum(-1).float()
+        sv = torch.sort(score, dim=-1, descending=True).values
+        nk = (W - carried.sum(-1)).clamp(min=0)
+        cut = (nk > 0) & (nk < (ch >= 0).sum(-1))
+        i1 = nk.clamp(min=1, max=2 * W_max - 1)
+        gap = sv.gather(1, (i1 - 1)[:, None])[:, 0] - sv.gather(1, i1[:, None])[:, 0]
+        margin = torch.where(cut, torch.minimum(margin, gap), margin)
     cells = torch.where(ref >= 0, tab["cell"][ref.clamp(min=0)], torch.full_like(ref, -1))
-    return cells, nvis
+    return cells, nvis, margin
 
 
 def union_candidates(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
@@ -329,19 +345,21 @@ def select_block(rf: RowForests, E: int, q, qpos, lam, sig, scale, s, ceil_row, 
                                      (rf.Fu, rf.flatu, m_bu, cfg["union_width"], cfg["union_W_max"])):
         sp = spine(F, flat, mb, rf.D)
         if sp["root"] < 0:
-            outs.append((torch.full((Bq, wmax), -1, dtype=torch.long), torch.zeros(Bq), sp))
+            outs.append((torch.full((Bq, wmax), -1, dtype=torch.long), torch.zeros(Bq), sp,
+                         torch.full((Bq,), float("inf"))))
             continue
         W, budget = beam_policy(sp["height"], width, cfg["delta"])
         tab = row_tables(flat, sp, rf.D)
-        cells, nv = beam_row(tab, sp["root"], q, qpos, lam, sig, scale, s, W, budget, wmax, cfg["rc"],
-                             sp["height"] + 1)
-        outs.append((cells, nv, sp))
+        cells, nv, bm = beam_row(tab, sp["root"], q, qpos, lam, sig, scale, s, W, budget, wmax, cfg["rc"],
+                                 sp["height"] + 1)
+        outs.append((cells, nv, sp, bm))
     cand = union_candidates(outs[0][0], outs[1][0])
     u = rerank_scores(cand, q, qpos, lam, sig, ceil_row, Ktok, scale, s)
     sel, margin = rerank_top(cand, u, cfg["read_top"])
     if want is not None:
         want.update(main=outs[0][0], union=outs[1][0], nvis=outs[0][1] + outs[1][1], cand=cand, u=u,
-                    height=(outs[0][2]["height"], outs[1][2]["height"]), m_b=(m_b, m_bu))
+                    height=(outs[0][2]["height"], outs[1][2]["height"]), m_b=(m_b, m_bu),
+                    beam_margin=torch.minimum(outs[0][3], outs[1][3]))
     return sel, margin
 
 

@@ -17,7 +17,7 @@ HEADER = os.path.join(ROOT, "include", "fsattn_b200.h")
 
 def _declared():
     src = open(HEADER).read()
-    return sorted(set(re.findall(r"^\s*FSATTN_API\s+(?:int|const char\*)\s+(fsattn_\w+)\s*\(", src, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*FSATTN_API\s+(?:int|int64_t|const char\*)\s+(fsattn_\w+)\s*\(", src, flags=re.M)))
 
 
 def test_every_declared_symbol_is_exported_and_bound(built_lib):
