@@ -557,7 +557,8 @@ __global__ void __launch_bounds__(NWARP * 32) fsl_decode_kernel(const fsattn_fsl
     const bool pos_ok = pos >= 0 && pos < st.cap_rows;
     const int blk_start = (int)((pos / st.Bq) * st.Bq);
     int pool_blk = 0;
-    if (rank == 0) {
+    const bool ext = a.ext_sel != nullptr;      // selections come from another kernel (FS-B): no pool, no scoring here
+    if (rank == 0 && !ext) {
         if (tid == 0) {
             sm.pool_timeout = 0;
             mbar_init(&sm.pool_bar, 1);
@@ -589,7 +590,7 @@ __global__ void __launch_bounds__(NWARP * 32) fsl_decode_kernel(const fsattn_fsl
     const bool do_window = (S == 1) || (rank > 0);
     RowFlight<D> wf[WIN_NF];
     if (do_window) window_issue2<D>(wf, w, a, hp, w.g_lo + w.gw, lane);
-    if (rank == 0) {
+    if (rank == 0 && !ext) {
         // the pool's bulk copy; the wait is bounded. The position priors of the candidates need no query: compute them now.
         if (!mbar_wait_bounded(&sm.pool_bar, 0, 1 << 22)) {
             if (lane == 0) { atomicAdd(st.status + FSATTN_ST_BAD_INDEX, 1); sm.pool_timeout = 1; }
@@ -633,7 +634,7 @@ __global__ void __launch_bounds__(NWARP * 32) fsl_decode_kernel(const fsattn_fsl
     float lr_l = 0.0f;
     if (rank == 0) {
         if (warp == NWARP - 1 && pos_ok) append_and_close<D>(st, hp, pos, k_in, v_in, lane);
-        if (pool_blk != blk_start) {               // CTA-uniform, once per Bq tokens
+        if (!ext && pool_blk != blk_start) {       // CTA-uniform, once per Bq tokens
             refresh_pool<D>(sm, st, hp, bh, blk_start, tid, pool_s, meta_s);
             for (int t = tid; t < C; t += blockDim.x) {
                 const int4 mt = meta_s[t];
@@ -642,6 +643,16 @@ __global__ void __launch_bounds__(NWARP * 32) fsl_decode_kernel(const fsattn_fsl
             __syncthreads();
         }
         STAMP(0, 3);
+        if (ext) {
+            // the selected cells were chosen by the FS-B selection kernel that ran before this one; full stores only
+            if (tid < st.kk) {
+                const int cell = a.ext_sel[(int64_t)bh * st.kk + tid];
+                const bool okc = cell >= 0 && (int64_t)(cell + 1) * FSATTN_CELL <= pos;
+                sm.selcell[tid] = okc ? cell : -1;
+                sm.selrow[tid] = okc ? cell : -1;
+                if (a.sel_out != nullptr) a.sel_out[(int64_t)bh * st.kk + tid] = okc ? cell : -1;
+            }
+        } else
         // ---- scores: 8 lanes per candidate, mean keys from shared memory ---------------------------------------------------
         {
             float qv[F];
@@ -678,7 +689,7 @@ __global__ void __launch_bounds__(NWARP * 32) fsl_decode_kernel(const fsattn_fsl
         STAMP(0, 4);
 
         // ---- top-kk by (score desc, slot asc): warp 0 ---------------------------------------------------------------------------------
-        if (warp == 0) {
+        if (warp == 0 && !ext) {
             float sv[SC_ITERS];
 #pragma unroll
             for (int j = 0; j < SC_ITERS; j++) { const int t = lane + 32 * j; sv[j] = (t < C) ? sm.score[t] : -INFINITY; }
@@ -858,6 +869,8 @@ extern "C" int fsattn_fsl_decode_step(const fsattn_fsl_decode_t* a, fsattn_strea
     }
     if (st.store_mode == 2)
         FS_REQUIRE(st.slot_of && st.cell_in && st.n_slots > 0, "fsl_decode_step: bounded store without slot tables");
+    FS_UNSUPPORTED(a->ext_sel != nullptr && st.store_mode == 2,
+                   "fsl_decode_step: external (FS-B) selections need a full KV store, not the bounded slot store");
     FS_REQUIRE(((uintptr_t)a->q & 15) == 0 && ((uintptr_t)a->k & 15) == 0 && ((uintptr_t)a->v & 15) == 0 && a->in_sb % 8 == 0 && a->in_sh % 8 == 0,
                "fsl_decode_step: q/k/v must be 16-byte aligned");
     FS_REQUIRE(((uintptr_t)st.kbar & 15) == 0 && st.kbar_sb % 4 == 0 && st.kbar_sh % 4 == 0, "fsl_decode_step: kbar must be 16-byte aligned");

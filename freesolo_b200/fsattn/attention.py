@@ -133,6 +133,7 @@ class FSAttn(nn.Module):
         self.fs_fused_attn = kwargs.get("fs_fused_attn", None)
         self.cell_fused_select = kwargs.get("cell_fused_select", None)
         self.fsb_enabled = bool(kwargs.get("fsb_enabled", False))
+        self._fsb_init(n_heads, kwargs)
         self.decode_splits = int(kwargs.get("decode_splits", os.environ.get("FSATTN_DECODE_SPLITS", "4")))
         if dropout != 0.0:
             raise NotImplementedError("inference only: dropout must be 0")
@@ -156,6 +157,60 @@ class FSAttn(nn.Module):
         self.dropout = nn.Dropout(dropout)
         self._last_sel = None          # selections of the last call when FSATTN_KEEP_SEL=1 (tests, diagnostics)
         self._last_margin = None
+
+    def _fsb_init(self, n_heads: int, kw: dict):
+        """The FS-B keywords of the reference layer (src/fsattn/fsb_tree.py:41-135, 136-155). Only the released serve
+        configuration is built: fixed policy, delta 0, 'bound' node score, forest, token-LSE re-rank with the raw query,
+        optional second beam and second forest. Anything else is refused at construction, as the reference refuses its
+        own inconsistent combinations."""
+        self.fsb_width = int(kw.get("fsb_width", 16))
+        self.fsb_delta = int(kw.get("fsb_delta", 0))
+        self.fsb_node_score = kw.get("fsb_node_score", "bound")
+        self.fsb_bound_radius_coef = float(kw.get("fsb_bound_radius_coef", 8.0))
+        self.fsb_tree = kw.get("fsb_tree", "forest")
+        self.fsb_read_top = int(kw.get("fsb_read_top", 4))
+        self.fsb_rerank_score = kw.get("fsb_rerank_score", "lse_pos")
+        self.fsb_rerank_query = kw.get("fsb_rerank_query", "raw")
+        self.fsb_union_width = int(kw.get("fsb_union_width", 0) or 0)
+        self.fsb_union_tau_quantile = float(kw.get("fsb_union_tau_quantile", 0.0) or 0.0)
+        self.fsb_policy_mode = kw.get("fsb_policy", "fixed") or "fixed"
+        self.fsb_W_max = 16
+        self.fsb_union_W_max = 16
+        self.fsb_kk = self.fsb_read_top
+        self.register_buffer("fsb_tau", torch.zeros(n_heads), persistent=True)
+        self.register_buffer("fsb_tau_union", torch.zeros(n_heads), persistent=False)
+        if not self.fsb_enabled:
+            return
+        bad = []
+        if self.fsb_policy_mode != "fixed": bad.append(f"fsb_policy={self.fsb_policy_mode!r} (fixed)")
+        if self.fsb_delta != 0: bad.append(f"fsb_delta={self.fsb_delta} (0)")
+        if self.fsb_node_score != "bound": bad.append(f"fsb_node_score={self.fsb_node_score!r} ('bound')")
+        if self.fsb_tree != "forest": bad.append(f"fsb_tree={self.fsb_tree!r} ('forest')")
+        if self.fsb_rerank_score != "lse_pos" or self.fsb_rerank_query != "raw":
+            bad.append("re-rank other than fsb_rerank_score='lse_pos' with fsb_rerank_query='raw'")
+        if not 1 <= self.fsb_width <= 16 or not 0 <= self.fsb_union_width <= 16:
+            bad.append(f"beam widths {self.fsb_width}/{self.fsb_union_width} (1..16 / 0..16)")
+        if not 1 <= self.fsb_read_top <= 8 or self.fsb_read_top != self.cell_topk:
+            bad.append(f"fsb_read_top={self.fsb_read_top} (must equal cell_topk={self.cell_topk}, at most 8)")
+        if not 0 <= self.fsb_union_tau_quantile < 1:
+            bad.append(f"fsb_union_tau_quantile={self.fsb_union_tau_quantile} (0 = off, else in (0, 1))")
+        if self.fsb_union_tau_quantile > 0 and self.fsb_union_width <= 0:
+            bad.append("fsb_union_tau_quantile needs fsb_union_width > 0")
+        for k in ("fsb_hybrid", "fsb_beam_quota", "fsb_union_quota", "fsb_read_margin", "fsb_route_adapter", "fsb_rerank_rr",
+                  "fsb_leaf_radius"):
+            if kw.get(k) not in (None, 0, 0.0, "off", "none", False):
+                bad.append(f"{k}={kw[k]!r}")
+        if bad:
+            raise NotImplementedError("FS-B: only the released serve configuration is implemented; got " + "; ".join(bad))
+
+    def _fsb_union_tau_on(self) -> bool:
+        return self.fsb_union_tau_quantile > 0
+
+    def _fsb_w2(self, fo) -> int:
+        """Width of the second beam. Without a second forest the reference runs it over the main forest, where it finds
+        the main beam's cells again and union_candidates blanks every one of them (src/fsattn/fsb_tree.py:1226-1231,
+        711-713): the selection is the same without it, so it is not launched."""
+        return self.fsb_union_width if fo.nf > 1 else 0
 
     # ---- configuration helpers (same names as the reference) ---------------------------------------------------------
     @property
@@ -187,9 +242,7 @@ class FSAttn(nn.Module):
             raise NotImplementedError("sel_content_only is not implemented")
         if self.cell_stride != ops.CELL:
             raise NotImplementedError(f"cell_stride {self.cell_stride}: the kernels are specialised for {ops.CELL}")
-        if self.fsb_enabled:
-            raise NotImplementedError("FS-B layers use freesolo_b200.fsattn.fsb (not built into this layer yet)")
-        if self._is_dense_lr():
+        if self._is_dense_lr() and not self.fsb_enabled:
             raise NotImplementedError("the dense FS variant (cell_prune_kernel=0) is not implemented")
 
     def _pool_cfg(self):
@@ -274,6 +327,15 @@ class FSAttn(nn.Module):
             # nothing completed: every selection is empty; the readout still applies the combine (lr = 0)
             sel = torch.full((B, H, nb * Bq, kk), -1, dtype=torch.int32, device=Q.device)
             margin = None
+        elif self.fsb_enabled:
+            # src/fsattn/fsb_tree.py:2368-2520: both forests over the prompt's cells, then per 128-query block the two
+            # beams, the union of their candidates and the token-level re-rank
+            fo = cache.fsb_forests(kbar, ceil, self)
+            fo.ingest(ncell)
+            sel = ops.fsb_select(fo, Q, K, lam, sigma, scale=self.scale, N=N, Bq=Bq, width=self.fsb_width,
+                                 width2=self._fsb_w2(fo), read_top=self.fsb_read_top,
+                                 radius_coef=self.fsb_bound_radius_coef)
+            margin = None
         else:
             st = cache.state
             topp = getattr(st, "prefill_topp", None) if st is not None else None
@@ -305,10 +367,27 @@ class FSAttn(nn.Module):
         if os.environ.get("FSATTN_KEEP_SEL", "0") == "1":
             sel_out = torch.empty(st.B, st.H, st.kk, dtype=torch.int32, device=q.device)
             self._last_sel = sel_out
+        ext = None
+        if self.fsb_enabled:
+            cache.fsb_block_change(cache.pos, self)
+            ext = self._fsb_decode_select(q, st, cache, pos_t, lam, sigma)
         y = ops.fsl_decode_step(st, q, k, v, pos_t, cos, sin, lam, sigma, lrs, norm_w, scale=self.scale,
-                                eps=self.lr_norm.eps, y=y, sel_out=sel_out, splits=self.decode_splits)
+                                eps=self.lr_norm.eps, y=y, sel_out=sel_out, splits=self.decode_splits, ext_sel=ext)
         cache.advance_in_place()
         return y
+
+    def _fsb_decode_select(self, q, st, cache, pos_t, lam, sigma):
+        """src/fsattn/fsb_tree.py:2909-3064: the decode query's two beams over the block's forests, union, re-rank with
+        the token keys as the cache reads them (raw bf16, or the int8 codes). q (B,H,D) view -> (B,H,1,kk) int32."""
+        fo = cache.fsb
+        q4 = q.unsqueeze(2)
+        if st.mode == "bf16":
+            return ops.fsb_select(fo, q4, st.kbuf, lam, sigma, scale=self.scale, width=self.fsb_width,
+                                  width2=self._fsb_w2(fo), read_top=self.fsb_read_top,
+                                  radius_coef=self.fsb_bound_radius_coef, pos=pos_t)
+        return ops.fsb_select(fo, q4, None, lam, sigma, scale=self.scale, width=self.fsb_width,
+                              width2=self._fsb_w2(fo), read_top=self.fsb_read_top,
+                              radius_coef=self.fsb_bound_radius_coef, pos=pos_t, kq=st.kq, ks=st.ks)
 
     def graph_decode_layer(self, x, buf):
         """One decode token inside a captured whole-step graph (src/fsattn/attention.py:1493-1559): x (B,1,d); buf holds
@@ -322,8 +401,10 @@ class FSAttn(nn.Module):
         st = cache.decode_state(qkv)
         cos, sin = self.rope.tables_bf16(st.cap_rows)
         lam, sigma, lrs, norm_w = self.head_params()
+        ext = self._fsb_decode_select(qkv[:, 0], st, cache, buf["pos_t"], lam, sigma) if self.fsb_enabled else None
         y = ops.fsl_decode_step(st, qkv[:, 0], qkv[:, 1], qkv[:, 2], buf["pos_t"], cos, sin, lam, sigma, lrs, norm_w,
-                                scale=self.scale, eps=self.lr_norm.eps, y=buf.get("y"), splits=self.decode_splits)
+                                scale=self.scale, eps=self.lr_norm.eps, y=buf.get("y"), splits=self.decode_splits,
+                                ext_sel=ext)
         return self.W_o(y.view(B, 1, dm))
 
     def graph_decode_attn(self, qkv, buf, y=None, pdl=True):
@@ -335,5 +416,11 @@ class FSAttn(nn.Module):
         st = buf["cache"].decode_state(q4)
         cos, sin = self.rope.tables_bf16(st.cap_rows)
         lam, sigma, lrs, norm_w = self.head_params()
+        ext = None
+        if self.fsb_enabled:
+            # the selection kernel reads q, so it waits for the projection like any dependent launch; the decode kernel
+            # then depends on it through ext_sel
+            ext = self._fsb_decode_select(q4[:, 0], st, buf["cache"], buf["pos_t"], lam, sigma)
         return ops.fsl_decode_step(st, q4[:, 0], q4[:, 1], q4[:, 2], buf["pos_t"], cos, sin, lam, sigma, lrs, norm_w,
-                                   scale=self.scale, eps=self.lr_norm.eps, y=y, splits=self.decode_splits, pdl=pdl)
+                                   scale=self.scale, eps=self.lr_norm.eps, y=y, splits=self.decode_splits,
+                                   pdl=pdl and ext is None, ext_sel=ext)

@@ -102,6 +102,40 @@ class FSKVCache:
         self.pos_t = torch.full((), N, dtype=torch.int64, device=K.device)
         return kbar, ceil
 
+    # ---- FS-B forests (src/fsattn/fsb_tree.py:1403-2260 ForestCache, 3598-3674 fsb_decode_prepare) --------------------------
+    def fsb_forests(self, kbar, ceil, attn):
+        """The layer's forests, created on first use over the cache's own statistics buffers (so the decode-time ingest
+        sees the cells the decode kernel closes) or, when the prompt's K/V are not retained, over the given tensors."""
+        if self.bounded_kv:
+            raise NotImplementedError("FS-B reads any admitted cell: it needs a full KV store, not the bounded slot store")
+        if self.state is not None:
+            kb, ce, cap = self.state.kbar, self.state.ceil, self.state.cap_cells
+        else:
+            kb, ce, cap = kbar.contiguous(), ceil.contiguous(), kbar.shape[2]
+        fo = getattr(self, "fsb", None)
+        if fo is None or fo.kbar.data_ptr() != kb.data_ptr() or fo.m_cap < cap:
+            tau_u = attn.fsb_tau_union if attn._fsb_union_tau_on() else None
+            fo = ops.FsbForests(kb, ce, attn.fsb_tau, tau_u, cap_cells=cap)
+            self.fsb = fo
+            self._fsb_blk = -1
+        return fo
+
+    def fsb_block_change(self, pos: int, attn) -> bool:
+        """Bring the forests to the 128-token block of position pos: admit the cells completed before the block starts,
+        build the chunks they complete, rebuild the spines. Happens once per block, on the host's side of the step
+        (the reference does the same between graph replays, fsb_tree.py:3634-3660). Returns whether anything ran."""
+        blk = (pos // attn._cell_block) * attn._cell_block
+        if getattr(self, "_fsb_blk", -1) == blk and getattr(self, "fsb", None) is not None:
+            return False
+        if self.state is None:
+            raise RuntimeError("FS-B decode needs the device KV state (prefill with retain_kv=True, or decode from empty)")
+        fo = self.fsb_forests(None, None, attn)
+        n_vis = min(blk // self.s, pos // self.s)
+        fo.ingest(n_vis)
+        fo.build_spines(n_vis)
+        self._fsb_blk = blk
+        return True
+
     # ---- decode bookkeeping --------------------------------------------------------------------------------------------------
     def advance_in_place(self):
         """The token the decode step wrote becomes part of the cache (experiments/scaling/kv_cache.py:394-404). The cell

@@ -378,7 +378,7 @@ def slot_prefill(state: FslDecodeState, K, V, kbar_cells, N: int):
 
 
 def fsl_decode_step(state: FslDecodeState, q, k, v, pos_t, cos, sin, lam, sigma, lrs, norm_w, *, scale: float, eps: float,
-                    y=None, sel_out=None, splits: int = 8, pdl: bool = False):
+                    y=None, sel_out=None, splits: int = 8, pdl: bool = False, ext_sel=None):
     """One decode token of one FS-L layer. q,k,v: (B,H,D) bf16 views with equal strides and unit inner stride (e.g. slices
     of a fused QKV projection); pos_t: int64 device scalar; lam/sigma/lrs (H) fp32, norm_w (D) fp32 (all device tensors
     that stay alive until the launch has run). Returns y (B, H*D) bf16."""
@@ -401,6 +401,9 @@ def fsl_decode_step(state: FslDecodeState, q, k, v, pos_t, cos, sin, lam, sigma,
     a.y, a.sel_out = y.data_ptr(), _p(sel_out)
     a.splits = int(splits)
     a.pdl = 1 if pdl else 0
+    if ext_sel is not None:         # FS-B: the cells chosen by fsb_select for this token
+        assert ext_sel.is_cuda and ext_sel.dtype == torch.int32 and ext_sel.is_contiguous() and ext_sel.numel() == B * H * state.kk
+        a.ext_sel = ext_sel.data_ptr()
     L.call("fsattn_fsl_decode_step", a, _stream(q))
     return y
 

@@ -214,6 +214,8 @@ typedef struct {
     void* y; int32_t* sel_out;
     int32_t splits;
     int32_t pdl; /* 1 = launch with programmatic stream serialization (overlaps the launch with the producer's tail) */
+    const int32_t* ext_sel; /* optional (B,H,kk) int32: cells chosen by fsattn_fsb_select for this token (FS-B layers); the
+                             * kernel then skips its own pool and scoring. Full stores (bf16, int8) only. NULL for FS-L. */
 } fsattn_fsl_decode_t;
 FSATTN_API int fsattn_fsl_decode_step(const fsattn_fsl_decode_t* a, fsattn_stream_t stream);
 

@@ -242,3 +242,111 @@ def test_select_int8_keys_and_empty_prefix():
     # a short prompt
     sel2 = ops.fsb_select(fo, Qd[:, :, :100], Kd, lam, sigma, scale=D ** -0.5, N=100)
     assert (sel2 == -1).all()
+
+
+def _fsb_layer(g, dev, int8=False, union=True):
+    from freesolo_b200.fsattn import FSAttn, FSKVCache
+    from freesolo_b200.serving import serve_kwargs
+    H, D = int(g["H"]), int(g["D"])
+    a = FSAttn(d_model=H * D, n_heads=H, causal=True, bias=False, max_seq_len=4096,
+               **serve_kwargs("fsb", 0.5 if union else 0.0)).to(dev).eval()
+    with torch.no_grad():
+        a.sel_scale.copy_(torch.from_numpy(g["lam"]))
+        a.log_sigma.copy_(torch.from_numpy(g["sigma"]).log())
+        a.long_range_scale.copy_(torch.from_numpy(g["lrs"]).view(H, 1, 1))
+        a.lr_norm.scale.copy_(torch.from_numpy(g["norm_w"]))
+        a.fsb_tau.copy_(torch.from_numpy(g["tau"]))
+        a.fsb_tau_union.copy_(torch.from_numpy(g["tau_u"]))
+    c = FSKVCache(a)
+    c.reserve = int(g["T"]) + 8
+    if int8:
+        c.enable_int8()
+    return a, c
+
+
+def _close_rows(got, want, what, max_abs=2e-2, mean_rel=4e-3):
+    """max-abs 2e-2 and mean-rel bar; an element may also differ by one bf16 unit in the last place of the expected
+    value (outputs are stored in bf16: a rounding flip at |y| >= 4 is 0.031 by itself)."""
+    got, want = got.float().cpu(), want.float().cpu()
+    d = (got - want).abs()
+    ulp = torch.exp2(torch.floor(torch.log2(want.abs().clamp(min=1e-30))) - 7)
+    over = d > torch.maximum(torch.full_like(d, max_abs), ulp)
+    mr = (d.mean() / want.abs().mean().clamp(min=1e-9)).item()
+    assert not over.any() and mr <= mean_rel, (f"{what}: max-abs {d.max().item():.3e} (bar {max_abs} or 1 bf16 ulp), "
+                                               f"mean-rel {mr:.3e} (bar {mean_rel})")
+
+
+@pytest.mark.parametrize("int8", [False, True])
+def test_fsb_layer_prefill_then_decode(int8):
+    """FSAttn with fsb_enabled behind FSKVCache: prefill and a decode run that crosses a block boundary, against the
+    oracle layer on the same bf16 inputs (tolerance: max-abs 2e-2, mean-rel 4e-3 per step as for FS-L decode) and
+    against the reference's own fp32 outputs on the rows whose selections agree."""
+    import os
+    from oracle import fsb
+    os.environ["FSATTN_KEEP_SEL"] = "1"
+    try:
+        g, Q, K, V = _golden_inputs("randn")
+        H, D, N, T = int(g["H"]), int(g["D"]), int(g["N"]), int(g["T"])
+        dev = _dev()
+        a, c = _fsb_layer(g, dev, int8=int8)
+        Qd, Kd, Vd = Q.to(dev), K.to(dev), V.to(dev)
+        with torch.no_grad():
+            y0 = a._prefill(Qd[:, :, :N], Kd[:, :, :N], Vd[:, :, :N], c).clone()
+            sel0 = a._last_sel[:, :, :N].cpu().long()
+        orc = fsb.FSBLayerOracle(H, D, tau=g["tau"], tau_u=g["tau_u"], lam=torch.from_numpy(g["lam"]),
+                                 sigma=torch.from_numpy(g["sigma"]), lrs=torch.from_numpy(g["lrs"]),
+                                 norm_w=torch.from_numpy(g["norm_w"]), eps=float(g["eps"]), act_dtype=torch.bfloat16,
+                                 int8=int8, rope_len=4096, rope_orig_len=4096)
+        yo, so, mo = orc.prefill(Q[:, :, :N], K[:, :, :N], V[:, :, :N])
+        diff = (sel0 != so).any(-1)
+        assert (diff & (mo > 1e-4)).float().mean() < 0.005, "prefill selections differ beyond the beam near-ties"
+        rows = ~diff.any(1)                                                  # (B, N) rows where every head agrees
+        assert rows.float().mean() > 0.95
+        _close_rows(y0.cpu()[rows], yo[rows], "FS-B prefill output vs oracle", mean_rel=2e-3)
+        ref_rows = (sel0 == torch.from_numpy(g["sel_prefill"]).long()).all(-1).all(1)
+        assert ref_rows.float().mean() > 0.9
+        _close_rows(y0.cpu()[ref_rows], torch.from_numpy(g["y_prefill"])[ref_rows], "FS-B prefill vs reference fp32",
+                    mean_rel=8e-3)
+        n_bad = 0
+        for t in range(T):
+            with torch.no_grad():
+                y = a._decode_one(Qd[:, :, N + t], Kd[:, :, N + t], Vd[:, :, N + t], c)
+            sel = a._last_sel.cpu().long()
+            sl = slice(N + t, N + t + 1)
+            yo, so, mo = orc.decode(Q[:, :, sl], K[:, :, sl], V[:, :, sl])
+            d = (sel != so[:, :, 0]).any(-1)
+            n_bad += int((d & (mo[:, :, 0] > 1e-4)).sum())
+            if not d.any():
+                _close_rows(y.view(-1), yo.reshape(-1), f"FS-B decode step {t}", mean_rel=4e-3)
+                if not int8:
+                    ref_sel = torch.from_numpy(g["sel_decode"][t]).long()
+                    if (sel == ref_sel).all():
+                        _close_rows(y.view(-1), torch.from_numpy(g["y_decode"][:, t]).reshape(-1),
+                                    f"FS-B decode step {t} vs reference fp32", mean_rel=1e-2)
+        assert n_bad <= 2, f"{n_bad} decode selections differ outside the re-rank margin"
+        assert c.state.faults() == (0, 0, 0)
+    finally:
+        os.environ.pop("FSATTN_KEEP_SEL", None)
+
+
+def test_fsb_without_second_forest_matches_oracle():
+    """fsb_union_tau_quantile = 0: the second beam would search the main forest again and add nothing."""
+    from oracle import fsb
+    g, Q, K, V = _golden_inputs("vocab")
+    H, D, N = int(g["H"]), int(g["D"]), int(g["N"])
+    dev = _dev()
+    a, c = _fsb_layer(g, dev, union=False)
+    import os
+    os.environ["FSATTN_KEEP_SEL"] = "1"
+    try:
+        with torch.no_grad():
+            a._prefill(Q[:, :, :N].to(dev), K[:, :, :N].to(dev), V[:, :, :N].to(dev), c)
+        sel = a._last_sel[:, :, :N].cpu().long()
+    finally:
+        os.environ.pop("FSATTN_KEEP_SEL", None)
+    from oracle.fsl import cell_stats
+    kbar, ceil = cell_stats(K[:, :, :N], 32)
+    so, mo = fsb.fsb_select_prefill(Q[:, :, :N].float(), K[:, :, :N].float(), kbar, ceil, g["tau"], None,
+                                    torch.from_numpy(g["lam"]), torch.from_numpy(g["sigma"]), D ** -0.5)
+    bad = (sel != so[:, :, :N]).any(-1) & (mo[:, :, :N] > 1e-4)
+    assert bad.float().mean() < 0.005
