@@ -88,7 +88,7 @@ __device__ __forceinline__ int count_below(const int* adm, int m_tot, int E) {
 }
 
 // ---- one beam (one warp). Returns the frontier's cell in lanes 0..15 (-1 none); adds the scored children to nvis ----
-template <int D>
+template <int D, bool PREFETCH = false>
 __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, const float* qs, float qn, float qpos,
                     float lam, float sig, float scale, int width, int lane, int* fr, int& nvis) {
     constexpr int DP = FsbDim<D>::DP;
@@ -122,7 +122,16 @@ __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, co
             int pm;
             float p[DP];
             if (pref >= 0) {
-                cref = pref + ((~pmeta) >> 4) + 1 + side;
+                const int np = (~pmeta) >> 4;
+                cref = pref + np + 1 + side;
+                if (PREFETCH && ((~pmeta) & 15) >= 2) {
+                    // the two children of this child sit side by side: ask L2 for them now, one level ahead of their use
+                    const int gc = cref + (2 * np + 1 + side) + 1;
+                    const char* g = (const char*)(node_mu + (int64_t)gc * D);
+#pragma unroll
+                    for (int o = 0; o < 2 * D * 2; o += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(g + o));
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(aux + gc));
+                }
             } else {
                 const float* x = S.node[-pref - 2] + D;
                 cref = __float_as_int(x[4 + side]);
@@ -178,6 +187,49 @@ __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, co
         __syncwarp();
     }
     return (lane < WMAX && ref >= 0 && meta >= 0) ? meta : -1;
+}
+
+// ---- re-rank score of one candidate cell (one warp, lane = token of the cell) -----------------------------------------
+template <int D>
+__device__ __forceinline__ float rerank_cell(const fsattn_fsb_select_t& a, int b, int hd, int t, int cell, const float* qs,
+                                             float qpos, float lam, float sig, int lane) {
+    constexpr int DP = FsbDim<D>::DP;
+    float p[DP];
+    const int64_t tok = (int64_t)cell * 32 + lane;
+    if (a.k.ptr) {
+        const uint4* kr = (const uint4*)((const bf16*)a.k.ptr + b * a.k.sb + hd * a.k.sh + tok * a.k.sn);
+#pragma unroll
+        for (int v = 0; v < D / 8; ++v) {
+            const uint4 w = kr[v];
+            const float4 qa = *(const float4*)(qs + v * 8), qb = *(const float4*)(qs + v * 8 + 4);
+            p[v * 8 + 0] = f_mul(bf_lo(w.x), qa.x); p[v * 8 + 1] = f_mul(bf_hi(w.x), qa.y);
+            p[v * 8 + 2] = f_mul(bf_lo(w.y), qa.z); p[v * 8 + 3] = f_mul(bf_hi(w.y), qa.w);
+            p[v * 8 + 4] = f_mul(bf_lo(w.z), qb.x); p[v * 8 + 5] = f_mul(bf_hi(w.z), qb.y);
+            p[v * 8 + 6] = f_mul(bf_lo(w.w), qb.z); p[v * 8 + 7] = f_mul(bf_hi(w.w), qb.w);
+        }
+    } else {
+        const uint32_t* kr = (const uint32_t*)(a.kq + b * a.kq_sb + hd * a.kq_sh + tok * D);
+        const float sc = __bfloat162float(((const bf16*)a.ks)[b * a.ks_sb + hd * a.ks_sh + cell]);
+#pragma unroll
+        for (int v = 0; v < D / 4; ++v) {
+            float o[4];
+            unpack4_i8(kr[v], o);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) p[v * 4 + e] = f_mul(bf_round(f_mul(o[e], sc)), qs[v * 4 + e]);
+        }
+    }
+#pragma unroll
+    for (int d = D; d < DP; ++d) p[d] = 0.f;
+    const float sc = f_mul(fsb_thread_det_sum<D>(p), a.scale);
+    const float m = warp_max(sc);
+    float e = expf(f_add(sc, -m));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) e = f_add(e, __shfl_xor_sync(FS_FULL, e, o));
+    const float lse = f_add(m, logf(e));
+    const float cpos = f_mul(f_add((float)cell, 0.5f), 32.0f);
+    const float er = erff(f_div(fabsf(f_add(qpos, -cpos)), f_mul(2.0f, sig)));
+    const float ceil_c = a.main.ceil[(int64_t)t * a.main.ceil_st + cell];
+    return f_add(lse, f_mul(f_mul(lam, ceil_c), er));
 }
 
 struct SelArgs {
@@ -264,45 +316,10 @@ __global__ void __launch_bounds__(NWARP * 32) fsb_select_kernel(SelArgs A) {
         if (a.nvis && lane == 0) a.nvis[row] = nv;
         // ---- re-rank: u = LSE_t((q.k_t) scale) + lam ceil erf(|p - (c+.5) 32| / (2 sig)) ----
         float u = -INFINITY;
-        const float* ceil = a.main.ceil + (int64_t)t * a.main.ceil_st;
         for (int i = 0; i < 32; ++i) {
             const int cell = __shfl_sync(FS_FULL, cand, i);
             if (cell < 0) continue;
-            float p[DP];
-            const int64_t tok = (int64_t)cell * 32 + lane;
-            if (a.k.ptr) {
-                const uint4* kr = (const uint4*)((const bf16*)a.k.ptr + b * a.k.sb + hd * a.k.sh + tok * a.k.sn);
-#pragma unroll
-                for (int v = 0; v < D / 8; ++v) {
-                    const uint4 w = kr[v];
-                    const float4 qa = *(const float4*)(qs + v * 8), qb = *(const float4*)(qs + v * 8 + 4);
-                    p[v * 8 + 0] = f_mul(bf_lo(w.x), qa.x); p[v * 8 + 1] = f_mul(bf_hi(w.x), qa.y);
-                    p[v * 8 + 2] = f_mul(bf_lo(w.y), qa.z); p[v * 8 + 3] = f_mul(bf_hi(w.y), qa.w);
-                    p[v * 8 + 4] = f_mul(bf_lo(w.z), qb.x); p[v * 8 + 5] = f_mul(bf_hi(w.z), qb.y);
-                    p[v * 8 + 6] = f_mul(bf_lo(w.w), qb.z); p[v * 8 + 7] = f_mul(bf_hi(w.w), qb.w);
-                }
-            } else {
-                const uint32_t* kr = (const uint32_t*)(a.kq + b * a.kq_sb + hd * a.kq_sh + tok * D);
-                const float sc = __bfloat162float(((const bf16*)a.ks)[b * a.ks_sb + hd * a.ks_sh + cell]);
-#pragma unroll
-                for (int v = 0; v < D / 4; ++v) {
-                    float o[4];
-                    unpack4_i8(kr[v], o);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) p[v * 4 + e] = f_mul(bf_round(f_mul(o[e], sc)), qs[v * 4 + e]);
-                }
-            }
-#pragma unroll
-            for (int d = D; d < DP; ++d) p[d] = 0.f;
-            const float sc = f_mul(fsb_thread_det_sum<D>(p), a.scale);
-            const float m = warp_max(sc);
-            float e = expf(f_add(sc, -m));
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) e = f_add(e, __shfl_xor_sync(FS_FULL, e, o));
-            const float lse = f_add(m, logf(e));
-            const float cpos = f_mul(f_add((float)cell, 0.5f), 32.0f);
-            const float er = erff(f_div(fabsf(f_add(qpos, -cpos)), f_mul(2.0f, sig)));
-            const float ui = f_add(lse, f_mul(f_mul(lam, ceil[cell]), er));
+            const float ui = rerank_cell<D>(a, b, hd, t, cell, qs, qpos, lam, sig, lane);
             if (lane == i) u = ui;
         }
         int rank = 0;
@@ -312,6 +329,91 @@ __global__ void __launch_bounds__(NWARP * 32) fsb_select_kernel(SelArgs A) {
             rank += (uo > u || (uo == u && o < lane)) ? 1 : 0;
         }
         if (rank < a.read_top) a.sel[row * a.read_top + rank] = (u == -INFINITY) ? -1 : cand;
+    }
+}
+
+// ---- decode: one query per row, one CTA per row --------------------------------------------------------------------------
+// Warp 0 runs the main beam and warp 1 the second beam at the same time (each a chain of dependent table reads, so the
+// chain length, not the bandwidth, sets the time; the grandchildren of every scored node are prefetched into L2 one
+// level ahead). All eight warps then share the re-rank of the <= 32 candidates, and warp 0 ranks the scores.
+// Everything that does not depend on the new token (spines, parameters) is read before the dependency wait, so under
+// programmatic dependent launch it overlaps the tail of the QKV projection.
+template <int D>
+__global__ void __launch_bounds__(256) fsb_decode_select_kernel(SelArgs A) {
+    constexpr int DP = FsbDim<D>::DP;
+    constexpr int NW = 8;
+    const fsattn_fsb_select_t& a = A.a;
+    const int t = blockIdx.x;
+    const int b = t / A.H, hd = t % A.H;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __shared__ SpineSm<D> sp[2];
+    __shared__ __align__(16) float qs[DP];
+    __shared__ int frs[2][WMAX * 2];
+    __shared__ int cand_s[32];
+    __shared__ float u_s[32];
+    __shared__ int nv_s[2];
+
+    const int nsp = a.width2 > 0 ? 2 : 1;
+    for (int w = 0; w < nsp; ++w) {
+        const float* src = a.spine[w] + (int64_t)t * SPW * (D + 8);
+        float* dst = &sp[w].node[0][0];
+        for (int i = tid; i < SPW * (D + 8); i += 256) dst[i] = src[i];
+        if (tid == 0) {
+            const int* h = a.hdr[w] + t * 4;
+            sp[w].root = h[0]; sp[w].height = h[1]; sp[w].m_b = h[2];
+        }
+    }
+    const float lam = a.lam[hd], sig = a.sigma[hd];
+    const float qpos = (float)(*a.pos);
+    if (tid < 32) { cand_s[tid] = -1; u_s[tid] = -INFINITY; }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const bf16* qp = (const bf16*)a.q.ptr + b * a.q.sb + hd * a.q.sh;
+    for (int d = tid; d < DP; d += 256) qs[d] = (d < D) ? __bfloat162float(qp[d]) : 0.f;
+    __syncthreads();
+    if (warp < nsp) {
+        float qq[FsbDim<D>::NPL];
+#pragma unroll
+        for (int i = 0; i < FsbDim<D>::NPL; ++i) { const float v = qs[lane + 32 * i]; qq[i] = f_mul(v, v); }
+        const float qn = f_mul(f_sqrt(fsb_warp_det_sum<D>(qq)), a.radius_coef);
+        int nv = 0;
+        const int c = beam<D, true>(warp == 0 ? a.main : a.second, t, sp[warp], qs, qn, qpos, lam, sig, a.scale,
+                                    warp == 0 ? a.width : a.width2, lane, frs[warp], nv);
+        if (lane < WMAX) cand_s[warp * WMAX + lane] = (lane < (warp == 0 ? a.width : a.width2)) ? c : -1;
+        if (lane == 0) nv_s[warp] = nv;
+    }
+    __syncthreads();
+    if (warp == 0) {                      // union: blank the second beam's repeats of a main cell
+        const int mine = cand_s[lane];
+        bool dup = false;
+        for (int o = 0; o < WMAX; ++o) dup |= (lane >= WMAX && cand_s[o] == mine);
+        __syncwarp();
+        if (dup) cand_s[lane] = -1;
+        if (a.nvis && lane == 0) a.nvis[t] = nv_s[0] + (nsp > 1 ? nv_s[1] : 0);
+    }
+    __syncthreads();
+    const int Wc = a.width + a.width2;
+    if (a.cand && tid < 32) {
+        if (tid < a.width) a.cand[(int64_t)t * Wc + tid] = cand_s[tid];
+        if (tid >= WMAX && tid - WMAX < a.width2) a.cand[(int64_t)t * Wc + a.width + tid - WMAX] = cand_s[tid];
+    }
+    for (int i = warp; i < 32; i += NW) {
+        const int cell = cand_s[i];
+        if (cell < 0) continue;
+        const float ui = rerank_cell<D>(a, b, hd, t, cell, qs, qpos, lam, sig, lane);
+        if (lane == 0) u_s[i] = ui;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const float u = u_s[lane];
+        const int cand = cand_s[lane];
+        int rank = 0;
+#pragma unroll 8
+        for (int o = 0; o < 32; ++o) {
+            const float uo = __shfl_sync(FS_FULL, u, o);
+            rank += (uo > u || (uo == u && o < lane)) ? 1 : 0;
+        }
+        if (rank < a.read_top) a.sel[(int64_t)t * a.read_top + rank] = (u == -INFINITY) ? -1 : cand;
     }
 }
 
@@ -385,11 +487,26 @@ extern "C" int fsattn_fsb_select(const fsattn_fsb_select_t* a, fsattn_stream_t s
     cudaStream_t st = (cudaStream_t)stream;
     dim3 grid(nb, a->main.T);
     if (a->use_spines) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(a->main.T, 1, 1);
+        cfg.blockDim = dim3(256, 1, 1);
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = a->pdl ? 1 : 0;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t e;
         switch (a->main.D) {
-            case 64: fsb_select_kernel<64, 2><<<grid, 64, 0, st>>>(A); break;
-            case 96: fsb_select_kernel<96, 2><<<grid, 64, 0, st>>>(A); break;
-            default: fsb_select_kernel<128, 2><<<grid, 64, 0, st>>>(A); break;
+            case 64: e = cudaLaunchKernelEx(&cfg, fsb_decode_select_kernel<64>, A); break;
+            case 96: e = cudaLaunchKernelEx(&cfg, fsb_decode_select_kernel<96>, A); break;
+            default: e = cudaLaunchKernelEx(&cfg, fsb_decode_select_kernel<128>, A); break;
         }
+        if (e != cudaSuccess) {
+            fs_set_error("fsb_select: launch failed: %s", cudaGetErrorString(e));
+            return FSATTN_ELAUNCH;
+        }
+        return FSATTN_OK;
     } else {
         switch (a->main.D) {
             case 64: fsb_select_kernel<64, 8><<<grid, 256, 0, st>>>(A); break;

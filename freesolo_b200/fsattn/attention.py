@@ -376,7 +376,7 @@ class FSAttn(nn.Module):
         cache.advance_in_place()
         return y
 
-    def _fsb_decode_select(self, q, st, cache, pos_t, lam, sigma):
+    def _fsb_decode_select(self, q, st, cache, pos_t, lam, sigma, pdl=False):
         """src/fsattn/fsb_tree.py:2909-3064: the decode query's two beams over the block's forests, union, re-rank with
         the token keys as the cache reads them (raw bf16, or the int8 codes). q (B,H,D) view -> (B,H,1,kk) int32."""
         fo = cache.fsb
@@ -384,10 +384,10 @@ class FSAttn(nn.Module):
         if st.mode == "bf16":
             return ops.fsb_select(fo, q4, st.kbuf, lam, sigma, scale=self.scale, width=self.fsb_width,
                                   width2=self._fsb_w2(fo), read_top=self.fsb_read_top,
-                                  radius_coef=self.fsb_bound_radius_coef, pos=pos_t)
+                                  radius_coef=self.fsb_bound_radius_coef, pos=pos_t, pdl=pdl)
         return ops.fsb_select(fo, q4, None, lam, sigma, scale=self.scale, width=self.fsb_width,
                               width2=self._fsb_w2(fo), read_top=self.fsb_read_top,
-                              radius_coef=self.fsb_bound_radius_coef, pos=pos_t, kq=st.kq, ks=st.ks)
+                              radius_coef=self.fsb_bound_radius_coef, pos=pos_t, kq=st.kq, ks=st.ks, pdl=pdl)
 
     def graph_decode_layer(self, x, buf):
         """One decode token inside a captured whole-step graph (src/fsattn/attention.py:1493-1559): x (B,1,d); buf holds
@@ -420,7 +420,7 @@ class FSAttn(nn.Module):
         if self.fsb_enabled:
             # the selection kernel reads q, so it waits for the projection like any dependent launch; the decode kernel
             # then depends on it through ext_sel
-            ext = self._fsb_decode_select(q4[:, 0], st, buf["cache"], buf["pos_t"], lam, sigma)
+            ext = self._fsb_decode_select(q4[:, 0], st, buf["cache"], buf["pos_t"], lam, sigma, pdl=pdl)
         return ops.fsl_decode_step(st, q4[:, 0], q4[:, 1], q4[:, 2], buf["pos_t"], cos, sin, lam, sigma, lrs, norm_w,
                                    scale=self.scale, eps=self.lr_norm.eps, y=y, splits=self.decode_splits,
-                                   pdl=pdl and ext is None, ext_sel=ext)
+                                   pdl=pdl, ext_sel=ext)

@@ -198,6 +198,9 @@ class GraphedDecoder:
         extend_rope_cache(m, self.Lmax + 8)
         self.cache = make_caches(m, reserve=max(0, self.Lmax - P0))
         kv = self.kv
+        self.fsb = any(a.fsb_enabled for a in self.attn)
+        if kv == "bounded" and self.fsb:
+            kv = "int8"      # FS-B reads any admitted cell: it keeps the full (int8) store
         if kv == "bounded" and not (P0 >= self.attn[0].window_size and _kvb.supported(self.attn, self.dt, self.dev)):
             kv = "int8"      # prompts shorter than the window keep the full store (decode_graph.py:89-93)
         for c in self.cache:
@@ -261,6 +264,13 @@ class GraphedDecoder:
         """Advance one token; returns the device tensor holding the new token ids (B,1)."""
         if self.pos + 1 >= self.Lmax:
             raise RuntimeError(f"decoder sized for {self.Lmax} positions")
+        if self.fsb and self.pos % self.attn[0]._cell_block == 0 or self.fsb and self._steps == 0:
+            # FS-B (experiments/scaling/decode_graph.py:499-541, src/fsattn/fsb_tree.py:3598-3674): at a query-block
+            # change every layer's forests take in the cells completed before the block and rebuild their spines, as
+            # plain launches ahead of the replay; buffers keep their addresses, so the graph is never re-captured
+            for a, c in zip(self.attn, self.cache):
+                if a.fsb_enabled:
+                    c.fsb_block_change(self.pos, a)
         if self.graph is None and self._steps >= self.eager_steps:
             self._capture()
         if self.graph is None:
@@ -276,6 +286,9 @@ class GraphedDecoder:
             c.pos = self.pos
             c._ncell = self.pos // c.s
 
+    def fsb_bytes(self) -> int:
+        return sum(c.fsb.nbytes() for c in self.cache if getattr(c, "fsb", None) is not None)
+
     def kv_faults(self) -> tuple:
         """(slot overflows, readable cells without a slot, rejected indices) over all layers; one host sync."""
         tot = torch.stack([c.state.status for c in self.cache]).sum(0).tolist()
@@ -283,6 +296,31 @@ class GraphedDecoder:
 
     def kv_bytes(self) -> int:
         return sum(c.state.nbytes() for c in self.cache)
+
+
+@torch.no_grad()
+def calibrate_fsb_tau(model, ids, quantile: float, target: str = "fsb_tau"):
+    """Set every FS-B layer's admission threshold to the per-head `quantile` of the cell ceilings seen on the token ids
+    `ids` (B, L): the reference's fsb_calibrate_tau (src/fsattn/fsb_tree.py:3944-3969) for one batch. target:
+    'fsb_tau' (main forest) or 'fsb_tau_union' (second forest; the layer must have been built with
+    fsb_union_tau_quantile > 0 for it to take effect). Returns the thresholds (layers, H)."""
+    if target not in ("fsb_tau", "fsb_tau_union"):
+        raise ValueError(f"calibrate_fsb_tau: target {target!r} (fsb_tau | fsb_tau_union)")
+    ids = ids.view(1, -1) if ids.dim() == 1 else ids
+    caches = make_caches(model)
+    extend_rope_cache(model, ids.shape[1] + 8)
+    trunk_cached(model, ids.to(next(model.parameters()).device), caches, last_n=1)
+    taus = []
+    for blk, c in zip(model.blocks, caches):
+        a = blk.attn.fsattn
+        if not a.fsb_enabled:
+            continue
+        _, ceil, ncell = c.completed_cells()
+        H = ceil.shape[1]
+        t = torch.quantile(ceil[:, :, :ncell].float().transpose(0, 1).reshape(H, -1), float(quantile), dim=1)
+        getattr(a, target).copy_(t)
+        taus.append(t)
+    return torch.stack(taus) if taus else None
 
 
 @torch.no_grad()

@@ -313,6 +313,7 @@ typedef struct {
     int32_t B, N, q_pos0, Bq, width, width2, read_top;
     int32_t use_spines; const float* spine[2]; const int32_t* hdr[2]; const int64_t* pos;
     int32_t* sel; int32_t* cand; int32_t* nvis;
+    int32_t pdl;  /* decode: 1 = launch with programmatic stream serialization (the kernel waits for its producer itself) */
 } fsattn_fsb_select_t;
 FSATTN_API int fsattn_fsb_select(const fsattn_fsb_select_t* a, fsattn_stream_t stream);
 

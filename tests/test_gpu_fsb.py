@@ -350,3 +350,37 @@ def test_fsb_without_second_forest_matches_oracle():
                                     torch.from_numpy(g["lam"]), torch.from_numpy(g["sigma"]), D ** -0.5)
     bad = (sel != so[:, :, :N]).any(-1) & (mo[:, :, :N] > 1e-4)
     assert bad.float().mean() < 0.005
+
+
+@pytest.mark.parametrize("kv", ["bf16", "int8"])
+def test_fsb_graph_decoder_matches_eager_steps(kv):
+    """An FS-B model (serve configuration, calibrated thresholds, second forest): tokens from the captured whole-step
+    graph equal the same decoder stepped without a graph across two block changes (forest ingest + spines between
+    replays), and the first token equals the eager per-token path's."""
+    from freesolo_b200.serving import FreeSoloLM, GraphedDecoder, cached_generate, calibrate_fsb_tau, serve_kwargs
+    dev = _dev()
+    torch.manual_seed(0)
+    m = FreeSoloLM.from_config("debug", max_seq_len=2048, **serve_kwargs("fsb", 0.9)).to(dev).to(torch.bfloat16).eval()
+    P0, T = 700, 300
+    g = torch.Generator().manual_seed(3)
+    ids = torch.randint(0, 32000, (2, P0), generator=g)
+    warm = torch.randint(0, 32000, (1, 1024), generator=g)
+    t1 = calibrate_fsb_tau(m, warm, 0.5, "fsb_tau")
+    t2 = calibrate_fsb_tau(m, warm, 0.9, "fsb_tau_union")
+    assert t1 is not None and (t1 > 0).all() and (t2[0] >= t1[0]).all()      # layer 0 sees the same keys both times
+    runs = []
+    for eager in (10 ** 9, 2):
+        gd = GraphedDecoder(m, ids, Lmax=P0 + T + 8, device=dev, kv=kv, eager_steps=eager)
+        toks = [gd.prefill().clone()]
+        for i in range(T - 1):
+            toks.append(gd.step().clone())
+        runs.append((torch.cat(toks, dim=1).cpu(), gd))
+    assert runs[0][1].graph is None and runs[1][1].graph is not None
+    assert torch.equal(runs[0][0], runs[1][0]), "graph replay diverges from the un-captured steps"
+    assert runs[1][1].kv_faults() == (0, 0, 0)
+    fo = runs[1][1].cache[0].fsb
+    assert fo.nf == 2 and fo.n_seen == ((P0 + T - 1) // 128) * 128 // 32
+    mt = fo.m_tot[0].cpu()
+    assert (mt > 0).all() and (fo.m_tot[1].cpu() <= mt).all()
+    want = cached_generate(m, ids, 2, device=dev, kv=kv)
+    assert torch.equal(want[:, P0].cpu(), runs[1][0][:, 0])
