@@ -25,6 +25,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 PUBLISHED_FSL_DECODE_TPS_131K = 515.1      # A100-40GB, README.md:62 of the reference
+PUBLISHED_FSB_DECODE_TPS_131K = 462.7      # A100-40GB, README.md:63 of the reference
+PUBLISHED_FSB_PREFILL_KTOKS_131K = 137.8   # A100-40GB, README.md:63 of the reference
 W_BYTES_341M = 2 * (24 * (4 * 1024 ** 2 + 3 * 1024 * 2816) + 32000 * 1024)
 
 
@@ -169,6 +171,52 @@ def time_decode_kernel(gd, n=48):
     return sum(ms) / len(ms), ms[len(ms) // 2]
 
 
+def run_fsb_section(args, dev, K, Wm):
+    """BASELINE config 3 on the same box: FS-B 341M (serve configuration with the second forest), thresholds calibrated
+    as the 50th / 90th percentile of the cell ceilings of a 4096-token warm-up, prefill + forest build at args.ctx,
+    then K graph-replayed decode steps (int8 KV store; the forests take in new cells at every 128-token block)."""
+    from freesolo_b200.serving import FreeSoloLM, GraphedDecoder, calibrate_fsb_tau, serve_kwargs
+    ctx = args.ctx
+    torch.manual_seed(0)
+    model = FreeSoloLM.from_config(args.model, max_seq_len=ctx + 512, **serve_kwargs("fsb", 0.9)).to(torch.bfloat16).to(dev).eval()
+    g = torch.Generator().manual_seed(99)
+    warm_ids = torch.randint(0, model.vocab_size, (1, 4096), generator=g)
+    calibrate_fsb_tau(model, warm_ids, 0.5, "fsb_tau")
+    calibrate_fsb_tau(model, warm_ids, 0.9, "fsb_tau_union")
+    ids = torch.randint(0, model.vocab_size, (args.batch, ctx), generator=torch.Generator().manual_seed(4321 + ctx))
+    gd = GraphedDecoder(model, ids, Lmax=ctx + Wm + K + 40, device=dev, kv="int8")
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    gd.prefill()
+    e1.record()
+    torch.cuda.synchronize()
+    prefill_ms = e0.elapsed_time(e1)
+    for _ in range(Wm):
+        gd.step()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(K):
+        gd.step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    fo = gd.cache[0].fsb
+    nL = len(gd.cache)
+    out = {"workload": f"FS-B {args.model} (two forests, beam 16+16, token-LSE re-rank to 4), prefill + forest build at {ctx}, "
+                       f"then {K} decode steps, batch {args.batch}, int8 KV",
+           "decode_tok_s": args.batch * K / (ms * 1e-3), "decode_ms_per_step": ms / K,
+           "prefill_ktok_s": args.batch * ctx / prefill_ms, "prefill_ms": prefill_ms,
+           "vs_published_decode": (args.batch * K / (ms * 1e-3)) / PUBLISHED_FSB_DECODE_TPS_131K if ctx == 131072 else None,
+           "vs_published_prefill": (args.batch * ctx / prefill_ms) / PUBLISHED_FSB_PREFILL_KTOKS_131K if ctx == 131072 else None,
+           "gpu_launches": K * (6 * nL + 1), "forest_bytes_per_layer": gd.fsb_bytes() // nL,
+           "admitted_cells_layer0": {"main": fo.m_tot[0].tolist(), "second": fo.m_tot[1].tolist()},
+           "kv_faults": list(gd.kv_faults())}
+    del gd, model
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args):
     import torch.distributed as dist
     from freesolo_b200.serving import FreeSoloLM, GraphedDecoder, serve_kwargs
@@ -280,6 +328,10 @@ def run_ours(args):
         "kv_bytes_per_layer": gd.kv_bytes() // nL, "kv_faults": list(faults),
         "peak_mem_gib": torch.cuda.max_memory_allocated() / 2 ** 30,
     }
+    if world == 1 and not args.no_fsb:
+        del gd, model
+        torch.cuda.empty_cache()
+        line["fsb"] = run_fsb_section(args, dev, K, Wm)
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline_sample()
     print(json.dumps(line), flush=True)
@@ -299,6 +351,7 @@ def main():
     ap.add_argument("--model", default="340m")
     ap.add_argument("--kv", default="bounded", choices=["bounded", "int8", "bf16"])
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-fsb", action="store_true", help="skip the FS-B section (BASELINE config 3) of the N=1 line")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -177,10 +177,10 @@ class FSAttn(nn.Module):
         self.fsb_W_max = 16
         self.fsb_union_W_max = 16
         self.fsb_kk = self.fsb_read_top
+        if not self.fsb_enabled:        # the reference registers the FS-B buffers only on FS-B layers (attention.py:122-128)
+            return
         self.register_buffer("fsb_tau", torch.zeros(n_heads), persistent=True)
         self.register_buffer("fsb_tau_union", torch.zeros(n_heads), persistent=False)
-        if not self.fsb_enabled:
-            return
         bad = []
         if self.fsb_policy_mode != "fixed": bad.append(f"fsb_policy={self.fsb_policy_mode!r} (fixed)")
         if self.fsb_delta != 0: bad.append(f"fsb_delta={self.fsb_delta} (0)")

@@ -48,9 +48,14 @@ def test_rotary_tables_match_oracle_and_grow_in_fp32():
 
 def test_uncacheable_configurations_raise():
     for over in (dict(rope_long_range=True), dict(sel_strict_causal=0), dict(cell_prune_kernel=0), dict(cell_stride=64),
-                 dict(fs_uniform_sr=False), dict(fsb_enabled=True)):
+                 dict(fs_uniform_sr=False)):
         with pytest.raises(NotImplementedError):
             FSKVCache(_attn(**over))
+    FSKVCache(_attn(fsb_enabled=True, fsb_read_top=4, cell_prune_kernel=0))     # an FS-B layer is cacheable
+    c = FSKVCache(_attn(fsb_enabled=True, fsb_read_top=4, cell_prune_kernel=0))
+    c.enable_bounded()
+    with pytest.raises(NotImplementedError):                                      # ... but not on the bounded slot store
+        c.fsb_forests(None, None, c.attn)
     a = _attn()
     with pytest.raises(NotImplementedError):
         a(torch.zeros(1, 4, 256))            # no cache: the training forward is not part of this build
@@ -71,3 +76,20 @@ def test_fused_projection_weights_are_views():
     assert w.shape == (768, 256) and a.W_k.weight.data_ptr() == w[dm:].data_ptr()
     w2, _ = a._ensure_qkv_cache()
     assert w2 is w
+
+
+def test_fsb_layer_construction_and_refusals():
+    """FS-B keywords of the reference layer (src/fsattn/fsb_tree.py:41-155): the serve preset builds, its persistent
+    buffer is named like the reference's, and configurations outside the built one are refused at construction."""
+    import pytest
+    a = FSAttn(256, 4, causal=True, bias=False, **serve_kwargs("fsb", 0.9))
+    assert a.fsb_enabled and "fsb_tau" in a.state_dict() and "fsb_tau_union" not in a.state_dict()
+    assert (a.fsb_width, a.fsb_union_width, a.fsb_read_top, a.fsb_W_max, a.fsb_delta) == (16, 16, 4, 16, 0)
+    assert a._fsb_union_tau_on()
+    assert not FSAttn(256, 4, causal=True, bias=False, **serve_kwargs("fsb"))._fsb_union_tau_on()
+    for bad in (dict(fsb_delta=1), dict(fsb_policy="learned"), dict(fsb_node_score="mean"), dict(fsb_tree="rebuild"),
+                dict(fsb_rerank_score="leaf"), dict(fsb_width=32), dict(fsb_hybrid="pool"), dict(fsb_read_top=2)):
+        kw = serve_kwargs("fsb", 0.9)
+        kw.update(bad)
+        with pytest.raises(NotImplementedError):
+            FSAttn(256, 4, causal=True, bias=False, **kw)
