@@ -12,10 +12,19 @@ namespace {
 constexpr int SPW = FSATTN_FSB_SPINE_MAX;      // spine slots per forest
 constexpr int WMAX = 16;                       // frontier slots
 
+// Node refs: -1 none; <= -2 the spine node of height -(ref+2); >= 0 a chunk node: arena node id in bits 0..19 and the
+// height k of its chunk in bits 20..23 (the chunk a descendant belongs to never changes on the way down).
+#define REF_ID(r) ((r) & 0xfffff)
+#define REF_K(r) ((r) >> 20)
+
 template <int D>
 struct SpineSm {
     float node[SPW][D + 8];     // [mu | rad amax pmin cnt chl chr pad pad]
     int root, height, m_b, pad;
+    // shallow levels staged in shared memory (prefill): for the chunk of height k, its first stg_cnt[k] nodes (level
+    // order, so a prefix of its node array) sit at rows stg_base[k] .. of the staging area
+    int stg_base[16], stg_cnt[16];
+    int stg_rows;
 };
 
 // ---- spine of the first m_b admitted cells of row t (one warp) ------------------------------------------------------
@@ -34,12 +43,13 @@ __device__ void build_spine(const fsattn_fsb_forest_t& F, int t, int m_b, SpineS
         if (!((m_b >> k) & 1)) continue;
         ++npres;
         const int j = (m_b >> (k + 1)) << 1;
-        const int cref = (int)fsb_root_node(k, j, m_cap);
+        const int cid = (int)fsb_root_node(k, j, m_cap);
+        const int cref = cid | (k << 20);
         const float* cr = root32 + (int64_t)fsb_chunk_id(k, j, m_cap) * (D + FSB_ROOT_PAD);
         float cmu[NPL];
         fsb_load_row<D>(cr, lane, cmu);
         const float c_rad = cr[D];
-        const float4 ca = aux[cref];
+        const float4 ca = aux[cid];
         const float c_am = ca.y, c_cnt = (float)(1 << k);
         const int c_pm = __float_as_int(ca.z);
         if (r_ref == -1) {
@@ -78,6 +88,35 @@ __device__ void build_spine(const fsattn_fsb_forest_t& F, int t, int m_b, SpineS
     }
 }
 
+// Which chunk nodes lie at tree depth <= DS: the chunks hang off the spine chain, the i-th present bit from the top has
+// its root at depth i+1 (the lowest one shares the depth of the one above it; a single chunk is the root itself), and a
+// chunk whose root is at depth d contributes its levels 0 .. DS-d, i.e. its first 2^(DS-d+1)-1 nodes. At most 2^(DS+1)-1
+// rows in total. One thread.
+template <int D>
+__host__ __device__ constexpr int STG_SW() { return D == 96 ? 3 : 7; }      // 16-byte-chunk XOR mask of a staged row
+template <int D>
+__host__ __device__ constexpr int STG_DS() { return D <= 64 ? 8 : 7; }      // deepest staged tree level
+template <int D>
+__host__ __device__ constexpr int STG_ROWS() { return (2 << STG_DS<D>()); }
+
+template <int D>
+__device__ void stage_plan(SpineSm<D>& S, int m_b, int DS) {
+    for (int k = 0; k < 16; ++k) { S.stg_base[k] = 0; S.stg_cnt[k] = 0; }
+    const int p = __popc(m_b);
+    int i = 0, base = 0;
+    for (int k = 31 - __clz(m_b | 1); k >= 0 && m_b > 0; --k) {
+        if (!((m_b >> k) & 1)) continue;
+        const int dep = (p == 1) ? 0 : ((i < p - 1) ? i + 1 : p - 1);
+        int cnt = (dep <= DS) ? ((1 << (DS - dep + 1)) - 1) : 0;
+        cnt = min(cnt, (2 << k) - 1);
+        S.stg_base[k] = base;
+        S.stg_cnt[k] = cnt;
+        base += cnt;
+        ++i;
+    }
+    S.stg_rows = base;
+}
+
 __device__ __forceinline__ int count_below(const int* adm, int m_tot, int E) {
     int lo = 0, hi = m_tot;                       // first index with adm[i] >= E
     while (lo < hi) {
@@ -88,9 +127,10 @@ __device__ __forceinline__ int count_below(const int* adm, int m_tot, int E) {
 }
 
 // ---- one beam (one warp). Returns the frontier's cell in lanes 0..15 (-1 none); adds the scored children to nvis ----
-template <int D, bool PREFETCH = false>
+template <int D, bool PREFETCH = false, bool STAGED = false>
 __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, const float* qs, float qn, float qpos,
-                    float lam, float sig, float scale, int width, int lane, int* fr, int& nvis) {
+                    float lam, float sig, float scale, int width, int lane, int* fr, int& nvis,
+                    const unsigned char* stg_mu = nullptr, const float4* stg_aux = nullptr) {
     constexpr int DP = FsbDim<D>::DP;
     const int m_cap = F.m_cap;
     const int64_t nrow = (int64_t)t * fsb_nodes_per_row(m_cap);
@@ -103,7 +143,7 @@ __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, co
     const int W = min(width, (d0 >= 5) ? 32 : (1 << d0));
     if (lane == 0) {
         ref = root;
-        meta = (root >= 0) ? __float_as_int(aux[root].w) : 0;
+        meta = (root >= 0) ? __float_as_int(aux[REF_ID(root)].w) : 0;
     }
     for (int it = 0; it < 40; ++it) {
         const bool active = lane < WMAX && ref != -1;
@@ -120,13 +160,17 @@ __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, co
         if (valid) {
             float rad, am;
             int pm;
-            float p[DP];
+            // q . mu with four running sums (plain FMAs: the beam's cut-offs are compared under a score margin, and a
+            // different summation order moves a score by ~1e-6)
+            float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+            int nc = 0;                                     // index of the child inside its chunk
             if (pref >= 0) {
                 const int np = (~pmeta) >> 4;
-                cref = pref + np + 1 + side;
+                nc = 2 * np + 1 + side;
+                cref = pref + np + 1 + side;                // same chunk: the height bits carry over
                 if (PREFETCH && ((~pmeta) & 15) >= 2) {
                     // the two children of this child sit side by side: ask L2 for them now, one level ahead of their use
-                    const int gc = cref + (2 * np + 1 + side) + 1;
+                    const int gc = REF_ID(cref) + nc + 1;
                     const char* g = (const char*)(node_mu + (int64_t)gc * D);
 #pragma unroll
                     for (int o = 0; o < 2 * D * 2; o += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(g + o));
@@ -134,30 +178,43 @@ __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, co
                 }
             } else {
                 const float* x = S.node[-pref - 2] + D;
-                cref = __float_as_int(x[4 + side]);
+                cref = __float_as_int(x[4 + side]);         // a chunk root (index 0 of its chunk) or a spine node
             }
             if (cref >= 0) {
-                const uint4* mr = (const uint4*)(node_mu + (int64_t)cref * D);
+                uint4 w[D / 8];
+                float4 ax;
+                const int ck = REF_K(cref);
+                if (STAGED && nc < S.stg_cnt[ck]) {
+                    const int row = S.stg_base[ck] + nc;
+                    const unsigned char* mr = stg_mu + (size_t)row * (D * 2);
+#pragma unroll
+                    for (int v = 0; v < D / 8; ++v) w[v] = *(const uint4*)(mr + (((v & ~STG_SW<D>()) | ((v ^ row) & STG_SW<D>())) << 4));
+                    ax = stg_aux[row];
+                } else {
+                    const uint4* mr = (const uint4*)(node_mu + (int64_t)REF_ID(cref) * D);
+#pragma unroll
+                    for (int v = 0; v < D / 8; ++v) w[v] = mr[v];
+                    ax = aux[REF_ID(cref)];
+                }
 #pragma unroll
                 for (int v = 0; v < D / 8; ++v) {
-                    const uint4 w = mr[v];
                     const float4 qa = *(const float4*)(qs + v * 8), qb = *(const float4*)(qs + v * 8 + 4);
-                    p[v * 8 + 0] = f_mul(qa.x, bf_lo(w.x)); p[v * 8 + 1] = f_mul(qa.y, bf_hi(w.x));
-                    p[v * 8 + 2] = f_mul(qa.z, bf_lo(w.y)); p[v * 8 + 3] = f_mul(qa.w, bf_hi(w.y));
-                    p[v * 8 + 4] = f_mul(qb.x, bf_lo(w.z)); p[v * 8 + 5] = f_mul(qb.y, bf_hi(w.z));
-                    p[v * 8 + 6] = f_mul(qb.z, bf_lo(w.w)); p[v * 8 + 7] = f_mul(qb.w, bf_hi(w.w));
+                    s0 = fmaf(qa.x, bf_lo(w[v].x), s0); s1 = fmaf(qa.y, bf_hi(w[v].x), s1);
+                    s2 = fmaf(qa.z, bf_lo(w[v].y), s2); s3 = fmaf(qa.w, bf_hi(w[v].y), s3);
+                    s0 = fmaf(qb.x, bf_lo(w[v].z), s0); s1 = fmaf(qb.y, bf_hi(w[v].z), s1);
+                    s2 = fmaf(qb.z, bf_lo(w[v].w), s2); s3 = fmaf(qb.w, bf_hi(w[v].w), s3);
                 }
-                const float4 ax = aux[cref];
                 rad = ax.x; am = ax.y; pm = __float_as_int(ax.z); cmeta = __float_as_int(ax.w);
             } else {
                 const float* x = S.node[-cref - 2];
-#pragma unroll
-                for (int d = 0; d < D; ++d) p[d] = f_mul(qs[d], x[d]);
+#pragma unroll 8
+                for (int d = 0; d < D; d += 4) {
+                    s0 = fmaf(qs[d], x[d], s0); s1 = fmaf(qs[d + 1], x[d + 1], s1);
+                    s2 = fmaf(qs[d + 2], x[d + 2], s2); s3 = fmaf(qs[d + 3], x[d + 3], s3);
+                }
                 rad = x[D]; am = x[D + 1]; pm = __float_as_int(x[D + 2]);
             }
-#pragma unroll
-            for (int d = D; d < DP; ++d) p[d] = 0.f;
-            float content = f_mul(fsb_thread_det_sum<D>(p), scale);
+            float content = f_mul((s0 + s1) + (s2 + s3), scale);
             content = f_add(content, f_mul(f_mul(qn, rad), scale));
             const float ppos = f_mul(f_add((float)pm, 0.5f), 32.0f);
             const float e = erff(f_div(fabsf(f_add(qpos, -ppos)), f_mul(2.0f, sig)));
@@ -237,68 +294,100 @@ struct SelArgs {
     int H, ncell_k;
 };
 
+// ---- prefill: one CTA per (128-query block, row) ---------------------------------------------------------------------------
+// Per forest: build the block's spine, copy every chunk node of tree depth <= DS into shared memory (<= 2^(DS+1)-1 rows:
+// the levels all 128 queries walk through), then one warp per query runs the beam, reading the shallow levels from
+// shared memory and only the deep ones from L2. The candidates of both beams meet in shared memory for the union.
+template <int D>
+struct SelSmem {
+    static constexpr size_t MU_OFF = 0;
+    static constexpr size_t AUX_OFF = MU_OFF + (size_t)STG_ROWS<D>() * D * 2;
+    static constexpr size_t TOTAL = AUX_OFF + (size_t)STG_ROWS<D>() * 16;
+};
+
 template <int D, int NWARP>
-__global__ void __launch_bounds__(NWARP * 32) fsb_select_kernel(SelArgs A) {
+__global__ void __launch_bounds__(NWARP * 32, 2) fsb_select_kernel(SelArgs A) {
     constexpr int DP = FsbDim<D>::DP;
+    constexpr int CH = D / 8;
     const fsattn_fsb_select_t& a = A.a;
     const int blk = blockIdx.x, t = blockIdx.y;
     const int b = t / A.H, hd = t % A.H;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    __shared__ SpineSm<D> sp[2];
+    extern __shared__ __align__(16) unsigned char dsm[];
+    unsigned char* stg_mu = dsm + SelSmem<D>::MU_OFF;
+    float4* stg_aux = (float4*)(dsm + SelSmem<D>::AUX_OFF);
+    __shared__ SpineSm<D> sp;
     __shared__ __align__(16) float qsm[NWARP][DP];
     __shared__ int frs[NWARP][WMAX * 2];
-
-    // ---- spines of this block (warp 0: main, warp 1: second) ----
-    if (warp < 2) {
-        const fsattn_fsb_forest_t& F = warp == 0 ? a.main : a.second;
-        if (a.use_spines) {
-            const float* src = a.spine[warp] + (int64_t)t * SPW * (D + 8);
-            float* dst = &sp[warp].node[0][0];
-            for (int i = lane; i < SPW * (D + 8); i += 32) dst[i] = src[i];
-            if (lane == 0) {
-                const int* h = a.hdr[warp] + t * 4;
-                sp[warp].root = h[0]; sp[warp].height = h[1]; sp[warp].m_b = h[2];
-            }
-        } else {
-            const int E = (a.q_pos0 + blk * a.Bq) / 32;
-            const int m_b = count_below(F.adm + (int64_t)t * F.m_cap, F.m_tot[t], E);
-            build_spine<D>(F, t, m_b, sp[warp], lane);
-        }
-    }
-    __syncthreads();
+    __shared__ int cand_sm[128][2 * WMAX];
+    __shared__ int nv_sm[128];
 
     const float lam = a.lam[hd], sig = a.sigma[hd];
     const int Wc = a.width + a.width2;
-    const int nq = a.use_spines ? 1 : min(a.Bq, a.N - blk * a.Bq);
-    const int64_t pos_dec = a.use_spines ? *a.pos : 0;
+    const int nq = min(a.Bq, a.N - blk * a.Bq);
+    const int E = (a.q_pos0 + blk * a.Bq) / 32;
+    for (int i = tid; i < 128 * 2 * WMAX; i += NWARP * 32) (&cand_sm[0][0])[i] = -1;
+    for (int i = tid; i < 128; i += NWARP * 32) nv_sm[i] = 0;
+    const int nbeam = a.width2 > 0 ? 2 : 1;
+    for (int f = 0; f < nbeam; ++f) {
+        const fsattn_fsb_forest_t& F = f == 0 ? a.main : a.second;
+        __syncthreads();
+        if (warp == 0) {
+            const int m_b = count_below(F.adm + (int64_t)t * F.m_cap, F.m_tot[t], E);
+            build_spine<D>(F, t, m_b, sp, lane);
+            if (lane == 0) stage_plan<D>(sp, m_b, STG_DS<D>());
+        }
+        __syncthreads();
+        {   // stage the shallow levels: rows of chunk k come from its node array's first stg_cnt[k] rows
+            const int64_t nrow = (int64_t)t * fsb_nodes_per_row(F.m_cap);
+            const bf16* node_mu = (const bf16*)F.node_mu + nrow * D;
+            const float4* aux = (const float4*)F.node_aux + nrow;
+            const int m_b = sp.m_b;
+            for (int k = 0; (m_b >> k) != 0; ++k) {
+                const int cnt = sp.stg_cnt[k];
+                if (!((m_b >> k) & 1) || cnt == 0) continue;
+                const int base = sp.stg_base[k];
+                const int64_t n0 = fsb_root_node(k, (m_b >> (k + 1)) << 1, F.m_cap);
+                for (int i = tid; i < cnt * CH; i += NWARP * 32) {
+                    const int r = i / CH, v = i % CH, row = base + r;
+                    const uint4 w = *(const uint4*)(node_mu + (n0 + r) * D + v * 8);
+                    *(uint4*)(stg_mu + (size_t)row * (D * 2) + (((v & ~STG_SW<D>()) | ((v ^ row) & STG_SW<D>())) << 4)) = w;
+                }
+                for (int i = tid; i < cnt; i += NWARP * 32) stg_aux[base + i] = aux[n0 + i];
+            }
+        }
+        __syncthreads();
+        const int width = f == 0 ? a.width : a.width2;
+        for (int qi = warp; qi < nq; qi += NWARP) {
+            const int qidx = blk * a.Bq + qi;
+            const float qpos = (float)(a.q_pos0 + qidx);
+            const bf16* qp = (const bf16*)a.q.ptr + b * a.q.sb + hd * a.q.sh + (int64_t)qidx * a.q.sn;
+            float* qs = qsm[warp];
+            __syncwarp();
+            for (int d = lane; d < DP; d += 32) qs[d] = (d < D) ? __bfloat162float(qp[d]) : 0.f;
+            __syncwarp();
+            float qq[FsbDim<D>::NPL];
+#pragma unroll
+            for (int i = 0; i < FsbDim<D>::NPL; ++i) { const float v = qs[lane + 32 * i]; qq[i] = f_mul(v, v); }
+            const float qn = f_mul(f_sqrt(fsb_warp_det_sum<D>(qq)), a.radius_coef);
+            int nv = 0;
+            const int c = beam<D, false, true>(F, t, sp, qs, qn, qpos, lam, sig, a.scale, width, lane, frs[warp], nv,
+                                               stg_mu, stg_aux);
+            if (lane < width) cand_sm[qi][f * WMAX + lane] = c;
+            if (lane == 0) nv_sm[qi] += nv;
+        }
+    }
+    __syncthreads();
+    // ---- union (second beam's repeats of a main cell blanked), outputs, and the per-query re-rank when asked ----
     for (int qi = warp; qi < a.Bq; qi += NWARP) {
         const int64_t row = ((int64_t)t * gridDim.x + blk) * a.Bq + qi;         // (B,H,Npad) flattened
         if (qi >= nq) {
-            if (lane < a.read_top) a.sel[row * a.read_top + lane] = -1;
+            if (lane < a.read_top && a.sel) a.sel[row * a.read_top + lane] = -1;
             if (a.cand && lane < Wc) a.cand[row * Wc + lane] = -1;
             if (a.nvis && lane == 0) a.nvis[row] = 0;
             continue;
         }
-        const int qidx = blk * a.Bq + qi;
-        const float qpos = a.use_spines ? (float)pos_dec : (float)(a.q_pos0 + qidx);
-        const bf16* qp = (const bf16*)a.q.ptr + b * a.q.sb + hd * a.q.sh + (int64_t)qidx * a.q.sn;
-        float* qs = qsm[warp];
-        __syncwarp();
-        for (int d = lane; d < DP; d += 32) qs[d] = (d < D) ? __bfloat162float(qp[d]) : 0.f;
-        __syncwarp();
-        float qq[FsbDim<D>::NPL];
-#pragma unroll
-        for (int i = 0; i < FsbDim<D>::NPL; ++i) { const float v = qs[lane + 32 * i]; qq[i] = f_mul(v, v); }
-        const float qn = f_mul(f_sqrt(fsb_warp_det_sum<D>(qq)), a.radius_coef);
-
-        int nv = 0;
-        int* fr = frs[warp];
-        const int c_main = beam<D>(a.main, t, sp[0], qs, qn, qpos, lam, sig, a.scale, a.width, lane, fr, nv);
-        int c_sec = -1;
-        if (a.width2 > 0) c_sec = beam<D>(a.second, t, sp[1], qs, qn, qpos, lam, sig, a.scale, a.width2, lane, fr, nv);
-        // ---- union: lanes 0..15 main, 16..31 second beam minus repeats of a main cell ----
-        const int c_sec_sh = __shfl_sync(FS_FULL, c_sec, lane & (WMAX - 1));     // every lane takes part
-        int cand = (lane < WMAX) ? c_main : c_sec_sh;
+        int cand = cand_sm[qi][lane];
         {
             bool dup = false;
             for (int o = 0; o < WMAX; ++o) {
@@ -307,13 +396,19 @@ __global__ void __launch_bounds__(NWARP * 32) fsb_select_kernel(SelArgs A) {
             }
             if (dup) cand = -1;
         }
-        if (lane >= WMAX && lane - WMAX >= a.width2) cand = -1;
-        if (lane < WMAX && lane >= a.width) cand = -1;
         if (a.cand) {
             if (lane < a.width) a.cand[row * Wc + lane] = cand;
             if (lane >= WMAX && lane - WMAX < a.width2) a.cand[row * Wc + a.width + lane - WMAX] = cand;
         }
-        if (a.nvis && lane == 0) a.nvis[row] = nv;
+        if (a.nvis && lane == 0) a.nvis[row] = nv_sm[qi];
+        if (a.read_top == 0) continue;          // beams only: the block-cooperative re-rank kernel follows
+        const int qidx = blk * a.Bq + qi;
+        const float qpos = (float)(a.q_pos0 + qidx);
+        const bf16* qp = (const bf16*)a.q.ptr + b * a.q.sb + hd * a.q.sh + (int64_t)qidx * a.q.sn;
+        float* qs = qsm[warp];
+        __syncwarp();
+        for (int d = lane; d < DP; d += 32) qs[d] = (d < D) ? __bfloat162float(qp[d]) : 0.f;
+        __syncwarp();
         // ---- re-rank: u = LSE_t((q.k_t) scale) + lam ceil erf(|p - (c+.5) 32| / (2 sig)) ----
         float u = -INFINITY;
         for (int i = 0; i < 32; ++i) {
@@ -436,6 +531,7 @@ __global__ void fsb_spine_kernel(fsattn_fsb_forest_t F, int n_visible, float* sp
 }  // namespace
 
 int fs_fsb_check_forest(const fsattn_fsb_forest_t& f, const char* what);
+int fs_fsb_rerank_block(const fsattn_fsb_select_t* a, cudaStream_t st);
 
 extern "C" int fsattn_fsb_spines(const fsattn_fsb_forest_t* forests, int32_t n_forests, int32_t n_visible,
                                  float* const* spine, int32_t* const* hdr, fsattn_stream_t stream) {
@@ -483,6 +579,9 @@ extern "C" int fsattn_fsb_select(const fsattn_fsb_select_t* a, fsattn_stream_t s
     A.a = *a;
     A.H = a->main.T / a->B;
     A.ncell_k = 0;
+    // prefill with full 128-query blocks and a candidate buffer: beams per query, then the block-cooperative re-rank
+    const bool two_pass = !a->use_spines && a->Bq == 128 && a->cand != nullptr;
+    if (two_pass) A.a.read_top = 0;
     const int nb = (a->N + a->Bq - 1) / a->Bq;
     cudaStream_t st = (cudaStream_t)stream;
     dim3 grid(nb, a->main.T);
@@ -508,11 +607,29 @@ extern "C" int fsattn_fsb_select(const fsattn_fsb_select_t* a, fsattn_stream_t s
         }
         return FSATTN_OK;
     } else {
+        FS_UNSUPPORTED(a->Bq > 128, "fsb_select: query blocks of %d (at most 128)", a->Bq);
+        cudaError_t e = cudaSuccess;
         switch (a->main.D) {
-            case 64: fsb_select_kernel<64, 8><<<grid, 256, 0, st>>>(A); break;
-            case 96: fsb_select_kernel<96, 8><<<grid, 256, 0, st>>>(A); break;
-            default: fsb_select_kernel<128, 8><<<grid, 256, 0, st>>>(A); break;
+            case 64:
+                e = cudaFuncSetAttribute(fsb_select_kernel<64, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SelSmem<64>::TOTAL);
+                if (e == cudaSuccess) fsb_select_kernel<64, 8><<<grid, 256, SelSmem<64>::TOTAL, st>>>(A);
+                break;
+            case 96:
+                e = cudaFuncSetAttribute(fsb_select_kernel<96, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SelSmem<96>::TOTAL);
+                if (e == cudaSuccess) fsb_select_kernel<96, 8><<<grid, 256, SelSmem<96>::TOTAL, st>>>(A);
+                break;
+            default:
+                e = cudaFuncSetAttribute(fsb_select_kernel<128, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SelSmem<128>::TOTAL);
+                if (e == cudaSuccess) fsb_select_kernel<128, 8><<<grid, 256, SelSmem<128>::TOTAL, st>>>(A);
+                break;
+        }
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            fs_set_error("fsb_select: shared-memory opt-in failed: %s", cudaGetErrorString(e));
+            return FSATTN_ELAUNCH;
         }
     }
-    return fs_check_launch("fsb_select_kernel");
+    rc = fs_check_launch("fsb_select_kernel");
+    if (rc != FSATTN_OK || !two_pass) return rc;
+    return fs_fsb_rerank_block(a, st);
 }

@@ -97,6 +97,17 @@ class Rotary(nn.Module):
         return c
 
 
+_SIDE_STREAMS = {}
+
+
+def _side_stream(device):
+    """One extra stream per device for work that overlaps the main stream inside a layer."""
+    key = (device.type, device.index)
+    if key not in _SIDE_STREAMS:
+        _SIDE_STREAMS[key] = torch.cuda.Stream(device=device)
+    return _SIDE_STREAMS[key]
+
+
 class FSAttn(nn.Module):
     VARIANTS = ("cell_topk",)
 
@@ -315,9 +326,24 @@ class FSAttn(nn.Module):
         s = self.cell_stride
         P, Wc = self._pool_cfg()
         cos, sin = self.rope.tables_bf16(N)
-        sr = ops.window_prefill(Q, K, V, cos, sin, self.window_size, self.scale)
-        kbar, ceil = cache.prefill(K, V)
         ncell = N // s
+        fo = build_done = None
+        if self.fsb_enabled and ncell > 0:
+            # FS-B: statistics first, then the forest build on a side stream while the window branch runs on this one.
+            # The build is a chain of dependent levels on a few SMs (its largest chunk sets the time), so it hides behind
+            # the window kernel (the reference overlaps its window branch the same way, attention.py:254 FSB_WINDOW_OVERLAP)
+            kbar, ceil = cache.prefill(K, V)
+            fo = cache.fsb_forests(kbar, ceil, self)
+            cur = torch.cuda.current_stream(Q.device)
+            side = _side_stream(Q.device)
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                fo.ingest(ncell)
+                build_done = torch.cuda.Event()
+                build_done.record(side)
+        sr = ops.window_prefill(Q, K, V, cos, sin, self.window_size, self.scale)
+        if fo is None:
+            kbar, ceil = cache.prefill(K, V)
         M = (N + s - 1) // s
         kk = min(self.cell_topk, M)
         Bq = min(self._cell_block, N)
@@ -330,8 +356,7 @@ class FSAttn(nn.Module):
         elif self.fsb_enabled:
             # src/fsattn/fsb_tree.py:2368-2520: both forests over the prompt's cells, then per 128-query block the two
             # beams, the union of their candidates and the token-level re-rank
-            fo = cache.fsb_forests(kbar, ceil, self)
-            fo.ingest(ncell)
+            torch.cuda.current_stream(Q.device).wait_event(build_done)
             sel = ops.fsb_select(fo, Q, K, lam, sigma, scale=self.scale, N=N, Bq=Bq, width=self.fsb_width,
                                  width2=self._fsb_w2(fo), read_top=self.fsb_read_top,
                                  radius_coef=self.fsb_bound_radius_coef)

@@ -545,7 +545,9 @@ def fsb_select(forests: FsbForests, Q, K, lam, sigma, *, scale: float, N: int = 
     nb = (N + Bq - 1) // Bq
     dev = Q.device
     sel = torch.empty(B, H, nb * Bq, read_top, dtype=torch.int32, device=dev)
-    cand = torch.empty(B, H, nb * Bq, width + width2, dtype=torch.int32, device=dev) if debug else None
+    # full blocks hand their candidates to the block-cooperative re-rank through this buffer
+    need_cand = debug or (not decode and Bq == 128)
+    cand = torch.empty(B, H, nb * Bq, width + width2, dtype=torch.int32, device=dev) if need_cand else None
     nvis = torch.empty(B, H, nb * Bq, dtype=torch.int32, device=dev) if debug else None
     lam, sigma = _f32(lam).to(dev), _f32(sigma).to(dev)
     a = L.FsbSelect()

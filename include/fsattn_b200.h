@@ -303,7 +303,10 @@ FSATTN_API int fsattn_fsb_spines(const fsattn_fsb_forest_t* forests, int32_t n_f
  * Prefill (n_q > 1): q (B,H,N,D) bf16, queries q_pos0 .. q_pos0+N-1 in blocks of Bq; block b sees the cells
  * [0, (q_pos0 + b Bq) / 32); spines are built on the fly. Decode (use_spines = 1): one query per row at *pos with the
  * spines of fsattn_fsb_spines. k: raw token keys (B,H,>=cells*32,D) bf16, or int8 codes + scales (kq/ks) when k.ptr is NULL.
- * sel (B,H,Npad,K) int32 (-1 pad). Optional outputs for tests: cand (B,H,Npad,W_main+W_second) int32, nvis (B,H,Npad). */
+ * sel (B,H,Npad,K) int32 (-1 pad). cand (B,H,Npad,W_main+W_second) int32: the beams' candidates after the union; in
+ * prefill with Bq = 128 it doubles as the hand-off to the block-cooperative re-rank (each distinct candidate cell of a
+ * block staged once, scored with bf16 tensor-core tiles) - without it the slower one-warp-per-query re-rank runs.
+ * nvis (B,H,Npad) optional visit counts. */
 typedef struct {
     fsattn_fsb_forest_t main, second;
     fsattn_bhnd_t q, k;
