@@ -25,6 +25,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 PUBLISHED_FSL_DECODE_TPS_131K = 515.1      # A100-40GB, README.md:62 of the reference
+NCU_DECODE_KERNEL_DRAM_BYTES = 1.87e6       # profiles/fsl_decode_kernel_340m_ncu_full.md
 PUBLISHED_FSB_DECODE_TPS_131K = 462.7      # A100-40GB, README.md:63 of the reference
 PUBLISHED_FSB_PREFILL_KTOKS_131K = 137.8   # A100-40GB, README.md:63 of the reference
 W_BYTES_341M = 2 * (24 * (4 * 1024 ** 2 + 3 * 1024 * 2816) + 32000 * 1024)
@@ -319,7 +320,10 @@ def run_ours(args):
         "e2e": {"value": world * B * K / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 8 * B},
         "gpu_launches": K * (5 * nL + 1),
         "roofline": {"kernel": "fsl_decode_kernel", "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind, "bytes_per_launch": kbytes,
+                     "frac": achieved / peak, "traffic": NCU_DECODE_KERNEL_DRAM_BYTES if (B == 1 and args.model == "340m") else None,
+                     "traffic_source": "ncu dram__bytes_read+write per launch, profiles/fsl_decode_kernel_340m_ncu_full.md "
+                                       "(captured at ctx 32768; the FS-L decode read does not depend on the context)",
+                     "peak_kind": peak_kind, "bytes_per_launch": kbytes,
                      "avg_launch_us": k_avg_ms * 1e3, "median_launch_us": k_med_ms * 1e3,
                      "how": "launched alone with an L2 flush before every launch, CUDA events on the launching stream"},
         "step_roofline": {"step_bytes": step_bytes, "achieved_gbs": step_bytes / (ms / K * 1e-3) / 1e9,
