@@ -117,6 +117,12 @@ class FSAttn(nn.Module):
                  max_seq_len: int = 8192, lr_scale_mode: str = "learn", cell_stride: int = 64, cell_topk: int = 1,
                  cell_select: str = "score", **kwargs):
         super().__init__()
+        # everything but the width, so that a head shard of this layer can be constructed the same way
+        self._ctor_kwargs = dict(window_size=window_size, sigma_init=sigma_init, learnable_sigma=learnable_sigma,
+                                 dropout=dropout, bias=bias, causal=causal, long_range_variant=long_range_variant,
+                                 use_rope=use_rope, rope_long_range=rope_long_range, max_seq_len=max_seq_len,
+                                 lr_scale_mode=lr_scale_mode, cell_stride=cell_stride, cell_topk=cell_topk,
+                                 cell_select=cell_select, **kwargs)
         assert d_model % n_heads == 0, "d_model must be divisible by n_heads"
         assert long_range_variant in self.VARIANTS, f"Unknown variant '{long_range_variant}'"
         assert cell_select in ("score",), f"bad cell_select '{cell_select}'"

@@ -211,7 +211,8 @@ def make_caches(model, *, lean_prefill=False, reserve=0, linear=None, retain_kv:
         raise NotImplementedError("the LinearFSCache streaming prefill is not part of this build")
     caches = []
     for blk in model.blocks:
-        c = FSKVCache(blk.attn.fsattn, lean_prefill=lean_prefill, retain_kv=retain_kv)
+        a = blk.attn.fsattn
+        c = FSKVCache(getattr(a, "inner", a), lean_prefill=lean_prefill, retain_kv=retain_kv)   # a head shard wraps its layer
         c.reserve = reserve
         caches.append(c)
     return caches

@@ -180,6 +180,7 @@ class GraphedDecoder:
         self.Lmax = int(Lmax)
         self.blocks = list(model.blocks)
         self.attn = [b.attn.fsattn for b in self.blocks]
+        self.attn_core = [getattr(a, "inner", a) for a in self.attn]      # the layer the kernels run through (head shards wrap it)
         self.prompt = prompt_ids
         self.kv = kv
         self.cache = None
@@ -201,7 +202,7 @@ class GraphedDecoder:
         self.fsb = any(a.fsb_enabled for a in self.attn)
         if kv == "bounded" and self.fsb:
             kv = "int8"      # FS-B reads any admitted cell: it keeps the full (int8) store
-        if kv == "bounded" and not (P0 >= self.attn[0].window_size and _kvb.supported(self.attn, self.dt, self.dev)):
+        if kv == "bounded" and not (P0 >= self.attn[0].window_size and _kvb.supported(self.attn_core, self.dt, self.dev)):
             kv = "int8"      # prompts shorter than the window keep the full store (decode_graph.py:89-93)
         for c in self.cache:
             if kv == "bounded":
@@ -220,7 +221,7 @@ class GraphedDecoder:
         d, f = m.d_model, self.blocks[0].ffn.w_gate.weight.shape[0]
         z = dict(dtype=torch.bfloat16, device=self.dev)
         self.x = torch.zeros(B, d, **z)             # residual stream of the current token
-        self.qkv = torch.zeros(B, 3 * d, **z)
+        self.qkv = torch.zeros(B, self.attn[0]._ensure_qkv_cache()[0].shape[0], **z)      # 3 d, or 3 d / g for a head shard
         self.y = torch.zeros(B, d, **z)
         self.act = torch.zeros(B, f, **z)
         self.logits = torch.zeros(B, m.vocab_size, **z)
@@ -268,7 +269,7 @@ class GraphedDecoder:
             # FS-B (experiments/scaling/decode_graph.py:499-541, src/fsattn/fsb_tree.py:3598-3674): at a query-block
             # change every layer's forests take in the cells completed before the block and rebuild their spines, as
             # plain launches ahead of the replay; buffers keep their addresses, so the graph is never re-captured
-            for a, c in zip(self.attn, self.cache):
+            for a, c in zip(self.attn_core, self.cache):
                 if a.fsb_enabled:
                     c.fsb_block_change(self.pos, a)
         if self.graph is None and self._steps >= self.eager_steps:
