@@ -227,7 +227,9 @@ def run_ours(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
+        import datetime
+        # a stuck collective aborts the run after two minutes instead of holding the GPUs
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     ctx, K, Wm = args.ctx, args.steps, max(args.warmup, 3)
     torch.manual_seed(0)
     model = FreeSoloLM.from_config(args.model, max_seq_len=ctx + 512, **serve_kwargs("sparse")).to(torch.bfloat16).to(dev).eval()
@@ -243,6 +245,9 @@ def run_ours(args):
     warm = GraphedDecoder(model, ids[:, :min(ctx, 2048)], Lmax=min(ctx, 2048) + 64, device=dev, kv=args.kv)
     warm.prefill()
     del warm
+    if os.environ.get("FSATTN_BENCH_TRACE", "0") == "1":
+        torch.cuda.synchronize()
+        print(f"[bench] rank {rank}: warm-up prefill ok", file=sys.stderr, flush=True)
     gd = GraphedDecoder(model, ids, Lmax=ctx + total, device=dev, kv=args.kv)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -254,7 +259,7 @@ def run_ours(args):
     def mark(what):
         if os.environ.get("FSATTN_BENCH_TRACE", "0") == "1":
             torch.cuda.synchronize()
-            print(f"[bench] {what} ok", file=sys.stderr, flush=True)
+            print(f"[bench] rank {rank}: {what} ok", file=sys.stderr, flush=True)
     mark("prefill")
     for _ in range(Wm):
         gd.step()
@@ -297,9 +302,12 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, e2e_ms = t.tolist()
     faults = gd.kv_faults()
+    if world > 1:
+        # every rank leaves the group together; what follows on rank 0 needs no communication
+        barrier()
+        dist.destroy_process_group()
+        mark("process group closed")
     if rank != 0:
-        if world > 1:
-            dist.destroy_process_group()
         return
     peak, peak_kind = _peaks()
     a0 = gd.attn_core[0]
@@ -346,8 +354,6 @@ def run_ours(args):
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline_sample()
     print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
 
 
 def main():
