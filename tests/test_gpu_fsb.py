@@ -384,3 +384,41 @@ def test_fsb_graph_decoder_matches_eager_steps(kv):
     assert (mt > 0).all() and (fo.m_tot[1].cpu() <= mt).all()
     want = cached_generate(m, ids, 2, device=dev, kv=kv)
     assert torch.equal(want[:, P0].cpu(), runs[1][0][:, 0])
+
+
+@pytest.mark.parametrize("D,B", [(96, 1), (128, 1), (64, 2)])
+def test_select_other_head_dims_and_batch(D, B):
+    """Head dims of the 743M-class configs (96) and 128, and batch 2: prefill selections (staged beams + block-cooperative
+    re-rank) and a decode query against the oracle on the same bf16 inputs."""
+    from freesolo_b200 import ops
+    from oracle import fsb
+    dev = _dev()
+    H, N = 2, 900
+    g = torch.Generator().manual_seed(100 + D + B)
+    Q = torch.randn(B, H, N, D, generator=g).to(torch.bfloat16)
+    K = torch.randn(B, H, N, D, generator=g).to(torch.bfloat16)
+    lam = 0.5 + torch.rand(H, generator=g)
+    sigma = 2.0 + torch.rand(H, generator=g) * 30
+    ncell = N // S
+    Qd, Kd = Q.to(dev), K.to(dev)
+    kbar, ceil = _gpu_stats(Kd, ncell)
+    ce = ceil.cpu()
+    tau = torch.quantile(ce.transpose(0, 1).reshape(H, -1), 0.3, dim=1)
+    tau_u = torch.quantile(ce.transpose(0, 1).reshape(H, -1), 0.7, dim=1)
+    fo = ops.FsbForests(kbar, ceil, tau, tau_u, cap_cells=ncell + 4)
+    fo.ingest(ncell)
+    scale = D ** -0.5
+    sel = ops.fsb_select(fo, Qd, Kd, lam, sigma, scale=scale, N=N).cpu().long()
+    so, mo = fsb.fsb_select_prefill(Q.float(), K.float(), kbar.cpu(), ce, tau, tau_u, lam, sigma, scale)
+    diff = (sel[:, :, :N] != so[:, :, :N]).any(-1)
+    assert (diff & (mo[:, :, :N] > 1e-4)).float().mean() < 0.005, f"D={D} B={B}: prefill selections differ beyond beam near-ties"
+    assert diff.float().mean() < 0.02
+    # one decode query per row at position N (block start 896 -> 28 visible cells)
+    n_vis = min((N // 128) * 128 // S, ncell)
+    fo.build_spines(n_vis)
+    pos_t = torch.full((), N, dtype=torch.int64, device=dev)
+    qd = torch.randn(B, H, 1, D, generator=g).to(torch.bfloat16)
+    sd = ops.fsb_select(fo, qd.to(dev), Kd, lam, sigma, scale=scale, pos=pos_t).cpu().long()
+    sdo, mdo = fsb.fsb_select_decode(qd[:, :, 0].float(), N, K.float(), kbar.cpu(), ce, ncell, tau, tau_u, lam, sigma, scale)
+    bad = (sd[:, :, 0] != sdo).any(-1) & (mdo > 1e-4)
+    assert int(bad.sum()) <= 1
