@@ -239,6 +239,8 @@ class GraphedDecoder:
         pdl = os.environ.get("FSATTN_PDL", "1") == "1"
         skip_attn = os.environ.get("FSATTN_DEBUG_SKIP_ATTN", "0") == "1"     # timing experiments only
         x.copy_(m.tok_emb(self.tok).view(x.shape))
+        if x.shape[0] > 8:
+            return self._trunk_step_batched()
         for i, blk in enumerate(self.blocks):
             a = self.attn[i]
             wqkv, _ = a._ensure_qkv_cache()
@@ -250,6 +252,24 @@ class GraphedDecoder:
             ops.trunk_gemv(x, wgu, norm_w=blk.ln2.weight, eps=blk.ln2.eps, swiglu=True, out=self.act, pdl=pdl)
             ops.trunk_gemv(self.act, blk.ffn.w_down.weight, res=x, out=x, pdl=pdl)
         ops.trunk_gemv(x, m.lm_head.weight, norm_w=m.ln_final.weight, eps=m.ln_final.eps, out=self.logits, pdl=pdl)
+        self.tok.copy_(self.logits.argmax(dim=-1, keepdim=True))
+        self.pos_t.add_(1)
+
+    def _trunk_step_batched(self):
+        """More than 8 sequences per step: the projections are real GEMMs (weights read once for all rows), so they go to
+        the library (cuBLAS through torch) instead of the row-streaming GEMV kernels; the attention step is the same
+        single launch per layer, now bandwidth-bound on the sequences' KV state."""
+        m, x = self.m, self.x
+        for i, blk in enumerate(self.blocks):
+            a = self.attn[i]
+            wqkv, _ = a._ensure_qkv_cache()
+            torch.matmul(blk.ln1(x), wqkv.t(), out=self.qkv)
+            a.graph_decode_attn(self.qkv, self.bufs[i], y=self.y, pdl=False)
+            x.add_(F.linear(self.y, a.W_o.weight))
+            wgu, f = blk.ffn._ensure_gu_cache()
+            gu = F.linear(blk.ln2(x), wgu)
+            x.add_(F.linear(F.silu(gu[:, :f]) * gu[:, f:], blk.ffn.w_down.weight))
+        torch.matmul(m.ln_final(x), m.lm_head.weight.t(), out=self.logits)
         self.tok.copy_(self.logits.argmax(dim=-1, keepdim=True))
         self.pos_t.add_(1)
 
