@@ -254,39 +254,20 @@ __global__ void __launch_bounds__(RB_THREADS) readout_block_kernel(const fsattn_
     const bf16* vbase = (const bf16*)a.v.ptr + b * a.v.sb + h * a.v.sh;
     constexpr int CH = D / 8;
     constexpr int DPL = D / 32;
-    // Two stages of GH = GC/2 cells each: the loads of round r+1 (cp.async, 16 bytes per request, zero-filled past n_kv)
-    // are in flight while round r is computed, so a round costs max(load, compute) instead of their sum.
-    constexpr int GH = S::GC / 2;
-    auto stage = [&](int g0, int buf) {
-        const int gc = min(GH, n_distinct - g0);
-        unsigned char* kd = ks + (size_t)buf * GH * 32 * S::ROWB;
-        unsigned char* vd = vs + (size_t)buf * GH * 32 * S::ROWB;
+    for (int g0 = 0; g0 < n_distinct; g0 += S::GC) {
+        const int gc = min(S::GC, n_distinct - g0);
         for (int i = tid; i < gc * 32 * CH; i += RB_THREADS) {
             const int row = i / CH, e = i - row * CH;             // row = local cell * 32 + token
             const int64_t tok = (int64_t)ucell[g0 + (row >> 5)] * FSATTN_CELL + (row & 31);
-            const bool ok = tok < a.n_kv;
-            const int64_t tk = ok ? tok : 0;
-            const uint32_t kdst = (uint32_t)__cvta_generic_to_shared(kd + (size_t)row * S::ROWB + e * 16);
-            const uint32_t vdst = (uint32_t)__cvta_generic_to_shared(vd + (size_t)row * S::ROWB + e * 16);
-            const int nbytes = ok ? 16 : 0;
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(kdst), "l"(kbase + tk * a.k.sn + e * 8), "r"(nbytes));
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(vdst), "l"(vbase + tk * a.v.sn + e * 8), "r"(nbytes));
-        }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-    };
-    if (n_distinct > 0) stage(0, 0);
-    int rbuf = 0;
-    for (int g0 = 0; g0 < n_distinct; g0 += GH, rbuf ^= 1) {
-        const int gc = min(GH, n_distinct - g0);
-        if (g0 + GH < n_distinct) {
-            stage(g0 + GH, rbuf ^ 1);
-            asm volatile("cp.async.wait_group 1;" ::: "memory");
-        } else {
-            asm volatile("cp.async.wait_group 0;" ::: "memory");
+            uint4 kw = make_uint4(0u, 0u, 0u, 0u), vw = kw;
+            if (tok < a.n_kv) {
+                kw = reinterpret_cast<const uint4*>(kbase + tok * a.k.sn)[e];
+                vw = reinterpret_cast<const uint4*>(vbase + tok * a.v.sn)[e];
+            }
+            *reinterpret_cast<uint4*>(ks + (size_t)row * S::ROWB + e * 16) = kw;
+            *reinterpret_cast<uint4*>(vs + (size_t)row * S::ROWB + e * 16) = vw;
         }
         __syncthreads();
-        const unsigned char* ksr = ks + (size_t)rbuf * GH * 32 * S::ROWB;
-        const unsigned char* vsr = vs + (size_t)rbuf * GH * 32 * S::ROWB;
         // each warp: its 16 queries, every selection that falls into this round
         for (int qi = warp * 16; qi < warp * 16 + 16; qi++) {
             const int qpos = a.q_pos0 + q0 + qi;
@@ -298,7 +279,7 @@ __global__ void __launch_bounds__(RB_THREADS) readout_block_kernel(const fsattn_
                 const int lc = u - g0;
                 const int tok = ucell[u] * FSATTN_CELL + lane;
                 const bool tok_ok = (tok < a.n_kv) && (tok < qpos);
-                const unsigned char* krow = ksr + (size_t)(lc * 32 + lane) * S::ROWB;
+                const unsigned char* krow = ks + (size_t)(lc * 32 + lane) * S::ROWB;
                 float d0 = 0.f, d1 = 0.f;
 #pragma unroll
                 for (int e = 0; e < CH; e++) {
@@ -320,7 +301,7 @@ __global__ void __launch_bounds__(RB_THREADS) readout_block_kernel(const fsattn_
                 float acc[DPL];
 #pragma unroll
                 for (int jj = 0; jj < DPL; jj++) acc[jj] = accs[qi * D + lane + 32 * jj] * alpha;
-                const unsigned char* vcell = vsr + (size_t)(lc * 32) * S::ROWB;
+                const unsigned char* vcell = vs + (size_t)(lc * 32) * S::ROWB;
 #pragma unroll 8
                 for (int t = 0; t < FSATTN_CELL; t++) {
                     const float pt = __shfl_sync(FS_FULL, p, t);
