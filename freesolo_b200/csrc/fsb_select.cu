@@ -221,14 +221,20 @@ __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, co
             score = f_add(content, f_mul(f_mul(lam, am), e));
         }
         nvis += __popc(__ballot_sync(FS_FULL, valid));
-        // ---- rank the children: (score desc, position asc) ----
-        int rank = 0;
-#pragma unroll 8
-        for (int o = 0; o < 32; ++o) {
-            const float so = __shfl_sync(FS_FULL, score, o);
-            rank += (so > score || (so == score && o < lane)) ? 1 : 0;
-        }
+        // ---- the best (W - carried) children by (score desc, position asc): one warp-wide max per kept child ----
         const int ncar = __popc(cmask & 0xffffu);
+        uint32_t key = 0;                                  // order-preserving image of the score; 0 = not a contender
+        if (valid && score > 0.5f * FS_NEG_SCORE) {
+            const uint32_t bits = __float_as_uint(score + 0.0f);
+            key = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
+        }
+        int rank = WMAX;
+        for (int r = 0; r < W - ncar; ++r) {
+            const uint32_t kmax = __reduce_max_sync(FS_FULL, key);
+            if (kmax == 0) break;
+            const int win = __ffs(__ballot_sync(FS_FULL, key == kmax)) - 1;      // ties: the lower position wins
+            if (lane == win) { rank = r; key = 0; }
+        }
         int* fm = fr + WMAX;                   // fr: WMAX refs then WMAX metas
         if (lane < WMAX) fr[lane] = -1;
         __syncwarp();
@@ -236,7 +242,7 @@ __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, co
             const int pos = __popc(cmask & ((1u << lane) - 1));
             fr[pos] = ref; fm[pos] = meta;
         }
-        if (valid && score > 0.5f * FS_NEG_SCORE && ncar + rank < W) {
+        if (rank < WMAX) {
             fr[ncar + rank] = cref; fm[ncar + rank] = cmeta;
         }
         __syncwarp();

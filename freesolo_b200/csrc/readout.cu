@@ -108,6 +108,7 @@ __global__ void __launch_bounds__(256) readout_combine_kernel(const fsattn_reado
 }
 
 int fs_readout_block(const fsattn_readout_combine_t* a, cudaStream_t st);
+int fs_readout_mma(const fsattn_readout_combine_t* a, cudaStream_t st);
 
 extern "C" int fsattn_readout_combine(const fsattn_readout_combine_t* a, fsattn_stream_t stream) {
     FS_REQUIRE(a != nullptr && a->q.ptr && a->k.ptr && a->v.ptr && a->sel && a->y && a->norm_w && a->lrs,
@@ -120,7 +121,12 @@ extern "C" int fsattn_readout_combine(const fsattn_readout_combine_t* a, fsattn_
                "readout_combine: Q and K rows must be 16-byte aligned");
     cudaStream_t st = (cudaStream_t)stream;
     // whole query blocks of 128 whose cells fit the block kernel's bitmap: the block-cooperative kernel
-    if (a->Bq == 128 && a->q_pos0 % 128 == 0 && a->n_kv <= 32768 * FSATTN_CELL && a->N >= 128) return fs_readout_block(a, st);
+    const bool blocks = a->Bq == 128 && a->q_pos0 % 128 == 0 && a->n_kv <= 32768 * FSATTN_CELL && a->N >= 128;
+    FS_REQUIRE(a->impl >= 0 && a->impl <= 2, "readout_combine: impl %d", a->impl);
+    FS_UNSUPPORTED(a->impl == 2 && !(blocks && a->D == 64), "readout_combine: the tensor-core kernel takes whole 128-query "
+                   "blocks at head_dim 64");
+    if (blocks && a->D == 64 && a->impl == 2) return fs_readout_mma(a, st);
+    if (blocks) return fs_readout_block(a, st);
     dim3 grid((a->N + 7) / 8, a->B * a->H);
     switch (a->D) {
         case 64: readout_combine_kernel<64><<<grid, 256, 0, st>>>(*a); break;

@@ -77,7 +77,7 @@ class ReadoutCombine(C.Structure):
                 ("norm_w", vp), ("lrs", vp),
                 ("B", i32), ("H", i32), ("D", i32), ("N", i32), ("n_kv", i32), ("Bq", i32), ("kk", i32),
                 ("q_pos0", i32),
-                ("scale", f32), ("eps", f32)]
+                ("scale", f32), ("eps", f32), ("impl", i32)]
 
 
 class FslState(C.Structure):

@@ -6,6 +6,7 @@ Every function raises when its tensors are not CUDA tensors: there is no CPU pat
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
@@ -220,7 +221,7 @@ def window_prefill_static(Q, K, V, cos, sin, W: int, scale: float, pos0: int = 0
 
 
 def readout_combine(Q, K, V, sel, sr, norm_w, lrs, eps: float, *, scale: float, Bq: int, n_kv: int | None = None,
-                    q_pos0: int = 0, out=None):
+                    q_pos0: int = 0, out=None, impl: int | None = None):
     """y (B,N,H*D) bf16 = bf16(sr + lrs[h] * lr_norm(bf16(readout of the selected cells))). sr (B,N,H*D) bf16 or None
     (treated as zero); out may be sr itself (in place)."""
     _need_cuda(Q, K, V, sel)
@@ -238,6 +239,7 @@ def readout_combine(Q, K, V, sel, sr, norm_w, lrs, eps: float, *, scale: float, 
     a.norm_w, a.lrs = norm_w.data_ptr(), lrs.data_ptr()
     a.B, a.H, a.D, a.N, a.n_kv, a.Bq, a.kk, a.q_pos0 = B, H, D, N, int(K.shape[2] if n_kv is None else n_kv), Bq, kk, q_pos0
     a.scale, a.eps = float(scale), float(eps)
+    a.impl = int(os.environ.get("FSATTN_READOUT_IMPL", "0")) if impl is None else int(impl)
     L.call("fsattn_readout_combine", a, _stream(Q))
     return out
 

@@ -165,6 +165,7 @@ typedef struct {
     const float* norm_w; const float* lrs;
     int32_t B, H, D, N, n_kv, Bq, kk, q_pos0;
     float scale, eps;
+    int32_t impl; /* 0 = choose; 1 = CUDA-core kernels; 2 = tensor-core tiles (whole 128-query blocks, head_dim 64) */
 } fsattn_readout_combine_t;
 FSATTN_API int fsattn_readout_combine(const fsattn_readout_combine_t* a, fsattn_stream_t stream);
 

@@ -402,3 +402,30 @@ def test_other_head_dims_layer(dev, D):
         yo, s_o, mo = orc.decode(Q[:, :, sl], K[:, :, sl], V[:, :, sl])
         _sel_check(so.unsqueeze(2), s_o, mo, f"D={D} decode step {t} selection")
         _close(yd.view(-1), yo.reshape(-1), f"D={D} decode step {t} output", mean_rel=6e-3)
+
+
+@pytest.mark.parametrize("kind", KINDS)
+def test_readout_combine_tensor_core_tiles(dev, kind):
+    """The mma.sync readout (whole 128-query blocks, head_dim 64) against the oracle and against the CUDA-core kernel."""
+    from freesolo_b200 import ops
+    g, Q, K, V = _g(kind)
+    N = int(g["N"])
+    p, pd = _params(g), _params(g, dev)
+    sel = torch.from_numpy(g["sel_prefill"])
+    B, H = Q.shape[:2]
+    sr = torch.randn(B, N, H * 64, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16)
+    args = (Q[:, :, :N].to(dev), K[:, :, :N].to(dev), V[:, :, :N].to(dev), sel.to(dev).contiguous(), sr.to(dev),
+            pd["norm_w"], pd["lrs"], float(g["eps"]))
+    y2 = ops.readout_combine(*args, scale=0.125, Bq=128, n_kv=N, impl=2)
+    y1 = ops.readout_combine(*args, scale=0.125, Bq=128, n_kv=N, impl=1)
+    o = fsl.cell_readout(Q[:, :, :N].float(), K[:, :, :N].float(), V[:, :, :N].float(), sel, 32, 128, 0.125, 0, N)
+    want = fsl.lr_norm_combine(sr.view(B, N, H, 64).transpose(1, 2), o, p["norm_w"], p["lrs"], float(g["eps"]))
+    _close(y2, want, f"{kind} tensor-core readout+combine vs oracle")
+    _close(y2, y1, f"{kind} tensor-core vs CUDA-core readout", mean_rel=5e-4)
+    # without a window output, and in place
+    y0 = ops.readout_combine(*args[:4], None, *args[5:], scale=0.125, Bq=128, n_kv=N, impl=2)
+    want0 = fsl.lr_norm_combine(torch.zeros(B, H, N, 64), o, p["norm_w"], p["lrs"], float(g["eps"]))
+    _close(y0, want0, f"{kind} tensor-core readout alone", mean_rel=3e-3)
+    srd = sr.to(dev).clone()
+    y3 = ops.readout_combine(*args[:4], srd, *args[5:], scale=0.125, Bq=128, n_kv=N, out=srd, impl=2)
+    assert torch.equal(y3, y2)
