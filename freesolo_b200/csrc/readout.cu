@@ -125,7 +125,7 @@ extern "C" int fsattn_readout_combine(const fsattn_readout_combine_t* a, fsattn_
     FS_REQUIRE(a->impl >= 0 && a->impl <= 2, "readout_combine: impl %d", a->impl);
     FS_UNSUPPORTED(a->impl == 2 && !(blocks && a->D == 64), "readout_combine: the tensor-core kernel takes whole 128-query "
                    "blocks at head_dim 64");
-    if (blocks && a->D == 64 && a->impl == 2) return fs_readout_mma(a, st);
+    if (blocks && a->D == 64 && a->impl != 1) return fs_readout_mma(a, st);
     if (blocks) return fs_readout_block(a, st);
     dim3 grid((a->N + 7) / 8, a->B * a->H);
     switch (a->D) {
