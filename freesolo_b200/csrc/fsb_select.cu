@@ -128,7 +128,7 @@ __device__ __forceinline__ int count_below(const int* adm, int m_tot, int E) {
 
 // ---- one beam (one warp). Returns the frontier's cell in lanes 0..15 (-1 none); adds the scored children to nvis ----
 template <int D, bool PREFETCH = false, bool STAGED = false>
-__device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, const float* qs, float qn, float qpos,
+__device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, const uint32_t (&qp)[D / 2], float qn, float qpos,
                     float lam, float sig, float scale, int width, int lane, int* fr, int& nvis,
                     const unsigned char* stg_mu = nullptr, const float4* stg_aux = nullptr) {
     constexpr int DP = FsbDim<D>::DP;
@@ -196,21 +196,21 @@ __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, co
                     for (int v = 0; v < D / 8; ++v) w[v] = mr[v];
                     ax = aux[REF_ID(cref)];
                 }
+                // the query sits in registers as bf16 pairs (it is a bf16 tensor): no shared-memory traffic for it
 #pragma unroll
                 for (int v = 0; v < D / 8; ++v) {
-                    const float4 qa = *(const float4*)(qs + v * 8), qb = *(const float4*)(qs + v * 8 + 4);
-                    s0 = fmaf(qa.x, bf_lo(w[v].x), s0); s1 = fmaf(qa.y, bf_hi(w[v].x), s1);
-                    s2 = fmaf(qa.z, bf_lo(w[v].y), s2); s3 = fmaf(qa.w, bf_hi(w[v].y), s3);
-                    s0 = fmaf(qb.x, bf_lo(w[v].z), s0); s1 = fmaf(qb.y, bf_hi(w[v].z), s1);
-                    s2 = fmaf(qb.z, bf_lo(w[v].w), s2); s3 = fmaf(qb.w, bf_hi(w[v].w), s3);
+                    s0 = fmaf(bf_lo(qp[v * 4 + 0]), bf_lo(w[v].x), s0); s1 = fmaf(bf_hi(qp[v * 4 + 0]), bf_hi(w[v].x), s1);
+                    s2 = fmaf(bf_lo(qp[v * 4 + 1]), bf_lo(w[v].y), s2); s3 = fmaf(bf_hi(qp[v * 4 + 1]), bf_hi(w[v].y), s3);
+                    s0 = fmaf(bf_lo(qp[v * 4 + 2]), bf_lo(w[v].z), s0); s1 = fmaf(bf_hi(qp[v * 4 + 2]), bf_hi(w[v].z), s1);
+                    s2 = fmaf(bf_lo(qp[v * 4 + 3]), bf_lo(w[v].w), s2); s3 = fmaf(bf_hi(qp[v * 4 + 3]), bf_hi(w[v].w), s3);
                 }
                 rad = ax.x; am = ax.y; pm = __float_as_int(ax.z); cmeta = __float_as_int(ax.w);
             } else {
                 const float* x = S.node[-cref - 2];
-#pragma unroll 8
+#pragma unroll
                 for (int d = 0; d < D; d += 4) {
-                    s0 = fmaf(qs[d], x[d], s0); s1 = fmaf(qs[d + 1], x[d + 1], s1);
-                    s2 = fmaf(qs[d + 2], x[d + 2], s2); s3 = fmaf(qs[d + 3], x[d + 3], s3);
+                    s0 = fmaf(bf_lo(qp[d / 2]), x[d], s0); s1 = fmaf(bf_hi(qp[d / 2]), x[d + 1], s1);
+                    s2 = fmaf(bf_lo(qp[d / 2 + 1]), x[d + 2], s2); s3 = fmaf(bf_hi(qp[d / 2 + 1]), x[d + 3], s3);
                 }
                 rad = x[D]; am = x[D + 1]; pm = __float_as_int(x[D + 2]);
             }
@@ -221,20 +221,16 @@ __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, co
             score = f_add(content, f_mul(f_mul(lam, am), e));
         }
         nvis += __popc(__ballot_sync(FS_FULL, valid));
-        // ---- the best (W - carried) children by (score desc, position asc): one warp-wide max per kept child ----
+        // ---- rank the children: (score desc, position asc) ----
+        // (32 independent shuffles pipeline well; a warp-wide max per kept child is a chain of dependent reductions and
+        // measured slower in the latency-bound decode kernel and no faster in prefill)
+        int rank = 0;
+#pragma unroll 8
+        for (int o = 0; o < 32; ++o) {
+            const float so = __shfl_sync(FS_FULL, score, o);
+            rank += (so > score || (so == score && o < lane)) ? 1 : 0;
+        }
         const int ncar = __popc(cmask & 0xffffu);
-        uint32_t key = 0;                                  // order-preserving image of the score; 0 = not a contender
-        if (valid && score > 0.5f * FS_NEG_SCORE) {
-            const uint32_t bits = __float_as_uint(score + 0.0f);
-            key = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
-        }
-        int rank = WMAX;
-        for (int r = 0; r < W - ncar; ++r) {
-            const uint32_t kmax = __reduce_max_sync(FS_FULL, key);
-            if (kmax == 0) break;
-            const int win = __ffs(__ballot_sync(FS_FULL, key == kmax)) - 1;      // ties: the lower position wins
-            if (lane == win) { rank = r; key = 0; }
-        }
         int* fm = fr + WMAX;                   // fr: WMAX refs then WMAX metas
         if (lane < WMAX) fr[lane] = -1;
         __syncwarp();
@@ -242,7 +238,7 @@ __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, co
             const int pos = __popc(cmask & ((1u << lane) - 1));
             fr[pos] = ref; fm[pos] = meta;
         }
-        if (rank < WMAX) {
+        if (valid && score > 0.5f * FS_NEG_SCORE && ncar + rank < W) {
             fr[ncar + rank] = cref; fm[ncar + rank] = cmeta;
         }
         __syncwarp();
@@ -376,8 +372,14 @@ __global__ void __launch_bounds__(NWARP * 32, 2) fsb_select_kernel(SelArgs A) {
 #pragma unroll
             for (int i = 0; i < FsbDim<D>::NPL; ++i) { const float v = qs[lane + 32 * i]; qq[i] = f_mul(v, v); }
             const float qn = f_mul(f_sqrt(fsb_warp_det_sum<D>(qq)), a.radius_coef);
+            uint32_t qreg[D / 2];
+#pragma unroll
+            for (int i = 0; i < D / 8; ++i) {
+                const uint4 w4 = *(const uint4*)(qp + i * 8);
+                qreg[i * 4 + 0] = w4.x; qreg[i * 4 + 1] = w4.y; qreg[i * 4 + 2] = w4.z; qreg[i * 4 + 3] = w4.w;
+            }
             int nv = 0;
-            const int c = beam<D, false, true>(F, t, sp, qs, qn, qpos, lam, sig, a.scale, width, lane, frs[warp], nv,
+            const int c = beam<D, false, true>(F, t, sp, qreg, qn, qpos, lam, sig, a.scale, width, lane, frs[warp], nv,
                                                stg_mu, stg_aux);
             if (lane < width) cand_sm[qi][f * WMAX + lane] = c;
             if (lane == 0) nv_sm[qi] += nv;
@@ -477,8 +479,14 @@ __global__ void __launch_bounds__(256) fsb_decode_select_kernel(SelArgs A) {
 #pragma unroll
         for (int i = 0; i < FsbDim<D>::NPL; ++i) { const float v = qs[lane + 32 * i]; qq[i] = f_mul(v, v); }
         const float qn = f_mul(f_sqrt(fsb_warp_det_sum<D>(qq)), a.radius_coef);
+        uint32_t qreg[D / 2];
+#pragma unroll
+        for (int i = 0; i < D / 8; ++i) {
+            const uint4 w4 = *(const uint4*)(qp + i * 8);
+            qreg[i * 4 + 0] = w4.x; qreg[i * 4 + 1] = w4.y; qreg[i * 4 + 2] = w4.z; qreg[i * 4 + 3] = w4.w;
+        }
         int nv = 0;
-        const int c = beam<D, true>(warp == 0 ? a.main : a.second, t, sp[warp], qs, qn, qpos, lam, sig, a.scale,
+        const int c = beam<D, true>(warp == 0 ? a.main : a.second, t, sp[warp], qreg, qn, qpos, lam, sig, a.scale,
                                     warp == 0 ? a.width : a.width2, lane, frs[warp], nv);
         if (lane < WMAX) cand_s[warp * WMAX + lane] = (lane < (warp == 0 ? a.width : a.width2)) ? c : -1;
         if (lane == 0) nv_s[warp] = nv;
