@@ -300,6 +300,11 @@ struct SelArgs {
 // Per forest: build the block's spine, copy every chunk node of tree depth <= DS into shared memory (<= 2^(DS+1)-1 rows:
 // the levels all 128 queries walk through), then one warp per query runs the beam, reading the shallow levels from
 // shared memory and only the deep ones from L2. The candidates of both beams meet in shared memory for the union.
+#ifndef FSB_SEL_NW
+#define FSB_SEL_NW 8
+#endif
+constexpr int SEL_NW = FSB_SEL_NW;          // warps per prefill selection CTA
+
 template <int D>
 struct SelSmem {
     static constexpr size_t MU_OFF = 0;
@@ -308,7 +313,7 @@ struct SelSmem {
 };
 
 template <int D, int NWARP>
-__global__ void __launch_bounds__(NWARP * 32, 2) fsb_select_kernel(SelArgs A) {
+__global__ void __launch_bounds__(NWARP * 32, (NWARP >= 16) ? 2 : 2) fsb_select_kernel(SelArgs A) {
     constexpr int DP = FsbDim<D>::DP;
     constexpr int CH = D / 8;
     const fsattn_fsb_select_t& a = A.a;
@@ -625,16 +630,16 @@ extern "C" int fsattn_fsb_select(const fsattn_fsb_select_t* a, fsattn_stream_t s
         cudaError_t e = cudaSuccess;
         switch (a->main.D) {
             case 64:
-                e = cudaFuncSetAttribute(fsb_select_kernel<64, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SelSmem<64>::TOTAL);
-                if (e == cudaSuccess) fsb_select_kernel<64, 8><<<grid, 256, SelSmem<64>::TOTAL, st>>>(A);
+                e = cudaFuncSetAttribute(fsb_select_kernel<64, SEL_NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SelSmem<64>::TOTAL);
+                if (e == cudaSuccess) fsb_select_kernel<64, SEL_NW><<<grid, SEL_NW * 32, SelSmem<64>::TOTAL, st>>>(A);
                 break;
             case 96:
-                e = cudaFuncSetAttribute(fsb_select_kernel<96, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SelSmem<96>::TOTAL);
-                if (e == cudaSuccess) fsb_select_kernel<96, 8><<<grid, 256, SelSmem<96>::TOTAL, st>>>(A);
+                e = cudaFuncSetAttribute(fsb_select_kernel<96, SEL_NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SelSmem<96>::TOTAL);
+                if (e == cudaSuccess) fsb_select_kernel<96, SEL_NW><<<grid, SEL_NW * 32, SelSmem<96>::TOTAL, st>>>(A);
                 break;
             default:
-                e = cudaFuncSetAttribute(fsb_select_kernel<128, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SelSmem<128>::TOTAL);
-                if (e == cudaSuccess) fsb_select_kernel<128, 8><<<grid, 256, SelSmem<128>::TOTAL, st>>>(A);
+                e = cudaFuncSetAttribute(fsb_select_kernel<128, SEL_NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SelSmem<128>::TOTAL);
+                if (e == cudaSuccess) fsb_select_kernel<128, SEL_NW><<<grid, SEL_NW * 32, SelSmem<128>::TOTAL, st>>>(A);
                 break;
         }
         if (e != cudaSuccess) {
