@@ -210,7 +210,7 @@ def run_fsb_section(args, dev, K, Wm):
            "prefill_ktok_s": args.batch * ctx / prefill_ms, "prefill_ms": prefill_ms,
            "vs_published_decode": (args.batch * K / (ms * 1e-3)) / PUBLISHED_FSB_DECODE_TPS_131K if ctx == 131072 else None,
            "vs_published_prefill": (args.batch * ctx / prefill_ms) / PUBLISHED_FSB_PREFILL_KTOKS_131K if ctx == 131072 else None,
-           "gpu_launches": K * (6 * nL + 1), "forest_bytes_per_layer": gd.fsb_bytes() // nL,
+           "gpu_launches": K * gd.launches_per_step(), "forest_bytes_per_layer": gd.fsb_bytes() // nL,
            "admitted_cells_layer0": {"main": fo.m_tot[0].tolist(), "second": fo.m_tot[1].tolist()},
            "kv_faults": list(gd.kv_faults())}
     del gd, model
@@ -333,7 +333,7 @@ def run_ours(args):
                                    else f"batch-sharded x{world}, no collective")},
         "clocks": cs.summary(),
         "e2e": {"value": seqs * K / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 8 * B},
-        "gpu_launches": K * ((5 * nL + 1) if B <= 8 else nL),      # above 8 rows the projections are library GEMMs
+        "gpu_launches": K * (gd.launches_per_step() if B <= 8 else nL),      # above 8 rows the projections are library GEMMs
         "roofline": {"kernel": "fsl_decode_kernel", "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": NCU_DECODE_KERNEL_DRAM_BYTES if (B == 1 and args.model == "340m") else None,
                      "traffic_source": "ncu dram__bytes_read+write per launch, profiles/fsl_decode_kernel_340m_ncu_full.md "
