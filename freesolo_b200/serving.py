@@ -246,7 +246,7 @@ class GraphedDecoder:
         # (126 MB holds about four 341M layers), so every projection kernel streams from L2 instead of waiting on HBM at
         # the head of a dependent chain. The branch forks here and joins before the step ends (capture-safe).
         nL = len(self.blocks)
-        prefetch = os.environ.get("FSATTN_L2_PREFETCH", "1") == "1"
+        prefetch = os.environ.get("FSATTN_L2_PREFETCH", "0") == "1"
         cur = torch.cuda.current_stream(self.dev)
         side = None
         if prefetch:
@@ -290,7 +290,7 @@ class GraphedDecoder:
         """Kernels of this library per decode step (batch <= 8): 5 per layer + the head, + the prefetch branch."""
         nL = len(self.blocks)
         n = 5 * nL + 1 + (nL if self.fsb else 0)
-        if os.environ.get("FSATTN_L2_PREFETCH", "1") == "1":
+        if os.environ.get("FSATTN_L2_PREFETCH", "0") == "1":
             n += 4 * (nL - 1) + 1
         return n
 
