@@ -579,9 +579,3 @@ def fsb_select(forests: FsbForests, Q, K, lam, sigma, *, scale: float, N: int = 
     L.call("fsattn_fsb_select", a, _stream(Q))
     return (sel, cand, nvis) if debug else sel
 
-
-def l2_prefetch(t: torch.Tensor) -> None:
-    """Ask L2 for the bytes of a contiguous CUDA tensor on the current stream (see fsattn_l2_prefetch)."""
-    _need_cuda(t)
-    assert t.is_contiguous()
-    L.check(L.load().fsattn_l2_prefetch(t.data_ptr(), t.numel() * t.element_size(), _stream(t)), "fsattn_l2_prefetch")

@@ -242,33 +242,10 @@ class GraphedDecoder:
         x.copy_(m.tok_emb(self.tok).view(x.shape))
         if x.shape[0] > 8:
             return self._trunk_step_batched()
-        # Weight prefetch on a side branch of the step: while layer i runs, the weights of layer i+2 are pulled into L2
-        # (126 MB holds about four 341M layers), so every projection kernel streams from L2 instead of waiting on HBM at
-        # the head of a dependent chain. The branch forks here and joins before the step ends (capture-safe).
-        nL = len(self.blocks)
-        prefetch = os.environ.get("FSATTN_L2_PREFETCH", "0") == "1"
-        cur = torch.cuda.current_stream(self.dev)
-        side = None
-        if prefetch:
-            if getattr(self, "_pf_stream", None) is None:
-                self._pf_stream = torch.cuda.Stream(device=self.dev)
-            side = self._pf_stream
-            side.wait_stream(cur)
-            if nL > 1:
-                with torch.cuda.stream(side):
-                    for w in self._layer_weights(1):
-                        ops.l2_prefetch(w)
         for i, blk in enumerate(self.blocks):
             a = self.attn[i]
             wqkv, _ = a._ensure_qkv_cache()
             ops.trunk_gemv(x, wqkv, norm_w=blk.ln1.weight, eps=blk.ln1.eps, out=self.qkv, pdl=pdl)
-            if prefetch and i + 2 <= nL:
-                ev = torch.cuda.Event()
-                ev.record(cur)
-                side.wait_event(ev)                      # stay two layers ahead of the main chain, not more
-                with torch.cuda.stream(side):
-                    for w in (self._layer_weights(i + 2) if i + 2 < nL else [m.lm_head.weight]):
-                        ops.l2_prefetch(w)
             if not skip_attn:
                 a.graph_decode_attn(self.qkv, self.bufs[i], y=self.y, pdl=pdl)
             ops.trunk_gemv(self.y, a.W_o.weight, res=x, out=x, pdl=pdl)
@@ -278,21 +255,11 @@ class GraphedDecoder:
         ops.trunk_gemv(x, m.lm_head.weight, norm_w=m.ln_final.weight, eps=m.ln_final.eps, out=self.logits, pdl=pdl)
         self.tok.copy_(self.logits.argmax(dim=-1, keepdim=True))
         self.pos_t.add_(1)
-        if side is not None:
-            cur.wait_stream(side)
-
-    def _layer_weights(self, i):
-        """The four projection weights a decode step reads in layer i (fused QKV, W_o, fused gate/up, down)."""
-        a, blk = self.attn[i], self.blocks[i]
-        return [a._ensure_qkv_cache()[0], a.W_o.weight, blk.ffn._ensure_gu_cache()[0], blk.ffn.w_down.weight]
 
     def launches_per_step(self) -> int:
-        """Kernels of this library per decode step (batch <= 8): 5 per layer + the head, + the prefetch branch."""
+        """Kernels of this library per decode step (batch <= 8): 5 per layer (6 with the FS-B selection) + the head."""
         nL = len(self.blocks)
-        n = 5 * nL + 1 + (nL if self.fsb else 0)
-        if os.environ.get("FSATTN_L2_PREFETCH", "0") == "1":
-            n += 4 * (nL - 1) + 1
-        return n
+        return 5 * nL + 1 + (nL if self.fsb else 0)
 
     def _trunk_step_batched(self):
         """More than 8 sequences per step: the projections are real GEMMs (weights read once for all rows), so they go to

@@ -252,12 +252,6 @@ typedef struct {
 } fsattn_trunk_gemv_t;
 FSATTN_API int fsattn_trunk_gemv(const fsattn_trunk_gemv_t* a, fsattn_stream_t stream);
 
-/* Ask L2 for the byte range [ptr, ptr + bytes) (16-byte aligned start) ahead of its use: bulk L2 prefetches, no data is
- * written and nothing waits. The decoder runs it on a side branch of the step graph for the weights of the layers to come,
- * so the projection kernels find them in L2 (126 MB holds about four 341M layers). No reference counterpart (its decode
- * projections go through cuBLAS/Triton with no cross-kernel prefetch). */
-FSATTN_API int fsattn_l2_prefetch(const void* ptr, int64_t bytes, fsattn_stream_t stream);
-
 /* ---- FS-B: two forests over the admitted cells, beam search, candidate re-rank ------------------------------------------
  * One fsattn_fsb_forest_t describes ONE forest (admission threshold tau) of one layer for all T = B*H rows.
  *
