@@ -471,34 +471,6 @@ __global__ void __launch_bounds__(256) fsb_decode_select_kernel(SelArgs A) {
             sp[w].root = h[0]; sp[w].height = h[1]; sp[w].m_b = h[2];
         }
     }
-    // The forests only change at block boundaries (plain launches between graph replays), so the shallow tree levels
-    // (depth <= DS: up to 511 nodes per forest) can be copied into shared memory BEFORE the dependency wait, under the tail
-    // of the QKV projection; the first DS levels of each beam then cost no memory round trip.
-    extern __shared__ __align__(16) unsigned char dsm[];
-    if (tid < nsp) stage_plan<D>(sp[tid], a.hdr[tid][t * 4 + 2], STG_DS<D>());
-    __syncthreads();
-    for (int w = 0; w < nsp; ++w) {
-        const fsattn_fsb_forest_t& F = w == 0 ? a.main : a.second;
-        unsigned char* smu = dsm + (size_t)w * SelSmem<D>::TOTAL + SelSmem<D>::MU_OFF;
-        float4* sax = (float4*)(dsm + (size_t)w * SelSmem<D>::TOTAL + SelSmem<D>::AUX_OFF);
-        const int64_t nrow = (int64_t)t * fsb_nodes_per_row(F.m_cap);
-        const bf16* node_mu = (const bf16*)F.node_mu + nrow * D;
-        const float4* aux = (const float4*)F.node_aux + nrow;
-        const int m_b = a.hdr[w][t * 4 + 2];
-        constexpr int CH = D / 8;
-        for (int k = 0; (m_b >> k) != 0; ++k) {
-            const int cnt = sp[w].stg_cnt[k];
-            if (!((m_b >> k) & 1) || cnt == 0) continue;
-            const int base = sp[w].stg_base[k];
-            const int64_t n0 = fsb_root_node(k, (m_b >> (k + 1)) << 1, F.m_cap);
-            for (int i = tid; i < cnt * CH; i += 256) {
-                const int r = i / CH, v = i % CH, row = base + r;
-                const uint4 wv = *(const uint4*)(node_mu + (n0 + r) * D + v * 8);
-                *(uint4*)(smu + (size_t)row * (D * 2) + (((v & ~STG_SW<D>()) | ((v ^ row) & STG_SW<D>())) << 4)) = wv;
-            }
-            for (int i = tid; i < cnt; i += 256) sax[base + i] = aux[n0 + i];
-        }
-    }
     const float lam = a.lam[hd], sig = a.sigma[hd];
     const float qpos = (float)(*a.pos);
     if (tid < 32) { cand_s[tid] = -1; u_s[tid] = -INFINITY; }
@@ -519,10 +491,8 @@ __global__ void __launch_bounds__(256) fsb_decode_select_kernel(SelArgs A) {
             qreg[i * 4 + 0] = w4.x; qreg[i * 4 + 1] = w4.y; qreg[i * 4 + 2] = w4.z; qreg[i * 4 + 3] = w4.w;
         }
         int nv = 0;
-        const int c = beam<D, true, true>(warp == 0 ? a.main : a.second, t, sp[warp], qreg, qn, qpos, lam, sig, a.scale,
-                                          warp == 0 ? a.width : a.width2, lane, frs[warp], nv,
-                                          dsm + (size_t)warp * SelSmem<D>::TOTAL + SelSmem<D>::MU_OFF,
-                                          (const float4*)(dsm + (size_t)warp * SelSmem<D>::TOTAL + SelSmem<D>::AUX_OFF));
+        const int c = beam<D, true>(warp == 0 ? a.main : a.second, t, sp[warp], qreg, qn, qpos, lam, sig, a.scale,
+                                    warp == 0 ? a.width : a.width2, lane, frs[warp], nv);
         if (lane < WMAX) cand_s[warp * WMAX + lane] = (lane < (warp == 0 ? a.width : a.width2)) ? c : -1;
         if (lane == 0) nv_s[warp] = nv;
     }
@@ -645,36 +615,15 @@ extern "C" int fsattn_fsb_select(const fsattn_fsb_select_t* a, fsattn_stream_t s
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         cudaError_t e;
-        static bool opted_dev[16][3] = {};                 // shared-memory opt-in done, per device and head dim
-        int dev = 0;
-        cudaGetDevice(&dev);
-        const int di = a->main.D == 64 ? 0 : (a->main.D == 96 ? 1 : 2);
-        const bool opted = dev >= 0 && dev < 16 && opted_dev[dev][di];
         switch (a->main.D) {
-            case 64:
-                cfg.dynamicSmemBytes = 2 * SelSmem<64>::TOTAL;
-                e = opted ? cudaSuccess
-                          : cudaFuncSetAttribute(fsb_decode_select_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cfg.dynamicSmemBytes);
-                if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, fsb_decode_select_kernel<64>, A);
-                break;
-            case 96:
-                cfg.dynamicSmemBytes = 2 * SelSmem<96>::TOTAL;
-                e = opted ? cudaSuccess
-                          : cudaFuncSetAttribute(fsb_decode_select_kernel<96>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cfg.dynamicSmemBytes);
-                if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, fsb_decode_select_kernel<96>, A);
-                break;
-            default:
-                cfg.dynamicSmemBytes = 2 * SelSmem<128>::TOTAL;
-                e = opted ? cudaSuccess
-                          : cudaFuncSetAttribute(fsb_decode_select_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cfg.dynamicSmemBytes);
-                if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, fsb_decode_select_kernel<128>, A);
-                break;
+            case 64: e = cudaLaunchKernelEx(&cfg, fsb_decode_select_kernel<64>, A); break;
+            case 96: e = cudaLaunchKernelEx(&cfg, fsb_decode_select_kernel<96>, A); break;
+            default: e = cudaLaunchKernelEx(&cfg, fsb_decode_select_kernel<128>, A); break;
         }
         if (e != cudaSuccess) {
             fs_set_error("fsb_select: launch failed: %s", cudaGetErrorString(e));
             return FSATTN_ELAUNCH;
         }
-        if (dev >= 0 && dev < 16) opted_dev[dev][di] = true;
         return FSATTN_OK;
     } else {
         FS_UNSUPPORTED(a->Bq > 128, "fsb_select: query blocks of %d (at most 128)", a->Bq);
