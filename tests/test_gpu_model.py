@@ -134,3 +134,25 @@ def test_trunk_gemv_against_torch(dev, M, K, N):
         f = N // 2
         rb = ref.to(torch.bfloat16)         # the kernel rounds gate, up and silu(gate) to bf16 like the eager bf16 ops
         close(ops.trunk_gemv(x, w, swiglu=True), (F.silu(rb[:, :f]) * rb[:, f:]).float(), "swiglu")
+
+
+def test_graph_decoder_many_sequences(dev):
+    """More than 8 sequences per step: the projections go through library GEMMs, the attention step stays one launch per
+    layer. Graph replay equals the un-captured steps; the first token equals the eager per-token path's."""
+    from freesolo_b200.serving import FreeSoloLM, GraphedDecoder, cached_generate, serve_kwargs
+    torch.manual_seed(0)
+    m = FreeSoloLM.from_config("debug", max_seq_len=2048, **serve_kwargs("sparse")).to(dev).to(torch.bfloat16).eval()
+    P0, T, B = 300, 70, 10
+    ids = torch.randint(0, 32000, (B, P0), generator=torch.Generator().manual_seed(7))
+    runs = []
+    for eager in (10 ** 9, 2):
+        gd = GraphedDecoder(m, ids, Lmax=P0 + T + 8, device=dev, kv="int8", eager_steps=eager)
+        toks = [gd.prefill().clone()]
+        for i in range(T - 1):
+            toks.append(gd.step().clone())
+        runs.append((torch.cat(toks, dim=1).cpu(), gd))
+    assert runs[1][1].graph is not None
+    assert torch.equal(runs[0][0], runs[1][0])
+    assert runs[1][1].kv_faults() == (0, 0, 0)
+    want = cached_generate(m, ids, 1, device=dev, kv="int8")
+    assert torch.equal(want[:, P0].cpu(), runs[1][0][:, 0])
