@@ -303,8 +303,13 @@ def run_ours(args):
     ms, e2e_ms = t.tolist()
     faults = gd.kv_faults()
     if world > 1:
-        # every rank leaves the group together; what follows on rank 0 needs no communication
+        # every rank leaves the group together; what follows on rank 0 needs no communication. A graph that captured
+        # NCCL collectives (head sharding) keeps the communicator busy: NCCL's teardown waits for it, so it goes first.
         barrier()
+        gd.graph = None
+        import gc
+        gc.collect()
+        torch.cuda.synchronize()
         dist.destroy_process_group()
         mark("process group closed")
     if rank != 0:

@@ -8,7 +8,8 @@
 //                            P written as bf16 into shared memory in the K-major swizzled operand layout
 //        PV = P V            tcgen05.mma 128x64x128 (8 k-steps) into a second TMEM accumulator; the running output lives in
 //                            registers: O = O * alpha + PV
-// Warp roles: warps 0-3 softmax/epilogue (TMEM lane quarter = warp id), warp 4 TMA producer, warp 5 MMA issuer.
+// Warp roles: warps 0-7 softmax/epilogue (TMEM lane quarter = warp id % 4, two threads per query row), warp 8 TMA producer,
+// warp 9 MMA issuer.
 // Every mbarrier wait is bounded; on a timeout the CTA records it in *status, stops issuing work and still frees its TMEM.
 //
 // FLOPs per CTA: (W/128+1) tiles * (2*128*128*64 + 2*128*128*64); algorithmic FLOPs per query 4*D*min(i+1, W+1).
@@ -22,7 +23,8 @@ namespace {
 constexpr int TC_BM = 128;          // queries per CTA
 constexpr int TC_BN = 128;          // keys per tile
 constexpr int TC_D = 64;
-constexpr int TC_THREADS = 192;
+constexpr int TC_THREADS = 320;     // 8 softmax warps (two per TMEM lane quarter), TMA producer, MMA issuer
+constexpr int TC_SOFTMAX_THREADS = 256;
 constexpr int TC_WAIT_ITERS = 1 << 24;
 
 // shared memory map (bytes, from a 1024-byte aligned base)
@@ -34,7 +36,7 @@ constexpr int SM_BAR = SM_P + 2 * 32768;        // mbarriers
 constexpr int SM_TOTAL = SM_BAR + 256;
 
 enum { BAR_Q = 0, BAR_KV_FULL = 1, BAR_KV_EMPTY = 3, BAR_S_FULL = 5, BAR_S_FREE = 7, BAR_P_FULL = 9, BAR_PV_FULL = 11,
-       BAR_PV_FREE = 13, BAR_COUNT = 15 };
+       BAR_PV_FREE = 13, BAR_MX = 15, BAR_L = 17, BAR_COUNT = 18 };
 
 __device__ __forceinline__ uint32_t s_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -163,6 +165,8 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     extern __shared__ unsigned char tc_smem_raw[];
     __shared__ uint32_t tmem_base_s;
     __shared__ int abort_s;
+    __shared__ float mx_s[2][2][TC_BM];      // [tile parity][column half][row]: the two halves of a row exchange their maxima
+    __shared__ float l_s[2][TC_BM];
     unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
     uint64_t* bars = reinterpret_cast<uint64_t*>(base + SM_BAR);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -180,15 +184,17 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             bar_init(&bars[BAR_KV_FULL + s], 1);
             bar_init(&bars[BAR_KV_EMPTY + s], 1);
             bar_init(&bars[BAR_S_FULL + s], 1);
-            bar_init(&bars[BAR_S_FREE + s], 128);
-            bar_init(&bars[BAR_P_FULL + s], 128);
+            bar_init(&bars[BAR_S_FREE + s], TC_SOFTMAX_THREADS);
+            bar_init(&bars[BAR_P_FULL + s], TC_SOFTMAX_THREADS);
             bar_init(&bars[BAR_PV_FULL + s], 1);
-            bar_init(&bars[BAR_PV_FREE + s], 128);
+            bar_init(&bars[BAR_PV_FREE + s], TC_SOFTMAX_THREADS);
+            bar_init(&bars[BAR_MX + s], TC_SOFTMAX_THREADS);
         }
+        bar_init(&bars[BAR_L], TC_SOFTMAX_THREADS);
         abort_s = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 4) {
+    if (warp == 8) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s_u32(&tmem_base_s)), "r"(512) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -198,7 +204,7 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     const uint32_t tmem = tmem_base_s;
     volatile int* abortp = &abort_s;
 
-    if (warp == 4) {
+    if (warp == 8) {
         // ================= TMA producer ====================================================================================
         if (lane == 0) {
             bar_expect_tx(&bars[BAR_Q], 16384);
@@ -212,7 +218,7 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
                 tma_load_4d(base + SM_V + s * 16384, &tm_v, 0, kt0, h, b, &bars[BAR_KV_FULL + s]);
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == 9) {
         // ================= MMA issuer ======================================================================================
         if (lane == 0) {
             const uint32_t idesc_s = instr_desc(TC_BN, 0, 1);
@@ -248,14 +254,19 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             if (!ok) *abortp = 1;
         }
     } else {
-        // ================= softmax + epilogue: one query row per thread ===================================================
-        const int r = warp * 32 + lane;
+        // ================= softmax + epilogue: two threads per query row =====================================================
+        // Warps w and w+4 share the TMEM lane quarter w (a warp reaches lanes 32 (w % 4) ..): each thread owns one row and
+        // one half of it - 64 of the tile's 128 score columns and 32 of the 64 output dims. The halves meet twice: the row
+        // maximum of every tile (shared memory + an mbarrier with a bounded wait) and the row sum at the end.
+        const int sw = warp & 3, half = warp >> 2;
+        const int r = sw * 32 + lane;
         const int qi = q0 + r;
-        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+        const uint32_t lane_base = tmem + ((uint32_t)(sw * 32) << 16);
+        constexpr int HC = TC_BN / 2, HD = TC_D / 2;
         float m = -INFINITY, l = 0.0f, a_pend = 0.0f;
-        float O[TC_D];
+        float O[HD];
 #pragma unroll
-        for (int d = 0; d < TC_D; d++) O[d] = 0.0f;
+        for (int d = 0; d < HD; d++) O[d] = 0.0f;
         bool ok = true;
         for (int i = 0; i < nt; i++) {
             const int bb = i & 1;
@@ -263,37 +274,48 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             ok = ok && bar_wait(&bars[BAR_S_FULL + bb], (i >> 1) & 1) && !*abortp;
             if (!__all_sync(FS_FULL, ok)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t s_addr = lane_base + bb * TC_BN;
+            const uint32_t s_addr = lane_base + bb * TC_BN + half * HC;
             const bool lower_edge = (t == 0), upper_edge = (t == ntile_total - 1);
-            // pass 1: masked row maximum
+            const bool edge = lower_edge || upper_edge;
+            // pass 1: masked maximum of this half row
             float mx = -INFINITY;
 #pragma unroll 1
-            for (int c0 = 0; c0 < TC_BN; c0 += 32) {
+            for (int c0 = 0; c0 < HC; c0 += 32) {
                 float v[32];
                 tmem_ld32(s_addr + c0, v);
+                if (edge) {
 #pragma unroll
-                for (int c = 0; c < 32; c++) {
-                    const int col = c0 + c;
-                    const bool valid = !(lower_edge && col < r) && !(upper_edge && col > r);
-                    mx = fmaxf(mx, valid ? v[c] : -INFINITY);
+                    for (int c = 0; c < 32; c++) {
+                        const int col = half * HC + c0 + c;
+                        const bool valid = !(lower_edge && col < r) && !(upper_edge && col > r);
+                        mx = fmaxf(mx, valid ? v[c] : -INFINITY);
+                    }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 32; c++) mx = fmaxf(mx, v[c]);
                 }
             }
+            mx_s[bb][half][r] = mx;
+            bar_arrive(&bars[BAR_MX + bb]);
+            ok = bar_wait(&bars[BAR_MX + bb], (i >> 1) & 1) && !*abortp;
+            if (!__all_sync(FS_FULL, ok)) { ok = false; break; }
+            mx = fmaxf(mx, mx_s[bb][half ^ 1][r]);
             const float m_new = fmaxf(m, mx);
             const float alpha = (m == -INFINITY) ? 0.0f : exp2f((m - m_new) * p.c2);
             const float mc = (m_new == -INFINITY) ? 0.0f : m_new * p.c2;
-            // pass 2: probabilities, row sum, bf16 P into the swizzled K-major operand layout
+            // pass 2: probabilities, partial row sum, bf16 P into the swizzled K-major operand layout
             float rowsum = 0.0f;
             unsigned char* prow = base + SM_P + bb * 32768 + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll 1
-            for (int c0 = 0; c0 < TC_BN; c0 += 32) {
+            for (int c0 = 0; c0 < HC; c0 += 32) {
                 float v[32];
                 tmem_ld32(s_addr + c0, v);
                 uint32_t pk[16];
 #pragma unroll
                 for (int c = 0; c < 32; c += 2) {
-                    const int col = c0 + c;
-                    const bool v0 = !(lower_edge && col < r) && !(upper_edge && col > r);
-                    const bool v1 = !(lower_edge && col + 1 < r) && !(upper_edge && col + 1 > r);
+                    const int col = half * HC + c0 + c;
+                    const bool v0 = !edge || (!(lower_edge && col < r) && !(upper_edge && col > r));
+                    const bool v1 = !edge || (!(lower_edge && col + 1 < r) && !(upper_edge && col + 1 > r));
                     const float p0 = v0 ? exp2f(v[c] * p.c2 - mc) : 0.0f;
                     const float p1 = v1 ? exp2f(v[c + 1] * p.c2 - mc) : 0.0f;
                     pk[c >> 1] = pack_bf2(p0, p1);
@@ -302,7 +324,7 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
                 }
 #pragma unroll
                 for (int q4 = 0; q4 < 4; q4++) {
-                    const int cc = (c0 >> 3) + q4;                 // 16-byte chunk index within the 128-key row
+                    const int cc = ((half * HC + c0) >> 3) + q4;   // 16-byte chunk index within the 128-key row
                     unsigned char* dst = prow + (cc >> 3) * 16384 + (((cc & 7) ^ (r & 7)) << 4);
                     *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
                 }
@@ -313,19 +335,16 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             bar_arrive(&bars[BAR_P_FULL + bb]);
             l = l * alpha + rowsum;
             m = m_new;
-            // fold the previous tile's P V into the running output
+            // fold the previous tile's P V into the running output (this thread's 32 dims)
             if (i >= 1) {
                 const int j = i - 1, jb = j & 1;
                 ok = bar_wait(&bars[BAR_PV_FULL + jb], (j >> 1) & 1) && !*abortp;
                 if (!__all_sync(FS_FULL, ok)) { ok = false; break; }
                 tc_fence_after();
+                float v[32];
+                tmem_ld32(lane_base + 256 + jb * TC_D + half * HD, v);
 #pragma unroll
-                for (int c0 = 0; c0 < TC_D; c0 += 32) {
-                    float v[32];
-                    tmem_ld32(lane_base + 256 + jb * TC_D + c0, v);
-#pragma unroll
-                    for (int c = 0; c < 32; c++) O[c0 + c] = fmaf(O[c0 + c], a_pend, v[c]);
-                }
+                for (int c = 0; c < HD; c++) O[c] = fmaf(O[c], a_pend, v[c]);
                 tc_fence_before();
                 bar_arrive(&bars[BAR_PV_FREE + jb]);
             }
@@ -336,24 +355,26 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             ok = bar_wait(&bars[BAR_PV_FULL + jb], (j >> 1) & 1) && !*abortp;
             if (__all_sync(FS_FULL, ok)) {
                 tc_fence_after();
+                float v[32];
+                tmem_ld32(lane_base + 256 + jb * TC_D + half * HD, v);
 #pragma unroll
-                for (int c0 = 0; c0 < TC_D; c0 += 32) {
-                    float v[32];
-                    tmem_ld32(lane_base + 256 + jb * TC_D + c0, v);
-#pragma unroll
-                    for (int c = 0; c < 32; c++) O[c0 + c] = fmaf(O[c0 + c], a_pend, v[c]);
-                }
+                for (int c = 0; c < HD; c++) O[c] = fmaf(O[c], a_pend, v[c]);
                 tc_fence_before();
             } else {
                 ok = false;
             }
         }
+        // the two halves of a row add their sums
+        l_s[half][r] = l;
+        bar_arrive(&bars[BAR_L]);
+        if (ok) ok = bar_wait(&bars[BAR_L], 0) && !*abortp;
         if (!ok) *abortp = 1;
         if (ok && qi < p.N) {
-            const float inv = (l > 0.0f) ? 1.0f / l : 0.0f;
-            bf16* op = p.out + ((int64_t)b * p.N + qi) * ((int64_t)p.H * TC_D) + (int64_t)h * TC_D;
+            const float lt = l + l_s[half ^ 1][r];
+            const float inv = (lt > 0.0f) ? 1.0f / lt : 0.0f;
+            bf16* op = p.out + ((int64_t)b * p.N + qi) * ((int64_t)p.H * TC_D) + (int64_t)h * TC_D + half * HD;
 #pragma unroll
-            for (int e = 0; e < TC_D / 8; e++) {
+            for (int e = 0; e < HD / 8; e++) {
                 uint4 w;
                 w.x = pack_bf2(O[8 * e + 0] * inv, O[8 * e + 1] * inv);
                 w.y = pack_bf2(O[8 * e + 2] * inv, O[8 * e + 3] * inv);
@@ -366,7 +387,7 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     tc_fence_before();
     __syncthreads();
     if (tid == 0 && abort_s && p.status != nullptr) atomicAdd(p.status, 1);
-    if (warp == 4) {
+    if (warp == 8) {
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
     }
 }
