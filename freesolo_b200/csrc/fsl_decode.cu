@@ -521,8 +521,11 @@ __device__ __forceinline__ void refresh_pool(Smem<D>& sm, const fsattn_fsl_state
     __syncthreads();
 }
 
-template <int D>
-__global__ void __launch_bounds__(NWARP * 32) fsl_decode_kernel(const fsattn_fsl_decode_t a) {
+// MINB: CTAs the compiler must fit per SM. 1 = all the registers it wants (the batch-1 shape: fewer CTAs than SMs, latency
+// is everything); 2 = at most 128 registers, so that two CTAs overlap each other's memory round trips once the grid is
+// larger than the machine (many sequences per step: the kernel is then bandwidth-bound and needs the occupancy).
+template <int D, int MINB>
+__global__ void __launch_bounds__(NWARP * 32, MINB) fsl_decode_kernel(const fsattn_fsl_decode_t a) {
     using L = RowL<D>;
     constexpr int F = D / 8;                  // floats per lane when 8 lanes share a mean key
     __shared__ Smem<D> sm;
@@ -797,8 +800,8 @@ __global__ void __launch_bounds__(NWARP * 32) fsl_decode_kernel(const fsattn_fsl
     STAMP(0, 8);
 }
 
-template <int D>
-int launch_decode(const fsattn_fsl_decode_t* a, cudaStream_t stream) {
+template <int D, int MINB>
+int launch_decode_v(const fsattn_fsl_decode_t* a, cudaStream_t stream) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a->splits, a->st.B * a->st.H, 1);
     cfg.blockDim = dim3(NWARP * 32, 1, 1);
@@ -807,7 +810,7 @@ int launch_decode(const fsattn_fsl_decode_t* a, cudaStream_t stream) {
     int dev = 0;
     cudaGetDevice(&dev);
     if (dyn > 24 * 1024 && dev >= 0 && dev < 16 && opted[dev] < dyn) {
-        if (cudaFuncSetAttribute(fsl_decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) != cudaSuccess) {
+        if (cudaFuncSetAttribute(fsl_decode_kernel<D, MINB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) != cudaSuccess) {
             fs_set_error("fsl_decode_step: cannot opt in to %zu bytes of shared memory", dyn);
             return FSATTN_ELAUNCH;
         }
@@ -824,13 +827,25 @@ int launch_decode(const fsattn_fsl_decode_t* a, cudaStream_t stream) {
     attr[1].val.programmaticStreamSerializationAllowed = a->pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, fsl_decode_kernel<D>, *a);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, fsl_decode_kernel<D, MINB>, *a);
     if (e != cudaSuccess) {
         (void)cudaGetLastError();       // the error is reported through the return code; do not leave it pending
         fs_set_error("fsl_decode_step: launch failed: %s", cudaGetErrorString(e));
         return FSATTN_ELAUNCH;
     }
     return FSATTN_OK;
+}
+
+template <int D>
+int launch_decode(const fsattn_fsl_decode_t* a, cudaStream_t stream) {
+    static int sms = 0;
+    if (sms == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+    }
+    const long ctas = (long)a->splits * a->st.B * a->st.H;
+    return ctas > sms ? launch_decode_v<D, 2>(a, stream) : launch_decode_v<D, 1>(a, stream);
 }
 
 }  // namespace
