@@ -164,7 +164,7 @@ def time_decode_kernel(gd, n=48):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         ops.fsl_decode_step(st, qkv[:, 0], qkv[:, 1], qkv[:, 2], pos_t, cos, sin, lam, sigma, lrs, nw, scale=a.scale,
-                            eps=a.lr_norm.eps, y=y, splits=a.decode_splits)
+                            eps=a.lr_norm.eps, y=y, splits=a._splits(B))
         e1.record()
         times.append((e0, e1))
     torch.cuda.synchronize()
