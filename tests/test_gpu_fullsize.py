@@ -32,7 +32,7 @@ def test_codec_round_trip_and_statistics(data):
     tests/test_kv_int8.py:16-39), scale = bf16(amax / 127); ceilings equal the largest token norm of their cell."""
     from freesolo_b200 import ops
     K, kq, ks, ncell = data["K"], data["kq"], data["ks"], data["ncell"]
-    deq = ops.dequant_cells(kq, ks, N)
+    deq = ops.dequant_cells(kq, ks)
     err = (deq.float() - K.float()).abs().view(1, H, ncell, S * D).amax(-1)
     bound = ks.float() * 0.5 + K.float().abs().view(1, H, ncell, S * D).amax(-1) * 2 ** -8      # + bf16 rounding of the product
     assert (err <= bound * (1 + 1e-6)).all()
