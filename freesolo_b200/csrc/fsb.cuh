@@ -3,7 +3,8 @@
 #include "common.cuh"
 
 #define FSB_SMALL_K 5          // chunks of up to 2^5 cells are built in shared memory by the small-chunk kernel
-#define FSB_MAX_MCAP 8192      // largest supported cell capacity per row (262 144 tokens)
+#define FSB_MAX_MCAP 16384     // largest supported cell capacity per row (room for 262 144 tokens plus decode growth)
+#define FSB_MAX_CHUNK 8192     // largest chunk the build kernel takes (a chunk of 16 384 cells needs 524 288 admitted tokens)
 #define FSB_AUX 4              // floats per node in node_aux
 #define FSB_ROOT_PAD 4         // floats after the D mean words of a root32 row (radius + 3 pad)
 

@@ -96,6 +96,7 @@ __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
     const int k = __ffs(p + 1) - 1;
     if (SMALL ? (k > FSB_SMALL_K) : (k <= FSB_SMALL_K)) return;
     const int n = 1 << k;
+    if (n > FSB_MAX_CHUNK) return;             // cannot happen below 524 288 admitted tokens per row
     const int j = ((p + 1) >> k) - 1, jj = j >> 1;
     const int pos0 = p + 1 - n;
 
@@ -110,7 +111,7 @@ __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
     // ---- working arrays ----
     __shared__ float sm_f[SMALL ? (SN * D * 2 + SN) : 1];
     __shared__ int sm_i[SMALL ? (SN * 2 + SN / 2) : 1];
-    __shared__ float sm_proj[SMALL ? 1 : FSB_MAX_MCAP];
+    __shared__ float sm_proj[SMALL ? 1 : FSB_MAX_CHUNK];
     float *XC, *Y, *VV, *S1;
     int *ordA, *ordB, *FAR;
     if constexpr (SMALL) {

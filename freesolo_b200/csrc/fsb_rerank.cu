@@ -12,7 +12,6 @@ constexpr int RB_Q = 128;        // queries per block
 constexpr int RB_C = 32;         // candidate slots per query
 constexpr int RB_THREADS = 512;
 constexpr int RB_WARPS = RB_THREADS / 32;
-constexpr int RB_G = RB_WARPS;   // cells staged per round: one per warp
 constexpr int RB_PAIRS = RB_Q * RB_C;
 
 struct RrArgs {
@@ -23,16 +22,17 @@ struct RrArgs {
 template <int D>
 struct RrSmem {
     static constexpr int ROWB = D * 2;                       // bytes per key / query row
+    static constexpr int G = (D > 96) ? 8 : RB_WARPS;         // cells staged per round, one per warp (fewer at D = 128: shared memory)
     static constexpr int SW = (D == 96) ? 3 : 7;             // 16-byte-chunk XOR mask (keeps D = 96 inside its 4-chunk groups)
     static constexpr size_t Q_OFF = 0;
     static constexpr size_t K_OFF = Q_OFF + (size_t)RB_Q * ROWB;
-    static constexpr size_t CAND_OFF = K_OFF + (size_t)RB_G * 32 * ROWB;
+    static constexpr size_t CAND_OFF = K_OFF + (size_t)G * 32 * ROWB;
     static constexpr size_t U_OFF = CAND_OFF + RB_PAIRS * 4;
     static constexpr size_t CUR_OFF = U_OFF + RB_PAIRS * 4;          // int[RB_PAIRS + 1]
     static constexpr size_t PIDX_OFF = CUR_OFF + (RB_PAIRS + 4) * 4; // u16[RB_PAIRS]
     static constexpr size_t SORT_OFF = PIDX_OFF + RB_PAIRS * 2;      // u16[RB_PAIRS]
-    static constexpr size_t BM_OFF = SORT_OFF + RB_PAIRS * 2;        // u32[256] bitmap, int[256] word base
-    static constexpr size_t TOTAL = BM_OFF + 256 * 4 * 2 + 64;
+    static constexpr size_t BM_OFF = SORT_OFF + RB_PAIRS * 2;        // u32[512] bitmap (16 384 cells), int[512] word base
+    static constexpr size_t TOTAL = BM_OFF + 512 * 4 * 2 + 64;
 };
 
 __device__ __forceinline__ uint32_t sw_off(int row, int byte_in_row, int rowb, int swmask) {
@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(RB_THREADS, 1) fsb_rerank_block_kernel(RrArgs 
     unsigned short* pidx = (unsigned short*)(smem + SM::PIDX_OFF);
     unsigned short* sorted = (unsigned short*)(smem + SM::SORT_OFF);
     uint32_t* bm = (uint32_t*)(smem + SM::BM_OFF);
-    int* wbase = (int*)(bm + 256);
+    int* wbase = (int*)(bm + 512);
     __shared__ int U_s;
 
     const int blk = blockIdx.x, t = blockIdx.y;
@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(RB_THREADS, 1) fsb_rerank_block_kernel(RrArgs 
             cand_s[i] = (r < nq && s < C) ? a.cand[(row0 + r) * C + s] : -1;
             u_s[i] = -INFINITY;
         }
-        for (int i = tid; i < 256; i += RB_THREADS) bm[i] = 0;
+        for (int i = tid; i < 512; i += RB_THREADS) bm[i] = 0;
     }
     __syncthreads();
     // ---- distinct cells: bitmap, rank of each cell, counting sort of the pairs by cell ----
@@ -95,7 +95,7 @@ __global__ void __launch_bounds__(RB_THREADS, 1) fsb_rerank_block_kernel(RrArgs 
     __syncthreads();
     if (warp == 0) {
         int run = 0;
-        for (int w0 = 0; w0 < 256; w0 += 32) {
+        for (int w0 = 0; w0 < 512; w0 += 32) {
             const int n = __popc(bm[w0 + lane]);
             int inc = n;
 #pragma unroll
@@ -143,13 +143,13 @@ __global__ void __launch_bounds__(RB_THREADS, 1) fsb_rerank_block_kernel(RrArgs 
     }
     __syncthreads();
 
-    // ---- rounds of RB_G distinct cells: stage their keys, score every pair that references them ----
+    // ---- rounds of G distinct cells: stage their keys, score every pair that references them ----
     const float lam = a.lam[hd], two_sig = f_mul(2.0f, a.sigma[hd]);
     const float* ceil = a.main.ceil + (int64_t)t * a.main.ceil_st;
     const int g = lane >> 2, tg = lane & 3;
     constexpr int CH = D / 8;
-    for (int c0 = 0; c0 < U; c0 += RB_G) {
-        const int ncell = min(RB_G, U - c0);
+    for (int c0 = 0; c0 < U; c0 += SM::G) {
+        const int ncell = min(SM::G, U - c0);
         // stage: cell slot j holds distinct cell c0 + j; its id comes from the first pair of its list
         for (int i = tid; i < ncell * 32 * CH; i += RB_THREADS) {
             const int j = i / (32 * CH), rem = i % (32 * CH);

@@ -140,7 +140,7 @@ class FsbSelect(C.Structure):
 
 
 FSB_SPINE_MAX = 20
-FSB_MAX_MCAP = 8192
+FSB_MAX_MCAP = 16384
 
 EXTRA_STRUCTS = {"fsattn_trunk_gemv_t": TrunkGemv, "fsattn_fsb_forest_t": FsbForest, "fsattn_fsb_select_t": FsbSelect}
 
