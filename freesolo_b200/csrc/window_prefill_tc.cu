@@ -29,14 +29,16 @@ constexpr int TC_WAIT_ITERS = 1 << 24;
 
 // shared memory map (bytes, from a 1024-byte aligned base)
 constexpr int SM_Q = 0;                         // 128 x 64 bf16
-constexpr int SM_K = SM_Q + 16384;              // 2 stages
-constexpr int SM_V = SM_K + 2 * 16384;          // 2 stages
-constexpr int SM_P = SM_V + 2 * 16384;          // 2 buffers of 128 x 128 bf16 (two K-blocks of 128 x 64)
+constexpr int TC_KV_STAGES = 4;                 // key/value tiles in flight: with W = 512 (five tiles) all but the last are
+                                                // requested before the first MMA, so tile loads are off the critical path
+constexpr int SM_K = SM_Q + 16384;              // TC_KV_STAGES stages
+constexpr int SM_V = SM_K + TC_KV_STAGES * 16384;
+constexpr int SM_P = SM_V + TC_KV_STAGES * 16384;   // 2 buffers of 128 x 128 bf16 (two K-blocks of 128 x 64)
 constexpr int SM_BAR = SM_P + 2 * 32768;        // mbarriers
 constexpr int SM_TOTAL = SM_BAR + 256;
 
-enum { BAR_Q = 0, BAR_KV_FULL = 1, BAR_KV_EMPTY = 3, BAR_S_FULL = 5, BAR_S_FREE = 7, BAR_P_FULL = 9, BAR_PV_FULL = 11,
-       BAR_PV_FREE = 13, BAR_MX = 15, BAR_L = 17, BAR_COUNT = 18 };
+enum { BAR_Q = 0, BAR_KV_FULL = 1, BAR_KV_EMPTY = 5, BAR_S_FULL = 9, BAR_S_FREE = 11, BAR_P_FULL = 13, BAR_PV_FULL = 15,
+       BAR_PV_FREE = 17, BAR_MX = 19, BAR_L = 21, BAR_COUNT = 22 };      // KV_FULL / KV_EMPTY hold TC_KV_STAGES barriers each
 
 __device__ __forceinline__ uint32_t s_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -180,9 +182,11 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 
     if (tid == 0) {
         bar_init(&bars[BAR_Q], 1);
-        for (int s = 0; s < 2; s++) {
+        for (int s = 0; s < TC_KV_STAGES; s++) {
             bar_init(&bars[BAR_KV_FULL + s], 1);
             bar_init(&bars[BAR_KV_EMPTY + s], 1);
+        }
+        for (int s = 0; s < 2; s++) {
             bar_init(&bars[BAR_S_FULL + s], 1);
             bar_init(&bars[BAR_S_FREE + s], TC_SOFTMAX_THREADS);
             bar_init(&bars[BAR_P_FULL + s], TC_SOFTMAX_THREADS);
@@ -210,9 +214,9 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             bar_expect_tx(&bars[BAR_Q], 16384);
             tma_load_3d(base + SM_Q, &tm_q, 0, q0, bh, &bars[BAR_Q]);
             for (int i = 0; i < nt && !*abortp; i++) {
-                const int s = i & 1;
+                const int s = i % TC_KV_STAGES;
                 const int kt0 = q0 - p.W + (t_first + i) * TC_BN;
-                if (i >= 2 && !bar_wait(&bars[BAR_KV_EMPTY + s], ((i >> 1) - 1) & 1)) { *abortp = 1; break; }
+                if (i >= TC_KV_STAGES && !bar_wait(&bars[BAR_KV_EMPTY + s], ((i / TC_KV_STAGES) - 1) & 1)) { *abortp = 1; break; }
                 bar_expect_tx(&bars[BAR_KV_FULL + s], 32768);
                 tma_load_3d(base + SM_K + s * 16384, &tm_k, 0, kt0, bh, &bars[BAR_KV_FULL + s]);
                 tma_load_4d(base + SM_V + s * 16384, &tm_v, 0, kt0, h, b, &bars[BAR_KV_FULL + s]);
@@ -226,12 +230,12 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             bool ok = bar_wait(&bars[BAR_Q], 0);
             for (int i = 0; i <= nt && ok && !*abortp; i++) {
                 if (i < nt) {
-                    const int s = i & 1;
-                    ok = bar_wait(&bars[BAR_KV_FULL + s], (i >> 1) & 1);
+                    const int s = i & 1, ks = i % TC_KV_STAGES;
+                    ok = bar_wait(&bars[BAR_KV_FULL + ks], (i / TC_KV_STAGES) & 1);
                     if (ok && i >= 2) ok = bar_wait(&bars[BAR_S_FREE + s], ((i >> 1) - 1) & 1);
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t aq = s_u32(base + SM_Q), bk = s_u32(base + SM_K + s * 16384);
+                    const uint32_t aq = s_u32(base + SM_Q), bk = s_u32(base + SM_K + ks * 16384);
 #pragma unroll
                     for (int k = 0; k < TC_D / 16; k++)
                         umma(tmem + s * TC_BN, smem_desc(aq + k * 32), smem_desc(bk + k * 32), idesc_s, k > 0);
@@ -243,12 +247,13 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
                     if (ok && j >= 2) ok = bar_wait(&bars[BAR_PV_FREE + bb], ((j >> 1) - 1) & 1);
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t ap = s_u32(base + SM_P + bb * 32768), bv = s_u32(base + SM_V + bb * 16384);
+                    const int vs = j % TC_KV_STAGES;
+                    const uint32_t ap = s_u32(base + SM_P + bb * 32768), bv = s_u32(base + SM_V + vs * 16384);
 #pragma unroll
                     for (int k = 0; k < TC_BN / 16; k++)
                         umma(tmem + 256 + bb * TC_D, smem_desc(ap + (k >> 2) * 16384 + (k & 3) * 32), smem_desc(bv + k * 2048), idesc_pv, k > 0);
                     umma_commit(&bars[BAR_PV_FULL + bb]);
-                    umma_commit(&bars[BAR_KV_EMPTY + bb]);
+                    umma_commit(&bars[BAR_KV_EMPTY + vs]);
                 }
             }
             if (!ok) *abortp = 1;
