@@ -282,24 +282,22 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             const uint32_t s_addr = lane_base + bb * TC_BN + half * HC;
             const bool lower_edge = (t == 0), upper_edge = (t == ntile_total - 1);
             const bool edge = lower_edge || upper_edge;
-            // pass 1: masked maximum of this half row
-            float mx = -INFINITY;
-#pragma unroll 1
-            for (int c0 = 0; c0 < HC; c0 += 32) {
-                float v[32];
-                tmem_ld32(s_addr + c0, v);
-                if (edge) {
+            // the half row's 64 scores, read from TMEM once and kept in registers for both passes
+            float v[HC];
+            tmem_ld32(s_addr, v);
+            tmem_ld32(s_addr + 32, v + 32);
+            if (edge) {                     // first / diagonal tile: keys outside [q - W, q] become -inf
 #pragma unroll
-                    for (int c = 0; c < 32; c++) {
-                        const int col = half * HC + c0 + c;
-                        const bool valid = !(lower_edge && col < r) && !(upper_edge && col > r);
-                        mx = fmaxf(mx, valid ? v[c] : -INFINITY);
-                    }
-                } else {
-#pragma unroll
-                    for (int c = 0; c < 32; c++) mx = fmaxf(mx, v[c]);
+                for (int c = 0; c < HC; c++) {
+                    const int col = half * HC + c;
+                    const bool valid = !(lower_edge && col < r) && !(upper_edge && col > r);
+                    v[c] = valid ? v[c] : -INFINITY;
                 }
             }
+            // pass 1: maximum of this half row, then of the whole row
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < HC; c++) mx = fmaxf(mx, v[c]);
             mx_s[bb][half][r] = mx;
             bar_arrive(&bars[BAR_MX + bb]);
             ok = bar_wait(&bars[BAR_MX + bb], (i >> 1) & 1) && !*abortp;
@@ -308,31 +306,25 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             const float m_new = fmaxf(m, mx);
             const float alpha = (m == -INFINITY) ? 0.0f : exp2f((m - m_new) * p.c2);
             const float mc = (m_new == -INFINITY) ? 0.0f : m_new * p.c2;
-            // pass 2: probabilities, partial row sum, bf16 P into the swizzled K-major operand layout
+            // pass 2: probabilities (ex2.approx of a masked score is exactly 0), partial row sum over the bf16-rounded values
+            // the tensor core will multiply, bf16 P into the swizzled K-major operand layout
             float rowsum = 0.0f;
             unsigned char* prow = base + SM_P + bb * 32768 + (r >> 3) * 1024 + (r & 7) * 128;
-#pragma unroll 1
-            for (int c0 = 0; c0 < HC; c0 += 32) {
-                float v[32];
-                tmem_ld32(s_addr + c0, v);
-                uint32_t pk[16];
 #pragma unroll
-                for (int c = 0; c < 32; c += 2) {
-                    const int col = half * HC + c0 + c;
-                    const bool v0 = !edge || (!(lower_edge && col < r) && !(upper_edge && col > r));
-                    const bool v1 = !edge || (!(lower_edge && col + 1 < r) && !(upper_edge && col + 1 > r));
-                    const float p0 = v0 ? exp2f(v[c] * p.c2 - mc) : 0.0f;
-                    const float p1 = v1 ? exp2f(v[c + 1] * p.c2 - mc) : 0.0f;
-                    pk[c >> 1] = pack_bf2(p0, p1);
-                    // the row sum uses the rounded values the tensor core will multiply
+            for (int c0 = 0; c0 < HC; c0 += 8) {
+                uint32_t pk[4];
+#pragma unroll
+                for (int c = 0; c < 8; c += 2) {
+                    float p0, p1;
+                    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p0) : "f"(fmaf(v[c0 + c], p.c2, -mc)));
+                    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p1) : "f"(fmaf(v[c0 + c + 1], p.c2, -mc)));
+                    const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+                    pk[c >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
                     rowsum += bf_lo(pk[c >> 1]) + bf_hi(pk[c >> 1]);
                 }
-#pragma unroll
-                for (int q4 = 0; q4 < 4; q4++) {
-                    const int cc = ((half * HC + c0) >> 3) + q4;   // 16-byte chunk index within the 128-key row
-                    unsigned char* dst = prow + (cc >> 3) * 16384 + (((cc & 7) ^ (r & 7)) << 4);
-                    *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
-                }
+                const int cc = (half * HC + c0) >> 3;              // 16-byte chunk index within the 128-key row
+                unsigned char* dst = prow + (cc >> 3) * 16384 + (((cc & 7) ^ (r & 7)) << 4);
+                *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
             tc_fence_before();
             bar_arrive(&bars[BAR_S_FREE + bb]);
