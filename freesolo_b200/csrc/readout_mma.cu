@@ -2,11 +2,12 @@
 //
 // One CTA (8 warps) per (b, h, 128-query block); a warp owns 16 queries for the whole kernel and keeps their softmax
 // state (running max, sum, 16 x 64 fp32 output tile) in registers, flash-attention style. The block's distinct selected
-// cells are found once (bitmap + ranks), then staged eight at a time (K and V rows, 16-byte chunks XOR-swizzled by the
-// row) and every warp processes the staged cells that at least one of its queries selected: S = Q K^T (16 x 32, bf16
+// cells are found once (bitmap + ranks); every warp then stages, one after the other, the cells that at least one of its
+// queries selected (K and V rows, 16-byte chunks XOR-swizzled by the row, cp.async into a private 8 KB buffer - no
+// block-wide barrier in the loop) and processes each: S = Q K^T (16 x 32, bf16
 // mma.sync m16n8k16, fp32 accumulate), rows that did not select the cell masked out, online softmax, O += P V with P
 // split into a bf16 high and low part (two MMAs) so that the probabilities keep ~16 bits. Cells are visited in ascending
-// order, so the result is deterministic. ~110 KB of shared memory: two CTAs per SM overlap each other's staging.
+// order, so the result is deterministic. ~110 KB of shared memory: two CTAs per SM.
 #include "common.cuh"
 
 namespace {
@@ -153,26 +154,43 @@ __global__ void __launch_bounds__(RM_THREADS, 2) readout_mma_kernel(const fsattn
     const bf16* kbase = (const bf16*)a.k.ptr + b * a.k.sb + h * a.k.sh;
     const bf16* vbase = (const bf16*)a.v.ptr + b * a.v.sb + h * a.v.sh;
     constexpr int CH = D / 8;
-    for (int g0 = 0; g0 < n_distinct; g0 += RM_GC) {
-        const int gc = min(RM_GC, n_distinct - g0);
-        for (int i = tid; i < gc * 32 * CH; i += RM_THREADS) {
-            const int row = i / CH, e = i - row * CH;             // row = local cell * 32 + token
-            const int64_t tok = (int64_t)ucell[g0 + (row >> 5)] * FSATTN_CELL + (row & 31);
-            uint4 kw = make_uint4(0u, 0u, 0u, 0u), vw = kw;
-            if (tok < a.n_kv) {
-                kw = reinterpret_cast<const uint4*>(kbase + tok * a.k.sn)[e];
-                vw = reinterpret_cast<const uint4*>(vbase + tok * a.v.sn)[e];
-            }
-            *reinterpret_cast<uint4*>(ks + rm_sw(row, e * 16)) = kw;
-            *reinterpret_cast<uint4*>(vs + rm_sw(row, e * 16)) = vw;
+    // Every warp walks the distinct cells its own 16 queries selected, in ascending order, and stages each one (K and V
+    // rows, 8 KB) into its private buffer with asynchronous 16-byte copies: no block-wide barrier in the loop, and the 16
+    // warps of the two resident CTAs hide one another's load latency.
+    unsigned char* kw = ks + (size_t)warp * 32 * RM_ROWB;
+    unsigned char* vw = vs + (size_t)warp * 32 * RM_ROWB;
+    for (int u0 = 0; u0 < n_distinct; u0 += 32) {
+        const int ul = u0 + lane;
+        unsigned mask_l = 0;
+        if (ul < n_distinct) {
+            const int idx = warp * RM_MAXU + ul;
+            mask_l = (rmask[idx >> 1] >> ((idx & 1) * 16)) & 0xffffu;
         }
-        __syncthreads();
-        for (int lc = 0; lc < gc; lc++) {
-            const int u = g0 + lc;
-            const int idx = warp * RM_MAXU + u;
-            const unsigned mask = (rmask[idx >> 1] >> ((idx & 1) * 16)) & 0xffffu;      // warp-uniform
-            if (mask == 0) continue;
-            const int cell = ucell[u];
+        unsigned need = __ballot_sync(FS_FULL, mask_l != 0);
+        while (need) {
+            const int bit = __ffs(need) - 1;
+            need &= need - 1;
+            const unsigned mask = __shfl_sync(FS_FULL, mask_l, bit);
+            const int cell = ucell[u0 + bit];
+            constexpr int lc = 0;
+            {
+#pragma unroll
+                for (int it = 0; it < CH; it++) {
+                    const int i = it * 32 + lane;
+                    const int row = i / CH, e = i - row * CH;
+                    const int64_t tok = (int64_t)cell * FSATTN_CELL + row;
+                    const bool okr = tok < a.n_kv;
+                    const int64_t tk = okr ? tok : 0;
+                    const int nbytes = okr ? 16 : 0;
+                    const uint32_t kd = (uint32_t)__cvta_generic_to_shared(kw + rm_sw(row, e * 16));
+                    const uint32_t vd = (uint32_t)__cvta_generic_to_shared(vw + rm_sw(row, e * 16));
+                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(kd), "l"(kbase + tk * a.k.sn + e * 8), "r"(nbytes));
+                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(vd), "l"(vbase + tk * a.v.sn + e * 8), "r"(nbytes));
+                }
+                asm volatile("cp.async.commit_group;" ::: "memory");
+                asm volatile("cp.async.wait_group 0;" ::: "memory");
+                __syncwarp();
+            }
             // ---- S = Q K^T over the cell's 32 tokens ----
             float s[4][4];
 #pragma unroll
@@ -184,8 +202,8 @@ __global__ void __launch_bounds__(RM_THREADS, 2) readout_mma_kernel(const fsattn
 #pragma unroll
                 for (int nt = 0; nt < 4; nt++) {
                     const int r = lc * 32 + nt * 8 + g;
-                    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(ks + rm_sw(r, kk * 32 + tg * 4));
-                    const uint32_t b1 = *reinterpret_cast<const uint32_t*>(ks + rm_sw(r, kk * 32 + 16 + tg * 4));
+                    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kw + rm_sw(r, kk * 32 + tg * 4));
+                    const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kw + rm_sw(r, kk * 32 + 16 + tg * 4));
                     rm_mma(s[nt], qf[kk], b0, b1);
                 }
             }
@@ -245,7 +263,7 @@ __global__ void __launch_bounds__(RM_THREADS, 2) readout_mma_kernel(const fsattn
                 for (int np = 0; np < 4; np++) {                       // two column tiles per ldmatrix.x4
                     const int row = lc * 32 + k2 * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
                     const int nt = np * 2 + (lane >> 4);
-                    const uint32_t addr = (uint32_t)__cvta_generic_to_shared(vs + rm_sw(row, nt * 16));
+                    const uint32_t addr = (uint32_t)__cvta_generic_to_shared(vw + rm_sw(row, nt * 16));
                     uint32_t v0, v1, v2, v3;
                     asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                                  : "=r"(v0), "=r"(v1), "=r"(v2), "=r"(v3) : "r"(addr));
@@ -255,8 +273,8 @@ __global__ void __launch_bounds__(RM_THREADS, 2) readout_mma_kernel(const fsattn
                     rm_mma(O[np * 2 + 1], alo, v2, v3);
                 }
             }
+            __syncwarp();                  // every lane is done with the buffers before the next cell overwrites them
         }
-        __syncthreads();
     }
 
     // ---- o -> bf16, lr_norm, combine with the window output ----
