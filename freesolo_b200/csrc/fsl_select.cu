@@ -21,13 +21,26 @@ __global__ void __launch_bounds__(32) fsl_prefix_topp_kernel(const fsattn_fsl_to
     for (int blk = 0; blk < a.nb; blk++) {
         int vis = (int)(((int64_t)blk * a.Bq) / FSATTN_CELL);
         if (vis > a.ncell) vis = a.ncell;
-        for (; done < vis; done++) {
+        while (done < vis) {
             if (done >= cbase + 32) {
                 cbase = done & ~31;
                 cbuf = (cbase + lane < a.ncell) ? ceil[cbase + lane] : 0.0f;
             }
-            const float cv = __shfl_sync(FS_FULL, cbuf, done - cbase);
-            pool_list_insert(lc, li, n, a.P, cv, done, lane);
+            // the new cells of this 32-cell segment, tested against the list's last entry all at once: most of them rank
+            // after it once the list is full, and the entry only ever tightens, so a cell rejected here stays rejected
+            const int seg_end = min(vis, cbase + 32);
+            const bool mine = lane >= done - cbase && lane < seg_end - cbase;
+            const bool full = (n == a.P);
+            const float thr_c = full ? lc[a.P - 1] : 0.0f;
+            const int thr_i = full ? li[a.P - 1] : 0;
+            unsigned pend = __ballot_sync(FS_FULL, mine && (!full || pool_before(cbuf, cbase + lane, thr_c, thr_i)));
+            while (pend) {
+                const int l = __ffs(pend) - 1;
+                pend &= pend - 1;
+                const float cv = __shfl_sync(FS_FULL, cbuf, l);
+                pool_list_insert(lc, li, n, a.P, cv, cbase + l, lane);
+            }
+            done = seg_end;
         }
         for (int p = lane; p < a.P; p += 32) out[(int64_t)blk * a.P + p] = (p < n) ? li[p] : -1;
     }

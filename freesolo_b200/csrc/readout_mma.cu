@@ -3,8 +3,8 @@
 // One CTA (8 warps) per (b, h, 128-query block); a warp owns 16 queries for the whole kernel and keeps their softmax
 // state (running max, sum, 16 x 64 fp32 output tile) in registers, flash-attention style. The block's distinct selected
 // cells are found once (bitmap + ranks); every warp then stages, one after the other, the cells that at least one of its
-// queries selected (K and V rows, 16-byte chunks XOR-swizzled by the row, cp.async into a private 8 KB buffer - no
-// block-wide barrier in the loop) and processes each: S = Q K^T (16 x 32, bf16
+// queries selected (K and V rows, 16-byte chunks XOR-swizzled by the row, cp.async into private 4 KB buffers, one tile
+// ahead of the MMAs - no block-wide barrier in the loop) and processes each: S = Q K^T (16 x 32, bf16
 // mma.sync m16n8k16, fp32 accumulate), rows that did not select the cell masked out, online softmax, O += P V with P
 // split into a bf16 high and low part (two MMAs) so that the probabilities keep ~16 bits. Cells are visited in ascending
 // order, so the result is deterministic. ~110 KB of shared memory: two CTAs per SM.
@@ -19,6 +19,7 @@ constexpr int RM_GC = 8;             // cells staged per round
 constexpr int RM_D = 64;
 constexpr int RM_ROWB = RM_D * 2;    // 128-byte rows
 constexpr int RM_MAXU = RM_Q * FSATTN_MAX_KK;
+constexpr int RM_WL = 16 * FSATTN_MAX_KK;   // most distinct cells the 16 queries of one warp can select
 
 struct RmSmem {
     static constexpr size_t Q_OFF = 0;
@@ -29,7 +30,9 @@ struct RmSmem {
     static constexpr size_t RMASK_OFF = UC_OFF + (size_t)RM_MAXU * 4;                  // uint16 [8 warps][MAXU], as 32-bit words
     static constexpr size_t BM_OFF = RMASK_OFF + (size_t)RM_WARPS * RM_MAXU * 2;       // bitmap 1024 words + ranks 1024 + 8
     static constexpr size_t TOTAL = BM_OFF + (2 * 1024 + 16) * 4;
+    static constexpr size_t WL_OFF = BM_OFF;     // per warp: (cell, row mask) of its tiles; reuses the bitmap once it is dead
 };
+static_assert((size_t)RM_WARPS * RM_WL * 8 <= (2 * 1024 + 16) * 4, "tile lists must fit in the bitmap area");
 
 __device__ __forceinline__ uint32_t rm_sw(int row, int byte_in_row) {
     return (uint32_t)(row * RM_ROWB + ((((byte_in_row >> 4) ^ (row & 7)) << 4) | (byte_in_row & 15)));
@@ -155,10 +158,13 @@ __global__ void __launch_bounds__(RM_THREADS, 2) readout_mma_kernel(const fsattn
     const bf16* vbase = (const bf16*)a.v.ptr + b * a.v.sb + h * a.v.sh;
     constexpr int CH = D / 8;
     // Every warp walks the distinct cells its own 16 queries selected, in ascending order, and stages each one (K and V
-    // rows, 8 KB) into its private buffer with asynchronous 16-byte copies: no block-wide barrier in the loop, and the 16
-    // warps of the two resident CTAs hide one another's load latency.
+    // rows, 4 KB each) into its private buffers with asynchronous 16-byte copies: no block-wide barrier in the loop. The
+    // copies run one tile ahead: K of the next cell is requested as soon as the scores of this one are out of the K buffer,
+    // V of the next cell as soon as this cell's P V is done, so a load overlaps the softmax and the other operand's MMAs.
     unsigned char* kw = ks + (size_t)warp * 32 * RM_ROWB;
     unsigned char* vw = vs + (size_t)warp * 32 * RM_ROWB;
+    int2* wl = reinterpret_cast<int2*>(rm_smem + S::WL_OFF) + warp * RM_WL;
+    int n_tiles = 0;
     for (int u0 = 0; u0 < n_distinct; u0 += 32) {
         const int ul = u0 + lane;
         unsigned mask_l = 0;
@@ -166,31 +172,40 @@ __global__ void __launch_bounds__(RM_THREADS, 2) readout_mma_kernel(const fsattn
             const int idx = warp * RM_MAXU + ul;
             mask_l = (rmask[idx >> 1] >> ((idx & 1) * 16)) & 0xffffu;
         }
-        unsigned need = __ballot_sync(FS_FULL, mask_l != 0);
-        while (need) {
-            const int bit = __ffs(need) - 1;
-            need &= need - 1;
-            const unsigned mask = __shfl_sync(FS_FULL, mask_l, bit);
-            const int cell = ucell[u0 + bit];
-            constexpr int lc = 0;
-            {
+        const unsigned need = __ballot_sync(FS_FULL, mask_l != 0);
+        if (mask_l != 0) wl[n_tiles + __popc(need & ((1u << lane) - 1u))] = make_int2(ucell[ul], (int)mask_l);
+        n_tiles += __popc(need);
+    }
+    __syncwarp();
+    auto stage = [&](unsigned char* dst, const bf16* base, int64_t sn, int cell) {
 #pragma unroll
-                for (int it = 0; it < CH; it++) {
-                    const int i = it * 32 + lane;
-                    const int row = i / CH, e = i - row * CH;
-                    const int64_t tok = (int64_t)cell * FSATTN_CELL + row;
-                    const bool okr = tok < a.n_kv;
-                    const int64_t tk = okr ? tok : 0;
-                    const int nbytes = okr ? 16 : 0;
-                    const uint32_t kd = (uint32_t)__cvta_generic_to_shared(kw + rm_sw(row, e * 16));
-                    const uint32_t vd = (uint32_t)__cvta_generic_to_shared(vw + rm_sw(row, e * 16));
-                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(kd), "l"(kbase + tk * a.k.sn + e * 8), "r"(nbytes));
-                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(vd), "l"(vbase + tk * a.v.sn + e * 8), "r"(nbytes));
-                }
-                asm volatile("cp.async.commit_group;" ::: "memory");
-                asm volatile("cp.async.wait_group 0;" ::: "memory");
-                __syncwarp();
-            }
+        for (int it = 0; it < CH; it++) {
+            const int i = it * 32 + lane;
+            const int row = i / CH, e = i - row * CH;
+            const int64_t tok = (int64_t)cell * FSATTN_CELL + row;
+            const bool okr = tok < a.n_kv;
+            const int64_t tk = okr ? tok : 0;
+            const int nbytes = okr ? 16 : 0;
+            const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst + rm_sw(row, e * 16));
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(base + tk * sn + e * 8), "r"(nbytes));
+        }
+    };
+    if (n_tiles > 0) {
+        const int c0 = wl[0].x;
+        stage(kw, kbase, a.k.sn, c0);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        stage(vw, vbase, a.v.sn, c0);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    {
+        for (int t = 0; t < n_tiles; t++) {
+            const int2 ent = wl[t];
+            const int cell = ent.x;
+            const unsigned mask = (unsigned)ent.y;
+            const int next_cell = (t + 1 < n_tiles) ? wl[t + 1].x : -1;
+            constexpr int lc = 0;
+            asm volatile("cp.async.wait_group 1;" ::: "memory");      // K of this cell has landed (V may still be in flight)
+            __syncwarp();
             // ---- S = Q K^T over the cell's 32 tokens ----
             float s[4][4];
 #pragma unroll
@@ -207,6 +222,9 @@ __global__ void __launch_bounds__(RM_THREADS, 2) readout_mma_kernel(const fsattn
                     rm_mma(s[nt], qf[kk], b0, b1);
                 }
             }
+            __syncwarp();                                             // every lane has read its K fragments
+            if (next_cell >= 0) stage(kw, kbase, a.k.sn, next_cell);
+            asm volatile("cp.async.commit_group;" ::: "memory");      // (an empty group after the last tile keeps the count)
             // ---- mask, online softmax (rows g: s[.][0..1]; rows g+8: s[.][2..3]) ----
             uint32_t p_hi[4][2], p_lo[4][2];           // per n-tile: packed probabilities of row g and row g+8
             float alpha[2];
@@ -254,6 +272,8 @@ __global__ void __launch_bounds__(RM_THREADS, 2) readout_mma_kernel(const fsattn
                 O[nt][0] *= alpha[0]; O[nt][1] *= alpha[0];
                 O[nt][2] *= alpha[1]; O[nt][3] *= alpha[1];
             }
+            asm volatile("cp.async.wait_group 1;" ::: "memory");      // V of this cell has landed (the next K may be in flight)
+            __syncwarp();
             // ---- O += P V: two k-steps of 16 tokens, eight 8-dim column tiles; V fragments by ldmatrix.trans ----
 #pragma unroll
             for (int k2 = 0; k2 < 2; k2++) {
@@ -273,9 +293,12 @@ __global__ void __launch_bounds__(RM_THREADS, 2) readout_mma_kernel(const fsattn
                     rm_mma(O[np * 2 + 1], alo, v2, v3);
                 }
             }
-            __syncwarp();                  // every lane is done with the buffers before the next cell overwrites them
+            __syncwarp();                                             // every lane has read its V fragments
+            if (next_cell >= 0) stage(vw, vbase, a.v.sn, next_cell);
+            asm volatile("cp.async.commit_group;" ::: "memory");
         }
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
 
     // ---- o -> bf16, lr_norm, combine with the window output ----
     const float glrs = a.lrs[h];

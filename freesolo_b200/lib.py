@@ -159,6 +159,7 @@ ENTRY_POINTS = {
     "fsattn_fsl_decode_step": FslDecode,
     "fsattn_slot_prefill": SlotPrefill,
     "fsattn_trunk_gemv": TrunkGemv,
+    "fsattn_swiglu": ([vp, i64, vp, i64, i64, i32, vp], C.c_int),
     "fsattn_fsb_scratch_floats": ([i32, i32, i32], i64),
     "fsattn_fsb_ingest": ([C.POINTER(FsbForest), i32, i32, i32, vp, i64, vp], C.c_int),
     "fsattn_fsb_spines": ([C.POINTER(FsbForest), i32, i32, C.POINTER(vp), C.POINTER(vp), vp], C.c_int),

@@ -579,3 +579,17 @@ def fsb_select(forests: FsbForests, Q, K, lam, sigma, *, scale: float, N: int = 
     L.call("fsattn_fsb_select", a, _stream(Q))
     return (sel, cand, nvis) if debug else sel
 
+
+
+def swiglu(gu: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out (..., f) = silu(gu[..., :f]) * gu[..., f:] for a fused gate/up projection gu (..., 2f) bf16, one pass."""
+    _need_cuda(gu)
+    assert gu.dtype == torch.bfloat16 and gu.stride(-1) == 1 and gu.shape[-1] % 16 == 0
+    f = gu.shape[-1] // 2
+    g2 = gu.reshape(-1, 2 * f)
+    if out is None:
+        out = torch.empty(*gu.shape[:-1], f, dtype=torch.bfloat16, device=gu.device)
+    o2 = out.view(-1, f)
+    L.check(L.load().fsattn_swiglu(g2.data_ptr(), g2.stride(0), o2.data_ptr(), o2.stride(0), g2.shape[0], f, _stream(gu)),
+            "fsattn_swiglu")
+    return out

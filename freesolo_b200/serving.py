@@ -75,6 +75,9 @@ class SwiGLU(nn.Module):
     def forward(self, x):
         gu_w, d_ff = self._ensure_gu_cache()
         gu = F.linear(x, gu_w)
+        if gu.is_cuda and gu.dtype == torch.bfloat16 and d_ff % 8 == 0:
+            from . import ops
+            return self.w_down(ops.swiglu(gu))                      # one elementwise pass, same roundings
         return self.w_down(F.silu(gu[..., :d_ff]) * gu[..., d_ff:])
 
 

@@ -252,6 +252,13 @@ typedef struct {
 } fsattn_trunk_gemv_t;
 FSATTN_API int fsattn_trunk_gemv(const fsattn_trunk_gemv_t* a, fsattn_stream_t stream);
 
+/* Elementwise SwiGLU gate of the prefill trunk: out (M, f) = silu(gu[:, :f]) * gu[:, f:] for the fused gate/up projection
+ * gu (M, 2f) bf16 (row strides in elements). Replaces F.silu + the elementwise product of SwiGLU.forward
+ * (experiments/scaling/model.py:111-145; trunk_triton.silu_mul on the reference's fused path), with the same two bf16
+ * roundings. */
+FSATTN_API int fsattn_swiglu(const void* gu, int64_t gu_stride, void* out, int64_t out_stride, int64_t M, int32_t f,
+                             fsattn_stream_t stream);
+
 /* ---- FS-B: two forests over the admitted cells, beam search, candidate re-rank ------------------------------------------
  * One fsattn_fsb_forest_t describes ONE forest (admission threshold tau) of one layer for all T = B*H rows.
  *

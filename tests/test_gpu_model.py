@@ -156,3 +156,26 @@ def test_graph_decoder_many_sequences(dev):
     assert runs[1][1].kv_faults() == (0, 0, 0)
     want = cached_generate(m, ids, 1, device=dev, kv="int8")
     assert torch.equal(want[:, P0].cpu(), runs[1][0][:, 0])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,f", [(1, 8), (37, 2816), (4099, 4096)])
+def test_swiglu_against_torch(dev, M, f):
+    """The one-pass SwiGLU gate equals F.silu(gate) * up in bf16, bit for bit up to one bf16 ulp of the silu rounding."""
+    from freesolo_b200 import ops
+    torch.manual_seed(M + f)
+    gu = (torch.randn(M, 2 * f, device=dev) * 2.0).to(torch.bfloat16)
+    got = ops.swiglu(gu)
+    want = torch.nn.functional.silu(gu[:, :f]) * gu[:, f:]
+    assert got.shape == want.shape and got.dtype == torch.bfloat16
+    # the fast exponential may move silu by an ulp before its bf16 rounding: allow one bf16 step of the result
+    err = (got.float() - want.float()).abs()
+    tol = want.float().abs() * 2.0 ** -7 + 1e-6
+    assert bool((err <= tol).all()), f"max excess {(err - tol).max().item()}"
+    assert (got != want).float().mean().item() < 0.01
+    # a strided (row-sliced) input and a preallocated output
+    big = torch.zeros(M, 2 * f + 16, device=dev, dtype=torch.bfloat16)
+    big[:, :2 * f] = gu
+    out = torch.empty(M, f, device=dev, dtype=torch.bfloat16)
+    ops.swiglu(big[:, :2 * f], out=out)
+    assert torch.equal(out, got)
