@@ -4,56 +4,9 @@
 // One warp per output row (or per gate/up row pair for the SwiGLU epilogue). Every kernel is launched with programmatic
 // dependent launch: it fetches its first weight rows into registers BEFORE waiting for the producer kernel, so weight
 // streaming continues across kernel boundaries and the post-dependency critical path is "read x, FMA, reduce, store".
-#include "common.cuh"
+#include "trunk_rows.cuh"
 
 namespace {
-
-constexpr int GEMV_THREADS = 256;
-constexpr int GEMV_WARPS = GEMV_THREADS / 32;
-
-__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
-template <int KC>
-struct RowRegs {
-    uint4 w[KC];
-};
-
-template <int KC>
-__device__ __forceinline__ void load_row(RowRegs<KC>& r, const bf16* row, int lane, int kchunks) {
-#pragma unroll
-    for (int j = 0; j < KC; j++) {
-        const int c = lane + 32 * j;
-        r.w[j] = (row != nullptr && c < kchunks) ? __ldg(reinterpret_cast<const uint4*>(row) + c) : make_uint4(0u, 0u, 0u, 0u);
-    }
-}
-
-template <int KC, int M>
-__device__ __forceinline__ void dot_row(const RowRegs<KC>& r, const uint4* xs, int kchunks, int lane, float* acc) {
-#pragma unroll
-    for (int m = 0; m < M; m++) acc[m] = 0.0f;
-#pragma unroll
-    for (int j = 0; j < KC; j++) {
-        const int c = lane + 32 * j;
-        if (c < kchunks) {
-            const uint4 w = r.w[j];
-            const float w0 = bf_lo(w.x), w1 = bf_hi(w.x), w2 = bf_lo(w.y), w3 = bf_hi(w.y);
-            const float w4 = bf_lo(w.z), w5 = bf_hi(w.z), w6 = bf_lo(w.w), w7 = bf_hi(w.w);
-#pragma unroll
-            for (int m = 0; m < M; m++) {
-                const uint4 x = xs[m * kchunks + c];
-                float a = acc[m];
-                a = fmaf(w0, bf_lo(x.x), a); a = fmaf(w1, bf_hi(x.x), a);
-                a = fmaf(w2, bf_lo(x.y), a); a = fmaf(w3, bf_hi(x.y), a);
-                a = fmaf(w4, bf_lo(x.z), a); a = fmaf(w5, bf_hi(x.z), a);
-                a = fmaf(w6, bf_lo(x.w), a); a = fmaf(w7, bf_hi(x.w), a);
-                acc[m] = a;
-            }
-        }
-    }
-#pragma unroll
-    for (int m = 0; m < M; m++) acc[m] = warp_sum(acc[m]);
-}
 
 // KC = ceil(K / 256) 16-byte chunks per lane; M rows of activations; EPI as in the header
 template <int KC, int M>

@@ -123,6 +123,22 @@ class TrunkGemv(C.Structure):
 
 
 EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU = 0, 1, 2
+
+
+class TrunkLayer(C.Structure):
+    _fields_ = [("x", vp), ("x_stride", i64),
+                ("y", vp), ("y_stride", i64),
+                ("w_o", vp),
+                ("norm2_w", vp), ("eps2", f32),
+                ("w_gu", vp),
+                ("act", vp), ("act_stride", i64),
+                ("w_down", vp),
+                ("norm_next_w", vp), ("eps_next", f32),
+                ("w_next", vp), ("out_next", vp), ("out_next_stride", i64), ("n_next", i32),
+                ("bar", vp), ("status", vp),
+                ("M", i32), ("d", i32), ("f", i32), ("pdl", i32)]
+
+
 class FsbForest(C.Structure):
     _fields_ = [("T", i32), ("H", i32), ("D", i32), ("m_cap", i32),
                 ("kbar", vp), ("kbar_st", i64), ("ceil", vp), ("ceil_st", i64), ("tau", vp),
@@ -142,7 +158,7 @@ class FsbSelect(C.Structure):
 FSB_SPINE_MAX = 20
 FSB_MAX_MCAP = 16384
 
-EXTRA_STRUCTS = {"fsattn_trunk_gemv_t": TrunkGemv, "fsattn_fsb_forest_t": FsbForest, "fsattn_fsb_select_t": FsbSelect}
+EXTRA_STRUCTS = {"fsattn_trunk_gemv_t": TrunkGemv, "fsattn_trunk_layer_t": TrunkLayer, "fsattn_fsb_forest_t": FsbForest, "fsattn_fsb_select_t": FsbSelect}
 
 # every exported symbol of include/fsattn_b200.h with its argument struct (None = no struct argument)
 ENTRY_POINTS = {
@@ -159,6 +175,7 @@ ENTRY_POINTS = {
     "fsattn_fsl_decode_step": FslDecode,
     "fsattn_slot_prefill": SlotPrefill,
     "fsattn_trunk_gemv": TrunkGemv,
+    "fsattn_trunk_layer": TrunkLayer,
     "fsattn_swiglu": ([vp, i64, vp, i64, i64, i32, vp], C.c_int),
     "fsattn_fsb_scratch_floats": ([i32, i32, i32], i64),
     "fsattn_fsb_ingest": ([C.POINTER(FsbForest), i32, i32, i32, vp, i64, vp], C.c_int),

@@ -438,6 +438,36 @@ def trunk_gemv(x, w, *, norm_w=None, eps: float = 1e-6, res=None, swiglu: bool =
     return out
 
 
+def trunk_layer(x, y, w_o, norm2_w, eps2, w_gu, act, w_down, bar, status, *, norm_next_w=None, eps_next: float = 1e-6,
+                w_next=None, out_next=None, pdl: bool = True):
+    """Everything of a layer after its attention for a decode step of M <= 8 rows, one cooperative launch:
+    x += y @ w_o^T; act = SwiGLU(rmsnorm(x) @ w_gu^T); x += act @ w_down^T; out_next = rmsnorm'(x) @ w_next^T.
+    x (M,d) is updated in place; bar (>= 3 int32, zeroed by the caller before the launch) carries the grid barriers;
+    status (int32[1]) is set to 1 if a barrier ran out of its bound."""
+    _need_cuda(x, y, w_o, norm2_w, w_gu, act, w_down, bar, status, norm_next_w, w_next, out_next)
+    M, d = x.shape
+    f = w_down.shape[1]
+    bf = torch.bfloat16
+    assert all(t.dtype == bf for t in (x, y, w_o, norm2_w, w_gu, act, w_down)) and x.stride(1) == 1 and y.stride(1) == 1
+    assert tuple(y.shape) == (M, d) and tuple(w_o.shape) == (d, d) and tuple(w_gu.shape) == (2 * f, d) and tuple(w_down.shape) == (d, f)
+    assert tuple(act.shape) == (M, f) and act.stride(1) == 1 and w_o.is_contiguous() and w_gu.is_contiguous() and w_down.is_contiguous()
+    assert bar.dtype == torch.int32 and bar.numel() >= 3 and bar.is_contiguous() and status.dtype == torch.int32
+    a = L.TrunkLayer()
+    a.x, a.x_stride, a.y, a.y_stride = x.data_ptr(), x.stride(0), y.data_ptr(), y.stride(0)
+    a.w_o, a.norm2_w, a.eps2, a.w_gu = w_o.data_ptr(), norm2_w.data_ptr(), float(eps2), w_gu.data_ptr()
+    a.act, a.act_stride, a.w_down = act.data_ptr(), act.stride(0), w_down.data_ptr()
+    if w_next is not None:
+        assert norm_next_w is not None and out_next is not None and w_next.dtype == bf and w_next.is_contiguous()
+        assert w_next.shape[1] == d and tuple(out_next.shape) == (M, w_next.shape[0]) and out_next.stride(1) == 1
+        assert norm_next_w.dtype == bf and norm_next_w.numel() == d and out_next.dtype == bf
+        a.norm_next_w, a.eps_next, a.w_next = norm_next_w.data_ptr(), float(eps_next), w_next.data_ptr()
+        a.out_next, a.out_next_stride, a.n_next = out_next.data_ptr(), out_next.stride(0), w_next.shape[0]
+    a.bar, a.status = bar.data_ptr(), status.data_ptr()
+    a.M, a.d, a.f, a.pdl = M, d, f, 1 if pdl else 0
+    L.call("fsattn_trunk_layer", a, _stream(x))
+    return x
+
+
 def default_scale(D: int) -> float:
     return 1.0 / math.sqrt(D)
 

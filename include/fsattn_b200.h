@@ -252,6 +252,30 @@ typedef struct {
 } fsattn_trunk_gemv_t;
 FSATTN_API int fsattn_trunk_gemv(const fsattn_trunk_gemv_t* a, fsattn_stream_t stream);
 
+/* Everything of a layer after its attention, for a decode step of M <= 8 rows, in one cooperative launch:
+ *   x += W_o y;  act = silu(gate) * up of W_gu rmsnorm(x; norm2_w);  x += W_down act;
+ *   out_next = W_next rmsnorm(x; norm_next_w)   (the next layer's QKV projection or the LM head; skipped when w_next is NULL).
+ * Same arithmetic and roundings as four fsattn_trunk_gemv calls (experiments/scaling/model.py:111-145,211-237 and
+ * src/fsattn/attention.py:1396-1420 in the reference), without the three launch boundaries: the phases are separated by
+ * grid-wide barriers on bar[0..2], which the caller zeroes before every launch (e.g. one memset per step for all layers).
+ * A barrier that does not complete within its bound sets *status to 1 and the kernel runs to its end; the caller reads
+ * status where it reads its other device flags. x (M, d) is updated in place; act (M, f) is scratch.
+ * W_o (d, d), W_gu (2f, d) gate rows then up rows, W_down (d, f), W_next (n_next, d): bf16 row-major, 16-byte aligned. */
+typedef struct {
+    void* x; int64_t x_stride;
+    const void* y; int64_t y_stride;
+    const void* w_o;
+    const void* norm2_w; float eps2;
+    const void* w_gu;
+    void* act; int64_t act_stride;
+    const void* w_down;
+    const void* norm_next_w; float eps_next;
+    const void* w_next; void* out_next; int64_t out_next_stride; int32_t n_next;
+    int32_t* bar; int32_t* status;
+    int32_t M, d, f, pdl;
+} fsattn_trunk_layer_t;
+FSATTN_API int fsattn_trunk_layer(const fsattn_trunk_layer_t* a, fsattn_stream_t stream);
+
 /* Elementwise SwiGLU gate of the prefill trunk: out (M, f) = silu(gu[:, :f]) * gu[:, f:] for the fused gate/up projection
  * gu (M, 2f) bf16 (row strides in elements). Replaces F.silu + the elementwise product of SwiGLU.forward
  * (experiments/scaling/model.py:111-145; trunk_triton.silu_mul on the reference's fused path), with the same two bf16

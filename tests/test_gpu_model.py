@@ -179,3 +179,77 @@ def test_swiglu_against_torch(dev, M, f):
     out = torch.empty(M, f, device=dev, dtype=torch.bfloat16)
     ops.swiglu(big[:, :2 * f], out=out)
     assert torch.equal(out, got)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B", [1, 3])
+def test_fused_layer_kernel_equals_separate_launches(dev, B, monkeypatch):
+    """The cooperative per-layer kernel (W_o + residual, norm + gate/up + SwiGLU, down + residual, next norm + QKV / LM head
+    behind grid barriers) reproduces the five-launch step bit for bit: same tokens and logits over a run that crosses cell
+    closes, both un-captured and replayed from the step graph; no barrier ran out of its bound."""
+    from freesolo_b200.serving import FreeSoloLM, GraphedDecoder, serve_kwargs
+    torch.manual_seed(0)
+    m = FreeSoloLM.from_config("debug", max_seq_len=2048, **serve_kwargs("sparse")).to(dev).to(torch.bfloat16).eval()
+    P0, T = 600, 70
+    ids = torch.randint(0, 32000, (B, P0), generator=torch.Generator().manual_seed(11 + B))
+    runs = {}
+    for fused, eager in (("0", 2), ("1", 10 ** 9), ("1", 2)):
+        monkeypatch.setenv("FSATTN_TRUNK_FUSED", fused)
+        gd = GraphedDecoder(m, ids, Lmax=P0 + T + 8, device=dev, kv="int8", eager_steps=eager)
+        toks = [gd.prefill().clone()]
+        lg = []
+        for i in range(T - 1):
+            toks.append(gd.step().clone())
+            if i in (0, T - 2):
+                lg.append(gd.logits.clone())
+        assert gd.fused_trunk == (fused == "1")
+        assert gd.trunk_status() == 0
+        runs[(fused, eager)] = (torch.cat(toks, dim=1).cpu(), lg, gd)
+    base = runs[("0", 2)]
+    for key in (("1", 10 ** 9), ("1", 2)):
+        got = runs[key]
+        assert torch.equal(base[0], got[0]), f"tokens differ for fused={key}"
+        for a, b in zip(base[1], got[1]):
+            assert torch.equal(a, b), f"logits differ for fused={key}"
+    assert runs[("1", 2)][2].graph is not None
+    assert runs[("1", 2)][2].launches_per_step() == 2 * len(m.blocks) + 1
+
+
+@pytest.mark.gpu
+def test_fused_layer_kernel_direct(dev):
+    """fsattn_trunk_layer against four fsattn_trunk_gemv calls on random operands at the 341M shapes (d 1024, f 2816),
+    5 rows, with and without the next projection; bit-exact."""
+    from freesolo_b200 import ops
+    torch.manual_seed(5)
+    M, d, f, n_next = 5, 1024, 2816, 3072
+    bf = dict(device=dev, dtype=torch.bfloat16)
+    x0 = torch.randn(M, d, **bf)
+    y = torch.randn(M, d, **bf)
+    w_o = (torch.randn(d, d, device=dev) * 0.03).to(torch.bfloat16)
+    w_gu = (torch.randn(2 * f, d, device=dev) * 0.03).to(torch.bfloat16)
+    w_dn = (torch.randn(d, f, device=dev) * 0.03).to(torch.bfloat16)
+    w_nx = (torch.randn(n_next, d, device=dev) * 0.03).to(torch.bfloat16)
+    n2 = (1.0 + 0.1 * torch.randn(d, device=dev)).to(torch.bfloat16)
+    n1 = (1.0 + 0.1 * torch.randn(d, device=dev)).to(torch.bfloat16)
+    # separate launches
+    xr = x0.clone()
+    ops.trunk_gemv(y, w_o, res=xr, out=xr)
+    act_r = ops.trunk_gemv(xr, w_gu, norm_w=n2, eps=1e-6, swiglu=True)
+    ops.trunk_gemv(act_r, w_dn, res=xr, out=xr)
+    nx_r = ops.trunk_gemv(xr, w_nx, norm_w=n1, eps=1e-5)
+    for with_next in (True, False):
+        x = x0.clone()
+        act = torch.zeros(M, f, **bf)
+        out = torch.zeros(M, n_next, **bf)
+        bar = torch.zeros(4, dtype=torch.int32, device=dev)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        kw = dict(norm_next_w=n1, eps_next=1e-5, w_next=w_nx, out_next=out) if with_next else {}
+        ops.trunk_layer(x, y, w_o, n2, 1e-6, w_gu, act, w_dn, bar, status, **kw)
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        assert torch.equal(x, xr) and torch.equal(act, act_r)
+        if with_next:
+            assert torch.equal(out, nx_r)
+            assert bar[:3].tolist() == [148, 148, 148] or bar[0].item() == bar[2].item() > 0
+        else:
+            assert bar[2].item() == 0
