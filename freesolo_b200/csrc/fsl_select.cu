@@ -57,7 +57,7 @@ extern "C" int fsattn_fsl_prefix_topp(const fsattn_fsl_topp_t* a, fsattn_stream_
 // ---- candidate scoring + top-kk -------------------------------------------------------------------------------------
 // One CTA per (block, b*h): the block's candidate mean keys are staged once in shared memory (fp32), each thread owns
 // one query: q in registers, fp32 dot per candidate (shared-memory broadcast reads), prior, running top-(kk+1).
-template <int D>
+template <int D, int KMAX>
 __global__ void __launch_bounds__(128) fsl_select_kernel(const fsattn_fsl_select_t a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int C = a.P + a.Wc;
@@ -121,7 +121,8 @@ __global__ void __launch_bounds__(128) fsl_select_kernel(const fsattn_fsl_select
     const float two_sigma = f_mul(2.0f, a.sigma[h]);
     const float qpos = (float)qi;
 
-    constexpr int KMAX = FSATTN_MAX_KK + 1;
+    // KMAX - 1 >= kk entries are kept (+1 for the margin): 5 for the serve configuration's top-4, so the sorted insert is
+    // five compare-and-swap steps per candidate instead of nine
     float ts[KMAX];
     int tslot[KMAX];
 #pragma unroll
@@ -165,12 +166,12 @@ __global__ void __launch_bounds__(128) fsl_select_kernel(const fsattn_fsl_select
     }
     int32_t* so = a.sel + ((int64_t)bh * a.nb * a.Bq + qi) * a.kk;
 #pragma unroll
-    for (int j = 0; j < FSATTN_MAX_KK; j++)
+    for (int j = 0; j < KMAX - 1; j++)
         if (j < a.kk) so[j] = (tslot[j] >= 0 && cok[tslot[j]]) ? ccell[tslot[j]] : -1;
     if (a.margin != nullptr) {
         float mg = INFINITY;
 #pragma unroll
-        for (int j = 0; j < FSATTN_MAX_KK; j++) {
+        for (int j = 0; j < KMAX - 1; j++) {
             if (j < a.kk && tslot[j] >= 0 && tslot[j + 1] >= 0 && ts[j] > FS_NEG_SCORE * 0.5f)
                 mg = fminf(mg, ts[j] - ts[j + 1]);
         }
@@ -180,22 +181,27 @@ __global__ void __launch_bounds__(128) fsl_select_kernel(const fsattn_fsl_select
 
 static size_t select_smem(int C, int D) { return (size_t)C * D * 4 + (size_t)C * 12; }
 
-template <int D>
-static int launch_select(const fsattn_fsl_select_t* a, cudaStream_t st) {
+template <int D, int KMAX>
+static int launch_select_k(const fsattn_fsl_select_t* a, cudaStream_t st) {
     const size_t smem = select_smem(a->P + a->Wc, D);
     static size_t opted[16] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 16 && opted[dev] < smem) {
-        if (cudaFuncSetAttribute(fsl_select_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+        if (cudaFuncSetAttribute(fsl_select_kernel<D, KMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
             fs_set_error("fsl_select: cannot opt in to %zu bytes of shared memory", smem);
             return FSATTN_ELAUNCH;
         }
         opted[dev] = smem;
     }
     dim3 grid(a->nb, a->B * a->H);
-    fsl_select_kernel<D><<<grid, 128, smem, st>>>(*a);
+    fsl_select_kernel<D, KMAX><<<grid, 128, smem, st>>>(*a);
     return fs_check_launch("fsl_select");
+}
+
+template <int D>
+static int launch_select(const fsattn_fsl_select_t* a, cudaStream_t st) {
+    return a->kk <= 4 ? launch_select_k<D, 5>(a, st) : launch_select_k<D, FSATTN_MAX_KK + 1>(a, st);
 }
 
 extern "C" int fsattn_fsl_select(const fsattn_fsl_select_t* a, fsattn_stream_t stream) {

@@ -5,25 +5,34 @@
 
 namespace {
 
+__device__ __forceinline__ uint4 swiglu8(const uint4& g, const uint4& u) {
+    const uint32_t gw[4] = {g.x, g.y, g.z, g.w}, uw[4] = {u.x, u.y, u.z, u.w};
+    uint32_t ow[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const float g0 = bf_lo(gw[k]), g1 = bf_hi(gw[k]);
+        const float s0 = bf_round(g0 / (1.0f + __expf(-g0))), s1 = bf_round(g1 / (1.0f + __expf(-g1)));
+        ow[k] = pack_bf2(s0 * bf_lo(uw[k]), s1 * bf_hi(uw[k]));
+    }
+    return make_uint4(ow[0], ow[1], ow[2], ow[3]);
+}
+
+// two 16-byte chunks per thread and iteration, so that four loads are in flight before the first use
 __global__ void __launch_bounds__(256) swiglu_kernel(const uint4* __restrict__ gu, uint4* __restrict__ out, int64_t M, int f8,
                                                      int64_t gu_stride8, int64_t out_stride8) {
     const int64_t total = M * f8;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t m = i / f8;
-        const int j = (int)(i - m * f8);
-        const uint4 g = gu[m * gu_stride8 + j];
-        const uint4 u = gu[m * gu_stride8 + f8 + j];
-        uint4 o;
-        const uint32_t gw[4] = {g.x, g.y, g.z, g.w}, uw[4] = {u.x, u.y, u.z, u.w};
-        uint32_t ow[4];
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const float g0 = bf_lo(gw[k]), g1 = bf_hi(gw[k]);
-            const float s0 = bf_round(g0 / (1.0f + __expf(-g0))), s1 = bf_round(g1 / (1.0f + __expf(-g1)));
-            ow[k] = pack_bf2(s0 * bf_lo(uw[k]), s1 * bf_hi(uw[k]));
-        }
-        o.x = ow[0]; o.y = ow[1]; o.z = ow[2]; o.w = ow[3];
-        out[m * out_stride8 + j] = o;
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += 2 * step) {
+        const int64_t i2 = i + step;
+        const bool two = i2 < total;
+        const int64_t m = i / f8, m2 = two ? i2 / f8 : m;
+        const int j = (int)(i - m * f8), j2 = two ? (int)(i2 - m2 * f8) : j;
+        const uint4 g = __ldcs(gu + m * gu_stride8 + j);
+        const uint4 u = __ldcs(gu + m * gu_stride8 + f8 + j);
+        const uint4 g2 = __ldcs(gu + m2 * gu_stride8 + j2);
+        const uint4 u2 = __ldcs(gu + m2 * gu_stride8 + f8 + j2);
+        out[m * out_stride8 + j] = swiglu8(g, u);
+        if (two) out[m2 * out_stride8 + j2] = swiglu8(g2, u2);
     }
 }
 
