@@ -38,6 +38,16 @@ __device__ __forceinline__ uint32_t rm_sw(int row, int byte_in_row) {
     return (uint32_t)(row * RM_ROWB + ((((byte_in_row >> 4) ^ (row & 7)) << 4) | (byte_in_row & 15)));
 }
 
+__device__ __forceinline__ float rm_ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ uint32_t rm_pack(float lo, float hi) {          // cvt.rn.bf16x2.f32: lo in bits 0..15
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+
 __device__ __forceinline__ void rm_mma(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
                  : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
@@ -152,7 +162,6 @@ __global__ void __launch_bounds__(RM_THREADS, 2) readout_mma_kernel(const fsattn
 #pragma unroll
         for (int e = 0; e < 4; e++) O[nt][e] = 0.f;
     float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-    const int qpos_lo = a.q_pos0 + q0 + r_lo, qpos_hi = qpos_lo + 8;
 
     const bf16* kbase = (const bf16*)a.k.ptr + b * a.k.sb + h * a.k.sh;
     const bf16* vbase = (const bf16*)a.v.ptr + b * a.v.sb + h * a.v.sh;
@@ -177,19 +186,33 @@ __global__ void __launch_bounds__(RM_THREADS, 2) readout_mma_kernel(const fsattn
         n_tiles += __popc(need);
     }
     __syncwarp();
+    // staging: lane -> (row group lane >> 3, 16-byte chunk lane & 7); iteration it adds four rows. The swizzled chunk only
+    // depends on the parity of it, so the destination is one of two per-lane bases plus a constant
+    const int st_r = lane >> 3, st_e = lane & 7;
+    const uint32_t st_d0 = (uint32_t)(st_r * RM_ROWB + ((st_e ^ st_r) << 4));
+    const uint32_t st_d1 = (uint32_t)(st_r * RM_ROWB + ((st_e ^ (4 + st_r)) << 4));
     auto stage = [&](unsigned char* dst, const bf16* base, int64_t sn, int cell) {
+        const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+        const int lim = min(FSATTN_CELL, a.n_kv - cell * FSATTN_CELL);          // rows of the cell that exist (32 but for a ragged tail)
+        const bf16* src = base + ((int64_t)cell * FSATTN_CELL + st_r) * sn + st_e * 8;
 #pragma unroll
         for (int it = 0; it < CH; it++) {
-            const int i = it * 32 + lane;
-            const int row = i / CH, e = i - row * CH;
-            const int64_t tok = (int64_t)cell * FSATTN_CELL + row;
-            const bool okr = tok < a.n_kv;
-            const int64_t tk = okr ? tok : 0;
-            const int nbytes = okr ? 16 : 0;
-            const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst + rm_sw(row, e * 16));
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(base + tk * sn + e * 8), "r"(nbytes));
+            const int row = it * 4 + st_r;
+            const int nbytes = row < lim ? 16 : 0;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d + it * 4 * RM_ROWB + ((it & 1) ? st_d1 : st_d0)),
+                         "l"(row < lim ? src + (int64_t)it * 4 * sn : base), "r"(nbytes));
         }
     };
+    // fragment-load addresses do not change from tile to tile (the warp's buffers are fixed): K by (k-step pair), V by
+    // (pair of 8-dim column tiles); the tile row / token half is a constant offset
+    uint32_t k_ld[2], v_ld[4];
+#pragma unroll
+    for (int kp = 0; kp < 2; kp++)
+        k_ld[kp] = (uint32_t)__cvta_generic_to_shared(kw + rm_sw(lane & 7, (kp * 4 + (lane >> 3)) * 16));
+#pragma unroll
+    for (int np = 0; np < 4; np++)
+        v_ld[np] = (uint32_t)__cvta_generic_to_shared(vw + rm_sw((lane & 7) + ((lane >> 3) & 1) * 8, (np * 2 + (lane >> 4)) * 16));
+    const float sl2 = a.scale * 1.4426950408889634f;
     if (n_tiles > 0) {
         const int c0 = wl[0].x;
         stage(kw, kbase, a.k.sn, c0);
@@ -203,63 +226,60 @@ __global__ void __launch_bounds__(RM_THREADS, 2) readout_mma_kernel(const fsattn
             const int cell = ent.x;
             const unsigned mask = (unsigned)ent.y;
             const int next_cell = (t + 1 < n_tiles) ? wl[t + 1].x : -1;
-            constexpr int lc = 0;
             asm volatile("cp.async.wait_group 1;" ::: "memory");      // K of this cell has landed (V may still be in flight)
             __syncwarp();
-            // ---- S = Q K^T over the cell's 32 tokens ----
+            // ---- S = Q K^T over the cell's 32 tokens: per 8-token tile two ldmatrix.x4 bring the B fragments of all four
+            // k-steps (matrix j of a load = 16-byte chunk kp*4 + j of the tile's eight rows) ----
             float s[4][4];
 #pragma unroll
-            for (int nt = 0; nt < 4; nt++)
+            for (int nt = 0; nt < 4; nt++) {
 #pragma unroll
                 for (int e = 0; e < 4; e++) s[nt][e] = 0.f;
 #pragma unroll
-            for (int kk = 0; kk < 4; kk++) {
-#pragma unroll
-                for (int nt = 0; nt < 4; nt++) {
-                    const int r = lc * 32 + nt * 8 + g;
-                    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kw + rm_sw(r, kk * 32 + tg * 4));
-                    const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kw + rm_sw(r, kk * 32 + 16 + tg * 4));
-                    rm_mma(s[nt], qf[kk], b0, b1);
+                for (int kp = 0; kp < 2; kp++) {
+                    uint32_t b0, b1, b2, b3;
+                    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                                 : "=r"(b0), "=r"(b1), "=r"(b2), "=r"(b3) : "r"(k_ld[kp] + nt * 8 * RM_ROWB));
+                    rm_mma(s[nt], qf[2 * kp], b0, b1);
+                    rm_mma(s[nt], qf[2 * kp + 1], b2, b3);
                 }
             }
             __syncwarp();                                             // every lane has read its K fragments
             if (next_cell >= 0) stage(kw, kbase, a.k.sn, next_cell);
             asm volatile("cp.async.commit_group;" ::: "memory");      // (an empty group after the last tile keeps the count)
-            // ---- mask, online softmax (rows g: s[.][0..1]; rows g+8: s[.][2..3]) ----
+            // ---- mask, online softmax in the log2 domain (rows g: s[.][0..1]; rows g+8: s[.][2..3]) ----
+            // A selected cell lies wholly before the query block, so every token is causal; only a ragged last cell needs a
+            // per-token mask. A row that did not select the cell contributes nothing.
+            const int lim = a.n_kv - cell * FSATTN_CELL;
+            if (lim < FSATTN_CELL) {
+#pragma unroll
+                for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+                    for (int e = 0; e < 4; e++)
+                        if (nt * 8 + tg * 2 + (e & 1) >= lim) s[nt][e] = -INFINITY;
+            }
             uint32_t p_hi[4][2], p_lo[4][2];           // per n-tile: packed probabilities of row g and row g+8
             float alpha[2];
 #pragma unroll
             for (int half = 0; half < 2; half++) {
                 const bool rsel = (mask >> (g + 8 * half)) & 1u;
-                const int qpos = half ? qpos_hi : qpos_lo;
-                float mt = -INFINITY;
-#pragma unroll
-                for (int nt = 0; nt < 4; nt++)
-#pragma unroll
-                    for (int e = 0; e < 2; e++) {
-                        const int tok = cell * FSATTN_CELL + nt * 8 + tg * 2 + e;
-                        const bool ok = rsel && tok < a.n_kv && tok < qpos;
-                        const float v = ok ? s[nt][2 * half + e] * a.scale : -INFINITY;
-                        s[nt][2 * half + e] = v;
-                        mt = fmaxf(mt, v);
-                    }
+                float mt = fmaxf(fmaxf(fmaxf(s[0][2 * half], s[0][2 * half + 1]), fmaxf(s[1][2 * half], s[1][2 * half + 1])),
+                                 fmaxf(fmaxf(s[2][2 * half], s[2][2 * half + 1]), fmaxf(s[3][2 * half], s[3][2 * half + 1])));
+                mt = rsel ? mt * sl2 : -INFINITY;
                 mt = fmaxf(mt, __shfl_xor_sync(FS_FULL, mt, 1));
                 mt = fmaxf(mt, __shfl_xor_sync(FS_FULL, mt, 2));
                 const float m_new = fmaxf(m_run[half], mt);
-                const float al = (m_run[half] == -INFINITY) ? 0.0f : __expf(m_run[half] - m_new);
+                const float m_safe = (m_new == -INFINITY) ? 0.0f : m_new;      // a row with nothing yet: exp2(-inf - 0) = 0
+                const float al = rm_ex2(m_run[half] - m_safe);
                 float psum = 0.f;
 #pragma unroll
                 for (int nt = 0; nt < 4; nt++) {
-                    float p[2];
-#pragma unroll
-                    for (int e = 0; e < 2; e++) {
-                        const float v = s[nt][2 * half + e];
-                        p[e] = (v == -INFINITY) ? 0.0f : __expf(v - m_new);
-                        psum += p[e];
-                    }
-                    const float h0 = bf_round(p[0]), h1 = bf_round(p[1]);
-                    p_hi[nt][half] = pack_bf2(h0, h1);
-                    p_lo[nt][half] = pack_bf2(p[0] - h0, p[1] - h1);
+                    const float p0 = rsel ? rm_ex2(fmaf(s[nt][2 * half], sl2, -m_safe)) : 0.0f;
+                    const float p1 = rsel ? rm_ex2(fmaf(s[nt][2 * half + 1], sl2, -m_safe)) : 0.0f;
+                    psum += p0 + p1;
+                    const uint32_t hi = rm_pack(p0, p1);                       // one packed convert for the pair
+                    p_hi[nt][half] = hi;
+                    p_lo[nt][half] = rm_pack(p0 - bf_lo(hi), p1 - bf_hi(hi));
                 }
                 psum += __shfl_xor_sync(FS_FULL, psum, 1);
                 psum += __shfl_xor_sync(FS_FULL, psum, 2);
@@ -281,12 +301,9 @@ __global__ void __launch_bounds__(RM_THREADS, 2) readout_mma_kernel(const fsattn
                 const uint32_t alo[4] = {p_lo[2 * k2][0], p_lo[2 * k2][1], p_lo[2 * k2 + 1][0], p_lo[2 * k2 + 1][1]};
 #pragma unroll
                 for (int np = 0; np < 4; np++) {                       // two column tiles per ldmatrix.x4
-                    const int row = lc * 32 + k2 * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-                    const int nt = np * 2 + (lane >> 4);
-                    const uint32_t addr = (uint32_t)__cvta_generic_to_shared(vw + rm_sw(row, nt * 16));
                     uint32_t v0, v1, v2, v3;
                     asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                                 : "=r"(v0), "=r"(v1), "=r"(v2), "=r"(v3) : "r"(addr));
+                                 : "=r"(v0), "=r"(v1), "=r"(v2), "=r"(v3) : "r"(v_ld[np] + k2 * 16 * RM_ROWB));
                     rm_mma(O[np * 2], ah, v0, v1);
                     rm_mma(O[np * 2], alo, v0, v1);
                     rm_mma(O[np * 2 + 1], ah, v2, v3);
