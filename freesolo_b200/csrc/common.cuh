@@ -45,7 +45,10 @@ __device__ __forceinline__ uint32_t f2bf_bits(float f) {
     return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(f));
 }
 __device__ __forceinline__ float bf_round(float f) { return __bfloat162float(__float2bfloat16_rn(f)); }
-__device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) { return f2bf_bits(lo) | (f2bf_bits(hi) << 16); }
+__device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {        // one cvt.rn.bf16x2.f32; lo in bits 0..15
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
 
 // four consecutive values starting at element e of a row: from int8 codes (one 32-bit word) or bf16 (one 64-bit word)
 __device__ __forceinline__ void unpack4_i8(uint32_t w, float* o) {

@@ -262,6 +262,12 @@ __global__ void __launch_bounds__(RM_THREADS, 2) readout_mma_kernel(const fsattn
             float alpha[2];
 #pragma unroll
             for (int half = 0; half < 2; half++) {
+                if (((mask >> (8 * half)) & 0xffu) == 0u) {            // none of these eight rows selected the cell (warp-uniform)
+#pragma unroll
+                    for (int nt = 0; nt < 4; nt++) p_hi[nt][half] = p_lo[nt][half] = 0u;
+                    alpha[half] = 1.0f;
+                    continue;
+                }
                 const bool rsel = (mask >> (g + 8 * half)) & 1u;
                 float mt = fmaxf(fmaxf(fmaxf(s[0][2 * half], s[0][2 * half + 1]), fmaxf(s[1][2 * half], s[1][2 * half + 1])),
                                  fmaxf(fmaxf(s[2][2 * half], s[2][2 * half + 1]), fmaxf(s[3][2 * half], s[3][2 * half + 1])));
