@@ -56,7 +56,7 @@ class FslSelect(C.Structure):
                 ("P", i32), ("Wc", i32), ("kk", i32),
                 ("scale", f32),
                 ("sel", vp), ("margin", vp),
-                ("topp_nb", i32)]
+                ("topp_nb", i32), ("impl", i32)]
 
 
 class WindowPrefill(C.Structure):

@@ -139,8 +139,8 @@ def fsl_prefix_topp(ceil, ncell: int, Bq: int, nb: int, P: int):
 
 
 def fsl_select(Q, kbar, ceil, topp, lam, sigma, *, N: int, ncell: int, Bq: int, nb: int, P: int, Wc: int, kk: int,
-               scale: float, want_margin: bool = False):
-    """sel (B,H,nb*Bq,kk) int32 (and the fp32 margins when asked)."""
+               scale: float, want_margin: bool = False, impl: int = 0):
+    """sel (B,H,nb*Bq,kk) int32 (and the fp32 margins when asked). impl 1 forces the CUDA-core kernel."""
     _need_cuda(Q, kbar, ceil, topp)
     B, H, _, D = Q.shape
     if ncell <= 0:      # nothing completed: no cell can be selected
@@ -161,6 +161,7 @@ def fsl_select(Q, kbar, ceil, topp, lam, sigma, *, N: int, ncell: int, Bq: int, 
     a.sel, a.margin = sel.data_ptr(), _p(margin)
     assert topp.is_contiguous() and topp.shape[0] == B * H and topp.shape[1] >= nb and topp.shape[2] == P
     a.topp_nb = topp.shape[1]
+    a.impl = int(impl)
     L.call("fsattn_fsl_select", a, _stream(Q))
     return (sel, margin) if want_margin else sel
 

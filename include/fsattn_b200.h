@@ -118,6 +118,7 @@ typedef struct {
     float scale;
     int32_t* sel; float* margin;
     int32_t topp_nb; /* blocks per head in the topp buffer when it holds more than nb (0: nb) */
+    int32_t impl;    /* 0: tensor-core dot products where the shape allows (head_dim 64, Bq 128, P+Wc <= 80); 1: CUDA-core kernel */
 } fsattn_fsl_select_t;
 FSATTN_API int fsattn_fsl_select(const fsattn_fsl_select_t* a, fsattn_stream_t stream);
 

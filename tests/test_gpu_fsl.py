@@ -146,8 +146,10 @@ def test_prefix_topp_is_the_stable_topk(dev, kind):
         assert torch.equal(got, want), f"top-{P} lists differ"
 
 
+@pytest.mark.parametrize("impl", [0, 1])
 @pytest.mark.parametrize("kind", KINDS)
-def test_prefill_selection_bit_exact_outside_margin(dev, kind):
+def test_prefill_selection_bit_exact_outside_margin(dev, kind, impl):
+    """impl 0: dot products on tensor-core tiles; impl 1: the CUDA-core kernel. Same bar for both."""
     from freesolo_b200 import ops
     g, Q, K, V = _g(kind)
     N = int(g["N"])
@@ -158,7 +160,7 @@ def test_prefill_selection_bit_exact_outside_margin(dev, kind):
     topp = ops.fsl_prefix_topp(ceil, N // 32, 128, nb, 64 if N // 32 >= 64 else (N + 31) // 32)
     P = topp.shape[-1]
     sel, mg = ops.fsl_select(Q[:, :, :N].to(dev), kbar, ceil, topp, pd["lam"], pd["sigma"], N=N, ncell=N // 32, Bq=128, nb=nb,
-                             P=P, Wc=8, kk=4, scale=0.125, want_margin=True)
+                             P=P, Wc=8, kk=4, scale=0.125, want_margin=True, impl=impl)
     # the oracle on the statistics the GPU produced: the comparison isolates the selection arithmetic
     want, margin = fsl.fsl_select_prefill(Q[:, :, :N].float(), kbar.cpu(), ceil.cpu(), p["lam"], p["sigma"], 0.125, 32, 128, 64, 8, 4, N)
     frac = _sel_check(sel[:, :, :N], want[:, :, :N], margin[:, :, :N], f"{kind} prefill selection")
