@@ -18,7 +18,13 @@ __global__ void __launch_bounds__(32) fsl_prefix_topp_kernel(const fsattn_fsl_to
     int done = 0;   // cells [0, done) are in
     float cbuf = 0.0f;
     int cbase = -32;
-    for (int blk = 0; blk < a.nb; blk++) {
+    // The blocks of a head are split over gridDim.y warps: a warp first brings its list up to its first block by scanning
+    // all earlier cells (32 at a time against the list's last entry, so a scan costs little more than its ~P ln(n/P)
+    // inserts), then walks its own blocks. The rescans are redundant work, but the serial chain per warp shrinks from nb
+    // blocks to nb / gridDim.y blocks plus one scan.
+    const int per = (a.nb + gridDim.y - 1) / gridDim.y;
+    const int b0 = blockIdx.y * per, b1 = min(a.nb, b0 + per);
+    for (int blk = b0; blk < b1; blk++) {
         int vis = (int)(((int64_t)blk * a.Bq) / FSATTN_CELL);
         if (vis > a.ncell) vis = a.ncell;
         while (done < vis) {
@@ -50,7 +56,8 @@ extern "C" int fsattn_fsl_prefix_topp(const fsattn_fsl_topp_t* a, fsattn_stream_
     FS_REQUIRE(a != nullptr && a->ceil != nullptr && a->topp != nullptr, "prefix_topp: null pointer");
     FS_REQUIRE(a->B > 0 && a->H > 0 && a->ncell >= 0 && a->nb > 0 && a->Bq > 0, "prefix_topp: bad sizes");
     FS_REQUIRE(a->P >= 1 && a->P <= FSATTN_MAX_POOL, "prefix_topp: pool size %d not in [1,%d]", a->P, FSATTN_MAX_POOL);
-    fsl_prefix_topp_kernel<<<a->B * a->H, 32, 0, (cudaStream_t)stream>>>(*a);
+    const int nseg = a->nb >= 256 ? 16 : (a->nb >= 32 ? 4 : 1);
+    fsl_prefix_topp_kernel<<<dim3(a->B * a->H, nseg), 32, 0, (cudaStream_t)stream>>>(*a);
     return fs_check_launch("fsl_prefix_topp");
 }
 
