@@ -1,29 +1,87 @@
 // FS-L prefill selection: per-block prefix top-P of the cell ceilings, candidate slots, chunk-mean-key scoring and the
 // per-query top-kk.
 #include "common.cuh"
-#include "pool_list.cuh"
 
 // ---- prefix top-P --------------------------------------------------------------------------------------------------
-// One warp per (b,h) walks the cells in index order and keeps the sorted top-P list in shared memory; after the cells
-// visible to block n are in, the list is written out as that block's row. Ceilings are fetched 32 at a time.
+// A warp keeps the sorted top-P list (ceiling descending, cell index ascending) in registers: list position p lives in
+// lane p & 31, register p >> 5. Cells join in index order; the new cells of a block are tested 32 at a time against the
+// list's last entry and only the few that pass are inserted (two ballots give the rank, shuffles shift the tail by one).
+// After the cells visible to block n are in, the list is written out as that block's row.
+constexpr int TOPP_E = FSATTN_MAX_POOL / 32;      // list entries per lane
+
+struct ToppList {
+    float c[TOPP_E];
+    int i[TOPP_E];
+};
+
+// entry at list position P-1 (valid when the list is full), the same in every lane
+__device__ __forceinline__ void topp_last(const ToppList& L, int P, float& tc, int& ti) {
+    const int jl = (P - 1) >> 5;
+    float c = L.c[0];
+    int i = L.i[0];
+#pragma unroll
+    for (int j = 1; j < TOPP_E; j++)
+        if (j == jl) { c = L.c[j]; i = L.i[j]; }
+    tc = __shfl_sync(FS_FULL, c, (P - 1) & 31);
+    ti = __shfl_sync(FS_FULL, i, (P - 1) & 31);
+}
+
+__device__ __forceinline__ void topp_insert(ToppList& L, int& n, int P, float cv, int ci, int lane) {
+    const int JP = (P + 31) >> 5;
+    int ins = 0;                                        // entries that rank before the new cell
+#pragma unroll
+    for (int j = 0; j < TOPP_E; j++)
+        if (j < JP) ins += __popc(__ballot_sync(FS_FULL, (lane + 32 * j) < n && pool_before(L.c[j], L.i[j], cv, ci)));
+    if (ins >= P) return;
+    const int nn = (n + 1 < P) ? n + 1 : P;
+    // position p > ins takes the old entry p-1: the lane below's register j, or lane 31's register j-1 for lane 0
+    float pc[TOPP_E];
+    int pi[TOPP_E];
+#pragma unroll
+    for (int j = 0; j < TOPP_E; j++) {
+        if (j < JP) {
+            pc[j] = __shfl_up_sync(FS_FULL, L.c[j], 1);
+            pi[j] = __shfl_up_sync(FS_FULL, L.i[j], 1);
+        }
+    }
+#pragma unroll
+    for (int j = TOPP_E - 1; j > 0; j--) {
+        if (j < JP) {
+            const float wc = __shfl_sync(FS_FULL, L.c[j - 1], 31);
+            const int wi = __shfl_sync(FS_FULL, L.i[j - 1], 31);
+            if (lane == 0) { pc[j] = wc; pi[j] = wi; }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < TOPP_E; j++) {
+        if (j < JP) {
+            const int p = lane + 32 * j;
+            if (p == ins) { L.c[j] = cv; L.i[j] = ci; }
+            else if (p > ins && p < nn) { L.c[j] = pc[j]; L.i[j] = pi[j]; }
+        }
+    }
+    n = nn;
+}
+
 __global__ void __launch_bounds__(32) fsl_prefix_topp_kernel(const fsattn_fsl_topp_t a) {
-    __shared__ float lc[FSATTN_MAX_POOL];
-    __shared__ int li[FSATTN_MAX_POOL];
     const int bh = blockIdx.x;
     const int b = bh / a.H, h = bh - b * a.H;
     const int lane = threadIdx.x;
     const float* ceil = a.ceil + b * a.ceil_sb + h * a.ceil_sh;
     int32_t* out = a.topp + (int64_t)bh * a.nb * a.P;
+    ToppList L;
+#pragma unroll
+    for (int j = 0; j < TOPP_E; j++) { L.c[j] = 0.0f; L.i[j] = -1; }
     int n = 0;      // entries in the list
     int done = 0;   // cells [0, done) are in
     float cbuf = 0.0f;
     int cbase = -32;
     // The blocks of a head are split over gridDim.y warps: a warp first brings its list up to its first block by scanning
-    // all earlier cells (32 at a time against the list's last entry, so a scan costs little more than its ~P ln(n/P)
-    // inserts), then walks its own blocks. The rescans are redundant work, but the serial chain per warp shrinks from nb
-    // blocks to nb / gridDim.y blocks plus one scan.
+    // all earlier cells (a scan costs little more than its ~P ln(n/P) inserts), then walks its own blocks. The rescans are
+    // redundant work, but the serial chain per warp shrinks from nb blocks to nb / gridDim.y blocks plus one scan.
     const int per = (a.nb + gridDim.y - 1) / gridDim.y;
     const int b0 = blockIdx.y * per, b1 = min(a.nb, b0 + per);
+    const int JP = (a.P + 31) >> 5;
     for (int blk = b0; blk < b1; blk++) {
         int vis = (int)(((int64_t)blk * a.Bq) / FSATTN_CELL);
         if (vis > a.ncell) vis = a.ncell;
@@ -32,23 +90,28 @@ __global__ void __launch_bounds__(32) fsl_prefix_topp_kernel(const fsattn_fsl_to
                 cbase = done & ~31;
                 cbuf = (cbase + lane < a.ncell) ? ceil[cbase + lane] : 0.0f;
             }
-            // the new cells of this 32-cell segment, tested against the list's last entry all at once: most of them rank
-            // after it once the list is full, and the entry only ever tightens, so a cell rejected here stays rejected
+            // most new cells rank after the full list's last entry, and that entry only ever tightens, so a cell rejected
+            // against it stays rejected
             const int seg_end = min(vis, cbase + 32);
             const bool mine = lane >= done - cbase && lane < seg_end - cbase;
             const bool full = (n == a.P);
-            const float thr_c = full ? lc[a.P - 1] : 0.0f;
-            const int thr_i = full ? li[a.P - 1] : 0;
+            float thr_c = 0.0f;
+            int thr_i = 0;
+            if (full) topp_last(L, a.P, thr_c, thr_i);
             unsigned pend = __ballot_sync(FS_FULL, mine && (!full || pool_before(cbuf, cbase + lane, thr_c, thr_i)));
             while (pend) {
                 const int l = __ffs(pend) - 1;
                 pend &= pend - 1;
                 const float cv = __shfl_sync(FS_FULL, cbuf, l);
-                pool_list_insert(lc, li, n, a.P, cv, cbase + l, lane);
+                topp_insert(L, n, a.P, cv, cbase + l, lane);
             }
             done = seg_end;
         }
-        for (int p = lane; p < a.P; p += 32) out[(int64_t)blk * a.P + p] = (p < n) ? li[p] : -1;
+#pragma unroll
+        for (int j = 0; j < TOPP_E; j++) {
+            const int p = lane + 32 * j;
+            if (j < JP && p < a.P) out[(int64_t)blk * a.P + p] = (p < n) ? L.i[j] : -1;
+        }
     }
 }
 
