@@ -119,7 +119,7 @@ extern "C" int fsattn_fsl_prefix_topp(const fsattn_fsl_topp_t* a, fsattn_stream_
     FS_REQUIRE(a != nullptr && a->ceil != nullptr && a->topp != nullptr, "prefix_topp: null pointer");
     FS_REQUIRE(a->B > 0 && a->H > 0 && a->ncell >= 0 && a->nb > 0 && a->Bq > 0, "prefix_topp: bad sizes");
     FS_REQUIRE(a->P >= 1 && a->P <= FSATTN_MAX_POOL, "prefix_topp: pool size %d not in [1,%d]", a->P, FSATTN_MAX_POOL);
-    const int nseg = a->nb >= 256 ? 16 : (a->nb >= 32 ? 4 : 1);
+    const int nseg = a->nb >= 512 ? 64 : (a->nb >= 128 ? 16 : (a->nb >= 32 ? 4 : 1));
     fsl_prefix_topp_kernel<<<dim3(a->B * a->H, nseg), 32, 0, (cudaStream_t)stream>>>(*a);
     return fs_check_launch("fsl_prefix_topp");
 }

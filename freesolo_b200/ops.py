@@ -624,3 +624,17 @@ def swiglu(gu: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     L.check(L.load().fsattn_swiglu(g2.data_ptr(), g2.stride(0), o2.data_ptr(), o2.stride(0), g2.shape[0], f, _stream(gu)),
             "fsattn_swiglu")
     return out
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out (..., d) = x * rsqrt(mean(x^2) + eps) * w for bf16 rows, fp32 arithmetic, one rounding; one read and one write."""
+    _need_cuda(x, w)
+    d = x.shape[-1]
+    assert x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.stride(-1) == 1 and w.is_contiguous() and w.numel() == d
+    x2 = x.reshape(-1, d)
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    o2 = out.view(-1, d)
+    L.check(L.load().fsattn_rms_norm(x2.data_ptr(), x2.stride(0), w.data_ptr(), float(eps), o2.data_ptr(), o2.stride(0),
+                                     x2.shape[0], d, _stream(x)), "fsattn_rms_norm")
+    return out

@@ -47,6 +47,9 @@ class RMSNorm(nn.Module):
         self.weight = nn.Parameter(torch.ones(dim))
 
     def forward(self, x):
+        if x.is_cuda and x.dtype == torch.bfloat16 and self.weight.dtype == torch.bfloat16 and x.shape[-1] % 8 == 0 and x.numel() > 0:
+            from . import ops
+            return ops.rms_norm(x, self.weight, self.eps)              # one read, one write
         return F.rms_norm(x, (x.shape[-1],), self.weight, self.eps)
 
 

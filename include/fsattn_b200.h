@@ -277,6 +277,11 @@ typedef struct {
 } fsattn_trunk_layer_t;
 FSATTN_API int fsattn_trunk_layer(const fsattn_trunk_layer_t* a, fsattn_stream_t stream);
 
+/* RMSNorm of the prefill trunk: out (M, d) = x * rsqrt(mean(x^2) + eps) * w in fp32, rounded once to bf16 (row strides in
+ * elements). Replaces F.rms_norm / trunk_triton.rms_norm_cast of experiments/scaling/model.py:82-108 on the prefill path. */
+FSATTN_API int fsattn_rms_norm(const void* x, int64_t x_stride, const void* w, float eps, void* out, int64_t out_stride, int64_t M,
+                               int32_t d, fsattn_stream_t stream);
+
 /* Elementwise SwiGLU gate of the prefill trunk: out (M, f) = silu(gu[:, :f]) * gu[:, f:] for the fused gate/up projection
  * gu (M, 2f) bf16 (row strides in elements). Replaces F.silu + the elementwise product of SwiGLU.forward
  * (experiments/scaling/model.py:111-145; trunk_triton.silu_mul on the reference's fused path), with the same two bf16

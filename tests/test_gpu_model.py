@@ -253,3 +253,24 @@ def test_fused_layer_kernel_direct(dev):
             assert bar[:3].tolist() == [148, 148, 148] or bar[0].item() == bar[2].item() > 0
         else:
             assert bar[2].item() == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,d", [(1, 256), (37, 1024), (4099, 1536), (5, 4224)])
+def test_rms_norm_against_torch(dev, M, d):
+    """The one-pass RMSNorm equals F.rms_norm on bf16 rows up to one bf16 ulp (the sum of squares is taken in another order)."""
+    from freesolo_b200 import ops
+    torch.manual_seed(M + d)
+    x = (torch.randn(M, d, device=dev) * 3.0).to(torch.bfloat16)
+    w = (1.0 + 0.2 * torch.randn(d, device=dev)).to(torch.bfloat16)
+    got = ops.rms_norm(x, w, 1e-6)
+    want = torch.nn.functional.rms_norm(x, (d,), w, 1e-6)
+    assert got.shape == want.shape and got.dtype == torch.bfloat16
+    err = (got.float() - want.float()).abs()
+    tol = want.float().abs() * 2.0 ** -7 + 1e-6
+    assert bool((err <= tol).all()), f"max excess {(err - tol).max().item()}"
+    assert (got != want).float().mean().item() < 0.02
+    # rows of a wider buffer (strided input)
+    big = torch.zeros(M, d + 64, device=dev, dtype=torch.bfloat16)
+    big[:, :d] = x
+    assert torch.equal(ops.rms_norm(big[:, :d], w, 1e-6), got)
