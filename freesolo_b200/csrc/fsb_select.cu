@@ -139,6 +139,7 @@ __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, co
     const int root = S.root;
     int ref = -1, meta = 0;
     if (root == -1) return -1;
+    const float inv_two_sig = f_div(1.0f, f_mul(2.0f, sig));
     const int d0 = S.height;                                  // delta = 0: stop depth = height, budget 1
     const int W = min(width, (d0 >= 5) ? 32 : (1 << d0));
     if (lane == 0) {
@@ -217,7 +218,11 @@ __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, co
             float content = f_mul((s0 + s1) + (s2 + s3), scale);
             content = f_add(content, f_mul(f_mul(qn, rad), scale));
             const float ppos = f_mul(f_add((float)pm, 0.5f), 32.0f);
-            const float e = erff(f_div(fabsf(f_add(qpos, -ppos)), f_mul(2.0f, sig)));
+            // erf(x) is 1 in fp32 from x = 4 on, which with a sigma of a few tokens is every node further than a cell or two
+            // from the query: the evaluation is skipped there (by the whole warp when all its children are that far); the
+            // quotient is a product with 1/(2 sigma), one rounding from the reference's division, far inside the margin
+            const float x = f_mul(fabsf(f_add(qpos, -ppos)), inv_two_sig);
+            const float e = (x < 4.0f) ? erff(x) : 1.0f;
             score = f_add(content, f_mul(f_mul(lam, am), e));
         }
         nvis += __popc(__ballot_sync(FS_FULL, valid));

@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(32) fsl_prefix_topp_kernel(const fsattn_fsl_to
     for (int j = 0; j < TOPP_E; j++) { L.c[j] = 0.0f; L.i[j] = -1; }
     int n = 0;      // entries in the list
     int done = 0;   // cells [0, done) are in
-    float cbuf = 0.0f;
+    float cbuf = 0.0f, cnext = 0.0f;
     int cbase = -32;
     // The blocks of a head are split over gridDim.y warps: a warp first brings its list up to its first block by scanning
     // all earlier cells (a scan costs little more than its ~P ln(n/P) inserts), then walks its own blocks. The rescans are
@@ -86,9 +86,11 @@ __global__ void __launch_bounds__(32) fsl_prefix_topp_kernel(const fsattn_fsl_to
         int vis = (int)(((int64_t)blk * a.Bq) / FSATTN_CELL);
         if (vis > a.ncell) vis = a.ncell;
         while (done < vis) {
-            if (done >= cbase + 32) {
-                cbase = done & ~31;
-                cbuf = (cbase + lane < a.ncell) ? ceil[cbase + lane] : 0.0f;
+            if (done >= cbase + 32) {                       // next 32 ceilings; the 32 after them are requested one step ahead
+                const int nbase = done & ~31;
+                cbuf = (nbase == cbase + 32 && cbase >= 0) ? cnext : ((nbase + lane < a.ncell) ? ceil[nbase + lane] : 0.0f);
+                cbase = nbase;
+                cnext = (cbase + 32 + lane < a.ncell) ? ceil[cbase + 32 + lane] : 0.0f;
             }
             // most new cells rank after the full list's last entry, and that entry only ever tightens, so a cell rejected
             // against it stays rejected
