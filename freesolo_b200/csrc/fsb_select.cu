@@ -126,25 +126,172 @@ __device__ __forceinline__ int count_below(const int* adm, int m_tot, int E) {
     return lo;
 }
 
+// ---- the query-independent head of a beam ------------------------------------------------------------------------------------
+// While a round's children all fit in the frontier (carried + 2 x expanding <= W) every child is kept whatever its score, so
+// the SET of frontier nodes after those rounds is the same for every query of the block: 1, 2, 4, 8, 16 nodes down the spine
+// and the top of the chunks. One warp walks those rounds once per (row, block) without scoring anything and records the
+// nodes with the round that created each; a query's beam then starts there, scoring the recorded nodes once to put them
+// in the order the skipped rounds would have left them in (older rounds first, a round's nodes by score), instead of
+// running three or four full rounds.
+struct BeamPre {
+    int ref[WMAX], meta[WMAX], nc[WMAX], rnd[WMAX];
+    int n, nvis, rounds, pad;
+};
+
+template <int D>
+__device__ void beam_prefix(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, int width, int lane, BeamPre& P) {
+    const float4* aux = (const float4*)F.node_aux + (int64_t)t * fsb_nodes_per_row(F.m_cap);
+    const int root = S.root;
+    int ref = -1, meta = 0, nc = 0, rnd = 0;
+    int n = 0, nvis = 0, rounds = 0;
+    if (root != -1) {
+        const int d0 = S.height;
+        const int W = min(width, (d0 >= 5) ? 32 : (1 << d0));
+        if (lane == 0) {
+            ref = root;
+            meta = (root >= 0) ? __float_as_int(aux[REF_ID(root)].w) : 0;
+        }
+        n = 1;
+        for (int it = 0; it < 6; ++it) {
+            const bool active = lane < WMAX && ref != -1;
+            const bool expand = active && (ref < -1 || meta < 0);
+            const unsigned emask = __ballot_sync(FS_FULL, expand);
+            const unsigned cmask = __ballot_sync(FS_FULL, active && !expand);
+            const int nexp = __popc(emask), ncar = __popc(cmask);
+            if (nexp == 0 || ncar + 2 * nexp > W) break;
+            const int ps = lane >> 1, side = lane & 1;
+            const int pref = __shfl_sync(FS_FULL, ref, ps), pmeta = __shfl_sync(FS_FULL, meta, ps);
+            const bool valid = (emask >> ps) & 1;
+            int cref = -1, cmeta = 0, cnc = 0;
+            if (valid) {
+                if (pref >= 0) {
+                    const int np = (~pmeta) >> 4;
+                    cnc = 2 * np + 1 + side;
+                    cref = pref + np + 1 + side;
+                } else {
+                    const float* x = S.node[-pref - 2] + D;
+                    cref = __float_as_int(x[4 + side]);
+                }
+                if (cref >= 0) cmeta = __float_as_int(aux[REF_ID(cref)].w);
+            }
+            const unsigned vmask = __ballot_sync(FS_FULL, valid);
+            const unsigned lt = (1u << lane) - 1u;
+            __syncwarp();
+            if (active && !expand) {
+                const int pos = __popc(cmask & lt);
+                P.ref[pos] = ref; P.meta[pos] = meta; P.nc[pos] = nc; P.rnd[pos] = rnd;
+            }
+            if (valid) {
+                const int pos = ncar + __popc(vmask & lt);
+                P.ref[pos] = cref; P.meta[pos] = cmeta; P.nc[pos] = cnc; P.rnd[pos] = rounds + 1;
+            }
+            __syncwarp();
+            n = ncar + __popc(vmask);
+            nvis += __popc(vmask);
+            ++rounds;
+            ref = -1; meta = 0; nc = 0; rnd = 0;
+            if (lane < n) { ref = P.ref[lane]; meta = P.meta[lane]; nc = P.nc[lane]; rnd = P.rnd[lane]; }
+        }
+    }
+    __syncwarp();
+    if (lane < WMAX) { P.ref[lane] = ref; P.meta[lane] = meta; P.nc[lane] = nc; P.rnd[lane] = rnd; }
+    if (lane == 0) { P.n = n; P.nvis = nvis; P.rounds = rounds; }
+    __syncwarp();
+}
+
 // ---- one beam (one warp). Returns the frontier's cell in lanes 0..15 (-1 none); adds the scored children to nvis ----
 template <int D, bool PREFETCH = false, bool STAGED = false>
-__device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, const uint32_t (&qp)[D / 2], float qn, float qpos,
-                    float lam, float sig, float scale, int width, int lane, int* fr, int& nvis,
+__device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, const BeamPre& P, const uint32_t (&qp)[D / 2], float qn,
+                    float qpos, float lam, float sig, float scale, int width, int lane, int* fr, int& nvis,
                     const unsigned char* stg_mu = nullptr, const float4* stg_aux = nullptr) {
     constexpr int DP = FsbDim<D>::DP;
     const int m_cap = F.m_cap;
     const int64_t nrow = (int64_t)t * fsb_nodes_per_row(m_cap);
     const bf16* node_mu = (const bf16*)F.node_mu + nrow * D;
     const float4* aux = (const float4*)F.node_aux + nrow;
-    const int root = S.root;
-    int ref = -1, meta = 0;
-    if (root == -1) return -1;
+    if (S.root == -1) return -1;
     const float inv_two_sig = f_div(1.0f, f_mul(2.0f, sig));
     const int d0 = S.height;                                  // delta = 0: stop depth = height, budget 1
     const int W = min(width, (d0 >= 5) ? 32 : (1 << d0));
-    if (lane == 0) {
-        ref = root;
-        meta = (root >= 0) ? __float_as_int(aux[REF_ID(root)].w) : 0;
+
+    // score of one node for this query: a chunk node (ref >= 0; nc = its index inside its chunk) or a spine node
+    auto node_score = [&](int cref, int nc, int& cmeta) -> float {
+        float rad, am;
+        int pm;
+        // q . mu with four running sums (plain FMAs: the beam's cut-offs are compared under a score margin, and a
+        // different summation order moves a score by ~1e-6)
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        if (cref >= 0) {
+            uint4 w[D / 8];
+            float4 ax;
+            const int ck = REF_K(cref);
+            if (STAGED && nc < S.stg_cnt[ck]) {
+                const int row = S.stg_base[ck] + nc;
+                const unsigned char* mr = stg_mu + (size_t)row * (D * 2);
+#pragma unroll
+                for (int v = 0; v < D / 8; ++v) w[v] = *(const uint4*)(mr + (((v & ~STG_SW<D>()) | ((v ^ row) & STG_SW<D>())) << 4));
+                ax = stg_aux[row];
+            } else {
+                const uint4* mr = (const uint4*)(node_mu + (int64_t)REF_ID(cref) * D);
+#pragma unroll
+                for (int v = 0; v < D / 8; ++v) w[v] = mr[v];
+                ax = aux[REF_ID(cref)];
+            }
+            // the query sits in registers as bf16 pairs (it is a bf16 tensor): no shared-memory traffic for it
+#pragma unroll
+            for (int v = 0; v < D / 8; ++v) {
+                s0 = fmaf(bf_lo(qp[v * 4 + 0]), bf_lo(w[v].x), s0); s1 = fmaf(bf_hi(qp[v * 4 + 0]), bf_hi(w[v].x), s1);
+                s2 = fmaf(bf_lo(qp[v * 4 + 1]), bf_lo(w[v].y), s2); s3 = fmaf(bf_hi(qp[v * 4 + 1]), bf_hi(w[v].y), s3);
+                s0 = fmaf(bf_lo(qp[v * 4 + 2]), bf_lo(w[v].z), s0); s1 = fmaf(bf_hi(qp[v * 4 + 2]), bf_hi(w[v].z), s1);
+                s2 = fmaf(bf_lo(qp[v * 4 + 3]), bf_lo(w[v].w), s2); s3 = fmaf(bf_hi(qp[v * 4 + 3]), bf_hi(w[v].w), s3);
+            }
+            rad = ax.x; am = ax.y; pm = __float_as_int(ax.z); cmeta = __float_as_int(ax.w);
+        } else {
+            const float* x = S.node[-cref - 2];
+#pragma unroll
+            for (int d = 0; d < D; d += 4) {
+                s0 = fmaf(bf_lo(qp[d / 2]), x[d], s0); s1 = fmaf(bf_hi(qp[d / 2]), x[d + 1], s1);
+                s2 = fmaf(bf_lo(qp[d / 2 + 1]), x[d + 2], s2); s3 = fmaf(bf_hi(qp[d / 2 + 1]), x[d + 3], s3);
+            }
+            rad = x[D]; am = x[D + 1]; pm = __float_as_int(x[D + 2]);
+            cmeta = 0;
+        }
+        float content = f_mul((s0 + s1) + (s2 + s3), scale);
+        content = f_add(content, f_mul(f_mul(qn, rad), scale));
+        const float ppos = f_mul(f_add((float)pm, 0.5f), 32.0f);
+        // erf(x) is 1 in fp32 from x = 4 on, which with a sigma of a few tokens is every node further than a cell or two
+        // from the query: the evaluation is skipped there (by the whole warp when all its children are that far); the
+        // quotient is a product with 1/(2 sigma), one rounding from the reference's division, far inside the margin
+        const float x = f_mul(fabsf(f_add(qpos, -ppos)), inv_two_sig);
+        const float e = (x < 4.0f) ? erff(x) : 1.0f;
+        return f_add(content, f_mul(f_mul(lam, am), e));
+    };
+
+    // ---- start from the block's query-independent head, put into this query's order ----
+    int ref = -1, meta = 0;
+    if (lane < P.n) { ref = P.ref[lane]; meta = P.meta[lane]; }
+    if (P.rounds > 0) {
+        float sc = FS_NEG_SCORE;
+        int rn = 1 << 20;
+        if (lane < P.n) {
+            int cm;
+            rn = P.rnd[lane];
+            sc = node_score(ref, P.nc[lane], cm);
+        }
+        int rank = 0;
+#pragma unroll
+        for (int o = 0; o < WMAX; ++o) {
+            const float so = __shfl_sync(FS_FULL, sc, o);
+            const int ro = __shfl_sync(FS_FULL, rn, o);
+            rank += (ro < rn || (ro == rn && (so > sc || (so == sc && o < lane)))) ? 1 : 0;
+        }
+        int* fm = fr + WMAX;
+        __syncwarp();
+        if (lane < P.n) { fr[rank] = ref; fm[rank] = meta; }
+        __syncwarp();
+        if (lane < P.n) { ref = fr[lane]; meta = fm[lane]; }
+        __syncwarp();
+        nvis += P.nvis;
     }
     for (int it = 0; it < 40; ++it) {
         const bool active = lane < WMAX && ref != -1;
@@ -159,11 +306,6 @@ __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, co
         int cref = -1, cmeta = 0;
         float score = FS_NEG_SCORE;
         if (valid) {
-            float rad, am;
-            int pm;
-            // q . mu with four running sums (plain FMAs: the beam's cut-offs are compared under a score margin, and a
-            // different summation order moves a score by ~1e-6)
-            float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
             int nc = 0;                                     // index of the child inside its chunk
             if (pref >= 0) {
                 const int np = (~pmeta) >> 4;
@@ -181,49 +323,7 @@ __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, co
                 const float* x = S.node[-pref - 2] + D;
                 cref = __float_as_int(x[4 + side]);         // a chunk root (index 0 of its chunk) or a spine node
             }
-            if (cref >= 0) {
-                uint4 w[D / 8];
-                float4 ax;
-                const int ck = REF_K(cref);
-                if (STAGED && nc < S.stg_cnt[ck]) {
-                    const int row = S.stg_base[ck] + nc;
-                    const unsigned char* mr = stg_mu + (size_t)row * (D * 2);
-#pragma unroll
-                    for (int v = 0; v < D / 8; ++v) w[v] = *(const uint4*)(mr + (((v & ~STG_SW<D>()) | ((v ^ row) & STG_SW<D>())) << 4));
-                    ax = stg_aux[row];
-                } else {
-                    const uint4* mr = (const uint4*)(node_mu + (int64_t)REF_ID(cref) * D);
-#pragma unroll
-                    for (int v = 0; v < D / 8; ++v) w[v] = mr[v];
-                    ax = aux[REF_ID(cref)];
-                }
-                // the query sits in registers as bf16 pairs (it is a bf16 tensor): no shared-memory traffic for it
-#pragma unroll
-                for (int v = 0; v < D / 8; ++v) {
-                    s0 = fmaf(bf_lo(qp[v * 4 + 0]), bf_lo(w[v].x), s0); s1 = fmaf(bf_hi(qp[v * 4 + 0]), bf_hi(w[v].x), s1);
-                    s2 = fmaf(bf_lo(qp[v * 4 + 1]), bf_lo(w[v].y), s2); s3 = fmaf(bf_hi(qp[v * 4 + 1]), bf_hi(w[v].y), s3);
-                    s0 = fmaf(bf_lo(qp[v * 4 + 2]), bf_lo(w[v].z), s0); s1 = fmaf(bf_hi(qp[v * 4 + 2]), bf_hi(w[v].z), s1);
-                    s2 = fmaf(bf_lo(qp[v * 4 + 3]), bf_lo(w[v].w), s2); s3 = fmaf(bf_hi(qp[v * 4 + 3]), bf_hi(w[v].w), s3);
-                }
-                rad = ax.x; am = ax.y; pm = __float_as_int(ax.z); cmeta = __float_as_int(ax.w);
-            } else {
-                const float* x = S.node[-cref - 2];
-#pragma unroll
-                for (int d = 0; d < D; d += 4) {
-                    s0 = fmaf(bf_lo(qp[d / 2]), x[d], s0); s1 = fmaf(bf_hi(qp[d / 2]), x[d + 1], s1);
-                    s2 = fmaf(bf_lo(qp[d / 2 + 1]), x[d + 2], s2); s3 = fmaf(bf_hi(qp[d / 2 + 1]), x[d + 3], s3);
-                }
-                rad = x[D]; am = x[D + 1]; pm = __float_as_int(x[D + 2]);
-            }
-            float content = f_mul((s0 + s1) + (s2 + s3), scale);
-            content = f_add(content, f_mul(f_mul(qn, rad), scale));
-            const float ppos = f_mul(f_add((float)pm, 0.5f), 32.0f);
-            // erf(x) is 1 in fp32 from x = 4 on, which with a sigma of a few tokens is every node further than a cell or two
-            // from the query: the evaluation is skipped there (by the whole warp when all its children are that far); the
-            // quotient is a product with 1/(2 sigma), one rounding from the reference's division, far inside the margin
-            const float x = f_mul(fabsf(f_add(qpos, -ppos)), inv_two_sig);
-            const float e = (x < 4.0f) ? erff(x) : 1.0f;
-            score = f_add(content, f_mul(f_mul(lam, am), e));
+            score = node_score(cref, nc, cmeta);
         }
         nvis += __popc(__ballot_sync(FS_FULL, valid));
         // ---- rank the children: (score desc, position asc) ----
@@ -338,6 +438,7 @@ __global__ void __launch_bounds__(NWARP * 32, (NWARP >= 16) ? 2 : 2) fsb_select_
     unsigned char* stg_mu = dsm + SelSmem<D>::MU_OFF;
     float4* stg_aux = (float4*)(dsm + SelSmem<D>::AUX_OFF);
     __shared__ SpineSm<D> sp;
+    __shared__ BeamPre pre;
     __shared__ __align__(16) float qsm[NWARP][DP];
     __shared__ int frs[NWARP][WMAX * 2];
     __shared__ int cand_sm[128][2 * WMAX];
@@ -357,6 +458,8 @@ __global__ void __launch_bounds__(NWARP * 32, (NWARP >= 16) ? 2 : 2) fsb_select_
             const int m_b = count_below(F.adm + (int64_t)t * F.m_cap, F.m_tot[t], E);
             build_spine<D>(F, t, m_b, sp, lane);
             if (lane == 0) stage_plan<D>(sp, m_b, STG_DS<D>());
+            __syncwarp();
+            beam_prefix<D>(F, t, sp, f == 0 ? a.width : a.width2, lane, pre);
         }
         __syncthreads();
         {   // stage the shallow levels: rows of chunk k come from its node array's first stg_cnt[k] rows
@@ -398,7 +501,7 @@ __global__ void __launch_bounds__(NWARP * 32, (NWARP >= 16) ? 2 : 2) fsb_select_
                 qreg[i * 4 + 0] = w4.x; qreg[i * 4 + 1] = w4.y; qreg[i * 4 + 2] = w4.z; qreg[i * 4 + 3] = w4.w;
             }
             int nv = 0;
-            const int c = beam<D, false, true>(F, t, sp, qreg, qn, qpos, lam, sig, a.scale, width, lane, frs[warp], nv,
+            const int c = beam<D, false, true>(F, t, sp, pre, qreg, qn, qpos, lam, sig, a.scale, width, lane, frs[warp], nv,
                                                stg_mu, stg_aux);
             if (lane < width) cand_sm[qi][f * WMAX + lane] = c;
             if (lane == 0) nv_sm[qi] += nv;
@@ -469,6 +572,7 @@ __global__ void __launch_bounds__(256) fsb_decode_select_kernel(SelArgs A) {
     const int b = t / A.H, hd = t % A.H;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     __shared__ SpineSm<D> sp[2];
+    __shared__ BeamPre pre[2];
     __shared__ __align__(16) float qs[DP];
     __shared__ int frs[2][WMAX * 2];
     __shared__ int cand_s[32];
@@ -488,6 +592,9 @@ __global__ void __launch_bounds__(256) fsb_decode_select_kernel(SelArgs A) {
     const float lam = a.lam[hd], sig = a.sigma[hd];
     const float qpos = (float)(*a.pos);
     if (tid < 32) { cand_s[tid] = -1; u_s[tid] = -INFINITY; }
+    __syncthreads();
+    // the query-independent head of each beam (a few dependent table reads) also runs before the dependency wait
+    if (warp < nsp) beam_prefix<D>(warp == 0 ? a.main : a.second, t, sp[warp], warp == 0 ? a.width : a.width2, lane, pre[warp]);
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const bf16* qp = (const bf16*)a.q.ptr + b * a.q.sb + hd * a.q.sh;
@@ -505,7 +612,7 @@ __global__ void __launch_bounds__(256) fsb_decode_select_kernel(SelArgs A) {
             qreg[i * 4 + 0] = w4.x; qreg[i * 4 + 1] = w4.y; qreg[i * 4 + 2] = w4.z; qreg[i * 4 + 3] = w4.w;
         }
         int nv = 0;
-        const int c = beam<D, true>(warp == 0 ? a.main : a.second, t, sp[warp], qreg, qn, qpos, lam, sig, a.scale,
+        const int c = beam<D, true>(warp == 0 ? a.main : a.second, t, sp[warp], pre[warp], qreg, qn, qpos, lam, sig, a.scale,
                                     warp == 0 ? a.width : a.width2, lane, frs[warp], nv);
         if (lane < WMAX) cand_s[warp * WMAX + lane] = (lane < (warp == 0 ? a.width : a.width2)) ? c : -1;
         if (lane == 0) nv_s[warp] = nv;
