@@ -172,6 +172,39 @@ def time_decode_kernel(gd, n=48):
     return sum(ms) / len(ms), ms[len(ms) // 2]
 
 
+def time_window_kernel(attn, dev, ctx: int, reps: int = 5):
+    """Prefill window attention alone (RoPE pre-pass + tcgen05 kernel) on random Q/K/V of the model's shape: useful
+    FLOPs 4*H*D*(sum_i min(i+1, W+1)) over its CUDA-event time, against the measured bf16 tensor peak. The operands
+    (3 x ctx*H*D*2 B = 805 MB at 131k) exceed L2, so no flush is needed between repetitions."""
+    from freesolo_b200 import ops
+    H, D, W = attn.n_heads, attn.head_dim, attn.window_size
+    n = min(ctx, 131072)
+    g = torch.Generator(device=dev).manual_seed(7)
+    Q, K, V = (torch.randn(1, n, 3 * H * D, device=dev, generator=g).to(torch.bfloat16).view(1, n, 3, H, D)[:, :, j].transpose(1, 2)
+               for j in range(3))
+    cos, sin = attn.rope.tables_bf16(n)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = torch.empty(1, n, H * D, dtype=torch.bfloat16, device=dev)
+    times = []
+    for i in range(reps + 2):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        ops.window_prefill(Q, K, V, cos, sin, W, attn.scale, out=out, status=status)
+        e1.record()
+        times.append((e0, e1))
+    torch.cuda.synchronize()
+    if int(status.item()) != 0:
+        raise RuntimeError("a bounded wait inside the window kernel ran out")
+    ms = sorted(a.elapsed_time(b) for a, b in times[2:])[reps // 2]
+    flops = 4.0 * H * D * ((W + 1) * n - W * (W + 1) / 2.0) if n > W else 4.0 * H * D * n * (n + 1) / 2.0
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peak, kind = (float(json.load(open(p))["bf16_tflops"]), "measured") if os.path.isfile(p) else (1590.0, "fallback")
+    return {"kernel": "rope_qk_kernel + window_tc_kernel", "bound": "tensor", "achieved": flops / (ms * 1e-3) / 1e12, "peak": peak,
+            "unit": "TFLOP/s", "frac": flops / (ms * 1e-3) / 1e12 / peak, "peak_kind": kind, "ms": ms, "tokens": n, "heads": H,
+            "how": "launched alone on random operands larger than L2, median of 5, CUDA events on the launching stream; "
+                   "useful FLOPs only (masked parts of the key tiles not counted)"}
+
+
 def timed_prefill(make_decoder, reps: int = 3):
     """The reference's prefill protocol (experiments/scaling/bench_efficiency.py:166-198, `--warm 1 --nmed 3`): one untimed
     prefill at the full context (the allocator's pools and every kernel attribute are warm afterwards), then the median of
@@ -363,6 +396,8 @@ def run_ours(args):
         "kv_bytes_per_layer": gd.kv_bytes() // nL, "kv_faults": list(faults),
         "peak_mem_gib": torch.cuda.max_memory_allocated() / 2 ** 30,
     }
+    if world == 1 and args.model == "340m":
+        line["window_roofline"] = time_window_kernel(gd.attn_core[0], dev, ctx)
     if world == 1 and not args.no_fsb:
         del gd, model
         torch.cuda.empty_cache()
