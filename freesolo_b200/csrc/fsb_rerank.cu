@@ -190,18 +190,26 @@ __global__ void __launch_bounds__(RB_THREADS, 1) fsb_rerank_block_kernel(RrArgs 
 #pragma unroll
                     for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
 #pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk) {
-                    uint32_t af[4];
-                    af[0] = *(const uint32_t*)(Qs + sw_off(qa, kk * 32 + tg * 4, SM::ROWB, SM::SW));
-                    af[1] = *(const uint32_t*)(Qs + sw_off(qb, kk * 32 + tg * 4, SM::ROWB, SM::SW));
-                    af[2] = *(const uint32_t*)(Qs + sw_off(qa, kk * 32 + 16 + tg * 4, SM::ROWB, SM::SW));
-                    af[3] = *(const uint32_t*)(Qs + sw_off(qb, kk * 32 + 16 + tg * 4, SM::ROWB, SM::SW));
+                for (int kp = 0; kp < D / 32; ++kp) {               // two k-steps per round: one ldmatrix.x4 per 8-token tile
+                    uint32_t af[2][4];
+#pragma unroll
+                    for (int h2 = 0; h2 < 2; ++h2) {
+                        const int kk = 2 * kp + h2;
+                        af[h2][0] = *(const uint32_t*)(Qs + sw_off(qa, kk * 32 + tg * 4, SM::ROWB, SM::SW));
+                        af[h2][1] = *(const uint32_t*)(Qs + sw_off(qb, kk * 32 + tg * 4, SM::ROWB, SM::SW));
+                        af[h2][2] = *(const uint32_t*)(Qs + sw_off(qa, kk * 32 + 16 + tg * 4, SM::ROWB, SM::SW));
+                        af[h2][3] = *(const uint32_t*)(Qs + sw_off(qb, kk * 32 + 16 + tg * 4, SM::ROWB, SM::SW));
+                    }
 #pragma unroll
                     for (int nt = 0; nt < 4; ++nt) {
-                        const int r = nt * 8 + g;
-                        const uint32_t b0 = *(const uint32_t*)(Kc + sw_off(r, kk * 32 + tg * 4, SM::ROWB, SM::SW));
-                        const uint32_t b1 = *(const uint32_t*)(Kc + sw_off(r, kk * 32 + 16 + tg * 4, SM::ROWB, SM::SW));
-                        mma_bf16(acc[nt], af, b0, b1);
+                        // matrix j of the load = 16-byte chunk kp*4 + j of the tile's eight key rows
+                        const uint32_t addr = (uint32_t)__cvta_generic_to_shared(
+                            Kc + sw_off(nt * 8 + (lane & 7), (kp * 4 + (lane >> 3)) * 16, SM::ROWB, SM::SW));
+                        uint32_t b0, b1, b2, b3;
+                        asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                                     : "=r"(b0), "=r"(b1), "=r"(b2), "=r"(b3) : "r"(addr));
+                        mma_bf16(acc[nt], af[0], b0, b1);
+                        mma_bf16(acc[nt], af[1], b2, b3);
                     }
                 }
                 // rows g (acc[.][0..1]) and g+8 (acc[.][2..3]): log-sum-exp over the 32 tokens, spread over the quad
@@ -218,7 +226,7 @@ __global__ void __launch_bounds__(RB_THREADS, 1) fsb_rerank_block_kernel(RrArgs 
                     m = fmaxf(m, __shfl_xor_sync(FS_FULL, m, 2));
                     float s = 0.f;
 #pragma unroll
-                    for (int nt = 0; nt < 4; ++nt) s += expf(acc[nt][2 * half] - m) + expf(acc[nt][2 * half + 1] - m);
+                    for (int nt = 0; nt < 4; ++nt) s += __expf(acc[nt][2 * half] - m) + __expf(acc[nt][2 * half + 1] - m);
                     s += __shfl_xor_sync(FS_FULL, s, 1);
                     s += __shfl_xor_sync(FS_FULL, s, 2);
                     const int id = half ? idb : ida;
