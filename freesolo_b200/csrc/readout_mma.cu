@@ -199,7 +199,7 @@ __global__ void __launch_bounds__(RM_THREADS, 2) readout_mma_kernel(const fsattn
         for (int it = 0; it < CH; it++) {
             const int row = it * 4 + st_r;
             const int nbytes = row < lim ? 16 : 0;
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d + it * 4 * RM_ROWB + ((it & 1) ? st_d1 : st_d0)),
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 16, %2;" ::"r"(d + it * 4 * RM_ROWB + ((it & 1) ? st_d1 : st_d0)),
                          "l"(row < lim ? src + (int64_t)it * 4 * sn : base), "r"(nbytes));
         }
     };
