@@ -381,14 +381,20 @@ __device__ __forceinline__ float rerank_cell(const fsattn_fsb_select_t& a, int b
             p[v * 8 + 6] = f_mul(bf_lo(w.w), qb.z); p[v * 8 + 7] = f_mul(bf_hi(w.w), qb.w);
         }
     } else {
-        const uint32_t* kr = (const uint32_t*)(a.kq + b * a.kq_sb + hd * a.kq_sh + tok * D);
+        const uint4* kr = (const uint4*)(a.kq + b * a.kq_sb + hd * a.kq_sh + tok * D);      // the row's codes, 16 bytes per load
         const float sc = __bfloat162float(((const bf16*)a.ks)[b * a.ks_sb + hd * a.ks_sh + cell]);
 #pragma unroll
-        for (int v = 0; v < D / 4; ++v) {
-            float o[4];
-            unpack4_i8(kr[v], o);
+        for (int v4 = 0; v4 < D / 16; ++v4) {
+            const uint4 w4 = kr[v4];
+            const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-            for (int e = 0; e < 4; ++e) p[v * 4 + e] = f_mul(bf_round(f_mul(o[e], sc)), qs[v * 4 + e]);
+            for (int j = 0; j < 4; ++j) {
+                const int v = v4 * 4 + j;
+                float o[4];
+                unpack4_i8(ws[j], o);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) p[v * 4 + e] = f_mul(bf_round(f_mul(o[e], sc)), qs[v * 4 + e]);
+            }
         }
     }
 #pragma unroll
@@ -632,6 +638,15 @@ __global__ void __launch_bounds__(256) fsb_decode_select_kernel(SelArgs A) {
         if (tid < a.width) a.cand[(int64_t)t * Wc + tid] = cand_s[tid];
         if (tid >= WMAX && tid - WMAX < a.width2) a.cand[(int64_t)t * Wc + a.width + tid - WMAX] = cand_s[tid];
     }
+    // every candidate's token keys are asked for now, so that a warp's second to fourth cell wait in L2, not in HBM
+    for (int i = warp; i < 32; i += NW) {
+        const int cell = cand_s[i];
+        if (cell < 0) continue;
+        const char* rows = a.k.ptr ? (const char*)((const bf16*)a.k.ptr + b * a.k.sb + hd * a.k.sh + (int64_t)cell * 32 * a.k.sn)
+                                   : (const char*)(a.kq + b * a.kq_sb + hd * a.kq_sh + (int64_t)cell * 32 * D);
+        const int nbytes = a.k.ptr ? (int)(32 * a.k.sn * 2) : 32 * D;
+        for (int o = lane * 128; o < nbytes; o += 32 * 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(rows + o));
+    }
     for (int i = warp; i < 32; i += NW) {
         const int cell = cand_s[i];
         if (cell < 0) continue;
@@ -703,6 +718,8 @@ extern "C" int fsattn_fsb_select(const fsattn_fsb_select_t* a, fsattn_stream_t s
     FS_REQUIRE(a->B > 0 && a->main.T % a->B == 0, "fsb_select: B = %d does not divide T = %d", a->B, a->main.T);
     FS_REQUIRE(a->q.ptr && a->sel && a->lam && a->sigma, "fsb_select: null q / sel / lam / sigma");
     FS_REQUIRE(a->k.ptr || (a->kq && a->ks), "fsb_select: token keys missing (bf16 k, or int8 kq + scales ks)");
+    FS_REQUIRE(a->k.ptr || (((uintptr_t)a->kq & 15) == 0 && a->kq_sb % 16 == 0 && a->kq_sh % 16 == 0),
+               "fsb_select: int8 key rows must be 16-byte aligned");
     FS_UNSUPPORTED(a->width < 1 || a->width > WMAX || a->width2 < 0 || a->width2 > WMAX,
                    "fsb_select: beam widths %d / %d (1..16 and 0..16)", a->width, a->width2);
     FS_REQUIRE(a->read_top >= 1 && a->read_top <= 32, "fsb_select: read_top = %d", a->read_top);
