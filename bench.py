@@ -24,7 +24,7 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-PUBLISHED_FSL_DECODE_TPS_131K = 515.1      # A100-40GB, README.md:62 of the reference (BASELINE.md section 1)
+PUBLISHED_FSL_DECODE_TPS_131K = 515.1      # A100-40GB, README.md:62 of the reference
 NCU_DECODE_KERNEL_DRAM_BYTES = 1.87e6       # profiles/fsl_decode_kernel_340m_ncu_full.md
 PUBLISHED_FSB_DECODE_TPS_131K = 462.7      # A100-40GB, README.md:63 of the reference
 PUBLISHED_FSB_PREFILL_KTOKS_131K = 137.8   # A100-40GB, README.md:63 of the reference
@@ -84,7 +84,7 @@ class ClockSampler:
 
 
 def attn_bytes_per_layer(B, H, D, W, P, Wc, kk, s, int8=True):
-    """Algorithmic bytes one decode-step launch of one layer moves (per SURVEY formulas: window rows of K and V, the pool's
+    """Algorithmic bytes one decode-step launch of one layer moves (window rows of K and V, the pool's
     mean keys + per-slot scalars, the kk cells read, the new row)."""
     e = 1 if int8 else 2
     win = (W + 1) * D * 2 * e

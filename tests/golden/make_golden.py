@@ -330,7 +330,8 @@ def gen_fsb(kind: str, B=1, H=2, D=64, N=2000, T=140, seed=23, q_main=0.3, q_uni
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("FREESOLO_REFERENCE", "/root/reference"),
+                    help="checkout of the reference project (zekun-shi/freesolo)")
     ap.add_argument("--only", default="")
     args = ap.parse_args()
     sys.path[:0] = [os.path.join(args.reference, "experiments", "scaling"), args.reference]
