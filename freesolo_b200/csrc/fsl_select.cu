@@ -270,12 +270,13 @@ __global__ void __launch_bounds__(128) fsl_select_kernel(const fsattn_fsl_select
 // Then each thread is one query again and walks its row of scores in slot order: prior, sorted insert - the scalar kernel's
 // epilogue, so ties resolve identically (lower slot first).
 constexpr int SM_MAXC = 80;                // candidate slots rounded up to whole 8-column tiles
-constexpr int SM_SCLD = SM_MAXC + 1;       // score row pitch in floats (odd: conflict-free column walks)
+constexpr int SM_NTH = SM_MAXC / 16;       // the candidates are scored in two halves of at most 5 tiles: the score array of a
+constexpr int SM_SCLD = SM_NTH * 8 + 1;    // half (row pitch in floats, odd: conflict-free column walks) lets 4 CTAs share an SM
 
 struct SelMmaSmem {
     static constexpr size_t KB_OFF = 0;                                        // [80][64] bf16, 16-byte chunks XOR-swizzled by row
     static constexpr size_t Q_OFF = KB_OFF + (size_t)SM_MAXC * 128;            // [128][64] bf16, swizzled
-    static constexpr size_t SC_OFF = Q_OFF + (size_t)128 * 128;                // [128][81] fp32 dot products
+    static constexpr size_t SC_OFF = Q_OFF + (size_t)128 * 128;                // [128][41] fp32 dot products of one half of the candidates
     static constexpr size_t META_OFF = SC_OFF + (size_t)128 * SM_SCLD * 4;     // ceil, cell, ok per slot
     static constexpr size_t TOTAL = META_OFF + (size_t)SM_MAXC * 16;           // lam*ceil, cell, ok, centre per slot
 };
@@ -363,38 +364,7 @@ __global__ void __launch_bounds__(128) fsl_select_mma_kernel(const fsattn_fsl_se
 #pragma unroll
     for (int kp = 0; kp < 2; kp++) k_ld[kp] = (uint32_t)__cvta_generic_to_shared(kb + sel_sw(lane & 7, kp * 4 + (lane >> 3)));
     float* scw = sc + (size_t)warp * 32 * SM_SCLD;
-    for (int nt = 0; nt < NT; nt++) {
-        float c[2][4];
-#pragma unroll
-        for (int mt = 0; mt < 2; mt++) c[mt][0] = c[mt][1] = c[mt][2] = c[mt][3] = 0.f;
-#pragma unroll
-        for (int kp = 0; kp < 2; kp++) {
-            uint32_t b0, b1, b2, b3;
-            asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                         : "=r"(b0), "=r"(b1), "=r"(b2), "=r"(b3) : "r"(k_ld[kp] + nt * 8 * 128));
-#pragma unroll
-            for (int mt = 0; mt < 2; mt++) {
-                asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-                             : "+f"(c[mt][0]), "+f"(c[mt][1]), "+f"(c[mt][2]), "+f"(c[mt][3])
-                             : "r"(qf[mt][2 * kp][0]), "r"(qf[mt][2 * kp][1]), "r"(qf[mt][2 * kp][2]), "r"(qf[mt][2 * kp][3]), "r"(b0), "r"(b1));
-                asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-                             : "+f"(c[mt][0]), "+f"(c[mt][1]), "+f"(c[mt][2]), "+f"(c[mt][3])
-                             : "r"(qf[mt][2 * kp + 1][0]), "r"(qf[mt][2 * kp + 1][1]), "r"(qf[mt][2 * kp + 1][2]), "r"(qf[mt][2 * kp + 1][3]), "r"(b2), "r"(b3));
-            }
-        }
-#pragma unroll
-        for (int mt = 0; mt < 2; mt++) {
-            const int col = nt * 8 + tg * 2;
-            scw[(mt * 16 + g) * SM_SCLD + col] = c[mt][0];
-            scw[(mt * 16 + g) * SM_SCLD + col + 1] = c[mt][1];
-            scw[(mt * 16 + g + 8) * SM_SCLD + col] = c[mt][2];
-            scw[(mt * 16 + g + 8) * SM_SCLD + col + 1] = c[mt][3];
-        }
-    }
-    __syncwarp();
-    if (tid >= a.Bq) return;
-
-    // ---- one query per thread: prior, sorted insert (slots in ascending order) ----
+    // ---- one query per thread for the walk over the scores: prior, sorted insert (slots in ascending order) ----
     const int qi = blk_start + tid;
     const float inv_two_sigma = f_div(1.0f, f_mul(2.0f, a.sigma[h]));
     const float qpos = (float)qi;
@@ -403,10 +373,44 @@ __global__ void __launch_bounds__(128) fsl_select_mma_kernel(const fsattn_fsl_se
     int tslot[KMAX];
 #pragma unroll
     for (int j = 0; j < KMAX; j++) { ts[j] = -INFINITY; tslot[j] = -1; }
-    for (int t = 0; t < C; t++) {
-        float score = FS_NEG_SCORE;
-        if (cok[t]) score = f_add(f_mul(myrow[t], a.scale), sel_prior(cceil[t], ccen[t], qpos, inv_two_sigma));
-        sel_insert<KMAX>(ts, tslot, score, t);
+    for (int nt0 = 0; nt0 < NT; nt0 += SM_NTH) {
+        const int nt1 = min(NT, nt0 + SM_NTH);
+        for (int nt = nt0; nt < nt1; nt++) {
+            float c[2][4];
+#pragma unroll
+            for (int mt = 0; mt < 2; mt++) c[mt][0] = c[mt][1] = c[mt][2] = c[mt][3] = 0.f;
+#pragma unroll
+            for (int kp = 0; kp < 2; kp++) {
+                uint32_t b0, b1, b2, b3;
+                asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                             : "=r"(b0), "=r"(b1), "=r"(b2), "=r"(b3) : "r"(k_ld[kp] + nt * 8 * 128));
+#pragma unroll
+                for (int mt = 0; mt < 2; mt++) {
+                    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                                 : "+f"(c[mt][0]), "+f"(c[mt][1]), "+f"(c[mt][2]), "+f"(c[mt][3])
+                                 : "r"(qf[mt][2 * kp][0]), "r"(qf[mt][2 * kp][1]), "r"(qf[mt][2 * kp][2]), "r"(qf[mt][2 * kp][3]), "r"(b0), "r"(b1));
+                    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                                 : "+f"(c[mt][0]), "+f"(c[mt][1]), "+f"(c[mt][2]), "+f"(c[mt][3])
+                                 : "r"(qf[mt][2 * kp + 1][0]), "r"(qf[mt][2 * kp + 1][1]), "r"(qf[mt][2 * kp + 1][2]), "r"(qf[mt][2 * kp + 1][3]), "r"(b2), "r"(b3));
+                }
+            }
+#pragma unroll
+            for (int mt = 0; mt < 2; mt++) {
+                const int col = (nt - nt0) * 8 + tg * 2;
+                scw[(mt * 16 + g) * SM_SCLD + col] = c[mt][0];
+                scw[(mt * 16 + g) * SM_SCLD + col + 1] = c[mt][1];
+                scw[(mt * 16 + g + 8) * SM_SCLD + col] = c[mt][2];
+                scw[(mt * 16 + g + 8) * SM_SCLD + col + 1] = c[mt][3];
+            }
+        }
+        __syncwarp();
+        const int t1 = min(C, nt1 * 8);
+        for (int t = nt0 * 8; t < t1; t++) {
+            float score = FS_NEG_SCORE;
+            if (cok[t]) score = f_add(f_mul(myrow[t - nt0 * 8], a.scale), sel_prior(cceil[t], ccen[t], qpos, inv_two_sigma));
+            sel_insert<KMAX>(ts, tslot, score, t);
+        }
+        __syncwarp();                   // the warp's rows are rewritten by the next half
     }
     int32_t* so = a.sel + ((int64_t)bh * a.nb * a.Bq + qi) * a.kk;
 #pragma unroll
