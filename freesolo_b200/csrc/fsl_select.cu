@@ -276,7 +276,8 @@ constexpr int SM_SCLD = SM_NTH * 8 + 1;    // half (row pitch in floats, odd: co
 struct SelMmaSmem {
     static constexpr size_t KB_OFF = 0;                                        // [80][64] bf16, 16-byte chunks XOR-swizzled by row
     static constexpr size_t Q_OFF = KB_OFF + (size_t)SM_MAXC * 128;            // [128][64] bf16, swizzled
-    static constexpr size_t SC_OFF = Q_OFF + (size_t)128 * 128;                // [128][41] fp32 dot products of one half of the candidates
+    static constexpr size_t SC_OFF = Q_OFF;     // [128][41] fp32 dot products of one half of the candidates: over the Q tile, which
+                                                // is dead once every warp holds its A fragments
     static constexpr size_t META_OFF = SC_OFF + (size_t)128 * SM_SCLD * 4;     // ceil, cell, ok per slot
     static constexpr size_t TOTAL = META_OFF + (size_t)SM_MAXC * 16;           // lam*ceil, cell, ok, centre per slot
 };
@@ -359,6 +360,7 @@ __global__ void __launch_bounds__(128) fsl_select_mma_kernel(const fsattn_fsl_se
             asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                          : "=r"(qf[mt][kk][0]), "=r"(qf[mt][kk][1]), "=r"(qf[mt][kk][2]), "=r"(qf[mt][kk][3]) : "r"(addr));
         }
+    __syncthreads();                            // the score array reuses the Q tile from here on
     const int g = lane >> 2, tg = lane & 3;
     uint32_t k_ld[2];
 #pragma unroll
