@@ -95,7 +95,7 @@ __device__ void build_spine(const fsattn_fsb_forest_t& F, int t, int m_b, SpineS
 template <int D>
 __host__ __device__ constexpr int STG_SW() { return D == 96 ? 3 : 7; }      // 16-byte-chunk XOR mask of a staged row
 template <int D>
-__host__ __device__ constexpr int STG_DS() { return D <= 64 ? 8 : 7; }      // deepest staged tree level
+__host__ __device__ constexpr int STG_DS() { return 7; }                    // deepest staged tree level
 template <int D>
 __host__ __device__ constexpr int STG_ROWS() { return (2 << STG_DS<D>()); }
 
@@ -203,7 +203,7 @@ __device__ void beam_prefix(const fsattn_fsb_forest_t& F, int t, const SpineSm<D
 template <int D, bool PREFETCH = false, bool STAGED = false>
 __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, const BeamPre& P, const uint32_t (&qp)[D / 2], float qn,
                     float qpos, float lam, float sig, float scale, int width, int lane, int* fr, int& nvis,
-                    const unsigned char* stg_mu = nullptr, const float4* stg_aux = nullptr) {
+                    const unsigned char* stg_mu = nullptr, const float4* stg_aux = nullptr, const float* qf = nullptr) {
     constexpr int DP = FsbDim<D>::DP;
     const int m_cap = F.m_cap;
     const int64_t nrow = (int64_t)t * fsb_nodes_per_row(m_cap);
@@ -237,21 +237,42 @@ __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, co
                 for (int v = 0; v < D / 8; ++v) w[v] = mr[v];
                 ax = aux[REF_ID(cref)];
             }
-            // the query sits in registers as bf16 pairs (it is a bf16 tensor): no shared-memory traffic for it
+            if constexpr (STAGED) {
+                // prefill: the query as fp32 from shared memory (two broadcast 16-byte reads per eight dims), which keeps 32
+                // registers free and lets a third CTA share the SM; same products, same four running sums
 #pragma unroll
-            for (int v = 0; v < D / 8; ++v) {
-                s0 = fmaf(bf_lo(qp[v * 4 + 0]), bf_lo(w[v].x), s0); s1 = fmaf(bf_hi(qp[v * 4 + 0]), bf_hi(w[v].x), s1);
-                s2 = fmaf(bf_lo(qp[v * 4 + 1]), bf_lo(w[v].y), s2); s3 = fmaf(bf_hi(qp[v * 4 + 1]), bf_hi(w[v].y), s3);
-                s0 = fmaf(bf_lo(qp[v * 4 + 2]), bf_lo(w[v].z), s0); s1 = fmaf(bf_hi(qp[v * 4 + 2]), bf_hi(w[v].z), s1);
-                s2 = fmaf(bf_lo(qp[v * 4 + 3]), bf_lo(w[v].w), s2); s3 = fmaf(bf_hi(qp[v * 4 + 3]), bf_hi(w[v].w), s3);
+                for (int v = 0; v < D / 8; ++v) {
+                    const float4 qa = reinterpret_cast<const float4*>(qf)[2 * v], qb = reinterpret_cast<const float4*>(qf)[2 * v + 1];
+                    s0 = fmaf(qa.x, bf_lo(w[v].x), s0); s1 = fmaf(qa.y, bf_hi(w[v].x), s1);
+                    s2 = fmaf(qa.z, bf_lo(w[v].y), s2); s3 = fmaf(qa.w, bf_hi(w[v].y), s3);
+                    s0 = fmaf(qb.x, bf_lo(w[v].z), s0); s1 = fmaf(qb.y, bf_hi(w[v].z), s1);
+                    s2 = fmaf(qb.z, bf_lo(w[v].w), s2); s3 = fmaf(qb.w, bf_hi(w[v].w), s3);
+                }
+            } else {
+                // decode (latency-bound): the query sits in registers as bf16 pairs, no shared-memory traffic for it
+#pragma unroll
+                for (int v = 0; v < D / 8; ++v) {
+                    s0 = fmaf(bf_lo(qp[v * 4 + 0]), bf_lo(w[v].x), s0); s1 = fmaf(bf_hi(qp[v * 4 + 0]), bf_hi(w[v].x), s1);
+                    s2 = fmaf(bf_lo(qp[v * 4 + 1]), bf_lo(w[v].y), s2); s3 = fmaf(bf_hi(qp[v * 4 + 1]), bf_hi(w[v].y), s3);
+                    s0 = fmaf(bf_lo(qp[v * 4 + 2]), bf_lo(w[v].z), s0); s1 = fmaf(bf_hi(qp[v * 4 + 2]), bf_hi(w[v].z), s1);
+                    s2 = fmaf(bf_lo(qp[v * 4 + 3]), bf_lo(w[v].w), s2); s3 = fmaf(bf_hi(qp[v * 4 + 3]), bf_hi(w[v].w), s3);
+                }
             }
             rad = ax.x; am = ax.y; pm = __float_as_int(ax.z); cmeta = __float_as_int(ax.w);
         } else {
             const float* x = S.node[-cref - 2];
+            if constexpr (STAGED) {
 #pragma unroll
-            for (int d = 0; d < D; d += 4) {
-                s0 = fmaf(bf_lo(qp[d / 2]), x[d], s0); s1 = fmaf(bf_hi(qp[d / 2]), x[d + 1], s1);
-                s2 = fmaf(bf_lo(qp[d / 2 + 1]), x[d + 2], s2); s3 = fmaf(bf_hi(qp[d / 2 + 1]), x[d + 3], s3);
+                for (int d = 0; d < D; d += 4) {
+                    s0 = fmaf(qf[d], x[d], s0); s1 = fmaf(qf[d + 1], x[d + 1], s1);
+                    s2 = fmaf(qf[d + 2], x[d + 2], s2); s3 = fmaf(qf[d + 3], x[d + 3], s3);
+                }
+            } else {
+#pragma unroll
+                for (int d = 0; d < D; d += 4) {
+                    s0 = fmaf(bf_lo(qp[d / 2]), x[d], s0); s1 = fmaf(bf_hi(qp[d / 2]), x[d + 1], s1);
+                    s2 = fmaf(bf_lo(qp[d / 2 + 1]), x[d + 2], s2); s3 = fmaf(bf_hi(qp[d / 2 + 1]), x[d + 3], s3);
+                }
             }
             rad = x[D]; am = x[D + 1]; pm = __float_as_int(x[D + 2]);
             cmeta = 0;
@@ -433,7 +454,7 @@ struct SelSmem {
 };
 
 template <int D, int NWARP>
-__global__ void __launch_bounds__(NWARP * 32, (NWARP >= 16) ? 2 : 2) fsb_select_kernel(SelArgs A) {
+__global__ void __launch_bounds__(NWARP * 32, (D == 64) ? 3 : 2) fsb_select_kernel(SelArgs A) {
     constexpr int DP = FsbDim<D>::DP;
     constexpr int CH = D / 8;
     const fsattn_fsb_select_t& a = A.a;
@@ -508,7 +529,7 @@ __global__ void __launch_bounds__(NWARP * 32, (NWARP >= 16) ? 2 : 2) fsb_select_
             }
             int nv = 0;
             const int c = beam<D, false, true>(F, t, sp, pre, qreg, qn, qpos, lam, sig, a.scale, width, lane, frs[warp], nv,
-                                               stg_mu, stg_aux);
+                                               stg_mu, stg_aux, qs);
             if (lane < width) cand_sm[qi][f * WMAX + lane] = c;
             if (lane == 0) nv_sm[qi] += nv;
         }
