@@ -384,17 +384,40 @@ __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, co
 }
 
 // ---- re-rank score of one candidate cell (one warp, lane = token of the cell) -----------------------------------------
+// The token keys of one candidate cell as a lane holds them (lane = token), fetched apart from the arithmetic so that a warp
+// with several cells to score can have all their rows in flight at once.
 template <int D>
-__device__ __forceinline__ float rerank_cell(const fsattn_fsb_select_t& a, int b, int hd, int t, int cell, const float* qs,
-                                             float qpos, float lam, float sig, int lane) {
-    constexpr int DP = FsbDim<D>::DP;
-    float p[DP];
+struct RrRow {
+    uint4 w[D / 8];          // bf16 store: the row; int8 store: its codes in w[0 .. D/16)
+    float sc, ceil_c;
+};
+
+template <int D>
+__device__ __forceinline__ void rr_load(RrRow<D>& r, const fsattn_fsb_select_t& a, int b, int hd, int t, int cell, int lane) {
     const int64_t tok = (int64_t)cell * 32 + lane;
     if (a.k.ptr) {
         const uint4* kr = (const uint4*)((const bf16*)a.k.ptr + b * a.k.sb + hd * a.k.sh + tok * a.k.sn);
 #pragma unroll
+        for (int v = 0; v < D / 8; ++v) r.w[v] = kr[v];
+        r.sc = 1.0f;
+    } else {
+        const uint4* kr = (const uint4*)(a.kq + b * a.kq_sb + hd * a.kq_sh + tok * D);      // the row's codes, 16 bytes per load
+#pragma unroll
+        for (int v4 = 0; v4 < D / 16; ++v4) r.w[v4] = kr[v4];
+        r.sc = __bfloat162float(((const bf16*)a.ks)[b * a.ks_sb + hd * a.ks_sh + cell]);
+    }
+    r.ceil_c = a.main.ceil[(int64_t)t * a.main.ceil_st + cell];
+}
+
+template <int D>
+__device__ __forceinline__ float rr_score(const RrRow<D>& r, const fsattn_fsb_select_t& a, int cell, const float* qs, float qpos,
+                                          float lam, float sig) {
+    constexpr int DP = FsbDim<D>::DP;
+    float p[DP];
+    if (a.k.ptr) {
+#pragma unroll
         for (int v = 0; v < D / 8; ++v) {
-            const uint4 w = kr[v];
+            const uint4 w = r.w[v];
             const float4 qa = *(const float4*)(qs + v * 8), qb = *(const float4*)(qs + v * 8 + 4);
             p[v * 8 + 0] = f_mul(bf_lo(w.x), qa.x); p[v * 8 + 1] = f_mul(bf_hi(w.x), qa.y);
             p[v * 8 + 2] = f_mul(bf_lo(w.y), qa.z); p[v * 8 + 3] = f_mul(bf_hi(w.y), qa.w);
@@ -402,11 +425,10 @@ __device__ __forceinline__ float rerank_cell(const fsattn_fsb_select_t& a, int b
             p[v * 8 + 6] = f_mul(bf_lo(w.w), qb.z); p[v * 8 + 7] = f_mul(bf_hi(w.w), qb.w);
         }
     } else {
-        const uint4* kr = (const uint4*)(a.kq + b * a.kq_sb + hd * a.kq_sh + tok * D);      // the row's codes, 16 bytes per load
-        const float sc = __bfloat162float(((const bf16*)a.ks)[b * a.ks_sb + hd * a.ks_sh + cell]);
+        const float sc = r.sc;
 #pragma unroll
         for (int v4 = 0; v4 < D / 16; ++v4) {
-            const uint4 w4 = kr[v4];
+            const uint4 w4 = r.w[v4];
             const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -428,8 +450,15 @@ __device__ __forceinline__ float rerank_cell(const fsattn_fsb_select_t& a, int b
     const float lse = f_add(m, logf(e));
     const float cpos = f_mul(f_add((float)cell, 0.5f), 32.0f);
     const float er = erff(f_div(fabsf(f_add(qpos, -cpos)), f_mul(2.0f, sig)));
-    const float ceil_c = a.main.ceil[(int64_t)t * a.main.ceil_st + cell];
-    return f_add(lse, f_mul(f_mul(lam, ceil_c), er));
+    return f_add(lse, f_mul(f_mul(lam, r.ceil_c), er));
+}
+
+template <int D>
+__device__ __forceinline__ float rerank_cell(const fsattn_fsb_select_t& a, int b, int hd, int t, int cell, const float* qs,
+                                             float qpos, float lam, float sig, int lane) {
+    RrRow<D> r;
+    rr_load<D>(r, a, b, hd, t, cell, lane);
+    return rr_score<D>(r, a, cell, qs, qpos, lam, sig);
 }
 
 struct SelArgs {
@@ -668,11 +697,24 @@ __global__ void __launch_bounds__(256) fsb_decode_select_kernel(SelArgs A) {
         const int nbytes = a.k.ptr ? (int)(32 * a.k.sn * 2) : 32 * D;
         for (int o = lane * 128; o < nbytes; o += 32 * 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(rows + o));
     }
-    for (int i = warp; i < 32; i += NW) {
-        const int cell = cand_s[i];
-        if (cell < 0) continue;
-        const float ui = rerank_cell<D>(a, b, hd, t, cell, qs, qpos, lam, sig, lane);
-        if (lane == 0) u_s[i] = ui;
+    {   // a warp's cells in groups: all rows of a group are requested before the first is scored
+        constexpr int RG = (D <= 64) ? 4 : 1;     // wider heads keep one row at a time: two already spill
+        for (int i0 = warp; i0 < 32; i0 += NW * RG) {
+            RrRow<D> rows[RG];
+            int cells[RG];
+#pragma unroll
+            for (int j = 0; j < RG; ++j) {
+                const int i = i0 + j * NW;
+                cells[j] = (i < 32) ? cand_s[i] : -1;
+                if (cells[j] >= 0) rr_load<D>(rows[j], a, b, hd, t, cells[j], lane);
+            }
+#pragma unroll
+            for (int j = 0; j < RG; ++j) {
+                if (cells[j] < 0) continue;
+                const float ui = rr_score<D>(rows[j], a, cells[j], qs, qpos, lam, sig);
+                if (lane == 0) u_s[i0 + j * NW] = ui;
+            }
+        }
     }
     __syncthreads();
     if (warp == 0) {
