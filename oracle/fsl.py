@@ -160,6 +160,39 @@ def fsl_select_prefill(Q, kbar, ceil, lam, sigma, scale: float, s: int, Bq: int,
     return sel_full, margin
 
 
+def fs_dense_select_prefill(Q, kbar, ceil, lam, sigma, scale: float, s: int, Bq: int, kk: int, N: int):
+    """Selected cells of every prefill query of the dense FS variant (cell_prune_kernel = 0, strict causal): every
+    completed cell that ends at or before the query's block start is a candidate, no pool; src/fsattn/attention.py:
+    362-423 with _cell_select_blk_logits(per_query=True, topk_k=kk) (472-517) and _cell_sel_cells (339-342). The
+    reference takes torch.topk over the logits, whose order among equal scores is unspecified: here (score desc, cell asc).
+    Returns sel_full (B,H,nb*Bq,kk_eff) int32 (-1 = nothing) and the per-query fp32 margin (B,H,nb*Bq)."""
+    B, H, _, D = Q.shape
+    M = (N + s - 1) // s
+    kk = min(kk, M)
+    Bq = min(Bq, N)
+    nb = (N + Bq - 1) // Bq
+    if kbar.shape[2] < M:
+        pad = M - kbar.shape[2]
+        kbar = torch.cat([kbar, kbar.new_zeros(B, H, pad, D)], dim=2)
+        ceil = torch.cat([ceil, ceil.new_zeros(B, H, pad)], dim=2)
+    kbar, ceil = kbar[:, :, :M], ceil[:, :, :M]
+    cells = torch.arange(M, dtype=torch.int64).expand(B, H, M)
+    sel_full = torch.full((B, H, nb * Bq, kk), -1, dtype=torch.int32)
+    margin = torch.full((B, H, nb * Bq), float("inf"))
+    for n in range(nb):
+        blk_start = n * Bq
+        ok = ((cells + 1) * s <= blk_start)
+        q = Q.new_zeros(B, H, Bq, D)
+        n_real = max(0, min(blk_start + Bq, N) - blk_start)
+        q[:, :, :n_real] = Q[:, :, blk_start:blk_start + n_real]
+        qpos = blk_start + torch.arange(Bq, dtype=torch.float32)
+        score = fsl_scores(q, kbar, ceil, cells, ok, qpos, lam, sigma, scale, s)
+        sel, mg = _pick(score, cells, ok, kk)
+        sel_full[:, :, blk_start:blk_start + Bq] = sel
+        margin[:, :, blk_start:blk_start + Bq] = mg
+    return sel_full, margin
+
+
 def fsl_decode_pool(kbar, ceil, blk_start: int, s: int, P: int, Wc: int):
     """Candidate pool of the decode block starting at blk_start; src/fsattn/attention.py:1313-1360 with the
     (ceiling desc, index asc) tie rule. kbar (B,H,ncell,D), ceil (B,H,ncell). Returns None when nothing is visible."""

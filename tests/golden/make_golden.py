@@ -169,6 +169,55 @@ def gen_fsl(kind: str, B=1, H=2, D=64, N=1000, T=72, seed=7):
     print("wrote", f"fsl_{kind}.npz")
 
 
+def gen_fs_dense(kind: str, B=1, H=2, D=64, N=1000, seed=31):
+    """The dense FS variant (serve preset "dense": cell_prune_kernel = 0, every completed visible cell is a candidate) at the
+    Q/K/V level: prefill selections and the layer output of an N-token prefill."""
+    from kv_cache import FSKVCache
+    from src.fsattn import FSAttn
+    from bench_efficiency import serve_kwargs
+    Q, K, V = make_inputs(kind, B, H, N, D, seed)
+    flat = [t.transpose(1, 2).reshape(B, N, H * D).contiguous() for t in (Q, K, V)]
+    out = {"kind": kind, "B": B, "H": H, "D": D, "N": N, "Q": _bf16_bits(Q), "K": _bf16_bits(K), "V": _bf16_bits(V)}
+    x = torch.zeros(B, N, H * D)
+    os.environ["FS_PRUNE_KERNEL"] = "0"
+    try:
+        def run(fused):
+            kw = serve_kwargs("dense")
+            kw.update(fs_fused_attn=1 if fused else 0)
+            a = FSAttn(d_model=H * D, n_heads=H, causal=True, bias=False, max_seq_len=4096, **kw).eval()
+            g = torch.Generator().manual_seed(seed + 1)
+            with torch.no_grad():
+                a.sel_scale.copy_(0.5 + torch.rand(H, generator=g) * 2)
+                a.log_sigma.copy_(torch.log(1.0 + torch.rand(H, generator=g) * 40))
+                a.long_range_scale.copy_((0.05 + torch.rand(H, generator=g)).view(H, 1, 1))
+                a.lr_norm.scale.copy_(0.5 + torch.rand(D, generator=g))
+                a.W_o.weight.copy_(torch.eye(H * D))
+            a.W_q, a.W_k, a.W_v = _Fixed(flat[0]), _Fixed(flat[1]), _Fixed(flat[2])
+            sels = []
+            if fused:
+                def grab(Qx, Kx, Vx, sel, s, Bq, bias=None, q_pos=0):
+                    sels.append(sel.clone())
+                    return torch.zeros_like(Qx)
+                a._cell_fused_lr = grab
+            c = FSKVCache(a)
+            with torch.no_grad():
+                y = a(x, cache=c)
+            return a, y, sels
+        a, y, _ = run(False)
+        out["lam"] = a.sel_scale.detach().numpy()
+        out["sigma"] = a.sigma.detach().numpy()
+        out["lrs"] = a.long_range_scale.detach().reshape(H).numpy()
+        out["norm_w"] = a.lr_norm.scale.detach().numpy()
+        out["eps"] = np.float32(a.lr_norm.eps)
+        out["y_prefill"] = y.numpy()
+        _, _, sels = run(True)
+        out["sel_prefill"] = sels[0][:, :, :N].numpy().astype(np.int32)
+    finally:
+        os.environ["FS_PRUNE_KERNEL"] = "1"
+    np.savez_compressed(os.path.join(HERE, f"fsdense_{kind}.npz"), **out)
+    print("wrote", f"fsdense_{kind}.npz", {k_: v_.shape for k_, v_ in out.items() if hasattr(v_, "shape") and v_.ndim})
+
+
 def gen_config1():
     """single random-init FS-L layer, d_model 1024, 16 heads x 64, fp32 on CPU, 4096-token
     prefix then one decode step."""
@@ -346,6 +395,8 @@ def main():
         "fsl_config1": gen_config1,
         "fsb_randn": lambda: gen_fsb("randn"),
         "fsb_vocab": lambda: gen_fsb("vocab", N=1500, T=40, seed=29),
+        "fsdense_randn": lambda: gen_fs_dense("randn"),
+        "fsdense_vocab": lambda: gen_fs_dense("vocab", N=900, seed=37),
     }
     for name, fn in jobs.items():
         if not only or name in only:
