@@ -193,6 +193,25 @@ def fs_dense_select_prefill(Q, kbar, ceil, lam, sigma, scale: float, s: int, Bq:
     return sel_full, margin
 
 
+def fs_dense_decode_select(q, kbar, ceil, pos: int, lam, sigma, scale: float, s: int, Bq: int, kk: int):
+    """Selected cells of one decode query of the dense FS variant at position pos: all cells completed before the
+    query's block start are scored; src/fsattn/attention.py:1159-1185 (_lr_decode_step_dense; torch.topk there, (score
+    desc, cell asc) here). q (B,H,1,D), kbar (B,H,ncell,D), ceil (B,H,ncell). Returns (sel (B,H,1,kk) int32, -1 padded when
+    fewer than kk cells are visible; margin (B,H,1))."""
+    B, H, _, D = q.shape
+    blk_start = (pos // Bq) * Bq
+    M_vis = min(blk_start // s, ceil.shape[2])
+    if M_vis <= 0:
+        return torch.full((B, H, 1, kk), -1, dtype=torch.int32), torch.full((B, H, 1), float("inf"))
+    cells = torch.arange(M_vis, dtype=torch.int64).expand(B, H, M_vis)
+    ok = torch.ones(B, H, M_vis, dtype=torch.bool)
+    score = fsl_scores(q, kbar[:, :, :M_vis], ceil[:, :, :M_vis], cells, ok, torch.tensor([float(pos)]), lam, sigma, scale, s)
+    sel, mg = _pick(score, cells, ok, kk)
+    if sel.shape[-1] < kk:
+        sel = torch.cat([sel, sel.new_full((B, H, 1, kk - sel.shape[-1]), -1)], dim=-1)
+    return sel, mg
+
+
 def fsl_decode_pool(kbar, ceil, blk_start: int, s: int, P: int, Wc: int):
     """Candidate pool of the decode block starting at blk_start; src/fsattn/attention.py:1313-1360 with the
     (ceiling desc, index asc) tie rule. kbar (B,H,ncell,D), ceil (B,H,ncell). Returns None when nothing is visible."""

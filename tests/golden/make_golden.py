@@ -169,16 +169,16 @@ def gen_fsl(kind: str, B=1, H=2, D=64, N=1000, T=72, seed=7):
     print("wrote", f"fsl_{kind}.npz")
 
 
-def gen_fs_dense(kind: str, B=1, H=2, D=64, N=1000, seed=31):
+def gen_fs_dense(kind: str, B=1, H=2, D=64, N=1000, T=40, seed=31):
     """The dense FS variant (serve preset "dense": cell_prune_kernel = 0, every completed visible cell is a candidate) at the
-    Q/K/V level: prefill selections and the layer output of an N-token prefill."""
+    Q/K/V level: selections and layer outputs of an N-token prefill and of T decode steps after it."""
     from kv_cache import FSKVCache
     from src.fsattn import FSAttn
     from bench_efficiency import serve_kwargs
-    Q, K, V = make_inputs(kind, B, H, N, D, seed)
-    flat = [t.transpose(1, 2).reshape(B, N, H * D).contiguous() for t in (Q, K, V)]
-    out = {"kind": kind, "B": B, "H": H, "D": D, "N": N, "Q": _bf16_bits(Q), "K": _bf16_bits(K), "V": _bf16_bits(V)}
-    x = torch.zeros(B, N, H * D)
+    Q, K, V = make_inputs(kind, B, H, N + T, D, seed)
+    flat = [t.transpose(1, 2).reshape(B, N + T, H * D).contiguous() for t in (Q, K, V)]
+    out = {"kind": kind, "B": B, "H": H, "D": D, "N": N, "T": T, "Q": _bf16_bits(Q), "K": _bf16_bits(K), "V": _bf16_bits(V)}
+    x = torch.zeros(B, N + T, H * D)
     os.environ["FS_PRUNE_KERNEL"] = "0"
     try:
         def run(fused):
@@ -200,10 +200,15 @@ def gen_fs_dense(kind: str, B=1, H=2, D=64, N=1000, seed=31):
                     return torch.zeros_like(Qx)
                 a._cell_fused_lr = grab
             c = FSKVCache(a)
+            ys = []
             with torch.no_grad():
-                y = a(x, cache=c)
-            return a, y, sels
-        a, y, _ = run(False)
+                ys.append(a(x[:, :N], cache=c))
+                for t in range(T):
+                    ys.append(a(x[:, N + t:N + t + 1], cache=c))
+            return a, ys, sels
+        a, ys, _ = run(False)
+        y = ys[0]
+        out["y_decode"] = torch.cat(ys[1:], dim=1).numpy()
         out["lam"] = a.sel_scale.detach().numpy()
         out["sigma"] = a.sigma.detach().numpy()
         out["lrs"] = a.long_range_scale.detach().reshape(H).numpy()
@@ -212,6 +217,11 @@ def gen_fs_dense(kind: str, B=1, H=2, D=64, N=1000, seed=31):
         out["y_prefill"] = y.numpy()
         _, _, sels = run(True)
         out["sel_prefill"] = sels[0][:, :, :N].numpy().astype(np.int32)
+        kk = a.cell_topk
+        sd = np.full((T, B, H, kk), -1, np.int32)
+        for t, s_ in enumerate(sels[1:]):
+            sd[t, :, :, :s_.shape[-1]] = s_[:, :, 0].numpy()
+        out["sel_decode"] = sd
     finally:
         os.environ["FS_PRUNE_KERNEL"] = "1"
     np.savez_compressed(os.path.join(HERE, f"fsdense_{kind}.npz"), **out)
@@ -396,7 +406,7 @@ def main():
         "fsb_randn": lambda: gen_fsb("randn"),
         "fsb_vocab": lambda: gen_fsb("vocab", N=1500, T=40, seed=29),
         "fsdense_randn": lambda: gen_fs_dense("randn"),
-        "fsdense_vocab": lambda: gen_fs_dense("vocab", N=900, seed=37),
+        "fsdense_vocab": lambda: gen_fs_dense("vocab", N=900, T=24, seed=37),
     }
     for name, fn in jobs.items():
         if not only or name in only:

@@ -11,8 +11,9 @@ from oracle import fsl
 @pytest.mark.parametrize("kind", ["randn", "vocab"])
 def test_dense_prefill_selection_and_output(kind):
     g = load_golden(f"fsdense_{kind}")
-    Q, K, V = (bf16_from_bits(g[k]).float() for k in ("Q", "K", "V"))
-    B, H, N, D = Q.shape
+    N = int(g["N"])
+    Q, K, V = (bf16_from_bits(g[k]).float()[:, :, :N] for k in ("Q", "K", "V"))
+    B, H, _, D = Q.shape
     lam, sigma = torch.from_numpy(g["lam"]), torch.from_numpy(g["sigma"])
     lrs, norm_w, eps = torch.from_numpy(g["lrs"]), torch.from_numpy(g["norm_w"]), float(g["eps"])
     s, Bq, kk, W, scale = 32, 128, 4, 512, D ** -0.5
@@ -39,3 +40,36 @@ def test_dense_prefill_selection_and_output(kind):
     y = fsl.lr_norm_combine(sr, o, norm_w, lrs, eps, torch.float32)
     want = torch.from_numpy(g["y_prefill"])
     assert (y - want).abs().max().item() < 2e-5
+
+
+@pytest.mark.parametrize("kind", ["randn", "vocab"])
+def test_dense_decode_selection_and_output(kind):
+    """T decode steps after the prefill (crossing cell closes and, for randn, a 128-token block change): the selected cells
+    and the layer output of every step."""
+    g = load_golden(f"fsdense_{kind}")
+    N, T = int(g["N"]), int(g["T"])
+    Q, K, V = (bf16_from_bits(g[k]).float() for k in ("Q", "K", "V"))
+    B, H, _, D = Q.shape
+    lam, sigma = torch.from_numpy(g["lam"]), torch.from_numpy(g["sigma"])
+    lrs, norm_w, eps = torch.from_numpy(g["lrs"]), torch.from_numpy(g["norm_w"]), float(g["eps"])
+    s, Bq, kk, W, scale = 32, 128, 4, 512, D ** -0.5
+    cos, sin = fsl.rope_tables(D, 4096, orig_len=4096)
+    ref_sel = torch.from_numpy(g["sel_decode"])                 # (T,B,H,kk)
+    ref_y = torch.from_numpy(g["y_decode"])                     # (B,T,H*D)
+    n_exact = 0
+    for t in range(T):
+        pos = N + t
+        kbar, ceil = fsl.cell_stats(K[:, :, :pos + 1], s)
+        q = Q[:, :, pos:pos + 1]
+        sel, margin = fsl.fs_dense_decode_select(q, kbar, ceil, pos, lam, sigma, scale, s, Bq, kk)
+        want = ref_sel[t].unsqueeze(2)
+        same_set = (sel.sort(-1).values == want.sort(-1).values).all(-1)
+        assert bool((same_set | (margin <= 1e-4)).all()), f"step {t}: dense decode selection differs outside the margin"
+        n_exact += int((sel == want).all(-1).sum())
+        j0 = max(0, pos - W)
+        sr = fsl.window_attention(q, K[:, :, j0:pos + 1], V[:, :, j0:pos + 1], cos, sin, W, scale, q_pos0=pos, k_pos0=j0,
+                                  act_dtype=torch.float32)
+        o = fsl.cell_readout(q, K[:, :, :pos + 1], V[:, :, :pos + 1], want.to(torch.int32), s, Bq, scale, pos, pos + 1)
+        y = fsl.lr_norm_combine(sr, o, norm_w, lrs, eps, torch.float32)
+        assert (y[:, 0] - ref_y[:, t]).abs().max().item() < 2e-5, f"step {t}"
+    assert n_exact >= 0.9 * T * B * H
