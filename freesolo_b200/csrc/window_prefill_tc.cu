@@ -2,17 +2,20 @@
 // TMA (cp.async.bulk.tensor, 128-byte swizzle), one CTA per 128 queries of one (batch, head).
 //
 //   pass 0 (rope_qk_kernel): rotate Q and K once into a (B*H, N, D) bf16 workspace (HBM-bound: 2 reads + 2 writes of N*D)
-//   pass 1 (window_tc_kernel): for the W/128 + 1 key tiles of the band
-//        S  = Qr Kr^T        tcgen05.mma 128x128x64 (4 k-steps), accumulator in TMEM
-//        P  = exp2(S*c - m)  4 softmax warps, one query row per thread (tcgen05.ld), band mask on the edge tiles,
-//                            P written as bf16 into shared memory in the K-major swizzled operand layout
-//        PV = P V            tcgen05.mma 128x64x128 (8 k-steps) into a second TMEM accumulator; the running output lives in
-//                            registers: O = O * alpha + PV
-// Warp roles: warps 0-7 softmax/epilogue (TMEM lane quarter = warp id % 4, two threads per query row), warp 8 TMA producer,
-// warp 9 MMA issuer.
+//   pass 1 (window_tc_kernel): for the W/64 + 2 key tiles (64 keys each) of the band
+//        S  = Qr Kr^T        tcgen05.mma 128x64x64 (4 k-steps), accumulator in TMEM
+//        P  = exp2(S*c - m)  4 softmax warps, one query row per thread (tcgen05.ld), band mask on the edge tiles. P never
+//                            leaves tensor memory: it is split into a bf16 high part and a bf16 low part (p - high), so
+//                            that the product keeps about 16 bits of every probability, and both are written with
+//                            tcgen05.st over the columns S occupied (64 fp32 columns = 32 packed columns high + 32 low)
+//        PV = P V            tcgen05.mma 128x64x64 with A read from tensor memory (4 k-steps for the high part, 4 for the low
+//                            part) into a second TMEM accumulator; the running output lives in registers: O = O*alpha + PV
+// Warp roles: warps 0-3 softmax/epilogue (TMEM lane quarter = warp id), warp 4 TMA producer, warp 5 MMA issuer. A CTA takes
+// 256 TMEM columns (S0, S1, PV0, PV1 of 64 each) and about 100 KB of shared memory, so two CTAs share an SM and one CTA's
+// softmax runs while the other's MMAs are in flight.
 // Every mbarrier wait is bounded; on a timeout the CTA records it in *status, stops issuing work and still frees its TMEM.
 //
-// FLOPs per CTA: (W/128+1) tiles * (2*128*128*64 + 2*128*128*64); algorithmic FLOPs per query 4*D*min(i+1, W+1).
+// FLOPs per CTA: (W/64+2) tiles * (2*128*64*64 + 2*2*128*64*64); algorithmic FLOPs per query 4*D*min(i+1, W+1).
 #include <cuda.h>
 #include <cuda_fp16.h>
 
@@ -21,24 +24,25 @@
 namespace {
 
 constexpr int TC_BM = 128;          // queries per CTA
-constexpr int TC_BN = 128;          // keys per tile
+constexpr int TC_BN = 64;           // keys per tile
 constexpr int TC_D = 64;
-constexpr int TC_THREADS = 320;     // 8 softmax warps (two per TMEM lane quarter), TMA producer, MMA issuer
-constexpr int TC_SOFTMAX_THREADS = 256;
+constexpr int TC_THREADS = 192;     // 4 softmax warps (one per TMEM lane quarter), TMA producer, MMA issuer
+constexpr int TC_SOFTMAX_THREADS = 128;
 constexpr int TC_WAIT_ITERS = 1 << 24;
+constexpr int TC_TMEM_COLS = 256;   // S0 | S1 | PV0 | PV1, 64 columns each
+constexpr int TC_TILE_BYTES = TC_BN * TC_D * 2;      // one K or V tile: 64 rows of 128 bytes
 
 // shared memory map (bytes, from a 1024-byte aligned base)
 constexpr int SM_Q = 0;                         // 128 x 64 bf16
-constexpr int TC_KV_STAGES = 4;                 // key/value tiles in flight: with W = 512 (five tiles) all but the last are
-                                                // requested before the first MMA, so tile loads are off the critical path
+constexpr int TC_KV_STAGES = 5;                 // key/value tiles in flight (320 keys): tile loads stay off the critical path
 constexpr int SM_K = SM_Q + 16384;              // TC_KV_STAGES stages
-constexpr int SM_V = SM_K + TC_KV_STAGES * 16384;
-constexpr int SM_P = SM_V + TC_KV_STAGES * 16384;   // 2 buffers of 128 x 128 bf16 (two K-blocks of 128 x 64)
-constexpr int SM_BAR = SM_P + 2 * 32768;        // mbarriers
+constexpr int SM_V = SM_K + TC_KV_STAGES * TC_TILE_BYTES;
+constexpr int SM_BAR = SM_V + TC_KV_STAGES * TC_TILE_BYTES;        // mbarriers
 constexpr int SM_TOTAL = SM_BAR + 256;
 
-enum { BAR_Q = 0, BAR_KV_FULL = 1, BAR_KV_EMPTY = 5, BAR_S_FULL = 9, BAR_S_FREE = 11, BAR_P_FULL = 13, BAR_PV_FULL = 15,
-       BAR_PV_FREE = 17, BAR_MX = 19, BAR_L = 21, BAR_COUNT = 22 };      // KV_FULL / KV_EMPTY hold TC_KV_STAGES barriers each
+enum { BAR_Q = 0, BAR_KV_FULL = 1, BAR_KV_EMPTY = BAR_KV_FULL + TC_KV_STAGES, BAR_S_FULL = BAR_KV_EMPTY + TC_KV_STAGES,
+       BAR_P_FULL = BAR_S_FULL + 2, BAR_PV_FULL = BAR_P_FULL + 2, BAR_PV_FREE = BAR_PV_FULL + 2, BAR_COUNT = BAR_PV_FREE + 2 };
+static_assert(BAR_COUNT * 8 <= 256, "mbarrier area");
 
 __device__ __forceinline__ uint32_t s_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -51,9 +55,11 @@ __device__ __forceinline__ void bar_arrive(uint64_t* bar) {
 __device__ __forceinline__ void bar_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(s_u32(bar)), "r"(bytes) : "memory");
 }
-__device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity) {
+// bounded wait; gives up early once another thread of the CTA has raised the abort flag
+__device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity, volatile int* abortp) {
     const uint32_t addr = s_u32(bar);
     for (int i = 0; i < TC_WAIT_ITERS; i++) {
+        if ((i & 63) == 63 && *abortp) return false;
         uint32_t done;
         asm volatile("{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}"
                      : "=r"(done) : "r"(addr), "r"(parity) : "memory");
@@ -93,6 +99,17 @@ __device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t b
     asm volatile("{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\ntcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
                  ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
 }
+// the same product with the A operand (128 rows x 16 bf16, lane = row, 8 packed 32-bit columns) read from tensor memory
+__device__ __forceinline__ void umma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc, int accumulate) {
+    asm volatile("{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\ntcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}"
+                 ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// eight 32-bit registers of this thread's TMEM lane into eight consecutive columns
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};"
+                 ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]) : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(s_u32(bar)) : "memory");
 }
@@ -161,21 +178,20 @@ struct TcParams {
 };
 
 // ---- pass 1 -------------------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(TC_THREADS, 1)
+__global__ void __launch_bounds__(TC_THREADS, 2)
 window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                  const __grid_constant__ CUtensorMap tm_v, const TcParams p) {
     extern __shared__ unsigned char tc_smem_raw[];
     __shared__ uint32_t tmem_base_s;
     __shared__ int abort_s;
-    __shared__ float mx_s[2][2][TC_BM];      // [tile parity][column half][row]: the two halves of a row exchange their maxima
-    __shared__ float l_s[2][TC_BM];
     unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
     uint64_t* bars = reinterpret_cast<uint64_t*>(base + SM_BAR);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int q0 = blockIdx.x * TC_BM;
     const int bh = blockIdx.y;
     const int b = bh / p.H, h = bh - b * p.H;
-    const int ntile_total = p.W / TC_BN + 1;
+    // tile t covers the keys q0 - W + 64 t .. + 63; the band of the CTA's 128 queries ends at key q0 + 127
+    const int ntile_total = (p.W + TC_BM) / TC_BN;
     int t_first = (p.W - q0) / TC_BN;                 // tiles that lie entirely before the sequence start are skipped
     if (t_first < 0) t_first = 0;
     const int nt = ntile_total - t_first;
@@ -188,27 +204,25 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         }
         for (int s = 0; s < 2; s++) {
             bar_init(&bars[BAR_S_FULL + s], 1);
-            bar_init(&bars[BAR_S_FREE + s], TC_SOFTMAX_THREADS);
             bar_init(&bars[BAR_P_FULL + s], TC_SOFTMAX_THREADS);
             bar_init(&bars[BAR_PV_FULL + s], 1);
             bar_init(&bars[BAR_PV_FREE + s], TC_SOFTMAX_THREADS);
-            bar_init(&bars[BAR_MX + s], TC_SOFTMAX_THREADS);
         }
-        bar_init(&bars[BAR_L], TC_SOFTMAX_THREADS);
         abort_s = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 8) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s_u32(&tmem_base_s)), "r"(512) : "memory");
+    if (warp == 4) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s_u32(&tmem_base_s)), "r"(TC_TMEM_COLS) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_base_s;
+    const uint32_t tmem_pv = tmem + 2 * TC_BN;          // PV0 | PV1 behind S0 | S1
     volatile int* abortp = &abort_s;
 
-    if (warp == 8) {
+    if (warp == 4) {
         // ================= TMA producer ====================================================================================
         if (lane == 0) {
             bar_expect_tx(&bars[BAR_Q], 16384);
@@ -216,26 +230,28 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             for (int i = 0; i < nt && !*abortp; i++) {
                 const int s = i % TC_KV_STAGES;
                 const int kt0 = q0 - p.W + (t_first + i) * TC_BN;
-                if (i >= TC_KV_STAGES && !bar_wait(&bars[BAR_KV_EMPTY + s], ((i / TC_KV_STAGES) - 1) & 1)) { *abortp = 1; break; }
-                bar_expect_tx(&bars[BAR_KV_FULL + s], 32768);
-                tma_load_3d(base + SM_K + s * 16384, &tm_k, 0, kt0, bh, &bars[BAR_KV_FULL + s]);
-                tma_load_4d(base + SM_V + s * 16384, &tm_v, 0, kt0, h, b, &bars[BAR_KV_FULL + s]);
+                if (i >= TC_KV_STAGES && !bar_wait(&bars[BAR_KV_EMPTY + s], ((i / TC_KV_STAGES) - 1) & 1, abortp)) { *abortp = 1; break; }
+                bar_expect_tx(&bars[BAR_KV_FULL + s], 2 * TC_TILE_BYTES);
+                tma_load_3d(base + SM_K + s * TC_TILE_BYTES, &tm_k, 0, kt0, bh, &bars[BAR_KV_FULL + s]);
+                tma_load_4d(base + SM_V + s * TC_TILE_BYTES, &tm_v, 0, kt0, h, b, &bars[BAR_KV_FULL + s]);
             }
         }
-    } else if (warp == 9) {
+    } else if (warp == 5) {
         // ================= MMA issuer ======================================================================================
+        // Issue order QK(0), QK(1), PV(0), QK(2), PV(1), ...: the tensor pipe runs one thread's MMAs in issue order, so
+        // QK(i+2), which overwrites the columns that held P(i), starts after PV(i) has read them - no barrier is needed
+        // for the S buffers beyond "P(i) is complete".
         if (lane == 0) {
             const uint32_t idesc_s = instr_desc(TC_BN, 0, 1);
-            const uint32_t idesc_pv = instr_desc(TC_D, 1, 1);      // A and B of one MMA must share their 16-bit format: P is bf16 like V
-            bool ok = bar_wait(&bars[BAR_Q], 0);
+            const uint32_t idesc_pv = instr_desc(TC_D, 1, 1);      // A (P, from TMEM) and B (V) share the bf16 format
+            bool ok = bar_wait(&bars[BAR_Q], 0, abortp);
             for (int i = 0; i <= nt && ok && !*abortp; i++) {
                 if (i < nt) {
                     const int s = i & 1, ks = i % TC_KV_STAGES;
-                    ok = bar_wait(&bars[BAR_KV_FULL + ks], (i / TC_KV_STAGES) & 1);
-                    if (ok && i >= 2) ok = bar_wait(&bars[BAR_S_FREE + s], ((i >> 1) - 1) & 1);
+                    ok = bar_wait(&bars[BAR_KV_FULL + ks], (i / TC_KV_STAGES) & 1, abortp);
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t aq = s_u32(base + SM_Q), bk = s_u32(base + SM_K + ks * 16384);
+                    const uint32_t aq = s_u32(base + SM_Q), bk = s_u32(base + SM_K + ks * TC_TILE_BYTES);
 #pragma unroll
                     for (int k = 0; k < TC_D / 16; k++)
                         umma(tmem + s * TC_BN, smem_desc(aq + k * 32), smem_desc(bk + k * 32), idesc_s, k > 0);
@@ -243,15 +259,19 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
                 }
                 if (i >= 1) {
                     const int j = i - 1, bb = j & 1;
-                    ok = bar_wait(&bars[BAR_P_FULL + bb], (j >> 1) & 1);
-                    if (ok && j >= 2) ok = bar_wait(&bars[BAR_PV_FREE + bb], ((j >> 1) - 1) & 1);
+                    ok = bar_wait(&bars[BAR_P_FULL + bb], (j >> 1) & 1, abortp);
+                    if (ok && j >= 2) ok = bar_wait(&bars[BAR_PV_FREE + bb], ((j >> 1) - 1) & 1, abortp);
                     if (!ok) break;
                     tc_fence_after();
                     const int vs = j % TC_KV_STAGES;
-                    const uint32_t ap = s_u32(base + SM_P + bb * 32768), bv = s_u32(base + SM_V + vs * 16384);
+                    const uint32_t ap = tmem + bb * TC_BN, bv = s_u32(base + SM_V + vs * TC_TILE_BYTES);
+                    // 16 keys per step: 8 packed columns of P, 16 rows (2048 bytes) of V; high parts, then low parts
 #pragma unroll
                     for (int k = 0; k < TC_BN / 16; k++)
-                        umma(tmem + 256 + bb * TC_D, smem_desc(ap + (k >> 2) * 16384 + (k & 3) * 32), smem_desc(bv + k * 2048), idesc_pv, k > 0);
+                        umma_ts(tmem_pv + bb * TC_D, ap + k * 8, smem_desc(bv + k * 2048), idesc_pv, k > 0);
+#pragma unroll
+                    for (int k = 0; k < TC_BN / 16; k++)
+                        umma_ts(tmem_pv + bb * TC_D, ap + TC_BN / 2 + k * 8, smem_desc(bv + k * 2048), idesc_pv, 1);
                     umma_commit(&bars[BAR_PV_FULL + bb]);
                     umma_commit(&bars[BAR_KV_EMPTY + vs]);
                 }
@@ -259,89 +279,80 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             if (!ok) *abortp = 1;
         }
     } else {
-        // ================= softmax + epilogue: two threads per query row =====================================================
-        // Warps w and w+4 share the TMEM lane quarter w (a warp reaches lanes 32 (w % 4) ..): each thread owns one row and
-        // one half of it - 64 of the tile's 128 score columns and 32 of the 64 output dims. The halves meet twice: the row
-        // maximum of every tile (shared memory + an mbarrier with a bounded wait) and the row sum at the end.
-        const int sw = warp & 3, half = warp >> 2;
-        const int r = sw * 32 + lane;
+        // ================= softmax + epilogue: one thread per query row ======================================================
+        // Warp w reaches the TMEM lanes 32 w .. 32 w + 31; a thread owns row r: the tile's 64 scores, its running maximum and
+        // sum, and the 64 output dims, so the rows never exchange anything.
+        const int r = warp * 32 + lane;
         const int qi = q0 + r;
-        const uint32_t lane_base = tmem + ((uint32_t)(sw * 32) << 16);
-        constexpr int HC = TC_BN / 2, HD = TC_D / 2;
+        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+        const uint32_t lane_pv = tmem_pv + ((uint32_t)(warp * 32) << 16);
+        const int t_upper = p.W / TC_BN;             // tiles from here on reach past some row's own position
         float m = -INFINITY, l = 0.0f, a_pend = 0.0f;
-        float O[HD];
+        float O[TC_D];
 #pragma unroll
-        for (int d = 0; d < HD; d++) O[d] = 0.0f;
+        for (int d = 0; d < TC_D; d++) O[d] = 0.0f;
         bool ok = true;
         for (int i = 0; i < nt; i++) {
             const int bb = i & 1;
             const int t = t_first + i;
-            ok = ok && bar_wait(&bars[BAR_S_FULL + bb], (i >> 1) & 1) && !*abortp;
+            ok = ok && bar_wait(&bars[BAR_S_FULL + bb], (i >> 1) & 1, abortp) && !*abortp;
             if (!__all_sync(FS_FULL, ok)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t s_addr = lane_base + bb * TC_BN + half * HC;
-            const bool lower_edge = (t == 0), upper_edge = (t == ntile_total - 1);
-            const bool edge = lower_edge || upper_edge;
-            // the half row's 64 scores, read from TMEM once and kept in registers for both passes
-            float v[HC];
+            const uint32_t s_addr = lane_base + bb * TC_BN;
+            // the row's 64 scores, read from TMEM once and kept in registers for both passes
+            float v[TC_BN];
             tmem_ld32(s_addr, v);
             tmem_ld32(s_addr + 32, v + 32);
-            if (edge) {                     // first / diagonal tile: keys outside [q - W, q] become -inf
+            if (t < 2 || t >= t_upper) {            // edge tile: keys outside [q - W, q] become -inf
+                const int c_lo = r - TC_BN * t, c_hi = r + p.W - TC_BN * t;
 #pragma unroll
-                for (int c = 0; c < HC; c++) {
-                    const int col = half * HC + c;
-                    const bool valid = !(lower_edge && col < r) && !(upper_edge && col > r);
-                    v[c] = valid ? v[c] : -INFINITY;
-                }
+                for (int c = 0; c < TC_BN; c++) v[c] = (c >= c_lo && c <= c_hi) ? v[c] : -INFINITY;
             }
-            // pass 1: maximum of this half row, then of the whole row
             float mx = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < HC; c++) mx = fmaxf(mx, v[c]);
-            mx_s[bb][half][r] = mx;
-            bar_arrive(&bars[BAR_MX + bb]);
-            ok = bar_wait(&bars[BAR_MX + bb], (i >> 1) & 1) && !*abortp;
-            if (!__all_sync(FS_FULL, ok)) { ok = false; break; }
-            mx = fmaxf(mx, mx_s[bb][half ^ 1][r]);
+            for (int c = 0; c < TC_BN; c++) mx = fmaxf(mx, v[c]);
             const float m_new = fmaxf(m, mx);
             const float alpha = (m == -INFINITY) ? 0.0f : exp2f((m - m_new) * p.c2);
             const float mc = (m_new == -INFINITY) ? 0.0f : m_new * p.c2;
-            // pass 2: probabilities (ex2.approx of a masked score is exactly 0), partial row sum over the bf16-rounded values
-            // the tensor core will multiply, bf16 P into the swizzled K-major operand layout
+            // probabilities (ex2.approx of a masked score is exactly 0). Each is split into bf16 high + bf16 low so the
+            // tensor core multiplies about 16 bits of it; both parts go back into the columns the scores came from.
             float rowsum = 0.0f;
-            unsigned char* prow = base + SM_P + bb * 32768 + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-            for (int c0 = 0; c0 < HC; c0 += 8) {
-                uint32_t pk[4];
+            for (int c0 = 0; c0 < TC_BN; c0 += 16) {
+                uint32_t ph[8], pl[8];
 #pragma unroll
-                for (int c = 0; c < 8; c += 2) {
+                for (int c = 0; c < 16; c += 2) {
                     float p0, p1;
                     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p0) : "f"(fmaf(v[c0 + c], p.c2, -mc)));
                     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p1) : "f"(fmaf(v[c0 + c + 1], p.c2, -mc)));
+                    rowsum += p0 + p1;
                     const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
-                    pk[c >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
-                    rowsum += bf_lo(pk[c >> 1]) + bf_hi(pk[c >> 1]);
+                    const uint32_t hb = *reinterpret_cast<const uint32_t*>(&h2);
+                    const __nv_bfloat162 l2 = __floats2bfloat162_rn(p0 - bf_lo(hb), p1 - bf_hi(hb));
+                    ph[c >> 1] = hb;
+                    pl[c >> 1] = *reinterpret_cast<const uint32_t*>(&l2);
                 }
-                const int cc = (half * HC + c0) >> 3;              // 16-byte chunk index within the 128-key row
-                unsigned char* dst = prow + (cc >> 3) * 16384 + (((cc & 7) ^ (r & 7)) << 4);
-                *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                tmem_st8(s_addr + (c0 >> 1), ph);
+                tmem_st8(s_addr + TC_BN / 2 + (c0 >> 1), pl);
             }
+            tmem_st_wait();
             tc_fence_before();
-            bar_arrive(&bars[BAR_S_FREE + bb]);
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             bar_arrive(&bars[BAR_P_FULL + bb]);
             l = l * alpha + rowsum;
             m = m_new;
-            // fold the previous tile's P V into the running output (this thread's 32 dims)
+            // fold the previous tile's P V into the running output
             if (i >= 1) {
                 const int j = i - 1, jb = j & 1;
-                ok = bar_wait(&bars[BAR_PV_FULL + jb], (j >> 1) & 1) && !*abortp;
+                ok = bar_wait(&bars[BAR_PV_FULL + jb], (j >> 1) & 1, abortp) && !*abortp;
                 if (!__all_sync(FS_FULL, ok)) { ok = false; break; }
                 tc_fence_after();
-                float v[32];
-                tmem_ld32(lane_base + 256 + jb * TC_D + half * HD, v);
 #pragma unroll
-                for (int c = 0; c < HD; c++) O[c] = fmaf(O[c], a_pend, v[c]);
+                for (int hh = 0; hh < 2; hh++) {
+                    float pv[32];
+                    tmem_ld32(lane_pv + jb * TC_D + hh * 32, pv);
+#pragma unroll
+                    for (int c = 0; c < 32; c++) O[hh * 32 + c] = fmaf(O[hh * 32 + c], a_pend, pv[c]);
+                }
                 tc_fence_before();
                 bar_arrive(&bars[BAR_PV_FREE + jb]);
             }
@@ -349,29 +360,27 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         }
         if (ok && nt > 0) {
             const int j = nt - 1, jb = j & 1;
-            ok = bar_wait(&bars[BAR_PV_FULL + jb], (j >> 1) & 1) && !*abortp;
+            ok = bar_wait(&bars[BAR_PV_FULL + jb], (j >> 1) & 1, abortp) && !*abortp;
             if (__all_sync(FS_FULL, ok)) {
                 tc_fence_after();
-                float v[32];
-                tmem_ld32(lane_base + 256 + jb * TC_D + half * HD, v);
 #pragma unroll
-                for (int c = 0; c < HD; c++) O[c] = fmaf(O[c], a_pend, v[c]);
+                for (int hh = 0; hh < 2; hh++) {
+                    float pv[32];
+                    tmem_ld32(lane_pv + jb * TC_D + hh * 32, pv);
+#pragma unroll
+                    for (int c = 0; c < 32; c++) O[hh * 32 + c] = fmaf(O[hh * 32 + c], a_pend, pv[c]);
+                }
                 tc_fence_before();
             } else {
                 ok = false;
             }
         }
-        // the two halves of a row add their sums
-        l_s[half][r] = l;
-        bar_arrive(&bars[BAR_L]);
-        if (ok) ok = bar_wait(&bars[BAR_L], 0) && !*abortp;
         if (!ok) *abortp = 1;
         if (ok && qi < p.N) {
-            const float lt = l + l_s[half ^ 1][r];
-            const float inv = (lt > 0.0f) ? 1.0f / lt : 0.0f;
-            bf16* op = p.out + ((int64_t)b * p.N + qi) * ((int64_t)p.H * TC_D) + (int64_t)h * TC_D + half * HD;
+            const float inv = (l > 0.0f) ? 1.0f / l : 0.0f;
+            bf16* op = p.out + ((int64_t)b * p.N + qi) * ((int64_t)p.H * TC_D) + (int64_t)h * TC_D;
 #pragma unroll
-            for (int e = 0; e < HD / 8; e++) {
+            for (int e = 0; e < TC_D / 8; e++) {
                 uint4 w;
                 w.x = pack_bf2(O[8 * e + 0] * inv, O[8 * e + 1] * inv);
                 w.y = pack_bf2(O[8 * e + 2] * inv, O[8 * e + 3] * inv);
@@ -384,8 +393,8 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     tc_fence_before();
     __syncthreads();
     if (tid == 0 && abort_s && p.status != nullptr) atomicAdd(p.status, 1);
-    if (warp == 8) {
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
+    if (warp == 4) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS) : "memory");
     }
 }
 
@@ -421,7 +430,7 @@ size_t fs_window_prefill_tc_workspace(const fsattn_window_prefill_t* a) {
 
 bool fs_window_prefill_tc_ok(const fsattn_window_prefill_t* a) {
     return a->D == TC_D && a->W >= TC_BN && a->W % TC_BN == 0 && a->workspace != nullptr &&
-           a->workspace_bytes >= (int64_t)fs_window_prefill_tc_workspace(a) && ((uintptr_t)a->workspace & 1023) == 0 &&
+           a->workspace_bytes >= (int64_t)fs_window_prefill_tc_workspace(a) && ((uintptr_t)a->workspace & 15) == 0 &&
            (a->v.sn * 2) % 16 == 0 && (a->v.sh * 2) % 16 == 0 && (a->v.sb * 2) % 16 == 0 && encode_fn() != nullptr;
 }
 
@@ -441,8 +450,8 @@ int fs_window_prefill_tc(const fsattn_window_prefill_t* a, cudaStream_t st) {
     {
         const cuuint64_t dims[3] = {TC_D, (cuuint64_t)a->N, BH};
         const cuuint64_t strides[2] = {TC_D * 2, (cuuint64_t)a->N * TC_D * 2};
-        const cuuint32_t box[3] = {TC_D, TC_BM, 1};
-        FS_REQUIRE(make_map(&tq, qr, 3, dims, strides, box) && make_map(&tk, kr, 3, dims, strides, box),
+        const cuuint32_t box[3] = {TC_D, TC_BM, 1}, boxk[3] = {TC_D, TC_BN, 1};
+        FS_REQUIRE(make_map(&tq, qr, 3, dims, strides, box) && make_map(&tk, kr, 3, dims, strides, boxk),
                    "window_prefill: cuTensorMapEncodeTiled failed for the rotated Q/K workspace");
     }
     {
@@ -492,7 +501,7 @@ extern "C" int fsattn_window_prefill_static(const fsattn_window_prefill_t* a, fs
     FS_REQUIRE(a != nullptr && a->q.ptr && a->k.ptr && a->v.ptr && a->cos && a->sin && a->out, "window_prefill_static: null pointer");
     FS_REQUIRE(a->B > 0 && a->H > 0 && a->N > 0 && a->pos0 >= 0, "window_prefill_static: bad sizes");
     FS_UNSUPPORTED(a->D != TC_D || a->W < TC_BN || a->W % TC_BN != 0,
-                   "window_prefill_static: only head_dim 64 and windows that are multiples of 128 (got D=%d, W=%d)", a->D, a->W);
+                   "window_prefill_static: only head_dim 64 and windows that are multiples of 64 (got D=%d, W=%d)", a->D, a->W);
     const fsattn_bhnd_t* t[3] = {&a->q, &a->k, &a->v};
     for (int i = 0; i < 3; i++)
         FS_REQUIRE(((uintptr_t)t[i]->ptr & 15) == 0 && t[i]->sn % 8 == 0 && t[i]->sh % 8 == 0 && t[i]->sb % 8 == 0,

@@ -183,13 +183,12 @@ def window_prefill(Q, K, V, cos, sin, W: int, scale: float, pos0: int = 0, impl:
     a.out = out.data_ptr()
     a.impl = int(impl)
     ws = None
-    if impl == 0 and D == 64 and W >= 128 and W % 128 == 0:
-        # scratch of the tensor-core kernel (rotated Q and K); torch's allocator returns 512-byte aligned blocks, so
-        # over-allocate and align to 1024
+    if impl == 0 and D == 64 and W >= 64 and W % 64 == 0:
+        # scratch of the tensor-core kernel (rotated Q and K); TMA wants a 16-byte aligned base, which torch's allocator
+        # (512-byte aligned blocks) always gives
         nbytes = 2 * B * H * N * D * 2
-        ws = torch.empty(nbytes + 1024, dtype=torch.uint8, device=Q.device)
-        off = (-ws.data_ptr()) % 1024
-        a.workspace, a.workspace_bytes = ws.data_ptr() + off, nbytes
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=Q.device)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), nbytes
     a.status = _p(status)
     L.call("fsattn_window_prefill", a, _stream(Q))
     if ws is not None:
@@ -200,7 +199,7 @@ def window_prefill(Q, K, V, cos, sin, W: int, scale: float, pos0: int = 0, impl:
 def window_prefill_static(Q, K, V, cos, sin, W: int, scale: float, pos0: int = 0, out=None, status=None):
     """window_prefill through the allocation-free entry point: the kernel's scratch is a fixed array inside the library, so
     nothing is allocated for it here. For callers that may not create device memory at call time. Only head_dim 64, W a
-    multiple of 128 and B*H*N <= 131072; larger or other shapes raise. `out` must be passed by such callers (when it is
+    multiple of 64 and B*H*N <= 131072; larger or other shapes raise. `out` must be passed by such callers (when it is
     None this convenience wrapper allocates the output, which is not scratch). Calls that overlap on the GPU race on the
     shared array; the first call on a device must come before any stream capture."""
     _need_cuda(Q, K, V, cos, sin)

@@ -134,8 +134,8 @@ typedef struct {
     float scale;
     void* out; /* (B,N,H*D) bf16 contiguous */
     int32_t impl; /* 0 = default (tensor-core kernel when the shape allows), 1 = force the CUDA-core kernel */
-    /* scratch for the tensor-core kernel: the rotated Q and K, 2*B*H*N*D*2 bytes, 1024-byte aligned (caller-owned; the
-     * kernel is used when head_dim = 64, W is a multiple of 128 and this is large enough, else the CUDA-core kernel runs) */
+    /* scratch for the tensor-core kernel: the rotated Q and K, 2*B*H*N*D*2 bytes, 16-byte aligned (caller-owned; the
+     * kernel is used when head_dim = 64, W is a multiple of 64 and this is large enough, else the CUDA-core kernel runs) */
     void* workspace; int64_t workspace_bytes;
     int32_t* status; /* optional int32: incremented when a bounded wait inside the tensor-core kernel ran out */
 } fsattn_window_prefill_t;
@@ -146,7 +146,7 @@ FSATTN_API int fsattn_window_prefill(const fsattn_window_prefill_t* a, fsattn_st
  * device synchronisation). It has no counterpart in the reference, which allocates through PyTorch wherever it likes.
  * The scratch for the rotated Q and K is a fixed array inside the library (FSATTN_WINDOW_STATIC_BYTES on every GPU that loads
  * it, until the process exits); a->workspace and a->workspace_bytes are ignored and nothing is allocated or freed.
- * Limits: head_dim 64, W a multiple of 128, and 2*B*H*N*64*2 bytes <= FSATTN_WINDOW_STATIC_BYTES, i.e. B*H*N <= 131072 rows;
+ * Limits: head_dim 64, W a multiple of 64, and 2*B*H*N*64*2 bytes <= FSATTN_WINDOW_STATIC_BYTES, i.e. B*H*N <= 131072 rows;
  * anything else is rejected with FSATTN_EINVAL / FSATTN_EUNSUPPORTED and a message. The first call on a device looks up the
  * array's device address: make that call before capturing a stream. All calls share the array, so calls that overlap on
  * the GPU race on it; consecutive calls on one stream are safe and need no clearing in between. */
