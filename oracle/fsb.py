@@ -336,8 +336,11 @@ class RowForests:
 
 def select_block(rf: RowForests, E: int, q, qpos, lam, sig, scale, s, ceil_row, Ktok, cfg=SERVE, want=None):
     """Selections of the queries of one block whose visible cells are [0, E): both beams, union, re-rank, top-K.
-    q (Bq, D) fp32, qpos (Bq,) fp32. Returns sel (Bq, K) int64 (-1 pad) and the re-rank margin (Bq,); `want`, when a
-    dict, also receives the two beams' cells, the visit counts and the spine heights."""
+    q (Bq, D) fp32, qpos (Bq,) fp32. Returns sel (Bq, K) int64 (-1 pad) and the margin (Bq,): the smaller of the
+    re-rank margin (smallest gap among the best K+1 re-rank scores) and the beam margin (smallest score gap at any
+    frontier cut-off of either beam), i.e. how far the fp32 scores are from changing the selection anywhere on the way.
+    `want`, when a dict, also receives the two beams' cells, the visit counts, the spine heights and the two margins
+    separately (`rerank_margin`, `beam_margin`)."""
     Bq = q.shape[0]
     m_b, m_bu = rf.prefix_counts(E)
     outs = []
@@ -356,11 +359,12 @@ def select_block(rf: RowForests, E: int, q, qpos, lam, sig, scale, s, ceil_row, 
     cand = union_candidates(outs[0][0], outs[1][0])
     u = rerank_scores(cand, q, qpos, lam, sig, ceil_row, Ktok, scale, s)
     sel, margin = rerank_top(cand, u, cfg["read_top"])
+    beam_margin = torch.minimum(outs[0][3], outs[1][3])
     if want is not None:
         want.update(main=outs[0][0], union=outs[1][0], nvis=outs[0][1] + outs[1][1], cand=cand, u=u,
                     height=(outs[0][2]["height"], outs[1][2]["height"]), m_b=(m_b, m_bu),
-                    beam_margin=torch.minimum(outs[0][3], outs[1][3]))
-    return sel, margin
+                    beam_margin=beam_margin, rerank_margin=margin)
+    return sel, torch.minimum(margin, beam_margin)
 
 
 def fsb_select_prefill(Q, K, kbar, ceil_c, tau, tau_u, lam, sigma, scale, s=32, Bq=128, cfg=SERVE, blocks=None):
