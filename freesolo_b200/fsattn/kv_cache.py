@@ -91,6 +91,11 @@ class FSKVCache:
             kbar, ceil = ops.cell_stats(K, ncell)
         self._ncell = ncell
         self.pos = N
+        # forests of an earlier prompt describe that prompt's cells: a new prefill starts them over
+        fo = getattr(self, "fsb", None)
+        if fo is not None:
+            fo.reset()
+        self._fsb_blk = -1
         if not self.retain_kv:
             self._kbar, self._ceil = kbar, ceil
             return kbar, ceil
@@ -118,6 +123,11 @@ class FSKVCache:
             fo = ops.FsbForests(kb, ce, attn.fsb_tau, tau_u, cap_cells=cap)
             self.fsb = fo
             self._fsb_blk = -1
+        elif fo.n_seen == 0:
+            # reused for a new prompt: the thresholds may have been re-calibrated since the forests were created
+            fo.taus[0].copy_(attn.fsb_tau.detach().float())
+            if fo.nf > 1:
+                fo.taus[1].copy_(attn.fsb_tau_union.detach().float())
         return fo
 
     def fsb_block_change(self, pos: int, attn) -> bool:

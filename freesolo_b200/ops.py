@@ -22,7 +22,14 @@ def _need_cuda(*ts):
 
 
 def _stream(t: torch.Tensor) -> int:
-    L.init(t.device.index if t.device.index is not None else torch.cuda.current_device())
+    """The current stream of the tensor's device. The library launches on the CUDA context's current device (kernel
+    attributes, SM counts and the static scratch address are per device), so that device must be the tensor's."""
+    cur = torch.cuda.current_device()
+    idx = t.device.index if t.device.index is not None else cur
+    if idx != cur:
+        raise RuntimeError(f"freesolo_b200: tensors live on cuda:{idx} but the current device is cuda:{cur}; "
+                           f"call under torch.cuda.device({idx})")
+    L.init(idx)
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
@@ -520,6 +527,16 @@ class FsbForests:
         self.root32 = [torch.zeros(T, m_cap, D + 4, dtype=torch.float32, device=dev) for _ in range(self.nf)]
         self.spine = [torch.zeros(T, L.FSB_SPINE_MAX, D + 8, dtype=torch.float32, device=dev) for _ in range(self.nf)]
         self.hdr = [torch.full((T, 4), -1, dtype=torch.int32, device=dev) for _ in range(self.nf)]
+        self.n_seen = 0
+
+    def reset(self) -> None:
+        """Forget every admitted cell (a new prompt over the same statistics buffers). Chunk nodes need no clearing: a
+        chunk is only ever read after the admission count says it is complete, and it is rebuilt before that."""
+        for i in range(self.nf):
+            self.adm[i].fill_(-1)
+            self.m_tot[i].zero_()
+            self.m_prev[i].zero_()
+            self.hdr[i].fill_(-1)
         self.n_seen = 0
 
     def nbytes(self) -> int:

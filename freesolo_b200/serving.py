@@ -250,18 +250,16 @@ class GraphedDecoder:
         m = self.m
         x = self.x
         pdl = os.environ.get("FSATTN_PDL", "1") == "1"
-        skip_attn = os.environ.get("FSATTN_DEBUG_SKIP_ATTN", "0") == "1"     # timing experiments only
         x.copy_(m.tok_emb(self.tok).view(x.shape))
         if x.shape[0] > 8:
             return self._trunk_step_batched()
         if self.fused_trunk:
-            return self._trunk_step_fused(pdl, skip_attn)
+            return self._trunk_step_fused(pdl)
         for i, blk in enumerate(self.blocks):
             a = self.attn[i]
             wqkv, _ = a._ensure_qkv_cache()
             ops.trunk_gemv(x, wqkv, norm_w=blk.ln1.weight, eps=blk.ln1.eps, out=self.qkv, pdl=pdl)
-            if not skip_attn:
-                a.graph_decode_attn(self.qkv, self.bufs[i], y=self.y, pdl=pdl)
+            a.graph_decode_attn(self.qkv, self.bufs[i], y=self.y, pdl=pdl)
             ops.trunk_gemv(self.y, a.W_o.weight, res=x, out=x, pdl=pdl)
             wgu, _ = blk.ffn._ensure_gu_cache()
             ops.trunk_gemv(x, wgu, norm_w=blk.ln2.weight, eps=blk.ln2.eps, swiglu=True, out=self.act, pdl=pdl)
@@ -270,7 +268,7 @@ class GraphedDecoder:
         self.tok.copy_(self.logits.argmax(dim=-1, keepdim=True))
         self.pos_t.add_(1)
 
-    def _trunk_step_fused(self, pdl: bool, skip_attn: bool):
+    def _trunk_step_fused(self, pdl: bool):
         """The same step with two launches per layer: the attention step, then ONE cooperative kernel for everything up to
         the next layer's QKV projection (W_o + residual, RMSNorm + gate/up + SwiGLU, down + residual, RMSNorm + QKV; after
         the last layer the final norm + LM head), its phases separated by grid-wide barriers instead of launches."""
@@ -282,8 +280,7 @@ class GraphedDecoder:
         ops.trunk_gemv(x, a0._ensure_qkv_cache()[0], norm_w=self.blocks[0].ln1.weight, eps=self.blocks[0].ln1.eps, out=self.qkv, pdl=pdl)
         for i, blk in enumerate(self.blocks):
             a = self.attn[i]
-            if not skip_attn:
-                a.graph_decode_attn(self.qkv, self.bufs[i], y=self.y, pdl=pdl)
+            a.graph_decode_attn(self.qkv, self.bufs[i], y=self.y, pdl=pdl)
             if i + 1 < nL:
                 nb = self.blocks[i + 1]
                 nxt = dict(norm_next_w=nb.ln1.weight, eps_next=nb.ln1.eps, w_next=self.attn[i + 1]._ensure_qkv_cache()[0], out_next=self.qkv)
@@ -324,12 +321,29 @@ class GraphedDecoder:
         self.tok.copy_(self.logits.argmax(dim=-1, keepdim=True))
         self.pos_t.add_(1)
 
+    def _graph_inputs(self) -> list:
+        """The cached tensors whose device addresses a captured step bakes in and that only module-level caches own: the
+        bf16 RoPE tables, the per-head parameter tuple and the fused projection weights of every layer."""
+        keep = []
+        for a, blk in zip(self.attn_core, self.blocks):
+            keep.append(a.rope._bf16)
+            keep.append(getattr(a, "_head_params", None))
+            keep.append(getattr(a, "_w_qkv_cache", None))
+            keep.append(getattr(blk.ffn, "_w_gu_cache", None))
+        return keep
+
     @torch.no_grad()
     def _capture(self):
         torch.cuda.synchronize()
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
             self._trunk_step()
+        # the graph holds raw pointers into these: keep them alive for its lifetime, and notice when a cache replaces one
+        # (a longer RoPE table, a changed parameter) so that the step is captured again instead of reading the old buffer
+        self._graph_keep = self._graph_inputs()
+
+    def _graph_stale(self) -> bool:
+        return any(x is not y for x, y in zip(self._graph_keep, self._graph_inputs()))
 
     @torch.no_grad()
     def step(self):
@@ -343,6 +357,8 @@ class GraphedDecoder:
             for a, c in zip(self.attn_core, self.cache):
                 if a.fsb_enabled:
                     c.fsb_block_change(self.pos, a)
+        if self.graph is not None and self._graph_stale():
+            self.graph = None
         if self.graph is None and self._steps >= self.eager_steps:
             self._capture()
         if self.graph is None:

@@ -264,7 +264,7 @@ def _fsb_layer(g, dev, int8=False, union=True):
     return a, c
 
 
-def _close_rows(got, want, what, max_abs=2e-2, mean_rel=4e-3):
+def _close_rows(got, want, what, max_abs=2e-2):
     """max-abs 2e-2 and mean-rel bar; an element may also differ by one bf16 unit in the last place of the expected
     value (outputs are stored in bf16: a rounding flip at |y| >= 4 is 0.031 by itself)."""
     got, want = got.float().cpu(), want.float().cpu()
@@ -279,8 +279,8 @@ def _close_rows(got, want, what, max_abs=2e-2, mean_rel=4e-3):
 @pytest.mark.parametrize("int8", [False, True])
 def test_fsb_layer_prefill_then_decode(int8):
     """FSAttn with fsb_enabled behind FSKVCache: prefill and a decode run that crosses a block boundary, against the
-    oracle layer on the same bf16 inputs (tolerance: max-abs 2e-2, mean-rel 4e-3 per step as for FS-L decode) and
-    against the reference's own fp32 outputs on the rows whose selections agree."""
+    oracle layer on the same bf16 inputs (max-abs 2e-2, mean-rel 1e-3 per step and over the whole run) and against the
+    reference's own fp32 outputs on the rows whose selections agree (4e-3: the bf16 rounding of inputs and outputs)."""
     import os
     from oracle import fsb
     os.environ["FSATTN_KEEP_SEL"] = "1"
@@ -302,12 +302,13 @@ def test_fsb_layer_prefill_then_decode(int8):
         assert int((diff & (mo > 1e-4)).sum()) == 0, "prefill selections differ outside the margin"
         rows = ~diff.any(1)                                                  # (B, N) rows where every head agrees
         assert rows.float().mean() > 0.95
-        _close_rows(y0.cpu()[rows], yo[rows], "FS-B prefill output vs oracle", mean_rel=2e-3)
+        _close_rows(y0.cpu()[rows], yo[rows], "FS-B prefill output vs oracle")
         ref_rows = (sel0 == torch.from_numpy(g["sel_prefill"]).long()).all(-1).all(1)
         assert ref_rows.float().mean() > 0.9
         _close_rows(y0.cpu()[ref_rows], torch.from_numpy(g["y_prefill"])[ref_rows], "FS-B prefill vs reference fp32",
-                    mean_rel=8e-3)
+                    mean_rel=4e-3)
         n_bad = 0
+        num = den = 0.0             # mean-rel aggregated over the decode run (a single row is a noisy statistic)
         for t in range(T):
             with torch.no_grad():
                 y = a._decode_one(Qd[:, :, N + t], Kd[:, :, N + t], Vd[:, :, N + t], c)
@@ -317,13 +318,16 @@ def test_fsb_layer_prefill_then_decode(int8):
             d = (sel != so[:, :, 0]).any(-1)
             n_bad += int((d & (mo[:, :, 0] > 1e-4)).sum())
             if not d.any():
-                _close_rows(y.view(-1), yo.reshape(-1), f"FS-B decode step {t}", mean_rel=4e-3)
+                _close_rows(y.view(-1), yo.reshape(-1), f"FS-B decode step {t}")
+                num += (y.float().cpu().view(-1) - yo.float().reshape(-1)).abs().sum().item()
+                den += yo.float().abs().sum().item()
                 if not int8:
                     ref_sel = torch.from_numpy(g["sel_decode"][t]).long()
                     if (sel == ref_sel).all():
                         _close_rows(y.view(-1), torch.from_numpy(g["y_decode"][:, t]).reshape(-1),
-                                    f"FS-B decode step {t} vs reference fp32", mean_rel=1e-2)
+                                    f"FS-B decode step {t} vs reference fp32", mean_rel=4e-3)
         assert n_bad == 0, f"{n_bad} decode selections differ outside the margin"
+        assert num / max(den, 1e-12) <= 1e-3, f"FS-B decode outputs: mean-rel over the whole run {num / den:.3e} (<= 1e-3)"
         assert c.state.faults() == (0, 0, 0)
     finally:
         os.environ.pop("FSATTN_KEEP_SEL", None)
@@ -422,3 +426,31 @@ def test_select_other_head_dims_and_batch(D, B):
     sdo, mdo = fsb.fsb_select_decode(qd[:, :, 0].float(), N, K.float(), kbar.cpu(), ce, ncell, tau, tau_u, lam, sigma, scale)
     bad = (sd[:, :, 0] != sdo).any(-1) & (mdo > 1e-4)
     assert int(bad.sum()) == 0
+
+
+def test_second_prefill_on_one_cache_starts_the_forests_over():
+    """A cache that is prefilled again with another prompt must select like a fresh cache: the forests of the first prompt
+    (admitted cells, chunk trees, spines) may not leak into the second."""
+    import os
+    g, Q, K, V = _golden_inputs("randn")
+    N = int(g["N"])
+    dev = _dev()
+    Qd, Kd, Vd = Q.to(dev), K.to(dev), V.to(dev)
+    gen = torch.Generator().manual_seed(77)
+    Q1, K1, V1 = (torch.randn(Q.shape[0], Q.shape[1], N, Q.shape[3], generator=gen).to(torch.bfloat16).to(dev) for _ in range(3))
+    os.environ["FSATTN_KEEP_SEL"] = "1"
+    try:
+        a, c = _fsb_layer(g, dev)
+        with torch.no_grad():
+            a._prefill(Q1, K1, V1, c)                                     # first prompt
+            c.pos = 0
+            y2 = a._prefill(Qd[:, :, :N], Kd[:, :, :N], Vd[:, :, :N], c).clone()   # second prompt, same cache
+            sel2 = a._last_sel[:, :, :N].clone()
+            a_f, c_f = _fsb_layer(g, dev)
+            y_f = a_f._prefill(Qd[:, :, :N], Kd[:, :, :N], Vd[:, :, :N], c_f)
+            sel_f = a_f._last_sel[:, :, :N]
+        assert torch.equal(sel2, sel_f), "selections of a re-used cache differ from a fresh cache"
+        assert torch.equal(y2, y_f)
+        assert torch.equal(c.fsb.m_tot[0], c_f.fsb.m_tot[0]) and torch.equal(c.fsb.m_tot[1], c_f.fsb.m_tot[1])
+    finally:
+        os.environ.pop("FSATTN_KEEP_SEL", None)

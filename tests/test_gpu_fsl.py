@@ -15,6 +15,9 @@ pytestmark = pytest.mark.gpu
 
 KINDS = ["randn", "vocab", "periodic", "lowprec"]
 MAX_ABS, MEAN_REL, MARGIN = 2e-2, 1e-3, 1e-4
+# Against the reference's own fp32 run the bf16 pipeline differs by the bf16 rounding of Q/K/V and of the stored output
+# (2^-9 relative per value, about 2e-3 in the mean) before any kernel arithmetic: that comparison alone has a wider bar.
+REF_FP32_REL = 4e-3
 
 
 @pytest.fixture(scope="module")
@@ -50,6 +53,24 @@ def _close(got, ref, what, max_abs=MAX_ABS, mean_rel=MEAN_REL):
     ma, mr = d.max().item(), (d.mean() / ref.abs().mean().clamp_min(1e-12)).item()
     assert ma <= max_abs and mr <= mean_rel, f"{what}: max-abs {ma:.3e} (<= {max_abs}), mean-rel {mr:.3e} (<= {mean_rel})"
     return ma, mr
+
+
+class _RunError:
+    """Mean-rel error aggregated over a whole decode run: sum |got - want| / sum |want| over every step's row. One row
+    holds only H*D values, so its own mean-rel is a noisy statistic (it keeps a looser bar); the run's must meet MEAN_REL."""
+
+    def __init__(self):
+        self.num = self.den = 0.0
+
+    def add(self, got, ref):
+        got, ref = got.float().cpu().reshape(-1), ref.float().cpu().reshape(-1)
+        self.num += (got - ref).abs().sum().item()
+        self.den += ref.abs().sum().item()
+
+    def check(self, what, bar=MEAN_REL):
+        mr = self.num / max(self.den, 1e-12)
+        assert mr <= bar, f"{what}: mean-rel over the whole run {mr:.3e} (<= {bar})"
+        return mr
 
 
 def _sel_check(got, ref, margin, what):
@@ -190,7 +211,7 @@ def test_window_prefill(dev, kind, impl):
     # the tensor-core kernel multiplies V with probabilities split into bf16 high + low parts (about 16 bits), so it
     # meets the same bar against the exact oracle as the CUDA-core kernel
     _close(got, want.to(torch.bfloat16), f"{kind} window (impl {impl}) vs oracle")
-    _close(got, torch.from_numpy(g["window_prefill"]), f"{kind} window (impl {impl}) vs reference fp32", mean_rel=6e-3)
+    _close(got, torch.from_numpy(g["window_prefill"]), f"{kind} window (impl {impl}) vs reference fp32", mean_rel=REF_FP32_REL)
 
 
 @pytest.mark.parametrize("N,W,pos0", [(1, 512, 0), (31, 512, 0), (513, 512, 0), (700, 64, 5), (300, 0, 0), (1100, 512, 37)])
@@ -228,7 +249,7 @@ def test_readout_combine(dev, kind):
     y0 = ops.readout_combine(Q[:, :, :N].to(dev), K[:, :, :N].to(dev), V[:, :, :N].to(dev), sel.to(dev).contiguous(), None,
                              pd["norm_w"], pd["lrs"], float(g["eps"]), scale=0.125, Bq=128, n_kv=N)
     want0 = fsl.lr_norm_combine(torch.zeros(B, H, N, 64), o, p["norm_w"], p["lrs"], float(g["eps"]))
-    _close(y0, want0, f"{kind} readout alone", mean_rel=3e-3)
+    _close(y0, want0, f"{kind} readout alone")
     srd = sr.to(dev).clone()
     y2 = ops.readout_combine(Q[:, :, :N].to(dev), K[:, :, :N].to(dev), V[:, :, :N].to(dev), sel.to(dev).contiguous(), srd,
                              pd["norm_w"], pd["lrs"], float(g["eps"]), scale=0.125, Bq=128, n_kv=N, out=srd)
@@ -279,20 +300,22 @@ def test_layer_prefill_then_decode(dev, kind, mode):
     # semantics; the output bound applies to the rows where every head reads the reference's cells
     agree = (sel.cpu() == torch.from_numpy(g["sel_prefill"])).all(-1).all(1)           # (B, N)
     assert agree.float().mean() > 0.9
-    _close(y[agree], torch.from_numpy(g["y_prefill"])[agree], f"{kind}/{mode} prefill output vs reference fp32", mean_rel=8e-3)
-    worst = 0.0
+    _close(y[agree], torch.from_numpy(g["y_prefill"])[agree], f"{kind}/{mode} prefill output vs reference fp32", mean_rel=REF_FP32_REL)
+    run = _RunError()
     for t in range(T):
         sl = slice(N + t, N + t + 1)
         yo, so, mo = orc.decode(Q[:, :, sl], K[:, :, sl], V[:, :, sl])
-        _sel_check(sels[t].unsqueeze(2), so, mo, f"{kind}/{mode} decode step {t} (pos {N + t}) selection")
-        ma, _ = _close(ys[t].view(-1), yo.reshape(-1), f"{kind}/{mode} decode step {t} (pos {N + t}) output", mean_rel=4e-3)
-        worst = max(worst, ma)
+        excused = _sel_check(sels[t].unsqueeze(2), so, mo, f"{kind}/{mode} decode step {t} (pos {N + t}) selection")
+        if excused == 0:
+            _close(ys[t].view(-1), yo.reshape(-1), f"{kind}/{mode} decode step {t} (pos {N + t}) output")
+            run.add(ys[t], yo)
+    run.check(f"{kind}/{mode} decode outputs")
     assert st.faults() == (0, 0, 0), f"device status words {st.faults()}"
     # against the reference's fp32 decode outputs (bf16 path: no quantisation error on top)
     if mode == "bf16":
         ref = torch.from_numpy(g["y_decode"])
         got = torch.stack([y_.view(Q.shape[0], -1) for y_ in ys], dim=1)
-        _close(got, ref, f"{kind} decode outputs vs reference fp32", mean_rel=8e-3)
+        _close(got, ref, f"{kind} decode outputs vs reference fp32", mean_rel=REF_FP32_REL)
 
 
 @pytest.mark.parametrize("splits", [1, 2, 8])
@@ -302,7 +325,7 @@ def test_decode_splits_agree(dev, splits):
     _, _, ys_b, sels_b, _ = _run_layer(dev, g, Q, K, V, "int8", splits, T=40)
     for t in range(40):
         assert torch.equal(sels_a[t], sels_b[t]), f"step {t}: selections depend on the split count"
-        _close(ys_b[t], ys_a[t], f"step {t}: outputs with {splits} vs 4 splits", mean_rel=2e-3)
+        _close(ys_b[t], ys_a[t], f"step {t}: outputs with {splits} vs 4 splits")
 
 
 def test_bounded_store_reads_equal_full_int8_store(dev):
@@ -356,12 +379,16 @@ def test_short_prompts_then_decode(dev, N):
         orc = _oracle(g, int8=(mode != "bf16"))
         y0, sel0, mg0 = orc.prefill(Q[:, :, :N], K[:, :, :N], V[:, :, :N])
         _sel_check(sel, sel0, mg0, f"N={N} prefill selection")
-        _close(y, y0, f"N={N}/{mode} prefill output", mean_rel=4e-3)
+        _close(y, y0, f"N={N}/{mode} prefill output")
+        run = _RunError()
         for t in range(T):
             sl = slice(N + t, N + t + 1)
             yo, so, mo = orc.decode(Q[:, :, sl], K[:, :, sl], V[:, :, sl])
-            _sel_check(sels[t].unsqueeze(2), so, mo, f"N={N}/{mode} decode step {t} selection")
-            _close(ys[t].view(-1), yo.reshape(-1), f"N={N}/{mode} decode step {t} output", mean_rel=6e-3)
+            excused = _sel_check(sels[t].unsqueeze(2), so, mo, f"N={N}/{mode} decode step {t} selection")
+            _close(ys[t].view(-1), yo.reshape(-1), f"N={N}/{mode} decode step {t} output")
+            if excused == 0:
+                run.add(ys[t], yo)
+        run.check(f"N={N}/{mode} decode outputs")
         assert st.faults() == (0, 0, 0)
 
 
@@ -390,8 +417,9 @@ def test_other_head_dims_layer(dev, D):
                             n_kv=N)
     y0, sel0, mg0 = orc.prefill(Q[:, :, :N], K[:, :, :N], V[:, :, :N])
     _sel_check(sel[:, :, :N], sel0, mg0, f"D={D} prefill selection")
-    _close(y, y0, f"D={D} prefill output", mean_rel=3e-3)
+    _close(y, y0, f"D={D} prefill output")
     pos_t = torch.zeros((), dtype=torch.int64, device=dev)
+    run = _RunError()
     for t in range(T):
         pos_t.fill_(N + t)
         so = torch.empty(B, H, 4, dtype=torch.int32, device=dev)
@@ -399,8 +427,11 @@ def test_other_head_dims_layer(dev, D):
                                  pd["lrs"], pd["norm_w"], scale=sc, eps=1e-8, sel_out=so, splits=2)
         sl = slice(N + t, N + t + 1)
         yo, s_o, mo = orc.decode(Q[:, :, sl], K[:, :, sl], V[:, :, sl])
-        _sel_check(so.unsqueeze(2), s_o, mo, f"D={D} decode step {t} selection")
-        _close(yd.view(-1), yo.reshape(-1), f"D={D} decode step {t} output", mean_rel=6e-3)
+        excused = _sel_check(so.unsqueeze(2), s_o, mo, f"D={D} decode step {t} selection")
+        _close(yd.view(-1), yo.reshape(-1), f"D={D} decode step {t} output")
+        if excused == 0:
+            run.add(yd, yo)
+    run.check(f"D={D} decode outputs")
 
 
 @pytest.mark.parametrize("kind", KINDS)
@@ -424,7 +455,7 @@ def test_readout_combine_tensor_core_tiles(dev, kind):
     # without a window output, and in place
     y0 = ops.readout_combine(*args[:4], None, *args[5:], scale=0.125, Bq=128, n_kv=N, impl=2)
     want0 = fsl.lr_norm_combine(torch.zeros(B, H, N, 64), o, p["norm_w"], p["lrs"], float(g["eps"]))
-    _close(y0, want0, f"{kind} tensor-core readout alone", mean_rel=3e-3)
+    _close(y0, want0, f"{kind} tensor-core readout alone")
     srd = sr.to(dev).clone()
     y3 = ops.readout_combine(*args[:4], srd, *args[5:], scale=0.125, Bq=128, n_kv=N, out=srd, impl=2)
     assert torch.equal(y3, y2)
