@@ -220,6 +220,7 @@ class GraphedDecoder:
         self.bounded_kv = kv == "bounded"
         hidden = trunk_cached(m, seq, self.cache, last_n=1)
         logits = lm_head(m, hidden[:, -1])
+        self.prefill_logits = logits                # (B, V): the last prompt token's logits
         self.tok = logits.argmax(dim=-1).view(B, 1)
         self.pos = P0
         self.pos_t = torch.full((), P0, dtype=torch.int64, device=self.dev)

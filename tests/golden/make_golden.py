@@ -14,6 +14,11 @@ Fixtures:
                    window branch alone, and a run of decode steps that crosses cell and block boundaries.
   fsb_<kind>.npz   one FS-B layer (serve configuration, two forests) driven the same way: the reference's forest
                    tables, spines and beam cells of the prefill stage, prefill and decode selections, outputs.
+  model_<variant>.npz  the reference's whole FreeSoloLM at a debug size (4 layers x 256, 4 heads x 64, vocabulary cut to
+                   1024), seed-0 init rounded to bf16-representable values, FS-L ("fsl") or FS-B ("fsb", thresholds from
+                   the reference's fsb_calibrate_tau): prefill of 330 tokens + 72 greedy tokens through its KV caches in
+                   fp32, then the same token sequence fed through the module cast to bf16 (teacher forcing, so every
+                   step's logits stay comparable); token ids and the last-token logits of every step of both runs.
   fsl_config1.npz  BASELINE config 1: FSAttn(d_model=1024, 16 heads) with its own seeded projections, 4096-token
                    prefill + 1 decode step, fp32; selections, margins and a strided sample of the outputs.
 """
@@ -387,6 +392,58 @@ def gen_fsb(kind: str, B=1, H=2, D=64, N=2000, T=140, seed=23, q_main=0.3, q_uni
     print("wrote", f"fsb_{kind}.npz", {k_: v_.shape for k_, v_ in out.items() if hasattr(v_, "shape") and v_.ndim})
 
 
+MODEL_DEBUG = dict(vocab_size=1024, d_model=256, n_layers=4, n_heads=4, d_ff=688, max_seq_len=1024)
+
+
+def gen_model(variant: str, P0=330, T=72, seed=0):
+    """The reference's FreeSoloLM + FSKVCache + its greedy loop (experiments/scaling/kv_cache.py:484-526) on CPU."""
+    from bench_efficiency import serve_kwargs
+    from kv_cache import make_caches, _trunk_cached
+    from longctx_infer import _lm_head_fp32, extend_rope_cache
+    from model import FreeSoloLM
+    from src.fsattn import fsb_tree
+    os.environ["FS_PRUNE_KERNEL"] = "1" if variant == "fsl" else "0"
+    kw = serve_kwargs("sparse") if variant == "fsl" else serve_kwargs("fsb", 0.9)
+    gi = torch.Generator().manual_seed(100 + seed)
+    ids = torch.randint(0, MODEL_DEBUG["vocab_size"], (2, P0), generator=gi)
+    warm = torch.randint(0, MODEL_DEBUG["vocab_size"], (1, 512), generator=gi)
+    out = {"variant": variant, "P0": P0, "T": T, "ids": ids.numpy().astype(np.int32), "warm": warm.numpy().astype(np.int32)}
+    for prec in ("fp32", "bf16"):
+        torch.manual_seed(seed)
+        m = FreeSoloLM(**MODEL_DEBUG, **kw).eval()
+        with torch.no_grad():
+            for p_ in m.parameters():                     # both sides hold exactly these weights
+                p_.copy_(p_.to(torch.bfloat16).float())
+        out["w_checksum"] = np.float64(sum(p_.double().sum().item() for p_ in m.parameters()))
+        out["w_abs_checksum"] = np.float64(sum(p_.double().abs().sum().item() for p_ in m.parameters()))
+        extend_rope_cache(m, P0 + T + 64)
+        if prec == "bf16":
+            m = m.to(torch.bfloat16)
+        if variant == "fsb":
+            with torch.no_grad():
+                r1 = fsb_tree.fsb_calibrate_tau(m, [warm], 0.5, target="fsb_tau")
+                r2 = fsb_tree.fsb_calibrate_tau(m, [warm], 0.9, target="fsb_tau_union")
+            out[f"tau_{prec}"] = r1["tau"].numpy()
+            out[f"tau_u_{prec}"] = r2["tau"].numpy()
+        caches = make_caches(m, reserve=T + 8)
+        logits, toks = [], []
+        step_in = ids
+        with torch.no_grad():
+            for t in range(T):
+                hidden = _trunk_cached(m, step_in, caches)
+                lg = _lm_head_fp32(m, hidden[:, -1:, :], 4096)[:, 0, :]
+                nxt = lg.argmax(dim=-1)
+                logits.append(lg.float())
+                toks.append(nxt)
+                # the bf16 run is fed the fp32 run's tokens
+                step_in = (nxt if prec == "fp32" else torch.from_numpy(out["tokens_fp32"][:, t]).long()).unsqueeze(1)
+        out[f"logits_{prec}"] = torch.stack(logits, 1).numpy()          # (B, T, V)
+        out[f"tokens_{prec}"] = torch.stack(toks, 1).numpy().astype(np.int32)
+    os.environ["FS_PRUNE_KERNEL"] = "1"
+    np.savez_compressed(os.path.join(HERE, f"model_{variant}.npz"), **out)
+    print(f"wrote model_{variant}.npz")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("FREESOLO_REFERENCE", "/root/reference"),
@@ -407,6 +464,8 @@ def main():
         "fsb_vocab": lambda: gen_fsb("vocab", N=1500, T=40, seed=29),
         "fsdense_randn": lambda: gen_fs_dense("randn"),
         "fsdense_vocab": lambda: gen_fs_dense("vocab", N=900, T=24, seed=37),
+        "model_fsl": lambda: gen_model("fsl"),
+        "model_fsb": lambda: gen_model("fsb"),
     }
     for name, fn in jobs.items():
         if not only or name in only:

@@ -274,3 +274,54 @@ def test_rms_norm_against_torch(dev, M, d):
     big = torch.zeros(M, d + 64, device=dev, dtype=torch.bfloat16)
     big[:, :d] = x
     assert torch.equal(ops.rms_norm(big[:, :d], w, 1e-6), got)
+
+
+@pytest.mark.parametrize("variant", ["fsl", "fsb"])
+def test_model_logits_against_the_reference_model(dev, variant):
+    """The whole model (trunk, attention, caches, graph decoder) against the reference's own FreeSoloLM + FSKVCache greedy
+    loop at a debug size (tests/golden/model_<variant>.npz: 4 layers x 256, vocabulary 1024, identical bf16-representable
+    weights from the same seeded init). The fixture holds the reference's fp32 run and its own bf16 run fed the same
+    tokens. This path computes in bf16, so against the fp32 logits it is held to what the reference's bf16 run achieves:
+    the residual stream is rounded to bf16 after every layer and a rounding that flips one cell selection changes which
+    tokens a query reads, which is why the reference's own two precisions differ by several percent at this size. Every
+    step is teacher-forced with the fp32 run's tokens so that all steps stay comparable."""
+    from freesolo_b200.serving import FreeSoloLM, GraphedDecoder, serve_kwargs
+    g = load_golden(f"model_{variant}")
+    P0, T = int(g["P0"]), int(g["T"])
+    kw = serve_kwargs("sparse") if variant == "fsl" else serve_kwargs("fsb", 0.9)
+    torch.manual_seed(0)
+    m = FreeSoloLM(vocab_size=1024, d_model=256, n_layers=4, n_heads=4, d_ff=688, max_seq_len=1024, **kw).eval()
+    with torch.no_grad():
+        for p in m.parameters():
+            p.copy_(p.to(torch.bfloat16).float())
+    wsum = sum(p.double().sum().item() for p in m.parameters())
+    assert abs(wsum - float(g["w_checksum"])) < 1e-6, "seeded init differs from the fixture's"
+    m = m.to(dev).to(torch.bfloat16)
+    if variant == "fsb":
+        with torch.no_grad():
+            for i, blk in enumerate(m.blocks):
+                blk.attn.fsattn.fsb_tau.copy_(torch.from_numpy(g["tau_fp32"][i]))
+                blk.attn.fsattn.fsb_tau_union.copy_(torch.from_numpy(g["tau_u_fp32"][i]))
+    ids = torch.from_numpy(g["ids"]).long()
+    ref_tok = torch.from_numpy(g["tokens_fp32"]).long().to(dev)
+    gd = GraphedDecoder(m, ids, Lmax=P0 + T + 8, device=dev, kv="int8" if variant == "fsb" else "bounded")
+    gd.prefill()
+    got = [gd.prefill_logits.float().cpu()]
+    for t in range(1, T):
+        gd.tok.copy_(ref_tok[:, t - 1:t])
+        gd.step()
+        got.append(gd.logits.float().cpu().clone())
+    assert gd.graph is not None and gd.kv_faults() == (0, 0, 0)
+    got = torch.stack(got, 1)                                        # (B, T, V)
+    ref32, ref16 = torch.from_numpy(g["logits_fp32"]), torch.from_numpy(g["logits_bf16"])
+
+    def err(a):
+        d = (a - ref32).abs()
+        return d.max().item(), (d.sum() / ref32.abs().sum()).item()
+    (ma, mr), (ma_r, mr_r) = err(got), err(ref16)
+    agree = (got.argmax(-1) == ref32.argmax(-1)).float().mean().item()
+    agree_r = (ref16.argmax(-1) == ref32.argmax(-1)).float().mean().item()
+    print(f"model {variant}: logits vs the reference's fp32 run: max-abs {ma:.3e}, mean-rel {mr:.3e}, greedy agreement {agree:.4f}; "
+          f"the reference's own bf16 run: max-abs {ma_r:.3e}, mean-rel {mr_r:.3e}, agreement {agree_r:.4f}")
+    assert mr <= 1.25 * mr_r and ma <= 1.5 * ma_r, "further from the fp32 reference than the reference's own bf16 run"
+    assert agree >= agree_r - 0.03
