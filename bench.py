@@ -1,18 +1,26 @@
-"""Benchmark of the FS-L decode hot path: `python bench.py --gpus N --steps K --warmup W [--impl reference]`.
+"""Benchmark of the FS-L / FS-B decode hot path: `python bench.py --gpus N --steps K --warmup W [--impl reference]`.
 
-Workload (the largest single-GPU point): FS-L 341M model (24 layers, d_model 1024, 16 heads x 64, vocab
-32000), random-init bf16 weights, batch 1, uniform random token ids; an untimed prefill of `--ctx` tokens (default 131072)
-through this repo's kernels, then greedy decode. A step = one decoded token through the whole model (one CUDA-graph replay).
+Headline workload (BASELINE config 2 at its largest published context): FS-L 341M model (24 layers, d_model 1024, 16 heads x
+64, vocab 32000), random-init bf16 weights, batch 1, uniform random token ids; an untimed prefill of `--ctx` tokens (default
+131072) through this repo's kernels, then greedy decode. A step = one decoded token through the whole model (one CUDA-graph
+replay).
   value  : tok/s over exactly K replays timed with CUDA events (inputs resident in HBM), max over ranks
   e2e    : tok/s through the public decoder API with the token id copied from pinned host memory every step and the
            sampled token read back to the host every step
-With N > 1 ranks (torchrun) every rank decodes its own sequence (batch sharding, no collective): weak scaling.
-`--impl reference` times the CPU port of the reference's eager decode (oracle/model.py) on the host cores.
+The same JSON line carries, outside the headline's timed region: the roofline of the step's dominant kernel (the trunk
+projection GEMV) and of the attention decode kernel, the prefill figures, the window-attention kernel against the tensor peak,
+short legs at 4k / 16k / 64k for FS-L and FS-B, BASELINE config 3 (FS-B at the headline context), config 4 (743M-class,
+batch 32, 32k, int8 KV) and a CPU baseline.
+With N > 1 ranks (torchrun) every rank decodes its own sequence (batch sharding, no collective): weak scaling; the line then
+also carries a head-sharded leg (one sequence, heads split over the ranks: strong scaling) and config 4's 32 sequences
+split 32/N.
+`--impl reference` times the reference's own eager CPU decode (oracle/ref_cpu.py) on the host cores.
 """
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import subprocess
 import sys
@@ -24,19 +32,24 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-PUBLISHED_FSL_DECODE_TPS_131K = 515.1      # A100-40GB, README.md:62 of the reference
-NCU_DECODE_KERNEL_DRAM_BYTES = 1.87e6       # profiles/fsl_decode_kernel_340m_ncu_full.md
-PUBLISHED_FSB_DECODE_TPS_131K = 462.7      # A100-40GB, README.md:63 of the reference
-PUBLISHED_FSB_PREFILL_KTOKS_131K = 137.8   # A100-40GB, README.md:63 of the reference
-W_BYTES_341M = 2 * (24 * (4 * 1024 ** 2 + 3 * 1024 * 2816) + 32000 * 1024)
+# the reference's published A100-40GB figures (README.md:61-63 of the reference), by context length
+PUBLISHED = {
+    "fsl_decode_tps": {4096: 515.6, 16384: 522.0, 65536: 514.5, 131072: 515.1},
+    "fsl_prefill_ktoks": {4096: 146.4, 16384: 187.5, 65536: 190.2, 131072: 189.8},
+    "fsb_decode_tps": {4096: 504.7, 16384: 497.9, 65536: 473.8, 131072: 462.7},
+    "fsb_prefill_ktoks": {4096: 127.7, 16384: 149.3, 65536: 143.1, 131072: 137.8},
+}
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from ncu captures of these kernels on small cases;
+# None where no capture of the current kernel exists
+NCU_DRAM_BYTES = {"fsl_decode_kernel/340m/b1": 1.87e6, "trunk_gemv_kernel/340m/b1": None}
 
 
 def _peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.isfile(p):
         d = json.load(open(p))
-        return float(d["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
 
 
 class ClockSampler:
@@ -83,9 +96,10 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+# ---- algorithmic bytes ------------------------------------------------------------------------------------------------------
 def attn_bytes_per_layer(B, H, D, W, P, Wc, kk, s, int8=True):
-    """Algorithmic bytes one decode-step launch of one layer moves (window rows of K and V, the pool's
-    mean keys + per-slot scalars, the kk cells read, the new row)."""
+    """Algorithmic bytes one FS-L decode-step launch of one layer moves (window rows of K and V, the pool's mean keys +
+    per-slot scalars, the kk cells read, the new row)."""
     e = 1 if int8 else 2
     win = (W + 1) * D * 2 * e
     pool = (P + Wc) * (D * 4 + 17)
@@ -94,57 +108,50 @@ def attn_bytes_per_layer(B, H, D, W, P, Wc, kk, s, int8=True):
     return B * H * (win + pool + read + new)
 
 
+def fsb_attn_bytes_per_layer(B, H, D, W, kk, s, m_main, m_union, width=16, width2=16, int8=True):
+    """Algorithmic bytes of one FS-B decode step of one layer: the window, both beams' visited nodes (bf16 mean + 36 bytes of
+    node data each; a beam of width w visits min(2^l, 2w) children at level l of a forest of height ceil(log2 m)), the
+    token keys of the <= width + width2 candidate cells for the re-rank, the kk cells' values, the new row."""
+    e = 1 if int8 else 2
+
+    def beam(m, w):
+        h = max(0, math.ceil(math.log2(max(m, 1))))
+        return sum(min(2 ** l, 2 * w) for l in range(1, h + 1)) * (2 * D + 36)
+    win = (W + 1) * D * 2 * e
+    rerank = (width + width2) * s * D * e
+    read = kk * s * D * e
+    new = 2 * D * 2
+    return B * H * (win + beam(m_main, width) + beam(m_union, width2) + rerank + read + new)
+
+
+def weight_bytes(model) -> int:
+    """All linear weights + the tied embedding / LM head, bf16, read once per decode step."""
+    return 2 * sum(p.numel() for _, p in model.named_parameters() if p.dim() > 1)
+
+
+# ---- the reference arm -------------------------------------------------------------------------------------------------------
 def run_reference(args):
-    """The reference's eager decode restated on CPU (oracle/model.py), all host threads, a bounded sample of the workload."""
-    from oracle.model import CpuFSLModel
+    """The reference's own eager decode on the host cores (oracle/_ref), a bounded sample of the headline workload."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    ctx = min(args.ctx, args.cpu_ctx)
+    from oracle.ref_cpu import time_fsl_decode
     steps, warm = min(args.steps, 24), min(args.warmup, 3)
-    torch.set_num_threads(os.cpu_count() or 1)
-    m = CpuFSLModel(max_len=ctx + steps + warm + 64)
-    m.synthetic_context(1, ctx)
-    tok = torch.zeros(1, 1, dtype=torch.long)
-    for _ in range(warm):
-        tok = m.step(tok)
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        tok = m.step(tok)
-    dt = time.perf_counter() - t0
-    tps = steps / dt
-    sample = f"{steps} greedy decode steps of the 341M FS-L model, fp32, batch 1, synthetic {ctx}-token context (the decode step's cost is context-independent for FS-L)"
-    line = {"impl": "reference", "metric": "fsl_decode_tok_s", "value": tps, "unit": "tok/s", "n_gpus": args.gpus, "steps": steps,
-            "warmup": warm, "ms_per_step": dt / steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"FS-L 341M decode, batch 1, ctx {args.ctx} (CPU sample at ctx {ctx})"},
-            "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port", "sample": sample},
-            "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    r = time_fsl_decode(min(args.ctx, args.cpu_ctx), steps, warm)
+    cb = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    line = {"impl": "reference", "metric": "fsl_decode_tok_s", "value": r["value"], "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": steps, "warmup": warm, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"FS-L 340m decode after a {args.ctx}-token prefill, batch 1 (CPU sample: {r['sample']})"},
+            "cpu_baseline": cb,
+            "e2e": {"value": r["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-def cpu_baseline_sample(ctx=4096, steps=12, warm=2):
-    from oracle.model import CpuFSLModel
-    nt = torch.get_num_threads()
-    torch.set_num_threads(os.cpu_count() or 1)
-    m = CpuFSLModel(max_len=ctx + steps + warm + 64)
-    m.synthetic_context(1, ctx)
-    tok = torch.zeros(1, 1, dtype=torch.long)
-    for _ in range(warm):
-        tok = m.step(tok)
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        tok = m.step(tok)
-    dt = time.perf_counter() - t0
-    cores = torch.get_num_threads()
-    torch.set_num_threads(nt)
-    return {"value": steps / dt, "unit": "tok/s", "cores": cores, "kind": "port",
-            "sample": f"{steps} decode steps of the 341M FS-L model (oracle/model.py, fp32, batch 1) at a synthetic {ctx}-token context"}
-
-
+# ---- kernel timers (outside the headline's timed region) ---------------------------------------------------------------
 def time_decode_kernel(gd, n=48):
-    """Average duration of the fused decode-step kernel launched alone, L2 flushed before every launch (in the real step
-    682 MB of weights pass through L2 between two launches of the same layer, so its KV rows are cold)."""
+    """Average duration of the fused attention decode-step kernel launched alone, L2 flushed before every launch (in the real
+    step hundreds of MB of weights pass through L2 between two launches of the same layer, so its KV rows are cold)."""
     from freesolo_b200 import ops
     dev = gd.dev
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
@@ -172,6 +179,40 @@ def time_decode_kernel(gd, n=48):
     return sum(ms) / len(ms), ms[len(ms) // 2]
 
 
+def time_gemv_chain(gd, reps=20):
+    """The trunk projection kernel (trunk_gemv_kernel) in the launch chain it has inside a decode step: the 4 projections
+    of every layer + the LM head, chained by programmatic dependent launch exactly as in the step, captured once and
+    replayed `reps` times with the attention launches left out. Every replay streams all weights (> L2), so the launches
+    run on cold weights as they do in the step. Returns (launches per replay, ms per replay)."""
+    from freesolo_b200 import ops
+    m, x = gd.m, gd.x
+
+    def chain():
+        for i, blk in enumerate(gd.blocks):
+            a = gd.attn[i]
+            ops.trunk_gemv(x, a._ensure_qkv_cache()[0], norm_w=blk.ln1.weight, eps=blk.ln1.eps, out=gd.qkv)
+            ops.trunk_gemv(gd.y, a.W_o.weight, res=x, out=x)
+            ops.trunk_gemv(x, blk.ffn._ensure_gu_cache()[0], norm_w=blk.ln2.weight, eps=blk.ln2.eps, swiglu=True, out=gd.act)
+            ops.trunk_gemv(gd.act, blk.ffn.w_down.weight, res=x, out=x)
+        ops.trunk_gemv(x, m.lm_head.weight, norm_w=m.ln_final.weight, eps=m.ln_final.eps, out=gd.logits)
+    x.zero_(); gd.y.zero_()
+    chain()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        chain()
+    for _ in range(3):
+        g.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return 4 * len(gd.blocks) + 1, e0.elapsed_time(e1) / reps
+
+
 def time_window_kernel(attn, dev, ctx: int, reps: int = 5):
     """Prefill window attention alone (RoPE pre-pass + tcgen05 kernel) on random Q/K/V of the model's shape: useful
     FLOPs 4*H*D*(sum_i min(i+1, W+1)) over its CUDA-event time, against the measured bf16 tensor peak. The operands
@@ -197,8 +238,7 @@ def time_window_kernel(attn, dev, ctx: int, reps: int = 5):
         raise RuntimeError("a bounded wait inside the window kernel ran out")
     ms = sorted(a.elapsed_time(b) for a, b in times[2:])[reps // 2]
     flops = 4.0 * H * D * ((W + 1) * n - W * (W + 1) / 2.0) if n > W else 4.0 * H * D * n * (n + 1) / 2.0
-    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    peak, kind = (float(json.load(open(p))["bf16_tflops"]), "measured") if os.path.isfile(p) else (1590.0, "fallback")
+    _, peak, kind = _peaks()
     return {"kernel": "rope_qk_kernel + window_tc_kernel", "bound": "tensor", "achieved": flops / (ms * 1e-3) / 1e12, "peak": peak,
             "unit": "TFLOP/s", "frac": flops / (ms * 1e-3) / 1e12 / peak, "peak_kind": kind, "ms": ms, "tokens": n, "heads": H,
             "how": "launched alone on random operands larger than L2, median of 5, CUDA events on the launching stream; "
@@ -209,7 +249,6 @@ def timed_prefill(make_decoder, reps: int = 3):
     """The reference's prefill protocol (experiments/scaling/bench_efficiency.py:166-198, `--warm 1 --nmed 3`): one untimed
     prefill at the full context (the allocator's pools and every kernel attribute are warm afterwards), then the median of
     `reps` timed ones, each on a fresh decoder (fresh KV stores / forests). Returns (last decoder, median ms, all ms)."""
-    import torch
     gd = make_decoder()
     gd.prefill()
     torch.cuda.synchronize()
@@ -227,47 +266,210 @@ def timed_prefill(make_decoder, reps: int = 3):
     return gd, sorted(times)[len(times) // 2], times
 
 
-
-def run_fsb_section(args, dev, K, Wm):
-    """BASELINE config 3 on the same box: FS-B 341M (serve configuration with the second forest), thresholds calibrated
-    as the 50th / 90th percentile of the cell ceilings of a 4096-token warm-up, prefill + forest build at args.ctx,
-    then K graph-replayed decode steps (int8 KV store; the forests take in new cells at every 128-token block)."""
-    from freesolo_b200.serving import FreeSoloLM, GraphedDecoder, calibrate_fsb_tau, serve_kwargs
-    ctx = args.ctx
-    torch.manual_seed(0)
-    model = FreeSoloLM.from_config(args.model, max_seq_len=ctx + 512, **serve_kwargs("fsb", 0.9)).to(torch.bfloat16).to(dev).eval()
-    g = torch.Generator().manual_seed(99)
-    warm_ids = torch.randint(0, model.vocab_size, (1, 4096), generator=g)
-    calibrate_fsb_tau(model, warm_ids, 0.5, "fsb_tau")
-    calibrate_fsb_tau(model, warm_ids, 0.9, "fsb_tau_union")
-    ids = torch.randint(0, model.vocab_size, (args.batch, ctx), generator=torch.Generator().manual_seed(4321 + ctx))
-    gd, prefill_ms, _ = timed_prefill(lambda: GraphedDecoder(model, ids, Lmax=ctx + Wm + K + 40, device=dev, kv="int8"))
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+def timed_decode(gd, K, Wm):
+    """Wm untimed steps (the graph is captured there), then K graph replays between two CUDA events. Returns ms."""
     for _ in range(Wm):
         gd.step()
     torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(K):
         gd.step()
     e1.record()
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
+    return e0.elapsed_time(e1)
+
+
+def fsl_step_bytes(model, gd, B, int8=True):
+    a0 = gd.attn_core[0]
+    P, Wc = a0._pool_cfg()
+    kb = attn_bytes_per_layer(B, a0.n_heads, a0.head_dim, a0.window_size, P, Wc, a0.cell_topk, 32, int8)
+    return weight_bytes(model) + len(gd.cache) * kb + B * a0.d_model * 2, kb
+
+
+def fsb_step_bytes(model, gd, B, int8=True):
+    a0 = gd.attn_core[0]
+    nL = len(gd.cache)
+    tot = 0
+    for c in gd.cache:                      # admitted cells differ per layer: every layer's own forest heights
+        fo = c.fsb
+        mm = float(fo.m_tot[0].float().mean())
+        mu = float(fo.m_tot[1].float().mean()) if fo.nf > 1 else 0.0
+        tot += fsb_attn_bytes_per_layer(B, a0.n_heads, a0.head_dim, a0.window_size, a0.fsb_read_top, 32, mm, mu,
+                                        a0.fsb_width, a0.fsb_union_width if fo.nf > 1 else 0, int8)
+    return weight_bytes(model) + tot + B * a0.d_model * 2, tot // nL
+
+
+# ---- legs outside the headline ------------------------------------------------------------------------------------------------
+def _pub(table, ctx, value):
+    ref = PUBLISHED[table].get(ctx)
+    return (value / ref) if ref else None
+
+
+def context_leg(model, variant, ctx, dev, K, Wm, peak):
+    """One shorter context of BASELINE's 4k-131k range: prefill Ktok/s (one untimed run, one timed, fresh stores) and K
+    graph-replayed decode steps, with the step's fraction of the HBM roofline."""
+    from freesolo_b200.serving import GraphedDecoder
+    ids = torch.randint(0, model.vocab_size, (1, ctx), generator=torch.Generator().manual_seed(4321 + ctx))
+    kv = "bounded" if variant == "fsl" else "int8"
+    gd, pms, _ = timed_prefill(lambda: GraphedDecoder(model, ids, Lmax=ctx + Wm + K + 40, device=dev, kv=kv), reps=1)
+    ms = timed_decode(gd, K, Wm)
+    sb, _ = (fsl_step_bytes if variant == "fsl" else fsb_step_bytes)(model, gd, 1)
+    tps, ktoks = K / (ms * 1e-3), ctx / pms
+    out = {"ctx": ctx, "prefill_ktok_s": ktoks, "decode_tok_s": tps, "decode_ms_per_step": ms / K, "decode_steps": K,
+           "step_bytes": sb, "step_frac": sb / (ms / K * 1e-3) / 1e9 / peak,
+           "vs_published_prefill": _pub(f"{variant}_prefill_ktoks", ctx, ktoks),
+           "vs_published_decode": _pub(f"{variant}_decode_tps", ctx, tps), "kv_faults": list(gd.kv_faults())}
+    del gd
+    torch.cuda.empty_cache()
+    return out
+
+
+def make_fsb_model(args, dev, ctx):
+    """the serve configuration with the second forest; thresholds = the 50th / 90th percentile of the
+    cell ceilings of a 4096-token warm-up (the reference's fsb_calibrate_tau)."""
+    from freesolo_b200.serving import FreeSoloLM, calibrate_fsb_tau, serve_kwargs
+    torch.manual_seed(0)
+    model = FreeSoloLM.from_config(args.model, max_seq_len=ctx + 512, **serve_kwargs("fsb", 0.9)).to(torch.bfloat16).to(dev).eval()
+    warm_ids = torch.randint(0, model.vocab_size, (1, 4096), generator=torch.Generator().manual_seed(99))
+    calibrate_fsb_tau(model, warm_ids, 0.5, "fsb_tau")
+    calibrate_fsb_tau(model, warm_ids, 0.9, "fsb_tau_union")
+    return model
+
+
+def time_fsb_select(gd, ctx, dev, reps=3):
+    """The FS-B prefill selection (both beams + re-rank) of one layer alone: layer 0's forests as the prefill left them,
+    random bf16 queries and token keys of the model's shape, median of `reps` CUDA-event timings."""
+    from freesolo_b200 import ops
+    a, fo = gd.attn_core[0], gd.cache[0].fsb
+    g = torch.Generator(device=dev).manual_seed(11)
+    Q, K = (torch.randn(1, a.n_heads, ctx, a.head_dim, device=dev, generator=g).to(torch.bfloat16) for _ in range(2))
+    lam, sigma, _, _ = a.head_params()
+    ts = []
+    for _ in range(reps + 1):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        ops.fsb_select(fo, Q, K, lam, sigma, scale=a.scale, N=ctx, Bq=a._cell_block, width=a.fsb_width, width2=a._fsb_w2(fo),
+                       read_top=a.fsb_read_top, radius_coef=a.fsb_bound_radius_coef)
+        e1.record()
+        ts.append((e0, e1))
+    torch.cuda.synchronize()
+    return sorted(x.elapsed_time(y) for x, y in ts[1:])[reps // 2]
+
+
+def run_fsb_section(args, dev, K, Wm, peak, peak_kind):
+    """FS-B 341M on the same box: prefill + forest build at args.ctx, K graph-replayed decode steps (int8 KV store; the
+    forests take in new cells at every 128-token block), the step's roofline, and the shorter contexts."""
+    from freesolo_b200.serving import GraphedDecoder
+    ctx = args.ctx
+    model = make_fsb_model(args, dev, ctx)
+    ids = torch.randint(0, model.vocab_size, (args.batch, ctx), generator=torch.Generator().manual_seed(4321 + ctx))
+    gd, prefill_ms, _ = timed_prefill(lambda: GraphedDecoder(model, ids, Lmax=ctx + Wm + K + 40, device=dev, kv="int8"))
+    ms = timed_decode(gd, K, Wm)
     fo = gd.cache[0].fsb
     nL = len(gd.cache)
+    sb, kb = fsb_step_bytes(model, gd, args.batch)
+    tps, ktoks = args.batch * K / (ms * 1e-3), args.batch * ctx / prefill_ms
     out = {"workload": f"FS-B {args.model} (two forests, beam 16+16, token-LSE re-rank to 4), prefill + forest build at {ctx}, "
                        f"then {K} decode steps, batch {args.batch}, int8 KV",
-           "decode_tok_s": args.batch * K / (ms * 1e-3), "decode_ms_per_step": ms / K,
-           "prefill_ktok_s": args.batch * ctx / prefill_ms, "prefill_ms": prefill_ms,
-           "vs_published_decode": (args.batch * K / (ms * 1e-3)) / PUBLISHED_FSB_DECODE_TPS_131K if ctx == 131072 else None,
-           "vs_published_prefill": (args.batch * ctx / prefill_ms) / PUBLISHED_FSB_PREFILL_KTOKS_131K if ctx == 131072 else None,
+           "decode_tok_s": tps, "decode_ms_per_step": ms / K, "prefill_ktok_s": ktoks, "prefill_ms": prefill_ms,
+           "vs_published_decode": _pub("fsb_decode_tps", ctx, tps), "vs_published_prefill": _pub("fsb_prefill_ktoks", ctx, ktoks),
+           "roofline": {"what": "whole decode step: weights + per layer window, both beams' visited nodes, the candidates' token "
+                                "keys, the cells read", "bound": "hbm", "step_bytes": sb, "attn_bytes_per_layer": kb,
+                        "achieved": sb / (ms / K * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                        "frac": sb / (ms / K * 1e-3) / 1e9 / peak, "peak_kind": peak_kind},
+           "prefill_select_ms_per_layer": time_fsb_select(gd, ctx, dev),
            "gpu_launches": K * gd.launches_per_step(), "forest_bytes_per_layer": gd.fsb_bytes() // nL,
            "admitted_cells_layer0": {"main": fo.m_tot[0].tolist(), "second": fo.m_tot[1].tolist()},
            "kv_faults": list(gd.kv_faults())}
+    del gd
+    torch.cuda.empty_cache()
+    if not args.no_contexts:
+        out["contexts"] = [context_leg(model, "fsb", c, dev, 32, Wm, peak) for c in (4096, 16384, 65536) if c < ctx]
+    del model
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_config4(dev, K, Wm, peak, peak_kind, batch=32, ctx=32768, dist=None, seed_off=0):
+    """FS-L, the 743M-class model ("800m": 24 x 1536, 16 heads x 96), `batch` sequences of `ctx` tokens on
+    this GPU, full int8 KV store. With `dist` (N > 1) the 32 sequences are split 32/N over the ranks, no collective in the
+    step; the time is the max over ranks. Above 8 sequences per GPU the trunk projections are library GEMMs."""
+    from freesolo_b200.serving import FreeSoloLM, GraphedDecoder, serve_kwargs
+    torch.manual_seed(0)
+    model = FreeSoloLM.from_config("800m", max_seq_len=ctx + 512, **serve_kwargs("sparse")).to(torch.bfloat16).to(dev).eval()
+    ids = torch.randint(0, model.vocab_size, (batch, ctx), generator=torch.Generator().manual_seed(777 + seed_off))
+    gd = GraphedDecoder(model, ids, Lmax=ctx + Wm + K + 40, device=dev, kv="int8")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    gd.prefill()
+    e1.record()
+    torch.cuda.synchronize()
+    pms = e0.elapsed_time(e1)
+    if dist is not None:
+        dist.barrier()
+    ms = timed_decode(gd, K, Wm)
+    world = 1
+    if dist is not None:
+        t = torch.tensor([ms, pms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, pms = t.tolist()
+        world = dist.get_world_size()
+    sb, kb = fsl_step_bytes(model, gd, batch)
+    k_avg, _ = time_decode_kernel(gd, n=24)
+    nL = len(gd.cache)
+    out = {"workload": f"FS-L 800m (24 x 1536, 16 heads x 96), {batch * world} sequences of {ctx} tokens ({batch} per GPU x {world}), "
+                       f"full int8 KV store, {K} graph-replayed decode steps",
+           "decode_tok_s": batch * world * K / (ms * 1e-3), "decode_ms_per_step": ms / K, "decode_steps": K,
+           "prefill_ktok_s": batch * world * ctx / pms, "prefill_ms": pms, "prefill_note": "one cold run",
+           "step_bytes_per_gpu": sb, "step_frac": sb / (ms / K * 1e-3) / 1e9 / peak,
+           "decode_kernel": {"kernel": "fsl_decode_kernel", "bytes_per_launch": kb, "avg_launch_us": k_avg * 1e3,
+                             "achieved": kb / (k_avg * 1e-3) / 1e9, "unit": "GB/s", "frac": kb / (k_avg * 1e-3) / 1e9 / peak,
+                             "peak_kind": peak_kind, "how": "launched alone, L2 flushed before every launch, CUDA events"},
+           "kv_bytes_per_layer": gd.kv_bytes() // nL, "kv_faults": list(gd.kv_faults())}
     del gd, model
     torch.cuda.empty_cache()
     return out
 
 
+def run_head_sharded(args, dev, K, Wm, rank, world, dist):
+    """One sequence, heads split over the ranks (BASELINE config 5's partition on the headline model): rank r owns heads
+    [r H/g, (r+1) H/g), its KV stores and pools; the head outputs meet once per layer in front of W_o. Strong scaling."""
+    from freesolo_b200.parallel import shard_model_heads
+    from freesolo_b200.serving import FreeSoloLM, GraphedDecoder, serve_kwargs
+    ctx = args.ctx
+    torch.manual_seed(0)
+    model = FreeSoloLM.from_config(args.model, max_seq_len=ctx + 512, **serve_kwargs("sparse")).to(torch.bfloat16).to(dev).eval()
+    n_heads = model.blocks[0].attn.fsattn.n_heads
+    shard_model_heads(model, rank, world)
+    ids = torch.randint(0, model.vocab_size, (1, ctx), generator=torch.Generator().manual_seed(4321 + ctx))
+    gd = GraphedDecoder(model, ids, Lmax=ctx + Wm + K + 40, device=dev, kv=args.kv)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    gd.prefill()
+    e1.record()
+    torch.cuda.synchronize()
+    pms = e0.elapsed_time(e1)
+    dist.barrier()
+    ms = timed_decode(gd, K, Wm)
+    t = torch.tensor([ms, pms], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, pms = t.tolist()
+    out = {"workload": f"FS-L {args.model}, ONE sequence of {ctx} tokens, {n_heads} heads split over "
+                       f"{world} GPUs, exchange of the head outputs once per layer, {K} graph-replayed decode steps",
+           "scaling": "strong", "decode_tok_s": K / (ms * 1e-3), "decode_ms_per_step": ms / K,
+           "prefill_ktok_s": ctx / pms, "prefill_ms": pms, "prefill_note": "one cold run", "kv_faults": list(gd.kv_faults())}
+    # a graph that captured collectives keeps the communicator busy: it goes before the process group does
+    gd.graph = None
+    del gd, model
+    import gc
+    gc.collect()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return out
+
+
+# ---- the measured arm ---------------------------------------------------------------------------------------------------------
 def run_ours(args):
     import torch.distributed as dist
     from freesolo_b200.serving import FreeSoloLM, GraphedDecoder, serve_kwargs
@@ -281,12 +483,13 @@ def run_ours(args):
         # a stuck collective aborts the run after two minutes instead of holding the GPUs
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     ctx, K, Wm = args.ctx, args.steps, max(args.warmup, 3)
+    hbm_peak, _, peak_kind = _peaks()
     torch.manual_seed(0)
     model = FreeSoloLM.from_config(args.model, max_seq_len=ctx + 512, **serve_kwargs("sparse")).to(torch.bfloat16).to(dev).eval()
     B = args.batch
     heads = world > 1 and args.shard == "heads"
     if heads:
-        # one sequence, 16/g heads per rank, NCCL all-gather of the head outputs per layer (captured in the step graph)
+        # one sequence, 16/g heads per rank, the head outputs exchanged once per layer inside the step graph
         from freesolo_b200.parallel import shard_model_heads
         shard_model_heads(model, rank, world)
     ids = torch.randint(0, model.vocab_size, (B, ctx), generator=torch.Generator().manual_seed(4321 + ctx + (0 if heads else rank)))
@@ -295,21 +498,12 @@ def run_ours(args):
     warm = GraphedDecoder(model, ids[:, :min(ctx, 2048)], Lmax=min(ctx, 2048) + 64, device=dev, kv=args.kv)
     warm.prefill()
     del warm
-    if os.environ.get("FSATTN_BENCH_TRACE", "0") == "1":
-        torch.cuda.synchronize()
-        print(f"[bench] rank {rank}: warm-up prefill ok", file=sys.stderr, flush=True)
     gd, prefill_ms, prefill_all = timed_prefill(lambda: GraphedDecoder(model, ids, Lmax=ctx + total, device=dev, kv=args.kv))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    def mark(what):
-        if os.environ.get("FSATTN_BENCH_TRACE", "0") == "1":
-            torch.cuda.synchronize()
-            print(f"[bench] rank {rank}: {what} ok", file=sys.stderr, flush=True)
-    mark("prefill")
     for _ in range(Wm):
         gd.step()
     torch.cuda.synchronize()
     assert gd.graph is not None
-    mark("warmup")
 
     def barrier():
         if world > 1:
@@ -325,7 +519,6 @@ def run_ours(args):
         e1.record()
         barrier()
     ms = e0.elapsed_time(e1)
-    mark("timed region")
     # ---- end to end: token id from pinned host memory in, sampled token back to the host, every step --------------
     tok_host = torch.zeros(B, 1, dtype=torch.int64).pin_memory()
     tok_host.copy_(gd.tok.cpu())
@@ -340,70 +533,94 @@ def run_ours(args):
         tok_host.copy_(out_host)
     barrier()
     e2e_s = time.perf_counter() - t0
-    mark("e2e region")
     t = torch.tensor([ms, e2e_s * 1e3], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, e2e_ms = t.tolist()
     faults = gd.kv_faults()
-    if world > 1:
-        # every rank leaves the group together; what follows on rank 0 needs no communication. A graph that captured
-        # NCCL collectives (head sharding) keeps the communicator busy: NCCL's teardown waits for it, so it goes first.
-        barrier()
-        gd.graph = None
-        import gc
-        gc.collect()
-        torch.cuda.synchronize()
-        dist.destroy_process_group()
-        mark("process group closed")
-    if rank != 0:
-        return
-    peak, peak_kind = _peaks()
     a0 = gd.attn_core[0]
-    P, Wc = a0._pool_cfg()
     int8 = args.kv != "bf16"
-    kbytes = attn_bytes_per_layer(B, a0.n_heads, a0.head_dim, a0.window_size, P, Wc, a0.cell_topk, 32, int8)
-    k_avg_ms, k_med_ms = time_decode_kernel(gd)
-    achieved = kbytes / (k_avg_ms * 1e-3) / 1e9
     nL = len(gd.cache)
-    w_bytes = 2 * sum(p.numel() for n_, p in model.named_parameters() if p.dim() > 1)
-    step_bytes = w_bytes + nL * kbytes + B * a0.d_model * 2
+    step_bytes, kbytes = fsl_step_bytes(model, gd, B, int8)
     seqs = B if heads else world * B
     value = seqs * K / (ms * 1e-3)
+    w_mb = weight_bytes(model) / 1e6
     line = {
         "metric": "fsl_decode_tok_s", "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": Wm,
         "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong" if heads else "weak",
-        "vs_baseline": value / PUBLISHED_FSL_DECODE_TPS_131K if (args.model == "340m" and B == 1 and world == 1) else None,
+        "vs_baseline": _pub("fsl_decode_tps", ctx, value) if (args.model == "340m" and B == 1 and world == 1) else None,
         "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"FS-L {args.model} decode after a {ctx}-token prefill, batch {B} per GPU, kv store {args.kv}, greedy, "
                                "one CUDA-graph replay per token", "ctx": ctx, "batch_per_gpu": B, "kv": args.kv,
-                   "l2": "every step streams all weights (682 MB for 340m) > 126 MB L2, no flush needed",
-                   "parallelism": (f"head-sharded x{world}, NCCL all-gather of head outputs per layer" if heads
+                   "l2": f"every step streams all weights ({w_mb:.0f} MB for {args.model}) > 126 MB L2, no flush needed",
+                   "parallelism": (f"head-sharded x{world}, head outputs exchanged once per layer" if heads
                                    else f"batch-sharded x{world}, no collective")},
         "clocks": cs.summary(),
         "e2e": {"value": seqs * K / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 8 * B},
         "gpu_launches": K * (gd.launches_per_step() if B <= 8 else nL),      # above 8 rows the projections are library GEMMs
-        "roofline": {"kernel": "fsl_decode_kernel", "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": NCU_DECODE_KERNEL_DRAM_BYTES if (B == 1 and args.model == "340m") else None,
-                     "traffic_source": "ncu dram__bytes_read+write per launch, profiles/fsl_decode_kernel_340m_ncu_full.md "
-                                       "(captured at ctx 32768; the FS-L decode read does not depend on the context)",
-                     "peak_kind": peak_kind, "bytes_per_launch": kbytes,
-                     "avg_launch_us": k_avg_ms * 1e3, "median_launch_us": k_med_ms * 1e3,
-                     "how": "launched alone with an L2 flush before every launch, CUDA events on the launching stream"},
         "step_roofline": {"step_bytes": step_bytes, "achieved_gbs": step_bytes / (ms / K * 1e-3) / 1e9,
-                          "frac": step_bytes / (ms / K * 1e-3) / 1e9 / peak, "peak_kind": peak_kind},
-        "prefill": {"ktok_s": B * ctx / prefill_ms, "ms": prefill_ms, "runs_ms": prefill_all, "note": "median of 3 after one untimed full-context prefill (the reference's --warm 1 --nmed 3), incl. KV store fill and last-token logits; outside the headline's timed region"},
+                          "frac": step_bytes / (ms / K * 1e-3) / 1e9 / hbm_peak, "peak_kind": peak_kind},
+        "prefill": {"ktok_s": B * ctx / prefill_ms, "ms": prefill_ms, "runs_ms": prefill_all,
+                    "vs_published": _pub("fsl_prefill_ktoks", ctx, B * ctx / prefill_ms) if (args.model == "340m" and B == 1) else None,
+                    "note": "median of 3 after one untimed full-context prefill (the reference's --warm 1 --nmed 3), incl. KV store "
+                            "fill and last-token logits; outside the headline's timed region"},
         "kv_bytes_per_layer": gd.kv_bytes() // nL, "kv_faults": list(faults),
-        "peak_mem_gib": torch.cuda.max_memory_allocated() / 2 ** 30,
     }
+    # ---- rooflines of the step's kernels, measured live (rank 0 reports; every rank runs them so the ranks stay in step) ----
+    k_avg_ms, k_med_ms = time_decode_kernel(gd)
+    dk = {"kernel": "fsl_decode_kernel", "bound": "hbm (latency-bound at batch 1: 1.6 MB per launch)", "bytes_per_launch": kbytes,
+          "avg_launch_us": k_avg_ms * 1e3, "median_launch_us": k_med_ms * 1e3, "achieved": kbytes / (k_avg_ms * 1e-3) / 1e9,
+          "peak": hbm_peak, "unit": "GB/s", "frac": kbytes / (k_avg_ms * 1e-3) / 1e9 / hbm_peak, "peak_kind": peak_kind,
+          "traffic": NCU_DRAM_BYTES.get(f"fsl_decode_kernel/{args.model}/b{B}"),
+          "traffic_source": "ncu dram__bytes_read + dram__bytes_write per launch, 32k-context capture (the FS-L decode read does "
+                            "not depend on the context); null = no capture of this shape",
+          "how": "launched alone with an L2 flush before every launch, CUDA events on the launching stream"}
+    if B <= 8 and not heads:
+        n_launch, chain_ms = time_gemv_chain(gd)
+        wb = weight_bytes(model)
+        line["roofline"] = {
+            "kernel": "trunk_gemv_kernel", "bound": "hbm", "achieved": wb / (chain_ms * 1e-3) / 1e9, "peak": hbm_peak, "unit": "GB/s",
+            "frac": wb / (chain_ms * 1e-3) / 1e9 / hbm_peak, "peak_kind": peak_kind,
+            "traffic": NCU_DRAM_BYTES.get(f"trunk_gemv_kernel/{args.model}/b{B}"),
+            "bytes_per_launch": wb / n_launch, "avg_launch_us": chain_ms * 1e3 / n_launch, "launches_per_step": n_launch,
+            "share_of_step": chain_ms / (ms / K),
+            "why": "the step's dominant kernel: the 4 projections of every layer + the LM head stream all weights once per token",
+            "how": "the step's own chain of projection launches (programmatic dependent launch, attention launches left out) "
+                   "captured once and replayed 20 times between two CUDA events; algorithmic bytes = all weights / launches"}
+        line["decode_kernel_roofline"] = dk
+    else:
+        line["roofline"] = dk
+    line["peak_mem_gib"] = torch.cuda.max_memory_allocated() / 2 ** 30
     if world == 1 and args.model == "340m":
         line["window_roofline"] = time_window_kernel(gd.attn_core[0], dev, ctx)
+    del gd
+    torch.cuda.empty_cache()
+    if world == 1 and args.model == "340m" and B == 1 and not args.no_contexts:
+        line["contexts"] = [context_leg(model, "fsl", c, dev, 32, Wm, hbm_peak) for c in (4096, 16384, 65536) if c < ctx]
+    del model
+    torch.cuda.empty_cache()
     if world == 1 and not args.no_fsb:
-        del gd, model
-        torch.cuda.empty_cache()
-        line["fsb"] = run_fsb_section(args, dev, K, Wm)
+        line["fsb"] = run_fsb_section(args, dev, K, Wm, hbm_peak, peak_kind)
+    if not args.no_config4 and args.model == "340m" and B == 1 and not heads:
+        per = max(1, 32 // world)
+        key = "config4" if world == 1 else "config4_split"
+        line[key] = run_config4(dev, min(K, 24), Wm, hbm_peak, peak_kind, batch=per, dist=dist if world > 1 else None, seed_off=rank)
+    if world > 1 and not heads and not args.no_head_leg and args.model == "340m" and B == 1:
+        line["head_sharded"] = run_head_sharded(args, dev, K, Wm, rank, world, dist)
+        line["head_sharded"]["speedup_vs_one_rank_of_this_run"] = line["head_sharded"]["decode_tok_s"] / (value / world)
+    if world > 1:
+        # every rank leaves the group together; what follows on rank 0 needs no communication
+        barrier()
+        import gc
+        gc.collect()
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
     if world == 1 and not args.no_cpu:
-        line["cpu_baseline"] = cpu_baseline_sample()
+        from oracle.ref_cpu import time_fsl_decode
+        r = time_fsl_decode(args.cpu_sample_ctx, 12, 2)
+        line["cpu_baseline"] = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
     print(json.dumps(line), flush=True)
 
 
@@ -414,15 +631,19 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ctx", type=int, default=131072)
-    ap.add_argument("--cpu-ctx", type=int, default=4096)
+    ap.add_argument("--cpu-ctx", type=int, default=2304, help="context of the reference arm's CPU sample (72 cells fill the FS-L pool)")
+    ap.add_argument("--cpu-sample-ctx", type=int, default=1152, help="context of the cpu_baseline leg inside the measured arm")
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--model", default="340m")
     ap.add_argument("--kv", default="bounded", choices=["bounded", "int8", "bf16"])
     ap.add_argument("--shard", default="batch", choices=["batch", "heads"],
                     help="N > 1: 'batch' = one sequence per rank, no collective (weak scaling); 'heads' = one sequence, heads "
-                         "split over the ranks with an all-gather per layer (strong scaling)")
+                         "split over the ranks, head outputs exchanged once per layer (strong scaling)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-fsb", action="store_true", help="skip the FS-B section (BASELINE config 3) of the N=1 line")
+    ap.add_argument("--no-contexts", action="store_true", help="skip the 4k / 16k / 64k legs")
+    ap.add_argument("--no-config4", action="store_true", help="skip BASELINE config 4 (743M-class, 32 sequences)")
+    ap.add_argument("--no-head-leg", action="store_true", help="N > 1: skip the head-sharded leg")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -116,3 +116,69 @@ def test_fsb_forest_structure_and_selection_properties(data):
     srt = sel.sort(-1).values
     assert not ((srt[..., 1:] == srt[..., :-1]) & (srt[..., 1:] >= 0)).any()
     assert (sel[:, :, -128:] >= 0).all()
+
+
+def test_fsl_selection_of_the_last_blocks_equals_the_oracle(data):
+    """The oracle itself at full size, on the part it can do in seconds: the last four 128-query blocks of the 131 072-token
+    sequence (each sees ~4090 cells; its pool is the stable top-64 of their ceilings plus the eight newest). Selections must
+    be identical wherever the oracle's fp32 margin exceeds 1e-4."""
+    from freesolo_b200 import ops
+    from oracle import fsl
+    Q, kbar, ceil, ncell, dev = data["Q"], data["kbar"], data["ceil"], data["ncell"], data["dev"]
+    nb = N // 128
+    lam = 0.5 + torch.rand(H, generator=torch.Generator().manual_seed(5)) * 2
+    sig = 2.0 + torch.rand(H, generator=torch.Generator().manual_seed(6)) * 60
+    topp = ops.fsl_prefix_topp(ceil, ncell, 128, nb, 64)
+    sel = ops.fsl_select(Q, kbar, ceil, topp, lam.to(dev), sig.to(dev), N=N, ncell=ncell, Bq=128, nb=nb, P=64, Wc=8, kk=4,
+                         scale=0.125).cpu()
+    kb, ce = kbar.cpu(), ceil.cpu()
+    n_diff = n_q = 0
+    for n in range(nb - 4, nb):
+        blk_start = n * 128
+        vis = blk_start // S
+        tp = fsl.stable_topk(ce[:, :, :vis], 64)
+        assert torch.equal(topp.view(1, H, nb, 64)[:, :, n].cpu().long(), tp), f"block {n}: top-P list differs from the oracle"
+        cand_c, ok = fsl.fsl_candidates(tp, blk_start, S, 8)
+        C = cand_c.shape[-1]
+        kbc = torch.gather(kb, 2, cand_c[..., None].expand(1, H, C, D))
+        clc = torch.gather(ce, 2, cand_c)
+        q = Q[:, :, blk_start:blk_start + 128].float().cpu()
+        qpos = blk_start + torch.arange(128, dtype=torch.float32)
+        score = fsl.fsl_scores(q, kbc, clc, cand_c, ok, qpos, lam, sig, 0.125, S)
+        want, margin = fsl._pick(score, cand_c, ok, 4)
+        got = sel[:, :, blk_start:blk_start + 128].long()
+        diff = (got != want.long()).any(-1)
+        assert not (diff & (margin > 1e-4)).any(), f"block {n}: selections differ from the oracle outside the margin"
+        n_diff += int(diff.sum()); n_q += diff.numel()
+    assert n_diff <= 0.02 * n_q
+
+
+def test_fsb_selection_at_16k_equals_the_oracle(data):
+    """FS-B against the oracle at 16 384 tokens (512 cells per row, forests of height 9): two heads, the first blocks that
+    see anything, two in the middle and the last four, exact outside the margin (beam cut-offs and re-rank)."""
+    from freesolo_b200 import ops
+    from oracle import fsb
+    Q, K, kbar, ceil, dev = data["Q"], data["K"], data["kbar"], data["ceil"], data["dev"]
+    n, hs = 16384, [3, 12]
+    nc = n // S
+    Qs, Ks = Q[:, hs, :n].contiguous(), K[:, hs, :n].contiguous()
+    kb, ce = kbar[:, hs, :nc].contiguous(), ceil[:, hs, :nc].contiguous()
+    tau = torch.quantile(ce[0], 0.5, dim=-1)
+    tau_u = torch.quantile(ce[0], 0.9, dim=-1)
+    g = torch.Generator().manual_seed(8)
+    lam = 0.5 + torch.rand(2, generator=g) * 2
+    sig = 2.0 + torch.rand(2, generator=g) * 60
+    fo = ops.FsbForests(kb, ce, tau, tau_u, cap_cells=nc)
+    fo.ingest(nc)
+    sel = ops.fsb_select(fo, Qs, Ks, lam, sig, scale=0.125, N=n).cpu().long()
+    blocks = [1, 2, 37, 64, 124, 125, 126, 127]
+    so, mo = fsb.fsb_select_prefill(Qs.float().cpu(), Ks.float().cpu(), kb.cpu(), ce.cpu(), tau.cpu(), tau_u.cpu(), lam, sig, 0.125,
+                                    blocks=blocks)
+    n_diff = n_q = 0
+    for b in blocks:
+        sl = slice(b * 128, (b + 1) * 128)
+        diff = (sel[:, :, sl] != so[:, :, sl]).any(-1)
+        bad = diff & (mo[:, :, sl] > 1e-4)
+        assert int(bad.sum()) == 0, f"block {b}: {int(bad.sum())} selections differ from the oracle outside the margin"
+        n_diff += int(diff.sum()); n_q += diff.numel()
+    assert n_diff <= 0.05 * n_q
