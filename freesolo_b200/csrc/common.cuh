@@ -51,11 +51,14 @@ __device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {        // one
 }
 
 // four consecutive values starting at element e of a row: from int8 codes (one 32-bit word) or bf16 (one 64-bit word)
+// Exact int8 -> fp32 without the conversion unit: byte c + 128 placed in the mantissa of 2^23 (one byte permute), minus
+// 2^23 + 128 (one exact add) - the integer-to-float instruction runs at a quarter of the rate of these.
 __device__ __forceinline__ void unpack4_i8(uint32_t w, float* o) {
-    o[0] = (float)(int8_t)(w & 0xff);
-    o[1] = (float)(int8_t)((w >> 8) & 0xff);
-    o[2] = (float)(int8_t)((w >> 16) & 0xff);
-    o[3] = (float)(int8_t)(w >> 24);
+    const uint32_t u = w ^ 0x80808080u;
+    o[0] = __fadd_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440)), -8388736.0f);
+    o[1] = __fadd_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441)), -8388736.0f);
+    o[2] = __fadd_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442)), -8388736.0f);
+    o[3] = __fadd_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443)), -8388736.0f);
 }
 __device__ __forceinline__ void unpack4_bf(uint2 w, float* o) {
     o[0] = bf_lo(w.x); o[1] = bf_hi(w.x); o[2] = bf_lo(w.y); o[3] = bf_hi(w.y);

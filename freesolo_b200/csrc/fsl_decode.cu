@@ -65,9 +65,11 @@ __device__ __forceinline__ void raw_floats(const RawRow<D>& r, float sc, float* 
             unpack4_i8(r.w[i].x, lo + 4 * i);
             unpack4_i8(r.w[L::NW + i].x, hi + 4 * i);
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                lo[4 * i + j] = bf_round(f_mul(lo[4 * i + j], sc));
-                hi[4 * i + j] = bf_round(f_mul(hi[4 * i + j], sc));
+            for (int j = 0; j < 4; j += 2) {              // two values per bf16 rounding instruction
+                const uint32_t a = pack_bf2(f_mul(lo[4 * i + j], sc), f_mul(lo[4 * i + j + 1], sc));
+                const uint32_t b = pack_bf2(f_mul(hi[4 * i + j], sc), f_mul(hi[4 * i + j + 1], sc));
+                lo[4 * i + j] = bf_lo(a); lo[4 * i + j + 1] = bf_hi(a);
+                hi[4 * i + j] = bf_lo(b); hi[4 * i + j + 1] = bf_hi(b);
             }
         } else {
             unpack4_bf(r.w[i], lo + 4 * i);
@@ -129,10 +131,9 @@ __device__ __forceinline__ void row_consume(Part<D>& P, const RowFlight<D>& f, c
         for (int i = 0; i < L::NW; i++) { unpack4_bf(f.c[i], c + 4 * i); unpack4_bf(f.s[i], s + 4 * i); }
 #pragma unroll
         for (int j = 0; j < L::DPL; j++) {
-            const float r1 = bf_round(klo[j] * c[j] - khi[j] * s[j]);
-            const float r2 = bf_round(khi[j] * c[j] + klo[j] * s[j]);
-            dot = fmaf(qlo[j], r1, dot);
-            dot = fmaf(qhi[j], r2, dot);
+            const uint32_t rr = pack_bf2(klo[j] * c[j] - khi[j] * s[j], khi[j] * c[j] + klo[j] * s[j]);   // one rounding instruction
+            dot = fmaf(qlo[j], bf_lo(rr), dot);
+            dot = fmaf(qhi[j], bf_hi(rr), dot);
         }
     } else {
 #pragma unroll
@@ -224,6 +225,9 @@ __device__ long long g_dec_stamps[2][16];
 #endif
 
 constexpr int WIN_NF = 3;                      // 8-row groups of window rows a warp keeps in flight
+constexpr int WIN_STAGES = 2;                  // staged window: tiles of WIN_TILE rows in flight per CTA
+constexpr int WIN_TILE = 64;                   // rows per tile = one 8-row group for each of the 8 warps
+constexpr int WIN_CELLS = 40;                  // cells a window may touch: W / 32 + 2 (W <= 1216)
 constexpr int SC_ITERS = (MAXC + 31) / 32;     // scoring rounds: 32 candidates per round over the 8 warps
 
 template <int D>
@@ -245,6 +249,10 @@ struct Smem {
     float lr_rec[D + 2];
     unsigned long long pool_bar;   // mbarrier of the pool's bulk copy
     int pool_timeout;
+    // staged window (many sequences per step): per-cell scales and row bases of the window's cells, stage barriers
+    float win_ks[WIN_CELLS], win_vs[WIN_CELLS];
+    int win_base[WIN_CELLS];
+    unsigned long long stage_bar[WIN_STAGES];
 };
 
 // ---- mbarrier + bulk (TMA) copy helpers; every wait is bounded ----------------------------------------------------
@@ -369,6 +377,164 @@ __device__ __forceinline__ void window_finish(Smem<D>& sm, RowFlight<D>* f, cons
         g0 += WIN_NF * (int64_t)w.nw;
         if (g0 > w.g_hi) break;                 // warp-uniform
         window_issue2<D>(f, w, a, hp, g0, lane);
+    }
+    if (w.gw == 0) {                            // the new token itself: always inside its own window
+        RowFlight<D> c;
+        const bool mine = w.pos_ok && grp == 0;
+        row_issue<D, true>(c, k_in, v_in, nullptr, nullptr, mine, false, cosT + w.pos * D, sinT + w.pos * D, sub);
+        row_consume<D, true>(P, c, qlo, qhi, a.scale);
+    }
+    part_merge_warp<D>(P);
+    part_store<D>(P, sm.wrec[warp], lane);
+    __syncthreads();
+    if (warp == 0) {
+        float l, acc[D / 32];
+        rec_merge<D>(&sm.wrec[0][0], NWARP, D + 2, lane, l, acc);
+        float m = -INFINITY;
+        for (int i = 0; i < NWARP; i++) m = fmaxf(m, sm.wrec[i][0]);
+        if (lane == 0) { out_rec[0] = m; out_rec[1] = l; }
+#pragma unroll
+        for (int j = 0; j < D / 32; j++) out_rec[2 + lane + 32 * j] = acc[j];
+    }
+}
+
+// ---- window branch with the K/V rows staged through shared memory by bulk copies (one CTA per (b,h), int8 stores) ----------
+// With many sequences per step the kernel is bandwidth-bound and per-lane 4-byte loads cannot keep enough bytes in flight.
+// Here thread 0 streams the window in tiles of 64 rows: the int8 rows of K and V (contiguous in the full store, one piece per
+// cell in the slot store) and the rows of the rotary tables, by cp.async.bulk onto an mbarrier, two tiles in flight; the
+// warps consume a tile from shared memory with the same per-row arithmetic, the same row-to-warp assignment and the same
+// merge order as the direct path, so the result is bit-identical to it. Rows of the open cell (bf16, at most 31) and the
+// new token's row are read directly. Stage s holds: K rows [0, 64 D), V rows, cos rows (bf16), sin rows (bf16).
+template <int D>
+struct WinStage {
+    static constexpr int K_OFF = 0, V_OFF = WIN_TILE * D, C_OFF = 2 * WIN_TILE * D, S_OFF = C_OFF + WIN_TILE * D * 2;
+    static constexpr int BYTES = S_OFF + WIN_TILE * D * 2;
+};
+
+// issue the copies of tile i (rows r0 .. r0+63) into stage buffer `buf`; thread 0 only
+template <int D>
+__device__ __forceinline__ void stage_issue(Smem<D>& sm, unsigned char* buf, unsigned long long* bar, const WinCtx<D>& w,
+                                            const fsattn_fsl_decode_t& a, const HeadPtrs& hp, int64_t r0, int c0) {
+    using WS = WinStage<D>;
+    int64_t q_end = r0 + WIN_TILE;                       // int8 rows of this tile: [r0, q_end)
+    if (q_end > w.nq) q_end = w.nq;
+    int64_t t_end = r0 + WIN_TILE;                       // table rows: up to the new token's own position
+    if (t_end > w.pos + 1) t_end = w.pos + 1;
+    uint32_t bytes = 0;
+    if (q_end > r0) bytes += (uint32_t)(q_end - r0) * D * 2;
+    if (t_end > r0) bytes += (uint32_t)(t_end - r0) * D * 4;
+    mbar_expect_tx(bar, bytes);
+    for (int64_t r = r0; r < q_end;) {                   // one piece per cell: rows [r, e)
+        const int64_t cell = r / FSATTN_CELL;
+        int64_t e = (cell + 1) * FSATTN_CELL;
+        if (e > q_end) e = q_end;
+        const int bs = sm.win_base[cell - c0];            // a cell without a slot: any valid rows, masked when consumed
+        const int64_t src_row = (int64_t)(bs < 0 ? 0 : bs) * FSATTN_CELL + (r - cell * FSATTN_CELL);
+        const uint32_t nb = (uint32_t)(e - r) * D;
+        bulk_g2s(buf + WS::K_OFF + (r - r0) * D, hp.kq + src_row * D, nb, bar);
+        bulk_g2s(buf + WS::V_OFF + (r - r0) * D, hp.vq + src_row * D, nb, bar);
+        r = e;
+    }
+    if (t_end > r0) {
+        const uint32_t nb = (uint32_t)(t_end - r0) * D * 2;
+        bulk_g2s(buf + WS::C_OFF, (const bf16*)a.cos + r0 * D, nb, bar);
+        bulk_g2s(buf + WS::S_OFF, (const bf16*)a.sin + r0 * D, nb, bar);
+    }
+}
+
+// before the dependency wait: the window's per-cell scales and row bases into shared memory, barriers, first tiles in flight
+template <int D>
+__device__ __forceinline__ void staged_prologue(Smem<D>& sm, unsigned char* stages, const WinCtx<D>& w, const fsattn_fsl_decode_t& a,
+                                                const HeadPtrs& hp, int tid) {
+    const fsattn_fsl_state_t& st = a.st;
+    const int c0 = (int)(w.lo_row / FSATTN_CELL);
+    const int ncq = (int)(w.nq / FSATTN_CELL);          // completed cells: [0, ncq)
+    if (tid < WIN_CELLS) {
+        const int cell = c0 + tid;
+        float ks = 1.0f, vs = 1.0f;
+        int base = 0;
+        if (w.pos_ok && cell < ncq) {
+            base = cell;
+            if (w.mode == 2) {
+                base = hp.slot_of[cell];
+                if (base < 0) { atomicAdd(st.status + FSATTN_ST_POOL_NO_SLOT, 1); base = -1; }
+            }
+            if (base >= 0) { ks = __bfloat162float(hp.ks[base]); vs = __bfloat162float(hp.vs[base]); }
+        }
+        sm.win_ks[tid] = ks; sm.win_vs[tid] = vs; sm.win_base[tid] = base;
+    }
+    if (tid == 0) {
+        for (int s = 0; s < WIN_STAGES; s++) mbar_init(&sm.stage_bar[s], 1);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    __syncthreads();
+    if (tid == 0 && w.pos_ok) {
+        const int64_t R0 = w.g_lo << 3;
+        const int ntiles = (int)((w.g_hi - w.g_lo) / NWARP) + 1;
+        for (int i = 0; i < WIN_STAGES && i < ntiles; i++) {
+            // a cell without a slot (counted above) leaves its rows out: they are masked when consumed
+            stage_issue<D>(sm, stages + (size_t)i * WinStage<D>::BYTES, &sm.stage_bar[i], w, a, hp, R0 + (int64_t)i * WIN_TILE, c0);
+        }
+    }
+}
+
+template <int D>
+__device__ __forceinline__ void window_finish_staged(Smem<D>& sm, unsigned char* stages, const WinCtx<D>& w, const fsattn_fsl_decode_t& a,
+                                                     const HeadPtrs& hp, const bf16* k_in, const bf16* v_in, float* out_rec, int warp,
+                                                     int lane, int tid) {
+    using L = RowL<D>;
+    using WS = WinStage<D>;
+    const fsattn_fsl_state_t& st = a.st;
+    const int sub = lane & 3, grp = lane >> 2;
+    const bf16* cosT = (const bf16*)a.cos;
+    const bf16* sinT = (const bf16*)a.sin;
+    float qlo[L::DPL], qhi[L::DPL];
+#pragma unroll
+    for (int j = 0; j < L::DPL; j++) { qlo[j] = sm.q_rot[sub * L::DPL + j]; qhi[j] = sm.q_rot[L::HALF + sub * L::DPL + j]; }
+    Part<D> P;
+    P.init();
+    const int c0 = (int)(w.lo_row / FSATTN_CELL);
+    const int64_t R0 = w.g_lo << 3;
+    const int ntiles = w.pos_ok ? (int)((w.g_hi - w.g_lo) / NWARP) + 1 : 0;
+    for (int i = 0; i < ntiles; i++) {
+        const int s = i % WIN_STAGES;
+        unsigned char* buf = stages + (size_t)s * WS::BYTES;
+        bool arrived = mbar_wait_bounded(&sm.stage_bar[s], (uint32_t)(i / WIN_STAGES) & 1u, 1 << 22);
+        if (!arrived && lane == 0) atomicAdd(st.status + FSATTN_ST_BAD_INDEX, 1);
+        const int64_t r0 = R0 + (int64_t)i * WIN_TILE;
+        const int64_t g = w.g_lo + (int64_t)i * NWARP + warp;
+        const int64_t r = (g << 3) + grp;
+        bool valid = arrived && g <= w.g_hi && r >= w.lo_row && r < w.pos;
+        const bool q8 = r < w.nq;                          // warp-uniform: a group never straddles the open cell's start
+        RowFlight<D> f;
+        if (q8) {
+            const int ci = (int)(r / FSATTN_CELL) - c0;
+            const int cidx = (ci >= 0 && ci < WIN_CELLS) ? ci : 0;
+            valid = valid && ci >= 0 && ci < WIN_CELLS && sm.win_base[cidx] >= 0;
+            f.valid = valid; f.i8 = valid;
+            f.ksc = sm.win_ks[cidx]; f.vsc = sm.win_vs[cidx];
+            raw_load<D, true>(f.k, buf + WS::K_OFF + (r - r0) * D, sub, valid);
+            raw_load<D, true>(f.v, buf + WS::V_OFF + (r - r0) * D, sub, valid);
+        } else {
+            const void* kp = valid ? (const void*)(hp.khot + (r - w.nq) * D) : nullptr;
+            const void* vp = valid ? (const void*)(hp.vhot + (r - w.nq) * D) : nullptr;
+            f.valid = valid; f.i8 = false; f.ksc = 1.0f; f.vsc = 1.0f;
+            raw_load<D, false>(f.k, kp, sub, valid);
+            raw_load<D, false>(f.v, vp, sub, valid);
+        }
+        {
+            const bf16* cr = reinterpret_cast<const bf16*>(buf + WS::C_OFF) + (r - r0) * D;
+            const bf16* sr = reinterpret_cast<const bf16*>(buf + WS::S_OFF) + (r - r0) * D;
+#pragma unroll
+            for (int u = 0; u < L::NW; u++) {
+                f.c[u] = valid ? reinterpret_cast<const uint2*>(cr + sub * L::DPL)[u] : make_uint2(0u, 0u);
+                f.s[u] = valid ? reinterpret_cast<const uint2*>(sr + sub * L::DPL)[u] : make_uint2(0u, 0u);
+            }
+        }
+        row_consume<D, true>(P, f, qlo, qhi, a.scale);
+        __syncthreads();                                   // every warp is done with this stage's buffer
+        if (tid == 0 && i + WIN_STAGES < ntiles)
+            stage_issue<D>(sm, buf, &sm.stage_bar[s], w, a, hp, R0 + (int64_t)(i + WIN_STAGES) * WIN_TILE, c0);
     }
     if (w.gw == 0) {                            // the new token itself: always inside its own window
         RowFlight<D> c;
@@ -524,7 +690,8 @@ __device__ __forceinline__ void refresh_pool(Smem<D>& sm, const fsattn_fsl_state
 // MINB: CTAs the compiler must fit per SM. 1 = all the registers it wants (the batch-1 shape: fewer CTAs than SMs, latency
 // is everything); 2 = at most 128 registers, so that two CTAs overlap each other's memory round trips once the grid is
 // larger than the machine (many sequences per step: the kernel is then bandwidth-bound and needs the occupancy).
-template <int D, int MINB>
+// STAGED: the window rows go through shared memory by bulk copies (one CTA per (b,h), int8 stores; see window_finish_staged).
+template <int D, int MINB, bool STAGED>
 __global__ void __launch_bounds__(NWARP * 32, MINB) fsl_decode_kernel(const fsattn_fsl_decode_t a) {
     using L = RowL<D>;
     constexpr int F = D / 8;                  // floats per lane when 8 lanes share a mean key
@@ -542,6 +709,7 @@ __global__ void __launch_bounds__(NWARP * 32, MINB) fsl_decode_kernel(const fsat
     const int C = st.P + st.Wc;
     float* pool_s = reinterpret_cast<float*>(dyn_smem);
     int4* meta_s = reinterpret_cast<int4*>(dyn_smem + (size_t)C * D * 4);
+    unsigned char* stages = dyn_smem + (((size_t)C * ((size_t)D * 4 + 16) + 127) & ~(size_t)127);   // STAGED only
     STAMP(0, 0); STAMP(1, 0);
 
     // "every CTA of the cluster has started": arrive now, wait right before the first distributed-shared-memory access
@@ -592,7 +760,8 @@ __global__ void __launch_bounds__(NWARP * 32, MINB) fsl_decode_kernel(const fsat
     w.gw = (S == 1) ? warp : (rank - 1) * NWARP + warp;
     const bool do_window = (S == 1) || (rank > 0);
     RowFlight<D> wf[WIN_NF];
-    if (do_window) window_issue2<D>(wf, w, a, hp, w.g_lo + w.gw, lane);
+    if (STAGED) staged_prologue<D>(sm, stages, w, a, hp, tid);
+    else if (do_window) window_issue2<D>(wf, w, a, hp, w.g_lo + w.gw, lane);
     if (rank == 0 && !ext) {
         // the pool's bulk copy; the wait is bounded. The position priors of the candidates need no query: compute them now.
         if (!mbar_wait_bounded(&sm.pool_bar, 0, 1 << 22)) {
@@ -629,7 +798,8 @@ __global__ void __launch_bounds__(NWARP * 32, MINB) fsl_decode_kernel(const fsat
             cluster.barrier_wait();                                   // rank 0 is running: its shared memory may be written
             out_rec = cluster.map_shared_rank(&sm.win_recs[rank][0], 0);
         }
-        window_finish<D>(sm, wf, w, a, hp, k_in, v_in, out_rec, warp, lane);
+        if (STAGED) window_finish_staged<D>(sm, stages, w, a, hp, k_in, v_in, out_rec, warp, lane, tid);
+        else window_finish<D>(sm, wf, w, a, hp, k_in, v_in, out_rec, warp, lane);
     }
     STAMP(1, 3);
 
@@ -800,17 +970,19 @@ __global__ void __launch_bounds__(NWARP * 32, MINB) fsl_decode_kernel(const fsat
     STAMP(0, 8);
 }
 
-template <int D, int MINB>
+template <int D, int MINB, bool STAGED>
 int launch_decode_v(const fsattn_fsl_decode_t* a, cudaStream_t stream) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a->splits, a->st.B * a->st.H, 1);
     cfg.blockDim = dim3(NWARP * 32, 1, 1);
-    const size_t dyn = (size_t)(a->st.P + a->st.Wc) * ((size_t)D * 4 + 16);
+    size_t dyn = (size_t)(a->st.P + a->st.Wc) * ((size_t)D * 4 + 16);
+    if (STAGED) dyn = ((dyn + 127) & ~(size_t)127) + (size_t)WIN_STAGES * WinStage<D>::BYTES;
     static size_t opted[16] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dyn > 24 * 1024 && dev >= 0 && dev < 16 && opted[dev] < dyn) {
-        if (cudaFuncSetAttribute(fsl_decode_kernel<D, MINB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) != cudaSuccess) {
+        if (cudaFuncSetAttribute(fsl_decode_kernel<D, MINB, STAGED>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) != cudaSuccess) {
+            (void)cudaGetLastError();
             fs_set_error("fsl_decode_step: cannot opt in to %zu bytes of shared memory", dyn);
             return FSATTN_ELAUNCH;
         }
@@ -827,7 +999,7 @@ int launch_decode_v(const fsattn_fsl_decode_t* a, cudaStream_t stream) {
     attr[1].val.programmaticStreamSerializationAllowed = a->pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, fsl_decode_kernel<D, MINB>, *a);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, fsl_decode_kernel<D, MINB, STAGED>, *a);
     if (e != cudaSuccess) {
         (void)cudaGetLastError();       // the error is reported through the return code; do not leave it pending
         fs_set_error("fsl_decode_step: launch failed: %s", cudaGetErrorString(e));
@@ -845,7 +1017,11 @@ int launch_decode(const fsattn_fsl_decode_t* a, cudaStream_t stream) {
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
     }
     const long ctas = (long)a->splits * a->st.B * a->st.H;
-    return ctas > sms ? launch_decode_v<D, 2>(a, stream) : launch_decode_v<D, 1>(a, stream);
+    // Many sequences per step: one CTA per (b,h) with the window rows staged through shared memory (int8 stores).
+    const bool can_stage = a->splits == 1 && a->st.store_mode != 0 && a->st.W / FSATTN_CELL + 2 <= WIN_CELLS;
+    const bool stage = a->window_path == 2 || (a->window_path == 0 && can_stage && ctas > sms);
+    if (stage) return launch_decode_v<D, 2, true>(a, stream);
+    return ctas > sms ? launch_decode_v<D, 2, false>(a, stream) : launch_decode_v<D, 1, false>(a, stream);
 }
 
 }  // namespace
@@ -884,6 +1060,10 @@ extern "C" int fsattn_fsl_decode_step(const fsattn_fsl_decode_t* a, fsattn_strea
     }
     if (st.store_mode == 2)
         FS_REQUIRE(st.slot_of && st.cell_in && st.n_slots > 0, "fsl_decode_step: bounded store without slot tables");
+    FS_REQUIRE(a->window_path >= 0 && a->window_path <= 2, "fsl_decode_step: window_path %d not in {0,1,2}", a->window_path);
+    FS_UNSUPPORTED(a->window_path == 2 && (a->splits != 1 || st.store_mode == 0 || st.W / FSATTN_CELL + 2 > WIN_CELLS),
+                   "fsl_decode_step: the staged window needs splits = 1, an int8 store and a window of at most %d tokens",
+                   (WIN_CELLS - 2) * FSATTN_CELL);
     FS_UNSUPPORTED(a->ext_sel != nullptr && st.store_mode == 2,
                    "fsl_decode_step: external (FS-B) selections need a full KV store, not the bounded slot store");
     FS_REQUIRE(((uintptr_t)a->q & 15) == 0 && ((uintptr_t)a->k & 15) == 0 && ((uintptr_t)a->v & 15) == 0 && a->in_sb % 8 == 0 && a->in_sh % 8 == 0,

@@ -105,7 +105,7 @@ class FslDecode(C.Structure):
                 ("lam", vp), ("sigma", vp), ("lrs", vp), ("norm_w", vp),
                 ("scale", f32), ("eps", f32),
                 ("y", vp), ("sel_out", vp),
-                ("splits", i32), ("pdl", i32), ("ext_sel", vp)]
+                ("splits", i32), ("pdl", i32), ("ext_sel", vp), ("window_path", i32)]
 
 
 class SlotPrefill(C.Structure):

@@ -387,7 +387,7 @@ def slot_prefill(state: FslDecodeState, K, V, kbar_cells, N: int):
 
 
 def fsl_decode_step(state: FslDecodeState, q, k, v, pos_t, cos, sin, lam, sigma, lrs, norm_w, *, scale: float, eps: float,
-                    y=None, sel_out=None, splits: int = 8, pdl: bool = False, ext_sel=None):
+                    y=None, sel_out=None, splits: int = 8, pdl: bool = False, ext_sel=None, window_path: int = 0):
     """One decode token of one FS-L layer. q,k,v: (B,H,D) bf16 views with equal strides and unit inner stride (e.g. slices
     of a fused QKV projection); pos_t: int64 device scalar; lam/sigma/lrs (H) fp32, norm_w (D) fp32 (all device tensors
     that stay alive until the launch has run). Returns y (B, H*D) bf16."""
@@ -409,6 +409,7 @@ def fsl_decode_step(state: FslDecodeState, q, k, v, pos_t, cos, sin, lam, sigma,
     a.scale, a.eps = float(scale), float(eps)
     a.y, a.sel_out = y.data_ptr(), _p(sel_out)
     a.splits = int(splits)
+    a.window_path = int(window_path)
     a.pdl = 1 if pdl else 0
     if ext_sel is not None:         # FS-B: the cells chosen by fsb_select for this token
         assert ext_sel.is_cuda and ext_sel.dtype == torch.int32 and ext_sel.is_contiguous() and ext_sel.numel() == B * H * state.kk

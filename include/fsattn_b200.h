@@ -218,6 +218,9 @@ typedef struct {
     int32_t pdl; /* 1 = launch with programmatic stream serialization (overlaps the launch with the producer's tail) */
     const int32_t* ext_sel; /* optional (B,H,kk) int32: cells chosen by fsattn_fsb_select for this token (FS-B layers); the
                              * kernel then skips its own pool and scoring. Full stores (bf16, int8) only. NULL for FS-L. */
+    int32_t window_path; /* how the window rows reach the SMs: 0 = chosen by the library (staged once B*H*splits exceeds the SM
+                          * count), 1 = per-lane loads, 2 = staged through shared memory by bulk copies (needs splits = 1
+                          * and an int8 store). Both give the same bits. */
 } fsattn_fsl_decode_t;
 FSATTN_API int fsattn_fsl_decode_step(const fsattn_fsl_decode_t* a, fsattn_stream_t stream);
 

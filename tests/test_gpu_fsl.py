@@ -256,7 +256,7 @@ def test_readout_combine(dev, kind):
     assert torch.equal(y2, y)
 
 
-def _run_layer(dev, g, Q, K, V, mode, splits, T=None):
+def _run_layer(dev, g, Q, K, V, mode, splits, T=None, window_path=0):
     """Prefill + T decode steps of one layer through ops; returns (y_prefill, sel_prefill, [y_t], [sel_t], state)."""
     from freesolo_b200 import ops
     N = int(g["N"]); T = int(g["T"]) if T is None else T
@@ -281,7 +281,8 @@ def _run_layer(dev, g, Q, K, V, mode, splits, T=None):
         pos_t.fill_(N + t)
         so = torch.empty(B, H, 4, dtype=torch.int32, device=dev)
         yd = ops.fsl_decode_step(st, Qd[:, :, N + t], Kd[:, :, N + t], Vd[:, :, N + t], pos_t, cos, sin, pd["lam"], pd["sigma"],
-                                 pd["lrs"], pd["norm_w"], scale=0.125, eps=float(g["eps"]), sel_out=so, splits=splits)
+                                 pd["lrs"], pd["norm_w"], scale=D ** -0.5, eps=float(g["eps"]), sel_out=so, splits=splits,
+                                 window_path=window_path)
         ys.append(yd.clone()); sels.append(so)
     return y, sel[:, :, :N], ys, sels, st
 
@@ -316,6 +317,50 @@ def test_layer_prefill_then_decode(dev, kind, mode):
         ref = torch.from_numpy(g["y_decode"])
         got = torch.stack([y_.view(Q.shape[0], -1) for y_ in ys], dim=1)
         _close(got, ref, f"{kind} decode outputs vs reference fp32", mean_rel=REF_FP32_REL)
+
+
+@pytest.mark.parametrize("mode", ["int8", "bounded"])
+@pytest.mark.parametrize("N", [1000, 40, 300])
+def test_decode_staged_window_is_bit_identical(dev, mode, N):
+    """The window rows staged through shared memory by bulk copies (the many-sequences path) against per-lane loads: same
+    per-row arithmetic, same row-to-warp assignment, same merge order, so the outputs and selections are identical bit for
+    bit - over a run that closes cells, refreshes the block's pool, frees slots, and (N = 40, 300) starts with a window that
+    is still growing."""
+    g, Q, K, V = _g("randn")
+    T = 300
+    rep = 2
+    Q2, K2, V2 = (torch.cat([t] * rep, dim=2) for t in (Q, K, V))
+    g2 = dict(g); g2["N"] = np.int64(N); g2["T"] = np.int64(T)
+    _, _, ys_a, sels_a, st_a = _run_layer(dev, g2, Q2, K2, V2, mode, 1, T=T, window_path=1)
+    _, _, ys_b, sels_b, st_b = _run_layer(dev, g2, Q2, K2, V2, mode, 1, T=T, window_path=2)
+    for t in range(T):
+        assert torch.equal(sels_a[t], sels_b[t]), f"step {t}: selections differ"
+        assert torch.equal(ys_a[t], ys_b[t]), f"step {t}: outputs differ between the staged and the direct window"
+    assert st_a.faults() == (0, 0, 0) and st_b.faults() == (0, 0, 0)
+
+
+@pytest.mark.parametrize("D", [96, 128])
+def test_decode_staged_window_other_head_dims(dev, D):
+    from freesolo_b200 import ops
+    B, H, N, T = 3, 2, 700, 70
+    gen = torch.Generator().manual_seed(D + 1)
+    Q, K, V = (torch.randn(B, H, N + T, D, generator=gen).to(torch.bfloat16).to(dev) for _ in range(3))
+    lam, sig, lrs, nw = (torch.ones(H, device=dev) * 1.5, torch.ones(H, device=dev) * 6, torch.ones(H, device=dev) * 0.3,
+                         torch.ones(D, device=dev))
+    cos, sin = (t.to(dev) for t in fsl.rope_tables(D, 1024, torch.bfloat16))
+    outs = []
+    for path in (1, 2):
+        st = ops.FslDecodeState(B, H, D, N + T, dev, mode="int8")
+        st.prefill(K[:, :, :N], V[:, :, :N], N)
+        pos_t = torch.zeros((), dtype=torch.int64, device=dev)
+        ys = []
+        for t in range(T):
+            pos_t.fill_(N + t)
+            ys.append(ops.fsl_decode_step(st, Q[:, :, N + t], K[:, :, N + t], V[:, :, N + t], pos_t, cos, sin, lam, sig, lrs, nw,
+                                          scale=D ** -0.5, eps=1e-8, splits=1, window_path=path).clone())
+        outs.append(torch.stack(ys))
+        assert st.faults() == (0, 0, 0)
+    assert torch.equal(outs[0], outs[1])
 
 
 @pytest.mark.parametrize("splits", [1, 2, 8])
