@@ -2,4 +2,4 @@
 attribute names; the computation runs in the sm_100a kernels of libfsattn_b200)."""
 from .attention import FSAttn, RMSNorm  # noqa: F401
 from .kv_cache import FSKVCache, make_caches  # noqa: F401
-from . import kv_int8, kv_bounded  # noqa: F401
+from . import kv_int8, kv_bounded, fsb_tree, fsb_prefill, fsl_select_cuda  # noqa: F401

@@ -108,6 +108,29 @@ def _side_stream(device):
     return _SIDE_STREAMS[key]
 
 
+def _pool_from_stats(kbar, ceil, slot_of, blk_start: int, s: int, P: int, Wc: int) -> dict:
+    """Pool dictionary (keys of the reference's _build_decode_pool) from the visible cells' statistics. kbar is indexed by
+    cell, or by slot when slot_of (B,H,cells) is given (bounded store)."""
+    B, H, M_vis = ceil.shape
+    Pk = min(P, M_vis)
+    topP = ceil.argsort(dim=-1, descending=True, stable=True)[..., :Pk]
+    hi = blk_start // s - 1
+    near = (hi - torch.arange(Wc, device=ceil.device)).expand(B, H, Wc)
+    cand = torch.cat([topP, near], dim=-1)
+    valid = cand >= 0
+    cand_c = cand.clamp(min=0)
+    vis = ((cand_c + 1) * s <= blk_start) & valid
+    C = cand.shape[-1]
+    tri = torch.tril(torch.ones(C, C, dtype=torch.bool, device=ceil.device), diagonal=-1)
+    dup = ((cand_c[..., None, :] == cand_c[..., :, None]) & tri).any(dim=-1)
+    ok = vis & ~dup
+    rows = cand_c if slot_of is None else torch.gather(slot_of.long(), 2, cand_c).clamp(min=0)
+    D = kbar.shape[-1]
+    kb = torch.gather(kbar, 2, rows[..., None].expand(B, H, C, D))
+    return {"M_vis": M_vis, "C": C, "cand_c": cand_c, "ok_cell": ok, "Kbar_cand": kb, "Kbar_cand_t": kb.transpose(2, 3).contiguous(),
+            "ceil_cand": torch.gather(ceil, 2, cand_c), "cen_cand": (cand_c.float() + 0.5) * s}
+
+
 class FSAttn(nn.Module):
     VARIANTS = ("cell_topk",)
 
@@ -448,6 +471,40 @@ class FSAttn(nn.Module):
                                 scale=self.scale, eps=self.lr_norm.eps, y=buf.get("y"), splits=self._splits(st.B),
                                 ext_sel=ext)
         return self.W_o(y.view(B, 1, dm))
+
+    def graph_decode_layer_fsb(self, x, cache, buf):
+        """src/fsattn/attention.py:1450-1491: the FS-B layer's decode token inside a captured whole-step graph, the cache
+        passed explicitly. The forests must have been brought to the token's block (fsb_tree.fsb_decode_prepare_all /
+        cache.fsb_block_change) outside the graph."""
+        return self.graph_decode_layer(x, dict(buf, cache=cache))
+
+    @torch.no_grad()
+    def _build_decode_pool(self, cache, blk_start, s, dev, need_tokens: bool = True, out: dict | None = None):
+        """The candidate pool of the decode block starting at blk_start as the reference hands it to its decode kernels
+        (src/fsattn/attention.py:1313-1369): top-P cells by (ceiling desc, index asc) among the visible ones, then the Wc
+        newest. The decode-step kernel of this library refreshes its own pool on the device; this method serves callers
+        that want the pool itself (inspection, tests). Returns {"empty": True} when nothing is visible."""
+        if getattr(cache, "bounded_kv", False):
+            if need_tokens:
+                cache._no_history("_build_decode_pool(need_tokens=True)")
+            return cache.bounded_pool(blk_start, out=out)
+        P, Wc = self._pool_cfg()
+        kbar, ceil, ncell = cache.completed_cells()
+        M_vis = min(blk_start // s, ncell)
+        if M_vis <= 0 or ncell <= 0:
+            return {"empty": True}
+        return _pool_from_stats(kbar[:, :, :M_vis], ceil[:, :, :M_vis], None, blk_start, s, P, Wc)
+
+    @torch.no_grad()
+    def _build_dense_decode_pool(self, cache, blk_start, s, dev, out: dict | None = None):
+        """src/fsattn/attention.py:1278-1311: the dense FS variant's "pool" is every visible cell."""
+        kbar, ceil, ncell = cache.completed_cells()
+        M_vis = min(blk_start // s, ncell)
+        if M_vis <= 0 or ncell <= 0:
+            return {"empty": True}
+        cells = torch.arange(M_vis, device=ceil.device)
+        return {"dense": True, "M_vis": M_vis, "C": M_vis, "Kbar_cand": kbar[:, :, :M_vis], "ceil_cand": ceil[:, :, :M_vis],
+                "cen_cand": (cells.float() + 0.5) * s, "cand_c": cells.expand(ceil.shape[0], ceil.shape[1], M_vis)}
 
     def graph_decode_attn(self, qkv, buf, y=None, pdl=True):
         """The attention part of one decode token given the fused projection qkv (B, 3*d) bf16: returns W_o's input

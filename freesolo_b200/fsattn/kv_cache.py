@@ -35,6 +35,7 @@ class FSKVCache:
         self.state: ops.FslDecodeState | None = None
         self.pos_t = None               # device int64 scalar mirroring pos for eager decode steps
         self._ncell = 0
+        self._prefill_cell_stats = None  # (kbar, ceil) handed over by the layer's own prefill, consumed by prefill()
         self._kbar = None               # statistics of the last prefill when retain_kv=False
         self._ceil = None
         self._lr_decode_pool = None
@@ -85,8 +86,10 @@ class FSKVCache:
         experiments/scaling/kv_cache.py:184-189)."""
         B, H, N, D = K.shape
         ncell = N // self.s
+        handed, self._prefill_cell_stats = self._prefill_cell_stats, None
+        cell_stats = handed if cell_stats is None else cell_stats
         if cell_stats is not None:
-            kbar, ceil = cell_stats
+            kbar, ceil = cell_stats[-2:]            # the reference hands (K, Kbar, ceil); (Kbar, ceil) is accepted too
         else:
             kbar, ceil = ops.cell_stats(K, ncell)
         self._ncell = ncell
@@ -182,6 +185,44 @@ class FSKVCache:
 
     def slot_table(self):
         return self.state.slot_of if self.bounded_kv else None
+
+    def bounded_pool(self, blk_start, out=None):
+        """The bounded store's candidate pool of the block starting at blk_start (experiments/scaling/kv_cache.py:79-81,
+        src/fsattn/kv_bounded.py:175-221), from its cell-indexed ceilings and slot-indexed mean keys. Read-only here:
+        slots are freed by the decode-step kernel at its own block refresh."""
+        from .attention import _pool_from_stats
+        st = self.state
+        M_vis = min(blk_start // self.s, self.pos // self.s)
+        if M_vis <= 0:
+            return {"empty": True}
+        return _pool_from_stats(st.kbar, st.ceil[:, :, :M_vis], st.slot_of, blk_start, self.s, st.P, st.Wc)
+
+    def graph_kv(self):
+        """(mode, args) a captured decode step reads KV through (experiments/scaling/kv_cache.py:90-99)."""
+        if self.bounded_kv:
+            self._no_history("graph_kv")
+        st = self.state
+        if st is None:
+            return (None, None)
+        if st.mode == "bf16":
+            return ("bf16", (st.kbuf, st.vbuf))
+        return ("int8", self.int8_state())
+
+    def rerank_keys(self):
+        """What the FS-B re-rank reads token keys from (experiments/scaling/kv_cache.py:101-107): the int8 read state, or
+        the bf16 history."""
+        if self.bounded_kv:
+            self._no_history("rerank_keys")
+        st = self.state
+        if st.mode == "bf16":
+            return st.kbuf
+        nq = torch.full((), (self.pos // self.s) * self.s, dtype=torch.int64, device=st.kq.device)
+        return _kvi.Int8Keys(st.kq, st.ks, st.khot, nq, self.s)
+
+    def row_capacity(self) -> int:
+        if self.bounded_kv:
+            self._no_history("row_capacity")
+        return 0 if self.state is None else self.state.cap_rows
 
     def lr_tokens(self):
         """bf16 (K, V) over the stored history [0, pos) (experiments/scaling/kv_cache.py:458-464); int8 mode materialises."""
