@@ -16,19 +16,14 @@
 // Every mbarrier wait is bounded; on a timeout the CTA records it in *status, stops issuing work and still frees its TMEM.
 //
 // FLOPs per CTA: (W/64+2) tiles * (2*128*64*64 + 2*2*128*64*64); algorithmic FLOPs per query 4*D*min(i+1, W+1).
-#include <cuda.h>
-#include <cuda_fp16.h>
-
-#include "common.cuh"
+#include "tc_common.cuh"
 
 namespace {
 
-constexpr int TC_BM = 128;          // queries per CTA
 constexpr int TC_BN = 64;           // keys per tile
 constexpr int TC_D = 64;
 constexpr int TC_THREADS = 192;     // 4 softmax warps (one per TMEM lane quarter), TMA producer, MMA issuer
 constexpr int TC_SOFTMAX_THREADS = 128;
-constexpr int TC_WAIT_ITERS = 1 << 24;
 constexpr int TC_TMEM_COLS = 256;   // S0 | S1 | PV0 | PV1, 64 columns each
 constexpr int TC_TILE_BYTES = TC_BN * TC_D * 2;      // one K or V tile: 64 rows of 128 bytes
 
@@ -43,93 +38,6 @@ constexpr int SM_TOTAL = SM_BAR + 256;
 enum { BAR_Q = 0, BAR_KV_FULL = 1, BAR_KV_EMPTY = BAR_KV_FULL + TC_KV_STAGES, BAR_S_FULL = BAR_KV_EMPTY + TC_KV_STAGES,
        BAR_P_FULL = BAR_S_FULL + 2, BAR_PV_FULL = BAR_P_FULL + 2, BAR_PV_FREE = BAR_PV_FULL + 2, BAR_COUNT = BAR_PV_FREE + 2 };
 static_assert(BAR_COUNT * 8 <= 256, "mbarrier area");
-
-__device__ __forceinline__ uint32_t s_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void bar_init(uint64_t* bar, int count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(s_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void bar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(s_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void bar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(s_u32(bar)), "r"(bytes) : "memory");
-}
-// bounded wait; gives up early once another thread of the CTA has raised the abort flag
-__device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity, volatile int* abortp) {
-    const uint32_t addr = s_u32(bar);
-    for (int i = 0; i < TC_WAIT_ITERS; i++) {
-        if ((i & 63) == 63 && *abortp) return false;
-        uint32_t done;
-        asm volatile("{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}"
-                     : "=r"(done) : "r"(addr), "r"(parity) : "memory");
-        if (done) return true;
-    }
-    return false;
-}
-
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
-    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
-                 ::"r"(s_u32(dst)), "l"(map), "r"(s_u32(bar)), "r"(c0), "r"(c1), "r"(c2) : "memory");
-}
-__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3, uint64_t* bar) {
-    asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];"
-                 ::"r"(s_u32(dst)), "l"(map), "r"(s_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3) : "memory");
-}
-
-// shared-memory matrix descriptor, 128-byte swizzle, 8-row groups 1024 bytes apart (K-major and MN-major tiles of 128-byte rows)
-__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr) {
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr & 0x3ffff) >> 4);           // start address
-    d |= (uint64_t)1 << 16;                            // leading byte offset (unused with one 128-byte atom per row)
-    d |= (uint64_t)(1024 >> 4) << 32;                  // stride byte offset: next 8-row group
-    d |= (uint64_t)1 << 46;                            // descriptor version (Blackwell)
-    d |= (uint64_t)2 << 61;                            // SWIZZLE_128B
-    return d;
-}
-
-// instruction descriptor: (bf16 | fp16) x bf16 -> fp32, M = 128, N = n, A K-major (a_bf16 = 0: fp16), B K-major (b_mn = 0) or
-// MN-major (b_mn = 1)
-__device__ __forceinline__ uint32_t instr_desc(int n, int b_mn, int a_bf16) {
-    return (1u << 4) | ((uint32_t)a_bf16 << 7) | (1u << 10) | ((uint32_t)b_mn << 16) | ((uint32_t)(n >> 3) << 17) |
-           ((uint32_t)(TC_BM >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, int accumulate) {
-    asm volatile("{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\ntcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
-                 ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
-}
-// the same product with the A operand (128 rows x 16 bf16, lane = row, 8 packed 32-bit columns) read from tensor memory
-__device__ __forceinline__ void umma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc, int accumulate) {
-    asm volatile("{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\ntcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}"
-                 ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
-}
-// eight 32-bit registers of this thread's TMEM lane into eight consecutive columns
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};"
-                 ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]) : "memory");
-}
-__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(s_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
-    uint32_t r[32];
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-                 "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-                   "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-                   "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-                 : "r"(taddr) : "memory");
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
-}
-
 
 // ---- pass 0: rotate Q and K into the workspace ----------------------------------------------------------------------
 __global__ void __launch_bounds__(256) rope_qk_kernel(const fsattn_window_prefill_t a, bf16* qr, bf16* kr) {
@@ -401,29 +309,6 @@ window_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
 }  // namespace
 
 // ---- host side -------------------------------------------------------------------------------------------------------------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
-                                  const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    if (fn == nullptr) {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    }
-    return fn;
-}
-
-static bool make_map(CUtensorMap* m, void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_bytes, const cuuint32_t* box) {
-    cuuint32_t es[4] = {1, 1, 1, 1};
-    EncodeTiledFn fn = encode_fn();
-    if (fn == nullptr) return false;
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, base, dims, strides_bytes, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 size_t fs_window_prefill_tc_workspace(const fsattn_window_prefill_t* a) {
     return (size_t)2 * a->B * a->H * a->N * TC_D * sizeof(bf16);
 }

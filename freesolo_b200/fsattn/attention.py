@@ -293,8 +293,8 @@ class FSAttn(nn.Module):
             raise NotImplementedError("sel_content_only is not implemented")
         if self.cell_stride != ops.CELL:
             raise NotImplementedError(f"cell_stride {self.cell_stride}: the kernels are specialised for {ops.CELL}")
-        if self._is_dense_lr() and not self.fsb_enabled:
-            raise NotImplementedError("the dense FS variant (cell_prune_kernel=0) is not implemented")
+        if self._is_dense_lr() and not self.fsb_enabled and (self.head_dim != 64 or self.cell_topk > 4):
+            raise NotImplementedError("the dense FS variant (cell_prune_kernel=0) is built for head_dim 64 and cell_topk <= 4")
 
     def _pool_cfg(self):
         return (self._prune_cfg("cell_prune_pool", "FS_PRUNE_POOL", 64), self._prune_cfg("cell_prune_window", "FS_PRUNE_WINDOW", 8))
@@ -401,6 +401,13 @@ class FSAttn(nn.Module):
                                  width2=self._fsb_w2(fo), read_top=self.fsb_read_top,
                                  radius_coef=self.fsb_bound_radius_coef)
             margin = None
+        elif self._is_dense_lr():
+            # dense FS (src/fsattn/attention.py:362-423): every cell completed before the query's block is a candidate
+            if Bq == self._cell_block:
+                sel = ops.fs_dense_select(Q, kbar, ceil, lam, sigma, N=N, ncell=ncell, Bq=Bq, nb=nb, kk=kk, scale=self.scale)
+            else:       # a prompt shorter than one query block: block 0 sees no completed cell
+                sel = torch.full((B, H, nb * Bq, kk), -1, dtype=torch.int32, device=Q.device)
+            margin = None
         else:
             st = cache.state
             topp = getattr(st, "prefill_topp", None) if st is not None else None
@@ -436,6 +443,8 @@ class FSAttn(nn.Module):
         if self.fsb_enabled:
             cache.fsb_block_change(cache.pos, self)
             ext = self._fsb_decode_select(q, st, cache, pos_t, lam, sigma)
+        elif self._is_dense_lr():
+            ext = self._dense_decode_select(q, st, pos_t, lam, sigma)
         y = ops.fsl_decode_step(st, q, k, v, pos_t, cos, sin, lam, sigma, lrs, norm_w, scale=self.scale,
                                 eps=self.lr_norm.eps, y=y, sel_out=sel_out, splits=self._splits(st.B), ext_sel=ext)
         cache.advance_in_place()
@@ -454,6 +463,17 @@ class FSAttn(nn.Module):
                               width2=self._fsb_w2(fo), read_top=self.fsb_read_top,
                               radius_coef=self.fsb_bound_radius_coef, pos=pos_t, kq=st.kq, ks=st.ks, pdl=pdl)
 
+    def _dense_decode_select(self, q, st, pos_t, lam, sigma, pdl=False):
+        """src/fsattn/attention.py:1159-1185: the dense variant's decode query scores every cell completed before its query
+        block (statistics of the layer's own KV state). q (B,H,D) view -> (B,H,kk) int32 for the decode step's ext_sel."""
+        if st.mode == "bounded":
+            raise NotImplementedError("the dense FS variant reads any completed cell: it needs a full KV store")
+        splits = 8
+        while splits > 1 and st.B * st.H * splits > 296:
+            splits //= 2
+        return ops.fs_dense_decode_select(q, st.kbar, st.ceil, lam, sigma, pos_t, Bq=self._cell_block, kk=st.kk, scale=self.scale,
+                                          ncell_cap=st.cap_cells, splits=splits, pdl=pdl)
+
     def graph_decode_layer(self, x, buf):
         """One decode token inside a captured whole-step graph (src/fsattn/attention.py:1493-1559): x (B,1,d); buf holds
         the shared device position `pos_t` and the layer's `cache`. Everything the reference does around its graph replay
@@ -466,7 +486,11 @@ class FSAttn(nn.Module):
         st = cache.decode_state(qkv)
         cos, sin = self.rope.tables_bf16(st.cap_rows)
         lam, sigma, lrs, norm_w = self.head_params()
-        ext = self._fsb_decode_select(qkv[:, 0], st, cache, buf["pos_t"], lam, sigma) if self.fsb_enabled else None
+        ext = None
+        if self.fsb_enabled:
+            ext = self._fsb_decode_select(qkv[:, 0], st, cache, buf["pos_t"], lam, sigma)
+        elif self._is_dense_lr():
+            ext = self._dense_decode_select(qkv[:, 0], st, buf["pos_t"], lam, sigma)
         y = ops.fsl_decode_step(st, qkv[:, 0], qkv[:, 1], qkv[:, 2], buf["pos_t"], cos, sin, lam, sigma, lrs, norm_w,
                                 scale=self.scale, eps=self.lr_norm.eps, y=buf.get("y"), splits=self._splits(st.B),
                                 ext_sel=ext)
@@ -520,6 +544,8 @@ class FSAttn(nn.Module):
             # the selection kernel reads q, so it waits for the projection like any dependent launch; the decode kernel
             # then depends on it through ext_sel
             ext = self._fsb_decode_select(q4[:, 0], st, buf["cache"], buf["pos_t"], lam, sigma, pdl=pdl)
+        elif self._is_dense_lr():
+            ext = self._dense_decode_select(q4[:, 0], st, buf["pos_t"], lam, sigma, pdl=pdl)
         return ops.fsl_decode_step(st, q4[:, 0], q4[:, 1], q4[:, 2], buf["pos_t"], cos, sin, lam, sigma, lrs, norm_w,
                                    scale=self.scale, eps=self.lr_norm.eps, y=y, splits=self._splits(st.B),
                                    pdl=pdl, ext_sel=ext)

@@ -59,6 +59,29 @@ class FslSelect(C.Structure):
                 ("topp_nb", i32), ("impl", i32)]
 
 
+class FsDenseSelect(C.Structure):
+    _fields_ = [("q", BHND),
+                ("kbar", vp), ("kbar_sb", i64), ("kbar_sh", i64),
+                ("ceil", vp), ("ceil_sb", i64), ("ceil_sh", i64),
+                ("lam", vp), ("sigma", vp),
+                ("B", i32), ("H", i32), ("D", i32), ("N", i32), ("ncell", i32), ("Bq", i32), ("nb", i32), ("kk", i32),
+                ("scale", f32),
+                ("sel", vp),
+                ("workspace", vp), ("workspace_bytes", i64),
+                ("status", vp)]
+
+
+class FsDenseDecodeSelect(C.Structure):
+    _fields_ = [("q", vp), ("q_sb", i64), ("q_sh", i64),
+                ("kbar", vp), ("kbar_sb", i64), ("kbar_sh", i64),
+                ("ceil", vp), ("ceil_sb", i64), ("ceil_sh", i64),
+                ("lam", vp), ("sigma", vp),
+                ("pos", vp),
+                ("B", i32), ("H", i32), ("D", i32), ("Bq", i32), ("kk", i32), ("ncell_cap", i32), ("splits", i32), ("pdl", i32),
+                ("scale", f32),
+                ("sel", vp)]
+
+
 class WindowPrefill(C.Structure):
     _fields_ = [("q", BHND), ("k", BHND), ("v", BHND),
                 ("cos", vp), ("sin", vp),
@@ -158,7 +181,8 @@ class FsbSelect(C.Structure):
 FSB_SPINE_MAX = 20
 FSB_MAX_MCAP = 16384
 
-EXTRA_STRUCTS = {"fsattn_trunk_gemv_t": TrunkGemv, "fsattn_trunk_layer_t": TrunkLayer, "fsattn_fsb_forest_t": FsbForest, "fsattn_fsb_select_t": FsbSelect}
+EXTRA_STRUCTS = {"fsattn_fs_dense_select_t": FsDenseSelect, "fsattn_fs_dense_decode_select_t": FsDenseDecodeSelect,
+                 "fsattn_trunk_gemv_t": TrunkGemv, "fsattn_trunk_layer_t": TrunkLayer, "fsattn_fsb_forest_t": FsbForest, "fsattn_fsb_select_t": FsbSelect}
 
 # every exported symbol of include/fsattn_b200.h with its argument struct (None = no struct argument)
 ENTRY_POINTS = {
@@ -169,6 +193,9 @@ ENTRY_POINTS = {
     "fsattn_dequant_cells": Dequant,
     "fsattn_fsl_prefix_topp": FslTopp,
     "fsattn_fsl_select": FslSelect,
+    "fsattn_fs_dense_workspace_bytes": ([i32, i32, i32, i32], i64),
+    "fsattn_fs_dense_select": FsDenseSelect,
+    "fsattn_fs_dense_decode_select": FsDenseDecodeSelect,
     "fsattn_window_prefill": WindowPrefill,
     "fsattn_window_prefill_static": WindowPrefill,
     "fsattn_readout_combine": ReadoutCombine,

@@ -173,6 +173,53 @@ def fsl_select(Q, kbar, ceil, topp, lam, sigma, *, N: int, ncell: int, Bq: int, 
     return (sel, margin) if want_margin else sel
 
 
+def fs_dense_select(Q, kbar, ceil, lam, sigma, *, N: int, ncell: int, Bq: int, nb: int, kk: int, scale: float, status=None):
+    """Dense FS prefill selection: sel (B,H,nb*Bq,kk) int32, for every query the kk best of ALL cells completed before its
+    query block (tensor-core kernel: head_dim 64, Bq = 128, kk <= 4)."""
+    _need_cuda(Q, kbar, ceil)
+    B, H, _, D = Q.shape
+    sel = torch.empty(B, H, nb * Bq, kk, dtype=torch.int32, device=Q.device)
+    lam, sigma = _f32(lam).to(Q.device), _f32(sigma).to(Q.device)
+    a = L.FsDenseSelect()
+    a.q = _bhnd(Q, "Q")
+    assert kbar.dtype == torch.float32 and kbar.stride(-1) == 1 and kbar.stride(2) == D and ceil.dtype == torch.float32 and ceil.stride(-1) == 1
+    a.kbar, a.kbar_sb, a.kbar_sh = kbar.data_ptr(), kbar.stride(0), kbar.stride(1)
+    a.ceil, a.ceil_sb, a.ceil_sh = ceil.data_ptr(), ceil.stride(0), ceil.stride(1)
+    a.lam, a.sigma = lam.data_ptr(), sigma.data_ptr()
+    a.B, a.H, a.D, a.N, a.ncell, a.Bq, a.nb, a.kk = B, H, D, int(N), int(ncell), int(Bq), int(nb), int(kk)
+    a.scale = float(scale)
+    a.sel = sel.data_ptr()
+    nbytes = int(L.load().fsattn_fs_dense_workspace_bytes(B, H, int(ncell), D))
+    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=Q.device)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), nbytes
+    a.status = _p(status)
+    L.call("fsattn_fs_dense_select", a, _stream(Q))
+    ws.record_stream(torch.cuda.current_stream(Q.device))
+    return sel
+
+
+def fs_dense_decode_select(q, kbar, ceil, lam, sigma, pos_t, *, Bq: int, kk: int, scale: float, ncell_cap: int, splits: int = 8,
+                           pdl: bool = False, sel=None):
+    """Dense FS decode selection: q (B,H,D) bf16 view at device position pos_t -> sel (B,H,kk) int32, the kk best of the
+    cells [0, min((pos // Bq) * Bq // 32, ncell_cap)). lam/sigma (H) fp32 device tensors."""
+    _need_cuda(q, kbar, ceil, lam, sigma, pos_t)
+    B, H, D = q.shape
+    if sel is None:
+        sel = torch.empty(B, H, kk, dtype=torch.int32, device=q.device)
+    assert q.dtype == torch.bfloat16 and q.stride(-1) == 1 and kbar.dtype == torch.float32 and kbar.stride(-1) == 1 and kbar.stride(2) == D
+    assert lam.dtype == torch.float32 and sigma.dtype == torch.float32 and pos_t.dtype == torch.int64 and sel.is_contiguous()
+    a = L.FsDenseDecodeSelect()
+    a.q, a.q_sb, a.q_sh = q.data_ptr(), q.stride(0), q.stride(1)
+    a.kbar, a.kbar_sb, a.kbar_sh = kbar.data_ptr(), kbar.stride(0), kbar.stride(1)
+    a.ceil, a.ceil_sb, a.ceil_sh = ceil.data_ptr(), ceil.stride(0), ceil.stride(1)
+    a.lam, a.sigma, a.pos = lam.data_ptr(), sigma.data_ptr(), pos_t.data_ptr()
+    a.B, a.H, a.D, a.Bq, a.kk, a.ncell_cap, a.splits, a.pdl = B, H, D, int(Bq), int(kk), int(ncell_cap), int(splits), 1 if pdl else 0
+    a.scale = float(scale)
+    a.sel = sel.data_ptr()
+    L.call("fsattn_fs_dense_decode_select", a, _stream(q))
+    return sel
+
+
 def window_prefill(Q, K, V, cos, sin, W: int, scale: float, pos0: int = 0, impl: int = 0, out=None, status=None):
     """Causal band attention with RoPE on Q and K. Returns (B,N,H*D) bf16 (W_o's input layout)."""
     _need_cuda(Q, K, V, cos, sin)

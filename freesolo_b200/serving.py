@@ -208,8 +208,9 @@ class GraphedDecoder:
         self.cache = make_caches(m, reserve=max(0, self.Lmax - P0))
         kv = self.kv
         self.fsb = any(a.fsb_enabled for a in self.attn)
-        if kv == "bounded" and self.fsb:
-            kv = "int8"      # FS-B reads any admitted cell: it keeps the full (int8) store
+        self.dense = any(a._is_dense_lr() and not a.fsb_enabled for a in self.attn_core)
+        if kv == "bounded" and (self.fsb or self.dense):
+            kv = "int8"      # FS-B and the dense variant read any completed cell: they keep the full (int8) store
         if kv == "bounded" and not (P0 >= self.attn[0].window_size and _kvb.supported(self.attn_core, self.dt, self.dev)):
             kv = "int8"      # prompts shorter than the window keep the full store (decode_graph.py:89-93)
         for c in self.cache:
@@ -301,8 +302,8 @@ class GraphedDecoder:
         the FS-B selection), the first QKV projection; without the fused kernel 5 per layer (6 with FS-B) + the head."""
         nL = len(self.blocks)
         if self.fused_trunk and self.x.shape[0] <= 8:
-            return 2 * nL + 1 + (nL if self.fsb else 0)
-        return 5 * nL + 1 + (nL if self.fsb else 0)
+            return 2 * nL + 1 + (nL if (self.fsb or self.dense) else 0)
+        return 5 * nL + 1 + (nL if (self.fsb or self.dense) else 0)
 
     def _trunk_step_batched(self):
         """More than 8 sequences per step: the projections are real GEMMs (weights read once for all rows), so they go to

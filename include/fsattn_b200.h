@@ -122,6 +122,46 @@ typedef struct {
 } fsattn_fsl_select_t;
 FSATTN_API int fsattn_fsl_select(const fsattn_fsl_select_t* a, fsattn_stream_t stream);
 
+/* ---- dense FS variant (no candidate pool): selection over every visible cell ---------------------------------------------
+ * Prefill: replaces the dense branch of FSAttn._lr_cell_topk (src/fsattn/attention.py:362-423 with
+ * _cell_select_blk_logits, 472-517) and its native kernel fsl_dense_fused (src/fsattn/fsl_select.cu:772-1018): for every
+ * query the kk best of ALL cells that end at or before its query block, score = (q . Kbar_c) * scale + lam * ceil_c *
+ * erf(|p - (c + 0.5) 32| / (2 sigma)), order (score desc, cell asc), -1 where fewer than kk cells are visible.
+ * q (B,H,N,D) bf16 view; kbar (B,H,>=ncell,D) fp32 holding bf16-exact values (row stride D); ceil (B,H,>=ncell) fp32;
+ * sel (B,H,nb*Bq,kk) int32. Tensor-core kernel (tcgen05 + TMEM + TMA): head_dim 64, Bq = 128, kk <= 4; anything else is
+ * refused. workspace: caller-owned scratch of fsattn_fs_dense_workspace_bytes() bytes, 16-byte aligned (bf16 copy of the
+ * mean keys and lam * ceil per cell). status (optional int32) counts bounded waits that ran out. */
+typedef struct {
+    fsattn_bhnd_t q;
+    const float* kbar; int64_t kbar_sb, kbar_sh;
+    const float* ceil; int64_t ceil_sb, ceil_sh;
+    const float* lam; const float* sigma;  /* (H) fp32 */
+    int32_t B, H, D, N, ncell, Bq, nb, kk;
+    float scale;
+    int32_t* sel;
+    void* workspace; int64_t workspace_bytes;
+    int32_t* status;
+} fsattn_fs_dense_select_t;
+FSATTN_API int64_t fsattn_fs_dense_workspace_bytes(int32_t B, int32_t H, int32_t ncell, int32_t D);
+FSATTN_API int fsattn_fs_dense_select(const fsattn_fs_dense_select_t* a, fsattn_stream_t stream);
+
+/* Decode: replaces FSAttn._lr_decode_step_dense (src/fsattn/attention.py:1159-1185) and fsl_dense_decode_topk
+ * (src/fsattn/fsl_select.cu:1026-1164): one query per (b,h) at position *pos scores the cells [0, min(blk_start / 32,
+ * ncell_cap)) with blk_start = (*pos / Bq) * Bq and keeps the kk best. The cells are split over `splits` CTAs (1, 2, 4 or
+ * 8: a thread-block cluster whose partial lists meet in rank 0's shared memory). sel (B,H,kk) int32 feeds
+ * fsattn_fsl_decode_step through ext_sel. kbar (B,H,>=cells,D) fp32, ceil (B,H,>=cells) fp32; q (B,H,D) bf16 (strides sb, sh). */
+typedef struct {
+    const void* q; int64_t q_sb, q_sh;
+    const float* kbar; int64_t kbar_sb, kbar_sh;
+    const float* ceil; int64_t ceil_sb, ceil_sh;
+    const float* lam; const float* sigma;
+    const int64_t* pos;
+    int32_t B, H, D, Bq, kk, ncell_cap, splits, pdl;
+    float scale;
+    int32_t* sel;
+} fsattn_fs_dense_decode_select_t;
+FSATTN_API int fsattn_fs_dense_decode_select(const fsattn_fs_dense_decode_select_t* a, fsattn_stream_t stream);
+
 /* ---- window branch, prefill -----------------------------------------------------------------------------------------
  * Replaces FSAttn._short_range / _chunked_rope_window (src/fsattn/attention.py:225-259) and
  * local_attention._batched_sliding_window_rope (src/utils/local_attention.py:191-235): causal band softmax attention

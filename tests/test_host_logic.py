@@ -47,10 +47,11 @@ def test_rotary_tables_match_oracle_and_grow_in_fp32():
 
 
 def test_uncacheable_configurations_raise():
-    for over in (dict(rope_long_range=True), dict(sel_strict_causal=0), dict(cell_prune_kernel=0), dict(cell_stride=64),
-                 dict(fs_uniform_sr=False)):
+    for over in (dict(rope_long_range=True), dict(sel_strict_causal=0), dict(cell_stride=64), dict(fs_uniform_sr=False),
+                 dict(cell_prune_kernel=0, cell_topk=8)):
         with pytest.raises(NotImplementedError):
             FSKVCache(_attn(**over))
+    FSKVCache(_attn(cell_prune_kernel=0))                                         # the dense FS variant is cacheable
     FSKVCache(_attn(fsb_enabled=True, fsb_read_top=4, cell_prune_kernel=0))     # an FS-B layer is cacheable
     c = FSKVCache(_attn(fsb_enabled=True, fsb_read_top=4, cell_prune_kernel=0))
     c.enable_bounded()

@@ -1,6 +1,6 @@
 """The dense FS variant (every completed visible cell is a candidate, no pool; the reference's serve preset "dense") in the CPU
-oracle against fixtures recorded from the reference itself (tests/golden/make_golden.py, gen_fs_dense). Oracle and fixtures
-only so far: no CUDA kernel takes this configuration yet, and constructing such a layer in the package raises."""
+oracle against fixtures recorded from the reference itself (tests/golden/make_golden.py, gen_fs_dense). The CUDA kernels of
+this configuration are compared with this oracle in tests/test_gpu_fsdense.py."""
 import pytest
 import torch
 
