@@ -9,8 +9,8 @@ replay).
            sampled token read back to the host every step
 The same JSON line carries, outside the headline's timed region: the roofline of the step's dominant kernel (the trunk
 projection GEMV) and of the attention decode kernel, the prefill figures, the window-attention kernel against the tensor peak,
-short legs at 4k / 16k / 64k for FS-L and FS-B, BASELINE config 3 (FS-B at the headline context), config 4 (743M-class,
-batch 32, 32k, int8 KV) and a CPU baseline.
+short legs at 4k / 16k / 64k for FS-L and FS-B, BASELINE config 3 (FS-B at the headline context), the dense FS variant,
+config 4 (743M-class, batch 32, 32k, int8 KV) and a CPU baseline.
 With N > 1 ranks (torchrun) every rank decodes its own sequence (batch sharding, no collective): weak scaling; the line then
 also carries a head-sharded leg (one sequence, heads split over the ranks: strong scaling) and config 4's 32 sequences
 split 32/N.
@@ -38,6 +38,8 @@ PUBLISHED = {
     "fsl_prefill_ktoks": {4096: 146.4, 16384: 187.5, 65536: 190.2, 131072: 189.8},
     "fsb_decode_tps": {4096: 504.7, 16384: 497.9, 65536: 473.8, 131072: 462.7},
     "fsb_prefill_ktoks": {4096: 127.7, 16384: 149.3, 65536: 143.1, 131072: 137.8},
+    "dense_decode_tps": {4096: 500.2, 16384: 488.1, 65536: 431.1, 131072: 385.8},
+    "dense_prefill_ktoks": {4096: 147.2, 16384: 179.5, 65536: 159.5, 131072: 134.8},
 }
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from ncu captures of these kernels on small cases;
 # None where no capture of the current kernel exists
@@ -391,6 +393,39 @@ def run_fsb_section(args, dev, K, Wm, peak, peak_kind):
     return out
 
 
+def dense_step_bytes(model, gd, B, ctx, int8=True):
+    """Dense FS decode step: weights + per layer the window, the fp32 mean key and ceiling of EVERY visible cell, the kk
+    cells read, the new row."""
+    a0 = gd.attn_core[0]
+    e = 1 if int8 else 2
+    m_vis = (ctx // a0._cell_block) * a0._cell_block // 32
+    per = (a0.window_size + 1) * a0.head_dim * 2 * e + m_vis * (a0.head_dim * 4 + 4) + a0.cell_topk * 32 * a0.head_dim * 2 * e + 4 * a0.head_dim
+    return weight_bytes(model) + len(gd.cache) * B * a0.n_heads * per + B * a0.d_model * 2
+
+
+def run_dense_section(args, dev, K, Wm, peak, peak_kind):
+    """The reference's third serving variant, FS (dense): no candidate pool, every completed visible cell is scored (tensor-core
+    selection in prefill, a cluster split top-k per decode token), int8 KV store."""
+    from freesolo_b200.serving import FreeSoloLM, GraphedDecoder, serve_kwargs
+    ctx = args.ctx
+    torch.manual_seed(0)
+    model = FreeSoloLM.from_config(args.model, max_seq_len=ctx + 512, **serve_kwargs("dense")).to(torch.bfloat16).to(dev).eval()
+    ids = torch.randint(0, model.vocab_size, (1, ctx), generator=torch.Generator().manual_seed(4321 + ctx))
+    gd, pms, _ = timed_prefill(lambda: GraphedDecoder(model, ids, Lmax=ctx + Wm + K + 40, device=dev, kv="int8"))
+    ms = timed_decode(gd, K, Wm)
+    sb = dense_step_bytes(model, gd, 1, ctx)
+    tps, ktoks = K / (ms * 1e-3), ctx / pms
+    out = {"workload": f"FS (dense) {args.model}: every visible cell scored, prefill at {ctx}, then {K} decode steps, batch 1, int8 KV",
+           "decode_tok_s": tps, "decode_ms_per_step": ms / K, "prefill_ktok_s": ktoks, "prefill_ms": pms,
+           "vs_published_decode": _pub("dense_decode_tps", ctx, tps), "vs_published_prefill": _pub("dense_prefill_ktoks", ctx, ktoks),
+           "roofline": {"what": "whole decode step", "bound": "hbm", "step_bytes": sb, "achieved": sb / (ms / K * 1e-3) / 1e9, "peak": peak,
+                        "unit": "GB/s", "frac": sb / (ms / K * 1e-3) / 1e9 / peak, "peak_kind": peak_kind},
+           "gpu_launches": K * gd.launches_per_step(), "kv_faults": list(gd.kv_faults())}
+    del gd, model
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_config4(dev, K, Wm, peak, peak_kind, batch=32, ctx=32768, dist=None, seed_off=0):
     """FS-L, the 743M-class model ("800m": 24 x 1536, 16 heads x 96), `batch` sequences of `ctx` tokens on
     this GPU, full int8 KV store. With `dist` (N > 1) the 32 sequences are split 32/N over the ranks, no collective in the
@@ -601,6 +636,8 @@ def run_ours(args):
     torch.cuda.empty_cache()
     if world == 1 and not args.no_fsb:
         line["fsb"] = run_fsb_section(args, dev, K, Wm, hbm_peak, peak_kind)
+    if world == 1 and not args.no_dense and args.model == "340m":
+        line["fs_dense"] = run_dense_section(args, dev, K, Wm, hbm_peak, peak_kind)
     if not args.no_config4 and args.model == "340m" and B == 1 and not heads:
         per = max(1, 32 // world)
         key = "config4" if world == 1 else "config4_split"
@@ -641,6 +678,7 @@ def main():
                          "split over the ranks, head outputs exchanged once per layer (strong scaling)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-fsb", action="store_true", help="skip the FS-B section (BASELINE config 3) of the N=1 line")
+    ap.add_argument("--no-dense", action="store_true", help="skip the dense FS section of the N=1 line")
     ap.add_argument("--no-contexts", action="store_true", help="skip the 4k / 16k / 64k legs")
     ap.add_argument("--no-config4", action="store_true", help="skip BASELINE config 4 (743M-class, 32 sequences)")
     ap.add_argument("--no-head-leg", action="store_true", help="N > 1: skip the head-sharded leg")
