@@ -80,7 +80,7 @@ struct Top4 {
 };
 
 // ---- pass 1 -------------------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(DS_THREADS, 3)
+__global__ void __launch_bounds__(DS_THREADS, 4)
 fs_dense_select_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k, const DsParams p) {
     extern __shared__ unsigned char ds_smem_raw[];
     __shared__ uint32_t tmem_base_s;
@@ -130,7 +130,7 @@ fs_dense_select_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
             tma_load_4d(base + DSM_Q, &tm_q, 0, q0, h, b, &bars[DB_Q]);
             for (int i = 0; i < nt && !*abortp; i++) {
                 const int s = i % DS_STAGES;
-                if (i >= DS_STAGES && !bar_wait(&bars[DB_EMPTY + s], ((i / DS_STAGES) - 1) & 1, abortp)) { *abortp = 1; break; }
+                if (i >= DS_STAGES && !bar_wait<true>(&bars[DB_EMPTY + s], ((i / DS_STAGES) - 1) & 1, abortp)) { *abortp = 1; break; }
                 bar_expect_tx(&bars[DB_FULL + s], DS_TILE_BYTES + DS_LC_BYTES);
                 tma_load_3d(base + DSM_K + s * DS_TILE_BYTES, &tm_k, 0, i * DS_BN, bh, &bars[DB_FULL + s]);
                 bulk_1d(base + DSM_LC + s * DS_LC_BYTES, p.lc + (int64_t)bh * p.ncell_pad + i * DS_BN, DS_LC_BYTES, &bars[DB_FULL + s]);
@@ -140,11 +140,11 @@ fs_dense_select_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
         // ================= MMA issuer ======================================================================================
         if (lane == 0) {
             const uint32_t idesc = instr_desc(DS_BN, 0, 1);
-            bool ok = bar_wait(&bars[DB_Q], 0, abortp);
+            bool ok = bar_wait<true>(&bars[DB_Q], 0, abortp);
             for (int i = 0; i < nt && ok && !*abortp; i++) {
                 const int s = i & 1, ks = i % DS_STAGES;
-                ok = bar_wait(&bars[DB_FULL + ks], (i / DS_STAGES) & 1, abortp);
-                if (ok && i >= 2) ok = bar_wait(&bars[DB_S_FREE + s], ((i >> 1) - 1) & 1, abortp);
+                ok = bar_wait<true>(&bars[DB_FULL + ks], (i / DS_STAGES) & 1, abortp);
+                if (ok && i >= 2) ok = bar_wait<true>(&bars[DB_S_FREE + s], ((i >> 1) - 1) & 1, abortp);
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t aq = s_u32(base + DSM_Q), bk = s_u32(base + DSM_K + ks * DS_TILE_BYTES);
@@ -162,50 +162,50 @@ fs_dense_select_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
         const float qpos = (float)(q0 + r);
         const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
         const float two_sigma = f_mul(2.0f, p.sigma[h]);
+        const float inv_two_sigma = 1.0f / two_sigma;      // for the "is erf exactly 1" decision only (taken with a margin)
         Top4 T;
         T.init();
         bool ok = true;
         for (int i = 0; i < nt; i++) {
             const int bb = i & 1, ks = i % DS_STAGES;
-            ok = ok && bar_wait(&bars[DB_S_FULL + bb], (i >> 1) & 1, abortp) && !*abortp;
+            ok = ok && bar_wait<true>(&bars[DB_S_FULL + bb], (i >> 1) & 1, abortp) && !*abortp;
             if (!__all_sync(FS_FULL, ok)) { ok = false; break; }
             tc_fence_after();
             const float* lcs = reinterpret_cast<const float*>(base + DSM_LC + ks * DS_LC_BYTES);
+            // eight columns at a time straight from TMEM: one small loop body for the whole tile keeps the kernel's code far
+            // below the instruction cache (a fully unrolled 64-column body with its inlined inserts and erf calls is not)
+#pragma unroll 1
+            for (int j0 = 0; j0 < DS_BN; j0 += 8) {
+                const int cell0 = i * DS_BN + j0;
+                const int cv = nvis - cell0;                          // valid columns of this group: j < cv
+                if (cv <= 0) break;
+                float v[8];
+                tmem_ld8(lane_base + bb * DS_BN + j0, v);
+                const float4 la = reinterpret_cast<const float4*>(lcs + j0)[0];
+                const float4 lb = reinterpret_cast<const float4*>(lcs + j0)[1];
+                const float lc8[8] = {la.x, la.y, la.z, la.w, lb.x, lb.y, lb.z, lb.w};
+                // the nearest cell of the group is its last valid one; beyond x = 4 erf is exactly 1 in fp32
+                const int clast = cell0 + (cv < 8 ? cv : 8) - 1;
+                const float xmin = fabsf(qpos - ((float)clast + 0.5f) * (float)FSATTN_CELL) * inv_two_sigma;
+                float s[8];
+                if (xmin >= 4.01f) {                                  // the exact quotient is then >= 4: erf is 1
 #pragma unroll
-            for (int hf = 0; hf < 2; hf++) {
-                float v[32];
-                tmem_ld32(lane_base + bb * DS_BN + hf * 32, v);
-                const int cell0 = i * DS_BN + hf * 32;
-                const int cv = nvis - cell0;                          // valid columns of this half: j < cv
-                if (cv <= 0) continue;
-                // the nearest cell of this half is its last valid one; beyond x = 4 erf is exactly 1 in fp32
-                const int clast = cell0 + (cv < 32 ? cv : 32) - 1;
-                const float xmin = f_div(fabsf(qpos - f_mul((float)clast + 0.5f, (float)FSATTN_CELL)), two_sigma);
-                if (xmin >= 4.0f && cv >= 32) {
-#pragma unroll
-                    for (int j0 = 0; j0 < 32; j0 += 8) {
-                        const float4 la = reinterpret_cast<const float4*>(lcs + hf * 32 + j0)[0];
-                        const float4 lb = reinterpret_cast<const float4*>(lcs + hf * 32 + j0)[1];
-                        float s[8];
-                        s[0] = f_add(f_mul(v[j0 + 0], p.scale), la.x); s[1] = f_add(f_mul(v[j0 + 1], p.scale), la.y);
-                        s[2] = f_add(f_mul(v[j0 + 2], p.scale), la.z); s[3] = f_add(f_mul(v[j0 + 3], p.scale), la.w);
-                        s[4] = f_add(f_mul(v[j0 + 4], p.scale), lb.x); s[5] = f_add(f_mul(v[j0 + 5], p.scale), lb.y);
-                        s[6] = f_add(f_mul(v[j0 + 6], p.scale), lb.z); s[7] = f_add(f_mul(v[j0 + 7], p.scale), lb.w);
-                        const float m8 = fmaxf(fmaxf(fmaxf(s[0], s[1]), fmaxf(s[2], s[3])), fmaxf(fmaxf(s[4], s[5]), fmaxf(s[6], s[7])));
-                        if (m8 > T.s3) {
-#pragma unroll
-                            for (int j = 0; j < 8; j++) T.insert(s[j], cell0 + j0 + j);
-                        }
-                    }
+                    for (int j = 0; j < 8; j++) s[j] = f_add(f_mul(v[j], p.scale), lc8[j]);
                 } else {
 #pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        if (j >= cv) continue;                        // (kept as a predicate: the scores stay in registers)
-                        const int cell = cell0 + j;
-                        const float x = f_div(fabsf(qpos - f_mul((float)cell + 0.5f, (float)FSATTN_CELL)), two_sigma);
-                        const float prior = f_mul(lcs[hf * 32 + j], erff(x));
-                        T.insert(f_add(f_mul(v[j], p.scale), prior), cell);
+                    for (int j = 0; j < 8; j++) {
+                        const float x = f_div(fabsf(qpos - f_mul((float)(cell0 + j) + 0.5f, (float)FSATTN_CELL)), two_sigma);
+                        s[j] = f_add(f_mul(v[j], p.scale), f_mul(lc8[j], erff(x)));
                     }
+                }
+                if (cv < 8) {
+#pragma unroll
+                    for (int j = 0; j < 8; j++) if (j >= cv) s[j] = -INFINITY;
+                }
+                const float m8 = fmaxf(fmaxf(fmaxf(s[0], s[1]), fmaxf(s[2], s[3])), fmaxf(fmaxf(s[4], s[5]), fmaxf(s[6], s[7])));
+                if (m8 > T.s3) {
+#pragma unroll
+                    for (int j = 0; j < 8; j++) T.insert(s[j], cell0 + j);
                 }
             }
             tc_fence_before();

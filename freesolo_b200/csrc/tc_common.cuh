@@ -22,14 +22,21 @@ __device__ __forceinline__ void bar_arrive(uint64_t* bar) {
 __device__ __forceinline__ void bar_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(s_u32(bar)), "r"(bytes) : "memory");
 }
-// bounded wait; gives up early once another thread of the CTA has raised the abort flag
+// bounded wait; gives up early once another thread of the CTA has raised the abort flag. PARK: every try carries a suspend
+// hint, so the hardware may park the thread for up to a microsecond (it is woken when the phase completes) instead of
+// polling - for kernels that are short of issue slots, at the price of a slightly later wake-up.
+template <bool PARK = false>
 __device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity, volatile int* abortp) {
     const uint32_t addr = s_u32(bar);
     for (int i = 0; i < TC_WAIT_ITERS; i++) {
         if ((i & 63) == 63 && *abortp) return false;
         uint32_t done;
-        asm volatile("{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}"
-                     : "=r"(done) : "r"(addr), "r"(parity) : "memory");
+        if (PARK)
+            asm volatile("{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\nselp.u32 %0, 1, 0, p;\n}"
+                         : "=r"(done) : "r"(addr), "r"(parity), "r"(1000u) : "memory");
+        else
+            asm volatile("{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}"
+                         : "=r"(done) : "r"(addr), "r"(parity) : "memory");
         if (done) return true;
     }
     return false;
@@ -98,6 +105,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
 }
 
 
+
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr) : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
+}
 
 // ---- host side: cuTensorMapEncodeTiled through the runtime's driver entry point ----------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
