@@ -41,9 +41,10 @@ PUBLISHED = {
     "dense_decode_tps": {4096: 500.2, 16384: 488.1, 65536: 431.1, 131072: 385.8},
     "dense_prefill_ktoks": {4096: 147.2, 16384: 179.5, 65536: 159.5, 131072: 134.8},
 }
-# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from ncu captures of these kernels on small cases;
-# None where no capture of the current kernel exists
-NCU_DRAM_BYTES = {"fsl_decode_kernel/340m/b1": 1.87e6, "trunk_gemv_kernel/340m/b1": None}
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from ncu --set full captures of the current kernels
+# (a 32k-context run; neither kernel's traffic depends on the context). trunk_gemv: the weighted mean over one step's 97
+# launches (24 x (6.32 + 2.13 + 11.56 + 5.81) + 66.0 MB). None where no capture of that shape exists.
+NCU_DRAM_BYTES = {"fsl_decode_kernel/340m/b1": 1.85e6, "trunk_gemv_kernel/340m/b1": 7.07e6}
 
 
 def _peaks():
@@ -608,7 +609,7 @@ def run_ours(args):
           "peak": hbm_peak, "unit": "GB/s", "frac": kbytes / (k_avg_ms * 1e-3) / 1e9 / hbm_peak, "peak_kind": peak_kind,
           "traffic": NCU_DRAM_BYTES.get(f"fsl_decode_kernel/{args.model}/b{B}"),
           "traffic_source": "ncu dram__bytes_read + dram__bytes_write per launch, 32k-context capture (the FS-L decode read does "
-                            "not depend on the context); null = no capture of this shape",
+                            "not depend on the context); null = no capture of this shape, not measured in this run",
           "how": "launched alone with an L2 flush before every launch, CUDA events on the launching stream"}
     if B <= 8 and not heads:
         n_launch, chain_ms = time_gemv_chain(gd)
@@ -617,6 +618,8 @@ def run_ours(args):
             "kernel": "trunk_gemv_kernel", "bound": "hbm", "achieved": wb / (chain_ms * 1e-3) / 1e9, "peak": hbm_peak, "unit": "GB/s",
             "frac": wb / (chain_ms * 1e-3) / 1e9 / hbm_peak, "peak_kind": peak_kind,
             "traffic": NCU_DRAM_BYTES.get(f"trunk_gemv_kernel/{args.model}/b{B}"),
+            "traffic_source": "ncu dram__bytes_read + dram__bytes_write, weighted mean over one step's 97 launches; null = no "
+                              "capture of this shape, not measured in this run",
             "bytes_per_launch": wb / n_launch, "avg_launch_us": chain_ms * 1e3 / n_launch, "launches_per_step": n_launch,
             "share_of_step": chain_ms / (ms / K),
             "why": "the step's dominant kernel: the 4 projections of every layer + the LM head stream all weights once per token",
@@ -641,7 +644,8 @@ def run_ours(args):
     if not args.no_config4 and args.model == "340m" and B == 1 and not heads:
         per = max(1, 32 // world)
         key = "config4" if world == 1 else "config4_split"
-        line[key] = run_config4(dev, min(K, 24), Wm, hbm_peak, peak_kind, batch=per, dist=dist if world > 1 else None, seed_off=rank)
+        line[key] = run_config4(dev, min(K, 24), Wm, hbm_peak, peak_kind, batch=per, ctx=args.config4_ctx,
+                                dist=dist if world > 1 else None, seed_off=rank)
     if world > 1 and not heads and not args.no_head_leg and args.model == "340m" and B == 1:
         line["head_sharded"] = run_head_sharded(args, dev, K, Wm, rank, world, dist)
         line["head_sharded"]["speedup_vs_one_rank_of_this_run"] = line["head_sharded"]["decode_tok_s"] / (value / world)
@@ -682,6 +686,7 @@ def main():
     ap.add_argument("--no-contexts", action="store_true", help="skip the 4k / 16k / 64k legs")
     ap.add_argument("--no-config4", action="store_true", help="skip BASELINE config 4 (743M-class, 32 sequences)")
     ap.add_argument("--no-head-leg", action="store_true", help="N > 1: skip the head-sharded leg")
+    ap.add_argument("--config4-ctx", type=int, default=32768, help="context of config 4's sequences (smaller for profiler captures)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
