@@ -505,6 +505,56 @@ def run_head_sharded(args, dev, K, Wm, rank, world, dist):
     return out
 
 
+def run_config5(args, dev, rank, world, dist):
+    """BASELINE config 5's shape: FS-B, the 743M-class model (16 heads x 96), ONE sequence of `--config5-ctx` tokens (default
+    262144), heads split over the ranks (each rank builds and searches the forests of its own heads; the head outputs meet once
+    per layer), thresholds from a 4096-token warm-up, int8 KV store, up to 128 graph-replayed decode steps."""
+    from freesolo_b200.parallel import shard_model_heads
+    from freesolo_b200.serving import FreeSoloLM, GraphedDecoder, calibrate_fsb_tau, serve_kwargs
+    ctx, nL = args.config5_ctx, args.config5_layers
+    torch.manual_seed(0)
+    model = FreeSoloLM.from_config("800m", n_layers=nL, max_seq_len=ctx + 512, **serve_kwargs("fsb", 0.9)).to(torch.bfloat16).to(dev).eval()
+    warm_ids = torch.randint(0, model.vocab_size, (1, 4096), generator=torch.Generator().manual_seed(99))
+    calibrate_fsb_tau(model, warm_ids, 0.5, "fsb_tau")
+    calibrate_fsb_tau(model, warm_ids, 0.9, "fsb_tau_union")
+    n_heads = model.blocks[0].attn.fsattn.n_heads
+    if world > 1:
+        shard_model_heads(model, rank, world)
+    K, Wm = min(args.steps, 128), 3
+    ids = torch.randint(0, model.vocab_size, (1, ctx), generator=torch.Generator().manual_seed(4321 + ctx))
+    torch.cuda.reset_peak_memory_stats()
+    gd = GraphedDecoder(model, ids, Lmax=ctx + Wm + K + 40, device=dev, kv="int8")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    gd.prefill()
+    e1.record()
+    torch.cuda.synchronize()
+    pms = e0.elapsed_time(e1)
+    if world > 1:
+        dist.barrier()
+    ms = timed_decode(gd, K, Wm)
+    if world > 1:
+        t = torch.tensor([ms, pms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, pms = t.tolist()
+    fo = gd.cache[0].fsb
+    out = {"workload": f"FS-B 800m-class ({nL} layers x 1536, {n_heads} heads x 96), ONE sequence of {ctx} tokens, heads split over "
+                       f"{world} GPU(s), int8 KV, {K} graph-replayed decode steps",
+           "layers": nL, "ctx": ctx, "decode_tok_s": K / (ms * 1e-3), "decode_ms_per_step": ms / K,
+           "prefill_ktok_s": ctx / pms, "prefill_ms": pms, "prefill_note": "one cold run, forest build included",
+           "forest_bytes_per_layer_per_gpu": gd.fsb_bytes() // nL, "forest_cells_cap": fo.m_cap,
+           "admitted_cells_layer0_rank0": {"main": fo.m_tot[0].tolist(), "second": fo.m_tot[1].tolist()},
+           "kv_bytes_per_layer_per_gpu": gd.kv_bytes() // nL, "peak_mem_gib_per_gpu": torch.cuda.max_memory_allocated() / 2 ** 30,
+           "kv_faults": list(gd.kv_faults())}
+    gd.graph = None
+    del gd, model
+    import gc
+    gc.collect()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return out
+
+
 # ---- the measured arm ---------------------------------------------------------------------------------------------------------
 def run_ours(args):
     import torch.distributed as dist
@@ -649,6 +699,8 @@ def run_ours(args):
     if world > 1 and not heads and not args.no_head_leg and args.model == "340m" and B == 1:
         line["head_sharded"] = run_head_sharded(args, dev, K, Wm, rank, world, dist)
         line["head_sharded"]["speedup_vs_one_rank_of_this_run"] = line["head_sharded"]["decode_tok_s"] / (value / world)
+    if args.config5:
+        line["config5"] = run_config5(args, dev, rank, world, dist)
     if world > 1:
         # every rank leaves the group together; what follows on rank 0 needs no communication
         barrier()
@@ -686,6 +738,10 @@ def main():
     ap.add_argument("--no-contexts", action="store_true", help="skip the 4k / 16k / 64k legs")
     ap.add_argument("--no-config4", action="store_true", help="skip BASELINE config 4 (743M-class, 32 sequences)")
     ap.add_argument("--no-head-leg", action="store_true", help="N > 1: skip the head-sharded leg")
+    ap.add_argument("--config5", action="store_true",
+                    help="also run BASELINE config 5's shape (FS-B 743M-class, one long sequence, heads split over the ranks)")
+    ap.add_argument("--config5-ctx", type=int, default=262144)
+    ap.add_argument("--config5-layers", type=int, default=24)
     ap.add_argument("--config4-ctx", type=int, default=32768, help="context of config 4's sequences (smaller for profiler captures)")
     args = ap.parse_args()
     if args.impl == "reference":
