@@ -5,8 +5,8 @@ Headline workload (BASELINE config 2 at its largest published context): FS-L 341
 131072) through this repo's kernels, then greedy decode. A step = one decoded token through the whole model (one CUDA-graph
 replay).
   value  : tok/s over exactly K replays timed with CUDA events (inputs resident in HBM), max over ranks
-  e2e    : tok/s through the public decoder API with the token id copied from pinned host memory every step and the
-           sampled token read back to the host every step
+  e2e    : tok/s through the public decoder API (GraphedDecoder.step_host) with the token id copied from pinned host
+           memory every step and the sampled token read back to the host every step
 The same JSON line carries, outside the headline's timed region: the roofline of the step's dominant kernel (the trunk
 projection GEMV) and of the attention decode kernel, the prefill figures, the window-attention kernel against the tensor peak,
 short legs at 4k / 16k / 64k for FS-L and FS-B, BASELINE config 3 (FS-B at the headline context), the dense FS variant,
@@ -579,7 +579,7 @@ def run_ours(args):
         from freesolo_b200.parallel import shard_model_heads
         shard_model_heads(model, rank, world)
     ids = torch.randint(0, model.vocab_size, (B, ctx), generator=torch.Generator().manual_seed(4321 + ctx + (0 if heads else rank)))
-    total = Wm + 2 * K + 32
+    total = Wm + 2 * K + 40
     # one short untimed prefill first: library handles, kernel attributes and allocator pools are initialised there
     warm = GraphedDecoder(model, ids[:, :min(ctx, 2048)], Lmax=min(ctx, 2048) + 64, device=dev, kv=args.kv)
     warm.prefill()
@@ -609,12 +609,13 @@ def run_ours(args):
     tok_host = torch.zeros(B, 1, dtype=torch.int64).pin_memory()
     tok_host.copy_(gd.tok.cpu())
     out_host = torch.zeros(B, 1, dtype=torch.int64).pin_memory()
+    gd.step_host(tok_host, out_host)                  # untimed: captures the graph that carries the two copies
+    torch.cuda.current_stream().synchronize()
+    tok_host.copy_(out_host)
     barrier()
     t0 = time.perf_counter()
     for _ in range(K):
-        gd.tok.copy_(tok_host, non_blocking=True)
-        gd.step()
-        out_host.copy_(gd.tok, non_blocking=True)
+        gd.step_host(tok_host, out_host)              # pinned host id in, step, sampled id back to pinned host memory
         torch.cuda.current_stream().synchronize()
         tok_host.copy_(out_host)
     barrier()

@@ -371,6 +371,37 @@ class GraphedDecoder:
         self.pos += 1
         return self.tok
 
+    @torch.no_grad()
+    def step_host(self, tok_host: torch.Tensor, out_host: torch.Tensor):
+        """One token end to end for a caller whose token ids live on the host: the id in `tok_host` (pinned (B,1) int64) goes
+        to the device, the step runs, and the sampled id lands in `out_host` (pinned (B,1) int64) - one graph launch whose
+        first and last nodes are the two copies. The caller synchronises the stream before reading `out_host`. The same
+        tensors must be passed on every call (their addresses are part of the captured graph)."""
+        if self.graph is None or self.fsb and self.pos % self.attn[0]._cell_block == 0:
+            # not captured yet, or a step with host-side work (an FS-B block change): the plain sequence
+            self.tok.copy_(tok_host, non_blocking=True)
+            self.step()
+            out_host.copy_(self.tok, non_blocking=True)
+            return
+        key = (tok_host.data_ptr(), out_host.data_ptr())
+        if getattr(self, "_host_graph_key", None) != key or self._host_graph_src is not self.graph:
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.tok.copy_(tok_host, non_blocking=True)
+                self._trunk_step()
+                out_host.copy_(self.tok, non_blocking=True)
+            self._host_graph, self._host_graph_key, self._host_graph_src = g, key, self.graph
+        if self._graph_stale():
+            self.graph = None
+            self._host_graph_key = None
+            return self.step_host(tok_host, out_host)
+        if self.pos + 1 >= self.Lmax:
+            raise RuntimeError(f"decoder sized for {self.Lmax} positions")
+        self._host_graph.replay()
+        self._steps += 1
+        self.pos += 1
+
     def sync_caches(self):
         for c in self.cache:
             c.pos = self.pos

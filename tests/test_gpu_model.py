@@ -325,3 +325,28 @@ def test_model_logits_against_the_reference_model(dev, variant):
           f"the reference's own bf16 run: max-abs {ma_r:.3e}, mean-rel {mr_r:.3e}, agreement {agree_r:.4f}")
     assert mr <= 1.25 * mr_r and ma <= 1.5 * ma_r, "further from the fp32 reference than the reference's own bf16 run"
     assert agree >= agree_r - 0.03
+
+
+def test_host_facing_step_equals_the_device_step(dev):
+    """GraphedDecoder.step_host (token id from pinned host memory in, sampled id back to pinned host memory, both copies
+    inside one graph launch) decodes the same tokens as step()."""
+    from freesolo_b200.serving import FreeSoloLM, GraphedDecoder, serve_kwargs
+    torch.manual_seed(0)
+    m = FreeSoloLM.from_config("debug", max_seq_len=2048, **serve_kwargs("sparse")).to(dev).to(torch.bfloat16).eval()
+    P0, T = 600, 80
+    ids = torch.randint(0, 32000, (2, P0), generator=torch.Generator().manual_seed(4))
+    a = GraphedDecoder(m, ids, Lmax=P0 + T + 8, device=dev, kv="bounded")
+    want = [a.prefill().clone()] + [a.step().clone() for _ in range(T - 1)]
+    b = GraphedDecoder(m, ids, Lmax=P0 + T + 8, device=dev, kv="bounded")
+    tok_host = torch.zeros(2, 1, dtype=torch.int64).pin_memory()
+    out_host = torch.zeros(2, 1, dtype=torch.int64).pin_memory()
+    first = b.prefill()
+    tok_host.copy_(first.cpu())
+    got = [first.clone().cpu()]
+    for _ in range(T - 1):
+        b.step_host(tok_host, out_host)
+        torch.cuda.current_stream().synchronize()
+        got.append(out_host.clone())
+        tok_host.copy_(out_host)
+    assert getattr(b, "_host_graph", None) is not None
+    assert torch.equal(torch.cat(got, dim=1), torch.cat(want, dim=1).cpu())
