@@ -466,6 +466,8 @@ struct SelArgs {
     int H, ncell_k;
 };
 
+#include "fsb_beam_block.cuh"
+
 // ---- prefill: one CTA per (128-query block, row) ---------------------------------------------------------------------------
 // Per forest: build the block's spine, copy every chunk node of tree depth <= DS into shared memory (<= 2^(DS+1)-1 rows:
 // the levels all 128 queries walk through), then one warp per query runs the beam, reading the shallow levels from
@@ -787,6 +789,7 @@ extern "C" int fsattn_fsb_select(const fsattn_fsb_select_t* a, fsattn_stream_t s
                    "fsb_select: beam widths %d / %d (1..16 and 0..16)", a->width, a->width2);
     FS_REQUIRE(a->read_top >= 1 && a->read_top <= 32, "fsb_select: read_top = %d", a->read_top);
     FS_REQUIRE(a->Bq >= 1 && a->N >= 1, "fsb_select: N = %d, Bq = %d", a->N, a->Bq);
+    FS_REQUIRE(a->beam_impl >= 0 && a->beam_impl <= 1, "fsb_select: beam_impl = %d (0 or 1)", a->beam_impl);
     if (a->use_spines) {
         FS_REQUIRE(a->spine[0] && a->hdr[0] && a->pos && (a->width2 == 0 || (a->spine[1] && a->hdr[1])),
                    "fsb_select: decode needs the spines, their headers and pos");
@@ -829,6 +832,22 @@ extern "C" int fsattn_fsb_select(const fsattn_fsb_select_t* a, fsattn_stream_t s
     } else {
         FS_UNSUPPORTED(a->Bq > 128, "fsb_select: query blocks of %d (at most 128)", a->Bq);
         cudaError_t e = cudaSuccess;
+        if (two_pass && a->beam_impl != 1) {
+            // whole 128-query blocks: one thread per query, the block's distinct nodes scored on tensor-core tiles
+            switch (a->main.D) {
+                case 64: e = launch_beam_block<64>(A, grid, st); break;
+                case 96: e = launch_beam_block<96>(A, grid, st); break;
+                default: e = launch_beam_block<128>(A, grid, st); break;
+            }
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                fs_set_error("fsb_select: shared-memory opt-in failed: %s", cudaGetErrorString(e));
+                return FSATTN_ELAUNCH;
+            }
+            rc = fs_check_launch("fsb_beam_block_kernel");
+            if (rc != FSATTN_OK) return rc;
+            return fs_fsb_rerank_block(a, st);
+        }
         switch (a->main.D) {
             case 64:
                 e = cudaFuncSetAttribute(fsb_select_kernel<64, SEL_NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SelSmem<64>::TOTAL);

@@ -175,7 +175,7 @@ class FsbSelect(C.Structure):
                 ("lam", vp), ("sigma", vp), ("scale", f32), ("radius_coef", f32),
                 ("B", i32), ("N", i32), ("q_pos0", i32), ("Bq", i32), ("width", i32), ("width2", i32), ("read_top", i32),
                 ("use_spines", i32), ("spine", vp * 2), ("hdr", vp * 2), ("pos", vp),
-                ("sel", vp), ("cand", vp), ("nvis", vp), ("pdl", i32)]
+                ("sel", vp), ("cand", vp), ("nvis", vp), ("pdl", i32), ("beam_impl", i32)]
 
 
 FSB_SPINE_MAX = 20

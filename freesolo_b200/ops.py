@@ -627,11 +627,13 @@ class FsbForests:
 
 def fsb_select(forests: FsbForests, Q, K, lam, sigma, *, scale: float, N: int = None, q_pos0: int = 0, Bq: int = 128,
                width: int = 16, width2: int = 16, read_top: int = 4, radius_coef: float = 8.0, pos=None,
-               kq=None, ks=None, debug: bool = False, pdl: bool = False):
+               kq=None, ks=None, debug: bool = False, pdl: bool = False, beam_impl: int = 0):
     """FS-B selection. Prefill (pos None): Q (B,H,N,D) bf16 at positions q_pos0.., blocks of Bq -> sel (B,H,nb*Bq,K)
     int32. Decode (pos = device int64 scalar): Q (B,H,1,D), the spines of forests.build_spines -> sel (B,H,1,K).
     K: raw bf16 token keys (B,H,>=cells*32,D), or None with the int8 codes kq (B,H,rows,D) and scales ks (B,H,cells).
-    debug=True also returns the candidates (B,H,Npad,width+width2) and the visit counts."""
+    debug=True also returns the candidates (B,H,Npad,width+width2) and the visit counts. beam_impl (prefill, whole
+    128-query blocks): 0 = one thread per query with the block's distinct nodes scored on tensor-core tiles, 1 = one warp
+    per query."""
     _need_cuda(Q, K, kq, ks)
     B, H, Nq, D = Q.shape
     decode = pos is not None
@@ -670,6 +672,7 @@ def fsb_select(forests: FsbForests, Q, K, lam, sigma, *, scale: float, N: int = 
         assert pos.dtype == torch.int64 and pos.is_cuda
         a.pos = pos.data_ptr()
         a.pdl = 1 if pdl else 0
+    a.beam_impl = int(beam_impl)
     a.sel, a.cand, a.nvis = sel.data_ptr(), _p(cand), _p(nvis)
     L.call("fsattn_fsb_select", a, _stream(Q))
     return (sel, cand, nvis) if debug else sel

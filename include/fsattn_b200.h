@@ -398,6 +398,8 @@ typedef struct {
     int32_t use_spines; const float* spine[2]; const int32_t* hdr[2]; const int64_t* pos;
     int32_t* sel; int32_t* cand; int32_t* nvis;
     int32_t pdl;  /* decode: 1 = launch with programmatic stream serialization (the kernel waits for its producer itself) */
+    int32_t beam_impl;  /* prefill with Bq = 128 and cand: 0 = one thread per query, the block's distinct nodes scored on
+                         * tensor-core tiles; 1 = one warp per query (the kernel ragged blocks always use) */
 } fsattn_fsb_select_t;
 FSATTN_API int fsattn_fsb_select(const fsattn_fsb_select_t* a, fsattn_stream_t stream);
 

@@ -115,8 +115,9 @@ def _gpu_stats(K, ncell):
     return kbar, ceil
 
 
+@pytest.mark.parametrize("beam_impl", [0, 1])
 @pytest.mark.parametrize("kind", ["randn", "vocab"])
-def test_select_prefill_vs_oracle(kind):
+def test_select_prefill_vs_oracle(kind, beam_impl):
     from freesolo_b200 import ops
     from oracle import fsb
     g, Q, K, V = _golden_inputs(kind)
@@ -130,7 +131,7 @@ def test_select_prefill_vs_oracle(kind):
     scale = D ** -0.5
     fo = ops.FsbForests(kbar, ceil, tau, tau_u, cap_cells=ncell)
     fo.ingest(ncell)
-    sel, cand, nvis = ops.fsb_select(fo, Qd, Kd, lam, sigma, scale=scale, N=N, debug=True)
+    sel, cand, nvis = ops.fsb_select(fo, Qd, Kd, lam, sigma, scale=scale, N=N, debug=True, beam_impl=beam_impl)
     torch.cuda.synchronize()
     sel, cand, nvis = sel.cpu().long(), cand.cpu().long(), nvis.cpu()
     kb, ce = kbar.cpu(), ceil.cpu()
@@ -426,6 +427,41 @@ def test_select_other_head_dims_and_batch(D, B):
     sdo, mdo = fsb.fsb_select_decode(qd[:, :, 0].float(), N, K.float(), kbar.cpu(), ce, ncell, tau, tau_u, lam, sigma, scale)
     bad = (sd[:, :, 0] != sdo).any(-1) & (mdo > 1e-4)
     assert int(bad.sum()) == 0
+
+
+@pytest.mark.parametrize("coherent", [False, True])
+def test_block_beams_equal_the_per_query_beams(coherent):
+    """The two prefill beam kernels (one thread per query with the block's distinct nodes on tensor-core tiles; one warp
+    per query) on 8192 tokens: the same candidate lists and visit counts, up to the queries whose cut-off is a near-tie
+    (the two sum a dot product in different orders). Random queries make a block's beams diverge (hundreds of distinct
+    nodes per level: several 64-column passes); queries that are one vector plus small noise make them coincide."""
+    from freesolo_b200 import ops
+    dev = _dev()
+    H, N, D = 2, 8192, 64
+    g = torch.Generator().manual_seed(77)
+    K = torch.randn(1, H, N, D, generator=g).to(torch.bfloat16)
+    if coherent:
+        Q = (torch.randn(1, H, 1, D, generator=g) + 0.05 * torch.randn(1, H, N, D, generator=g)).to(torch.bfloat16)
+    else:
+        Q = torch.randn(1, H, N, D, generator=g).to(torch.bfloat16)
+    lam = 0.5 + torch.rand(H, generator=g)
+    sigma = 2.0 + torch.rand(H, generator=g) * 30
+    ncell = N // S
+    Qd, Kd = Q.to(dev), K.to(dev)
+    kbar, ceil = _gpu_stats(Kd, ncell)
+    ce = ceil.cpu()
+    tau = torch.quantile(ce.transpose(0, 1).reshape(H, -1), 0.3, dim=1)
+    tau_u = torch.quantile(ce.transpose(0, 1).reshape(H, -1), 0.7, dim=1)
+    fo = ops.FsbForests(kbar, ceil, tau, tau_u, cap_cells=ncell)
+    fo.ingest(ncell)
+    out = [ops.fsb_select(fo, Qd, Kd, lam, sigma, scale=D ** -0.5, N=N, debug=True, beam_impl=i) for i in (0, 1)]
+    torch.cuda.synchronize()
+    (s0, c0, v0), (s1, c1, v1) = out
+    same = (c0 == c1).all(-1)
+    assert same.float().mean() > 0.995, float(same.float().mean())
+    assert torch.equal(v0[same], v1[same])
+    assert ((s0 == s1).all(-1) | ~same).all()
+    assert int((c0 >= 0).sum()) > 0.5 * c0[:, :, 256:].numel()
 
 
 def test_second_prefill_on_one_cache_starts_the_forests_over():
