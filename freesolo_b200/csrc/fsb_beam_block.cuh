@@ -27,8 +27,8 @@ struct BeamSmem {
     static constexpr int PITCH = D * 2 + 16;                            // staged mean row: conflict-free fragment reads
     static constexpr size_t HKEY = 0;                                   // int[BK_HT]: node ref or -1
     static constexpr size_t HIDX = HKEY + (size_t)BK_HT * 4;            // uint16[BK_HT]: column of the slot's node
-    static constexpr size_t ULIST = HIDX + (size_t)BK_HT * 2;           // int[BK_HT]: column -> node ref
-    static constexpr size_t MU = ULIST + (size_t)BK_HT * 4;
+    static constexpr size_t ULIST = HIDX + (size_t)BK_HT * 2;           // uint16[BK_HT]: column -> slot
+    static constexpr size_t MU = ULIST + (size_t)BK_HT * 2;
     static constexpr size_t AUX = MU + (size_t)BK_CT * PITCH;           // float4[BK_CT]
     static constexpr size_t SC = AUX + (size_t)BK_CT * 16;              // float[128][BK_SLD]
     static constexpr size_t FREF = SC;                                  // int[WMAX][128]: the new frontier's refs; lies over
@@ -42,12 +42,20 @@ __device__ __forceinline__ void bk_mma(float (&c)[4], const uint32_t (&a)[4], ui
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// slot of `ref` in the open-addressing set (inserted if absent); at most BK_HT distinct refs are ever offered
-__device__ __forceinline__ int bk_insert(int* hkey, int ref) {
-    uint32_t h = ((uint32_t)ref * 2654435761u) >> 20;                   // 12 bits
+// slot of `ref` in the open-addressing set; a new ref is appended to the level's list (its slot in ulist, its column in
+// hidx - both read only after the block barrier that follows the inserts). At most BK_HT distinct refs are ever offered.
+__device__ __forceinline__ uint32_t bk_hash(int ref) { return ((uint32_t)ref * 2654435761u) >> 20; }        // 12 bits
+__device__ __forceinline__ int bk_insert(int* hkey, unsigned short* hidx, unsigned short* ulist, int* ucount, int ref) {
+    uint32_t h = bk_hash(ref);
     for (int probe = 0; probe < BK_HT; ++probe) {
         const int old = atomicCAS(&hkey[h], -1, ref);
-        if (old == -1 || old == ref) break;
+        if (old == -1) {
+            const int idx = atomicAdd(ucount, 1);
+            hidx[h] = (unsigned short)idx;
+            ulist[idx] = (unsigned short)h;
+            break;
+        }
+        if (old == ref) break;
         h = (h + 1) & (BK_HT - 1);
     }
     return (int)h;
@@ -94,13 +102,14 @@ __global__ void __launch_bounds__(BK_THREADS, 2) fsb_beam_block_kernel(SelArgs A
     extern __shared__ __align__(16) unsigned char dsm[];
     int* hkey = (int*)(dsm + SM::HKEY);
     unsigned short* hidx = (unsigned short*)(dsm + SM::HIDX);
-    int* ulist = (int*)(dsm + SM::ULIST);
+    unsigned short* ulist = (unsigned short*)(dsm + SM::ULIST);
     unsigned char* smu = dsm + SM::MU;
     float4* saux = (float4*)(dsm + SM::AUX);
     float* ssc = (float*)(dsm + SM::SC);
     int* frs_ref = (int*)(dsm + SM::FREF) + qi;          // [slot * 128]
     int* frs_meta = (int*)(dsm + SM::FMETA) + qi;
     __shared__ SpineSm<D> sp;
+    __shared__ BeamPre pre;
     __shared__ int ucount;
 
     const float lam = a.lam[hd], sig = a.sigma[hd];
@@ -148,6 +157,8 @@ __global__ void __launch_bounds__(BK_THREADS, 2) fsb_beam_block_kernel(SelArgs A
         if (warp == 0) {
             const int m_b = count_below(F.adm + (int64_t)t * F.m_cap, F.m_tot[t], E);
             build_spine<D>(F, t, m_b, sp, lane);
+            __syncwarp();
+            beam_prefix<D>(F, t, sp, width, lane, pre);
         }
         __syncthreads();
         const int64_t nrow = (int64_t)t * fsb_nodes_per_row(F.m_cap);
@@ -158,79 +169,46 @@ __global__ void __launch_bounds__(BK_THREADS, 2) fsb_beam_block_kernel(SelArgs A
         const int d0 = sp.height;
         const int W = min(width, (d0 >= 5) ? 32 : (1 << d0));
 
-        int fref[BK_HS], fmeta[BK_HS];            // this thread's frontier slots BK_HS * sub + j (the frontier is compact)
-#pragma unroll
-        for (int j = 0; j < BK_HS; ++j) { fref[j] = -1; fmeta[j] = 0; }
-        if (isq && sub == 0) {
-            fref[0] = root;
-            fmeta[0] = (root >= 0) ? __float_as_int(aux[REF_ID(root)].w) : 0;
-        }
-        for (int it = 0; it < 40; ++it) {
-            // ---- which slots expand, which are carried (leaves: budget 1) ----
-            unsigned expm = 0, carm = 0;
-#pragma unroll
-            for (int j = 0; j < BK_HS; ++j) {
-                const bool act = fref[j] != -1;
-                const bool ex = act && (fref[j] < -1 || fmeta[j] < 0);
-                expm |= (ex ? 1u : 0u) << j;
-                carm |= ((act && !ex) ? 1u : 0u) << j;
-            }
-            // ---- children: chunk nodes into the block's set (one insert per distinct node of the warp), spine nodes scored ----
-            int cx[NC];                           // per child: hash slot -> column -> score bits
-            unsigned spm = 0;                     // children that are spine nodes (already scored)
-#pragma unroll
-            for (int c = 0; c < NC; ++c) {
-                const int j = c >> 1, side = c & 1;
-                int cref = -1;
-                if ((expm >> j) & 1) {
-                    cref = (fref[j] >= 0) ? fref[j] + ((~fmeta[j]) >> 4) + 1 + side       // same chunk: the height bits carry over
-                                          : __float_as_int(sp.node[-fref[j] - 2][D + 4 + side]);
-                }
-                const int key = cref >= 0 ? cref : -1;
-                const unsigned grp = __match_any_sync(FS_FULL, key);
+        // one child of this thread: a chunk node goes into the block's set (cx = its slot), a spine node is scored here.
+        // Most nodes are already in the set when a warp offers them (another warp, or an earlier child): one plain read of the
+        // home slot finds those; the rest take the slow path, one insert per distinct node of the warp.
+        auto place = [&](int cref, int c, int (&cx)[NC], unsigned& spm) {
+            const int key = cref >= 0 ? cref : -1;
+            const uint32_t h0 = bk_hash(key);
+            const bool hit = key < 0 || *(volatile int*)&hkey[h0] == key;
+            int slot = (int)h0;
+            if (__any_sync(FS_FULL, !hit)) {
+                const int k2 = hit ? -1 : key;
+                const unsigned grp = __match_any_sync(FS_FULL, k2);
                 const int leader = __ffs(grp) - 1;
-                int slot = 0;
-                if (key >= 0 && lane == leader) slot = bk_insert(hkey, key);
-                cx[c] = __shfl_sync(FS_FULL, slot, leader);
-                if (cref < -1) {
-                    cx[c] = __float_as_int(bk_spine_score<D>(sp.node[-cref - 2], qrow, qn, qpos, lam, inv_two_sig, a.scale));
-                    spm |= 1u << c;
-                }
+                int s2 = 0;
+                if (k2 >= 0 && lane == leader) s2 = bk_insert(hkey, hidx, ulist, &ucount, k2);
+                s2 = __shfl_sync(FS_FULL, s2, leader);
+                if (!hit) slot = s2;
             }
-            if (!__syncthreads_or(expm != 0)) break;
-            nv += 2 * __popc(expm);
-            // ---- the set as a list: every used slot gets a column, and is emptied for the next level ----
-            for (int s = tid; s < BK_HT; s += BK_THREADS) {
-                const int key = hkey[s];
-                if (key != -1) {
-                    const int idx = atomicAdd(&ucount, 1);
-                    hidx[s] = (unsigned short)idx;
-                    ulist[idx] = key;
-                    hkey[s] = -1;
-                }
+            cx[c] = slot;
+            if (cref < -1) {
+                cx[c] = __float_as_int(bk_spine_score<D>(sp.node[-cref - 2], qrow, qn, qpos, lam, inv_two_sig, a.scale));
+                spm |= 1u << c;
             }
-            __syncthreads();
+        };
+        // scores of the children in vm that are chunk nodes (after the block barrier that follows their inserts): the level's
+        // distinct nodes, BK_CT per pass, staged, multiplied with the 128 queries, read back per child
+        auto score_level = [&](int (&cx)[NC], unsigned vm, unsigned spm) {
             const int U = ucount;
-            unsigned pend = 0;                    // chunk children whose score is still to be read
+            unsigned pend = vm & ~spm;
 #pragma unroll
-            for (int c = 0; c < NC; ++c) {
-                if (((expm >> (c >> 1)) & 1) && !((spm >> c) & 1)) {
-                    cx[c] = hidx[cx[c]];
-                    pend |= 1u << c;
-                }
-            }
-            __syncthreads();
-            if (tid == 0) ucount = 0;
-            // ---- score the distinct nodes, BK_CT per pass ----
+            for (int c = 0; c < NC; ++c)
+                if ((pend >> c) & 1) cx[c] = hidx[cx[c]];
             for (int p0 = 0; p0 < U; p0 += BK_CT) {
                 const int ncol = min(BK_CT, U - p0);
                 for (int i = tid; i < BK_CT * CH; i += BK_THREADS) {
                     const int r = i / CH, v = i % CH;
                     uint4 w = make_uint4(0u, 0u, 0u, 0u);
-                    if (r < ncol) w = *(const uint4*)(node_mu + (int64_t)REF_ID(ulist[p0 + r]) * D + v * 8);
+                    if (r < ncol) w = *(const uint4*)(node_mu + (int64_t)REF_ID(hkey[ulist[p0 + r]]) * D + v * 8);
                     *(uint4*)(smu + (size_t)r * SM::PITCH + v * 16) = w;
                 }
-                if (tid < ncol) saux[tid] = aux[REF_ID(ulist[p0 + tid])];
+                if (tid < ncol) saux[tid] = aux[REF_ID(hkey[ulist[p0 + tid]])];
                 uint32_t afr[KS][4];              // this warp's 16 query rows (L1-resident after the first pass)
                 {
                     const bf16* q0 = qbase + (int64_t)mr0 * a.q.sn;
@@ -244,6 +222,7 @@ __global__ void __launch_bounds__(BK_THREADS, 2) fsb_beam_block_kernel(SelArgs A
                     }
                 }
                 __syncthreads();
+                if (tid == 0) ucount = 0;         // every thread has read U
                 {
                     const int ntile = (ncol + 7) >> 3;
                     for (int nt = warp >> 3; nt < ntile; nt += 2) {
@@ -271,14 +250,110 @@ __global__ void __launch_bounds__(BK_THREADS, 2) fsb_beam_block_kernel(SelArgs A
                         pend &= ~(1u << c);
                     }
                 }
+                if (p0 + BK_CT >= U)              // last pass: empty the set for the next level
+                    for (int i = tid; i < U; i += BK_THREADS) hkey[ulist[i]] = -1;
                 __syncthreads();
             }
+        };
+
+        int fref[BK_HS], fmeta[BK_HS];            // this thread's frontier slots BK_HS * sub + j (the frontier is compact)
+#pragma unroll
+        for (int j = 0; j < BK_HS; ++j) { fref[j] = -1; fmeta[j] = 0; }
+        if (pre.rounds > 0) {
+            // ---- the block's query-independent head (the rounds whose children all fit in the frontier): its nodes are
+            // scored once and put into this query's order - older rounds first, a round's nodes by score ----
+            int cx[NC];
+            unsigned vm = 0, spm = 0;
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                const int idx = BK_HS * sub + c;
+                const bool valid = c < BK_HS && isq && idx < pre.n;
+                vm |= (valid ? 1u : 0u) << c;
+                place(valid ? pre.ref[idx] : -1, c, cx, spm);
+            }
+            __syncthreads();
+            score_level(cx, vm, spm);
+            float sc[BK_HS];
+            int rn[BK_HS], rank[BK_HS];
+#pragma unroll
+            for (int c = 0; c < BK_HS; ++c) {
+                const bool valid = (vm >> c) & 1;
+                sc[c] = valid ? __int_as_float(cx[c]) : FS_NEG_SCORE;
+                rn[c] = valid ? pre.rnd[BK_HS * sub + c] : (1 << 20);
+                rank[c] = 0;
+            }
+#pragma unroll
+            for (int i = 0; i < BK_HS; ++i)
+#pragma unroll
+                for (int k = i + 1; k < BK_HS; ++k) {
+                    const bool first = rn[i] < rn[k] || (rn[i] == rn[k] && sc[i] >= sc[k]);
+                    rank[k] += first ? 1 : 0;
+                    rank[i] += first ? 0 : 1;
+                }
+#pragma unroll 1
+            for (int p = 1; p < BK_T; ++p) {
+                const bool plow = (sub ^ p) < sub;
+#pragma unroll
+                for (int o = 0; o < BK_HS; ++o) {
+                    const float po = __shfl_xor_sync(FS_FULL, sc[o], p);
+                    const int pr = __shfl_xor_sync(FS_FULL, rn[o], p);
+#pragma unroll
+                    for (int c = 0; c < BK_HS; ++c)
+                        rank[c] += (pr < rn[c] || (pr == rn[c] && (po > sc[c] || (plow && po == sc[c])))) ? 1 : 0;
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < BK_HS; ++j) { frs_ref[(BK_HS * sub + j) * 128] = -1; frs_meta[(BK_HS * sub + j) * 128] = 0; }
+            __syncwarp();
+#pragma unroll
+            for (int c = 0; c < BK_HS; ++c) {
+                if ((vm >> c) & 1) {
+                    frs_ref[rank[c] * 128] = pre.ref[BK_HS * sub + c];
+                    frs_meta[rank[c] * 128] = pre.meta[BK_HS * sub + c];
+                }
+            }
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < BK_HS; ++j) { fref[j] = frs_ref[(BK_HS * sub + j) * 128]; fmeta[j] = frs_meta[(BK_HS * sub + j) * 128]; }
+            __syncwarp();
+            if (isq && sub == 0) nv += pre.nvis;
+        } else if (isq && sub == 0) {
+            fref[0] = root;
+            fmeta[0] = (root >= 0) ? __float_as_int(aux[REF_ID(root)].w) : 0;
+        }
+        for (int it = 0; it < 40; ++it) {
+            // ---- which slots expand, which are carried (leaves: budget 1) ----
+            unsigned expm = 0, carm = 0;
+#pragma unroll
+            for (int j = 0; j < BK_HS; ++j) {
+                const bool act = fref[j] != -1;
+                const bool ex = act && (fref[j] < -1 || fmeta[j] < 0);
+                expm |= (ex ? 1u : 0u) << j;
+                carm |= ((act && !ex) ? 1u : 0u) << j;
+            }
+            // ---- children ----
+            int cx[NC];                           // per child: hash slot -> column -> score bits
+            unsigned vm = 0, spm = 0;             // children that exist; those that are spine nodes (already scored)
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                const int j = c >> 1, side = c & 1;
+                int cref = -1;
+                if ((expm >> j) & 1) {
+                    cref = (fref[j] >= 0) ? fref[j] + ((~fmeta[j]) >> 4) + 1 + side       // same chunk: the height bits carry over
+                                          : __float_as_int(sp.node[-fref[j] - 2][D + 4 + side]);
+                    vm |= 1u << c;
+                }
+                place(cref, c, cx, spm);
+            }
+            if (!__syncthreads_or(expm != 0)) break;
+            nv += __popc(vm);
+            score_level(cx, vm, spm);
             // ---- rank the query's 32 children: (score desc, position asc); position = 8 sub + c ----
             float sc[NC];
             int rank[NC];
 #pragma unroll
             for (int c = 0; c < NC; ++c) {
-                sc[c] = ((expm >> (c >> 1)) & 1) ? __int_as_float(cx[c]) : FS_NEG_SCORE;
+                sc[c] = ((vm >> c) & 1) ? __int_as_float(cx[c]) : FS_NEG_SCORE;
                 rank[c] = 0;
             }
 #pragma unroll
@@ -326,7 +401,7 @@ __global__ void __launch_bounds__(BK_THREADS, 2) fsb_beam_block_kernel(SelArgs A
 #pragma unroll
                 for (int c = 0; c < NC; ++c) {
                     const int j = c >> 1, side = c & 1;
-                    if (((expm >> j) & 1) && sc[c] > 0.5f * FS_NEG_SCORE && ncar + rank[c] < W) {
+                    if (((vm >> c) & 1) && sc[c] > 0.5f * FS_NEG_SCORE && ncar + rank[c] < W) {
                         const int cref = (fref[j] >= 0) ? fref[j] + ((~fmeta[j]) >> 4) + 1 + side
                                                         : __float_as_int(sp.node[-fref[j] - 2][D + 4 + side]);
                         const int pos = ncar + rank[c];
