@@ -22,15 +22,15 @@ struct RrArgs {
 template <int D>
 struct RrSmem {
     static constexpr int ROWB = D * 2;                       // bytes per key / query row
-    static constexpr int G = (D > 96) ? 8 : RB_WARPS;         // cells staged per round, one per warp (fewer at D = 128: shared memory)
+    static constexpr int G = (D > 64) ? 4 : 8;                // cells staged per round (two CTAs share an SM: 32 / 24 / 32 KB of keys)
     static constexpr int SW = (D == 96) ? 3 : 7;             // 16-byte-chunk XOR mask (keeps D = 96 inside its 4-chunk groups)
     static constexpr size_t Q_OFF = 0;
     static constexpr size_t K_OFF = Q_OFF + (size_t)RB_Q * ROWB;
     static constexpr size_t CAND_OFF = K_OFF + (size_t)G * 32 * ROWB;
     static constexpr size_t U_OFF = CAND_OFF + RB_PAIRS * 4;
     static constexpr size_t CUR_OFF = U_OFF + RB_PAIRS * 4;          // int[RB_PAIRS + 1]
-    static constexpr size_t PIDX_OFF = CUR_OFF + (RB_PAIRS + 4) * 4; // u16[RB_PAIRS]
-    static constexpr size_t SORT_OFF = PIDX_OFF + RB_PAIRS * 2;      // u16[RB_PAIRS]
+    static constexpr size_t PIDX_OFF = K_OFF;                        // u16[RB_PAIRS]: only during the sort, over the key area
+    static constexpr size_t SORT_OFF = CUR_OFF + (RB_PAIRS + 4) * 4; // u16[RB_PAIRS]
     static constexpr size_t BM_OFF = SORT_OFF + RB_PAIRS * 2;        // u32[512] bitmap (16 384 cells), int[512] word base
     static constexpr size_t TOTAL = BM_OFF + 512 * 4 * 2 + 64;
 };
@@ -47,7 +47,7 @@ __device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], 
 }
 
 template <int D>
-__global__ void __launch_bounds__(RB_THREADS, 1) fsb_rerank_block_kernel(RrArgs A) {
+__global__ void __launch_bounds__(RB_THREADS, 2) fsb_rerank_block_kernel(RrArgs A) {
     using SM = RrSmem<D>;
     const fsattn_fsb_select_t& a = A.a;
     extern __shared__ __align__(16) unsigned char smem[];
@@ -173,14 +173,16 @@ __global__ void __launch_bounds__(RB_THREADS, 1) fsb_rerank_block_kernel(RrArgs 
             *(uint4*)(Ks + (size_t)j * 32 * SM::ROWB + sw_off(r, c * 16, SM::ROWB, SM::SW)) = v;
         }
         __syncthreads();
-        if (warp < ncell) {
-            const int ix = c0 + warp;
+        constexpr int WPC = RB_WARPS / SM::G;                     // warps that share a cell's groups of 16 pairs
+        const int cj = warp % SM::G;
+        if (cj < ncell) {
+            const int ix = c0 + cj;
             const int start = ix == 0 ? 0 : cur[ix - 1], end = cur[ix];
             const int cell = cand_s[sorted[start]];
-            const unsigned char* Kc = Ks + (size_t)warp * 32 * SM::ROWB;
+            const unsigned char* Kc = Ks + (size_t)cj * 32 * SM::ROWB;
             const float pcoef = f_mul(lam, ceil[cell]);
             const float cpos = f_mul(f_add((float)cell, 0.5f), 32.0f);
-            for (int p0 = start; p0 < end; p0 += 16) {
+            for (int p0 = start + 16 * (warp / SM::G); p0 < end; p0 += 16 * WPC) {
                 const int pa = p0 + g, pb = p0 + g + 8;
                 const int ida = pa < end ? sorted[pa] : -1, idb = pb < end ? sorted[pb] : -1;
                 const int qa = ida >= 0 ? (ida >> 5) : 0, qb = idb >= 0 ? (idb >> 5) : 0;
@@ -213,6 +215,7 @@ __global__ void __launch_bounds__(RB_THREADS, 1) fsb_rerank_block_kernel(RrArgs 
                     }
                 }
                 // rows g (acc[.][0..1]) and g+8 (acc[.][2..3]): log-sum-exp over the 32 tokens, spread over the quad
+                float mh[2], sh[2];
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
                     float m = -INFINITY;
@@ -229,12 +232,16 @@ __global__ void __launch_bounds__(RB_THREADS, 1) fsb_rerank_block_kernel(RrArgs 
                     for (int nt = 0; nt < 4; ++nt) s += __expf(acc[nt][2 * half] - m) + __expf(acc[nt][2 * half + 1] - m);
                     s += __shfl_xor_sync(FS_FULL, s, 1);
                     s += __shfl_xor_sync(FS_FULL, s, 2);
-                    const int id = half ? idb : ida;
-                    if (tg == 0 && id >= 0) {
-                        const float qpos = (float)(a.q_pos0 + blk * RB_Q + (id >> 5));
-                        const float er = erff(f_div(fabsf(f_add(qpos, -cpos)), two_sig));
-                        u_s[id] = f_add(f_add(m, logf(s)), f_mul(pcoef, er));
-                    }
+                    mh[half] = m; sh[half] = s;
+                }
+                // the quad's lane 0 finishes row g, lane 1 row g + 8 (one logarithm and one erf per lane, both rows at once);
+                // erf is 1 in fp32 from 4 on, which is every cell further than a few sigma from the query
+                const int id = tg == 0 ? ida : (tg == 1 ? idb : -1);
+                if (id >= 0) {
+                    const float qpos = (float)(a.q_pos0 + blk * RB_Q + (id >> 5));
+                    const float x = f_div(fabsf(f_add(qpos, -cpos)), two_sig);
+                    const float er = x < 4.0f ? erff(x) : 1.0f;
+                    u_s[id] = f_add(f_add(tg == 0 ? mh[0] : mh[1], logf(tg == 0 ? sh[0] : sh[1])), f_mul(pcoef, er));
                 }
             }
         }
