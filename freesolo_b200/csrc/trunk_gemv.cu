@@ -144,7 +144,11 @@ int launch_gemv(const fsattn_trunk_gemv_t& a, cudaStream_t st, int sm_count) {
     }
     const int nunits = (a.epilogue == FSATTN_EPI_SWIGLU) ? a.n_out / 2 : a.n_out;
     int blocks = (nunits + GEMV_WARPS - 1) / GEMV_WARPS;
-    if (blocks > sm_count) blocks = sm_count;      // one resident CTA per SM; warps loop over the remaining rows
+    // two resident CTAs per SM, the warps loop over the remaining rows: with one, a warp of the wide projections holds three or
+    // four rows of which only the first is in registers when the producer finishes; with three, the next kernel's CTAs no
+    // longer fit beside this one's and its prologue (weight prefetch) starts late. Measured on the 341M decode step:
+    // 0.640 / 0.596 / 0.657 ms for 1 / 2 / 3.
+    if (blocks > 2 * sm_count) blocks = 2 * sm_count;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(blocks, 1, 1);
     cfg.blockDim = dim3(GEMV_THREADS, 1, 1);
