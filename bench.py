@@ -251,13 +251,19 @@ def time_window_kernel(attn, dev, ctx: int, reps: int = 5):
 def timed_prefill(make_decoder, reps: int = 3):
     """The reference's prefill protocol (experiments/scaling/bench_efficiency.py:166-198, `--warm 1 --nmed 3`): one untimed
     prefill at the full context (the allocator's pools and every kernel attribute are warm afterwards), then the median of
-    `reps` timed ones, each on a fresh decoder (fresh KV stores / forests). Returns (last decoder, median ms, all ms)."""
+    `reps` timed ones, each on a fresh decoder (fresh KV stores / forests). Returns (last decoder, median ms, all ms).
+    PREFILL_PEAK_GIB[0] = the peak allocated bytes over the timed prefills (statistics reset after the warm-up one, the
+    reference's `_reset_mem`; unlike its `retain_kv=False` prefill this one fills the KV store the decode then reads)."""
     gd = make_decoder()
     gd.prefill()
     torch.cuda.synchronize()
     times = []
-    for _ in range(reps):
+    for i in range(reps):
         del gd
+        if i == 0:
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
+            torch.cuda.reset_peak_memory_stats()
         gd = make_decoder()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -266,7 +272,11 @@ def timed_prefill(make_decoder, reps: int = 3):
         e1.record()
         torch.cuda.synchronize()
         times.append(e0.elapsed_time(e1))
+    PREFILL_PEAK_GIB[0] = torch.cuda.max_memory_allocated() / 2 ** 30
     return gd, sorted(times)[len(times) // 2], times
+
+
+PREFILL_PEAK_GIB = [None]
 
 
 def timed_decode(gd, K, Wm):
@@ -368,7 +378,9 @@ def run_fsb_section(args, dev, K, Wm, peak, peak_kind):
     model = make_fsb_model(args, dev, ctx)
     ids = torch.randint(0, model.vocab_size, (args.batch, ctx), generator=torch.Generator().manual_seed(4321 + ctx))
     gd, prefill_ms, _ = timed_prefill(lambda: GraphedDecoder(model, ids, Lmax=ctx + Wm + K + 40, device=dev, kv="int8"))
+    prefill_peak = PREFILL_PEAK_GIB[0]
     ms = timed_decode(gd, K, Wm)
+    decode_peak = torch.cuda.max_memory_allocated() / 2 ** 30
     fo = gd.cache[0].fsb
     nL = len(gd.cache)
     sb, kb = fsb_step_bytes(model, gd, args.batch)
@@ -377,6 +389,7 @@ def run_fsb_section(args, dev, K, Wm, peak, peak_kind):
                        f"then {K} decode steps, batch {args.batch}, int8 KV",
            "decode_tok_s": tps, "decode_ms_per_step": ms / K, "prefill_ktok_s": ktoks, "prefill_ms": prefill_ms,
            "vs_published_decode": _pub("fsb_decode_tps", ctx, tps), "vs_published_prefill": _pub("fsb_prefill_ktoks", ctx, ktoks),
+           "prefill_peak_gib": prefill_peak, "decode_peak_gib": decode_peak,
            "roofline": {"what": "whole decode step: weights + per layer window, both beams' visited nodes, the candidates' token "
                                 "keys, the cells read", "bound": "hbm", "step_bytes": sb, "attn_bytes_per_layer": kb,
                         "achieved": sb / (ms / K * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
@@ -413,12 +426,15 @@ def run_dense_section(args, dev, K, Wm, peak, peak_kind):
     model = FreeSoloLM.from_config(args.model, max_seq_len=ctx + 512, **serve_kwargs("dense")).to(torch.bfloat16).to(dev).eval()
     ids = torch.randint(0, model.vocab_size, (1, ctx), generator=torch.Generator().manual_seed(4321 + ctx))
     gd, pms, _ = timed_prefill(lambda: GraphedDecoder(model, ids, Lmax=ctx + Wm + K + 40, device=dev, kv="int8"))
+    prefill_peak = PREFILL_PEAK_GIB[0]
     ms = timed_decode(gd, K, Wm)
+    decode_peak = torch.cuda.max_memory_allocated() / 2 ** 30
     sb = dense_step_bytes(model, gd, 1, ctx)
     tps, ktoks = K / (ms * 1e-3), ctx / pms
     out = {"workload": f"FS (dense) {args.model}: every visible cell scored, prefill at {ctx}, then {K} decode steps, batch 1, int8 KV",
            "decode_tok_s": tps, "decode_ms_per_step": ms / K, "prefill_ktok_s": ktoks, "prefill_ms": pms,
            "vs_published_decode": _pub("dense_decode_tps", ctx, tps), "vs_published_prefill": _pub("dense_prefill_ktoks", ctx, ktoks),
+           "prefill_peak_gib": prefill_peak, "decode_peak_gib": decode_peak,
            "roofline": {"what": "whole decode step", "bound": "hbm", "step_bytes": sb, "achieved": sb / (ms / K * 1e-3) / 1e9, "peak": peak,
                         "unit": "GB/s", "frac": sb / (ms / K * 1e-3) / 1e9 / peak, "peak_kind": peak_kind},
            "gpu_launches": K * gd.launches_per_step(), "kv_faults": list(gd.kv_faults())}
@@ -585,6 +601,7 @@ def run_ours(args):
     warm.prefill()
     del warm
     gd, prefill_ms, prefill_all = timed_prefill(lambda: GraphedDecoder(model, ids, Lmax=ctx + total, device=dev, kv=args.kv))
+    prefill_peak = PREFILL_PEAK_GIB[0]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     for _ in range(Wm):
         gd.step()
@@ -605,6 +622,7 @@ def run_ours(args):
         e1.record()
         barrier()
     ms = e0.elapsed_time(e1)
+    decode_peak = torch.cuda.max_memory_allocated() / 2 ** 30       # the timed prefills + the graph capture + the decode steps
     # ---- end to end: token id from pinned host memory in, sampled token back to the host, every step --------------
     tok_host = torch.zeros(B, 1, dtype=torch.int64).pin_memory()
     tok_host.copy_(gd.tok.cpu())
@@ -649,6 +667,7 @@ def run_ours(args):
                           "frac": step_bytes / (ms / K * 1e-3) / 1e9 / hbm_peak, "peak_kind": peak_kind},
         "prefill": {"ktok_s": B * ctx / prefill_ms, "ms": prefill_ms, "runs_ms": prefill_all,
                     "vs_published": _pub("fsl_prefill_ktoks", ctx, B * ctx / prefill_ms) if (args.model == "340m" and B == 1) else None,
+                    "peak_gib": prefill_peak,
                     "note": "median of 3 after one untimed full-context prefill (the reference's --warm 1 --nmed 3), incl. KV store "
                             "fill and last-token logits; outside the headline's timed region"},
         "kv_bytes_per_layer": gd.kv_bytes() // nL, "kv_faults": list(faults),
@@ -679,7 +698,7 @@ def run_ours(args):
         line["decode_kernel_roofline"] = dk
     else:
         line["roofline"] = dk
-    line["peak_mem_gib"] = torch.cuda.max_memory_allocated() / 2 ** 30
+    line["peak_mem_gib"] = decode_peak
     if world == 1 and args.model == "340m":
         line["window_roofline"] = time_window_kernel(gd.attn_core[0], dev, ctx)
     del gd

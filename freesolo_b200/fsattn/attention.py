@@ -92,9 +92,23 @@ class Rotary(nn.Module):
             self._build_cache(need)
         c = self._bf16
         if c is None or c[0].shape[0] != self.cos_cached.shape[0] or c[0].device != self.cos_cached.device:
-            c = (self.cos_cached.to(torch.bfloat16).contiguous(), self.sin_cached.to(torch.bfloat16).contiguous())
+            cos, sin = self.cos_cached.to(torch.bfloat16).contiguous(), self.sin_cached.to(torch.bfloat16).contiguous()
+            # every layer of a model builds the same tables (33 MB per layer at 131 072 positions): the layers share one copy
+            key = (cos.device, self.dim, self.base, self.original_max_seq_len, self.beta_fast, self.beta_slow)
+            sh = _SHARED_ROPE.get(key)
+            if sh is not None and sh[0].shape == cos.shape and torch.equal(sh[0], cos) and torch.equal(sh[1], sin):
+                cos, sin = sh
+                if self.cos_cached.dtype == torch.bfloat16:      # the module's own buffers were duplicates of it
+                    self.register_buffer("cos_cached", cos, persistent=False)
+                    self.register_buffer("sin_cached", sin, persistent=False)
+            else:
+                _SHARED_ROPE[key] = (cos, sin)
+            c = (cos, sin)
             self._bf16 = c
         return c
+
+
+_SHARED_ROPE = {}
 
 
 _SIDE_STREAMS = {}
@@ -329,34 +343,46 @@ class FSAttn(nn.Module):
         return c[1]
 
     # ---- forward ---------------------------------------------------------------------------------------------------------
-    def forward(self, x: torch.Tensor, mask: torch.Tensor | None = None, cache=None) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, mask: torch.Tensor | None = None, cache=None, pre_norm=None) -> torch.Tensor:
+        """pre_norm (optional, not in the reference's signature): the block's input norm, applied here to x in token chunks
+        on the way into the projection, so that a long prefill never holds a normalised copy of the whole sequence."""
         if cache is None:
             raise NotImplementedError("this build covers cached inference only: pass an FSKVCache (the training forward "
                                       "stays with the reference implementation)")
-        return self._forward_cached(x, cache)
+        return self._forward_cached(x, cache, pre_norm)
 
-    def _project_qkv(self, x):
+    PROJ_CHUNK = 16384          # tokens per projection call when the input norm is applied here
+
+    def _project_qkv(self, x, pre_norm=None):
         B, N, _ = x.shape
         H, D = self.n_heads, self.head_dim
         if self.W_q.bias is not None:
             raise NotImplementedError("projection biases are not supported (the LM uses bias=False)")
         w, dm = self._ensure_qkv_cache()
-        qkv = F.linear(x, w)                                   # (B, N, 3d), one GEMM
+        if pre_norm is None:
+            qkv = F.linear(x, w)                               # (B, N, 3d), one GEMM
+        else:
+            qkv = torch.empty(B, N, 3 * dm, dtype=x.dtype, device=x.device)
+            wt = w.t()
+            for b in range(B):
+                for s0 in range(0, N, self.PROJ_CHUNK):
+                    torch.mm(pre_norm(x[b, s0:s0 + self.PROJ_CHUNK]), wt, out=qkv[b, s0:s0 + self.PROJ_CHUNK])
         q, k, v = (qkv[..., i * dm:(i + 1) * dm].view(B, N, H, D).transpose(1, 2) for i in range(3))
         return q, k, v
 
     @torch.no_grad()
-    def _forward_cached(self, x, cache):
+    def _forward_cached(self, x, cache, pre_norm=None):
         B, N, _ = x.shape
         self._assert_cacheable(phase="prefill" if (cache.pos == 0 and N > 1) else "decode")
         if x.dtype != torch.bfloat16 or not x.is_cuda:
             raise RuntimeError("FSAttn runs on bf16 CUDA activations only (there is no CPU or fp32 path)")
-        Q, K, V = self._project_qkv(x)
+        Q, K, V = self._project_qkv(x, pre_norm)
         if cache.pos == 0 and N > 1:
             y = self._prefill(Q, K, V, cache)
         else:
             ys = [self._decode_one(Q[:, :, t], K[:, :, t], V[:, :, t], cache) for t in range(N)]
             y = torch.stack(ys, dim=1) if N > 1 else ys[0].unsqueeze(1)
+        del Q, K, V                                            # the projections are dead: W_o's output reuses their memory
         return self.W_o(y)
 
     def _prefill(self, Q, K, V, cache):

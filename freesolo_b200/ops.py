@@ -229,6 +229,28 @@ def window_prefill(Q, K, V, cos, sin, W: int, scale: float, pos0: int = 0, impl:
     assert cos.dtype == torch.bfloat16 and sin.dtype == torch.bfloat16 and cos.is_contiguous() and sin.is_contiguous()
     assert cos.shape[1] == D and cos.shape[0] >= pos0 + N, "rope table too short"
     assert out.is_contiguous()
+    tc = impl == 0 and D == 64 and W >= 64 and W % 64 == 0
+    if tc and B == 1 and N > 2 * WINDOW_CHUNK:
+        # A long single sequence goes through the tensor-core kernel in chunks of WINDOW_CHUNK queries, LAST chunk first, so
+        # that its scratch (rotated Q and K) is chunk-sized: 69 MB instead of 537 MB at 131 072 tokens. A chunk starts one
+        # window (rounded up to whole 128-query blocks) early; those rows lack their own left context, their outputs are
+        # wrong, and the next call - the chunk before, which ends where this one's own rows begin - overwrites them. Tiles
+        # stay aligned to absolute positions, so every query sees the same tiles in the same order as in a single call.
+        halo = (int(W) + 127) // 128 * 128
+        for c0 in reversed(range(0, N, WINDOW_CHUNK)):
+            c1, h0 = min(N, c0 + WINDOW_CHUNK), max(0, c0 - halo)
+            _window_prefill_call(Q[:, :, h0:c1], K[:, :, h0:c1], V[:, :, h0:c1], cos, sin, W, scale, pos0 + h0, impl,
+                                 out[:, h0:c1], status, tc)
+        return out
+    _window_prefill_call(Q, K, V, cos, sin, W, scale, pos0, impl, out, status, tc)
+    return out
+
+
+WINDOW_CHUNK = 16384
+
+
+def _window_prefill_call(Q, K, V, cos, sin, W, scale, pos0, impl, out, status, tc):
+    B, H, N, D = Q.shape
     a = L.WindowPrefill()
     a.q, a.k, a.v = _bhnd(Q, "Q"), _bhnd(K, "K"), _bhnd(V, "V")
     a.cos, a.sin = cos.data_ptr(), sin.data_ptr()
@@ -237,7 +259,7 @@ def window_prefill(Q, K, V, cos, sin, W: int, scale: float, pos0: int = 0, impl:
     a.out = out.data_ptr()
     a.impl = int(impl)
     ws = None
-    if impl == 0 and D == 64 and W >= 64 and W % 64 == 0:
+    if tc:
         # scratch of the tensor-core kernel (rotated Q and K); TMA wants a 16-byte aligned base, which torch's allocator
         # (512-byte aligned blocks) always gives
         nbytes = 2 * B * H * N * D * 2
@@ -247,7 +269,6 @@ def window_prefill(Q, K, V, cos, sin, W: int, scale: float, pos0: int = 0, impl:
     L.call("fsattn_window_prefill", a, _stream(Q))
     if ws is not None:
         ws.record_stream(torch.cuda.current_stream(Q.device))
-    return out
 
 
 def window_prefill_static(Q, K, V, cos, sin, W: int, scale: float, pos0: int = 0, out=None, status=None):

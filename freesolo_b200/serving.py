@@ -94,8 +94,8 @@ class AttentionWithRoPE(nn.Module):
         self.fsattn = FSAttn(d_model, n_heads, causal=causal, bias=False, use_rope=use_rope, max_seq_len=max_seq_len,
                              **attn_kwargs)
 
-    def forward(self, x, cache=None):
-        return self.fsattn(x, cache=cache)
+    def forward(self, x, cache=None, pre_norm=None):
+        return self.fsattn(x, cache=cache, pre_norm=pre_norm)
 
 
 class TransformerBlock(nn.Module):
@@ -110,14 +110,17 @@ class TransformerBlock(nn.Module):
     def forward(self, x, cache=None):
         """RMSNorm -> attention -> residual -> RMSNorm -> SwiGLU -> residual (experiments/scaling/model.py:211-237); the
         FFN of a long prefill runs in token chunks to bound its intermediate."""
-        x = x + self.attn(self.ln1(x), cache=cache)
         N = x.shape[1]
         chunk = 16384
-        if N > chunk:
+        if N > chunk and not torch.is_grad_enabled():
+            # long prefill: the input norm runs inside the attention in token chunks, the residuals are added in place
+            # (x is this forward's own activation: the embedding output or the previous block's result), the FFN in chunks
+            x.add_(self.attn(x, cache=cache, pre_norm=self.ln1))
             for s0 in range(0, N, chunk):
                 xc = x[:, s0:s0 + chunk]
                 xc.add_(self.ffn(self.ln2(xc)))
             return x
+        x = x + self.attn(self.ln1(x), cache=cache)
         return x + self.ffn(self.ln2(x))
 
 

@@ -231,6 +231,22 @@ def test_window_prefill_shapes(dev, N, W, pos0):
         _close(out.view(B, N, H, D).transpose(1, 2), want.to(torch.bfloat16), f"window N={N} W={W} pos0={pos0} impl={impl}")
 
 
+def test_window_prefill_in_chunks_is_bit_identical(dev, monkeypatch):
+    """A long single sequence goes through the tensor-core window kernel in query chunks (last chunk first, each starting a
+    window early, the wrong halo rows overwritten by the chunk before): the result equals the one-call result bit for bit."""
+    from freesolo_b200 import ops
+    H, D, N, W = 2, 64, 5000, 512
+    g = torch.Generator().manual_seed(5)
+    Q, K, V = (torch.randn(1, H, N, D, generator=g).to(torch.bfloat16).to(dev) for _ in range(3))
+    cos, sin = (t.to(dev) for t in fsl.rope_tables(D, 8192, torch.bfloat16))
+    whole = ops.window_prefill(Q, K, V, cos, sin, W, 0.125, pos0=3)
+    monkeypatch.setattr(ops, "WINDOW_CHUNK", 1024)
+    parts = ops.window_prefill(Q, K, V, cos, sin, W, 0.125, pos0=3)
+    assert torch.equal(whole, parts)
+    monkeypatch.setattr(ops, "WINDOW_CHUNK", 640)          # chunks that are not whole multiples of the window
+    assert torch.equal(whole, ops.window_prefill(Q, K, V, cos, sin, W, 0.125, pos0=3))
+
+
 @pytest.mark.parametrize("kind", KINDS)
 def test_readout_combine(dev, kind):
     from freesolo_b200 import ops
