@@ -407,6 +407,42 @@ def run_fsb_section(args, dev, K, Wm, peak, peak_kind):
     return out
 
 
+def run_linear_section(args, dev, ctx):
+    """The streaming cache (LinearFSCache, a state of fixed size per layer): the 341M FS-L model takes a ctx-token prompt
+    in 2048-token chunks, then a few greedy tokens through the same caches (eager, one attend per layer per token)."""
+    from freesolo_b200.fsattn.kv_cache import linear_prefill, make_caches
+    from freesolo_b200.serving import FreeSoloLM, extend_rope_cache, lm_head, serve_kwargs, trunk_cached
+    torch.manual_seed(0)
+    model = FreeSoloLM.from_config(args.model, max_seq_len=ctx + 512, **serve_kwargs("sparse")).to(torch.bfloat16).to(dev).eval()
+    extend_rope_cache(model, ctx + 64)
+    ids = torch.randint(0, model.vocab_size, (1, ctx), generator=torch.Generator().manual_seed(4321 + ctx)).to(dev)
+    with torch.no_grad():
+        linear_prefill(model, ids[:, :4096], make_caches(model, linear=True))        # untimed: handles, allocator pools
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        torch.cuda.reset_peak_memory_stats()
+        caches = make_caches(model, linear=True)
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record()
+        h = linear_prefill(model, ids, caches)
+        e1.record()
+        tok = lm_head(model, h[:, -1]).argmax(-1).view(1, 1)
+        steps = 8
+        for _ in range(steps):
+            tok = lm_head(model, trunk_cached(model, tok, caches)[:, -1]).argmax(-1).view(1, 1)
+        e2.record()
+        torch.cuda.synchronize()
+    pms, dms = e0.elapsed_time(e1), e1.elapsed_time(e2)
+    out = {"workload": f"FS-L {args.model} through LinearFSCache: {ctx}-token prompt in 2048-token chunks, then {steps} eager tokens",
+           "prefill_ktok_s": ctx / pms, "prefill_ms": pms, "decode_tok_s": steps / (dms * 1e-3),
+           "state_bytes_per_layer": caches[0].state_bytes(), "peak_gib": torch.cuda.max_memory_allocated() / 2 ** 30,
+           "note": "state and activations do not grow with the prompt; every 128-token block is one readout launch plus the "
+                   "pool bookkeeping in torch operations, so the rate is launch-bound (the reference's is pure torch)"}
+    del caches, model
+    torch.cuda.empty_cache()
+    return out
+
+
 def dense_step_bytes(model, gd, B, ctx, int8=True):
     """Dense FS decode step: weights + per layer the window, the fp32 mean key and ceiling of EVERY visible cell, the kk
     cells read, the new row."""
@@ -711,6 +747,8 @@ def run_ours(args):
         line["fsb"] = run_fsb_section(args, dev, K, Wm, hbm_peak, peak_kind)
     if world == 1 and not args.no_dense and args.model == "340m":
         line["fs_dense"] = run_dense_section(args, dev, K, Wm, hbm_peak, peak_kind)
+    if world == 1 and args.linear_ctx > 0 and args.model == "340m" and B == 1:
+        line["linear_cache"] = run_linear_section(args, dev, args.linear_ctx)
     if not args.no_config4 and args.model == "340m" and B == 1 and not heads:
         per = max(1, 32 // world)
         key = "config4" if world == 1 else "config4_split"
@@ -755,6 +793,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-fsb", action="store_true", help="skip the FS-B section (BASELINE config 3) of the N=1 line")
     ap.add_argument("--no-dense", action="store_true", help="skip the dense FS section of the N=1 line")
+    ap.add_argument("--linear-ctx", type=int, default=16384,
+                    help="prompt length of the streaming-cache (LinearFSCache) leg of the N=1 line; 0 skips it")
     ap.add_argument("--no-contexts", action="store_true", help="skip the 4k / 16k / 64k legs")
     ap.add_argument("--no-config4", action="store_true", help="skip BASELINE config 4 (743M-class, 32 sequences)")
     ap.add_argument("--no-head-leg", action="store_true", help="N > 1: skip the head-sharded leg")

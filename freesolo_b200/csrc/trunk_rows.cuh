@@ -5,7 +5,10 @@
 
 namespace {
 
-constexpr int GEMV_THREADS = 256;
+#ifndef FS_GEMV_THREADS
+#define FS_GEMV_THREADS 256
+#endif
+constexpr int GEMV_THREADS = FS_GEMV_THREADS;
 constexpr int GEMV_WARPS = GEMV_THREADS / 32;
 
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

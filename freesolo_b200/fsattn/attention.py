@@ -377,6 +377,11 @@ class FSAttn(nn.Module):
         if x.dtype != torch.bfloat16 or not x.is_cuda:
             raise RuntimeError("FSAttn runs on bf16 CUDA activations only (there is no CPU or fp32 path)")
         Q, K, V = self._project_qkv(x, pre_norm)
+        if getattr(cache, "attend", None) is not None:
+            # the streaming cache runs the layer's attention itself (src/fsattn/attention.py:995-999)
+            out = cache.attend(Q, K, V)
+            del Q, K, V
+            return self.W_o(out.transpose(1, 2).reshape(B, N, self.d_model))
         if cache.pos == 0 and N > 1:
             y = self._prefill(Q, K, V, cache)
         else:

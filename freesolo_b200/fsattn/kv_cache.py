@@ -10,6 +10,8 @@ Differences from the reference that callers can observe:
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from .. import ops
@@ -257,13 +259,36 @@ class FSKVCache:
 
 
 def make_caches(model, *, lean_prefill=False, reserve=0, linear=None, retain_kv: bool = True) -> list:
-    """One FSKVCache per layer (experiments/scaling/kv_cache.py:467-481)."""
-    if linear:
-        raise NotImplementedError("the LinearFSCache streaming prefill is not part of this build")
+    """One FSKVCache per layer, or one LinearFSCache (fixed-size streaming state) with linear=True or FSL_LINEAR_CACHE=1
+    (experiments/scaling/kv_cache.py:467-481)."""
+    linear = os.environ.get("FSL_LINEAR_CACHE", "0") == "1" if linear is None else linear
     caches = []
     for blk in model.blocks:
         a = blk.attn.fsattn
-        c = FSKVCache(getattr(a, "inner", a), lean_prefill=lean_prefill, retain_kv=retain_kv)   # a head shard wraps its layer
+        a = getattr(a, "inner", a)                               # a head shard wraps its layer
+        if linear:
+            from .linear_cache import LinearFSCache
+            caches.append(LinearFSCache(a))
+            continue
+        c = FSKVCache(a, lean_prefill=lean_prefill, retain_kv=retain_kv)
         c.reserve = reserve
         caches.append(c)
     return caches
+
+
+@torch.no_grad()
+def linear_prefill(model, idx, cache, *, chunk_size=2048, trunk=None):
+    """Prompt through the model in chunks of chunk_size tokens with streaming caches in every layer: activations and
+    state stay bounded whatever the prompt length (experiments/scaling/kv_cache.py:529-538). Returns the last position's
+    hidden state (B,1,d). `trunk(model, ids, caches)` runs the blocks (the serving module's trunk_cached by default)."""
+    if chunk_size <= 0 or idx.shape[1] == 0:
+        raise ValueError("linear_prefill needs a positive chunk size and nonempty input")
+    if not all(getattr(c, "bounded", False) for c in cache):
+        raise ValueError("linear_prefill requires bounded caches in every layer")
+    if trunk is None:
+        from ..serving import trunk_cached as trunk
+    device = model.tok_emb.weight.device
+    hidden = None
+    for start in range(0, idx.shape[1], chunk_size):
+        hidden = trunk(model, idx[:, start:start + chunk_size].to(device), cache)
+    return hidden[:, -1:].clone()

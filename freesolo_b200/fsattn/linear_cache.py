@@ -1,0 +1,235 @@
+"""Streaming FS-L cache with a state of fixed size (ref: src/fsattn/linear_cache.py:33-240, `LinearFSCache`).
+
+The reference keeps, per layer, exactly what a later query of FS-L can read: the P completed cells with the highest
+ceilings (ties to the lower cell), the Wc newest completed cells, the tokens of the cells still open, and the last W
+keys/values of the window - and rebuilds that state with gathers and concatenations at every 128-token block. Here
+the same state lives in buffers allocated once:
+
+    ids / prio / mean / k / v   C = P + Wc slots: [0, P) the top list in no particular order, [P, C) a ring of the newest
+                                cells (cell c sits in slot P + c mod Wc); an empty slot has id -1; one more slot at the
+                                end takes the writes of new cells that do not make the top list
+    win_k / win_v               the last <= W raw rows;  pend_k / pend_v  the rows of the cells not yet eligible
+
+At a block change only the cells that ENTER the top list are written, into the slots of the cells that leave it (at
+most Bq/s = 4 of them), so a block costs a few kilobytes of traffic instead of a copy of the whole pool. The two hot
+operations are this library's kernels: the window branch of a whole `attend` call is one launch of the tensor-core
+window kernel over [last W rows | new rows], and every block's long-range branch is one launch of the fused readout +
+combine kernel reading the pool slots as cells. Cell statistics come from the cell-ingest kernel (bit-exact mean and
+ceiling); the candidate scores (at most 72 per query) and the bookkeeping are torch operations on the device.
+
+Selections and outputs equal the standard FS-L prefill over the same tokens (same candidates: prefix top-P plus the Wc
+newest; same scores; ties to the lower cell id), which is how the reference's own tests state it.
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import ops
+
+
+class LinearFSCache:
+    bounded = True
+
+    def __init__(self, attn):
+        attn._assert_cacheable(phase="prefill")
+        if attn._is_dense_lr():
+            raise ValueError("LinearFSCache requires native prefix pruning.")
+        if getattr(attn, "fsb_enabled", False):
+            raise NotImplementedError("FS-B has no bounded-cache (linear) path; use FSKVCache.")
+        self.attn = attn
+        self.s, self.Bq, self.W = attn.cell_stride, attn._cell_block, attn.window_size
+        self.P, self.Wc = attn._pool_cfg()
+        if min(self.s, self.Bq, self.P) <= 0 or min(self.W, self.Wc) < 0:
+            raise ValueError("Invalid linear-cache capacities.")
+        self.C = self.P + self.Wc
+        self.pos = 0
+        self.eligible = 0              # completed cells visible to the current block
+        self.block_start = -1
+        self.pool = None               # dict of views for `select`, None while no cell is eligible
+        self.max_merge_cells = self.merged_cells = self.updates = 0
+        self._ready = False
+
+    # ---- state ---------------------------------------------------------------------------------------------------------
+    def _alloc(self, k):
+        B, H, _, D = k.shape
+        dev, C, s = k.device, self.C, self.s
+        self.ids = torch.full((B, H, C + 1), -1, dtype=torch.int64, device=dev)
+        self.prio = torch.full((B, H, C + 1), float("-inf"), dtype=torch.float32, device=dev)
+        self.mean = torch.zeros(B, H, C + 1, D, dtype=torch.float32, device=dev)
+        self.k = torch.zeros(B, H, (C + 1) * s, D, dtype=torch.bfloat16, device=dev)
+        self.v = torch.zeros(B, H, (C + 1) * s, D, dtype=torch.bfloat16, device=dev)
+        self.win_k = torch.zeros(B, H, 0, D, dtype=torch.bfloat16, device=dev)
+        self.win_v = torch.zeros(B, H, 0, D, dtype=torch.bfloat16, device=dev)
+        self.pend_k = torch.zeros(B, H, 0, D, dtype=torch.bfloat16, device=dev)
+        self.pend_v = torch.zeros(B, H, 0, D, dtype=torch.bfloat16, device=dev)
+        self._ready = True
+
+    _TENSORS = ("ids", "prio", "mean", "k", "v", "win_k", "win_v", "pend_k", "pend_v")
+
+    def fork(self):
+        """An independent copy of the state (ref: linear_cache.py:207-211)."""
+        other = object.__new__(type(self))
+        other.__dict__ = dict(self.__dict__)
+        if self._ready:
+            for name in self._TENSORS:
+                setattr(other, name, getattr(self, name).clone())
+            other.pool = None
+            other.block_start = -1       # the views of `pool` are rebuilt on the copy's own buffers
+        return other
+
+    def state_bytes(self) -> int:
+        if not self._ready:
+            return 0
+        return sum(getattr(self, n).untyped_storage().nbytes() for n in self._TENSORS)
+
+    # ---- block change: the cells completed since the last one become eligible -------------------------------------------
+    def prepare(self):
+        start = self.pos // self.Bq * self.Bq
+        if start == self.block_start:
+            return
+        s, P, Wc = self.s, self.P, self.Wc
+        count = start // s - self.eligible
+        if count > 0:
+            n = count * s
+            nk, nv = self.pend_k[:, :, :n].contiguous(), self.pend_v[:, :, :n].contiguous()
+            mean, prio = ops.cell_stats(nk, count)                       # (B,H,count,D), (B,H,count) fp32
+            B, H = prio.shape[:2]
+            dev = prio.device
+            new_ids = torch.arange(self.eligible, self.eligible + count, device=dev).view(1, 1, count).expand(B, H, count)
+            width = min(P, self.eligible) + count
+            self.max_merge_cells = max(self.max_merge_cells, width)
+            self.merged_cells += width
+            self.updates += 1
+            # the P best of (top list, new cells) by (ceiling desc, cell id asc); an empty slot loses to everything
+            cand_prio = torch.cat([self.prio[:, :, :P], prio], dim=2)
+            cand_ids = torch.cat([self.ids[:, :, :P], new_ids], dim=2)
+            by_id = cand_ids.masked_fill(cand_ids < 0, torch.iinfo(torch.int64).max).argsort(dim=-1, stable=True)
+            rank_in_id = cand_prio.gather(-1, by_id).argsort(dim=-1, descending=True, stable=True)
+            order = by_id.gather(-1, rank_in_id)                         # candidates, best first
+            keep = torch.zeros(B, H, P + count, dtype=torch.bool, device=dev)
+            keep.scatter_(-1, order[:, :, :P], True)
+            leave = ~keep[:, :, :P]                                       # top slots that are free or lose their cell
+            enter = keep[:, :, P:]                                        # new cells that make the list
+            # the r-th entering cell takes the r-th leaving slot (there are at least as many: |keep| = P); the others are
+            # written to the spare slot C, so that no two writes of one scatter meet
+            slot_rank = (leave.cumsum(-1) - 1).masked_fill(~leave, P + count)
+            leaving_slots = slot_rank.argsort(dim=-1, stable=True)[:, :, :count]          # (B,H,count)
+            target = leaving_slots.gather(-1, (enter.cumsum(-1) - 1).clamp_(min=0))
+            target = torch.where(enter, target, torch.full_like(target, self.C))
+            D = mean.shape[-1]
+            self.ids.scatter_(-1, target, new_ids)
+            self.prio.scatter_(-1, target, prio)
+            self.mean.scatter_(2, target.unsqueeze(-1).expand(B, H, count, D), mean)
+            rows = (target.unsqueeze(-1) * s + torch.arange(s, device=dev)).reshape(B, H, n)      # row of every new token
+            r4 = rows.unsqueeze(-1).expand(B, H, n, D)
+            self.k.scatter_(2, r4, nk)
+            self.v.scatter_(2, r4, nv)
+            self.ids[:, :, self.C] = -1
+            self.prio[:, :, self.C] = float("-inf")
+            if Wc:
+                # ring of the newest cells: cell c in slot P + c mod Wc (of more than Wc new cells the last Wc stay)
+                first = max(0, count - Wc)
+                cells = torch.arange(self.eligible + first, self.eligible + count, device=dev)
+                sl = P + cells % Wc
+                self.ids[:, :, sl] = new_ids[:, :, first:]
+                self.prio[:, :, sl] = prio[:, :, first:]
+                self.mean[:, :, sl] = mean[:, :, first:]
+                rr = (sl.unsqueeze(-1) * s + torch.arange(s, device=dev)).reshape(-1)
+                self.k[:, :, rr] = nk[:, :, first * s:]
+                self.v[:, :, rr] = nv[:, :, first * s:]
+            self.pend_k, self.pend_v = self.pend_k[:, :, n:].clone(), self.pend_v[:, :, n:].clone()
+            self.eligible += count
+        self.block_start = start
+        if self.eligible == 0:
+            self.pool = None
+            return
+        # a ring cell that is also in the top list counts once (ref: linear_cache.py:114-118, later occurrence dropped)
+        C = self.C
+        top_ids, ring_ids = self.ids[:, :, :P], self.ids[:, :, P:C]
+        dup = (ring_ids.unsqueeze(-1) == top_ids.unsqueeze(-2)).any(-1)
+        valid = self.ids[:, :, :C] >= 0
+        valid[:, :, P:] &= ~dup
+        self.pool = dict(ids=self.ids[:, :, :C], priority=self.prio[:, :, :C], mean=self.mean[:, :, :C],
+                         k=self.k[:, :, :C * s], v=self.v[:, :, :C * s], valid=valid)
+
+    # ---- new tokens ------------------------------------------------------------------------------------------------------
+    def ingest(self, k, v):
+        """Append the raw keys / values of n tokens of ONE query block (ref: linear_cache.py:120-130)."""
+        n = k.shape[2]
+        if n > self.Bq - self.pos % self.Bq:
+            raise ValueError("ingest must not cross a query-block boundary")
+        if not self._ready:
+            self._alloc(k)
+        k, v = k.to(torch.bfloat16), v.to(torch.bfloat16)
+        self.pend_k, self.pend_v = torch.cat([self.pend_k, k], dim=2), torch.cat([self.pend_v, v], dim=2)
+        W = self.W
+        self.win_k = torch.cat([self.win_k, k], dim=2)[:, :, -W:] if W else self.win_k[:, :, :0]
+        self.win_v = torch.cat([self.win_v, v], dim=2)[:, :, -W:] if W else self.win_v[:, :, :0]
+        self.pos += n
+
+    # ---- selection over the pool (ref: linear_cache.py:154-170) --------------------------------------------------------------
+    def select(self, q):
+        """q (B,H,n,D) at positions pos .. pos+n-1 -> (slots (B,H,n,k) int64 into the pool, cell ids with -1 for none)."""
+        pool = self.pool
+        if pool is None:
+            return None, None
+        a = self.attn
+        lam, sigma, _, _ = a.head_params()
+        content = torch.einsum("bhqd,bhcd->bhqc", q.float(), pool["mean"]) * a.scale
+        score = content
+        if not getattr(a, "sel_content_only", False):
+            qpos = torch.arange(q.shape[2], device=q.device, dtype=torch.float32) + self.pos
+            centre = (pool["ids"].float() + 0.5) * self.s
+            dist = (qpos[None, None, :, None] - centre[:, :, None]).abs()
+            gate = torch.erf(dist / (2 * sigma.to(q.device)[None, :, None, None]))
+            score = content + lam.to(q.device)[None, :, None, None] * pool["priority"][:, :, None] * gate
+        ok = pool["valid"][:, :, None]
+        score = score.masked_fill(~ok, float("-inf"))
+        ids = pool["ids"][:, :, None].expand_as(score).masked_fill(~ok, -1)
+        # the best k by (score desc, cell id asc): order by id first, then a stable descending sort of the scores
+        by_id = ids.masked_fill(ids < 0, torch.iinfo(torch.int64).max).argsort(dim=-1, stable=True)
+        k = min(a.cell_topk, self.eligible)
+        best = score.gather(-1, by_id).argsort(dim=-1, descending=True, stable=True)[..., :k]
+        slots = by_id.gather(-1, best)
+        return slots, ids.gather(-1, slots)
+
+    # ---- one forward of the layer's attention over new tokens (ref: linear_cache.py:192-205) -------------------------------
+    def attend(self, q, k, v):
+        """q,k,v (B,H,n,D) bf16, un-rotated, any n: window branch + long-range branch + combine, then the tokens join
+        the state. Returns (B,H,n,D) (a view of the (B,n,H*D) buffer W_o reads)."""
+        if torch.is_grad_enabled():
+            raise RuntimeError("LinearFSCache is inference-only; use torch.no_grad().")
+        a = self.attn
+        B, H, n, D = q.shape
+        if not self._ready:
+            self._alloc(k)
+        lam, sigma, lrs, norm_w = a.head_params()
+        # window branch of the whole call: [the last <= W stored rows | the new rows]; the stored rows get dummy queries
+        old = self.win_k.shape[2]
+        kc = torch.cat([self.win_k, k.to(torch.bfloat16)], dim=2)
+        vc = torch.cat([self.win_v, v.to(torch.bfloat16)], dim=2)
+        qc = torch.cat([torch.zeros(B, H, old, D, dtype=torch.bfloat16, device=q.device), q.to(torch.bfloat16)], dim=2)
+        cos, sin = a.rope.tables_bf16(self.pos + n)
+        sr_all = ops.window_prefill(qc, kc, vc, cos, sin, self.W, a.scale, pos0=self.pos - old)[:, old:]      # (B,n,H*D)
+        y = torch.empty(B, n, H * D, dtype=torch.bfloat16, device=q.device)
+        off = 0
+        while off < n:
+            self.prepare()
+            m = min(n - off, self.Bq - self.pos % self.Bq)
+            qp = q[:, :, off:off + m]
+            sr = sr_all[:, off:off + m].contiguous()
+            if self.pool is None:
+                y[:, off:off + m] = sr                  # no completed cell yet: the long-range branch is zero
+            else:
+                slots, ids = self.select(qp)
+                sel = torch.full((B, H, m, a.cell_topk), -1, dtype=torch.int32, device=q.device)
+                sel[..., :slots.shape[-1]] = torch.where(ids >= 0, slots, torch.full_like(slots, -1)).to(torch.int32)
+                # the pool slots are the "cells" of this readout; every pool token lies before the virtual query position
+                n_kv = self.C * self.s
+                out = ops.readout_combine(qp.to(torch.bfloat16), self.pool["k"], self.pool["v"], sel, sr, norm_w, lrs,
+                                          a.lr_norm.eps, scale=a.scale, Bq=self.Bq, n_kv=n_kv,
+                                          q_pos0=(n_kv + self.Bq - 1) // self.Bq * self.Bq)
+                y[:, off:off + m] = out
+            self.ingest(k[:, :, off:off + m], v[:, :, off:off + m])
+            off += m
+        return y.view(B, n, H, D).transpose(1, 2)

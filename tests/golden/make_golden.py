@@ -19,6 +19,10 @@ Fixtures:
                    the reference's fsb_calibrate_tau): prefill of 330 tokens + 72 greedy tokens through its KV caches in
                    fp32, then the same token sequence fed through the module cast to bf16 (teacher forcing, so every
                    step's logits stay comparable); token ids and the last-token logits of every step of both runs.
+  linear_<kind>.npz  the reference's streaming cache (src/fsattn/linear_cache.py LinearFSCache) of one FS-L layer at the
+                   Q/K/V level: 3000 tokens pushed through `attend` in pieces of uneven sizes (single tokens included),
+                   fp32: the outputs, the cell ids every query selected, the ids left in the top-P list at the end and
+                   the cache's counters.
   fsl_config1.npz  BASELINE config 1: FSAttn(d_model=1024, 16 heads) with its own seeded projections, 4096-token
                    prefill + 1 decode step, fp32; selections, margins and a strided sample of the outputs.
 """
@@ -231,6 +235,47 @@ def gen_fs_dense(kind: str, B=1, H=2, D=64, N=1000, T=40, seed=31):
         os.environ["FS_PRUNE_KERNEL"] = "1"
     np.savez_compressed(os.path.join(HERE, f"fsdense_{kind}.npz"), **out)
     print("wrote", f"fsdense_{kind}.npz", {k_: v_.shape for k_, v_ in out.items() if hasattr(v_, "shape") and v_.ndim})
+
+
+def gen_linear(kind: str, B=1, H=2, D=64, N=3000, seed=41):
+    """The reference's LinearFSCache driven directly with Q/K/V pieces (its attend splits them at query-block boundaries)."""
+    from src.fsattn.linear_cache import LinearFSCache
+    Q, K, V = make_inputs(kind, B, H, N, D, seed)
+    a = _layer(None, H, D, seed + 1, False)
+    c = LinearFSCache(a)
+    picked = []
+    inner = c.select
+
+    def select(q):
+        slots, ids = inner(q)
+        if ids is None:
+            picked.append(torch.full((B, H, q.shape[2], a.cell_topk), -1, dtype=torch.int64))
+        else:
+            pad = a.cell_topk - ids.shape[-1]
+            picked.append(torch.nn.functional.pad(ids, (0, pad), value=-1) if pad else ids.clone())
+        return slots, ids
+    c.select = select
+    pieces = [700, 129, 1, 1, 1, 37, 900, 3, 128, 512]
+    pieces.append(N - sum(pieces))
+    ys, o = [], 0
+    with torch.no_grad():
+        for n in pieces:
+            ys.append(c.attend(Q[:, :, o:o + n], K[:, :, o:o + n], V[:, :, o:o + n]))
+            o += n
+    sel = torch.cat(picked, dim=2)
+    # the queries of the first block see no completed cell: the cache does not call select for them
+    sel = torch.nn.functional.pad(sel, (0, 0, N - sel.shape[2], 0), value=-1)
+    out = {"kind": kind, "B": B, "H": H, "D": D, "N": N, "pieces": np.array(pieces, np.int64),
+           "Q": _bf16_bits(Q), "K": _bf16_bits(K), "V": _bf16_bits(V),
+           "lam": a.sel_scale.detach().numpy(), "sigma": a.sigma.detach().numpy(),
+           "lrs": a.long_range_scale.detach().reshape(H).numpy(), "norm_w": a.lr_norm.scale.detach().numpy(),
+           "eps": np.float32(a.lr_norm.eps), "W": a.window_size, "P": c.P, "Wc": c.Wc,
+           "y": torch.cat(ys, dim=2).numpy(), "sel": sel.numpy().astype(np.int32),
+           "top_ids": c._top["ids"].sort(-1).values.numpy().astype(np.int32),
+           "counters": np.array([c.pos, c.eligible, c.max_merge_cells, c.merged_cells, c.updates], np.int64),
+           "state_bytes": np.int64(c.state_bytes())}
+    np.savez_compressed(os.path.join(HERE, f"linear_{kind}.npz"), **out)
+    print("wrote", f"linear_{kind}.npz")
 
 
 def gen_config1():
@@ -460,6 +505,8 @@ def main():
         "fsl_periodic": lambda: gen_fsl("periodic", N=640, T=8, seed=13),
         "fsl_lowprec": lambda: gen_fsl("lowprec", N=640, T=8, seed=17),
         "fsl_config1": gen_config1,
+        "linear_randn": lambda: gen_linear("randn"),
+        "linear_vocab": lambda: gen_linear("vocab", seed=43),
         "fsb_randn": lambda: gen_fsb("randn"),
         "fsb_vocab": lambda: gen_fsb("vocab", N=1500, T=40, seed=29),
         "fsdense_randn": lambda: gen_fs_dense("randn"),

@@ -1,4 +1,6 @@
 """Host-side mirror of the reference API: construction, names, configuration errors (CPU only)."""
+import os
+
 import pytest
 import torch
 
@@ -94,3 +96,35 @@ def test_fsb_layer_construction_and_refusals():
         kw.update(bad)
         with pytest.raises(NotImplementedError):
             FSAttn(256, 4, causal=True, bias=False, **kw)
+
+
+def test_streaming_cache_construction_and_refusals():
+    """make_caches(linear=True) gives one LinearFSCache per layer (ref: experiments/scaling/kv_cache.py:467-481); the dense
+    and FS-B variants are refused as the reference refuses them; linear_prefill checks its arguments."""
+    from freesolo_b200.fsattn.kv_cache import linear_prefill, make_caches
+    from freesolo_b200.fsattn.linear_cache import LinearFSCache
+    from freesolo_b200.serving import FreeSoloLM, serve_kwargs
+    m = FreeSoloLM(vocab_size=64, d_model=128, n_layers=2, n_heads=2, d_ff=256, max_seq_len=256, **serve_kwargs("sparse"))
+    caches = make_caches(m, linear=True)
+    assert len(caches) == 2 and all(isinstance(c, LinearFSCache) and c.bounded for c in caches)
+    c = caches[0]
+    assert (c.s, c.Bq, c.W, c.P, c.Wc, c.C) == (32, 128, 512, 64, 8, 72) and c.state_bytes() == 0 and c.pool is None
+    os.environ["FSL_LINEAR_CACHE"] = "1"
+    try:
+        assert isinstance(make_caches(m)[0], LinearFSCache)
+    finally:
+        del os.environ["FSL_LINEAR_CACHE"]
+    assert not isinstance(make_caches(m)[0], LinearFSCache)
+    dense = FreeSoloLM(vocab_size=64, d_model=128, n_layers=1, n_heads=2, d_ff=256, max_seq_len=256, **serve_kwargs("dense"))
+    with pytest.raises(ValueError):
+        make_caches(dense, linear=True)
+    fsb = FreeSoloLM(vocab_size=64, d_model=128, n_layers=1, n_heads=2, d_ff=256, max_seq_len=256, **serve_kwargs("fsb"))
+    with pytest.raises((ValueError, NotImplementedError)):        # no pool pruning in the FS-B configuration either
+        make_caches(fsb, linear=True)
+    ids = torch.zeros(1, 8, dtype=torch.long)
+    with pytest.raises(ValueError):
+        linear_prefill(m, ids, caches, chunk_size=0)
+    with pytest.raises(ValueError):
+        linear_prefill(m, ids, make_caches(m))          # FSKVCache is not a bounded streaming cache
+    with pytest.raises(ValueError):
+        c.ingest(torch.zeros(1, 2, 129, 64), torch.zeros(1, 2, 129, 64))      # more than one query block at once

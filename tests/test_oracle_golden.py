@@ -145,3 +145,25 @@ def test_config1_fixture_consistency():
     assert (sel[:, :, :128] == -1).all(), "block 0 has no long-range read (strict causal)"
     x = torch.randn(1, 4097, 1024, generator=torch.Generator().manual_seed(1234))
     assert abs(float(x.double().sum()) - float(g["x_checksum"])) < 1e-6 * 4097 * 1024
+
+
+@pytest.mark.parametrize("kind", ["randn", "vocab"])
+def test_streaming_cache_fixture_equals_the_fsl_oracle_over_the_whole_sequence(kind):
+    """The reference's LinearFSCache (src/fsattn/linear_cache.py), fed 3000 tokens in uneven pieces, selects the cells and
+    produces the outputs of the standard FS-L prefill over the same tokens: the FS-L oracle run once over the whole
+    sequence is therefore the oracle of the streaming cache too (selections equal in order, outputs to fp32 rounding)."""
+    g = load_golden(f"linear_{kind}")
+    Q, K, V = _inputs(g)
+    H, D, N = int(g["H"]), int(g["D"]), int(g["N"])
+    L = fsl.FSLLayerOracle(H, D, W=int(g["W"]), P=int(g["P"]), Wc=int(g["Wc"]), lam=torch.from_numpy(g["lam"]),
+                           sigma=torch.from_numpy(g["sigma"]), lrs=torch.from_numpy(g["lrs"]), norm_w=torch.from_numpy(g["norm_w"]),
+                           eps=float(g["eps"]), act_dtype=torch.float32, rope_len=4096, rope_orig_len=4096)
+    y, sel, margin = L.prefill(Q, K, V)
+    ref_sel = torch.from_numpy(g["sel"]).long()
+    differ = (sel != ref_sel).any(-1)
+    assert int((differ & (margin > 1e-4)).sum()) == 0
+    assert differ.float().mean() < 0.01
+    ref_y = torch.from_numpy(g["y"]).transpose(1, 2).reshape(1, N, H * D)
+    assert (y - ref_y).abs().max() < 1e-4
+    # the reference's counters: 92 eligible cells after 3000 tokens, 23 block changes, at most P + 4 candidates per merge
+    assert g["counters"].tolist() == [N, (N // 128) * 128 // 32, int(g["P"]) + 4, g["counters"][3], N // 128]
