@@ -262,7 +262,8 @@ def timed_prefill(make_decoder, reps: int = 3):
         del gd
         if i == 0:
             torch.cuda.synchronize()
-            torch.cuda.empty_cache()
+            if reps > 1:                      # (a single timed run keeps the allocator's pools: it must not pay for cudaMalloc)
+                torch.cuda.empty_cache()
             torch.cuda.reset_peak_memory_stats()
         gd = make_decoder()
         torch.cuda.synchronize()
