@@ -352,10 +352,14 @@ def make_fsb_model(args, dev, ctx):
 
 
 def time_fsb_select(gd, ctx, dev, reps=3):
-    """The FS-B prefill selection (both beams + re-rank) of one layer alone: layer 0's forests as the prefill left them,
-    random bf16 queries and token keys of the model's shape, median of `reps` CUDA-event timings."""
+    """The FS-B prefill selection (both beams + re-rank) of one layer alone: forests rebuilt over layer 0's cell statistics
+    and thresholds (the decoder's own were reduced to the decode arena after its prefill), random bf16 queries and token keys
+    of the model's shape - random queries make a block's beams diverge, the slow case of the block-shared beam kernel; inside
+    a real prefill they coincide - median of `reps` CUDA-event timings."""
     from freesolo_b200 import ops
-    a, fo = gd.attn_core[0], gd.cache[0].fsb
+    a, live = gd.attn_core[0], gd.cache[0].fsb
+    fo = ops.FsbForests(live.kbar, live.ceil, live.taus[0], live.taus[1] if live.nf > 1 else None, cap_cells=ctx // 32)
+    fo.ingest(ctx // 32)
     g = torch.Generator(device=dev).manual_seed(11)
     Q, K = (torch.randn(1, a.n_heads, ctx, a.head_dim, device=dev, generator=g).to(torch.bfloat16) for _ in range(2))
     lam, sigma, _, _ = a.head_params()

@@ -13,15 +13,26 @@ __host__ __device__ __forceinline__ int fsb_log2(int x) {
     while ((1 << l) < x) ++l;
     return l;
 }
+// Two arenas. Full (compact = 0): every aligned even-j chunk has its own place, so a prefill can name the forest of any
+// earlier prefix. Compact (compact = 1): one place per chunk HEIGHT (the reference's decode arena, fsb_tree.py:1496-1522): a
+// new chunk of height k is completed exactly when bit k of the admitted count turns on, i.e. when no chunk of that height is
+// alive, so the place is free; only the current prefix can be named, which is all a decode step asks.
+#define FSB_COMPACT_ROOTS 32   // rows of root32 per forest row in the compact arena (one per height)
 // first node id of the chunks of height k inside a row's arena
 __host__ __device__ __forceinline__ int64_t fsb_nbase(int k, int m_cap) {
     return (int64_t)k * m_cap - m_cap + (m_cap >> k);
 }
-__host__ __device__ __forceinline__ int64_t fsb_root_node(int k, int j, int m_cap) {
+__host__ __device__ __forceinline__ int64_t fsb_root_node(int k, int j, int m_cap, int compact = 0) {
+    if (compact) return (int64_t)(2 << k) - 2 - k;                        // sum of the sizes 2^{k'+1} - 1 of the lower heights
     return fsb_nbase(k, m_cap) + (int64_t)(j >> 1) * ((2 << k) - 1);
 }
-__host__ __device__ __forceinline__ int fsb_chunk_id(int k, int j, int m_cap) { return m_cap - (m_cap >> k) + (j >> 1); }
-__host__ __device__ __forceinline__ int64_t fsb_nodes_per_row(int m_cap) { return (int64_t)(fsb_log2(m_cap) + 1) * m_cap; }
+__host__ __device__ __forceinline__ int fsb_chunk_id(int k, int j, int m_cap, int compact = 0) {
+    return compact ? k : m_cap - (m_cap >> k) + (j >> 1);
+}
+__host__ __device__ __forceinline__ int64_t fsb_nodes_per_row(int m_cap, int compact = 0) {
+    return compact ? 4 * (int64_t)m_cap : (int64_t)(fsb_log2(m_cap) + 1) * m_cap;
+}
+__host__ __device__ __forceinline__ int64_t fsb_root_rows(int m_cap, int compact = 0) { return compact ? FSB_COMPACT_ROOTS : m_cap; }
 
 // ---- halving-order sum over the head dimension, one warp per vector ------------------------------------------------
 // Lane L holds the values of dims L, L+32, L+64, L+96 (zero beyond D). The order is that of repeated halving over the

@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(BK_THREADS, 2) fsb_beam_block_kernel(SelArgs A
             beam_prefix<D>(F, t, sp, width, lane, pre);
         }
         __syncthreads();
-        const int64_t nrow = (int64_t)t * fsb_nodes_per_row(F.m_cap);
+        const int64_t nrow = (int64_t)t * fsb_nodes_per_row(F.m_cap, F.compact);
         const bf16* node_mu = (const bf16*)F.node_mu + nrow * D;
         const float4* aux = (const float4*)F.node_aux + nrow;
         const int root = sp.root;

@@ -99,14 +99,20 @@ __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
     if (n > FSB_MAX_CHUNK) return;             // cannot happen below 524 288 admitted tokens per row
     const int j = ((p + 1) >> k) - 1, jj = j >> 1;
     const int pos0 = p + 1 - n;
+    if (F.compact) {
+        // one place per height: of the chunks this ingest completes only the one still named by the new admitted count is
+        // built (an earlier one of the same height has already been merged into a higher chunk, and would race for the place)
+        const int m = F.m_tot[t];
+        if (!((m >> k) & 1) || j != ((m >> (k + 1)) << 1)) return;
+    }
 
     const int* adm = F.adm + (int64_t)t * m_cap + pos0;
     const float* kbar = F.kbar + (int64_t)t * F.kbar_st;
     const float* ceil = F.ceil + (int64_t)t * F.ceil_st;
-    const int64_t node0 = (int64_t)t * fsb_nodes_per_row(m_cap) + fsb_nbase(k, m_cap) + (int64_t)jj * (2 * n - 1);
+    const int64_t node0 = (int64_t)t * fsb_nodes_per_row(m_cap, F.compact) + fsb_root_node(k, j, m_cap, F.compact);
     bf16* node_mu = (bf16*)F.node_mu + node0 * D;
     float4* node_aux = (float4*)F.node_aux + node0;
-    float* root32 = F.root32 + ((int64_t)t * m_cap + fsb_chunk_id(k, j, m_cap)) * (D + FSB_ROOT_PAD);
+    float* root32 = F.root32 + ((int64_t)t * fsb_root_rows(m_cap, F.compact) + fsb_chunk_id(k, j, m_cap, F.compact)) * (D + FSB_ROOT_PAD);
 
     // ---- working arrays ----
     __shared__ float sm_f[SMALL ? (SN * D * 2 + SN) : 1];
@@ -333,7 +339,52 @@ int fs_fsb_check_forest(const fsattn_fsb_forest_t& f, const char* what) {
     FS_UNSUPPORTED(f.m_cap > FSB_MAX_MCAP, "%s: m_cap = %d cells (at most %d)", what, f.m_cap, FSB_MAX_MCAP);
     FS_REQUIRE(f.kbar && f.ceil && f.tau && f.adm && f.m_tot && f.m_prev && f.node_mu && f.node_aux && f.root32,
                "%s: null forest buffer", what);
+    FS_REQUIRE(f.compact == 0 || f.compact == 1, "%s: compact = %d (0 or 1)", what, f.compact);
     return FSATTN_OK;
+}
+
+namespace {
+// one CTA per (row, height): the chunk of that height named by the row's admitted count, full arena -> compact arena
+template <int D>
+__global__ void fsb_compact_kernel(fsattn_fsb_forest_t S, fsattn_fsb_forest_t C) {
+    const int t = blockIdx.x, k = blockIdx.y;
+    const int m = S.m_tot[t];
+    if (!((m >> k) & 1)) return;
+    const int j = (m >> (k + 1)) << 1;
+    const int n = (2 << k) - 1;
+    const int64_t s0 = (int64_t)t * fsb_nodes_per_row(S.m_cap, 0) + fsb_root_node(k, j, S.m_cap, 0);
+    const int64_t d0 = (int64_t)t * fsb_nodes_per_row(S.m_cap, 1) + fsb_root_node(k, j, S.m_cap, 1);
+    const uint4* smu = (const uint4*)((const bf16*)S.node_mu + s0 * D);
+    uint4* dmu = (uint4*)((bf16*)C.node_mu + d0 * D);
+    for (int64_t i = threadIdx.x; i < (int64_t)n * (D / 8); i += blockDim.x) dmu[i] = smu[i];
+    const float4* sa = (const float4*)S.node_aux + s0;
+    float4* da = (float4*)C.node_aux + d0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) da[i] = sa[i];
+    const float* sr = S.root32 + ((int64_t)t * fsb_root_rows(S.m_cap, 0) + fsb_chunk_id(k, j, S.m_cap, 0)) * (D + FSB_ROOT_PAD);
+    float* dr = C.root32 + ((int64_t)t * fsb_root_rows(S.m_cap, 1) + fsb_chunk_id(k, j, S.m_cap, 1)) * (D + FSB_ROOT_PAD);
+    for (int i = threadIdx.x; i < D + FSB_ROOT_PAD; i += blockDim.x) dr[i] = sr[i];
+}
+}  // namespace
+
+extern "C" int fsattn_fsb_compact(const fsattn_fsb_forest_t* src, const fsattn_fsb_forest_t* dst, fsattn_stream_t stream) {
+    FS_REQUIRE(src && dst, "fsb_compact: null argument");
+    int rc = fs_fsb_check_forest(*src, "fsb_compact(src)");
+    if (rc != FSATTN_OK) return rc;
+    rc = fs_fsb_check_forest(*dst, "fsb_compact(dst)");
+    if (rc != FSATTN_OK) return rc;
+    FS_REQUIRE(src->compact == 0 && dst->compact == 1, "fsb_compact: from the full arena (compact = 0) to a compact one (1)");
+    FS_REQUIRE(src->T == dst->T && src->D == dst->D && src->m_cap == dst->m_cap && src->m_tot == dst->m_tot,
+               "fsb_compact: both arenas describe the same forest (T, D, m_cap, m_tot)");
+    FS_REQUIRE(src->node_mu != dst->node_mu && src->node_aux != dst->node_aux && src->root32 != dst->root32,
+               "fsb_compact: the compact arena needs buffers of its own");
+    cudaStream_t st = (cudaStream_t)stream;
+    const dim3 grid(src->T, fsb_log2(src->m_cap) + 1);
+    switch (src->D) {
+        case 64: fsb_compact_kernel<64><<<grid, 256, 0, st>>>(*src, *dst); break;
+        case 96: fsb_compact_kernel<96><<<grid, 256, 0, st>>>(*src, *dst); break;
+        default: fsb_compact_kernel<128><<<grid, 256, 0, st>>>(*src, *dst); break;
+    }
+    return fs_check_launch("fsb_compact_kernel");
 }
 
 extern "C" int fsattn_fsb_ingest(const fsattn_fsb_forest_t* forests, int32_t n_forests, int32_t cell_begin,

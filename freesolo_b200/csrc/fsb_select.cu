@@ -32,8 +32,8 @@ template <int D>
 __device__ void build_spine(const fsattn_fsb_forest_t& F, int t, int m_b, SpineSm<D>& S, int lane) {
     constexpr int NPL = FsbDim<D>::NPL;
     const int m_cap = F.m_cap;
-    const float4* aux = (const float4*)F.node_aux + (int64_t)t * fsb_nodes_per_row(m_cap);
-    const float* root32 = F.root32 + (int64_t)t * m_cap * (D + FSB_ROOT_PAD);
+    const float4* aux = (const float4*)F.node_aux + (int64_t)t * fsb_nodes_per_row(m_cap, F.compact);
+    const float* root32 = F.root32 + (int64_t)t * fsb_root_rows(m_cap, F.compact) * (D + FSB_ROOT_PAD);
     float rmu[NPL];
     float r_rad = 0.f, r_am = 0.f, r_cnt = 0.f;
     int r_pm = 0x7fffffff, r_ref = -1, npres = 0;
@@ -43,9 +43,9 @@ __device__ void build_spine(const fsattn_fsb_forest_t& F, int t, int m_b, SpineS
         if (!((m_b >> k) & 1)) continue;
         ++npres;
         const int j = (m_b >> (k + 1)) << 1;
-        const int cid = (int)fsb_root_node(k, j, m_cap);
+        const int cid = (int)fsb_root_node(k, j, m_cap, F.compact);
         const int cref = cid | (k << 20);
-        const float* cr = root32 + (int64_t)fsb_chunk_id(k, j, m_cap) * (D + FSB_ROOT_PAD);
+        const float* cr = root32 + (int64_t)fsb_chunk_id(k, j, m_cap, F.compact) * (D + FSB_ROOT_PAD);
         float cmu[NPL];
         fsb_load_row<D>(cr, lane, cmu);
         const float c_rad = cr[D];
@@ -140,7 +140,7 @@ struct BeamPre {
 
 template <int D>
 __device__ void beam_prefix(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, int width, int lane, BeamPre& P) {
-    const float4* aux = (const float4*)F.node_aux + (int64_t)t * fsb_nodes_per_row(F.m_cap);
+    const float4* aux = (const float4*)F.node_aux + (int64_t)t * fsb_nodes_per_row(F.m_cap, F.compact);
     const int root = S.root;
     int ref = -1, meta = 0, nc = 0, rnd = 0;
     int n = 0, nvis = 0, rounds = 0;
@@ -206,7 +206,7 @@ __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, co
                     const unsigned char* stg_mu = nullptr, const float4* stg_aux = nullptr, const float* qf = nullptr) {
     constexpr int DP = FsbDim<D>::DP;
     const int m_cap = F.m_cap;
-    const int64_t nrow = (int64_t)t * fsb_nodes_per_row(m_cap);
+    const int64_t nrow = (int64_t)t * fsb_nodes_per_row(m_cap, F.compact);
     const bf16* node_mu = (const bf16*)F.node_mu + nrow * D;
     const float4* aux = (const float4*)F.node_aux + nrow;
     if (S.root == -1) return -1;
@@ -521,7 +521,7 @@ __global__ void __launch_bounds__(NWARP * 32, (D == 64) ? 3 : 2) fsb_select_kern
         }
         __syncthreads();
         {   // stage the shallow levels: rows of chunk k come from its node array's first stg_cnt[k] rows
-            const int64_t nrow = (int64_t)t * fsb_nodes_per_row(F.m_cap);
+            const int64_t nrow = (int64_t)t * fsb_nodes_per_row(F.m_cap, F.compact);
             const bf16* node_mu = (const bf16*)F.node_mu + nrow * D;
             const float4* aux = (const float4*)F.node_aux + nrow;
             const int m_b = sp.m_b;
@@ -529,7 +529,7 @@ __global__ void __launch_bounds__(NWARP * 32, (D == 64) ? 3 : 2) fsb_select_kern
                 const int cnt = sp.stg_cnt[k];
                 if (!((m_b >> k) & 1) || cnt == 0) continue;
                 const int base = sp.stg_base[k];
-                const int64_t n0 = fsb_root_node(k, (m_b >> (k + 1)) << 1, F.m_cap);
+                const int64_t n0 = fsb_root_node(k, (m_b >> (k + 1)) << 1, F.m_cap, F.compact);
                 for (int i = tid; i < cnt * CH; i += NWARP * 32) {
                     const int r = i / CH, v = i % CH, row = base + r;
                     const uint4 w = *(const uint4*)(node_mu + (n0 + r) * D + v * 8);
@@ -795,6 +795,8 @@ extern "C" int fsattn_fsb_select(const fsattn_fsb_select_t* a, fsattn_stream_t s
                    "fsb_select: decode needs the spines, their headers and pos");
         FS_REQUIRE(a->N == 1 && a->Bq == 1, "fsb_select: decode takes one query per row (N = Bq = 1)");
     } else {
+        FS_REQUIRE(a->main.compact == 0 && a->second.compact == 0,
+                   "fsb_select: a prefill names the forests of earlier prefixes, which only the full arena (compact = 0) keeps");
         FS_REQUIRE((a->q_pos0 % 32) == 0 && ((a->Bq % 32) == 0 || a->N <= a->Bq),
                    "fsb_select: q_pos0 and Bq must be multiples of the cell (Bq may be ragged for a single block)");
     }

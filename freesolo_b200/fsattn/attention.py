@@ -431,6 +431,10 @@ class FSAttn(nn.Module):
             sel = ops.fsb_select(fo, Q, K, lam, sigma, scale=self.scale, N=N, Bq=Bq, width=self.fsb_width,
                                  width2=self._fsb_w2(fo), read_top=self.fsb_read_top,
                                  radius_coef=self.fsb_bound_radius_coef)
+            # the prompt's queries were the only ones that name earlier prefixes: keep one chunk per height for the decode
+            # (the reference's decode arena, src/fsattn/fsb_tree.py:1496-1522) and release the rest
+            if os.environ.get("FSATTN_FSB_KEEP_ARENA", "0") != "1":
+                fo.compact_arena((N // self._cell_block) * self._cell_block // s)
             margin = None
         elif self._is_dense_lr():
             # dense FS (src/fsattn/attention.py:362-423): every cell completed before the query's block is a candidate

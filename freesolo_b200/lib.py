@@ -166,7 +166,7 @@ class FsbForest(C.Structure):
     _fields_ = [("T", i32), ("H", i32), ("D", i32), ("m_cap", i32),
                 ("kbar", vp), ("kbar_st", i64), ("ceil", vp), ("ceil_st", i64), ("tau", vp),
                 ("adm", vp), ("m_tot", vp), ("m_prev", vp),
-                ("node_mu", vp), ("node_aux", vp), ("root32", vp)]
+                ("node_mu", vp), ("node_aux", vp), ("root32", vp), ("compact", i32)]
 
 
 class FsbSelect(C.Structure):
@@ -207,6 +207,7 @@ ENTRY_POINTS = {
     "fsattn_rms_norm": ([vp, i64, vp, f32, vp, i64, i64, i32, vp], C.c_int),
     "fsattn_fsb_scratch_floats": ([i32, i32, i32], i64),
     "fsattn_fsb_ingest": ([C.POINTER(FsbForest), i32, i32, i32, vp, i64, vp], C.c_int),
+    "fsattn_fsb_compact": ([C.POINTER(FsbForest), C.POINTER(FsbForest), vp], C.c_int),
     "fsattn_fsb_spines": ([C.POINTER(FsbForest), i32, i32, C.POINTER(vp), C.POINTER(vp), vp], C.c_int),
     "fsattn_fsb_select": FsbSelect,
 }

@@ -586,21 +586,61 @@ class FsbForests:
         dev = kbar.device
         self.taus = [_f32(tau).to(dev)] + ([_f32(tau_u).to(dev)] if tau_u is not None else [])
         self.nf = len(self.taus)
-        nodes = (self.k_cap + 1) * m_cap
         T = self.T
         self.adm = [torch.full((T, m_cap), -1, dtype=torch.int32, device=dev) for _ in range(self.nf)]
         self.m_tot = [torch.zeros(T, dtype=torch.int32, device=dev) for _ in range(self.nf)]
         self.m_prev = [torch.zeros(T, dtype=torch.int32, device=dev) for _ in range(self.nf)]
-        self.node_mu = [torch.zeros(T, nodes, D, dtype=torch.bfloat16, device=dev) for _ in range(self.nf)]
-        self.node_aux = [torch.zeros(T, nodes, 4, dtype=torch.float32, device=dev) for _ in range(self.nf)]
-        self.root32 = [torch.zeros(T, m_cap, D + 4, dtype=torch.float32, device=dev) for _ in range(self.nf)]
+        self.compact = 0
+        self._alloc_arena(0)
         self.spine = [torch.zeros(T, L.FSB_SPINE_MAX, D + 8, dtype=torch.float32, device=dev) for _ in range(self.nf)]
         self.hdr = [torch.full((T, 4), -1, dtype=torch.int32, device=dev) for _ in range(self.nf)]
         self.n_seen = 0
 
+    def _arena(self, compact: int):
+        """(node_mu, node_aux, root32) lists of a full (every aligned chunk) or compact (one chunk per height) arena."""
+        T, D, dev = self.T, self.D, self.kbar.device
+        nodes = 4 * self.m_cap if compact else (self.k_cap + 1) * self.m_cap
+        roots = 32 if compact else self.m_cap
+        return ([torch.zeros(T, nodes, D, dtype=torch.bfloat16, device=dev) for _ in range(self.nf)],
+                [torch.zeros(T, nodes, 4, dtype=torch.float32, device=dev) for _ in range(self.nf)],
+                [torch.zeros(T, roots, D + 4, dtype=torch.float32, device=dev) for _ in range(self.nf)])
+
+    def _alloc_arena(self, compact: int) -> None:
+        self.node_mu, self.node_aux, self.root32 = self._arena(compact)
+        self.compact = compact
+
+    def compact_arena(self, n_visible: int | None = None) -> None:
+        """After a prefill: keep only the chunks of the current prefix, one place per chunk height, and release the arena
+        that held every aligned chunk (which only a prefill, naming earlier prefixes, needs). Decode-time ingest, spines
+        and selection continue on the small arena; a later prefill needs reset() first.
+
+        n_visible: the cells the NEXT query can see (the start of its 128-token block, in cells), at most the cells ingested.
+        The forest is first taken back to that prefix - the admitted counts drop to the cells below n_visible; the up to
+        three later cells are admitted again at the next block change - because the small arena can only name the prefix
+        it was compacted at."""
+        if self.compact:
+            return
+        if n_visible is not None and n_visible < self.n_seen:
+            for i in range(self.nf):
+                below = ((self.adm[i] >= 0) & (self.adm[i] < int(n_visible))).sum(-1).to(torch.int32)
+                self.m_tot[i].copy_(torch.minimum(below, self.m_tot[i]))
+                self.m_prev[i].copy_(self.m_tot[i])
+            self.n_seen = int(n_visible)
+        src = [self.struct(i) for i in range(self.nf)]
+        old = (self.node_mu, self.node_aux, self.root32)
+        self._alloc_arena(1)
+        lib = L.load()
+        for i in range(self.nf):
+            dst = self.struct(i)
+            L.check(lib.fsattn_fsb_compact(L.C.byref(src[i]), L.C.byref(dst), _stream(self.kbar)), "fsattn_fsb_compact")
+        del old                              # freed in stream order: the copies above were launched on this stream
+
     def reset(self) -> None:
         """Forget every admitted cell (a new prompt over the same statistics buffers). Chunk nodes need no clearing: a
-        chunk is only ever read after the admission count says it is complete, and it is rebuilt before that."""
+        chunk is only ever read after the admission count says it is complete, and it is rebuilt before that. A compacted
+        forest gets its full arena back."""
+        if self.compact:
+            self._alloc_arena(0)
         for i in range(self.nf):
             self.adm[i].fill_(-1)
             self.m_tot[i].zero_()
@@ -620,6 +660,7 @@ class FsbForests:
         f.tau = self.taus[i].data_ptr()
         f.adm, f.m_tot, f.m_prev = self.adm[i].data_ptr(), self.m_tot[i].data_ptr(), self.m_prev[i].data_ptr()
         f.node_mu, f.node_aux, f.root32 = self.node_mu[i].data_ptr(), self.node_aux[i].data_ptr(), self.root32[i].data_ptr()
+        f.compact = self.compact
         return f
 
     def ingest(self, cell_end: int) -> None:
@@ -693,7 +734,7 @@ def fsb_select(forests: FsbForests, Q, K, lam, sigma, *, scale: float, N: int = 
         assert pos.dtype == torch.int64 and pos.is_cuda
         a.pos = pos.data_ptr()
         a.pdl = 1 if pdl else 0
-    a.beam_impl = int(beam_impl)
+    a.beam_impl = int(os.environ.get("FSATTN_FSB_BEAM_IMPL", beam_impl))      # A/B switch for measurements
     a.sel, a.cand, a.nvis = sel.data_ptr(), _p(cand), _p(nvis)
     L.call("fsattn_fsb_select", a, _stream(Q))
     return (sel, cand, nvis) if debug else sel

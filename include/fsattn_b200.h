@@ -357,6 +357,11 @@ typedef struct {
     const float* tau;                  /* (H) admission threshold per head */
     int32_t* adm; int32_t* m_tot; int32_t* m_prev;
     void* node_mu; float* node_aux; float* root32;
+    int32_t compact;                   /* 0: the arena above (every aligned chunk kept: a prefill can name any earlier prefix).
+                                        * 1: one place per chunk height - node id of node n of the chunk of height k:
+                                        * 2^{k+1} - 2 - k + n, 4 m_cap nodes per row, chunk id k, root32 (T, 32, D+4) - which
+                                        * holds the CURRENT prefix only (decode; the reference's decode arena,
+                                        * fsb_tree.py:1496-1522). fsattn_fsb_compact converts 0 -> 1 after a prefill. */
 } fsattn_fsb_forest_t;
 
 /* Admit the cells [cell_begin, cell_end) of every row (ceil >= tau[h], fsb_tree.py:936-941, 1465-1494) into each of
@@ -366,6 +371,12 @@ typedef struct {
  * order of det_reduce.det_sum and no multiply-add is contracted. scratch: fsattn_fsb_scratch_floats(m_cap, D, T) floats
  * per forest, used only during the call. */
 FSATTN_API int64_t fsattn_fsb_scratch_floats(int32_t m_cap, int32_t D, int32_t T);
+/* Copies the chunks of the current prefix (one per set bit of m_tot, per row) from a full arena into a compact one.
+ * src and dst share T, H, D, m_cap, adm, m_tot, m_prev; dst->compact = 1 with its own node_mu (T, 4 m_cap, D), node_aux
+ * (T, 4 m_cap, 4) and root32 (T, 32, D+4). After it the decode-time ingest, spines and selection run on dst; the full arena
+ * can be released (at 131 072 tokens: 300 MB -> 19 MB per forest and layer at head_dim 64). */
+FSATTN_API int fsattn_fsb_compact(const fsattn_fsb_forest_t* src, const fsattn_fsb_forest_t* dst, fsattn_stream_t stream);
+
 FSATTN_API int fsattn_fsb_ingest(const fsattn_fsb_forest_t* forests, int32_t n_forests, int32_t cell_begin,
                                  int32_t cell_end, float* scratch, int64_t scratch_floats, fsattn_stream_t stream);
 

@@ -90,6 +90,70 @@ def test_forest_build_bit_exact(cells, D, tied):
         assert torch.equal(fo.root32[i].view(torch.int32), fo2.root32[i].view(torch.int32))
 
 
+@pytest.mark.parametrize("cells,D", [(300, 64), (130, 96)])
+def test_compact_arena_holds_the_current_chunks_and_keeps_growing(cells, D):
+    """After a prefill the forests keep one chunk per height (the reference's decode arena, src/fsattn/fsb_tree.py:1496-1522):
+    every chunk named by the bits of the admitted count is a bit-exact copy, cells ingested afterwards build their chunks in
+    the small arena exactly as they would in the full one, and the decode selection reads the same cells from either."""
+    from freesolo_b200 import ops
+    dev = _dev()
+    H, first = 2, cells - 41
+    kbar, ceil = _stats(cells, H, D, 9 + cells, False)
+    tau = torch.quantile(ceil[0], 0.3, dim=-1)
+    tau_u = torch.quantile(ceil[0], 0.7, dim=-1)
+    full = ops.FsbForests(kbar.to(dev), ceil.to(dev), tau, tau_u, cap_cells=cells)
+    small = ops.FsbForests(kbar.to(dev), ceil.to(dev), tau, tau_u, cap_cells=cells)
+    full.ingest(first)
+    small.ingest(first)
+    before = small.nbytes()
+    # the next query's block starts three cells before the last ingested one: the forest is taken back to that prefix, the
+    # three cells come in again with the next ingest
+    small.compact_arena(first - 3)
+    assert small.compact == 1 and small.nbytes() < before and small.n_seen == first - 3
+    small.build_spines(first - 3)
+    full.build_spines(first - 3)
+    torch.cuda.synchronize()
+    for i in range(2):                       # the spine of the visible prefix: same means, radii and shape from either arena
+        assert torch.equal(full.hdr[i][:, 1:3], small.hdr[i][:, 1:3])
+        assert torch.equal(full.spine[i][:, :, :D + 4].view(torch.int32), small.spine[i][:, :, :D + 4].view(torch.int32))
+    for end in (first + 1, first + 7, first + 8, cells):          # decode-time growth, in the arena each one has
+        full.ingest(end)
+        small.ingest(end)
+    torch.cuda.synchronize()
+    m_cap = full.m_cap
+    for i in range(2):
+        assert torch.equal(full.m_tot[i], small.m_tot[i]) and torch.equal(full.adm[i], small.adm[i])
+        for t in range(H):
+            m = int(full.m_tot[i][t])
+            for k in range(m.bit_length()):
+                if not (m >> k) & 1:
+                    continue
+                j, n = (m >> (k + 1)) << 1, (2 << k) - 1
+                f0 = k * m_cap - m_cap + (m_cap >> k) + (j >> 1) * n
+                c0 = (2 << k) - 2 - k
+                assert torch.equal(full.node_mu[i][t, f0:f0 + n].view(torch.int16), small.node_mu[i][t, c0:c0 + n].view(torch.int16))
+                assert torch.equal(full.node_aux[i][t, f0:f0 + n].view(torch.int32), small.node_aux[i][t, c0:c0 + n].view(torch.int32))
+                cid = m_cap - (m_cap >> k) + (j >> 1)
+                assert torch.equal(full.root32[i][t, cid].view(torch.int32), small.root32[i][t, k].view(torch.int32))
+    # one decode query per row: spines and selection from either arena
+    g = torch.Generator().manual_seed(1)
+    N = cells * S
+    K = torch.randn(1, H, N, D, generator=g).to(torch.bfloat16).to(dev)
+    q = torch.randn(1, H, 1, D, generator=g).to(torch.bfloat16).to(dev)
+    lam, sigma = 0.5 + torch.rand(H, generator=g), 2.0 + torch.rand(H, generator=g) * 30
+    pos_t = torch.full((), N, dtype=torch.int64, device=dev)
+    out = []
+    for fo in (full, small):
+        fo.build_spines(cells)
+        out.append(ops.fsb_select(fo, q, K, lam, sigma, scale=D ** -0.5, pos=pos_t, debug=True))
+    assert all(torch.equal(a, b) for a, b in zip(out[0], out[1]))
+    # a prefill on the compact arena is refused; reset() brings the full arena back
+    with pytest.raises(RuntimeError):
+        ops.fsb_select(small, K[:, :, :256], K, lam, sigma, scale=D ** -0.5, N=256)
+    small.reset()
+    assert small.compact == 0 and small.nbytes() == before
+
+
 def test_forest_tau_zero_admits_everything():
     from freesolo_b200 import ops
     kbar, ceil = _stats(64, 2, 64, 3)
