@@ -100,12 +100,18 @@ class ShardedFSAttn(nn.Module):
         return self.shard.gather(y_local, self.group, out=y)
 
     @torch.no_grad()
-    def forward(self, x, mask=None, cache=None):
+    def forward(self, x, mask=None, cache=None, pre_norm=None):
         if cache is None:
             raise NotImplementedError("cached inference only")
         sh = self.shard
         B, N, _ = x.shape
-        qkv = F.linear(x, self.w_qkv)
+        if pre_norm is None:
+            qkv = F.linear(x, self.w_qkv)
+        else:                                 # long prefill: the block's input norm applied here in token chunks (see FSAttn.forward)
+            chunk = self.inner.PROJ_CHUNK
+            qkv = torch.empty(B, N, self.w_qkv.shape[0], dtype=x.dtype, device=x.device)
+            for s0 in range(0, N, chunk):
+                qkv[:, s0:s0 + chunk] = F.linear(pre_norm(x[:, s0:s0 + chunk]), self.w_qkv)
         q, k, v = (qkv[..., i * sh.dl:(i + 1) * sh.dl].view(B, N, sh.Hl, sh.D).transpose(1, 2) for i in range(3))
         a = self.inner
         a._assert_cacheable(phase="prefill" if (cache.pos == 0 and N > 1) else "decode")
