@@ -15,7 +15,8 @@ most Bq/s = 4 of them), so a block costs a few kilobytes of traffic instead of a
 operations are this library's kernels: the window branch of a whole `attend` call is one launch of the tensor-core
 window kernel over [last W rows | new rows], and every block's long-range branch is one launch of the fused readout +
 combine kernel reading the pool slots as cells. Cell statistics come from the cell-ingest kernel (bit-exact mean and
-ceiling); the candidate scores (at most 72 per query) and the bookkeeping are torch operations on the device.
+ceiling); the pool update of a block change and the selection (at most 72 candidate scores per query, top-k) are two
+small kernels of their own (csrc/linear_pool.cu); only the concatenation of the pending / window rows is left to torch.
 
 Selections and outputs equal the standard FS-L prefill over the same tokens (same candidates: prefix top-P plus the Wc
 newest; same scores; ties to the lower cell id), which is how the reference's own tests state it.
@@ -53,7 +54,8 @@ class LinearFSCache:
     def _alloc(self, k):
         B, H, _, D = k.shape
         dev, C, s = k.device, self.C, self.s
-        self.ids = torch.full((B, H, C + 1), -1, dtype=torch.int64, device=dev)
+        self.ids = torch.full((B, H, C + 1), -1, dtype=torch.int32, device=dev)
+        self.valid = torch.zeros(B, H, C, dtype=torch.uint8, device=dev)
         self.prio = torch.full((B, H, C + 1), float("-inf"), dtype=torch.float32, device=dev)
         self.mean = torch.zeros(B, H, C + 1, D, dtype=torch.float32, device=dev)
         self.k = torch.zeros(B, H, (C + 1) * s, D, dtype=torch.bfloat16, device=dev)
@@ -64,7 +66,7 @@ class LinearFSCache:
         self.pend_v = torch.zeros(B, H, 0, D, dtype=torch.bfloat16, device=dev)
         self._ready = True
 
-    _TENSORS = ("ids", "prio", "mean", "k", "v", "win_k", "win_v", "pend_k", "pend_v")
+    _TENSORS = ("ids", "valid", "prio", "mean", "k", "v", "win_k", "win_v", "pend_k", "pend_v")
 
     def fork(self):
         """An independent copy of the state (ref: linear_cache.py:207-211)."""
@@ -87,70 +89,28 @@ class LinearFSCache:
         start = self.pos // self.Bq * self.Bq
         if start == self.block_start:
             return
-        s, P, Wc = self.s, self.P, self.Wc
+        s, P, Wc, C = self.s, self.P, self.Wc, self.C
         count = start // s - self.eligible
         if count > 0:
             n = count * s
             nk, nv = self.pend_k[:, :, :n].contiguous(), self.pend_v[:, :, :n].contiguous()
-            mean, prio = ops.cell_stats(nk, count)                       # (B,H,count,D), (B,H,count) fp32
-            B, H = prio.shape[:2]
-            dev = prio.device
-            new_ids = torch.arange(self.eligible, self.eligible + count, device=dev).view(1, 1, count).expand(B, H, count)
+            mean, prio = ops.cell_stats(nk, count)                       # (B,H,count,D), (B,H,count) fp32, bit-exact statistics
             width = min(P, self.eligible) + count
             self.max_merge_cells = max(self.max_merge_cells, width)
             self.merged_cells += width
             self.updates += 1
-            # the P best of (top list, new cells) by (ceiling desc, cell id asc); an empty slot loses to everything
-            cand_prio = torch.cat([self.prio[:, :, :P], prio], dim=2)
-            cand_ids = torch.cat([self.ids[:, :, :P], new_ids], dim=2)
-            by_id = cand_ids.masked_fill(cand_ids < 0, torch.iinfo(torch.int64).max).argsort(dim=-1, stable=True)
-            rank_in_id = cand_prio.gather(-1, by_id).argsort(dim=-1, descending=True, stable=True)
-            order = by_id.gather(-1, rank_in_id)                         # candidates, best first
-            keep = torch.zeros(B, H, P + count, dtype=torch.bool, device=dev)
-            keep.scatter_(-1, order[:, :, :P], True)
-            leave = ~keep[:, :, :P]                                       # top slots that are free or lose their cell
-            enter = keep[:, :, P:]                                        # new cells that make the list
-            # the r-th entering cell takes the r-th leaving slot (there are at least as many: |keep| = P); the others are
-            # written to the spare slot C, so that no two writes of one scatter meet
-            slot_rank = (leave.cumsum(-1) - 1).masked_fill(~leave, P + count)
-            leaving_slots = slot_rank.argsort(dim=-1, stable=True)[:, :, :count]          # (B,H,count)
-            target = leaving_slots.gather(-1, (enter.cumsum(-1) - 1).clamp_(min=0))
-            target = torch.where(enter, target, torch.full_like(target, self.C))
-            D = mean.shape[-1]
-            self.ids.scatter_(-1, target, new_ids)
-            self.prio.scatter_(-1, target, prio)
-            self.mean.scatter_(2, target.unsqueeze(-1).expand(B, H, count, D), mean)
-            rows = (target.unsqueeze(-1) * s + torch.arange(s, device=dev)).reshape(B, H, n)      # row of every new token
-            r4 = rows.unsqueeze(-1).expand(B, H, n, D)
-            self.k.scatter_(2, r4, nk)
-            self.v.scatter_(2, r4, nv)
-            self.ids[:, :, self.C] = -1
-            self.prio[:, :, self.C] = float("-inf")
-            if Wc:
-                # ring of the newest cells: cell c in slot P + c mod Wc (of more than Wc new cells the last Wc stay)
-                first = max(0, count - Wc)
-                cells = torch.arange(self.eligible + first, self.eligible + count, device=dev)
-                sl = P + cells % Wc
-                self.ids[:, :, sl] = new_ids[:, :, first:]
-                self.prio[:, :, sl] = prio[:, :, first:]
-                self.mean[:, :, sl] = mean[:, :, first:]
-                rr = (sl.unsqueeze(-1) * s + torch.arange(s, device=dev)).reshape(-1)
-                self.k[:, :, rr] = nk[:, :, first * s:]
-                self.v[:, :, rr] = nv[:, :, first * s:]
+            # the P best of (top list, new cells) by (ceiling desc, cell id asc) stay; entering cells take the slots of the
+            # leaving ones; the newest Wc cells also go into the ring; `valid` is rewritten - one launch, a few KB written
+            ops.linear_merge(self.ids, self.prio, self.mean, self.k, self.v, self.valid, P=P, Wc=Wc, first_id=self.eligible,
+                             new_prio=prio, new_mean=mean, new_k=nk, new_v=nv)
             self.pend_k, self.pend_v = self.pend_k[:, :, n:].clone(), self.pend_v[:, :, n:].clone()
             self.eligible += count
         self.block_start = start
         if self.eligible == 0:
             self.pool = None
             return
-        # a ring cell that is also in the top list counts once (ref: linear_cache.py:114-118, later occurrence dropped)
-        C = self.C
-        top_ids, ring_ids = self.ids[:, :, :P], self.ids[:, :, P:C]
-        dup = (ring_ids.unsqueeze(-1) == top_ids.unsqueeze(-2)).any(-1)
-        valid = self.ids[:, :, :C] >= 0
-        valid[:, :, P:] &= ~dup
         self.pool = dict(ids=self.ids[:, :, :C], priority=self.prio[:, :, :C], mean=self.mean[:, :, :C],
-                         k=self.k[:, :, :C * s], v=self.v[:, :, :C * s], valid=valid)
+                         k=self.k[:, :, :C * s], v=self.v[:, :, :C * s], valid=self.valid)
 
     # ---- new tokens ------------------------------------------------------------------------------------------------------
     def ingest(self, k, v):
@@ -168,30 +128,22 @@ class LinearFSCache:
         self.pos += n
 
     # ---- selection over the pool (ref: linear_cache.py:154-170) --------------------------------------------------------------
-    def select(self, q):
-        """q (B,H,n,D) at positions pos .. pos+n-1 -> (slots (B,H,n,k) int64 into the pool, cell ids with -1 for none)."""
-        pool = self.pool
-        if pool is None:
-            return None, None
+    def _select_slots(self, q, want_ids=False):
         a = self.attn
         lam, sigma, _, _ = a.head_params()
-        content = torch.einsum("bhqd,bhcd->bhqc", q.float(), pool["mean"]) * a.scale
-        score = content
-        if not getattr(a, "sel_content_only", False):
-            qpos = torch.arange(q.shape[2], device=q.device, dtype=torch.float32) + self.pos
-            centre = (pool["ids"].float() + 0.5) * self.s
-            dist = (qpos[None, None, :, None] - centre[:, :, None]).abs()
-            gate = torch.erf(dist / (2 * sigma.to(q.device)[None, :, None, None]))
-            score = content + lam.to(q.device)[None, :, None, None] * pool["priority"][:, :, None] * gate
-        ok = pool["valid"][:, :, None]
-        score = score.masked_fill(~ok, float("-inf"))
-        ids = pool["ids"][:, :, None].expand_as(score).masked_fill(~ok, -1)
-        # the best k by (score desc, cell id asc): order by id first, then a stable descending sort of the scores
-        by_id = ids.masked_fill(ids < 0, torch.iinfo(torch.int64).max).argsort(dim=-1, stable=True)
-        k = min(a.cell_topk, self.eligible)
-        best = score.gather(-1, by_id).argsort(dim=-1, descending=True, stable=True)[..., :k]
-        slots = by_id.gather(-1, best)
-        return slots, ids.gather(-1, slots)
+        return ops.linear_select(q.to(torch.bfloat16), self.ids, self.prio, self.mean, self.valid, lam, sigma, pos0=self.pos,
+                                 kk=min(a.cell_topk, self.eligible), kk_out=a.cell_topk, scale=a.scale,
+                                 content_only=bool(getattr(a, "sel_content_only", False)), want_ids=want_ids)
+
+    def select(self, q):
+        """q (B,H,n<=128,D) at positions pos .. pos+n-1 -> (slots (B,H,n,k) int64 into the pool, cell ids with -1 for none),
+        k = min(cell_topk, eligible cells): the best by (score desc, cell id asc)."""
+        if self.pool is None:
+            return None, None
+        k = min(self.attn.cell_topk, self.eligible)
+        slots, ids = self._select_slots(q, want_ids=True)
+        slots, ids = slots[..., :k].long(), ids[..., :k].long()
+        return slots.clamp_(min=0), ids
 
     # ---- one forward of the layer's attention over new tokens (ref: linear_cache.py:192-205) -------------------------------
     def attend(self, q, k, v):
@@ -221,9 +173,12 @@ class LinearFSCache:
             if self.pool is None:
                 y[:, off:off + m] = sr                  # no completed cell yet: the long-range branch is zero
             else:
-                slots, ids = self.select(qp)
-                sel = torch.full((B, H, m, a.cell_topk), -1, dtype=torch.int32, device=q.device)
-                sel[..., :slots.shape[-1]] = torch.where(ids >= 0, slots, torch.full_like(slots, -1)).to(torch.int32)
+                if type(self).select is not LinearFSCache.select or "select" in self.__dict__:
+                    slots, ids = self.select(qp)                 # an overridden / wrapped select stays in the loop
+                    sel = torch.full((B, H, m, a.cell_topk), -1, dtype=torch.int32, device=q.device)
+                    sel[..., :slots.shape[-1]] = torch.where(ids >= 0, slots, torch.full_like(slots, -1)).to(torch.int32)
+                else:
+                    sel = self._select_slots(qp)
                 # the pool slots are the "cells" of this readout; every pool token lies before the virtual query position
                 n_kv = self.C * self.s
                 out = ops.readout_combine(qp.to(torch.bfloat16), self.pool["k"], self.pool["v"], sel, sr, norm_w, lrs,

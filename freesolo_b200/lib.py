@@ -169,6 +169,19 @@ class FsbForest(C.Structure):
                 ("node_mu", vp), ("node_aux", vp), ("root32", vp), ("compact", i32)]
 
 
+class LinearMerge(C.Structure):
+    _fields_ = [("ids", vp), ("prio", vp), ("mean", vp), ("k", vp), ("v", vp), ("valid", vp),
+                ("new_prio", vp), ("new_mean", vp), ("new_k", vp), ("new_v", vp), ("nk_sb", i64), ("nk_sh", i64),
+                ("B", i32), ("H", i32), ("D", i32), ("P", i32), ("Wc", i32), ("count", i32), ("first_id", i32)]
+
+
+class LinearSelect(C.Structure):
+    _fields_ = [("ids", vp), ("prio", vp), ("mean", vp), ("valid", vp),
+                ("q", BHND), ("lam", vp), ("sigma", vp), ("scale", f32),
+                ("B", i32), ("H", i32), ("D", i32), ("C", i32), ("n", i32), ("n_pad", i32), ("kk", i32), ("kk_out", i32),
+                ("pos0", i32), ("content_only", i32), ("sel", vp), ("sel_ids", vp)]
+
+
 class FsbSelect(C.Structure):
     _fields_ = [("main", FsbForest), ("second", FsbForest), ("q", BHND), ("k", BHND),
                 ("kq", vp), ("ks", vp), ("kq_sb", i64), ("kq_sh", i64), ("ks_sb", i64), ("ks_sh", i64),
@@ -182,7 +195,8 @@ FSB_SPINE_MAX = 20
 FSB_MAX_MCAP = 16384
 
 EXTRA_STRUCTS = {"fsattn_fs_dense_select_t": FsDenseSelect, "fsattn_fs_dense_decode_select_t": FsDenseDecodeSelect,
-                 "fsattn_trunk_gemv_t": TrunkGemv, "fsattn_trunk_layer_t": TrunkLayer, "fsattn_fsb_forest_t": FsbForest, "fsattn_fsb_select_t": FsbSelect}
+                 "fsattn_trunk_gemv_t": TrunkGemv, "fsattn_trunk_layer_t": TrunkLayer, "fsattn_fsb_forest_t": FsbForest, "fsattn_fsb_select_t": FsbSelect,
+                 "fsattn_linear_merge_t": LinearMerge, "fsattn_linear_select_t": LinearSelect}
 
 # every exported symbol of include/fsattn_b200.h with its argument struct (None = no struct argument)
 ENTRY_POINTS = {
@@ -208,6 +222,8 @@ ENTRY_POINTS = {
     "fsattn_fsb_scratch_floats": ([i32, i32, i32], i64),
     "fsattn_fsb_ingest": ([C.POINTER(FsbForest), i32, i32, i32, vp, i64, vp], C.c_int),
     "fsattn_fsb_compact": ([C.POINTER(FsbForest), C.POINTER(FsbForest), vp], C.c_int),
+    "fsattn_linear_merge": LinearMerge,
+    "fsattn_linear_select": LinearSelect,
     "fsattn_fsb_spines": ([C.POINTER(FsbForest), i32, i32, C.POINTER(vp), C.POINTER(vp), vp], C.c_int),
     "fsattn_fsb_select": FsbSelect,
 }

@@ -741,6 +741,52 @@ def fsb_select(forests: FsbForests, Q, K, lam, sigma, *, scale: float, N: int = 
 
 
 
+def linear_merge(ids, prio, mean, k, v, valid, *, P: int, Wc: int, first_id: int = 0, new_prio=None, new_mean=None,
+                 new_k=None, new_v=None) -> None:
+    """Block change of the streaming cache's pool (see fsattn_linear_merge_t): the new cells (statistics new_prio (B,H,n),
+    new_mean (B,H,n,D); rows new_k / new_v (B,H,n*32,D) bf16, contiguous) enter the top list / the ring in place and `valid`
+    is rewritten. Without new cells only `valid` is rewritten."""
+    _need_cuda(ids, prio, mean, k, v, valid)
+    B, H, C1 = ids.shape
+    D = mean.shape[-1]
+    assert C1 == P + Wc + 1 and ids.dtype == torch.int32 and prio.dtype == torch.float32 and mean.dtype == torch.float32
+    assert k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16 and valid.dtype == torch.uint8
+    assert all(t.is_contiguous() for t in (ids, prio, mean, k, v, valid)) and k.shape[2] == C1 * CELL and valid.shape[-1] == C1 - 1
+    a = L.LinearMerge()
+    a.ids, a.prio, a.mean, a.k, a.v, a.valid = (t.data_ptr() for t in (ids, prio, mean, k, v, valid))
+    a.B, a.H, a.D, a.P, a.Wc, a.first_id = B, H, D, int(P), int(Wc), int(first_id)
+    a.count = 0
+    if new_prio is not None:
+        n = new_prio.shape[-1]
+        assert new_prio.is_contiguous() and new_mean.is_contiguous() and new_k.is_contiguous() and new_v.is_contiguous()
+        assert new_k.shape == (B, H, n * CELL, D) and new_k.dtype == torch.bfloat16 and new_v.shape == new_k.shape
+        a.count = n
+        a.new_prio, a.new_mean, a.new_k, a.new_v = new_prio.data_ptr(), new_mean.data_ptr(), new_k.data_ptr(), new_v.data_ptr()
+        a.nk_sb, a.nk_sh = new_k.stride(0), new_k.stride(1)
+    L.call("fsattn_linear_merge", a, _stream(ids))
+
+
+def linear_select(q, ids, prio, mean, valid, lam, sigma, *, pos0: int, kk: int, kk_out: int, scale: float,
+                  content_only: bool = False, want_ids: bool = False):
+    """The streaming cache's selection (see fsattn_linear_select_t): q (B,H,n<=128,D) bf16 -> pool slots (B,H,n,kk_out)
+    int32 (-1 none), and the cell ids when asked."""
+    _need_cuda(q, ids, prio, mean, valid)
+    B, H, n, D = q.shape
+    C = valid.shape[-1]
+    sel = torch.empty(B, H, n, kk_out, dtype=torch.int32, device=q.device)
+    sid = torch.empty(B, H, n, kk_out, dtype=torch.int32, device=q.device) if want_ids else None
+    lam, sigma = _f32(lam).to(q.device), _f32(sigma).to(q.device)
+    a = L.LinearSelect()
+    a.ids, a.prio, a.mean, a.valid = ids.data_ptr(), prio.data_ptr(), mean.data_ptr(), valid.data_ptr()
+    a.q = _bhnd(q, "q")
+    a.lam, a.sigma, a.scale = lam.data_ptr(), sigma.data_ptr(), float(scale)
+    a.B, a.H, a.D, a.C, a.n, a.n_pad, a.kk, a.kk_out, a.pos0 = B, H, D, C, n, n, int(kk), int(kk_out), int(pos0)
+    a.content_only = 1 if content_only else 0
+    a.sel, a.sel_ids = sel.data_ptr(), _p(sid)
+    L.call("fsattn_linear_select", a, _stream(q))
+    return (sel, sid) if want_ids else sel
+
+
 def swiglu(gu: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """out (..., f) = silu(gu[..., :f]) * gu[..., f:] for a fused gate/up projection gu (..., 2f) bf16, one pass."""
     _need_cuda(gu)

@@ -371,6 +371,37 @@ typedef struct {
  * order of det_reduce.det_sum and no multiply-add is contracted. scratch: fsattn_fsb_scratch_floats(m_cap, D, T) floats
  * per forest, used only during the call. */
 FSATTN_API int64_t fsattn_fsb_scratch_floats(int32_t m_cap, int32_t D, int32_t T);
+/* ---- streaming FS-L cache (replaces the pool bookkeeping and selection of src/fsattn/linear_cache.py) -----------------------
+ * Pool of one (b,h): C = P + Wc cell slots plus one spare - slots [0, P) the cells with the highest ceilings seen so far (in no
+ * particular order), [P, C) a ring of the newest cells (cell c in slot P + c mod Wc); id -1 = empty.
+ *   ids (B,H,C+1) int32, prio (B,H,C+1) fp32 ceilings, mean (B,H,C+1,D) fp32 chunk-mean keys, k / v (B,H,(C+1)*32,D) bf16 token
+ *   rows of the slots, valid (B,H,C) uint8. All contiguous. */
+
+/* Block change (linear_cache.py:86-118): `count` newly completed cells with ids first_id .. first_id+count-1, their
+ * statistics new_prio (B,H,count), new_mean (B,H,count,D) (from fsattn_cell_ingest) and token rows new_k / new_v (B,H,count*32,D)
+ * bf16 (batch / head strides nk_sb / nk_sh, rows contiguous). The P best of (top list, new cells) by (ceiling desc, id asc)
+ * stay: an entering cell is written into the slot of a leaving one, nothing else moves; the newest Wc cells also go into the
+ * ring; valid is rewritten (a ring cell that is in the top list too counts once). count = 0 only rewrites valid. */
+typedef struct {
+    int32_t* ids; float* prio; float* mean; void* k; void* v; unsigned char* valid;
+    const float* new_prio; const float* new_mean; const void* new_k; const void* new_v; int64_t nk_sb, nk_sh;
+    int32_t B, H, D, P, Wc, count, first_id;
+} fsattn_linear_merge_t;
+FSATTN_API int fsattn_linear_merge(const fsattn_linear_merge_t* a, fsattn_stream_t stream);
+
+/* Selection of n <= 128 queries of one block (linear_cache.py:154-170): q (B,H,n,D) bf16 at positions pos0 .. pos0+n-1;
+ * score = (q . mean) scale + lam_h ceil erf(|p - (id + 0.5) 32| / (2 sigma_h)) over the valid slots (content_only = 1 drops
+ * the second term); the best kk <= 4 by (score desc, cell id asc) as POOL SLOTS in sel (B,H,n_pad,kk_out) int32, -1 for none
+ * (and beyond kk); sel_ids (optional, same shape): the cell ids. The slots index the pool's k / v as 32-row cells, which is
+ * what fsattn_readout_combine then reads. */
+typedef struct {
+    const int32_t* ids; const float* prio; const float* mean; const unsigned char* valid;
+    fsattn_bhnd_t q; const float* lam; const float* sigma; float scale;
+    int32_t B, H, D, C, n, n_pad, kk, kk_out, pos0, content_only;
+    int32_t* sel; int32_t* sel_ids;
+} fsattn_linear_select_t;
+FSATTN_API int fsattn_linear_select(const fsattn_linear_select_t* a, fsattn_stream_t stream);
+
 /* Copies the chunks of the current prefix (one per set bit of m_tot, per row) from a full arena into a compact one.
  * src and dst share T, H, D, m_cap, adm, m_tot, m_prev; dst->compact = 1 with its own node_mu (T, 4 m_cap, D), node_aux
  * (T, 4 m_cap, 4) and root32 (T, 32, D+4). After it the decode-time ingest, spines and selection run on dst; the full arena
