@@ -9,6 +9,14 @@
 
 namespace {
 
+#ifdef FSATTN_FSB_TIMING
+// debug build only: clock64 stamps of the decode selection of row 0 (warp 0 lane 0), read back with fsattn_debug_fsb_timing
+__device__ long long g_fsb_stamps[64];
+#define FSTAMP(i) do { if (blockIdx.x == 0 && threadIdx.x == 0) g_fsb_stamps[(i)] = clock64(); } while (0)
+#else
+#define FSTAMP(i) do { } while (0)
+#endif
+
 constexpr int SPW = FSATTN_FSB_SPINE_MAX;      // spine slots per forest
 constexpr int WMAX = 16;                       // frontier slots
 
@@ -315,6 +323,7 @@ __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, co
         nvis += P.nvis;
     }
     for (int it = 0; it < 40; ++it) {
+        if constexpr (!STAGED) { if (it < 20) FSTAMP(16 + it); }
         const bool active = lane < WMAX && ref != -1;
         const bool expand = active && (ref < -1 || meta < 0);
         const unsigned emask = __ballot_sync(FS_FULL, expand);
@@ -347,6 +356,7 @@ __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, co
             score = node_score(cref, nc, cmeta);
         }
         nvis += __popc(__ballot_sync(FS_FULL, valid));
+        if constexpr (!STAGED) { if (it < 4 && __float_as_int(score) != 0x7fc00001) FSTAMP(36 + 2 * it); }
         // ---- rank the children: (score desc, position asc) ----
         // (32 independent shuffles pipeline well; a warp-wide max per kept child is a chain of dependent reductions and
         // measured slower in the latency-bound decode kernel and no faster in prefill)
@@ -365,6 +375,7 @@ __device__ int beam(const fsattn_fsb_forest_t& F, int t, const SpineSm<D>& S, co
                 rank += (so > score || (so == score && o < lane)) ? 1 : 0;
             }
         }
+        if constexpr (!STAGED) { if (it < 4 && rank >= 0) FSTAMP(37 + 2 * it); }
         const int ncar = __popc(cmask & 0xffffu);
         int* fm = fr + WMAX;                   // fr: WMAX refs then WMAX metas
         if (lane < WMAX) fr[lane] = -1;
@@ -637,23 +648,55 @@ __global__ void __launch_bounds__(256) fsb_decode_select_kernel(SelArgs A) {
     __shared__ float u_s[32];
     __shared__ int nv_s[2];
 
+    FSTAMP(0);
     const int nsp = a.width2 > 0 ? 2 : 1;
-    for (int w = 0; w < nsp; ++w) {
-        const float* src = a.spine[w] + (int64_t)t * SPW * (D + 8);
-        float* dst = &sp[w].node[0][0];
-        for (int i = tid; i < SPW * (D + 8); i += 256) dst[i] = src[i];
-        if (tid == 0) {
-            const int* h = a.hdr[w] + t * 4;
-            sp[w].root = h[0]; sp[w].height = h[1]; sp[w].m_b = h[2];
+    {
+        // every load of both spines is issued before the first store to shared memory: a load-then-store loop would wait for
+        // each memory round trip in turn (in-order issue), a dozen of them back to back
+        constexpr int NSPF = SPW * (D + 8), NIT = (NSPF + 255) / 256;
+        float tmp[2][NIT];
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {
+            const float* src = a.spine[w < nsp ? w : 0] + (int64_t)t * NSPF;
+#pragma unroll
+            for (int j = 0; j < NIT; ++j) tmp[w][j] = (w < nsp && tid + 256 * j < NSPF) ? src[tid + 256 * j] : 0.f;
+        }
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {
+            float* dst = &sp[w].node[0][0];
+#pragma unroll
+            for (int j = 0; j < NIT; ++j)
+                if (w < nsp && tid + 256 * j < NSPF) dst[tid + 256 * j] = tmp[w][j];
         }
     }
     const float lam = a.lam[hd], sig = a.sigma[hd];
     const float qpos = (float)(*a.pos);
+    if (tid == 0) {
+        const int4 h0 = *reinterpret_cast<const int4*>(a.hdr[0] + t * 4);
+        const int4 h1 = *reinterpret_cast<const int4*>(a.hdr[nsp > 1 ? 1 : 0] + t * 4);
+        sp[0].root = h0.x; sp[0].height = h0.y; sp[0].m_b = h0.z;
+        sp[0].pad = h0.w;                         // beam width the stored beam head was computed for (0 = none)
+        if (nsp > 1) { sp[1].root = h1.x; sp[1].height = h1.y; sp[1].m_b = h1.z; sp[1].pad = h1.w; }
+    }
     if (tid < 32) { cand_s[tid] = -1; u_s[tid] = -INFINITY; }
     __syncthreads();
     // the query-independent head of each beam (a few dependent table reads) also runs before the dependency wait
-    if (warp < nsp) beam_prefix<D>(warp == 0 ? a.main : a.second, t, sp[warp], warp == 0 ? a.width : a.width2, lane, pre[warp]);
+    FSTAMP(1);
+    if (warp < nsp) {
+        // the query-independent head of the beam: stored beside the spine at the block change, else walked here
+        const int wd = warp == 0 ? a.width : a.width2;
+        if (sp[warp].pad == wd) {
+            const int* src = reinterpret_cast<const int*>(&sp[warp].node[SPW - 1][0]);
+            int* dst = reinterpret_cast<int*>(&pre[warp]);
+            for (int i = lane; i < (int)(sizeof(BeamPre) / 4); i += 32) dst[i] = src[i];
+            __syncwarp();
+        } else {
+            beam_prefix<D>(warp == 0 ? a.main : a.second, t, sp[warp], wd, lane, pre[warp]);
+        }
+    }
+    FSTAMP(2);
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    FSTAMP(3);
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const bf16* qp = (const bf16*)a.q.ptr + b * a.q.sb + hd * a.q.sh;
     for (int d = tid; d < DP; d += 256) qs[d] = (d < D) ? __bfloat162float(qp[d]) : 0.f;
@@ -670,12 +713,15 @@ __global__ void __launch_bounds__(256) fsb_decode_select_kernel(SelArgs A) {
             qreg[i * 4 + 0] = w4.x; qreg[i * 4 + 1] = w4.y; qreg[i * 4 + 2] = w4.z; qreg[i * 4 + 3] = w4.w;
         }
         int nv = 0;
+        FSTAMP(4);
         const int c = beam<D, true>(warp == 0 ? a.main : a.second, t, sp[warp], pre[warp], qreg, qn, qpos, lam, sig, a.scale,
                                     warp == 0 ? a.width : a.width2, lane, frs[warp], nv);
         if (lane < WMAX) cand_s[warp * WMAX + lane] = (lane < (warp == 0 ? a.width : a.width2)) ? c : -1;
         if (lane == 0) nv_s[warp] = nv;
     }
+    FSTAMP(5);
     __syncthreads();
+    FSTAMP(6);
     if (warp == 0) {                      // union: blank the second beam's repeats of a main cell
         const int mine = cand_s[lane];
         bool dup = false;
@@ -699,6 +745,7 @@ __global__ void __launch_bounds__(256) fsb_decode_select_kernel(SelArgs A) {
         const int nbytes = a.k.ptr ? (int)(32 * a.k.sn * 2) : 32 * D;
         for (int o = lane * 128; o < nbytes; o += 32 * 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(rows + o));
     }
+    FSTAMP(7);
     {   // a warp's cells in groups: all rows of a group are requested before the first is scored
         constexpr int RG = (D <= 64) ? 4 : 1;     // wider heads keep one row at a time: two already spill
         for (int i0 = warp; i0 < 32; i0 += NW * RG) {
@@ -718,7 +765,9 @@ __global__ void __launch_bounds__(256) fsb_decode_select_kernel(SelArgs A) {
             }
         }
     }
+    FSTAMP(8);
     __syncthreads();
+    FSTAMP(9);
     if (warp == 0) {
         const float u = u_s[lane];
         const int cand = cand_s[lane];
@@ -730,21 +779,33 @@ __global__ void __launch_bounds__(256) fsb_decode_select_kernel(SelArgs A) {
         }
         if (rank < a.read_top) a.sel[(int64_t)t * a.read_top + rank] = (u == -INFINITY) ? -1 : cand;
     }
+    FSTAMP(10);
 }
 
+// The last spine slot is never a spine node (heights stay below 15): it carries the beam's query-independent head
+// (beam_prefix) for the beam width the caller names, so that a decode step only copies it (hdr[3] = that width, 0 = none).
+static_assert(sizeof(BeamPre) <= (64 + 8) * sizeof(float), "the beam head must fit one spine slot");
+
 template <int D>
-__global__ void fsb_spine_kernel(fsattn_fsb_forest_t F, int n_visible, float* spine, int* hdr) {
+__global__ void fsb_spine_kernel(fsattn_fsb_forest_t F, int n_visible, int width, float* spine, int* hdr) {
     const int t = blockIdx.x, lane = threadIdx.x;
     __shared__ SpineSm<D> S;
+    __shared__ BeamPre P;
     for (int i = lane; i < SPW * (D + 8); i += 32) (&S.node[0][0])[i] = 0.f;
     __syncwarp();
     const int m_b = count_below(F.adm + (int64_t)t * F.m_cap, F.m_tot[t], n_visible);
     build_spine<D>(F, t, m_b, S, lane);
     __syncwarp();
+    if (width > 0) {
+        beam_prefix<D>(F, t, S, width, lane, P);
+        int* slot = reinterpret_cast<int*>(&S.node[SPW - 1][0]);
+        for (int i = lane; i < (int)(sizeof(BeamPre) / 4); i += 32) slot[i] = reinterpret_cast<const int*>(&P)[i];
+        __syncwarp();
+    }
     float* dst = spine + (int64_t)t * SPW * (D + 8);
     for (int i = lane; i < SPW * (D + 8); i += 32) dst[i] = (&S.node[0][0])[i];
     if (lane == 0) {
-        hdr[t * 4 + 0] = S.root; hdr[t * 4 + 1] = S.height; hdr[t * 4 + 2] = S.m_b; hdr[t * 4 + 3] = 0;
+        hdr[t * 4 + 0] = S.root; hdr[t * 4 + 1] = S.height; hdr[t * 4 + 2] = S.m_b; hdr[t * 4 + 3] = width > 0 ? width : 0;
     }
 }
 
@@ -753,8 +814,14 @@ __global__ void fsb_spine_kernel(fsattn_fsb_forest_t F, int n_visible, float* sp
 int fs_fsb_check_forest(const fsattn_fsb_forest_t& f, const char* what);
 int fs_fsb_rerank_block(const fsattn_fsb_select_t* a, cudaStream_t st);
 
+#ifdef FSATTN_FSB_TIMING
+extern "C" __attribute__((visibility("default"))) int fsattn_debug_fsb_timing(long long* out64) {
+    return cudaMemcpyFromSymbol(out64, g_fsb_stamps, sizeof(long long) * 64) == cudaSuccess ? 0 : -1;
+}
+#endif
+
 extern "C" int fsattn_fsb_spines(const fsattn_fsb_forest_t* forests, int32_t n_forests, int32_t n_visible,
-                                 float* const* spine, int32_t* const* hdr, fsattn_stream_t stream) {
+                                 float* const* spine, int32_t* const* hdr, const int32_t* widths, fsattn_stream_t stream) {
     FS_REQUIRE(forests && spine && hdr && n_forests >= 1, "fsb_spines: null argument");
     for (int i = 0; i < n_forests; ++i) {
         const fsattn_fsb_forest_t& F = forests[i];
@@ -762,10 +829,12 @@ extern "C" int fsattn_fsb_spines(const fsattn_fsb_forest_t* forests, int32_t n_f
         if (rc != FSATTN_OK) return rc;
         FS_REQUIRE(spine[i] && hdr[i] && n_visible >= 0, "fsb_spines: null output");
         cudaStream_t st = (cudaStream_t)stream;
+        const int width = widths ? widths[i] : 0;
+        FS_REQUIRE(width >= 0 && width <= WMAX, "fsb_spines: beam width %d (0 = no beam head, at most %d)", width, WMAX);
         switch (F.D) {
-            case 64: fsb_spine_kernel<64><<<F.T, 32, 0, st>>>(F, n_visible, spine[i], hdr[i]); break;
-            case 96: fsb_spine_kernel<96><<<F.T, 32, 0, st>>>(F, n_visible, spine[i], hdr[i]); break;
-            default: fsb_spine_kernel<128><<<F.T, 32, 0, st>>>(F, n_visible, spine[i], hdr[i]); break;
+            case 64: fsb_spine_kernel<64><<<F.T, 32, 0, st>>>(F, n_visible, width, spine[i], hdr[i]); break;
+            case 96: fsb_spine_kernel<96><<<F.T, 32, 0, st>>>(F, n_visible, width, spine[i], hdr[i]); break;
+            default: fsb_spine_kernel<128><<<F.T, 32, 0, st>>>(F, n_visible, width, spine[i], hdr[i]); break;
         }
         rc = fs_check_launch("fsb_spine_kernel");
         if (rc != FSATTN_OK) return rc;

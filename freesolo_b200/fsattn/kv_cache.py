@@ -147,7 +147,7 @@ class FSKVCache:
         fo = self.fsb_forests(None, None, attn)
         n_vis = min(blk // self.s, pos // self.s)
         fo.ingest(n_vis)
-        fo.build_spines(n_vis)
+        fo.build_spines(n_vis, widths=(attn.fsb_width, attn._fsb_w2(fo)))
         self._fsb_blk = blk
         return True
 

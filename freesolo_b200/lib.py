@@ -224,7 +224,7 @@ ENTRY_POINTS = {
     "fsattn_fsb_compact": ([C.POINTER(FsbForest), C.POINTER(FsbForest), vp], C.c_int),
     "fsattn_linear_merge": LinearMerge,
     "fsattn_linear_select": LinearSelect,
-    "fsattn_fsb_spines": ([C.POINTER(FsbForest), i32, i32, C.POINTER(vp), C.POINTER(vp), vp], C.c_int),
+    "fsattn_fsb_spines": ([C.POINTER(FsbForest), i32, i32, C.POINTER(vp), C.POINTER(vp), C.POINTER(i32), vp], C.c_int),
     "fsattn_fsb_select": FsbSelect,
 }
 

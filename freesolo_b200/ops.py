@@ -678,13 +678,16 @@ class FsbForests:
                                       _stream(self.kbar)), "fsattn_fsb_ingest")
         self.n_seen = cell_end
 
-    def build_spines(self, n_visible: int) -> None:
-        """Spines of the prefix of cells [0, n_visible) for decode queries (kept until the next call)."""
+    def build_spines(self, n_visible: int, widths=None) -> None:
+        """Spines of the prefix of cells [0, n_visible) for decode queries (kept until the next call). widths: the beam width
+        per forest; with it the beams' query-independent heads are stored beside the spines, and a decode step copies them
+        instead of walking them."""
         lib = L.load()
         arr = (L.FsbForest * self.nf)(*[self.struct(i) for i in range(self.nf)])
         sp = (L.vp * self.nf)(*[t.data_ptr() for t in self.spine])
         hd = (L.vp * self.nf)(*[t.data_ptr() for t in self.hdr])
-        L.check(lib.fsattn_fsb_spines(arr, self.nf, int(n_visible), sp, hd, _stream(self.kbar)), "fsattn_fsb_spines")
+        wd = None if widths is None else (L.i32 * self.nf)(*[int(w) for w in list(widths)[:self.nf]])
+        L.check(lib.fsattn_fsb_spines(arr, self.nf, int(n_visible), sp, hd, wd, _stream(self.kbar)), "fsattn_fsb_spines")
 
 
 def fsb_select(forests: FsbForests, Q, K, lam, sigma, *, scale: float, N: int = None, q_pos0: int = 0, Bq: int = 128,

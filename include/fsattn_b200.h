@@ -414,10 +414,13 @@ FSATTN_API int fsattn_fsb_ingest(const fsattn_fsb_forest_t* forests, int32_t n_f
 /* Spines (fsb_tree.py:1070-1132): per forest and row, the nodes that merge the chunk roots named by the bits of
  * m_b = #admitted cells with id < n_visible. spine (T, FSATTN_FSB_SPINE_MAX, D+8) fp32 per forest:
  * [mu (D) | rad, amax, pmin(int), cnt(int), child_l(int), child_r(int), pad, pad]; hdr (T, 4) int32: root ref, height,
- * m_b, 0. Node refs: >= 0 a node id of the row's arena, -(k+2) the spine node of height k, -1 none. */
+ * m_b, w. Node refs: >= 0 a node id of the row's arena, -(k+2) the spine node of height k, -1 none.
+ * widths (host array, one beam width per forest, or NULL): with a width w > 0 the last spine slot (never a spine node) also
+ * receives the beam's query-independent head for that width - the rounds whose children all fit in the frontier, walked
+ * once here instead of in every decode step - and hdr[3] = w; the decode selection uses it when its beam width equals w. */
 #define FSATTN_FSB_SPINE_MAX 20
 FSATTN_API int fsattn_fsb_spines(const fsattn_fsb_forest_t* forests, int32_t n_forests, int32_t n_visible,
-                                 float* const* spine, int32_t* const* hdr, fsattn_stream_t stream);
+                                 float* const* spine, int32_t* const* hdr, const int32_t* widths, fsattn_stream_t stream);
 
 /* Selection for queries. Replaces traverse_forest in the serve configuration (fsb_tree.py:1183-1317: fixed policy,
  * delta 0, 'bound' node score, second beam, token-LSE re-rank 'lse_pos' with the raw query, read_top): both beams
