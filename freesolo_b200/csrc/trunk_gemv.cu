@@ -38,6 +38,17 @@ __global__ void __launch_bounds__(GEMV_THREADS) trunk_gemv_kernel(const fsattn_t
             }
         }
     }
+    // the norm weights do not depend on the producer either: this thread's chunks go to registers now
+    constexpr int NIT = (KC + 7) / 8;                                 // activation chunks per thread (256 threads, 8 per lane-row)
+    constexpr bool XREG = NIT * M <= 8;                               // small enough to keep the activations in registers
+    uint4 nwr[NIT];
+    if (a.norm_w != nullptr) {
+#pragma unroll
+        for (int i = 0; i < NIT; i++) {
+            const int c = tid + i * GEMV_THREADS;
+            nwr[i] = c < kchunks ? *reinterpret_cast<const uint4*>((const bf16*)a.norm_w + c * 8) : make_uint4(0u, 0u, 0u, 0u);
+        }
+    }
     // Wait for the producer, THEN release the consumer: at most two kernels of the chain overlap, so a consumer's
     // prologue only ever runs beside its direct producer's main phase.
     pdl_wait();
@@ -45,6 +56,70 @@ __global__ void __launch_bounds__(GEMV_THREADS) trunk_gemv_kernel(const fsattn_t
 
     // ---- activations -> shared memory (optionally RMS-normalised, rounded to bf16 like the eager norm's output) ----
     const bf16* X = (const bf16*)a.x + (int64_t)a.m0 * a.x_stride;
+    if constexpr (XREG) {
+        // every activation chunk of this thread is loaded before anything uses it: a load-use-load loop would pay the memory
+        // round trips one after the other (in-order issue), and the normalised pass would read x a second time
+        uint4 xr[M][NIT];
+#pragma unroll
+        for (int i = 0; i < NIT; i++) {
+            const int c = tid + i * GEMV_THREADS;
+#pragma unroll
+            for (int m = 0; m < M; m++)
+                xr[m][i] = c < kchunks ? *reinterpret_cast<const uint4*>(X + (int64_t)m * a.x_stride + c * 8) : make_uint4(0u, 0u, 0u, 0u);
+        }
+        if (a.norm_w != nullptr) {
+            float ss[M];
+#pragma unroll
+            for (int m = 0; m < M; m++) {
+                ss[m] = 0.0f;
+                // chunk by chunk in the order of the loop version (the sum of squares is rounding-sensitive)
+#pragma unroll
+                for (int i = 0; i < NIT; i++) {
+                    const uint4 x = xr[m][i];
+                    const float v[8] = {bf_lo(x.x), bf_hi(x.x), bf_lo(x.y), bf_hi(x.y), bf_lo(x.z), bf_hi(x.z), bf_lo(x.w), bf_hi(x.w)};
+#pragma unroll
+                    for (int j = 0; j < 8; j++) ss[m] = fmaf(v[j], v[j], ss[m]);
+                }
+                const float sw = warp_sum(ss[m]);
+                if (lane == 0) red[warp][m] = sw;
+            }
+            __syncthreads();
+            float rinv[M];
+#pragma unroll
+            for (int m = 0; m < M; m++) {
+                float sr = 0.0f;
+#pragma unroll
+                for (int w = 0; w < GEMV_WARPS; w++) sr += red[w][m];
+                rinv[m] = rsqrtf(sr / (float)a.K + a.eps);
+            }
+#pragma unroll
+            for (int i = 0; i < NIT; i++) {
+                const int c = tid + i * GEMV_THREADS;
+                if (c >= kchunks) continue;
+                const uint4 nw = nwr[i];
+                const float g[8] = {bf_lo(nw.x), bf_hi(nw.x), bf_lo(nw.y), bf_hi(nw.y), bf_lo(nw.z), bf_hi(nw.z), bf_lo(nw.w), bf_hi(nw.w)};
+#pragma unroll
+                for (int m = 0; m < M; m++) {
+                    const uint4 x = xr[m][i];
+                    const float v[8] = {bf_lo(x.x), bf_hi(x.x), bf_lo(x.y), bf_hi(x.y), bf_lo(x.z), bf_hi(x.z), bf_lo(x.w), bf_hi(x.w)};
+                    uint4 o;
+                    o.x = pack_bf2(v[0] * rinv[m] * g[0], v[1] * rinv[m] * g[1]);
+                    o.y = pack_bf2(v[2] * rinv[m] * g[2], v[3] * rinv[m] * g[3]);
+                    o.z = pack_bf2(v[4] * rinv[m] * g[4], v[5] * rinv[m] * g[5]);
+                    o.w = pack_bf2(v[6] * rinv[m] * g[6], v[7] * rinv[m] * g[7]);
+                    xs[m * kchunks + c] = o;
+                }
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < NIT; i++) {
+                const int c = tid + i * GEMV_THREADS;
+                if (c >= kchunks) continue;
+#pragma unroll
+                for (int m = 0; m < M; m++) xs[m * kchunks + c] = xr[m][i];
+            }
+        }
+    } else
     if (a.norm_w != nullptr) {
         float ss[M];
 #pragma unroll
