@@ -218,6 +218,8 @@ ENTRY_POINTS = {
     "fsattn_trunk_gemv": TrunkGemv,
     "fsattn_trunk_layer": TrunkLayer,
     "fsattn_swiglu": ([vp, i64, vp, i64, i64, i32, vp], C.c_int),
+    "fsattn_embed_rows": ([vp, vp, vp, i32, i32, i64, vp], C.c_int),
+    "fsattn_argmax_advance": ([vp, i64, i32, i32, vp, vp, vp], C.c_int),
     "fsattn_rms_norm": ([vp, i64, vp, f32, vp, i64, i64, i32, vp], C.c_int),
     "fsattn_fsb_scratch_floats": ([i32, i32, i32], i64),
     "fsattn_fsb_ingest": ([C.POINTER(FsbForest), i32, i32, i32, vp, i64, vp], C.c_int),

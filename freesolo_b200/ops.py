@@ -790,6 +790,28 @@ def linear_select(q, ids, prio, mean, valid, lam, sigma, *, pos0: int, kk: int, 
     return (sel, sid) if want_ids else sel
 
 
+def embed_rows(tok: torch.Tensor, table: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """out (B,d) bf16 = table[tok[b]] for tok (B,) or (B,1) int64: the decode step's embedding lookup as one launch."""
+    _need_cuda(tok, table, out)
+    B = tok.numel()
+    assert tok.dtype == torch.int64 and tok.is_contiguous() and table.dtype == torch.bfloat16 and table.is_contiguous()
+    assert out.dtype == torch.bfloat16 and out.is_contiguous() and out.numel() == B * table.shape[1]
+    L.check(L.load().fsattn_embed_rows(tok.data_ptr(), table.data_ptr(), out.data_ptr(), B, table.shape[1], table.shape[0],
+                                       _stream(out)), "fsattn_embed_rows")
+    return out
+
+
+def argmax_advance(logits: torch.Tensor, tok: torch.Tensor, pos: torch.Tensor | None = None) -> torch.Tensor:
+    """tok (B,) or (B,1) int64 = argmax over the last dim of logits (B,V) bf16 (lowest index on ties); pos (0-d int64 device
+    tensor) is incremented when given: the decode step's sampling tail as one launch."""
+    _need_cuda(logits, tok)
+    assert logits.dim() == 2 and logits.dtype == torch.bfloat16 and logits.stride(1) == 1 and tok.dtype == torch.int64
+    assert tok.is_contiguous() and tok.numel() == logits.shape[0] and (pos is None or (pos.dtype == torch.int64 and pos.is_cuda))
+    L.check(L.load().fsattn_argmax_advance(logits.data_ptr(), logits.stride(0), logits.shape[0], logits.shape[1], tok.data_ptr(),
+                                           _p(pos), _stream(logits)), "fsattn_argmax_advance")
+    return tok
+
+
 def swiglu(gu: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """out (..., f) = silu(gu[..., :f]) * gu[..., f:] for a fused gate/up projection gu (..., 2f) bf16, one pass."""
     _need_cuda(gu)

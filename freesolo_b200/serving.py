@@ -255,11 +255,13 @@ class GraphedDecoder:
         m = self.m
         x = self.x
         pdl = os.environ.get("FSATTN_PDL", "1") == "1"
-        x.copy_(m.tok_emb(self.tok).view(x.shape))
         if x.shape[0] > 8:
+            x.copy_(m.tok_emb(self.tok).view(x.shape))
             return self._trunk_step_batched()
         if self.fused_trunk:
+            x.copy_(m.tok_emb(self.tok).view(x.shape))
             return self._trunk_step_fused(pdl)
+        ops.embed_rows(self.tok, m.tok_emb.weight, x)
         for i, blk in enumerate(self.blocks):
             a = self.attn[i]
             wqkv, _ = a._ensure_qkv_cache()
@@ -270,8 +272,7 @@ class GraphedDecoder:
             ops.trunk_gemv(x, wgu, norm_w=blk.ln2.weight, eps=blk.ln2.eps, swiglu=True, out=self.act, pdl=pdl)
             ops.trunk_gemv(self.act, blk.ffn.w_down.weight, res=x, out=x, pdl=pdl)
         ops.trunk_gemv(x, m.lm_head.weight, norm_w=m.ln_final.weight, eps=m.ln_final.eps, out=self.logits, pdl=pdl)
-        self.tok.copy_(self.logits.argmax(dim=-1, keepdim=True))
-        self.pos_t.add_(1)
+        ops.argmax_advance(self.logits, self.tok, self.pos_t)
 
     def _trunk_step_fused(self, pdl: bool):
         """The same step with two launches per layer: the attention step, then ONE cooperative kernel for everything up to
@@ -302,11 +303,12 @@ class GraphedDecoder:
 
     def launches_per_step(self) -> int:
         """Kernels of this library per decode step (batch <= 8): the attention step and the fused rest of the layer (plus
-        the FS-B selection), the first QKV projection; without the fused kernel 5 per layer (6 with FS-B) + the head."""
+        the FS-B selection), the first QKV projection; without the fused kernel 5 per layer (6 with FS-B) + the head, the
+        embedding lookup and the argmax."""
         nL = len(self.blocks)
         if self.fused_trunk and self.x.shape[0] <= 8:
             return 2 * nL + 1 + (nL if (self.fsb or self.dense) else 0)
-        return 5 * nL + 1 + (nL if (self.fsb or self.dense) else 0)
+        return 5 * nL + 3 + (nL if (self.fsb or self.dense) else 0)       # + the embedding lookup and the argmax / advance
 
     def _trunk_step_batched(self):
         """More than 8 sequences per step: the projections are real GEMMs (weights read once for all rows), so they go to

@@ -325,6 +325,14 @@ FSATTN_API int fsattn_trunk_layer(const fsattn_trunk_layer_t* a, fsattn_stream_t
 FSATTN_API int fsattn_rms_norm(const void* x, int64_t x_stride, const void* w, float eps, void* out, int64_t out_stride, int64_t M,
                                int32_t d, fsattn_stream_t stream);
 
+/* The two ends of a greedy decode step (replace torch's embedding gather + copy and argmax + copy + add):
+ * x (B,d) bf16 = table[tok[b]] (table (vocab,d) bf16, tok int64; an id outside the table reads row 0), and
+ * tok[b] = argmax of logits (B,V) bf16 with row stride `stride` (lowest index on ties), *pos += 1 when pos is given.
+ * Both wait for their producer themselves (programmatic dependent launch). */
+FSATTN_API int fsattn_embed_rows(const int64_t* tok, const void* table, void* x, int32_t B, int32_t d, int64_t vocab, fsattn_stream_t stream);
+FSATTN_API int fsattn_argmax_advance(const void* logits, int64_t stride, int32_t B, int32_t V, int64_t* tok, int64_t* pos,
+                                     fsattn_stream_t stream);
+
 /* Elementwise SwiGLU gate of the prefill trunk: out (M, f) = silu(gu[:, :f]) * gu[:, f:] for the fused gate/up projection
  * gu (M, 2f) bf16 (row strides in elements). Replaces F.silu + the elementwise product of SwiGLU.forward
  * (experiments/scaling/model.py:111-145; trunk_triton.silu_mul on the reference's fused path), with the same two bf16

@@ -350,3 +350,26 @@ def test_host_facing_step_equals_the_device_step(dev):
         tok_host.copy_(out_host)
     assert getattr(b, "_host_graph", None) is not None
     assert torch.equal(torch.cat(got, dim=1), torch.cat(want, dim=1).cpu())
+
+
+def test_step_ends_embedding_lookup_and_argmax():
+    """The two ends of a decode step as kernels of this library: the embedding rows equal torch's lookup bit for bit; the
+    argmax equals torch.argmax, takes the lowest index on ties, handles a vocabulary that is not a multiple of eight, and
+    advances the position."""
+    from freesolo_b200 import ops
+    dev = torch.device("cuda:0")
+    g = torch.Generator().manual_seed(0)
+    table = torch.randn(1000, 256, generator=g).to(torch.bfloat16).to(dev)
+    tok = torch.tensor([[3], [999], [0], [17]], dtype=torch.int64, device=dev)
+    x = torch.zeros(4, 256, dtype=torch.bfloat16, device=dev)
+    ops.embed_rows(tok, table, x)
+    assert torch.equal(x, table[tok.view(-1)])
+    for V in (32000, 1003):
+        logits = torch.randn(3, V, generator=g).to(torch.bfloat16).to(dev)
+        logits[1, 77] = logits[1, 901] = 9.0              # a tie: the lower index wins
+        logits[2, V - 1] = 11.0                           # the last element (beyond the 16-byte chunks when V % 8 != 0)
+        out = torch.full((3, 1), -1, dtype=torch.int64, device=dev)
+        pos = torch.full((), 41, dtype=torch.int64, device=dev)
+        ops.argmax_advance(logits, out, pos)
+        want = logits.float().argmax(-1)
+        assert out.view(-1).tolist() == [int(want[0]), 77, V - 1] and int(pos) == 42
