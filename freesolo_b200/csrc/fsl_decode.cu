@@ -229,6 +229,7 @@ constexpr int WIN_STAGES = 2;                  // staged window: tiles of WIN_TI
 constexpr int WIN_TILE = 64;                   // rows per tile = one 8-row group for each of the 8 warps
 constexpr int WIN_CELLS = 40;                  // cells a window may touch: W / 32 + 2 (W <= 1216)
 constexpr int SC_ITERS = (MAXC + 31) / 32;     // scoring rounds: 32 candidates per round over the 8 warps
+static_assert(MAXC <= 224, "the candidates are ranked by the first seven warps, one thread each");
 
 template <int D>
 struct Smem {
@@ -806,7 +807,6 @@ __global__ void __launch_bounds__(NWARP * 32, MINB) fsl_decode_kernel(const fsat
     // ================= long-range branch + bookkeeping (rank 0) ==============================================================
     float lr_l = 0.0f;
     if (rank == 0) {
-        if (warp == NWARP - 1 && pos_ok) append_and_close<D>(st, hp, pos, k_in, v_in, lane);
         if (!ext && pool_blk != blk_start) {       // CTA-uniform, once per Bq tokens
             refresh_pool<D>(sm, st, hp, bh, blk_start, tid, pool_s, meta_s);
             for (int t = tid; t < C; t += blockDim.x) {
@@ -828,6 +828,10 @@ __global__ void __launch_bounds__(NWARP * 32, MINB) fsl_decode_kernel(const fsat
         } else
         // ---- scores: 8 lanes per candidate, mean keys from shared memory ---------------------------------------------------
         {
+            if (tid < FSATTN_MAX_KK) {             // slots no candidate ranks into stay empty
+                sm.selcell[tid] = -1; sm.selrow[tid] = -1;
+                if (a.sel_out != nullptr && tid < st.kk) a.sel_out[(int64_t)bh * st.kk + tid] = -1;
+            }
             float qv[F];
 #pragma unroll
             for (int j = 0; j < F; j++) qv[j] = sm.q_raw[s8 * F + j];
@@ -861,33 +865,24 @@ __global__ void __launch_bounds__(NWARP * 32, MINB) fsl_decode_kernel(const fsat
         __syncthreads();
         STAMP(0, 4);
 
-        // ---- top-kk by (score desc, slot asc): warp 0 ---------------------------------------------------------------------------------
-        if (warp == 0 && !ext) {
-            float sv[SC_ITERS];
-#pragma unroll
-            for (int j = 0; j < SC_ITERS; j++) { const int t = lane + 32 * j; sv[j] = (t < C) ? sm.score[t] : -INFINITY; }
-            for (int k = 0; k < st.kk; k++) {
-                float best = -INFINITY; int bslot = 0x7fffffff;
-#pragma unroll
-                for (int j = 0; j < SC_ITERS; j++) {
-                    const int t = lane + 32 * j;
-                    if (sv[j] > best) { best = sv[j]; bslot = t; }     // ascending t: ties keep the lower slot
-                }
-                // order-preserving map float -> uint, then two warp reductions: the best score, the lowest slot holding it
-                const uint32_t bits = __float_as_uint(best);
-                const uint32_t key = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
-                const uint32_t kmax = __reduce_max_sync(FS_FULL, key);
-                const int wslot = (int)__reduce_min_sync(FS_FULL, (key == kmax) ? (uint32_t)bslot : 0x7fffffffu);
-                int cell = -1, row = -1;
-                if (kmax > 0x007fffffu && wslot < C) {                 // kmax of -inf maps to 0x007fffff
-                    cell = sm.ccell[wslot]; row = sm.crow[wslot];
-#pragma unroll
-                    for (int j = 0; j < SC_ITERS; j++) if (lane + 32 * j == wslot) sv[j] = -INFINITY;
-                }
-                if (lane == 0) {
-                    sm.selcell[k] = cell; sm.selrow[k] = (cell >= 0) ? row : -1;
-                    if (a.sel_out != nullptr) a.sel_out[(int64_t)bh * st.kk + k] = cell;
-                }
+        // ---- the new row joins the store (and closes its cell) in the one warp that has no candidate to rank: nothing in this
+        // step reads it, so it stays off the path from the query to the output ----------------------------------------------------
+        if (warp == NWARP - 1 && pos_ok) append_and_close<D>(st, hp, pos, k_in, v_in, lane);
+        // ---- top-kk by (score desc, slot asc): every candidate counts the candidates ahead of it (the scores are broadcast
+        // reads of shared memory); the kk with the fewest are the selection, in rank order -------------------------------------------
+        if (!ext && tid < C) {
+            const float sc = sm.score[tid];
+            int ahead = 0;
+#pragma unroll 8
+            for (int u = 0; u < C; u++) {
+                const float su = sm.score[u];
+                ahead += (su > sc || (su == sc && u < tid)) ? 1 : 0;
+            }
+            if (ahead < st.kk) {
+                const int cell = sm.ccell[tid];
+                sm.selcell[ahead] = cell;
+                sm.selrow[ahead] = (cell >= 0) ? sm.crow[tid] : -1;
+                if (a.sel_out != nullptr) a.sel_out[(int64_t)bh * st.kk + ahead] = cell;
             }
         }
         __syncthreads();
