@@ -96,8 +96,8 @@ template <int D>
 struct RowFlight {
     RawRow<D> k, v;
     uint2 c[RowL<D>::NW], s[RowL<D>::NW];
-    float ksc, vsc;
-    bool valid, i8;
+    unsigned short ksc, vsc;        // the cell's scales as bf16 bits: converted where they are used, not where they are loaded (a
+    bool valid, i8;                 // dependent instruction right after the load would hold up every later load: in-order issue)
 };
 
 template <int D, bool ROPE>
@@ -105,8 +105,11 @@ __device__ __forceinline__ void row_issue(RowFlight<D>& f, const void* krow, con
                                           bool valid, bool i8, const bf16* cosr, const bf16* sinr, int sub) {
     using L = RowL<D>;
     f.valid = valid; f.i8 = i8;
-    f.ksc = 1.0f; f.vsc = 1.0f;
-    if (valid && i8) { f.ksc = __bfloat162float(*ksc_p); f.vsc = __bfloat162float(*vsc_p); }
+    f.ksc = 0x3f80; f.vsc = 0x3f80;             // 1.0 in bf16
+    if (valid && i8) {
+        f.ksc = *reinterpret_cast<const unsigned short*>(ksc_p);
+        f.vsc = *reinterpret_cast<const unsigned short*>(vsc_p);
+    }
     if (i8) { raw_load<D, true>(f.k, krow, sub, valid); raw_load<D, true>(f.v, vrow, sub, valid); }
     else { raw_load<D, false>(f.k, krow, sub, valid); raw_load<D, false>(f.v, vrow, sub, valid); }
     if (ROPE) {
@@ -123,7 +126,7 @@ template <int D, bool ROPE>
 __device__ __forceinline__ void row_consume(Part<D>& P, const RowFlight<D>& f, const float* qlo, const float* qhi, float scale) {
     using L = RowL<D>;
     float klo[L::DPL], khi[L::DPL];
-    if (f.i8) raw_floats<D, true>(f.k, f.ksc, klo, khi); else raw_floats<D, false>(f.k, 1.0f, klo, khi);
+    if (f.i8) raw_floats<D, true>(f.k, __uint_as_float((uint32_t)f.ksc << 16), klo, khi); else raw_floats<D, false>(f.k, 1.0f, klo, khi);
     float dot = 0.0f;
     if (ROPE) {
         float c[L::DPL], s[L::DPL];
@@ -147,7 +150,7 @@ __device__ __forceinline__ void row_consume(Part<D>& P, const RowFlight<D>& f, c
     if (!f.valid) return;   // uniform within the 4-lane group; no shuffles below
     const float sc = dot * scale;
     float vlo[L::DPL], vhi[L::DPL];
-    if (f.i8) raw_floats<D, true>(f.v, f.vsc, vlo, vhi); else raw_floats<D, false>(f.v, 1.0f, vlo, vhi);
+    if (f.i8) raw_floats<D, true>(f.v, __uint_as_float((uint32_t)f.vsc << 16), vlo, vhi); else raw_floats<D, false>(f.v, 1.0f, vlo, vhi);
     const float m_new = fmaxf(P.m, sc);
     const float alpha = (P.m == -INFINITY) ? 0.0f : __expf(P.m - m_new);
     const float p = __expf(sc - m_new);
@@ -251,7 +254,7 @@ struct Smem {
     unsigned long long pool_bar;   // mbarrier of the pool's bulk copy
     int pool_timeout;
     // staged window (many sequences per step): per-cell scales and row bases of the window's cells, stage barriers
-    float win_ks[WIN_CELLS], win_vs[WIN_CELLS];
+    unsigned short win_ks[WIN_CELLS], win_vs[WIN_CELLS];      // bf16 bits
     int win_base[WIN_CELLS];
     unsigned long long stage_bar[WIN_STAGES];
 };
@@ -452,7 +455,7 @@ __device__ __forceinline__ void staged_prologue(Smem<D>& sm, unsigned char* stag
     const int ncq = (int)(w.nq / FSATTN_CELL);          // completed cells: [0, ncq)
     if (tid < WIN_CELLS) {
         const int cell = c0 + tid;
-        float ks = 1.0f, vs = 1.0f;
+        unsigned short ks = 0x3f80, vs = 0x3f80;         // 1.0 in bf16
         int base = 0;
         if (w.pos_ok && cell < ncq) {
             base = cell;
@@ -460,7 +463,10 @@ __device__ __forceinline__ void staged_prologue(Smem<D>& sm, unsigned char* stag
                 base = hp.slot_of[cell];
                 if (base < 0) { atomicAdd(st.status + FSATTN_ST_POOL_NO_SLOT, 1); base = -1; }
             }
-            if (base >= 0) { ks = __bfloat162float(hp.ks[base]); vs = __bfloat162float(hp.vs[base]); }
+            if (base >= 0) {
+                ks = *reinterpret_cast<const unsigned short*>(hp.ks + base);
+                vs = *reinterpret_cast<const unsigned short*>(hp.vs + base);
+            }
         }
         sm.win_ks[tid] = ks; sm.win_vs[tid] = vs; sm.win_base[tid] = base;
     }
@@ -519,7 +525,7 @@ __device__ __forceinline__ void window_finish_staged(Smem<D>& sm, unsigned char*
         } else {
             const void* kp = valid ? (const void*)(hp.khot + (r - w.nq) * D) : nullptr;
             const void* vp = valid ? (const void*)(hp.vhot + (r - w.nq) * D) : nullptr;
-            f.valid = valid; f.i8 = false; f.ksc = 1.0f; f.vsc = 1.0f;
+            f.valid = valid; f.i8 = false; f.ksc = 0x3f80; f.vsc = 0x3f80;
             raw_load<D, false>(f.k, kp, sub, valid);
             raw_load<D, false>(f.v, vp, sub, valid);
         }
@@ -835,7 +841,8 @@ __global__ void __launch_bounds__(NWARP * 32, MINB) fsl_decode_kernel(const fsat
             float qv[F];
 #pragma unroll
             for (int j = 0; j < F; j++) qv[j] = sm.q_raw[s8 * F + j];
-            for (int t0 = warp * 4; t0 < C; t0 += NWARP * 4) {
+            // (the last warp appends the new row instead, below)
+            for (int t0 = warp * 4; t0 < C && warp < NWARP - 1; t0 += (NWARP - 1) * 4) {
                 const int t = t0 + (lane >> 3);
                 int4 mt = make_int4(-1, 0, 0, 0);
                 if (t < C) mt = meta_s[t];
@@ -862,12 +869,15 @@ __global__ void __launch_bounds__(NWARP * 32, MINB) fsl_decode_kernel(const fsat
                 }
             }
         }
-        __syncthreads();
+        // ---- the new row joins the store (and closes its cell) in the last warp, which takes no part in scoring and ranking and
+        // skips their barrier: nothing in this step reads the row, so it stays off the path from the query to the output -------------
+        if (warp == NWARP - 1) {
+            if (pos_ok) append_and_close<D>(st, hp, pos, k_in, v_in, lane);
+        } else {
+            asm volatile("bar.sync 1, %0;" ::"n"((NWARP - 1) * 32) : "memory");        // the scores of warps 0 .. NWARP-2 are complete
+        }
         STAMP(0, 4);
 
-        // ---- the new row joins the store (and closes its cell) in the one warp that has no candidate to rank: nothing in this
-        // step reads it, so it stays off the path from the query to the output ----------------------------------------------------
-        if (warp == NWARP - 1 && pos_ok) append_and_close<D>(st, hp, pos, k_in, v_in, lane);
         // ---- top-kk by (score desc, slot asc): every candidate counts the candidates ahead of it (the scores are broadcast
         // reads of shared memory); the kk with the fewest are the selection, in rank order -------------------------------------------
         if (!ext && tid < C) {
