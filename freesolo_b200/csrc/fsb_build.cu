@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
                 am = fmaxf(am, __shfl_xor_sync(FS_FULL, am, o));
                 pm = min(pm, __shfl_xor_sync(FS_FULL, pm, o));
             }
-            if (lane == 0) FAR[g] = bi;
+            if (lane == 0 && l < k) FAR[g] = bi;      // leaves are not split: FAR holds one entry per INNER node (n/2)
             float mu[NPL], er[NPL];
             if (m >= 2) {
                 fsb_load_row<D>(Y + (int64_t)g * h * D, lane, mu);
