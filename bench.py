@@ -536,26 +536,48 @@ def run_head_sharded(args, dev, K, Wm, rank, world, dist):
     n_heads = model.blocks[0].attn.fsattn.n_heads
     shard_model_heads(model, rank, world)
     ids = torch.randint(0, model.vocab_size, (1, ctx), generator=torch.Generator().manual_seed(4321 + ctx))
-    gd = GraphedDecoder(model, ids, Lmax=ctx + Wm + K + 40, device=dev, kv=args.kv)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    gd.prefill()
-    e1.record()
-    torch.cuda.synchronize()
-    pms = e0.elapsed_time(e1)
-    dist.barrier()
-    ms = timed_decode(gd, K, Wm)
-    t = torch.tensor([ms, pms], dtype=torch.float64, device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, pms = t.tolist()
+    import gc
+
+    def one(peer: bool):
+        """prefill + K timed steps with the exchange over peer memory (this library's kernel) or as NCCL all-gathers"""
+        os.environ["FSATTN_PEER_GATHER"] = "1" if peer else "0"
+        try:
+            gd = GraphedDecoder(model, ids, Lmax=ctx + Wm + K + 40, device=dev, kv=args.kv)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            gd.prefill()
+            e1.record()
+            torch.cuda.synchronize()
+            pms = e0.elapsed_time(e1)
+            dist.barrier()
+            ms = timed_decode(gd, K, Wm)
+            t = torch.tensor([ms, pms, float(gd.peer_status())], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            faults = list(gd.kv_faults())
+            used_peer = gd.peer is not None
+            # a graph that captured collectives keeps the communicator busy: it goes before the process group does
+            gd.graph = None
+            if gd.peer is not None:
+                gd.peer.close()
+            del gd
+            gc.collect()
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
+            return t.tolist() + [faults, used_peer]
+        finally:
+            del os.environ["FSATTN_PEER_GATHER"]
+
+    ms, pms, status, faults, used_peer = one(True)
+    ms_nccl, _, _, _, _ = one(False)
     out = {"workload": f"FS-L {args.model}, ONE sequence of {ctx} tokens, {n_heads} heads split over "
                        f"{world} GPUs, exchange of the head outputs once per layer, {K} graph-replayed decode steps",
            "scaling": "strong", "decode_tok_s": K / (ms * 1e-3), "decode_ms_per_step": ms / K,
-           "prefill_ktok_s": ctx / pms, "prefill_ms": pms, "prefill_note": "one cold run", "kv_faults": list(gd.kv_faults())}
-    # a graph that captured collectives keeps the communicator busy: it goes before the process group does
-    gd.graph = None
-    del gd, model
-    import gc
+           "exchange": ("one launch of this library per rank and layer: stores + flag into the peers' memory, bounded wait"
+                        if used_peer else "NCCL all-gather"),
+           "peer_wait_status": int(status),
+           "decode_tok_s_nccl_allgather": K / (ms_nccl * 1e-3), "decode_ms_per_step_nccl_allgather": ms_nccl / K,
+           "prefill_ktok_s": ctx / pms, "prefill_ms": pms, "prefill_note": "one cold run", "kv_faults": faults}
+    del model
     gc.collect()
     torch.cuda.synchronize()
     torch.cuda.empty_cache()

@@ -193,10 +193,19 @@ class FsbSelect(C.Structure):
 
 FSB_SPINE_MAX = 20
 FSB_MAX_MCAP = 16384
+PEER_MAX = 8
+PEER_HANDLE_BYTES = 64
+
+
+class PeerGather(C.Structure):
+    _fields_ = [("y_local", vp), ("y_out", vp), ("ll_dst", vp * PEER_MAX), ("epoch", vp), ("status", vp),
+                ("B", i32), ("dl", i32), ("rank", i32), ("world", i32), ("slot", i32), ("pdl", i32), ("timeout_ns", i64)]
+
 
 EXTRA_STRUCTS = {"fsattn_fs_dense_select_t": FsDenseSelect, "fsattn_fs_dense_decode_select_t": FsDenseDecodeSelect,
                  "fsattn_trunk_gemv_t": TrunkGemv, "fsattn_trunk_layer_t": TrunkLayer, "fsattn_fsb_forest_t": FsbForest, "fsattn_fsb_select_t": FsbSelect,
-                 "fsattn_linear_merge_t": LinearMerge, "fsattn_linear_select_t": LinearSelect}
+                 "fsattn_linear_merge_t": LinearMerge, "fsattn_linear_select_t": LinearSelect,
+                 "fsattn_peer_gather_t": PeerGather}
 
 # every exported symbol of include/fsattn_b200.h with its argument struct (None = no struct argument)
 ENTRY_POINTS = {
@@ -228,6 +237,13 @@ ENTRY_POINTS = {
     "fsattn_linear_select": LinearSelect,
     "fsattn_fsb_spines": ([C.POINTER(FsbForest), i32, i32, C.POINTER(vp), C.POINTER(vp), C.POINTER(i32), vp], C.c_int),
     "fsattn_fsb_select": FsbSelect,
+    "fsattn_peer_gather": PeerGather,
+    "fsattn_peer_ll_bytes": ([i32, i32, i32, i32], i64),
+    "fsattn_peer_alloc": ([i64, C.POINTER(vp)], C.c_int),
+    "fsattn_peer_free": ([vp], C.c_int),
+    "fsattn_peer_export": ([vp, C.c_char_p], C.c_int),
+    "fsattn_peer_open": ([C.c_char_p, C.POINTER(vp)], C.c_int),
+    "fsattn_peer_close": ([vp], C.c_int),
 }
 
 _lib = None

@@ -7,6 +7,10 @@ slices of the per-head parameters. The single exchange step of a layer is an all
 same residual stream and no second collective is needed. (The reference has no multi-GPU path; this follows the partition
 its per-head data layout allows.)
 
+In the captured decode step that exchange is one small kernel of this library per rank and layer over peer memory
+(`PeerExchange`: stores + a flag into slabs the ranks opened from one another through CUDA IPC, a bounded wait on the rank's
+own flags); the prefill, and a decoder built with FSATTN_PEER_GATHER=0, use the NCCL all-gather.
+
 Batch sharding needs no code here: sequences are independent, each rank runs its own sequences with a full replica and the
 host gathers the sampled tokens.
 """
@@ -58,6 +62,104 @@ class HeadShard:
         return y
 
 
+class _RawBytes:
+    """A device address as something torch.as_tensor can wrap (the CUDA array interface)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 2}
+
+
+class PeerExchange:
+    """The per-layer exchange of head outputs of a decode step over peer memory (csrc/peer_gather.cu).
+
+    One slab per rank, allocated by the library with cudaMalloc and zeroed: the receive area (8-byte words of data + flag,
+    per slot, call parity and source rank), n_slots call counters, one status word. The ranks swap the slabs' IPC handles
+    once (a collective over `group`) and open them; after that a layer's exchange is one launch per rank and no library
+    call. `status()` is non-zero if a wait ever ran out (bit p: rank p's rows did not arrive within `timeout_ms`)."""
+
+    def __init__(self, shard: HeadShard, B: int, n_slots: int, device, group=None, timeout_ms: float = 1000.0, exchange=None):
+        import ctypes as C
+        from . import lib as L
+        self.shard, self.B, self.n_slots, self.group = shard, int(B), int(n_slots), group
+        self.dev = torch.device(device)
+        self.timeout_ns = int(timeout_ms * 1e6)
+        lib = L.load()
+        up = lambda n: (n + 255) // 256 * 256
+        self.off_epoch = up(int(lib.fsattn_peer_ll_bytes(self.B, shard.dl, shard.world, self.n_slots)))
+        self.off_status = self.off_epoch + up(self.n_slots * 4)
+        self.nbytes = self.off_status + 256
+        with torch.cuda.device(self.dev):
+            ptr = C.c_void_p()
+            L.check(lib.fsattn_peer_alloc(self.nbytes, C.byref(ptr)), "fsattn_peer_alloc")
+            self.ptr = int(ptr.value)
+            h = C.create_string_buffer(L.PEER_HANDLE_BYTES)
+            L.check(lib.fsattn_peer_export(self.ptr, h), "fsattn_peer_export")
+            mine = bytes(h.raw)
+            if exchange is not None:                  # a caller's own channel: the handles of all ranks in rank order
+                handles = exchange(mine)
+            elif shard.world == 1:
+                handles = [mine]
+            else:
+                handles = [None] * shard.world
+                dist.all_gather_object(handles, mine, group=group)
+            self.base, self._opened = [], []
+            for r, hr in enumerate(handles):
+                if r == shard.rank:
+                    self.base.append(self.ptr)
+                    continue
+                q = C.c_void_p()
+                L.check(lib.fsattn_peer_open(hr, C.byref(q)), "fsattn_peer_open")
+                self.base.append(int(q.value))
+                self._opened.append(int(q.value))
+            raw = torch.as_tensor(_RawBytes(self.ptr, self.nbytes), device=self.dev)
+        self._raw = raw
+        self.epoch = raw[self.off_epoch:self.off_epoch + self.n_slots * 4].view(torch.int32)
+        self._status = raw[self.off_status:self.off_status + 4].view(torch.int32)
+        self.y = torch.zeros(self.B, shard.d, dtype=torch.bfloat16, device=self.dev)      # the gathered rows W_o reads
+        a = L.PeerGather()
+        for r, b in enumerate(self.base):
+            a.ll_dst[r] = b
+        a.y_out = self.y.data_ptr()
+        a.epoch, a.status = self.ptr + self.off_epoch, self.ptr + self.off_status
+        a.B, a.dl, a.rank, a.world = self.B, shard.dl, shard.rank, shard.world
+        a.timeout_ns = self.timeout_ns
+        self._args = a
+
+    def gather(self, y_local: torch.Tensor, slot: int, pdl: bool = True) -> torch.Tensor:
+        """y_local (B, dl) bf16 -> the gathered rows (B, d): valid when the launch has completed with status 0."""
+        import ctypes as C
+        from . import lib as L
+        from .ops import _stream
+        if not (y_local.is_cuda and y_local.dtype == torch.bfloat16 and y_local.is_contiguous()
+                and y_local.numel() == self.B * self.shard.dl and 0 <= slot < self.n_slots):
+            raise ValueError("PeerExchange.gather: y_local must be a contiguous (B, dl) bf16 CUDA tensor and slot < n_slots")
+        a = self._args
+        a.y_local = y_local.data_ptr()
+        a.slot, a.pdl = slot, int(pdl)
+        L.check(L.load().fsattn_peer_gather(C.byref(a), _stream(y_local)), "fsattn_peer_gather")
+        return self.y
+
+    def status(self) -> int:
+        return int(self._status.item())
+
+    def close(self):
+        """Unmap the peers' slabs, then (after every rank has done so) free this rank's. A collective over `group`."""
+        from . import lib as L
+        if self.ptr is None:
+            return
+        torch.cuda.synchronize(self.dev)
+        lib = L.load()
+        with torch.cuda.device(self.dev):
+            for q in self._opened:
+                lib.fsattn_peer_close(q)
+            self._opened = []
+            if self.shard.world > 1 and dist.is_initialized():
+                dist.barrier(group=self.group)
+            self.epoch = self._status = self._raw = None
+            lib.fsattn_peer_free(self.ptr)
+        self.ptr = None
+
+
 class ShardedFSAttn(nn.Module):
     """An FSAttn layer cut to this rank's heads. The kernels run through an inner FSAttn of H/g heads (whose own projection
     weights are unused); this module owns the local rows of the fused QKV weight and the replicated W_o."""
@@ -97,6 +199,9 @@ class ShardedFSAttn(nn.Module):
     def graph_decode_attn(self, qkv, buf, y=None, pdl=True):
         """qkv (B, 3 dl) of this rank's heads -> W_o's input (B, d) after the all-gather (captured with the step)."""
         y_local = self.inner.graph_decode_attn(qkv, buf, pdl=pdl)
+        px = buf.get("peer")
+        if px is not None:                          # one launch over peer memory; returns the slot's own gathered buffer
+            return px.gather(y_local.view(y_local.shape[0], -1), buf["peer_slot"], pdl=pdl)
         return self.shard.gather(y_local, self.group, out=y)
 
     @torch.no_grad()

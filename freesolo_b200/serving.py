@@ -229,6 +229,25 @@ class GraphedDecoder:
         self.pos = P0
         self.pos_t = torch.full((), P0, dtype=torch.int64, device=self.dev)
         self.bufs = [{"pos_t": self.pos_t, "cache": c} for c in self.cache]
+        # head shards: the per-layer exchange of head outputs as one launch over peer memory (parallel.PeerExchange; a
+        # collective set-up over the shard's group); FSATTN_PEER_GATHER=0 keeps the NCCL all-gather in the step
+        self.peer = None
+        shard = getattr(self.attn[0], "shard", None)
+        if shard is not None and shard.world > 1 and os.environ.get("FSATTN_PEER_GATHER", "1") == "1":
+            import torch.distributed as dist
+            from .parallel import PeerExchange
+            try:
+                self.peer = PeerExchange(shard, B, len(self.blocks), self.dev, group=self.attn[0].group)
+            except RuntimeError as e:                 # e.g. the box does not let the ranks open one another's memory
+                self.peer_error = str(e)
+            # the ranks agree: one that could not map its peers sends every rank back to the library all-gather
+            ok = torch.tensor([int(self.peer is not None)], device=self.dev)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.attn[0].group)
+            if int(ok.item()) == 0:
+                self.peer = None
+            else:
+                for i, b in enumerate(self.bufs):
+                    b["peer"], b["peer_slot"] = self.peer, i
         for blk in self.blocks:
             blk.ffn._ensure_gu_cache()
         d, f = m.d_model, self.blocks[0].ffn.w_gate.weight.shape[0]
@@ -266,8 +285,8 @@ class GraphedDecoder:
             a = self.attn[i]
             wqkv, _ = a._ensure_qkv_cache()
             ops.trunk_gemv(x, wqkv, norm_w=blk.ln1.weight, eps=blk.ln1.eps, out=self.qkv, pdl=pdl)
-            a.graph_decode_attn(self.qkv, self.bufs[i], y=self.y, pdl=pdl)
-            ops.trunk_gemv(self.y, a.W_o.weight, res=x, out=x, pdl=pdl)
+            y = a.graph_decode_attn(self.qkv, self.bufs[i], y=self.y, pdl=pdl)      # self.y, or a head shard's gathered buffer
+            ops.trunk_gemv(y, a.W_o.weight, res=x, out=x, pdl=pdl)
             wgu, _ = blk.ffn._ensure_gu_cache()
             ops.trunk_gemv(x, wgu, norm_w=blk.ln2.weight, eps=blk.ln2.eps, swiglu=True, out=self.act, pdl=pdl)
             ops.trunk_gemv(self.act, blk.ffn.w_down.weight, res=x, out=x, pdl=pdl)
@@ -286,16 +305,20 @@ class GraphedDecoder:
         ops.trunk_gemv(x, a0._ensure_qkv_cache()[0], norm_w=self.blocks[0].ln1.weight, eps=self.blocks[0].ln1.eps, out=self.qkv, pdl=pdl)
         for i, blk in enumerate(self.blocks):
             a = self.attn[i]
-            a.graph_decode_attn(self.qkv, self.bufs[i], y=self.y, pdl=pdl)
+            y = a.graph_decode_attn(self.qkv, self.bufs[i], y=self.y, pdl=pdl)
             if i + 1 < nL:
                 nb = self.blocks[i + 1]
                 nxt = dict(norm_next_w=nb.ln1.weight, eps_next=nb.ln1.eps, w_next=self.attn[i + 1]._ensure_qkv_cache()[0], out_next=self.qkv)
             else:
                 nxt = dict(norm_next_w=m.ln_final.weight, eps_next=m.ln_final.eps, w_next=m.lm_head.weight, out_next=self.logits)
-            ops.trunk_layer(x, self.y, a.W_o.weight, blk.ln2.weight, blk.ln2.eps, blk.ffn._ensure_gu_cache()[0], self.act,
+            ops.trunk_layer(x, y, a.W_o.weight, blk.ln2.weight, blk.ln2.eps, blk.ffn._ensure_gu_cache()[0], self.act,
                             blk.ffn.w_down.weight, self.tl_bar[i], self.tl_status, pdl=pdl, **nxt)
         self.tok.copy_(self.logits.argmax(dim=-1, keepdim=True))
         self.pos_t.add_(1)
+
+    def peer_status(self) -> int:
+        """Head shards: non-zero if a wait for a peer's head outputs ever ran out (bit p = rank p; one host sync)."""
+        return 0 if self.peer is None else self.peer.status()
 
     def trunk_status(self) -> int:
         """Non-zero if a grid barrier of the fused layer kernel ever ran out of its bound (one host sync)."""
@@ -319,8 +342,8 @@ class GraphedDecoder:
             a = self.attn[i]
             wqkv, _ = a._ensure_qkv_cache()
             torch.matmul(blk.ln1(x), wqkv.t(), out=self.qkv)
-            a.graph_decode_attn(self.qkv, self.bufs[i], y=self.y, pdl=False)
-            x.add_(F.linear(self.y, a.W_o.weight))
+            y = a.graph_decode_attn(self.qkv, self.bufs[i], y=self.y, pdl=False)
+            x.add_(F.linear(y, a.W_o.weight))
             wgu, f = blk.ffn._ensure_gu_cache()
             gu = F.linear(blk.ln2(x), wgu)
             x.add_(F.linear(F.silu(gu[:, :f]) * gu[:, f:], blk.ffn.w_down.weight))

@@ -333,6 +333,41 @@ FSATTN_API int fsattn_embed_rows(const int64_t* tok, const void* table, void* x,
 FSATTN_API int fsattn_argmax_advance(const void* logits, int64_t stride, int32_t B, int32_t V, int64_t* tok, int64_t* pos,
                                      fsattn_stream_t stream);
 
+/* ---- head-sharded decode: the per-layer exchange of head outputs over peer memory -------------------------------------
+ * The reference has no multi-GPU path; its per-head data layout (src/fsattn/attention.py:1450-1491: one decode call per
+ * layer over (B, H) rows) is what lets the heads be split over the GPUs of a box, with ONE exchange per layer in front of
+ * W_o. This entry point is that exchange as a single small kernel per rank instead of a library all-gather.
+ *
+ * Every rank owns a slab (fsattn_peer_alloc: cudaMalloc, zeroed), exports it once (fsattn_peer_export: a 64-byte CUDA IPC
+ * handle, sent to the peers by any host channel) and opens the peers' slabs (fsattn_peer_open: addresses valid on the
+ * calling device). ll_dst[p] is rank p's receive area of fsattn_peer_ll_bytes(B, dl, world, n_slots) bytes, 8-byte words
+ * {4 bytes of data, 4 bytes of flag} laid out [slot][call parity][source rank][B dl / 2]. A call takes its call count e =
+ * epoch[slot] + 1 (epoch: n_slots int32, local, zero at start), stores its rows y_local (B, dl) bf16 with the flag e into
+ * ll_dst[p][slot][e & 1][rank] of every peer p and into the columns [rank dl, (rank+1) dl) of its own y_out (B, world dl)
+ * bf16, then polls ll_dst[rank][slot][e & 1][p] for every peer p until every word carries the flag e and writes the data
+ * into p's columns of y_out. The polls are bounded by timeout_ns of the global timer: when one runs out bit p of *status
+ * is set and the kernel returns (y_out is then incomplete). Stores go to peer memory; no load does, and nothing is
+ * multicast. Every rank must make the same sequence of calls (slot, B, dl). */
+#define FSATTN_PEER_MAX 8
+#define FSATTN_PEER_HANDLE_BYTES 64
+typedef struct {
+    const void* y_local;
+    void* y_out;
+    void* ll_dst[FSATTN_PEER_MAX];
+    int32_t* epoch;
+    int32_t* status;
+    int32_t B, dl, rank, world, slot;
+    int32_t pdl;                 /* 1: launched as a programmatic dependent launch (the kernel waits for its producer itself) */
+    int64_t timeout_ns;          /* (0, 2e9] */
+} fsattn_peer_gather_t;
+FSATTN_API int fsattn_peer_gather(const fsattn_peer_gather_t* g, fsattn_stream_t stream);
+FSATTN_API int64_t fsattn_peer_ll_bytes(int32_t B, int32_t dl, int32_t world, int32_t n_slots);
+FSATTN_API int fsattn_peer_alloc(int64_t bytes, void** ptr);
+FSATTN_API int fsattn_peer_free(void* ptr);
+FSATTN_API int fsattn_peer_export(void* ptr, uint8_t* handle /* FSATTN_PEER_HANDLE_BYTES */);
+FSATTN_API int fsattn_peer_open(const uint8_t* handle, void** ptr);
+FSATTN_API int fsattn_peer_close(void* ptr);
+
 /* Elementwise SwiGLU gate of the prefill trunk: out (M, f) = silu(gu[:, :f]) * gu[:, f:] for the fused gate/up projection
  * gu (M, 2f) bf16 (row strides in elements). Replaces F.silu + the elementwise product of SwiGLU.forward
  * (experiments/scaling/model.py:111-145; trunk_triton.silu_mul on the reference's fused path), with the same two bf16

@@ -39,11 +39,20 @@ def main():
             if i == 0:
                 logits0 = gd.logits.float().clone()
         assert gd.graph is not None and gd.kv_faults() == (0, 0, 0)
+        assert gd.peer_status() == 0, "a wait for a peer's head outputs ran out"
+        run.used_peer = gd.peer is not None
         return torch.cat(toks, dim=1), logits0
 
     full_toks, full_logits = run(build())
     m2 = shard_model_heads(build(), rank, world)
     sh_toks, sh_logits = run(m2)
+    assert run.used_peer, "the head shards' exchange did not run over peer memory"
+    # the same step with the library all-gather instead of the peer-memory kernel: identical bits
+    os.environ["FSATTN_PEER_GATHER"] = "0"
+    nccl_toks, nccl_logits = run(m2)
+    del os.environ["FSATTN_PEER_GATHER"]
+    assert not run.used_peer
+    assert torch.equal(nccl_toks, sh_toks) and torch.equal(nccl_logits, sh_logits), "peer exchange and all-gather disagree"
     d = (sh_logits - full_logits).abs().max().item()
     agree = (sh_toks == full_toks).float().mean().item()
     # every rank must hold the same tokens (the residual stream is replicated)
