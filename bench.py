@@ -280,6 +280,40 @@ def timed_prefill(make_decoder, reps: int = 3):
 PREFILL_PEAK_GIB = [None]
 
 
+def timed_graph_prefill(model, ids, dev, reps: int = 3):
+    """The reference's graphed prefill protocol (experiments/scaling/bench_efficiency.py:201-229): the whole prefill of this
+    shape captured once (`GraphedPrefiller`, `retain_kv=False`: chunk statistics, selection, readout, last-token logits; no
+    KV store fill), one untimed replay, then the median of `reps` replays between CUDA events."""
+    from freesolo_b200.serving import GraphedPrefiller
+    import gc
+    B, L = ids.shape
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    torch.cuda.reset_peak_memory_stats()
+    gp = GraphedPrefiller(model, L, B=B, device=dev, tail_tokens=min(64, L), retain_kv=False)
+    ids = ids.to(dev)
+    gp.capture(ids)
+    gp.run(ids)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        gp.run(ids)
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    peak = torch.cuda.max_memory_allocated() / 2 ** 30
+    ms = sorted(times)[len(times) // 2]
+    gp.graph = None
+    del gp
+    gc.collect()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return {"ktok_s": B * L / ms, "ms": ms, "runs_ms": times, "peak_gib": peak,
+            "note": "whole prefill as one CUDA-graph replay, retain_kv=False (the reference's prefill benchmark protocol)"}
+
+
 def timed_decode(gd, K, Wm):
     """Wm untimed steps (the graph is captured there), then K graph replays between two CUDA events. Returns ms."""
     for _ in range(Wm):
@@ -336,6 +370,9 @@ def context_leg(model, variant, ctx, dev, K, Wm, peak):
            "vs_published_decode": _pub(f"{variant}_decode_tps", ctx, tps), "kv_faults": list(gd.kv_faults())}
     del gd
     torch.cuda.empty_cache()
+    g = timed_graph_prefill(model, ids, dev, reps=3)
+    out["prefill_graph_ktok_s"] = g["ktok_s"]
+    out["vs_published_prefill_graph"] = _pub(f"{variant}_prefill_ktoks", ctx, g["ktok_s"])
     return out
 
 
@@ -405,6 +442,10 @@ def run_fsb_section(args, dev, K, Wm, peak, peak_kind):
            "kv_faults": list(gd.kv_faults())}
     del gd
     torch.cuda.empty_cache()
+    if args.batch == 1:
+        g = timed_graph_prefill(model, ids, dev)
+        g["vs_published"] = _pub("fsb_prefill_ktoks", ctx, g["ktok_s"])
+        out["prefill_graphed"] = g
     if not args.no_contexts:
         out["contexts"] = [context_leg(model, "fsb", c, dev, 32, Wm, peak) for c in (4096, 16384, 65536) if c < ctx]
     del model
@@ -479,7 +520,12 @@ def run_dense_section(args, dev, K, Wm, peak, peak_kind):
            "roofline": {"what": "whole decode step", "bound": "hbm", "step_bytes": sb, "achieved": sb / (ms / K * 1e-3) / 1e9, "peak": peak,
                         "unit": "GB/s", "frac": sb / (ms / K * 1e-3) / 1e9 / peak, "peak_kind": peak_kind},
            "gpu_launches": K * gd.launches_per_step(), "kv_faults": list(gd.kv_faults())}
-    del gd, model
+    del gd
+    torch.cuda.empty_cache()
+    g = timed_graph_prefill(model, ids, dev)
+    g["vs_published"] = _pub("dense_prefill_ktoks", ctx, g["ktok_s"])
+    out["prefill_graphed"] = g
+    del model
     torch.cuda.empty_cache()
     return out
 
@@ -766,6 +812,10 @@ def run_ours(args):
         line["window_roofline"] = time_window_kernel(gd.attn_core[0], dev, ctx)
     del gd
     torch.cuda.empty_cache()
+    if world == 1 and B == 1:
+        g = timed_graph_prefill(model, ids, dev)
+        g["vs_published"] = _pub("fsl_prefill_ktoks", ctx, g["ktok_s"])
+        line["prefill"]["graphed"] = g
     if world == 1 and args.model == "340m" and B == 1 and not args.no_contexts:
         line["contexts"] = [context_leg(model, "fsl", c, dev, 32, Wm, hbm_peak) for c in (4096, 16384, 65536) if c < ctx]
     del model

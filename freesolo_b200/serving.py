@@ -447,6 +447,77 @@ class GraphedDecoder:
         return sum(c.state.nbytes() for c in self.cache)
 
 
+class GraphedPrefiller:
+    """Whole-forward CUDA-graph prefill at a fixed (B, L) shape (experiments/scaling/decode_graph.py:623-709): the token
+    input, every layer's cache buffers and the outputs are static, one eager pass allocates the cache state and opts the
+    kernels into their shared-memory sizes, then the whole prefill - embedding, every block with its cache, final norm,
+    last-token logits - is captured once and replayed for every prompt of that shape. At short contexts the prefill is a
+    chain of short launches, and the replay removes the host's share of it; the kernels and their results are the eager
+    path's. `retain_kv=False` is the reference's prefill-benchmark protocol (chunk statistics only, no KV store fill).
+    kv: None keeps the caches' default store, "int8" / "bounded" select one before the first pass."""
+
+    def __init__(self, model, L: int, B: int = 1, device="cuda", dtype=torch.bfloat16, reserve: int = 0,
+                 tail_tokens: int = 64, retain_kv: bool = True, kv: str | None = None):
+        self.m = model
+        self.dev = torch.device(device)
+        self.dt = dtype
+        self.B, self.L, self.reserve = int(B), int(L), int(reserve)
+        self.tail_tokens = min(int(tail_tokens), self.L) if tail_tokens > 0 else 1
+        self.retain_kv = bool(retain_kv)
+        self.kv = kv
+        self.graph = None
+        self.x_static = self.static_logits = self.static_tail = self.cache = None
+
+    def _body(self):
+        for c in self.cache:
+            c.pos = 0
+        h = trunk_cached(self.m, self.x_static, self.cache, last_n=self.tail_tokens)
+        tail = h[:, -self.tail_tokens:, :].clone()
+        return lm_head(self.m, h[:, -1]), tail
+
+    @torch.no_grad()
+    def capture(self, sample_ids: torch.Tensor | None = None):
+        m = self.m
+        extend_rope_cache(m, self.L + max(self.reserve, 256))
+        self.x_static = torch.zeros((self.B, self.L), dtype=torch.int64, device=self.dev)
+        if sample_ids is not None:
+            self.x_static.copy_(sample_ids.to(self.dev).view(self.B, self.L))
+        self.cache = make_caches(m, reserve=self.reserve, linear=False, retain_kv=self.retain_kv)
+        if self.retain_kv and self.kv in ("int8", "bounded"):
+            for c in self.cache:
+                c.enable_bounded() if self.kv == "bounded" else c.enable_int8()
+        side = torch.cuda.Stream(device=self.dev)
+        side.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(side):
+            self._body()                       # allocates the caches' state; every later pass reuses it
+        torch.cuda.current_stream(self.dev).wait_stream(side)
+        torch.cuda.synchronize(self.dev)
+        torch.cuda.empty_cache()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.static_logits, self.static_tail = self._body()
+        return self
+
+    @torch.no_grad()
+    def run(self, prompt_ids: torch.Tensor):
+        """Prefill one prompt of the captured shape; returns the last token's logits (B, V) (a static buffer)."""
+        if prompt_ids.numel() != self.B * self.L:
+            raise ValueError(f"GraphedPrefiller was built for prompts of shape ({self.B}, {self.L})")
+        if self.graph is None:
+            self.capture(prompt_ids)
+        else:
+            self.x_static.copy_(prompt_ids.to(self.dev).view(self.B, self.L))
+        self.graph.replay()
+        for c in self.cache:
+            c.pos = self.L
+        return self.static_logits
+
+    @torch.no_grad()
+    def tail_logits(self):
+        """Logits of the last `tail_tokens` positions of the prompt run last (B, tail, V)."""
+        return lm_head(self.m, self.static_tail)
+
+
 @torch.no_grad()
 def calibrate_fsb_tau(model, ids, quantile: float, target: str = "fsb_tau"):
     """Set every FS-B layer's admission threshold to the per-head `quantile` of the cell ceilings seen on the token ids

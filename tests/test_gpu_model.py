@@ -373,3 +373,49 @@ def test_step_ends_embedding_lookup_and_argmax():
         ops.argmax_advance(logits, out, pos)
         want = logits.float().argmax(-1)
         assert out.view(-1).tolist() == [int(want[0]), 77, V - 1] and int(pos) == 42
+
+
+@pytest.mark.parametrize("serve,kv,retain", [("sparse", "int8", True), ("sparse", None, False), ("fsb", "int8", True), ("dense", "int8", True)])
+def test_graphed_prefill_equals_the_eager_prefill(dev, serve, kv, retain):
+    """experiments/scaling/decode_graph.py:623-709 (GraphedPrefiller): the whole prefill captured once at a fixed shape and
+    replayed per prompt gives the eager prefill's logits bit for bit, for the prompt it was captured on and for the next one
+    (every replay starts the caches over), and leaves caches a decoder can continue from."""
+    from freesolo_b200.fsattn.kv_cache import make_caches
+    from freesolo_b200.serving import FreeSoloLM, GraphedPrefiller, calibrate_fsb_tau, lm_head, serve_kwargs, trunk_cached
+    L, tail = 1500, 16
+    torch.manual_seed(0)
+    m = FreeSoloLM.from_config("debug", max_seq_len=2048, **serve_kwargs(serve, 0.9 if serve == "fsb" else 0.0))
+    m = m.to(dev).to(torch.bfloat16).eval()
+    if serve == "fsb":
+        warm = torch.randint(0, 32000, (1, 1024), generator=torch.Generator().manual_seed(5))
+        calibrate_fsb_tau(m, warm, 0.5, "fsb_tau")
+        calibrate_fsb_tau(m, warm, 0.9, "fsb_tau_union")
+    prompts = [torch.randint(0, 32000, (1, L), generator=torch.Generator().manual_seed(s)).to(dev) for s in (11, 12)]
+
+    def eager(ids):
+        with torch.no_grad():
+            caches = make_caches(m, reserve=8, retain_kv=retain)
+            if retain and kv == "int8":
+                for c in caches:
+                    c.enable_int8()
+            h = trunk_cached(m, ids, caches, last_n=tail)
+            return lm_head(m, h[:, -1]).clone(), lm_head(m, h[:, -tail:]).clone(), caches
+
+    gp = GraphedPrefiller(m, L, B=1, device=dev, reserve=8, tail_tokens=tail, retain_kv=retain, kv=kv)
+    for ids in prompts:
+        want, want_tail, caches = eager(ids)
+        got = gp.run(ids)
+        torch.cuda.synchronize()
+        assert gp.graph is not None
+        assert torch.equal(got, want)
+        assert torch.equal(gp.tail_logits(), want_tail)
+        assert all(c.pos == L for c in gp.cache)
+    if retain:
+        # one more token through the graph's caches and through the eager prefill's: the same hidden state
+        tok = want.argmax(-1).view(1, 1)
+        with torch.no_grad():
+            h1 = trunk_cached(m, tok, gp.cache)
+            h2 = trunk_cached(m, tok, caches)
+        assert torch.equal(h1, h2)
+    with pytest.raises(ValueError):
+        gp.run(prompts[0][:, :100])
