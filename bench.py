@@ -670,8 +670,11 @@ def run_config5(args, dev, rank, world, dist):
            "forest_bytes_per_layer_per_gpu": gd.fsb_bytes() // nL, "forest_cells_cap": fo.m_cap,
            "admitted_cells_layer0_rank0": {"main": fo.m_tot[0].tolist(), "second": fo.m_tot[1].tolist()},
            "kv_bytes_per_layer_per_gpu": gd.kv_bytes() // nL, "peak_mem_gib_per_gpu": torch.cuda.max_memory_allocated() / 2 ** 30,
-           "kv_faults": list(gd.kv_faults())}
+           "exchange": "peer memory" if gd.peer is not None else ("NCCL all-gather" if world > 1 else "none"),
+           "peer_wait_status": gd.peer_status(), "kv_faults": list(gd.kv_faults())}
     gd.graph = None
+    if gd.peer is not None:
+        gd.peer.close()
     del gd, model
     import gc
     gc.collect()
