@@ -2,6 +2,7 @@
 #pragma once
 #include "common.cuh"
 
+#define FSB_CLUSTER_K 9        // chunks of 2^9 cells and more are built by a thread-block cluster
 #define FSB_SMALL_K 5          // chunks of up to 2^5 cells are built in shared memory by the small-chunk kernel
 #define FSB_MAX_MCAP 16384     // largest supported cell capacity per row (room for 262 144 tokens plus decode growth)
 #define FSB_MAX_CHUNK 8192     // largest chunk the build kernel takes (a chunk of 16 384 cells needs 524 288 admitted tokens)

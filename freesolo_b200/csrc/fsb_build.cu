@@ -68,20 +68,76 @@ __global__ void __launch_bounds__(256) fsb_admit_kernel(BuildArgs a, int cb, int
 // ------------------------------------------------------------------------------------------------------------------
 // chunk build
 // ------------------------------------------------------------------------------------------------------------------
-template <int D, int THREADS, bool SMALL>
+// CS > 1: the chunk is built by a thread-block cluster of CS CTAs. Every pass strides over the cluster's threads (or warps)
+// instead of the CTA's, and the barriers between passes are cluster barriers (hardware, release / acquire at cluster scope:
+// the working arrays live in the L2-resident scratch, so the other CTAs' writes are visible after them). Which thread
+// computes an element changes nothing in its arithmetic, so the trees stay bit-identical. Every barrier sits at a point all
+// CTAs of the cluster reach the same number of times (the early returns depend on the chunk only, never on the CTA).
+template <int CS>
+__device__ __forceinline__ void fsb_build_sync() {
+    if constexpr (CS == 1) {
+        __syncthreads();
+    } else {
+        asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    }
+}
+
+// The halving steps of a node sum: on entry Y[(g h + i) D + d], i < h, hold the first-level sums of node g; after the
+// caller's barrier Y[g h D + d] is the node's sum. Steps over 16 and more pairs per node are flat passes separated by
+// barriers; the last four (at most 16 values per node and dimension) are done by one thread in registers, in the same
+// association order (v[i] + v[i + s] for s = 8, 4, 2, 1), which saves four barriers per sum.
+constexpr int FSB_HALVE_TAIL = 16;
+template <int D, int CS, int CT>
+__device__ __forceinline__ void fsb_halve(float* Y, int nodes, int h, int tid) {
+    for (int h2 = h >> 1; h2 >= FSB_HALVE_TAIL; h2 >>= 1) {
+        fsb_build_sync<CS>();
+        const int lh2 = 31 - __clz(h2);
+        for (int e = tid; e < nodes * h2 * D; e += CT) {
+            const int d = e % D, q = e / D;
+            const int g = q >> lh2, i = q & (h2 - 1);
+            const int64_t r = ((int64_t)g * h + i) * D + d;
+            Y[r] = f_add(Y[r], Y[r + (int64_t)h2 * D]);
+        }
+    }
+    const int w = min(h, FSB_HALVE_TAIL);             // values left per (node, dimension); a power of two
+    if (w < 2) return;
+    fsb_build_sync<CS>();
+    for (int e = tid; e < nodes * D; e += CT) {
+        const int g = e / D, d = e % D;
+        float* base = Y + (int64_t)g * h * D + d;
+        float v[FSB_HALVE_TAIL];
+#pragma unroll
+        for (int i = 0; i < FSB_HALVE_TAIL; ++i) v[i] = i < w ? base[(int64_t)i * D] : 0.0f;
+#pragma unroll
+        for (int sft = FSB_HALVE_TAIL / 2; sft >= 1; sft >>= 1) {
+            if (sft < w) {
+#pragma unroll
+                for (int i = 0; i < sft; ++i) v[i] = f_add(v[i], v[i + sft]);
+            }
+        }
+        base[0] = v[0];
+    }
+}
+
+template <int D, int THREADS, bool SMALL, int CS>
 __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
+    static_assert(!SMALL || CS == 1, "small chunks live in one CTA's shared memory");
     constexpr int NPL = FsbDim<D>::NPL;
-    constexpr int NW = THREADS / 32;
+    constexpr int NW = THREADS / 32 * CS;                 // warps of the cluster
     constexpr int SN = SMALL ? 32 : 1;                    // shared-memory capacity in cells (small kernel)
     const fsattn_fsb_forest_t& F = a.f[blockIdx.z];
     const int t = blockIdx.y;
     const int m_cap = F.m_cap, k_cap = a.k_cap;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int ltid = threadIdx.x, lane = ltid & 31;
+    int crank = 0;
+    if constexpr (CS > 1) asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(crank));
+    const int tid = crank * THREADS + ltid, warp = tid >> 5;       // identity inside the cluster
+    constexpr int CT = THREADS * CS;
 
     // ---- which admitted position does this CTA complete a chunk for? ----
     int p;
     if (a.mode == 0) {
-        const int x = a.x0 + blockIdx.x;
+        const int x = a.x0 + blockIdx.x / CS;
         if (x == 0) {
             p = m_cap - 1;
         } else {
@@ -90,11 +146,17 @@ __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
             p = ((2 * (x - (1 << fl)) + 1) << k_) - 1;
         }
     } else {
-        p = F.m_prev[t] + blockIdx.x;
+        p = F.m_prev[t] + blockIdx.x / CS;
     }
     if (p < F.m_prev[t] || p >= F.m_tot[t]) return;
     const int k = __ffs(p + 1) - 1;
-    if (SMALL ? (k > FSB_SMALL_K) : (k <= FSB_SMALL_K)) return;
+    if constexpr (SMALL) {
+        if (k > FSB_SMALL_K) return;
+    } else if constexpr (CS > 1) {
+        if (k < FSB_CLUSTER_K) return;
+    } else {
+        if (k <= FSB_SMALL_K || k >= FSB_CLUSTER_K) return;
+    }
     const int n = 1 << k;
     if (n > FSB_MAX_CHUNK) return;             // cannot happen below 524 288 admitted tokens per row
     const int j = ((p + 1) >> k) - 1, jj = j >> 1;
@@ -129,31 +191,22 @@ __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
         XC = base; Y = XC + (int64_t)n * D; VV = Y + (int64_t)(n / 2) * D; S1 = VV + (int64_t)(n / 2) * D;
         ordA = (int*)(S1 + n); ordB = ordA + n; FAR = ordB + n;
     }
-    for (int i = tid; i < n; i += THREADS) ordA[i] = i;
-    __syncthreads();
+    for (int i = tid; i < n; i += CT) ordA[i] = i;
+    fsb_build_sync<CS>();
 
     for (int l = 0; l <= k; ++l) {
         const int lm = k - l, m = 1 << lm, h = m >> 1, nodes = 1 << l;
         // ---- P1: mean = halving sum of the members / m ----
         if (m >= 2) {
-            for (int e = tid; e < (n / 2) * D; e += THREADS) {
+            for (int e = tid; e < (n / 2) * D; e += CT) {
                 const int d = e % D, q = e / D;
                 const int g = q >> (lm - 1), i = q & (h - 1);
                 const float x0 = kbar[(int64_t)adm[ordA[(g << lm) + i]] * D + d];
                 const float x1 = kbar[(int64_t)adm[ordA[(g << lm) + i + h]] * D + d];
                 Y[(int64_t)q * D + d] = f_add(x0, x1);
             }
-            for (int h2 = h >> 1; h2 >= 1; h2 >>= 1) {
-                __syncthreads();
-                const int lh2 = 31 - __clz(h2);
-                for (int e = tid; e < nodes * h2 * D; e += THREADS) {
-                    const int d = e % D, q = e / D;
-                    const int g = q >> lh2, i = q & (h2 - 1);
-                    const int64_t r = ((int64_t)g * h + i) * D + d;
-                    Y[r] = f_add(Y[r], Y[r + (int64_t)h2 * D]);
-                }
-            }
-            __syncthreads();
+            fsb_halve<D, CS, CT>(Y, nodes, h, tid);
+            fsb_build_sync<CS>();
         }
         // ---- P2: centre the members, squared distance ----
         for (int c = warp; c < n; c += NW) {
@@ -177,7 +230,7 @@ __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
             const float d2 = fsb_warp_det_sum<D>(sq);
             if (lane == 0) S1[c] = d2;
         }
-        __syncthreads();
+        fsb_build_sync<CS>();
         // ---- P3: node statistics, node tables, farthest member ----
         for (int g = warp; g < nodes; g += NW) {
             float best = -1.0f, am = -INFINITY;
@@ -227,14 +280,14 @@ __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
             }
         }
         if (l == k) break;
-        __syncthreads();
+        fsb_build_sync<CS>();
         // ---- P4: start direction = farthest member, normalised ----
-        for (int e = tid; e < nodes * D; e += THREADS) {
+        for (int e = tid; e < nodes * D; e += CT) {
             const int g = e / D, d = e % D;
             const int fc = FAR[g];
             VV[e] = f_div(XC[(int64_t)fc * D + d], fmaxf(f_sqrt(S1[fc]), 1e-6f));
         }
-        __syncthreads();
+        fsb_build_sync<CS>();
         // ---- P5: two power iterations v <- normalise(sum_c xc_c (xc_c . v)) ; P6: projections ----
         for (int it = 0; it < 3; ++it) {
             for (int c = warp; c < n; c += NW) {
@@ -246,25 +299,16 @@ __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
                 const float pv = fsb_warp_det_sum<D>(pr);
                 if (lane == 0) S1[c] = pv;
             }
-            __syncthreads();
+            fsb_build_sync<CS>();
             if (it == 2) break;
-            for (int e = tid; e < (n / 2) * D; e += THREADS) {
+            for (int e = tid; e < (n / 2) * D; e += CT) {
                 const int d = e % D, q = e / D;
                 const int g = q >> (lm - 1), i = q & (h - 1);
                 const int c0 = (g << lm) + i, c1 = c0 + h;
                 Y[(int64_t)q * D + d] = f_add(f_mul(XC[(int64_t)c0 * D + d], S1[c0]), f_mul(XC[(int64_t)c1 * D + d], S1[c1]));
             }
-            for (int h2 = h >> 1; h2 >= 1; h2 >>= 1) {
-                __syncthreads();
-                const int lh2 = 31 - __clz(h2);
-                for (int e = tid; e < nodes * h2 * D; e += THREADS) {
-                    const int d = e % D, q = e / D;
-                    const int g = q >> lh2, i = q & (h2 - 1);
-                    const int64_t r = ((int64_t)g * h + i) * D + d;
-                    Y[r] = f_add(Y[r], Y[r + (int64_t)h2 * D]);
-                }
-            }
-            __syncthreads();
+            fsb_halve<D, CS, CT>(Y, nodes, h, tid);
+            fsb_build_sync<CS>();
             for (int g = warp; g < nodes; g += NW) {
                 float vn[NPL], sq[NPL];
                 fsb_load_row<D>(Y + (int64_t)g * h * D, lane, vn);
@@ -275,16 +319,16 @@ __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
                 for (int i = 0; i < NPL; ++i) vn[i] = f_div(vn[i], nrm);
                 fsb_store_row<D>(VV + (int64_t)g * D, lane, vn);
             }
-            __syncthreads();
+            fsb_build_sync<CS>();
         }
         // ---- P7: stable ascending rank of the projections inside each node; the lower half becomes the left child ----
         const float* PJ = S1;
         if constexpr (!SMALL) {
-            for (int i = tid; i < n; i += THREADS) sm_proj[i] = S1[i];
+            for (int i = ltid; i < n; i += THREADS) sm_proj[i] = S1[i];      // every CTA keeps its own copy
             __syncthreads();
             PJ = sm_proj;
         }
-        for (int c = tid; c < n; c += THREADS) {
+        for (int c = tid; c < n; c += CT) {
             const int b0 = (c >> lm) << lm;
             const float pc = PJ[c];
             int r = 0;
@@ -294,27 +338,56 @@ __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
             }
             ordB[b0 + r] = ordA[c];
         }
-        __syncthreads();
+        fsb_build_sync<CS>();
         int* tmp = ordA; ordA = ordB; ordB = tmp;
     }
+}
+
+// chunks of 2^FSB_CLUSTER_K cells and more are built by a cluster of FSB_BUILD_CS CTAs: they are the critical path of an
+// ingest (one CTA walks 2048 cells x 11 levels in about 5 ms), and only a few of them exist per row
+constexpr int FSB_BUILD_CS = 4;
+
+template <int D>
+cudaError_t launch_build_cluster(const BuildArgs& a, int items, int T, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(items * FSB_BUILD_CS, T, a.nf);
+    cfg.blockDim = dim3(512);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = FSB_BUILD_CS;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, fsb_build_kernel<D, 512, false, FSB_BUILD_CS>, a);
 }
 
 template <int D>
 int launch_build(const BuildArgs& a0, int T, int new_cells, cudaStream_t st) {
     BuildArgs a = a0;
     const int m_cap = a.f[0].m_cap;
+    cudaError_t ce = cudaSuccess;
     if (a.mode == 0) {
+        // item x of the big-first order is a chunk of height k_cap - 1 - floor(log2 x) (x = 0: k_cap): the first m_cap >> K
+        // items are the chunks of height K and more
+        const int cl_items = (a.k_cap >= FSB_CLUSTER_K) ? (m_cap >> FSB_CLUSTER_K) : 0;
         const int big_items = (a.k_cap > FSB_SMALL_K) ? (m_cap >> (FSB_SMALL_K + 1)) : 0;
-        if (big_items > 0) {
-            a.x0 = 0;
-            fsb_build_kernel<D, 512, false><<<dim3(big_items, T, a.nf), 512, 0, st>>>(a);
-        }
+        a.x0 = 0;
+        if (cl_items > 0) ce = launch_build_cluster<D>(a, cl_items, T, st);
+        if (big_items > 0) fsb_build_kernel<D, 512, false, 1><<<dim3(big_items, T, a.nf), 512, 0, st>>>(a);
         a.x0 = big_items;
         if (m_cap - big_items > 0)
-            fsb_build_kernel<D, 128, true><<<dim3(m_cap - big_items, T, a.nf), 128, 0, st>>>(a);
+            fsb_build_kernel<D, 128, true, 1><<<dim3(m_cap - big_items, T, a.nf), 128, 0, st>>>(a);
     } else {
-        if (a.k_cap > FSB_SMALL_K) fsb_build_kernel<D, 512, false><<<dim3(new_cells, T, a.nf), 512, 0, st>>>(a);
-        fsb_build_kernel<D, 128, true><<<dim3(new_cells, T, a.nf), 128, 0, st>>>(a);
+        if (a.k_cap >= FSB_CLUSTER_K) ce = launch_build_cluster<D>(a, new_cells, T, st);
+        if (a.k_cap > FSB_SMALL_K) fsb_build_kernel<D, 512, false, 1><<<dim3(new_cells, T, a.nf), 512, 0, st>>>(a);
+        fsb_build_kernel<D, 128, true, 1><<<dim3(new_cells, T, a.nf), 128, 0, st>>>(a);
+    }
+    if (ce != cudaSuccess) {
+        (void)cudaGetLastError();
+        fs_set_error("fsb_build_kernel (cluster): launch failed: %s", cudaGetErrorString(ce));
+        return FSATTN_ELAUNCH;
     }
     return fs_check_launch("fsb_build_kernel");
 }

@@ -66,7 +66,8 @@ def _check_forest(fo, i, kbar, ceil, tau, H, D, upto):
     return nchunks
 
 
-@pytest.mark.parametrize("cells,D,tied", [(300, 64, False), (77, 64, True), (130, 96, False), (200, 128, False)])
+@pytest.mark.parametrize("cells,D,tied", [(300, 64, False), (77, 64, True), (130, 96, False), (200, 128, False),
+                                          (1500, 64, False), (1200, 96, True), (3000, 128, False)])      # chunks of 512+ cells: the cluster build
 def test_forest_build_bit_exact(cells, D, tied):
     from freesolo_b200 import ops
     H = 2
