@@ -92,11 +92,22 @@ __device__ __forceinline__ void fsb_halve(float* Y, int nodes, int h, int tid) {
     for (int h2 = h >> 1; h2 >= FSB_HALVE_TAIL; h2 >>= 1) {
         fsb_build_sync<CS>();
         const int lh2 = 31 - __clz(h2);
-        for (int e = tid; e < nodes * h2 * D; e += CT) {
-            const int d = e % D, q = e / D;
-            const int g = q >> lh2, i = q & (h2 - 1);
-            const int64_t r = ((int64_t)g * h + i) * D + d;
-            Y[r] = f_add(Y[r], Y[r + (int64_t)h2 * D]);
+        const int tot = nodes * h2 * D;
+        for (int e0 = tid; e0 < tot; e0 += CT * 4) {
+            float ya[4], yb[4];
+            int64_t rr[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int e = (e0 + u * CT < tot) ? e0 + u * CT : 0;        // element 0 stands in for the ones past the end
+                const int d = e % D, q = e / D;
+                const int g = q >> lh2, i = q & (h2 - 1);
+                rr[u] = ((int64_t)g * h + i) * D + d;
+                ya[u] = Y[rr[u]];
+                yb[u] = Y[rr[u] + (int64_t)h2 * D];
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (e0 + u * CT < tot) Y[rr[u]] = f_add(ya[u], yb[u]);
         }
     }
     const int w = min(h, FSB_HALVE_TAIL);             // values left per (node, dimension); a power of two
@@ -133,6 +144,10 @@ __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
     if constexpr (CS > 1) asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(crank));
     const int tid = crank * THREADS + ltid, warp = tid >> 5;       // identity inside the cluster
     constexpr int CT = THREADS * CS;
+    // The flat passes are chains of dependent reads of L2-resident arrays, and the hardware issues in order: a loop body
+    // "load, load, use, store" pays its memory round trips one iteration after the other. They take U elements per trip and
+    // issue all their loads before the first use; elements past the end read element 0 and store nothing.
+    constexpr int U = 4;
 
     // ---- which admitted position does this CTA complete a chunk for? ----
     int p;
@@ -198,37 +213,65 @@ __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
         const int lm = k - l, m = 1 << lm, h = m >> 1, nodes = 1 << l;
         // ---- P1: mean = halving sum of the members / m ----
         if (m >= 2) {
-            for (int e = tid; e < (n / 2) * D; e += CT) {
-                const int d = e % D, q = e / D;
-                const int g = q >> (lm - 1), i = q & (h - 1);
-                const float x0 = kbar[(int64_t)adm[ordA[(g << lm) + i]] * D + d];
-                const float x1 = kbar[(int64_t)adm[ordA[(g << lm) + i + h]] * D + d];
-                Y[(int64_t)q * D + d] = f_add(x0, x1);
+            for (int e0 = tid; e0 < (n / 2) * D; e0 += CT * U) {
+                int o0[U], o1[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int e = e0 + u * CT;
+                    const bool ok = e < (n / 2) * D;
+                    const int q = ok ? e / D : 0;
+                    const int g = q >> (lm - 1), i = q & (h - 1);
+                    o0[u] = ordA[(g << lm) + i];
+                    o1[u] = ordA[(g << lm) + i + h];
+                }
+#pragma unroll
+                for (int u = 0; u < U; ++u) { o0[u] = adm[o0[u]]; o1[u] = adm[o1[u]]; }
+                float x0[U], x1[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int e = e0 + u * CT;
+                    const int d = (e < (n / 2) * D) ? e % D : 0;
+                    x0[u] = kbar[(int64_t)o0[u] * D + d];
+                    x1[u] = kbar[(int64_t)o1[u] * D + d];
+                }
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int e = e0 + u * CT;
+                    if (e < (n / 2) * D) Y[e] = f_add(x0[u], x1[u]);
+                }
             }
             fsb_halve<D, CS, CT>(Y, nodes, h, tid);
             fsb_build_sync<CS>();
         }
         // ---- P2: centre the members, squared distance ----
-        for (int c = warp; c < n; c += NW) {
-            const int g = c >> lm;
-            float x[NPL], mu[NPL], xc[NPL], sq[NPL];
-            fsb_load_row<D>(kbar + (int64_t)adm[ordA[c]] * D, lane, x);
+        for (int c0 = warp; c0 < n; c0 += NW * 2) {      // two members per trip: both rows are in flight before either is used
+            const int c1 = c0 + NW;
+            const bool two = c1 < n;
+            const int cb = two ? c1 : c0;
+            const int o0 = ordA[c0], o1 = ordA[cb];
+            const int id0 = adm[o0], id1 = adm[o1];
+            float x[2][NPL], mu[2][NPL];
+            fsb_load_row<D>(kbar + (int64_t)id0 * D, lane, x[0]);
+            fsb_load_row<D>(kbar + (int64_t)id1 * D, lane, x[1]);
             if (m >= 2) {
-                fsb_load_row<D>(Y + (int64_t)g * h * D, lane, mu);
-#pragma unroll
-                for (int i = 0; i < NPL; ++i) mu[i] = f_div(mu[i], (float)m);
-            } else {
-#pragma unroll
-                for (int i = 0; i < NPL; ++i) mu[i] = x[i];
+                fsb_load_row<D>(Y + (int64_t)(c0 >> lm) * h * D, lane, mu[0]);
+                fsb_load_row<D>(Y + (int64_t)(cb >> lm) * h * D, lane, mu[1]);
             }
 #pragma unroll
-            for (int i = 0; i < NPL; ++i) {
-                xc[i] = f_add(x[i], -mu[i]);
-                sq[i] = f_mul(xc[i], xc[i]);
+            for (int r = 0; r < 2; ++r) {
+                if (r == 1 && !two) break;
+                float xc[NPL], sq[NPL];
+#pragma unroll
+                for (int i = 0; i < NPL; ++i) {
+                    const float mm = (m >= 2) ? f_div(mu[r][i], (float)m) : x[r][i];
+                    xc[i] = f_add(x[r][i], -mm);
+                    sq[i] = f_mul(xc[i], xc[i]);
+                }
+                const int c = r == 0 ? c0 : c1;
+                fsb_store_row<D>(XC + (int64_t)c * D, lane, xc);
+                const float d2 = fsb_warp_det_sum<D>(sq);
+                if (lane == 0) S1[c] = d2;
             }
-            fsb_store_row<D>(XC + (int64_t)c * D, lane, xc);
-            const float d2 = fsb_warp_det_sum<D>(sq);
-            if (lane == 0) S1[c] = d2;
         }
         fsb_build_sync<CS>();
         // ---- P3: node statistics, node tables, farthest member ----
@@ -282,30 +325,65 @@ __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
         if (l == k) break;
         fsb_build_sync<CS>();
         // ---- P4: start direction = farthest member, normalised ----
-        for (int e = tid; e < nodes * D; e += CT) {
-            const int g = e / D, d = e % D;
-            const int fc = FAR[g];
-            VV[e] = f_div(XC[(int64_t)fc * D + d], fmaxf(f_sqrt(S1[fc]), 1e-6f));
+        for (int e0 = tid; e0 < nodes * D; e0 += CT * U) {
+            int fc[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) { const int e = e0 + u * CT; fc[u] = FAR[e < nodes * D ? e / D : 0]; }
+            float xv[U], sv[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int e = e0 + u * CT;
+                const int d = e < nodes * D ? e % D : 0;
+                xv[u] = XC[(int64_t)fc[u] * D + d];
+                sv[u] = S1[fc[u]];
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int e = e0 + u * CT;
+                if (e < nodes * D) VV[e] = f_div(xv[u], fmaxf(f_sqrt(sv[u]), 1e-6f));
+            }
         }
         fsb_build_sync<CS>();
         // ---- P5: two power iterations v <- normalise(sum_c xc_c (xc_c . v)) ; P6: projections ----
         for (int it = 0; it < 3; ++it) {
-            for (int c = warp; c < n; c += NW) {
-                float xc[NPL], v[NPL], pr[NPL];
-                fsb_load_row<D>(XC + (int64_t)c * D, lane, xc);
-                fsb_load_row<D>(VV + (int64_t)(c >> lm) * D, lane, v);
+            for (int c0 = warp; c0 < n; c0 += NW * 2) {
+                const int c1 = c0 + NW;
+                const bool two = c1 < n;
+                const int cb = two ? c1 : c0;
+                float xc[2][NPL], v[2][NPL];
+                fsb_load_row<D>(XC + (int64_t)c0 * D, lane, xc[0]);
+                fsb_load_row<D>(XC + (int64_t)cb * D, lane, xc[1]);
+                fsb_load_row<D>(VV + (int64_t)(c0 >> lm) * D, lane, v[0]);
+                fsb_load_row<D>(VV + (int64_t)(cb >> lm) * D, lane, v[1]);
 #pragma unroll
-                for (int i = 0; i < NPL; ++i) pr[i] = f_mul(xc[i], v[i]);
-                const float pv = fsb_warp_det_sum<D>(pr);
-                if (lane == 0) S1[c] = pv;
+                for (int r = 0; r < 2; ++r) {
+                    if (r == 1 && !two) break;
+                    float pr[NPL];
+#pragma unroll
+                    for (int i = 0; i < NPL; ++i) pr[i] = f_mul(xc[r][i], v[r][i]);
+                    const float pv = fsb_warp_det_sum<D>(pr);
+                    if (lane == 0) S1[r == 0 ? c0 : c1] = pv;
+                }
             }
             fsb_build_sync<CS>();
             if (it == 2) break;
-            for (int e = tid; e < (n / 2) * D; e += CT) {
-                const int d = e % D, q = e / D;
-                const int g = q >> (lm - 1), i = q & (h - 1);
-                const int c0 = (g << lm) + i, c1 = c0 + h;
-                Y[(int64_t)q * D + d] = f_add(f_mul(XC[(int64_t)c0 * D + d], S1[c0]), f_mul(XC[(int64_t)c1 * D + d], S1[c1]));
+            for (int e0 = tid; e0 < (n / 2) * D; e0 += CT * U) {
+                float xa[U], xb[U], sa[U], sb[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int e = e0 + u * CT;
+                    const bool ok = e < (n / 2) * D;
+                    const int d = ok ? e % D : 0, q = ok ? e / D : 0;
+                    const int g = q >> (lm - 1), i = q & (h - 1);
+                    const int c0 = (g << lm) + i, c1 = c0 + h;
+                    xa[u] = XC[(int64_t)c0 * D + d]; xb[u] = XC[(int64_t)c1 * D + d];
+                    sa[u] = S1[c0]; sb[u] = S1[c1];
+                }
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int e = e0 + u * CT;
+                    if (e < (n / 2) * D) Y[e] = f_add(f_mul(xa[u], sa[u]), f_mul(xb[u], sb[u]));
+                }
             }
             fsb_halve<D, CS, CT>(Y, nodes, h, tid);
             fsb_build_sync<CS>();
