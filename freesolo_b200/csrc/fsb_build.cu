@@ -87,18 +87,19 @@ __device__ __forceinline__ void fsb_build_sync() {
 // barriers; the last four (at most 16 values per node and dimension) are done by one thread in registers, in the same
 // association order (v[i] + v[i + s] for s = 8, 4, 2, 1), which saves four barriers per sum.
 constexpr int FSB_HALVE_TAIL = 16;
-template <int D, int CS, int CT>
-__device__ __forceinline__ void fsb_halve(float* Y, int nodes, int h, int tid) {
+template <int D, int CS>
+__device__ __forceinline__ void fsb_halve(float* Y, int nodes, int h, int part, int parts, int T0, int TS, bool own) {
     for (int h2 = h >> 1; h2 >= FSB_HALVE_TAIL; h2 >>= 1) {
-        fsb_build_sync<CS>();
+        if (own) __syncthreads(); else fsb_build_sync<CS>();
         const int lh2 = 31 - __clz(h2);
         const int tot = nodes * h2 * D;
-        for (int e0 = tid; e0 < tot; e0 += CT * 4) {
+        const int e_lo = part * (tot / parts), e_hi = e_lo + tot / parts;
+        for (int e0 = e_lo + T0; e0 < e_hi; e0 += TS * 4) {
             float ya[4], yb[4];
             int64_t rr[4];
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-                const int e = (e0 + u * CT < tot) ? e0 + u * CT : 0;        // element 0 stands in for the ones past the end
+                const int e = (e0 + u * TS < e_hi) ? e0 + u * TS : e_lo;        // the range's first element stands in past the end
                 const int d = e % D, q = e / D;
                 const int g = q >> lh2, i = q & (h2 - 1);
                 rr[u] = ((int64_t)g * h + i) * D + d;
@@ -107,13 +108,15 @@ __device__ __forceinline__ void fsb_halve(float* Y, int nodes, int h, int tid) {
             }
 #pragma unroll
             for (int u = 0; u < 4; ++u)
-                if (e0 + u * CT < tot) Y[rr[u]] = f_add(ya[u], yb[u]);
+                if (e0 + u * TS < e_hi) Y[rr[u]] = f_add(ya[u], yb[u]);
         }
     }
     const int w = min(h, FSB_HALVE_TAIL);             // values left per (node, dimension); a power of two
     if (w < 2) return;
-    fsb_build_sync<CS>();
-    for (int e = tid; e < nodes * D; e += CT) {
+    if (own) __syncthreads(); else fsb_build_sync<CS>();
+    const int tot = nodes * D;
+    const int e_lo = part * (tot / parts), e_hi = e_lo + tot / parts;
+    for (int e = e_lo + T0; e < e_hi; e += TS) {
         const int g = e / D, d = e % D;
         float* base = Y + (int64_t)g * h * D + d;
         float v[FSB_HALVE_TAIL];
@@ -211,15 +214,25 @@ __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
 
     for (int l = 0; l <= k; ++l) {
         const int lm = k - l, m = 1 << lm, h = m >> 1, nodes = 1 << l;
+        // Once a level has at least CS nodes, every CTA of the cluster owns whole subtrees: it walks its own 1/CS of the nodes,
+        // members and elements, and its passes are separated by CTA barriers only (no CTA executes a cluster barrier from then
+        // on); above that the cluster works together. With CS = 1 this is the plain one-CTA build.
+        const bool own = CS > 1 && nodes >= CS;
+        const int part = own ? crank : 0, parts = own ? CS : 1;
+        const int T0 = own ? ltid : tid, TS = own ? THREADS : CT;                    // flat passes: offset and stride
+        const int W0 = own ? (ltid >> 5) : warp, WS = own ? THREADS / 32 : NW;       // per-row passes
+        auto lo = [&](int total) { return part * (total / parts); };
+        auto hi = [&](int total) { return (part + 1) * (total / parts); };
+        auto sync = [&]() { if (own) __syncthreads(); else fsb_build_sync<CS>(); };
         // ---- P1: mean = halving sum of the members / m ----
         if (m >= 2) {
-            for (int e0 = tid; e0 < (n / 2) * D; e0 += CT * U) {
+            const int e_lo = lo((n / 2) * D), e_hi = hi((n / 2) * D);
+            for (int e0 = e_lo + T0; e0 < e_hi; e0 += TS * U) {
                 int o0[U], o1[U];
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
-                    const int e = e0 + u * CT;
-                    const bool ok = e < (n / 2) * D;
-                    const int q = ok ? e / D : 0;
+                    const int e = (e0 + u * TS < e_hi) ? e0 + u * TS : e_lo;       // past the end: the range's first element
+                    const int q = e / D;
                     const int g = q >> (lm - 1), i = q & (h - 1);
                     o0[u] = ordA[(g << lm) + i];
                     o1[u] = ordA[(g << lm) + i + h];
@@ -229,24 +242,24 @@ __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
                 float x0[U], x1[U];
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
-                    const int e = e0 + u * CT;
-                    const int d = (e < (n / 2) * D) ? e % D : 0;
+                    const int e = (e0 + u * TS < e_hi) ? e0 + u * TS : e_lo;
+                    const int d = e % D;
                     x0[u] = kbar[(int64_t)o0[u] * D + d];
                     x1[u] = kbar[(int64_t)o1[u] * D + d];
                 }
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
-                    const int e = e0 + u * CT;
-                    if (e < (n / 2) * D) Y[e] = f_add(x0[u], x1[u]);
+                    const int e = e0 + u * TS;
+                    if (e < e_hi) Y[e] = f_add(x0[u], x1[u]);
                 }
             }
-            fsb_halve<D, CS, CT>(Y, nodes, h, tid);
-            fsb_build_sync<CS>();
+            fsb_halve<D, CS>(Y, nodes, h, part, parts, T0, TS, own);
+            sync();
         }
         // ---- P2: centre the members, squared distance ----
-        for (int c0 = warp; c0 < n; c0 += NW * 2) {      // two members per trip: both rows are in flight before either is used
-            const int c1 = c0 + NW;
-            const bool two = c1 < n;
+        for (int c0 = lo(n) + W0; c0 < hi(n); c0 += WS * 2) {      // two members per trip: both rows are in flight before either is used
+            const int c1 = c0 + WS;
+            const bool two = c1 < hi(n);
             const int cb = two ? c1 : c0;
             const int o0 = ordA[c0], o1 = ordA[cb];
             const int id0 = adm[o0], id1 = adm[o1];
@@ -273,9 +286,9 @@ __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
                 if (lane == 0) S1[c] = d2;
             }
         }
-        fsb_build_sync<CS>();
+        sync();
         // ---- P3: node statistics, node tables, farthest member ----
-        for (int g = warp; g < nodes; g += NW) {
+        for (int g = lo(nodes) + W0; g < hi(nodes); g += WS) {
             float best = -1.0f, am = -INFINITY;
             int bi = 0x7fffffff, pm = 0x7fffffff;
             for (int c = (g << lm) + lane; c < ((g + 1) << lm); c += 32) {
@@ -323,32 +336,32 @@ __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
             }
         }
         if (l == k) break;
-        fsb_build_sync<CS>();
+        sync();
         // ---- P4: start direction = farthest member, normalised ----
-        for (int e0 = tid; e0 < nodes * D; e0 += CT * U) {
+        const int v_lo = lo(nodes * D), v_hi = hi(nodes * D);
+        for (int e0 = v_lo + T0; e0 < v_hi; e0 += TS * U) {
             int fc[U];
 #pragma unroll
-            for (int u = 0; u < U; ++u) { const int e = e0 + u * CT; fc[u] = FAR[e < nodes * D ? e / D : 0]; }
+            for (int u = 0; u < U; ++u) { const int e = (e0 + u * TS < v_hi) ? e0 + u * TS : v_lo; fc[u] = FAR[e / D]; }
             float xv[U], sv[U];
 #pragma unroll
             for (int u = 0; u < U; ++u) {
-                const int e = e0 + u * CT;
-                const int d = e < nodes * D ? e % D : 0;
-                xv[u] = XC[(int64_t)fc[u] * D + d];
+                const int e = (e0 + u * TS < v_hi) ? e0 + u * TS : v_lo;
+                xv[u] = XC[(int64_t)fc[u] * D + e % D];
                 sv[u] = S1[fc[u]];
             }
 #pragma unroll
             for (int u = 0; u < U; ++u) {
-                const int e = e0 + u * CT;
-                if (e < nodes * D) VV[e] = f_div(xv[u], fmaxf(f_sqrt(sv[u]), 1e-6f));
+                const int e = e0 + u * TS;
+                if (e < v_hi) VV[e] = f_div(xv[u], fmaxf(f_sqrt(sv[u]), 1e-6f));
             }
         }
-        fsb_build_sync<CS>();
+        sync();
         // ---- P5: two power iterations v <- normalise(sum_c xc_c (xc_c . v)) ; P6: projections ----
         for (int it = 0; it < 3; ++it) {
-            for (int c0 = warp; c0 < n; c0 += NW * 2) {
-                const int c1 = c0 + NW;
-                const bool two = c1 < n;
+            for (int c0 = lo(n) + W0; c0 < hi(n); c0 += WS * 2) {
+                const int c1 = c0 + WS;
+                const bool two = c1 < hi(n);
                 const int cb = two ? c1 : c0;
                 float xc[2][NPL], v[2][NPL];
                 fsb_load_row<D>(XC + (int64_t)c0 * D, lane, xc[0]);
@@ -365,15 +378,15 @@ __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
                     if (lane == 0) S1[r == 0 ? c0 : c1] = pv;
                 }
             }
-            fsb_build_sync<CS>();
+            sync();
             if (it == 2) break;
-            for (int e0 = tid; e0 < (n / 2) * D; e0 += CT * U) {
+            const int e_lo = lo((n / 2) * D), e_hi = hi((n / 2) * D);
+            for (int e0 = e_lo + T0; e0 < e_hi; e0 += TS * U) {
                 float xa[U], xb[U], sa[U], sb[U];
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
-                    const int e = e0 + u * CT;
-                    const bool ok = e < (n / 2) * D;
-                    const int d = ok ? e % D : 0, q = ok ? e / D : 0;
+                    const int e = (e0 + u * TS < e_hi) ? e0 + u * TS : e_lo;
+                    const int d = e % D, q = e / D;
                     const int g = q >> (lm - 1), i = q & (h - 1);
                     const int c0 = (g << lm) + i, c1 = c0 + h;
                     xa[u] = XC[(int64_t)c0 * D + d]; xb[u] = XC[(int64_t)c1 * D + d];
@@ -381,13 +394,13 @@ __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
                 }
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
-                    const int e = e0 + u * CT;
-                    if (e < (n / 2) * D) Y[e] = f_add(f_mul(xa[u], sa[u]), f_mul(xb[u], sb[u]));
+                    const int e = e0 + u * TS;
+                    if (e < e_hi) Y[e] = f_add(f_mul(xa[u], sa[u]), f_mul(xb[u], sb[u]));
                 }
             }
-            fsb_halve<D, CS, CT>(Y, nodes, h, tid);
-            fsb_build_sync<CS>();
-            for (int g = warp; g < nodes; g += NW) {
+            fsb_halve<D, CS>(Y, nodes, h, part, parts, T0, TS, own);
+            sync();
+            for (int g = lo(nodes) + W0; g < hi(nodes); g += WS) {
                 float vn[NPL], sq[NPL];
                 fsb_load_row<D>(Y + (int64_t)g * h * D, lane, vn);
 #pragma unroll
@@ -397,16 +410,16 @@ __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
                 for (int i = 0; i < NPL; ++i) vn[i] = f_div(vn[i], nrm);
                 fsb_store_row<D>(VV + (int64_t)g * D, lane, vn);
             }
-            fsb_build_sync<CS>();
+            sync();
         }
         // ---- P7: stable ascending rank of the projections inside each node; the lower half becomes the left child ----
         const float* PJ = S1;
         if constexpr (!SMALL) {
-            for (int i = ltid; i < n; i += THREADS) sm_proj[i] = S1[i];      // every CTA keeps its own copy
+            for (int i = lo(n) + ltid; i < hi(n); i += THREADS) sm_proj[i] = S1[i];      // every CTA keeps its own copy (of its own part)
             __syncthreads();
             PJ = sm_proj;
         }
-        for (int c = tid; c < n; c += CT) {
+        for (int c = lo(n) + T0; c < hi(n); c += TS) {
             const int b0 = (c >> lm) << lm;
             const float pc = PJ[c];
             int r = 0;
@@ -416,7 +429,7 @@ __global__ void __launch_bounds__(THREADS) fsb_build_kernel(BuildArgs a) {
             }
             ordB[b0 + r] = ordA[c];
         }
-        fsb_build_sync<CS>();
+        sync();
         int* tmp = ordA; ordA = ordB; ordB = tmp;
     }
 }
