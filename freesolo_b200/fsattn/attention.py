@@ -80,6 +80,7 @@ class Rotary(nn.Module):
         self.register_buffer("cos_cached", cos, persistent=False)
         self.register_buffer("sin_cached", sin, persistent=False)
         self._bf16 = None
+        CACHE_GEN[0] += 1
 
     def forward(self, seq_len: int):
         if seq_len > self.cos_cached.shape[0]:
@@ -105,10 +106,14 @@ class Rotary(nn.Module):
                 _SHARED_ROPE[key] = (cos, sin)
             c = (cos, sin)
             self._bf16 = c
+            CACHE_GEN[0] += 1
         return c
 
 
 _SHARED_ROPE = {}
+# Bumped whenever a module replaces one of the cached tensors a captured decode graph holds addresses of (rope tables,
+# per-head parameters, fused projection weights): a decoder compares it before a replay instead of walking every layer.
+CACHE_GEN = [0]
 
 
 _SIDE_STREAMS = {}
@@ -328,6 +333,7 @@ class FSAttn(nn.Module):
             key = (wq.data_ptr(), wq._version, wk.data_ptr(), wk._version, wv.data_ptr(), wv._version, wq.dtype)
             c = (key, qkv_w)
             self._w_qkv_cache = c
+            CACHE_GEN[0] += 1
         return c[1], dm
 
     def head_params(self):
@@ -340,6 +346,7 @@ class FSAttn(nn.Module):
                     self.long_range_scale.detach().float().reshape(-1).contiguous(), self.lr_norm.scale.detach().float().contiguous())
             c = (key, vals)
             self._head_params = c
+            CACHE_GEN[0] += 1
         return c[1]
 
     # ---- forward ---------------------------------------------------------------------------------------------------------

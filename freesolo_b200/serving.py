@@ -15,6 +15,7 @@ import torch.nn.functional as F
 
 from .fsattn import FSAttn, FSKVCache, make_caches
 from .fsattn import kv_bounded as _kvb
+from .fsattn.attention import CACHE_GEN as _CACHE_GEN
 
 MODEL_CONFIGS = {   # experiments/scaling/model.py:38-80 (vocab 32000 as the benchmark loads them)
     "debug": dict(d_model=256, n_layers=4, n_heads=4, d_ff=688, max_seq_len=1024, vocab_size=32000),
@@ -73,6 +74,7 @@ class SwiGLU(nn.Module):
             wg, wu = self.w_gate.weight, self.w_up.weight
             c = ((wg.data_ptr(), wg._version, wu.data_ptr(), wu._version, wg.dtype), gu)
             self._w_gu_cache = c
+            _CACHE_GEN[0] += 1
         return c[1], self.w_gate.weight.shape[0]
 
     def forward(self, x):
@@ -371,9 +373,15 @@ class GraphedDecoder:
         # the graph holds raw pointers into these: keep them alive for its lifetime, and notice when a cache replaces one
         # (a longer RoPE table, a changed parameter) so that the step is captured again instead of reading the old buffer
         self._graph_keep = self._graph_inputs()
+        self._graph_gen = _CACHE_GEN[0]
 
     def _graph_stale(self) -> bool:
-        return any(x is not y for x, y in zip(self._graph_keep, self._graph_inputs()))
+        if _CACHE_GEN[0] == self._graph_gen:           # nothing was rebuilt anywhere since the last look
+            return False
+        stale = any(x is not y for x, y in zip(self._graph_keep, self._graph_inputs()))
+        if not stale:
+            self._graph_gen = _CACHE_GEN[0]
+        return stale
 
     @torch.no_grad()
     def step(self):

@@ -419,3 +419,25 @@ def test_graphed_prefill_equals_the_eager_prefill(dev, serve, kv, retain):
         assert torch.equal(h1, h2)
     with pytest.raises(ValueError):
         gp.run(prompts[0][:, :100])
+
+
+def test_a_rebuilt_table_makes_the_decoder_capture_again(dev):
+    """A captured step holds the addresses of tensors that module-level caches own (rope tables, per-head parameters, fused
+    weights). When another decoder on the same model makes a cache rebuild one of them (here: longer rope tables), the first
+    decoder notices before its next replay, captures again and goes on producing the tokens of an undisturbed run."""
+    from freesolo_b200.serving import FreeSoloLM, GraphedDecoder, serve_kwargs
+    torch.manual_seed(0)
+    m = FreeSoloLM.from_config("debug", max_seq_len=1024, **serve_kwargs("sparse")).to(dev).to(torch.bfloat16).eval()
+    ids = torch.randint(0, 32000, (1, 700), generator=torch.Generator().manual_seed(3))
+    ref = GraphedDecoder(m, ids, Lmax=760, device=dev, kv="int8")
+    want = [ref.prefill().clone()] + [ref.step().clone() for _ in range(12)]
+    a = GraphedDecoder(m, ids, Lmax=760, device=dev, kv="int8")
+    got = [a.prefill().clone()] + [a.step().clone() for _ in range(6)]
+    g0 = a.graph
+    assert g0 is not None and not a._graph_stale()
+    other = GraphedDecoder(m, torch.randint(0, 32000, (1, 900), generator=torch.Generator().manual_seed(4)), Lmax=3000, device=dev, kv="int8")
+    other.prefill()                                   # needs rope tables of 3000 positions: the cache builds new ones
+    assert a._graph_stale()
+    got += [a.step().clone() for _ in range(6)]
+    assert a.graph is not None and a.graph is not g0 and not a._graph_stale()
+    assert torch.equal(torch.cat(got, dim=1), torch.cat(want, dim=1))
