@@ -30,8 +30,20 @@ __host__ __device__ __forceinline__ int64_t fsb_root_node(int k, int j, int m_ca
 __host__ __device__ __forceinline__ int fsb_chunk_id(int k, int j, int m_cap, int compact = 0) {
     return compact ? k : m_cap - (m_cap >> k) + (j >> 1);
 }
+// nodes per row: full arena (k_cap + 1) m_cap; compact = 1: 4 m_cap (room for every height a row of m_cap cells can have);
+// compact > 1: a compact arena of exactly `compact` nodes per row, sized by the caller for the admitted counts it can reach
 __host__ __device__ __forceinline__ int64_t fsb_nodes_per_row(int m_cap, int compact = 0) {
-    return compact ? 4 * (int64_t)m_cap : (int64_t)(fsb_log2(m_cap) + 1) * m_cap;
+    return compact > 1 ? (int64_t)compact : compact ? 4 * (int64_t)m_cap : (int64_t)(fsb_log2(m_cap) + 1) * m_cap;
+}
+// nodes a compact arena needs for chunks up to height kt: the places of heights 0..kt, sum of 2^{k+1} - 1
+__host__ __device__ __forceinline__ int64_t fsb_compact_nodes(int kt) { return ((int64_t)4 << kt) - 3 - kt; }
+// most cells a row may admit: m_cap, and in a sized compact arena no count that would need a height without a place
+__host__ __device__ __forceinline__ int fsb_admit_limit(int m_cap, int compact) {
+    if (compact <= 1) return m_cap;
+    int kt = 0;
+    while (kt < 30 && fsb_compact_nodes(kt + 1) <= (int64_t)compact) ++kt;
+    const int64_t lim = ((int64_t)2 << kt) - 1;                          // all heights 0..kt alive
+    return lim < m_cap ? (int)lim : m_cap;
 }
 __host__ __device__ __forceinline__ int64_t fsb_root_rows(int m_cap, int compact = 0) { return compact ? FSB_COMPACT_ROOTS : m_cap; }
 

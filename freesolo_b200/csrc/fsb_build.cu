@@ -39,6 +39,7 @@ __global__ void __launch_bounds__(256) fsb_admit_kernel(BuildArgs a, int cb, int
     const float tau = F.tau[t % F.H];
     const float* ceil = F.ceil + (int64_t)t * F.ceil_st;
     int* adm = F.adm + (int64_t)t * F.m_cap;
+    const int lim = fsb_admit_limit(F.m_cap, F.compact);      // a sized compact arena admits no more than it has places for
     if (tid == 0) {
         base = F.m_tot[t];
         F.m_prev[t] = base;
@@ -53,12 +54,12 @@ __global__ void __launch_bounds__(256) fsb_admit_kernel(BuildArgs a, int cb, int
         int off = base;
         for (int w = 0; w < warp; ++w) off += wsum[w];
         off += __popc(bal & ((1u << lane) - 1));
-        if (ok && off < F.m_cap) adm[off] = c;
+        if (ok && off < lim) adm[off] = c;
         __syncthreads();
         if (tid == 0) {
             int tot = 0;
             for (int w = 0; w < 8; ++w) tot += wsum[w];
-            base = min(base + tot, F.m_cap);
+            base = min(base + tot, lim);
         }
         __syncthreads();
     }
@@ -503,7 +504,8 @@ int fs_fsb_check_forest(const fsattn_fsb_forest_t& f, const char* what) {
     FS_UNSUPPORTED(f.m_cap > FSB_MAX_MCAP, "%s: m_cap = %d cells (at most %d)", what, f.m_cap, FSB_MAX_MCAP);
     FS_REQUIRE(f.kbar && f.ceil && f.tau && f.adm && f.m_tot && f.m_prev && f.node_mu && f.node_aux && f.root32,
                "%s: null forest buffer", what);
-    FS_REQUIRE(f.compact == 0 || f.compact == 1, "%s: compact = %d (0 or 1)", what, f.compact);
+    FS_REQUIRE(f.compact == 0 || f.compact == 1 || f.compact >= fsb_compact_nodes(0),
+               "%s: compact = %d (0: full arena, 1: compact with 4 m_cap nodes per row, n > 1: compact with n nodes per row)", what, f.compact);
     return FSATTN_OK;
 }
 
@@ -517,7 +519,8 @@ __global__ void fsb_compact_kernel(fsattn_fsb_forest_t S, fsattn_fsb_forest_t C)
     const int j = (m >> (k + 1)) << 1;
     const int n = (2 << k) - 1;
     const int64_t s0 = (int64_t)t * fsb_nodes_per_row(S.m_cap, 0) + fsb_root_node(k, j, S.m_cap, 0);
-    const int64_t d0 = (int64_t)t * fsb_nodes_per_row(S.m_cap, 1) + fsb_root_node(k, j, S.m_cap, 1);
+    if (m > fsb_admit_limit(C.m_cap, C.compact)) return;          // (refused on the host side; never copy past the arena)
+    const int64_t d0 = (int64_t)t * fsb_nodes_per_row(C.m_cap, C.compact) + fsb_root_node(k, j, S.m_cap, 1);
     const uint4* smu = (const uint4*)((const bf16*)S.node_mu + s0 * D);
     uint4* dmu = (uint4*)((bf16*)C.node_mu + d0 * D);
     for (int64_t i = threadIdx.x; i < (int64_t)n * (D / 8); i += blockDim.x) dmu[i] = smu[i];
@@ -536,7 +539,7 @@ extern "C" int fsattn_fsb_compact(const fsattn_fsb_forest_t* src, const fsattn_f
     if (rc != FSATTN_OK) return rc;
     rc = fs_fsb_check_forest(*dst, "fsb_compact(dst)");
     if (rc != FSATTN_OK) return rc;
-    FS_REQUIRE(src->compact == 0 && dst->compact == 1, "fsb_compact: from the full arena (compact = 0) to a compact one (1)");
+    FS_REQUIRE(src->compact == 0 && dst->compact >= 1, "fsb_compact: from the full arena (compact = 0) to a compact one (>= 1)");
     FS_REQUIRE(src->T == dst->T && src->D == dst->D && src->m_cap == dst->m_cap && src->m_tot == dst->m_tot,
                "fsb_compact: both arenas describe the same forest (T, D, m_cap, m_tot)");
     FS_REQUIRE(src->node_mu != dst->node_mu && src->node_aux != dst->node_aux && src->root32 != dst->root32,

@@ -581,6 +581,7 @@ class FsbForests:
         if m_cap > L.FSB_MAX_MCAP:
             raise RuntimeError(f"FS-B: {cap_cells} cells per row exceed the supported {L.FSB_MAX_MCAP}")
         self.m_cap = m_cap
+        self.cap_cells = max(1, int(cap_cells))
         self.k_cap = m_cap.bit_length() - 1
         self.kbar, self.ceil = kbar, ceil
         dev = kbar.device
@@ -596,18 +597,29 @@ class FsbForests:
         self.hdr = [torch.full((T, 4), -1, dtype=torch.int32, device=dev) for _ in range(self.nf)]
         self.n_seen = 0
 
-    def _arena(self, compact: int):
-        """(node_mu, node_aux, root32) lists of a full (every aligned chunk) or compact (one chunk per height) arena."""
+    def _arena(self, compact: int, nodes=None):
+        """(node_mu, node_aux, root32) lists of a full (every aligned chunk) or compact (one chunk per height) arena;
+        nodes: per forest, the nodes per row of a compact arena (default 4 m_cap, room for every height)."""
         T, D, dev = self.T, self.D, self.kbar.device
-        nodes = 4 * self.m_cap if compact else (self.k_cap + 1) * self.m_cap
+        if nodes is None:
+            nodes = [4 * self.m_cap if compact else (self.k_cap + 1) * self.m_cap] * self.nf
         roots = 32 if compact else self.m_cap
-        return ([torch.zeros(T, nodes, D, dtype=torch.bfloat16, device=dev) for _ in range(self.nf)],
-                [torch.zeros(T, nodes, 4, dtype=torch.float32, device=dev) for _ in range(self.nf)],
+        return ([torch.zeros(T, n, D, dtype=torch.bfloat16, device=dev) for n in nodes],
+                [torch.zeros(T, n, 4, dtype=torch.float32, device=dev) for n in nodes],
                 [torch.zeros(T, roots, D + 4, dtype=torch.float32, device=dev) for _ in range(self.nf)])
 
-    def _alloc_arena(self, compact: int) -> None:
-        self.node_mu, self.node_aux, self.root32 = self._arena(compact)
+    def _alloc_arena(self, compact: int, nodes=None) -> None:
+        self.node_mu, self.node_aux, self.root32 = self._arena(compact, nodes)
         self.compact = compact
+        # what the C struct carries: 0 full, 1 compact with 4 m_cap nodes per row, n > 1 compact with n nodes per row
+        self.compact_arg = [0] * self.nf if not compact else [1] * self.nf if nodes is None else [int(n) for n in nodes]
+
+    @staticmethod
+    def compact_nodes_for(max_admitted: int) -> int:
+        """Nodes per row of a compact arena whose rows never admit more than max_admitted cells: the places of the heights
+        0 .. floor(log2(max_admitted)), i.e. sum of 2^(k+1) - 1 (csrc/fsb.cuh: fsb_compact_nodes)."""
+        kt = max(int(max_admitted), 1).bit_length() - 1
+        return max((4 << kt) - 3 - kt, 2)
 
     def compact_arena(self, n_visible: int | None = None) -> None:
         """After a prefill: keep only the chunks of the current prefix, one place per chunk height, and release the arena
@@ -628,7 +640,15 @@ class FsbForests:
             self.n_seen = int(n_visible)
         src = [self.struct(i) for i in range(self.nf)]
         old = (self.node_mu, self.node_aux, self.root32)
-        self._alloc_arena(1)
+        # Size of the small arena: a row can still admit the cells that are not ingested yet, so no row's count can pass
+        # (its count now) + (capacity - cells seen); the admission kernel holds a sized arena to what it has places for. Reading
+        # the counts is one host synchronisation per layer; inside a stream capture the bound is the capacity itself.
+        room = max(0, self.cap_cells - self.n_seen)
+        if torch.cuda.is_current_stream_capturing():
+            bound = [min(self.m_cap, self.cap_cells)] * self.nf
+        else:
+            bound = [min(self.m_cap, int(self.m_tot[i].max().item()) + room) for i in range(self.nf)]
+        self._alloc_arena(1, [self.compact_nodes_for(b) for b in bound])
         lib = L.load()
         for i in range(self.nf):
             dst = self.struct(i)
@@ -660,7 +680,7 @@ class FsbForests:
         f.tau = self.taus[i].data_ptr()
         f.adm, f.m_tot, f.m_prev = self.adm[i].data_ptr(), self.m_tot[i].data_ptr(), self.m_prev[i].data_ptr()
         f.node_mu, f.node_aux, f.root32 = self.node_mu[i].data_ptr(), self.node_aux[i].data_ptr(), self.root32[i].data_ptr()
-        f.compact = self.compact
+        f.compact = self.compact_arg[i]
         return f
 
     def ingest(self, cell_end: int) -> None:

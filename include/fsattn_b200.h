@@ -404,7 +404,10 @@ typedef struct {
                                         * 1: one place per chunk height - node id of node n of the chunk of height k:
                                         * 2^{k+1} - 2 - k + n, 4 m_cap nodes per row, chunk id k, root32 (T, 32, D+4) - which
                                         * holds the CURRENT prefix only (decode; the reference's decode arena,
-                                        * fsb_tree.py:1496-1522). fsattn_fsb_compact converts 0 -> 1 after a prefill. */
+                                        * fsb_tree.py:1496-1522). fsattn_fsb_compact converts 0 -> 1 after a prefill.
+                                        * n > 1: the same with n nodes per row instead of 4 m_cap, for a caller that knows
+                                        * how far the admitted counts can grow: heights 0..kt need 2^{kt+2} - 3 - kt nodes,
+                                        * and a row then admits at most 2^{kt+1} - 1 cells (the admission stops there). */
 } fsattn_fsb_forest_t;
 
 /* Admit the cells [cell_begin, cell_end) of every row (ceil >= tau[h], fsb_tree.py:936-941, 1465-1494) into each of
@@ -446,8 +449,8 @@ typedef struct {
 FSATTN_API int fsattn_linear_select(const fsattn_linear_select_t* a, fsattn_stream_t stream);
 
 /* Copies the chunks of the current prefix (one per set bit of m_tot, per row) from a full arena into a compact one.
- * src and dst share T, H, D, m_cap, adm, m_tot, m_prev; dst->compact = 1 with its own node_mu (T, 4 m_cap, D), node_aux
- * (T, 4 m_cap, 4) and root32 (T, 32, D+4). After it the decode-time ingest, spines and selection run on dst; the full arena
+ * src and dst share T, H, D, m_cap, adm, m_tot, m_prev; dst->compact = 1 (or the nodes per row n) with its own node_mu
+ * (T, 4 m_cap or n, D), node_aux (T, 4 m_cap or n, 4) and root32 (T, 32, D+4). After it the decode-time ingest, spines and selection run on dst; the full arena
  * can be released (at 131 072 tokens: 300 MB -> 19 MB per forest and layer at head_dim 64). */
 FSATTN_API int fsattn_fsb_compact(const fsattn_fsb_forest_t* src, const fsattn_fsb_forest_t* dst, fsattn_stream_t stream);
 
