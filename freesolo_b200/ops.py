@@ -614,6 +614,8 @@ class FsbForests:
         # what the C struct carries: 0 full, 1 compact with 4 m_cap nodes per row, n > 1 compact with n nodes per row
         self.compact_arg = [0] * self.nf if not compact else [1] * self.nf if nodes is None else [int(n) for n in nodes]
 
+    TIGHT_ARENA_FROM = 3000      # cells of capacity above which the decode arena is sized from the admitted counts (one host sync per layer)
+
     @staticmethod
     def compact_nodes_for(max_admitted: int) -> int:
         """Nodes per row of a compact arena whose rows never admit more than max_admitted cells: the places of the heights
@@ -644,7 +646,9 @@ class FsbForests:
         # (its count now) + (capacity - cells seen); the admission kernel holds a sized arena to what it has places for. Reading
         # the counts is one host synchronisation per layer; inside a stream capture the bound is the capacity itself.
         room = max(0, self.cap_cells - self.n_seen)
-        if torch.cuda.is_current_stream_capturing():
+        if self.cap_cells <= self.TIGHT_ARENA_FROM or torch.cuda.is_current_stream_capturing():
+            # short prompts (the arena is a few MB anyway, and their prefill is bound by the host's launch rate, which a
+            # synchronisation per layer would stall) and captures: no read-back
             bound = [min(self.m_cap, self.cap_cells)] * self.nf
         else:
             bound = [min(self.m_cap, int(self.m_tot[i].max().item()) + room) for i in range(self.nf)]

@@ -91,13 +91,15 @@ def test_forest_build_bit_exact(cells, D, tied):
         assert torch.equal(fo.root32[i].view(torch.int32), fo2.root32[i].view(torch.int32))
 
 
-@pytest.mark.parametrize("cells,D", [(300, 64), (130, 96)])
-def test_compact_arena_holds_the_current_chunks_and_keeps_growing(cells, D):
+@pytest.mark.parametrize("cells,D,tight", [(300, 64, False), (130, 96, False), (300, 64, True), (1300, 128, True)])
+def test_compact_arena_holds_the_current_chunks_and_keeps_growing(cells, D, tight, monkeypatch):
     """After a prefill the forests keep one chunk per height (the reference's decode arena, src/fsattn/fsb_tree.py:1496-1522):
     every chunk named by the bits of the admitted count is a bit-exact copy, cells ingested afterwards build their chunks in
     the small arena exactly as they would in the full one, and the decode selection reads the same cells from either."""
     from freesolo_b200 import ops
     dev = _dev()
+    if tight:           # size the small arena from the admitted counts (what long prompts do) instead of the capacity
+        monkeypatch.setattr(ops.FsbForests, "TIGHT_ARENA_FROM", 0)
     H, first = 2, cells - 41
     kbar, ceil = _stats(cells, H, D, 9 + cells, False)
     tau = torch.quantile(ceil[0], 0.3, dim=-1)
