@@ -482,8 +482,9 @@ def run_linear_section(args, dev, ctx):
     out = {"workload": f"FS-L {args.model} through LinearFSCache: {ctx}-token prompt in 2048-token chunks, then {steps} eager tokens",
            "prefill_ktok_s": ctx / pms, "prefill_ms": pms, "decode_tok_s": steps / (dms * 1e-3),
            "state_bytes_per_layer": caches[0].state_bytes(), "peak_gib": torch.cuda.max_memory_allocated() / 2 ** 30,
-           "note": "state and activations do not grow with the prompt; every 128-token block is one readout launch plus the "
-                   "pool bookkeeping in torch operations, so the rate is launch-bound (the reference's is pure torch)"}
+           "note": "state and activations do not grow with the prompt; every 128-token block of every layer is four launches "
+                   "(cell statistics, pool merge, selection, readout + combine) issued from Python, so the rate is bound by "
+                   "the host (the reference's is pure torch)"}
     del caches, model
     torch.cuda.empty_cache()
     return out

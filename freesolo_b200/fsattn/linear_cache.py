@@ -89,28 +89,36 @@ class LinearFSCache:
         start = self.pos // self.Bq * self.Bq
         if start == self.block_start:
             return
-        s, P, Wc, C = self.s, self.P, self.Wc, self.C
-        count = start // s - self.eligible
+        count = start // self.s - self.eligible
         if count > 0:
-            n = count * s
-            nk, nv = self.pend_k[:, :, :n].contiguous(), self.pend_v[:, :, :n].contiguous()
-            mean, prio = ops.cell_stats(nk, count)                       # (B,H,count,D), (B,H,count) fp32, bit-exact statistics
-            width = min(P, self.eligible) + count
-            self.max_merge_cells = max(self.max_merge_cells, width)
-            self.merged_cells += width
-            self.updates += 1
-            # the P best of (top list, new cells) by (ceiling desc, cell id asc) stay; entering cells take the slots of the
-            # leaving ones; the newest Wc cells also go into the ring; `valid` is rewritten - one launch, a few KB written
-            ops.linear_merge(self.ids, self.prio, self.mean, self.k, self.v, self.valid, P=P, Wc=Wc, first_id=self.eligible,
-                             new_prio=prio, new_mean=mean, new_k=nk, new_v=nv)
+            n = count * self.s
+            self._merge(self.pend_k[:, :, :n], self.pend_v[:, :, :n], count)
             self.pend_k, self.pend_v = self.pend_k[:, :, n:].clone(), self.pend_v[:, :, n:].clone()
-            self.eligible += count
         self.block_start = start
+        self._set_pool()
+
+    def _merge(self, nk, nv, count):
+        """The rows nk / nv (B,H,count*s,D; views with dense rows are fine) of `count` newly completed cells enter the pool."""
+        P = self.P
+        mean, prio = ops.cell_stats(nk, count)                       # (B,H,count,D), (B,H,count) fp32, bit-exact statistics
+        width = min(P, self.eligible) + count
+        self.max_merge_cells = max(self.max_merge_cells, width)
+        self.merged_cells += width
+        self.updates += 1
+        # the P best of (top list, new cells) by (ceiling desc, cell id asc) stay; entering cells take the slots of the
+        # leaving ones; the newest Wc cells also go into the ring; `valid` is rewritten - one launch, a few KB written
+        ops.linear_merge(self.ids, self.prio, self.mean, self.k, self.v, self.valid, P=P, Wc=self.Wc, first_id=self.eligible,
+                         new_prio=prio, new_mean=mean, new_k=nk, new_v=nv)
+        self.eligible += count
+
+    def _set_pool(self):
         if self.eligible == 0:
             self.pool = None
             return
-        self.pool = dict(ids=self.ids[:, :, :C], priority=self.prio[:, :, :C], mean=self.mean[:, :, :C],
-                         k=self.k[:, :, :C * s], v=self.v[:, :, :C * s], valid=self.valid)
+        C, s = self.C, self.s
+        if self.pool is None:                        # the views never change: built once
+            self.pool = dict(ids=self.ids[:, :, :C], priority=self.prio[:, :, :C], mean=self.mean[:, :, :C],
+                             k=self.k[:, :, :C * s], v=self.v[:, :, :C * s], valid=self.valid)
 
     # ---- new tokens ------------------------------------------------------------------------------------------------------
     def ingest(self, k, v):
@@ -148,7 +156,78 @@ class LinearFSCache:
     # ---- one forward of the layer's attention over new tokens (ref: linear_cache.py:192-205) -------------------------------
     def attend(self, q, k, v):
         """q,k,v (B,H,n,D) bf16, un-rotated, any n: window branch + long-range branch + combine, then the tokens join
-        the state. Returns (B,H,n,D) (a view of the (B,n,H*D) buffer W_o reads)."""
+        the state. Returns (B,H,n,D) (a view of the (B,n,H*D) buffer W_o reads).
+
+        The call concatenates [stored window rows | new rows] and [pending rows | new rows] ONCE; every 128-token block then
+        reads its newly completed cells, its queries and its part of the window branch as views of those buffers (no copies),
+        so a block is four launches (cell statistics, pool merge, selection, readout + combine); the stored window and
+        pending rows are cut out once at the end."""
+        if torch.is_grad_enabled():
+            raise RuntimeError("LinearFSCache is inference-only; use torch.no_grad().")
+        a = self.attn
+        B, H, n, D = q.shape
+        if n <= 32:
+            return self._attend_tokens(q, k, v)
+        if not self._ready:
+            self._alloc(k)
+        lam, sigma, lrs, norm_w = a.head_params()
+        s, Bq, W = self.s, self.Bq, self.W
+        q, kb, vb = q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16)
+        # window branch of the whole call: [the last <= W stored rows | the new rows]; the stored rows get dummy queries
+        old = self.win_k.shape[2]
+        kc = torch.cat([self.win_k, kb], dim=2)
+        vc = torch.cat([self.win_v, vb], dim=2)
+        qc = torch.cat([torch.zeros(B, H, old, D, dtype=torch.bfloat16, device=q.device), q], dim=2)
+        cos, sin = a.rope.tables_bf16(self.pos + n)
+        sr_all = ops.window_prefill(qc, kc, vc, cos, sin, W, a.scale, pos0=self.pos - old)[:, old:]      # (B,n,H*D)
+        # rows of the cells that are not eligible yet, stored ones first: row r is token p0 + r
+        pk = torch.cat([self.pend_k, kb], dim=2)
+        pv = torch.cat([self.pend_v, vb], dim=2)
+        p0 = self.pos - self.pend_k.shape[2]
+        y = torch.empty(B, n, H * D, dtype=torch.bfloat16, device=q.device)
+        views = B == 1                                   # a token range of a (1, n, H*D) buffer is contiguous
+        wrapped = type(self).select is not LinearFSCache.select or "select" in self.__dict__
+        n_kv = self.C * s
+        q_pos0 = (n_kv + Bq - 1) // Bq * Bq              # every pool token lies before this virtual query position
+        off = 0
+        while off < n:
+            start = self.pos // Bq * Bq
+            if start != self.block_start:                # block change: the cells completed before it become eligible
+                count = start // s - self.eligible
+                if count > 0:
+                    r0 = self.eligible * s - p0
+                    self._merge(pk[:, :, r0:r0 + count * s], pv[:, :, r0:r0 + count * s], count)
+                self.block_start = start
+                self._set_pool()
+            m = min(n - off, Bq - self.pos % Bq)
+            qp = q[:, :, off:off + m]
+            sr = sr_all[:, off:off + m] if views else sr_all[:, off:off + m].contiguous()
+            if self.pool is None:
+                y[:, off:off + m] = sr                   # no completed cell yet: the long-range branch is zero
+            else:
+                if wrapped:                              # an overridden / wrapped select stays in the loop
+                    slots, ids = self.select(qp)
+                    sel = torch.full((B, H, m, a.cell_topk), -1, dtype=torch.int32, device=q.device)
+                    sel[..., :slots.shape[-1]] = torch.where(ids >= 0, slots, torch.full_like(slots, -1)).to(torch.int32)
+                else:
+                    sel = self._select_slots(qp)
+                # the pool slots are the "cells" of this readout
+                out = ops.readout_combine(qp, self.pool["k"], self.pool["v"], sel, sr, norm_w, lrs, a.lr_norm.eps, scale=a.scale,
+                                          Bq=Bq, n_kv=n_kv, q_pos0=q_pos0, out=y[:, off:off + m] if views else None)
+                if not views:
+                    y[:, off:off + m] = out
+            self.pos += m
+            off += m
+        done = self.eligible * s - p0                    # rows of pk that went into the pool
+        # what stays: the pending rows and the last W rows, copied out so that the call's buffers can go
+        self.pend_k, self.pend_v = pk[:, :, done:].clone(), pv[:, :, done:].clone()
+        self.win_k = kc[:, :, -W:].clone() if W else kc[:, :, :0]
+        self.win_v = vc[:, :, -W:].clone() if W else vc[:, :, :0]
+        return y.view(B, n, H, D).transpose(1, 2)
+
+    def _attend_tokens(self, q, k, v):
+        """`attend` for a few tokens (a decode step): block by block through prepare / ingest, whose small concatenations are
+        cheaper than the buffers of the long-call path below."""
         if torch.is_grad_enabled():
             raise RuntimeError("LinearFSCache is inference-only; use torch.no_grad().")
         a = self.attn

@@ -771,7 +771,7 @@ def fsb_select(forests: FsbForests, Q, K, lam, sigma, *, scale: float, N: int = 
 def linear_merge(ids, prio, mean, k, v, valid, *, P: int, Wc: int, first_id: int = 0, new_prio=None, new_mean=None,
                  new_k=None, new_v=None) -> None:
     """Block change of the streaming cache's pool (see fsattn_linear_merge_t): the new cells (statistics new_prio (B,H,n),
-    new_mean (B,H,n,D); rows new_k / new_v (B,H,n*32,D) bf16, contiguous) enter the top list / the ring in place and `valid`
+    new_mean (B,H,n,D); rows new_k / new_v (B,H,n*32,D) bf16, dense rows, any batch / head strides) enter the top list / the ring in place and `valid`
     is rewritten. Without new cells only `valid` is rewritten."""
     _need_cuda(ids, prio, mean, k, v, valid)
     B, H, C1 = ids.shape
@@ -785,8 +785,10 @@ def linear_merge(ids, prio, mean, k, v, valid, *, P: int, Wc: int, first_id: int
     a.count = 0
     if new_prio is not None:
         n = new_prio.shape[-1]
-        assert new_prio.is_contiguous() and new_mean.is_contiguous() and new_k.is_contiguous() and new_v.is_contiguous()
-        assert new_k.shape == (B, H, n * CELL, D) and new_k.dtype == torch.bfloat16 and new_v.shape == new_k.shape
+        assert new_prio.is_contiguous() and new_mean.is_contiguous()
+        # the rows may be a token range of a longer buffer: dense rows, any batch / head strides, the same for k and v
+        assert new_k.stride(-1) == 1 and new_k.stride(2) == D and new_v.stride() == new_k.stride()
+        assert new_k.shape == (B, H, n * CELL, D) and new_k.dtype == torch.bfloat16 and new_v.shape == new_k.shape and new_v.dtype == new_k.dtype
         a.count = n
         a.new_prio, a.new_mean, a.new_k, a.new_v = new_prio.data_ptr(), new_mean.data_ptr(), new_k.data_ptr(), new_v.data_ptr()
         a.nk_sb, a.nk_sh = new_k.stride(0), new_k.stride(1)
