@@ -28,6 +28,98 @@ import torch
 from .. import ops
 
 
+class _BlockCalls:
+    """The launches of one 128-token block of a long `attend` call - cell statistics and pool merge at the block change,
+    selection, readout + combine - with their argument structs built ONCE per call: per block only addresses, counts
+    and positions are rewritten and the four entry points are called directly, which takes the Python wrappers' checks
+    and allocations (most of the time of a block) out of the loop. Single-sequence calls only (B = 1: a token range of the
+    (1, n, H D) window-branch and output buffers is contiguous)."""
+
+    def __init__(self, cache, q, pk, pv, sr_all, y, lam, sigma, lrs, norm_w):
+        from .. import lib as L
+        a = cache.attn
+        B, H, n, D = q.shape
+        self.L, self.lib, self.c = L, L.load(), cache
+        self.stream = L.vp(ops._stream(q))
+        self.D, self.HD, self.kk_out = D, H * D, a.cell_topk
+        self.pk, self.pv, self.q, self.sr, self.y = pk.data_ptr(), pv.data_ptr(), q.data_ptr(), sr_all.data_ptr(), y.data_ptr()
+        assert q.stride(-1) == 1 and pk.stride(2) == D and pv.stride() == pk.stride() and sr_all.is_contiguous() and y.is_contiguous()
+        lam, sigma, lrs, norm_w = (t.detach().float().contiguous() for t in (lam, sigma, lrs.reshape(-1), norm_w))
+        self.sel = torch.empty(B, H, cache.Bq, self.kk_out, dtype=torch.int32, device=q.device)
+        self.stats = {}                                  # count -> (mean (B,H,count,D), prio (B,H,count)) fp32
+        self.keep = (lam, sigma, lrs, norm_w, q, pk, pv, sr_all, y)       # every address below stays valid while this object lives
+        ci = L.CellIngest()
+        ci.k = L.BHND(self.pk, pk.stride(0), pk.stride(1), pk.stride(2))
+        ci.v = L.BHND(None, 0, 0, 0)
+        ci.B, ci.H, ci.D, ci.cell0 = B, H, D, 0
+        lm = L.LinearMerge()
+        lm.ids, lm.prio, lm.mean, lm.k, lm.v, lm.valid = (t.data_ptr() for t in (cache.ids, cache.prio, cache.mean, cache.k, cache.v, cache.valid))
+        lm.nk_sb, lm.nk_sh = pk.stride(0), pk.stride(1)
+        lm.B, lm.H, lm.D, lm.P, lm.Wc = B, H, D, cache.P, cache.Wc
+        ls = L.LinearSelect()
+        ls.ids, ls.prio, ls.mean, ls.valid = cache.ids.data_ptr(), cache.prio.data_ptr(), cache.mean.data_ptr(), cache.valid.data_ptr()
+        ls.q = L.BHND(self.q, q.stride(0), q.stride(1), q.stride(2))
+        ls.lam, ls.sigma, ls.scale = lam.data_ptr(), sigma.data_ptr(), float(a.scale)
+        ls.B, ls.H, ls.D, ls.C, ls.n_pad, ls.kk_out = B, H, D, cache.C, cache.Bq, self.kk_out
+        ls.content_only = 1 if getattr(a, "sel_content_only", False) else 0
+        ls.sel, ls.sel_ids = self.sel.data_ptr(), None
+        rc = L.ReadoutCombine()
+        rc.q = L.BHND(self.q, q.stride(0), q.stride(1), q.stride(2))
+        # the pool slots are the "cells" of the readout: rows [0, C s) of the slot buffers
+        rc.k = L.BHND(cache.k.data_ptr(), cache.k.stride(0), cache.k.stride(1), cache.k.stride(2))
+        rc.v = L.BHND(cache.v.data_ptr(), cache.v.stride(0), cache.v.stride(1), cache.v.stride(2))
+        rc.sel, rc.sel_sb, rc.sel_sh = self.sel.data_ptr(), self.sel.stride(0), self.sel.stride(1)
+        rc.norm_w, rc.lrs = norm_w.data_ptr(), lrs.data_ptr()
+        n_kv = cache.C * cache.s
+        rc.B, rc.H, rc.D, rc.n_kv, rc.Bq, rc.kk = B, H, D, n_kv, cache.Bq, self.kk_out
+        rc.q_pos0 = (n_kv + cache.Bq - 1) // cache.Bq * cache.Bq
+        rc.scale, rc.eps, rc.impl = float(a.scale), float(a.lr_norm.eps), 0
+        self.ci, self.lm, self.ls, self.rc = ci, lm, ls, rc
+        self.q_sn = q.stride(2)
+
+    def _run(self, name, args):
+        rc = getattr(self.lib, name)(self.L.C.byref(args), self.stream)
+        if rc != self.L.OK:
+            self.L.check(rc, name)
+
+    def merge(self, r0: int, count: int):
+        """The cells of the rows [r0, r0 + count s) of the pending buffer enter the pool (LinearFSCache._merge)."""
+        c = self.c
+        st = self.stats.get(count)
+        if st is None:
+            B, H = self.ci.B, self.ci.H
+            st = (torch.empty(B, H, count, self.D, dtype=torch.float32, device=c.ids.device),
+                  torch.empty(B, H, count, dtype=torch.float32, device=c.ids.device))
+            self.stats[count] = st
+        mean, prio = st
+        off = r0 * self.D * 2
+        ci, lm = self.ci, self.lm
+        ci.k.ptr = self.pk + off
+        ci.ncell = count
+        ci.kbar, ci.kbar_sb, ci.kbar_sh = mean.data_ptr(), mean.stride(0), mean.stride(1)
+        ci.ceil, ci.ceil_sb, ci.ceil_sh = prio.data_ptr(), prio.stride(0), prio.stride(1)
+        self._run("fsattn_cell_ingest", ci)
+        width = min(c.P, c.eligible) + count
+        c.max_merge_cells = max(c.max_merge_cells, width)
+        c.merged_cells += width
+        c.updates += 1
+        lm.new_prio, lm.new_mean, lm.new_k, lm.new_v = prio.data_ptr(), mean.data_ptr(), self.pk + off, self.pv + off
+        lm.count, lm.first_id = count, c.eligible
+        self._run("fsattn_linear_merge", lm)
+        c.eligible += count
+
+    def block(self, off: int, m: int):
+        """Selection and readout + combine of the queries [off, off + m) of the call, at positions cache.pos .. + m - 1."""
+        c = self.c
+        ls, rc = self.ls, self.rc
+        qptr = self.q + off * self.q_sn * 2
+        ls.q.ptr, ls.n, ls.pos0, ls.kk = qptr, m, c.pos, min(self.kk_out, c.eligible)
+        self._run("fsattn_linear_select", ls)
+        tok = off * self.HD * 2
+        rc.q.ptr, rc.sr, rc.y, rc.N = qptr, self.sr + tok, self.y + tok, m
+        self._run("fsattn_readout_combine", rc)
+
+
 class LinearFSCache:
     bounded = True
 
@@ -187,6 +279,8 @@ class LinearFSCache:
         y = torch.empty(B, n, H * D, dtype=torch.bfloat16, device=q.device)
         views = B == 1                                   # a token range of a (1, n, H*D) buffer is contiguous
         wrapped = type(self).select is not LinearFSCache.select or "select" in self.__dict__
+        sr_all = sr_all.contiguous() if views else sr_all
+        fast = _BlockCalls(self, q, pk, pv, sr_all, y, lam, sigma, lrs, norm_w) if (views and not wrapped) else None
         n_kv = self.C * s
         q_pos0 = (n_kv + Bq - 1) // Bq * Bq              # every pool token lies before this virtual query position
         off = 0
@@ -196,10 +290,18 @@ class LinearFSCache:
                 count = start // s - self.eligible
                 if count > 0:
                     r0 = self.eligible * s - p0
-                    self._merge(pk[:, :, r0:r0 + count * s], pv[:, :, r0:r0 + count * s], count)
+                    if fast is not None:
+                        fast.merge(r0, count)
+                    else:
+                        self._merge(pk[:, :, r0:r0 + count * s], pv[:, :, r0:r0 + count * s], count)
                 self.block_start = start
                 self._set_pool()
             m = min(n - off, Bq - self.pos % Bq)
+            if fast is not None and self.pool is not None:
+                fast.block(off, m)
+                self.pos += m
+                off += m
+                continue
             qp = q[:, :, off:off + m]
             sr = sr_all[:, off:off + m] if views else sr_all[:, off:off + m].contiguous()
             if self.pool is None:

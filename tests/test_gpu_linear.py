@@ -184,3 +184,29 @@ def test_linear_prefill_of_a_model_matches_its_standard_prefill():
             h = trunk_cached(m, tok, lin)
             tok = lm_head(m, h[:, -1]).argmax(-1).view(1, 1)
     assert lin[0].pos == 4503 and lin[0].state_bytes() == lin[1].state_bytes()
+
+
+def test_the_direct_block_calls_equal_the_per_operation_path():
+    """A long attend call of one sequence drives its blocks through argument structs built once per call; a cache whose
+    `select` is wrapped takes the per-operation path. Same outputs, same state, bit for bit."""
+    from freesolo_b200.fsattn.linear_cache import LinearFSCache
+    dev = _dev()
+    g = load_golden("linear_vocab")
+    Q, K, V = (bf16_from_bits(g[k]).to(dev) for k in ("Q", "K", "V"))
+    a = _layer(g, dev)
+    pieces = [700, 1, 333, 129, 600]
+    slow = LinearFSCache(a)
+    y_slow, _ = _run(slow, Q, K, V, pieces)
+    fast = LinearFSCache(a)
+    ys, o = [], 0
+    with torch.no_grad():
+        for n in pieces:
+            ys.append(fast.attend(Q[:, :, o:o + n], K[:, :, o:o + n], V[:, :, o:o + n]))
+            o += n
+    y_fast = torch.cat(ys, dim=2)
+    B, H, N, D = y_fast.shape
+    assert torch.equal(y_fast.transpose(1, 2).reshape(B, N, H * D), y_slow)
+    for name in LinearFSCache._TENSORS:
+        assert torch.equal(getattr(fast, name), getattr(slow, name)), name
+    assert [fast.pos, fast.eligible, fast.max_merge_cells, fast.merged_cells, fast.updates] == \
+           [slow.pos, slow.eligible, slow.max_merge_cells, slow.merged_cells, slow.updates]
