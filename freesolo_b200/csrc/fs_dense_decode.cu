@@ -99,25 +99,38 @@ __global__ void __launch_bounds__(DD_WARPS * 32) fs_dense_decode_select_kernel(c
 
     DTop4 T;
     T.init();
-    for (int c0 = c_lo + warp * 4; c0 < c_hi; c0 += DD_WARPS * 4) {
-        const int cell = c0 + ci;
-        const bool ok = cell < c_hi;
-        float dot = 0.0f;
-        if (ok) {
-            const float4* kr = reinterpret_cast<const float4*>(kbar + (int64_t)cell * D + s8 * F);
+    // Four groups of cells per trip, every load issued before the first use: the hardware issues in order, so a loop body
+    // "load a mean key, score it" would pay one memory round trip per group, one after the other.
+    constexpr int DU = 4;
+    for (int c0 = c_lo + warp * 4; c0 < c_hi; c0 += DD_WARPS * 4 * DU) {
+        float4 kv[DU][F / 4];
+        float ce[DU];
+#pragma unroll
+        for (int u = 0; u < DU; u++) {
+            const int cell = c0 + u * DD_WARPS * 4 + ci;
+            const bool ok = cell < c_hi;
+            const float4* kr = reinterpret_cast<const float4*>(kbar + (int64_t)(ok ? cell : c_lo) * D + s8 * F);
+#pragma unroll
+            for (int j = 0; j < F / 4; j++) kv[u][j] = kr[j];
+            ce[u] = ceil[ok ? cell : c_lo];
+        }
+#pragma unroll
+        for (int u = 0; u < DU; u++) {
+            const int cell = c0 + u * DD_WARPS * 4 + ci;
+            const bool ok = cell < c_hi;
+            float dot = 0.0f;
 #pragma unroll
             for (int j = 0; j < F / 4; j++) {
-                const float4 kv = kr[j];
-                dot = fmaf(qv[4 * j + 0], kv.x, dot); dot = fmaf(qv[4 * j + 1], kv.y, dot);
-                dot = fmaf(qv[4 * j + 2], kv.z, dot); dot = fmaf(qv[4 * j + 3], kv.w, dot);
+                dot = fmaf(qv[4 * j + 0], kv[u][j].x, dot); dot = fmaf(qv[4 * j + 1], kv[u][j].y, dot);
+                dot = fmaf(qv[4 * j + 2], kv[u][j].z, dot); dot = fmaf(qv[4 * j + 3], kv[u][j].w, dot);
             }
-        }
-        dot += __shfl_xor_sync(FS_FULL, dot, 1);
-        dot += __shfl_xor_sync(FS_FULL, dot, 2);
-        dot += __shfl_xor_sync(FS_FULL, dot, 4);
-        if (ok && s8 == 0) {
-            const float prior = fs_prior(lam, ceil[cell], qpos, cell, (float)FSATTN_CELL, two_sigma);
-            T.insert(f_add(f_mul(dot, a.scale), prior), cell);
+            dot += __shfl_xor_sync(FS_FULL, dot, 1);
+            dot += __shfl_xor_sync(FS_FULL, dot, 2);
+            dot += __shfl_xor_sync(FS_FULL, dot, 4);
+            if (ok && s8 == 0) {
+                const float prior = fs_prior(lam, ce[u], qpos, cell, (float)FSATTN_CELL, two_sigma);
+                T.insert(f_add(f_mul(dot, a.scale), prior), cell);
+            }
         }
     }
     if (s8 == 0) {
